@@ -1,0 +1,378 @@
+#!/usr/bin/env python
+"""Benchmark: RWKV-v7 L12 D768 GPT-mode prefill tok/s on B200 (one process per GPU).
+
+Default workload (the one BASELINE.json's metric is quoted on): a randomly
+initialised L12 D768 model (12 heads x 64, ChannelMix hidden 3072, vocab 65568;
+fp16 weights with fp32 decay bias w0, orthogonal init as rwkv_mlx/train.py:209-310),
+prefill of B=8 sequences x T=4096 uniform-random tokens per GPU.  Each rank runs
+its own batch (data-parallel replicas, no collective on the data path); `value`
+is the tokens all ranks processed per second (weak scaling).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload prefill|wkv_fwd|wkv_bwd|decode|moe]
+
+Multi-GPU: launched by torch.distributed.run (RANK/LOCAL_RANK/WORLD_SIZE from the
+environment).  `--impl reference` times the CPU restatement of the reference
+path (the reference itself is MLX/Metal and cannot run here) on rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+CFG_L12 = dict(n_layer=12, n_embd=768, vocab_size=65568, dim_ffn=3072)
+
+
+# ---------------------------------------------------------------------------
+# helpers
+# ---------------------------------------------------------------------------
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d["hbm_gbs"], d.get("bf16_tflops"), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def dist_setup():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1:
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    return ws, rank, local
+
+
+def barrier(ws):
+    if ws > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(x: float, ws: int) -> float:
+    if ws == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason sampling during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, dev):
+        self.proc = None
+        self.out = ROOT / "gpurun_out" / f"clocks_{os.getpid()}.csv"
+        try:
+            uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+            self.out.parent.mkdir(exist_ok=True)
+            self.fh = open(self.out, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", uuid, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=self.fh, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.fh.close()
+        sm, smax, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.out.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                smax = max(smax, float(parts[1]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[3:7]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cuda_timed(fn, steps, stream=None):
+    """Run fn() `steps` times between CUDA events on the current stream; ms per step."""
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(steps):
+        fn()
+    e1.record(s)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+# ---------------------------------------------------------------------------
+# model construction
+# ---------------------------------------------------------------------------
+def build_model(dev, cfg_kw, seed=0, dtype=torch.float16):
+    from rwkv_mlx_b200.model import RWKV, RWKVConfig, cast_for_inference, init_weights
+
+    cfg = RWKVConfig(**cfg_kw)
+    with torch.device(dev):
+        m = RWKV(cfg)
+    init_weights(m, seed=seed)
+    cast_for_inference(m, dtype)
+    m.eval()
+    return cfg, m
+
+
+def wkv_algo_bytes(B, T, H, act_bytes, w_bytes):
+    """Algorithmic HBM bytes of one forward launch: r,k,v,a,b,y in the activation
+    dtype + w in its own dtype (7*E*s when all share one dtype)."""
+    E = B * T * H * 64
+    return E * (6 * act_bytes + w_bytes)
+
+
+def cpu_prefill_sample(cfg_kw, tokens_T, steps, seed=0):
+    """CPU restatement of the reference forward (oracle) on a bounded sample."""
+    from oracle import model_oracle as mo
+    from rwkv_mlx_b200.model import RWKV, RWKVConfig, init_weights
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count()))
+    cfg = RWKVConfig(**cfg_kw)
+    with torch.device("cpu"):
+        m = RWKV(cfg)
+    init_weights(m, seed=seed)
+    sd = {k: v.detach().float() for k, v in m.state_dict().items()}
+    del m
+    g = torch.Generator().manual_seed(seed)
+    idx = torch.randint(0, 65536, (1, tokens_T), generator=g)
+    with torch.no_grad():
+        mo.forward(sd, cfg, idx)  # warm-up
+        times = []
+        for _ in range(steps):
+            t0 = time.perf_counter()
+            mo.forward(sd, cfg, idx)
+            times.append(time.perf_counter() - t0)
+    per = statistics.median(times)
+    return {"value": tokens_T / per, "unit": "tok/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"L12 D768 GPT-mode forward, fp32, B=1 T={tokens_T}, median of {steps} steps "
+                      f"(oracle/model_oracle.py + oracle/wkv7_metal_port.c, OpenMP)"}
+
+
+# ---------------------------------------------------------------------------
+# workloads
+# ---------------------------------------------------------------------------
+def run_prefill(args, ws, rank, dev):
+    from rwkv_mlx_b200 import _native, wkv7
+
+    B, T = args.batch, args.seq
+    cfg, model = build_model(dev, CFG_L12, seed=0)
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    idx = torch.randint(0, 65536, (B, T), device=dev, generator=g)
+    host_idx = idx.cpu().pin_memory()
+    host_out = torch.empty((B, cfg.vocab_size), dtype=torch.float16).pin_memory()
+
+    def step():
+        with torch.no_grad():
+            logits, _ = model(idx)
+        return logits
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+
+    # ---- device-resident timed region ----
+    wkv7.fwd_timings = []
+    launches0 = _native.launch_count
+    barrier(ws)
+    torch.cuda.synchronize()
+    clk = ClockSampler(dev)
+    ms = cuda_timed(step, args.steps)
+    clocks = clk.stop()
+    barrier(ws)
+    launches = _native.launch_count - launches0
+    kt = [a.elapsed_time(b) for a, b in wkv7.fwd_timings]
+    wkv7.fwd_timings = None
+    ms_max = max_over_ranks(ms, ws)
+    tokens = B * T * ws
+    value = tokens / (ms_max / 1e3)
+
+    # ---- end-to-end through the public API, host buffers ----
+    dev_idx = torch.empty_like(idx)
+
+    def e2e_step():
+        dev_idx.copy_(host_idx, non_blocking=True)
+        with torch.no_grad():
+            logits, _ = model(dev_idx)
+        host_out.copy_(logits[:, -1], non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    barrier(ws)
+    t0 = time.perf_counter()
+    e2e_ms = cuda_timed(e2e_step, args.steps)
+    wall_ms = (time.perf_counter() - t0) * 1e3 / args.steps
+    e2e_ms = max_over_ranks(max(e2e_ms, wall_ms), ws)
+
+    hbm, _, src = peaks()
+    H = cfg.n_head
+    bytes_launch = wkv_algo_bytes(B, T, H, 2, 4)
+    k_ms = statistics.mean(kt) if kt else float("nan")
+    achieved = bytes_launch / (k_ms / 1e3) / 1e9
+    line = {
+        "metric": "prefill tok/s (L12 D768)", "value": value, "unit": "tok/s", "n_gpus": ws,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp16 (fp32 WKV state)",
+        "data": "synthetic: random-init weights, uniform-random tokens",
+        "config": {"workload": "L12 D768 GPT-mode prefill (BASELINE configs[1])", "model": "RWKV-v7 L12 D768",
+                   "global_batch": B * ws, "batch_per_gpu": B, "seq_len": T, "parallelism": f"dp{ws}",
+                   "l2": "per-step working set (4.3 GB logits, 0.37 GB weights) far larger than L2"},
+        "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": "tok/s", "h2d_bytes_per_step": B * T * 8,
+                "d2h_bytes_per_step": B * cfg.vocab_size * 2,
+                "path": "RWKV.forward via the public API; tokens H2D from pinned host, last-position logits D2H"},
+        "gpu_launches": launches,
+        "roofline": {"kernel": "wkv7_fwd (rwkv_wkv7_forward)", "bound": "hbm", "achieved": achieved,
+                     "peak": hbm, "unit": "GB/s", "frac": achieved / hbm, "traffic": traffic_for("wkv7_fwd", B, T, H),
+                     "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else "fallback 6650 GB/s",
+                     "algorithmic_bytes_per_launch": bytes_launch, "launch_ms": k_ms, "launches_timed": len(kt)},
+        "clocks": clocks,
+    }
+    return line
+
+
+def traffic_for(kernel, B, T, H):
+    """Per-launch DRAM bytes from the committed ncu summary (scaled by units), or None."""
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    d = json.loads(p.read_text()).get(kernel)
+    if not d:
+        return None
+    return d["bytes_per_unit"] * B * T * H
+
+
+def run_wkv(args, ws, rank, dev, backward=False):
+    """WKV-7 op alone at config-2 scale (B=8, T=4096, H=12, fp16 + fp32 w)."""
+    from rwkv_mlx_b200 import wkv7
+
+    B, T, H = args.batch, args.seq, 12
+    C = H * 64
+    g = torch.Generator(device=dev).manual_seed(rank)
+    mk = lambda: torch.randn(B, T, C, device=dev, generator=g).half()
+    r, k, v = mk(), mk(), mk()
+    w = torch.empty(B, T, C, device=dev).uniform_(-6, -0.5, generator=g)
+    kk = torch.nn.functional.normalize(torch.randn(B, T, H, 64, device=dev, generator=g), dim=-1).view(B, T, C)
+    a = (-kk).half()
+    b = (kk * torch.sigmoid(torch.randn(B, T, C, device=dev, generator=g))).half()
+    dy = mk()
+    if backward:
+        _, ck, _, _ = wkv7._fwd(r, w, k, v, a, b, want_ckpt=True)
+        fn = lambda: wkv7._bwd(r, w, k, v, a, b, dy, ck)
+        nbytes = B * T * C * (12 * 2 + 4)
+    else:
+        fn = lambda: wkv7.wkv7(r, w, k, v, a, b)
+        nbytes = wkv_algo_bytes(B, T, H, 2, 4)
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    barrier(ws)
+    clk = ClockSampler(dev)
+    ms = cuda_timed(fn, args.steps)
+    clocks = clk.stop()
+    ms = max_over_ranks(ms, ws)
+    hbm, _, src = peaks()
+    gbs = nbytes / (ms / 1e3) / 1e9
+    name = "wkv7_bwd" if backward else "wkv7_fwd"
+    return {"metric": f"{name} HBM GB/s", "value": gbs * ws, "unit": "GB/s", "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp16 (fp32 w, fp32 state)", "data": "synthetic (config 1 distributions)",
+            "config": {"workload": f"{name} B={B} T={T} H={H}", "l2": "inputs larger than L2"},
+            "roofline": {"kernel": name, "bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s",
+                         "frac": gbs / hbm, "traffic": traffic_for(name, B, T, H), "peak_source": src},
+            "clocks": clocks}
+
+
+def run_reference(args):
+    """CPU restatement of the reference path, rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    sample_T = args.cpu_sample_tokens
+    res = cpu_prefill_sample(CFG_L12, sample_T, max(1, args.steps))
+    return {"impl": "reference", "metric": "prefill tok/s (L12 D768)", "value": res["value"], "unit": "tok/s",
+            "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "dtype": "fp32", "data": "synthetic",
+            "config": {"workload": "L12 D768 GPT-mode prefill (BASELINE configs[1]), bounded CPU sample"},
+            "cpu_baseline": res,
+            "e2e": {"value": res["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "reference is MLX/Metal (not installable here); this is its CPU restatement"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="prefill", choices=["prefill", "wkv_fwd", "wkv_bwd"])
+    ap.add_argument("--batch", type=int, default=8)
+    ap.add_argument("--seq", type=int, default=4096)
+    ap.add_argument("--cpu-sample-tokens", type=int, default=128)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    if args.impl == "reference":
+        line = run_reference(args)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+
+    ws, rank, local = dist_setup()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if args.workload == "prefill":
+        line = run_prefill(args, ws, rank, dev)
+    else:
+        line = run_wkv(args, ws, rank, dev, backward=args.workload == "wkv_bwd")
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline and args.workload == "prefill":
+        line["cpu_baseline"] = cpu_prefill_sample(CFG_L12, args.cpu_sample_tokens, 2)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

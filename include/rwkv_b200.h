@@ -1,0 +1,156 @@
+/*
+ * rwkv_b200.h -- C ABI of the B200 (sm_100a) WKV-7 and LoRA-MoE kernels.
+ *
+ * Every entry point takes plain device pointers, sizes and an opaque CUDA
+ * stream (cudaStream_t passed as void*; NULL = legacy default stream).  Work is
+ * enqueued on that stream; no entry point synchronises the host.  The caller
+ * allocates every input, output and workspace buffer.  Return value: 0 on
+ * success, otherwise a rwkv_status code (a launch failure is reported as
+ * RWKV_ERR_CUDA; rwkv_last_error() gives the CUDA error string).
+ *
+ * Conventions shared by the WKV-7 entry points (reference:
+ * rwkv_mlx/kernels/wkv7_metal.py:250-319):
+ *   - per-token tensors r, w, k, v, a, b, y, dy and the six gradients are
+ *     (B, T, H, N) row-major, i.e. (B, T, C) with C = H*N, in `dtype`;
+ *   - w is the log-log decay: the per-step decay is exp(-exp(w))
+ *     (wkv7_metal.py:57) unless stated otherwise; w has its own dtype code
+ *     `w_dtype`, either equal to `dtype` or RWKV_F32 (the reference model
+ *     promotes w to fp32 through its fp32 bias w0, model.py:200, and the Metal
+ *     kernel reads each input in its own dtype);
+ *   - states are float32 (B, H, N, N), row i = value index, column j = key
+ *     index; one step is  S <- S diag(decay) + (S a) b^T + v k^T,  y = S r;
+ *   - N (head size) must be 64 (the reference asserts the same,
+ *     rwkv_mlx/model.py:115).
+ */
+#ifndef RWKV_B200_H
+#define RWKV_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    RWKV_OK = 0,
+    RWKV_ERR_SHAPE = 1,     /* a size is <= 0, inconsistent or too large */
+    RWKV_ERR_DTYPE = 2,     /* unsupported dtype code */
+    RWKV_ERR_HEAD_SIZE = 3, /* N != 64 */
+    RWKV_ERR_CUDA = 4,      /* a CUDA call or launch failed */
+    RWKV_ERR_ALIGN = 5,     /* a pointer is not aligned as required */
+    RWKV_ERR_ARG = 6,       /* a required pointer is NULL or an option is invalid */
+    RWKV_ERR_WORKSPACE = 7  /* workspace smaller than the *_workspace_size query */
+} rwkv_status;
+
+typedef enum { RWKV_F32 = 0, RWKV_F16 = 1, RWKV_BF16 = 2 } rwkv_dtype;
+
+/* Human-readable text of the last CUDA error seen by this library (per thread). */
+const char* rwkv_last_error(void);
+/* ABI version of this header (bumped on any signature change). */
+int rwkv_abi_version(void);
+
+/* ------------------------------------------------------------------------ */
+/* WKV-7 forward.
+ * Replaces wkv7_metal_forward (rwkv_mlx/kernels/wkv7_metal.py:250-279) and the
+ * forward kernel body (:28-91).
+ *   s0    optional initial state (B,H,N,N) fp32; NULL = zeros (the reference
+ *         always starts from zero).
+ *   y     output (B,T,H,N) in dtype.
+ *   sT    optional final state (B,H,N,N) fp32.
+ *   ckpt  optional state snapshots, (B,H,T/ckpt_len,N,N) fp32: snapshot c is
+ *         the state after step (c+1)*ckpt_len-1, as the reference writes `s`
+ *         every 16 steps (:80-89).  Needed by rwkv_wkv7_backward.
+ *   sa    optional (B,T,H,N) fp32: sa_t = S_{t-1} a_t per step (the reference's
+ *         `sa_out`, :63-68).
+ *   ckpt_len  multiple of 16, >= 16 (ignored when ckpt == NULL).          */
+int rwkv_wkv7_forward(const void* r, const void* w, const void* k, const void* v,
+                      const void* a, const void* b, const float* s0, void* y,
+                      float* sT, float* ckpt, float* sa, int B, int T, int H, int N,
+                      int dtype, int w_dtype, int ckpt_len, void* stream);
+
+/* WKV-7 backward, exact (no division by the decay).
+ * Replaces wkv7_metal_backward (wkv7_metal.py:282-319) and the backward kernel
+ * body (:102-214).  The reference reconstructs earlier states by dividing by the
+ * decay (:174-178); this entry point recomputes them from `ckpt` instead.
+ *   ckpt  snapshots from rwkv_wkv7_forward with the same ckpt_len and s0.
+ *   dsT   optional gradient w.r.t. the final state; ds0 optional output.
+ *   dr..db outputs (B,T,H,N) in dtype; dw is w.r.t. the log-log w input.   */
+int rwkv_wkv7_backward(const void* r, const void* w, const void* k, const void* v,
+                       const void* a, const void* b, const void* dy, const float* s0,
+                       const float* dsT, const float* ckpt, void* dr, void* dw, void* dk,
+                       void* dv, void* da, void* db, float* ds0, int B, int T, int H,
+                       int N, int dtype, int w_dtype, int ckpt_len, void* stream);
+
+/* One RNN-mode step for Bs independent sequences, state updated in place.
+ * Replaces the state update of _time_mixing_rnn (rwkv_mlx/model.py:475-483),
+ * batched over sequences (the reference runs one sequence per call).
+ *   S      (Bs,H,N,N) fp32, read and written.
+ *   r..b   (Bs,H,N) in dtype; y (Bs,H,N) in dtype.
+ *   w_mode 0: w is log-log (decay = exp(-exp(w)), as in GPT mode);
+ *          1: w is the decay itself (model.py:477 computes it directly). */
+int rwkv_wkv7_step(float* S, const void* r, const void* w, const void* k, const void* v,
+                   const void* a, const void* b, void* y, int Bs, int H, int N, int dtype,
+                   int w_dtype, int w_mode, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* LoRA-MoE router.  Replaces Router.__call__ (rwkv_mlx/moe.py:51-86).
+ *   x       (ntok, C) in dtype.      gate_w (E, C) fp32 (nn.Linear weight).
+ *   bias    optional (E,) fp32 added to the logits (NULL = reference router).
+ *   logits  optional output (ntok, E) fp32.
+ *   inds    output (ntok, topk) int32, slots in descending logit order, ties
+ *           to the lower expert id (argpartition leaves both unspecified,
+ *           moe.py:66-68).
+ *   scores  output (ntok, topk) in dtype: softmax over the selected logits.
+ *   stats   output fp32[2 + E]: [aux, z, f_0..f_{E-1}] with
+ *           aux = E * sum_e f_e p_e, z = mean_t (log sum_e exp l_te)^2
+ *           (moe.py:61-62, :76-84).
+ *   counts  optional output int32[E]: tokens-slots routed to each expert.
+ *   workspace  >= rwkv_moe_router_workspace_size(ntok, E) bytes.
+ * Constraints: E <= 32, topk <= E, C % 8 == 0, x 16-byte aligned.          */
+size_t rwkv_moe_router_workspace_size(int ntok, int E);
+int rwkv_moe_router(const void* x, const float* gate_w, const float* bias, float* logits,
+                    int32_t* inds, void* scores, float* stats, int32_t* counts,
+                    void* workspace, size_t workspace_bytes, int ntok, int C, int E,
+                    int topk, int dtype, void* stream);
+
+/* Stable counting sort of the (token, slot) routing entries by expert.
+ * The reference has no counterpart (it loops densely over all experts,
+ * moe.py:139-145); this builds the dispatch order its output is invariant to.
+ *   inds     (ntok, topk) int32 expert ids in [0, E).
+ *   perm     output int32[ntok*topk]: perm[p] = entry (tok*topk+slot) placed at
+ *            sorted position p; entries of one expert keep ascending entry order.
+ *   inv      output int32[ntok*topk]: inv[entry] = p.
+ *   offsets  output int32[E+1]: expert e owns positions [offsets[e], offsets[e+1]).
+ *   workspace >= rwkv_moe_permute_workspace_size(ntok*topk, E) bytes.      */
+size_t rwkv_moe_permute_workspace_size(int n_entries, int E);
+int rwkv_moe_permute(const int32_t* inds, int32_t* perm, int32_t* inv, int32_t* offsets,
+                     void* workspace, size_t workspace_bytes, int ntok, int topk, int E,
+                     void* stream);
+
+/* Grouped down-projection of the routed entries: for sorted position p with
+ * entry = perm[p], token = entry / topk, expert e (offsets):
+ *   h[p, :] = x[token, :] @ A[e]         (moe.py:142, first product)
+ *   x (ntok, C) dtype; A (E, C, R) dtype; h (ntok*topk, R) fp32.          */
+int rwkv_moe_lora_down(const void* x, const void* A, const int32_t* perm,
+                       const int32_t* offsets, float* h, int ntok, int C, int R, int E,
+                       int topk, int dtype, void* stream);
+
+/* Combine: out[t] = base[t] + sum_slot scores[t,slot] * (h[inv[t*topk+slot]] @ B[e])
+ * with e = inds[t,slot] (moe.py:142-147).  base may equal out (in place) or be
+ * NULL (treated as zeros).  B (E, R, C) dtype; out (ntok, C) dtype.        */
+int rwkv_moe_lora_combine(const void* base, const float* h, const void* B,
+                          const int32_t* inds, const void* scores, const int32_t* inv,
+                          void* out, int ntok, int C, int R, int E, int topk, int dtype,
+                          void* stream);
+
+/* sum_{i<j} ||A_i^T A_j||_F^2 over the expert down-projections
+ * (LoRAMoE_CMix.orthogonal_loss, moe.py:149-163).  A (E, C, R) dtype;
+ * out: one fp32 scalar.  R <= 64.                                          */
+int rwkv_moe_ortho_loss(const void* A, float* out, int E, int C, int R, int dtype,
+                        void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* RWKV_B200_H */

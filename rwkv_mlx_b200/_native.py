@@ -1,0 +1,115 @@
+"""ctypes binding of the C-ABI library ``_lib/librwkv_b200.so`` (include/rwkv_b200.h).
+
+The library is the only compute path: if it is missing, or no CUDA device is
+present, the public functions raise instead of falling back to anything else.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "_lib" / "librwkv_b200.so"
+
+STATUS = {
+    0: "ok",
+    1: "bad shape",
+    2: "unsupported dtype",
+    3: "unsupported head size (must be 64)",
+    4: "CUDA error",
+    5: "misaligned pointer",
+    6: "invalid argument",
+    7: "workspace too small",
+}
+
+DTYPE_CODE = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_SZ = ctypes.c_size_t
+
+# name -> (restype, argtypes); must match include/rwkv_b200.h
+SIGNATURES = {
+    "rwkv_last_error": (ctypes.c_char_p, []),
+    "rwkv_abi_version": (_I, []),
+    "rwkv_wkv7_forward": (_I, [_P] * 11 + [_I] * 7 + [_P]),
+    "rwkv_wkv7_backward": (_I, [_P] * 17 + [_I] * 7 + [_P]),
+    "rwkv_wkv7_step": (_I, [_P] * 8 + [_I] * 6 + [_P]),
+    "rwkv_moe_router_workspace_size": (_SZ, [_I, _I]),
+    "rwkv_moe_router": (_I, [_P] * 9 + [_SZ] + [_I] * 5 + [_P]),
+    "rwkv_moe_permute_workspace_size": (_SZ, [_I, _I]),
+    "rwkv_moe_permute": (_I, [_P] * 5 + [_SZ] + [_I] * 3 + [_P]),
+    "rwkv_moe_lora_down": (_I, [_P] * 5 + [_I] * 6 + [_P]),
+    "rwkv_moe_lora_combine": (_I, [_P] * 7 + [_I] * 6 + [_P]),
+    "rwkv_moe_ortho_loss": (_I, [_P] * 2 + [_I] * 4 + [_P]),
+}
+
+_lib = None
+
+
+class RwkvNativeError(RuntimeError):
+    pass
+
+
+def load(path: Path | None = None) -> ctypes.CDLL:
+    """Load the library (no GPU needed to load it)."""
+    global _lib
+    if _lib is None or path is not None:
+        p = Path(path or os.environ.get("RWKV_B200_LIB", LIB_PATH))
+        if not p.exists():
+            raise RwkvNativeError(
+                f"{p} not found: build it with `python -m rwkv_mlx_b200.build` (there is no fallback)"
+            )
+        lib = ctypes.CDLL(str(p))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        if path is not None:
+            return lib
+        _lib = lib
+    return _lib
+
+
+def lib() -> ctypes.CDLL:
+    if not torch.cuda.is_available():
+        raise RwkvNativeError("rwkv_mlx_b200 kernels need a CUDA device (no CPU fallback)")
+    return load()
+
+
+# Kernel launches issued through this binding (per C-ABI entry point: the number of
+# kernels that entry point enqueues).  bench.py reads it to report gpu_launches.
+KERNELS_PER_CALL = {
+    "rwkv_wkv7_forward": 1, "rwkv_wkv7_backward": 1, "rwkv_wkv7_step": 1,
+    "rwkv_moe_router": 2, "rwkv_moe_permute": 3, "rwkv_moe_lora_down": 1,
+    "rwkv_moe_lora_combine": 1, "rwkv_moe_ortho_loss": 1,
+}
+launch_count = 0
+
+
+def check(rc: int, what: str) -> None:
+    global launch_count
+    if rc == 0:
+        launch_count += KERNELS_PER_CALL.get(what, 0)
+    if rc != 0:
+        msg = STATUS.get(rc, f"status {rc}")
+        if rc == 4:
+            msg += ": " + (load().rwkv_last_error() or b"").decode()
+        raise RwkvNativeError(f"{what} failed: {msg}")
+
+
+def ptr(t: torch.Tensor | None):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def stream_ptr(device=None):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def dtype_code(t: torch.Tensor) -> int:
+    if t.dtype not in DTYPE_CODE:
+        raise RwkvNativeError(f"unsupported dtype {t.dtype}")
+    return DTYPE_CODE[t.dtype]

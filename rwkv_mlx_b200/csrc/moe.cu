@@ -1,0 +1,501 @@
+// LoRA-MoE ChannelMix kernels (reference rwkv_mlx/moe.py:35-163).
+//
+//   moe_router     : fp32 logits x @ Wg^T (+ optional bias), warp-level top-k
+//                    (ties -> lower expert id), softmax over the selected logits,
+//                    per-CTA partial sums for aux / z-loss (moe.py:56-84).
+//   moe_finalize   : deterministic (fixed-order) reduction of those partials.
+//   moe_count / moe_scan / moe_scatter : stable counting sort of the
+//                    (token, slot) entries by expert -> perm, inv, offsets.
+//   moe_lora_down  : h[p] = x[token(p)] @ A[e(p)]  for every sorted entry p.
+//   moe_combine    : out[t] = base[t] + sum_slot score * (h @ B[e]).
+//   moe_ortho      : sum_{i<j} ||A_i^T A_j||_F^2 (moe.py:149-163).
+#include <cfloat>
+
+#include "common.cuh"
+
+namespace rwkv {
+
+constexpr int ROUTER_WARPS = 8;
+constexpr int ROUTER_MAX_CTAS = 148 * 8;
+constexpr int PERM_TILE = 2048;
+constexpr int PERM_THREADS = 256;
+
+__host__ __device__ inline int router_ctas(int ntok) {
+    int need = (ntok + ROUTER_WARPS - 1) / ROUTER_WARPS;
+    return need < ROUTER_MAX_CTAS ? need : ROUTER_MAX_CTAS;
+}
+
+// ---------------------------------------------------------------------------
+// Router
+// ---------------------------------------------------------------------------
+template <typename T, int EM>
+__global__ void __launch_bounds__(ROUTER_WARPS * 32)
+    moe_router_kernel(const T* __restrict__ x, const float* __restrict__ gate_w,
+                      const float* __restrict__ bias, float* __restrict__ logits,
+                      int32_t* __restrict__ inds, T* __restrict__ scores,
+                      float* __restrict__ part_f, int32_t* __restrict__ part_c, int ntok, int C,
+                      int E, int topk) {
+    extern __shared__ float wsm[];  // [E][C] gate weights
+    __shared__ float red_f[ROUTER_WARPS][EM + 1];
+    __shared__ int red_c[ROUTER_WARPS][EM];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    for (int i = tid; i < E * C; i += blockDim.x) wsm[i] = gate_w[i];
+    __syncthreads();
+
+    float acc_p = 0.f, acc_z = 0.f;  // lane e: sum of p_e; lane 0: sum of lse^2
+    int acc_c = 0;                   // lane e: count of expert e
+    const float lbias = (bias && lane < E) ? bias[lane] : 0.f;
+    const int nvec = C / 8;
+    for (int tok = blockIdx.x * ROUTER_WARPS + warp; tok < ntok; tok += gridDim.x * ROUTER_WARPS) {
+        float acc[EM];
+#pragma unroll
+        for (int e = 0; e < EM; e++) acc[e] = 0.f;
+        const T* xr = x + (size_t)tok * C;
+        for (int vi = lane; vi < nvec; vi += 32) {
+            float xf[8];
+            if constexpr (sizeof(T) == 2) {
+                uint4 raw = *reinterpret_cast<const uint4*>(xr + vi * 8);
+                const T* h = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+                for (int q = 0; q < 8; q++) xf[q] = to_f32(h[q]);
+            } else {
+                float4 r0 = *reinterpret_cast<const float4*>(xr + vi * 8);
+                float4 r1 = *reinterpret_cast<const float4*>(xr + vi * 8 + 4);
+                xf[0] = r0.x, xf[1] = r0.y, xf[2] = r0.z, xf[3] = r0.w;
+                xf[4] = r1.x, xf[5] = r1.y, xf[6] = r1.z, xf[7] = r1.w;
+            }
+#pragma unroll
+            for (int e = 0; e < EM; e++) {
+                if (e < E) {
+                    const float* wr = wsm + e * C + vi * 8;
+#pragma unroll
+                    for (int q = 0; q < 8; q++) acc[e] = fmaf(xf[q], wr[q], acc[e]);
+                }
+            }
+        }
+        // butterfly: every lane ends with every logit
+#pragma unroll
+        for (int e = 0; e < EM; e++) {
+            if (e < E) {
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], o);
+            }
+        }
+        float my = -FLT_MAX;
+#pragma unroll
+        for (int e = 0; e < EM; e++)
+            if (e == lane) my = acc[e];
+        const bool valid = lane < E;
+        float lg = valid ? my + lbias : -INFINITY;
+        if (logits && valid) logits[(size_t)tok * E + lane] = lg;
+
+        // full softmax statistics (max-stabilised log-sum-exp)
+        float m = lg;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        float ex = valid ? expf(lg - m) : 0.f;
+        float se = ex;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) se += __shfl_xor_sync(0xffffffffu, se, o);
+        if (valid) acc_p += ex / se;
+        const float lse = m + logf(se);
+        if (lane == 0) acc_z = fmaf(lse, lse, acc_z);
+
+        // warp top-k: repeated argmax, ties to the lower expert id
+        bool taken = !valid;
+        float sel0 = 0.f, denom = 0.f;
+        float my_sel_logit = 0.f;
+        int my_slot = -1;
+        for (int kk = 0; kk < topk; kk++) {
+            float bv = taken ? -INFINITY : lg;
+            int bi = taken ? 0x7fffffff : lane;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                if (ov > bv || (ov == bv && oi < bi)) bv = ov, bi = oi;
+            }
+            if (kk == 0) sel0 = bv;
+            denom += expf(bv - sel0);
+            if (lane == bi) {
+                taken = true;
+                my_slot = kk;
+                my_sel_logit = bv;
+            }
+            if (lane == 0) inds[(size_t)tok * topk + kk] = bi;
+        }
+        if (my_slot >= 0) {
+            scores[(size_t)tok * topk + my_slot] = from_f32<T>(expf(my_sel_logit - sel0) / denom);
+            acc_c += 1;
+        }
+    }
+    if (lane < EM) {
+        red_f[warp][lane] = (lane < E) ? acc_p : 0.f;
+        red_c[warp][lane] = (lane < E) ? acc_c : 0;
+    }
+    if (lane == 0) red_f[warp][EM] = acc_z;
+    __syncthreads();
+    if (tid < E) {
+        float s = 0.f;
+        int c = 0;
+        for (int w = 0; w < ROUTER_WARPS; w++) s += red_f[w][tid], c += red_c[w][tid];
+        part_f[(size_t)blockIdx.x * (E + 1) + tid] = s;
+        part_c[(size_t)blockIdx.x * E + tid] = c;
+    }
+    if (tid == 0) {
+        float s = 0.f;
+        for (int w = 0; w < ROUTER_WARPS; w++) s += red_f[w][EM];
+        part_f[(size_t)blockIdx.x * (E + 1) + E] = s;
+    }
+}
+
+__global__ void moe_router_finalize_kernel(const float* __restrict__ part_f,
+                                           const int32_t* __restrict__ part_c, int nblk, int ntok,
+                                           int E, int topk, float* __restrict__ stats,
+                                           int32_t* __restrict__ counts) {
+    __shared__ float fp[64];
+    const int e = threadIdx.x;
+    if (e < E) {
+        float p = 0.f;
+        long long c = 0;
+        for (int b = 0; b < nblk; b++) p += part_f[(size_t)b * (E + 1) + e], c += part_c[(size_t)b * E + e];
+        const float pe = p / (float)ntok;
+        const float fe = (float)c / ((float)ntok * (float)topk);
+        stats[2 + e] = fe;
+        fp[e] = fe * pe;
+        if (counts) counts[e] = (int32_t)c;
+    }
+    __syncthreads();
+    if (e == 0) {
+        float aux = 0.f;
+        for (int i = 0; i < E; i++) aux += fp[i];
+        float z = 0.f;
+        for (int b = 0; b < nblk; b++) z += part_f[(size_t)b * (E + 1) + E];
+        stats[0] = (float)E * aux;
+        stats[1] = z / (float)ntok;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Permutation (stable counting sort by expert)
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(PERM_THREADS)
+    moe_count_kernel(const int32_t* __restrict__ inds, int n, int E, int32_t* __restrict__ blkcnt) {
+    extern __shared__ int hist[];
+    for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e] = 0;
+    __syncthreads();
+    const int t0 = blockIdx.x * PERM_TILE;
+    const int t1 = min(n, t0 + PERM_TILE);
+    for (int i = t0 + threadIdx.x; i < t1; i += blockDim.x) atomicAdd(&hist[inds[i]], 1);
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x) blkcnt[(size_t)blockIdx.x * E + e] = hist[e];
+}
+
+// blkoff[b][e] = start of expert e + entries of e in tiles < b ; offsets[E+1]
+__global__ void moe_scan_kernel(const int32_t* __restrict__ blkcnt, int nblk, int E,
+                                int32_t* __restrict__ blkoff, int32_t* __restrict__ offsets) {
+    extern __shared__ int tot[];
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        int s = 0;
+        for (int b = 0; b < nblk; b++) {
+            blkoff[(size_t)b * E + e] = s;
+            s += blkcnt[(size_t)b * E + e];
+        }
+        tot[e] = s;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int s = 0;
+        for (int e = 0; e < E; e++) {
+            offsets[e] = s;
+            const int t = tot[e];
+            tot[e] = s;
+            s += t;
+        }
+        offsets[E] = s;
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        const int st = tot[e];
+        for (int b = 0; b < nblk; b++) blkoff[(size_t)b * E + e] += st;
+    }
+}
+
+__global__ void __launch_bounds__(PERM_THREADS)
+    moe_scatter_kernel(const int32_t* __restrict__ inds, int n, int E,
+                       const int32_t* __restrict__ blkoff, int32_t* __restrict__ perm,
+                       int32_t* __restrict__ inv) {
+    constexpr int NW = PERM_THREADS / 32, SUB = PERM_TILE / NW;
+    extern __shared__ int sm[];
+    int* wcnt = sm;           // [NW][E]
+    int* wrun = sm + NW * E;  // [NW][E]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int i = threadIdx.x; i < NW * E; i += blockDim.x) wcnt[i] = 0;
+    __syncthreads();
+    const int s0 = blockIdx.x * PERM_TILE + warp * SUB;
+    const int s1 = min(n, s0 + SUB);
+    for (int i = s0 + lane; i < s1; i += 32) atomicAdd(&wcnt[warp * E + inds[i]], 1);
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        int s = blkoff[(size_t)blockIdx.x * E + e];
+        for (int w = 0; w < NW; w++) {
+            wrun[w * E + e] = s;
+            s += wcnt[w * E + e];
+        }
+    }
+    __syncthreads();
+    for (int base = s0; base < s1; base += 32) {
+        const int i = base + lane;
+        const bool act = i < s1;
+        const unsigned mask = __ballot_sync(0xffffffffu, act);
+        if (act) {
+            const int e = inds[i];
+            const unsigned peers = __match_any_sync(mask, e);
+            const int rank = __popc(peers & ((1u << lane) - 1u));
+            const int pos = wrun[warp * E + e] + rank;
+            perm[pos] = i;
+            inv[i] = pos;
+            __syncwarp(mask);
+            if (rank == 0) wrun[warp * E + e] += __popc(peers);
+        }
+        __syncwarp();
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Grouped LoRA down-projection: one warp per sorted entry.
+// ---------------------------------------------------------------------------
+template <typename T, int R>
+__global__ void __launch_bounds__(256)
+    moe_lora_down_kernel(const T* __restrict__ x, const T* __restrict__ A,
+                         const int32_t* __restrict__ perm, const int32_t* __restrict__ offsets,
+                         float* __restrict__ h, int n, int C, int E, int topk) {
+    __shared__ int offs[257];
+    for (int i = threadIdx.x; i <= E; i += blockDim.x) offs[i] = offsets[i];
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int p = blockIdx.x * 8 + warp; p < n; p += gridDim.x * 8) {
+        int e = 0;
+        while (e + 1 < E && offs[e + 1] <= p) e++;
+        const int tok = perm[p] / topk;
+        const T* xr = x + (size_t)tok * C;
+        const T* Ae = A + (size_t)e * C * R;
+        float acc[R];
+#pragma unroll
+        for (int q = 0; q < R; q++) acc[q] = 0.f;
+        for (int c = lane; c < C; c += 32) {
+            const float xv = to_f32(xr[c]);
+            const T* ar = Ae + (size_t)c * R;
+#pragma unroll
+            for (int q = 0; q < R; q++) acc[q] = fmaf(xv, to_f32(ar[q]), acc[q]);
+        }
+#pragma unroll
+        for (int q = 0; q < R; q++) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) acc[q] += __shfl_xor_sync(0xffffffffu, acc[q], o);
+        }
+        if (lane == 0) {
+#pragma unroll
+            for (int q = 0; q < R; q++) h[(size_t)p * R + q] = acc[q];
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Combine: one warp per token.
+// ---------------------------------------------------------------------------
+template <typename T, int R>
+__global__ void __launch_bounds__(256)
+    moe_combine_kernel(const T* base, const float* __restrict__ h, const T* __restrict__ B,
+                       const int32_t* __restrict__ inds, const T* __restrict__ scores,
+                       const int32_t* __restrict__ inv, T* out, int ntok, int C, int topk) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int tok = blockIdx.x * 8 + warp; tok < ntok; tok += gridDim.x * 8) {
+        float hs[8][R];  // topk <= 8
+        int es[8];
+        for (int s = 0; s < topk; s++) {
+            const int ent = tok * topk + s;
+            const int p = inv[ent];
+            es[s] = inds[ent];
+            const float sc = to_f32(scores[ent]);
+#pragma unroll
+            for (int q = 0; q < R; q++) hs[s][q] = sc * h[(size_t)p * R + q];
+        }
+        for (int c = lane; c < C; c += 32) {
+            float o = base ? to_f32(base[(size_t)tok * C + c]) : 0.f;
+            for (int s = 0; s < topk; s++) {
+                const T* Be = B + (size_t)es[s] * R * C + c;
+                float d = 0.f;
+#pragma unroll
+                for (int q = 0; q < R; q++) d = fmaf(hs[s][q], to_f32(Be[(size_t)q * C]), d);
+                o += d;
+            }
+            out[(size_t)tok * C + c] = from_f32<T>(o);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Orthogonality loss, one CTA; thread (r1, r2) accumulates every pair i<j.
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(1024)
+    moe_ortho_kernel(const T* __restrict__ A, float* __restrict__ out, int E, int C, int R) {
+    __shared__ float red[32];
+    float tot = 0.f;
+    for (int idx = threadIdx.x; idx < R * R; idx += blockDim.x) {
+        const int r1 = idx / R, r2 = idx % R;
+        for (int i = 0; i < E; i++)
+            for (int j = i + 1; j < E; j++) {
+                const T* Ai = A + (size_t)i * C * R;
+                const T* Aj = A + (size_t)j * C * R;
+                float s = 0.f;
+                for (int c = 0; c < C; c++) s = fmaf(to_f32(Ai[(size_t)c * R + r1]), to_f32(Aj[(size_t)c * R + r2]), s);
+                tot = fmaf(s, s, tot);
+            }
+    }
+    for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = tot;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float s = 0.f;
+        for (int w = 0; w < (int)(blockDim.x + 31) / 32; w++) s += red[w];
+        *out = s;
+    }
+}
+
+}  // namespace rwkv
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+using namespace rwkv;
+
+static size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+extern "C" size_t rwkv_moe_router_workspace_size(int ntok, int E) {
+    if (ntok <= 0 || E <= 0) return 0;
+    const size_t nb = (size_t)router_ctas(ntok);
+    return align_up(nb * (E + 1) * sizeof(float), 256) + align_up(nb * E * sizeof(int32_t), 256);
+}
+
+template <typename T, int EM>
+static int launch_router(const void* x, const float* gw, const float* bias, float* logits,
+                         int32_t* inds, void* scores, float* pf, int32_t* pc, int ntok, int C,
+                         int E, int topk, cudaStream_t st) {
+    const int nb = router_ctas(ntok);
+    const size_t smem = (size_t)E * C * sizeof(float);
+    auto kern = moe_router_kernel<T, EM>;
+    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (err != cudaSuccess) return set_cuda_error(err);
+    kern<<<nb, ROUTER_WARPS * 32, smem, st>>>((const T*)x, gw, bias, logits, inds, (T*)scores, pf,
+                                              pc, ntok, C, E, topk);
+    return check_launch();
+}
+
+extern "C" int rwkv_moe_router(const void* x, const float* gate_w, const float* bias,
+                               float* logits, int32_t* inds, void* scores, float* stats,
+                               int32_t* counts, void* workspace, size_t workspace_bytes, int ntok,
+                               int C, int E, int topk, int dtype, void* stream) {
+    if (ntok <= 0 || C <= 0 || E <= 0 || E > 32 || topk <= 0 || topk > E || topk > 8)
+        return RWKV_ERR_SHAPE;
+    if (C % 8) return RWKV_ERR_SHAPE;
+    if ((size_t)E * C * sizeof(float) > 200 * 1024) return RWKV_ERR_SHAPE;
+    if (!x || !gate_w || !inds || !scores || !stats || !workspace) return RWKV_ERR_ARG;
+    if (!aligned(x, 16)) return RWKV_ERR_ALIGN;
+    if (workspace_bytes < rwkv_moe_router_workspace_size(ntok, E)) return RWKV_ERR_WORKSPACE;
+    const int nb = router_ctas(ntok);
+    float* pf = (float*)workspace;
+    int32_t* pc = (int32_t*)((char*)workspace + align_up((size_t)nb * (E + 1) * sizeof(float), 256));
+    cudaStream_t st = (cudaStream_t)stream;
+    int rc;
+    RWKV_DISPATCH_DTYPE(dtype, T, {
+        if (E <= 8)
+            rc = launch_router<T, 8>(x, gate_w, bias, logits, inds, scores, pf, pc, ntok, C, E, topk, st);
+        else if (E <= 16)
+            rc = launch_router<T, 16>(x, gate_w, bias, logits, inds, scores, pf, pc, ntok, C, E, topk, st);
+        else
+            rc = launch_router<T, 32>(x, gate_w, bias, logits, inds, scores, pf, pc, ntok, C, E, topk, st);
+    });
+    if (rc) return rc;
+    moe_router_finalize_kernel<<<1, 64, 0, st>>>(pf, pc, nb, ntok, E, topk, stats, counts);
+    return check_launch();
+}
+
+extern "C" size_t rwkv_moe_permute_workspace_size(int n_entries, int E) {
+    if (n_entries <= 0 || E <= 0) return 0;
+    const size_t nb = (size_t)(n_entries + PERM_TILE - 1) / PERM_TILE;
+    return 2 * align_up(nb * E * sizeof(int32_t), 256);
+}
+
+extern "C" int rwkv_moe_permute(const int32_t* inds, int32_t* perm, int32_t* inv,
+                                int32_t* offsets, void* workspace, size_t workspace_bytes,
+                                int ntok, int topk, int E, void* stream) {
+    if (ntok <= 0 || topk <= 0 || E <= 0 || E > 1024) return RWKV_ERR_SHAPE;
+    if ((long long)ntok * topk > 0x7fffffffLL) return RWKV_ERR_SHAPE;
+    if (!inds || !perm || !inv || !offsets || !workspace) return RWKV_ERR_ARG;
+    const int n = ntok * topk;
+    if (workspace_bytes < rwkv_moe_permute_workspace_size(n, E)) return RWKV_ERR_WORKSPACE;
+    const int nb = (n + PERM_TILE - 1) / PERM_TILE;
+    int32_t* blkcnt = (int32_t*)workspace;
+    int32_t* blkoff = (int32_t*)((char*)workspace + align_up((size_t)nb * E * sizeof(int32_t), 256));
+    cudaStream_t st = (cudaStream_t)stream;
+    moe_count_kernel<<<nb, PERM_THREADS, E * sizeof(int), st>>>(inds, n, E, blkcnt);
+    int rc = check_launch();
+    if (rc) return rc;
+    moe_scan_kernel<<<1, 256, E * sizeof(int), st>>>(blkcnt, nb, E, blkoff, offsets);
+    rc = check_launch();
+    if (rc) return rc;
+    moe_scatter_kernel<<<nb, PERM_THREADS, 2 * (PERM_THREADS / 32) * E * sizeof(int), st>>>(
+        inds, n, E, blkoff, perm, inv);
+    return check_launch();
+}
+
+extern "C" int rwkv_moe_lora_down(const void* x, const void* A, const int32_t* perm,
+                                  const int32_t* offsets, float* h, int ntok, int C, int R, int E,
+                                  int topk, int dtype, void* stream) {
+    if (ntok <= 0 || C <= 0 || E <= 0 || E > 256 || topk <= 0) return RWKV_ERR_SHAPE;
+    if (R != 8 && R != 16 && R != 32 && R != 64) return RWKV_ERR_SHAPE;
+    if (!x || !A || !perm || !offsets || !h) return RWKV_ERR_ARG;
+    const int n = ntok * topk;
+    const int grid = (n + 7) / 8 < 148 * 16 ? (n + 7) / 8 : 148 * 16;
+    cudaStream_t st = (cudaStream_t)stream;
+    RWKV_DISPATCH_DTYPE(dtype, T, {
+        switch (R) {
+            case 8: moe_lora_down_kernel<T, 8><<<grid, 256, 0, st>>>((const T*)x, (const T*)A, perm, offsets, h, n, C, E, topk); break;
+            case 16: moe_lora_down_kernel<T, 16><<<grid, 256, 0, st>>>((const T*)x, (const T*)A, perm, offsets, h, n, C, E, topk); break;
+            case 32: moe_lora_down_kernel<T, 32><<<grid, 256, 0, st>>>((const T*)x, (const T*)A, perm, offsets, h, n, C, E, topk); break;
+            default: moe_lora_down_kernel<T, 64><<<grid, 256, 0, st>>>((const T*)x, (const T*)A, perm, offsets, h, n, C, E, topk); break;
+        }
+    });
+    return check_launch();
+}
+
+extern "C" int rwkv_moe_lora_combine(const void* base, const float* h, const void* B,
+                                     const int32_t* inds, const void* scores, const int32_t* inv,
+                                     void* out, int ntok, int C, int R, int E, int topk, int dtype,
+                                     void* stream) {
+    if (ntok <= 0 || C <= 0 || E <= 0 || topk <= 0 || topk > 8) return RWKV_ERR_SHAPE;
+    if (R != 8 && R != 16 && R != 32) return RWKV_ERR_SHAPE;
+    if (!h || !B || !inds || !scores || !inv || !out) return RWKV_ERR_ARG;
+    const int grid = (ntok + 7) / 8 < 148 * 16 ? (ntok + 7) / 8 : 148 * 16;
+    cudaStream_t st = (cudaStream_t)stream;
+    RWKV_DISPATCH_DTYPE(dtype, T, {
+        switch (R) {
+            case 8: moe_combine_kernel<T, 8><<<grid, 256, 0, st>>>((const T*)base, h, (const T*)B, inds, (const T*)scores, inv, (T*)out, ntok, C, topk); break;
+            case 16: moe_combine_kernel<T, 16><<<grid, 256, 0, st>>>((const T*)base, h, (const T*)B, inds, (const T*)scores, inv, (T*)out, ntok, C, topk); break;
+            default: moe_combine_kernel<T, 32><<<grid, 256, 0, st>>>((const T*)base, h, (const T*)B, inds, (const T*)scores, inv, (T*)out, ntok, C, topk); break;
+        }
+    });
+    return check_launch();
+}
+
+extern "C" int rwkv_moe_ortho_loss(const void* A, float* out, int E, int C, int R, int dtype,
+                                   void* stream) {
+    if (E <= 0 || C <= 0 || R <= 0 || R > 64) return RWKV_ERR_SHAPE;
+    if (!A || !out) return RWKV_ERR_ARG;
+    cudaStream_t st = (cudaStream_t)stream;
+    const int threads = R * R < 1024 ? ((R * R + 31) / 32) * 32 : 1024;
+    RWKV_DISPATCH_DTYPE(dtype, T, moe_ortho_kernel<T><<<1, threads, 0, st>>>((const T*)A, out, E, C, R));
+    return check_launch();
+}

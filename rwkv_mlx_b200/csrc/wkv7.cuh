@@ -1,0 +1,29 @@
+// Internal launcher interface of the WKV-7 kernels.
+#pragma once
+#include <cuda_runtime.h>
+
+namespace rwkv {
+
+struct WkvFwdArgs {
+    const void *r, *w, *k, *v, *a, *b;
+    const float* s0;
+    void* y;
+    float *sT, *ckpt, *sa;
+    int B, T, H, dtype, w_dtype, ckpt_len;
+};
+
+struct WkvBwdArgs {
+    const void *r, *w, *k, *v, *a, *b, *dy;
+    const float *s0, *dsT, *ckpt;
+    void *dr, *dw, *dk, *dv, *da, *db;
+    float* ds0;
+    int B, T, H, dtype, w_dtype, ckpt_len;
+};
+
+int wkv7_fwd_seq(const WkvFwdArgs& p, cudaStream_t st);
+int wkv7_bwd_seq(const WkvBwdArgs& p, cudaStream_t st);
+int wkv7_step_launch(float* S, const void* r, const void* w, const void* k, const void* v,
+                     const void* a, const void* b, void* y, int Bs, int H, int dtype, int w_dtype,
+                     int w_mode, cudaStream_t st);
+
+}  // namespace rwkv

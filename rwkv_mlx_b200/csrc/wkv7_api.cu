@@ -1,0 +1,54 @@
+// C ABI entry points for WKV-7 (declared in include/rwkv_b200.h).
+#include "common.cuh"
+#include "wkv7.cuh"
+
+using namespace rwkv;
+
+static int check_dims(int B, int T, int H, int N, int dtype) {
+    if (N != 64) return RWKV_ERR_HEAD_SIZE;
+    if (B <= 0 || T <= 0 || H <= 0) return RWKV_ERR_SHAPE;
+    if ((long long)B * H > 0x7fffffffLL || (long long)B * T * H * N > (1LL << 40)) return RWKV_ERR_SHAPE;
+    if (dtype < RWKV_F32 || dtype > RWKV_BF16) return RWKV_ERR_DTYPE;
+    return RWKV_OK;
+}
+
+extern "C" int rwkv_wkv7_forward(const void* r, const void* w, const void* k, const void* v,
+                                 const void* a, const void* b, const float* s0, void* y,
+                                 float* sT, float* ckpt, float* sa, int B, int T, int H, int N,
+                                 int dtype, int w_dtype, int ckpt_len, void* stream) {
+    int rc = check_dims(B, T, H, N, dtype);
+    if (rc) return rc;
+    if (!r || !w || !k || !v || !a || !b || !y) return RWKV_ERR_ARG;
+    if (ckpt && (ckpt_len < 16 || ckpt_len % 16)) return RWKV_ERR_ARG;
+    WkvFwdArgs p{r, w, k, v, a, b, s0, y, sT, ckpt, sa, B, T, H, dtype, w_dtype, ckpt ? ckpt_len : 16};
+    return wkv7_fwd_seq(p, (cudaStream_t)stream);
+}
+
+extern "C" int rwkv_wkv7_backward(const void* r, const void* w, const void* k, const void* v,
+                                  const void* a, const void* b, const void* dy, const float* s0,
+                                  const float* dsT, const float* ckpt, void* dr, void* dw,
+                                  void* dk, void* dv, void* da, void* db, float* ds0, int B,
+                                  int T, int H, int N, int dtype, int w_dtype, int ckpt_len,
+                                  void* stream) {
+    int rc = check_dims(B, T, H, N, dtype);
+    if (rc) return rc;
+    if (!r || !w || !k || !v || !a || !b || !dy || !dr || !dw || !dk || !dv || !da || !db)
+        return RWKV_ERR_ARG;
+    if (ckpt_len < 16 || ckpt_len % 16) return RWKV_ERR_ARG;
+    if (T > ckpt_len && !ckpt) return RWKV_ERR_ARG;
+    WkvBwdArgs p{r, w, k, v, a, b, dy, s0, dsT, ckpt, dr, dw, dk, dv, da, db, ds0,
+                 B, T, H, dtype, w_dtype, ckpt_len};
+    return wkv7_bwd_seq(p, (cudaStream_t)stream);
+}
+
+extern "C" int rwkv_wkv7_step(float* S, const void* r, const void* w, const void* k,
+                              const void* v, const void* a, const void* b, void* y, int Bs, int H,
+                              int N, int dtype, int w_dtype, int w_mode, void* stream) {
+    int rc = check_dims(Bs, 1, H, N, dtype);
+    if (rc) return rc;
+    if (!S || !r || !w || !k || !v || !a || !b || !y) return RWKV_ERR_ARG;
+    if (w_mode != 0 && w_mode != 1) return RWKV_ERR_ARG;
+    if (!aligned(S, 8)) return RWKV_ERR_ALIGN;
+    return wkv7_step_launch(S, r, w, k, v, a, b, y, Bs, H, dtype, w_dtype, w_mode,
+                            (cudaStream_t)stream);
+}

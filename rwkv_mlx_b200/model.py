@@ -1,0 +1,451 @@
+"""RWKV-v7 model shell on the B200 kernels (the callers of the two hot paths).
+
+Mirrors rwkv_mlx/model.py: ``RWKVConfig`` (:18-64), ``RWKV_Tmix_x070`` (:119-240),
+``RWKV_CMix_x070`` (:243-263), ``Block`` (:266-327), ``RWKV`` with GPT-mode
+``forward`` (:346-375), RNN-mode ``forward_rnn`` (:377-421) and ``init_state``
+(:423-431), plus the weight init of rwkv_mlx/train.py:209-310.  Parameter names
+and shapes follow the reference so its safetensors names map one to one.
+
+The WKV-7 recurrence runs on ``wkv7_recurrent`` / ``wkv7_with_state`` /
+``wkv7_step``; LoRA-MoE ChannelMix on ``LoRAMoE_CMix``.  Dense projections are
+cuBLAS GEMMs through torch.  Additions over the reference: a batched RNN step
+(``forward_rnn_batch``) and a GPT-mode forward that also returns the RNN state
+(``forward_with_state``), so a prompt can be prefilled in parallel and then
+decoded step by step.
+
+``ln_x`` grouping: the reference builds ``nn.GroupNorm(H, C)`` with MLX's default
+``pytorch_compatible=False``; MLX then forms group g from the channels
+c = g (mod H) (strided), not from the contiguous 64 channels of head g.  That is
+the default here (``RWKVConfig.groupnorm = "mlx"``); ``"per_head"`` gives the
+contiguous grouping of upstream RWKV-7 / PyTorch.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from .wkv7 import wkv7_recurrent, wkv7_step, wkv7_with_state
+
+
+@dataclass
+class RWKVConfig:
+    """Same fields and defaults as rwkv_mlx/model.py:18-64 (+ ``groupnorm``)."""
+
+    n_layer: int = 12
+    n_embd: int = 768
+    vocab_size: int = 65568
+    head_size: int = 64
+    ctx_len: int = 4096
+    dim_att: int = 0
+    dim_ffn: int = 0
+    d_decay_lora: int = 0
+    d_aaa_lora: int = 0
+    d_mv_lora: int = 0
+    d_gate_lora: int = 0
+    moe_num_experts: int = 0
+    moe_top_k: int = 2
+    moe_mode: str = "lora"
+    moe_lora_rank: int = 64
+    moe_layers: tuple = ()
+    moe_aux_loss_coeff: float = 0.01
+    moe_z_loss_coeff: float = 0.001
+    moe_ortho_coeff: float = 0.001
+    groupnorm: str = "mlx"
+
+    def __post_init__(self):
+        if self.dim_att <= 0:
+            self.dim_att = self.n_embd
+        if self.dim_ffn <= 0:
+            self.dim_ffn = int((self.n_embd * 3.5) // 32 * 32)
+
+    @property
+    def n_head(self) -> int:
+        return self.dim_att // self.head_size
+
+    def lora_dim(self, kind: str) -> int:
+        C = self.n_embd
+        if kind == "decay":
+            return self.d_decay_lora or max(32, int(round((2.5 * (C ** 0.5)) / 32) * 32))
+        if kind == "aaa":
+            return self.d_aaa_lora or max(32, int(round((2.5 * (C ** 0.5)) / 32) * 32))
+        if kind == "mv":
+            return self.d_mv_lora or max(32, int(round((1.7 * (C ** 0.5)) / 32) * 32))
+        if kind == "gate":
+            return self.d_gate_lora or max(32, int(round((5.0 * (C ** 0.5)) / 32) * 32))
+        raise ValueError(f"Unknown LoRA kind: {kind}")
+
+
+def time_shift(x: torch.Tensor) -> torch.Tensor:
+    """Prepend a zero row along T and drop the last (model.py:67-75)."""
+    return F.pad(x, (0, 0, 1, -1))
+
+
+class GroupNormMLX(nn.Module):
+    """GroupNorm over (N, C) with MLX's grouping (see the module docstring)."""
+
+    def __init__(self, num_groups: int, dims: int, eps: float = 1e-5, mode: str = "mlx"):
+        super().__init__()
+        self.num_groups, self.dims, self.eps, self.mode = num_groups, dims, eps, mode
+        self.weight = nn.Parameter(torch.ones(dims))
+        self.bias = nn.Parameter(torch.zeros(dims))
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        n, C = x.shape
+        G = self.num_groups
+        xf = x.float()
+        if self.mode == "mlx":
+            xg = xf.view(n, C // G, G)
+            mean = xg.mean(1, keepdim=True)
+            var = xg.var(1, unbiased=False, keepdim=True)
+        else:
+            xg = xf.view(n, G, C // G)
+            mean = xg.mean(2, keepdim=True)
+            var = xg.var(2, unbiased=False, keepdim=True)
+        y = ((xg - mean) * torch.rsqrt(var + self.eps)).view(n, C)
+        return (y * self.weight.float() + self.bias.float()).to(x.dtype)
+
+
+class RWKV_Tmix_x070(nn.Module):
+    """Time mixing (model.py:119-240)."""
+
+    def __init__(self, config: RWKVConfig, layer_id: int):
+        super().__init__()
+        self.config, self.layer_id = config, layer_id
+        self.head_size, self.n_head = config.head_size, config.n_head
+        C, H, N = config.n_embd, config.n_head, config.head_size
+        z = lambda *s: nn.Parameter(torch.zeros(*s))
+        self.x_r, self.x_w, self.x_k, self.x_v, self.x_a, self.x_g = (z(1, 1, C) for _ in range(6))
+        D = config.lora_dim("decay")
+        self.w0, self.w1, self.w2 = z(1, 1, C), z(C, D), z(D, C)
+        D = config.lora_dim("aaa")
+        self.a0, self.a1, self.a2 = z(1, 1, C), z(C, D), z(D, C)
+        D = config.lora_dim("mv")
+        self.v0, self.v1, self.v2 = z(1, 1, C), z(C, D), z(D, C)
+        D = config.lora_dim("gate")
+        self.g1, self.g2 = z(C, D), z(D, C)
+        self.k_k, self.k_a, self.r_k = z(1, 1, C), z(1, 1, C), z(H, N)
+        self.receptance = nn.Linear(C, C, bias=False)
+        self.key = nn.Linear(C, C, bias=False)
+        self.value = nn.Linear(C, C, bias=False)
+        self.output = nn.Linear(C, C, bias=False)
+        self.ln_x = GroupNormMLX(H, C, eps=64e-5, mode=config.groupnorm)
+
+    def _project(self, x, xx, v_first):
+        """Shared by GPT and RNN mode: returns r, w(log-log), k, v, a, g, kk, v_first."""
+        H, N = self.n_head, self.head_size
+        xr, xw, xk = x + xx * self.x_r, x + xx * self.x_w, x + xx * self.x_k
+        xv, xa, xg = x + xx * self.x_v, x + xx * self.x_a, x + xx * self.x_g
+        r = self.receptance(xr)
+        w = -F.softplus(-(self.w0 + torch.tanh(xw @ self.w1) @ self.w2)) - 0.5
+        k = self.key(xk)
+        v = self.value(xv)
+        if self.layer_id == 0:
+            v_first = v
+        else:
+            v = v + (v_first - v) * torch.sigmoid(self.v0 + (xv @ self.v1) @ self.v2)
+        a = torch.sigmoid(self.a0 + (xa @ self.a1) @ self.a2)
+        g = torch.sigmoid(xg @ self.g1) @ self.g2
+        kk = k * self.k_k
+        kk_h = kk.view(*kk.shape[:-1], H, N)
+        kk = (kk_h / (torch.sqrt((kk_h * kk_h).sum(-1, keepdim=True)) + 1e-12)).view(kk.shape)
+        k = k * (1 + (a - 1) * self.k_a)
+        return r, w, k, v, a, g, kk, v_first
+
+    def _post(self, y, r, k, v, g):
+        H, N = self.n_head, self.head_size
+        shp = y.shape
+        C = shp[-1]
+        y = self.ln_x(y.reshape(-1, C)).view(shp)
+        rh, kh, vh = r.view(*shp[:-1], H, N), k.view(*shp[:-1], H, N), v.view(*shp[:-1], H, N)
+        bonus = ((rh * kh * self.r_k).sum(-1, keepdim=True) * vh).view(shp)
+        y = y + bonus
+        return self.output((y * g).to(self.output.weight.dtype))
+
+    def forward(self, x, v_first, s0=None, return_state=False):
+        xx = time_shift(x) - x
+        r, w, k, v, a, g, kk, v_first = self._project(x, xx, v_first)
+        if return_state or s0 is not None:
+            y, sT = wkv7_with_state(r, w, k, v, -kk, kk * a, s0=s0, head_size=self.head_size)
+        else:
+            y, sT = wkv7_recurrent(r, w, k, v, -kk, kk * a, self.head_size), None
+        out = self._post(y, r, k, v, g)
+        return (out, v_first, sT) if return_state else (out, v_first)
+
+    def forward_rnn(self, x, x_prev, v_first, state):
+        """Batched RNN step (model.py:441-495): x, x_prev (Bs, C); state (Bs,H,N,N)
+        fp32 updated in place.  Returns (out, x, state, v_first)."""
+        # run the GPT-mode projections on (Bs, 1, C) so parameter broadcasting matches
+        xx = (x_prev - x)[:, None]
+        r, w, k, v, a, g, kk, v_first = self._project(x[:, None], xx, v_first[:, None])
+        # model.py:475-477 forms the decay as exp(-0.606531*sigmoid(w0 + w_lora)); that is
+        # exp(-exp(w)) of GPT mode's w = -softplus(-(w0 + w_lora)) - 0.5, which the kernel
+        # evaluates (the constant differs from e^-0.5 by 6e-8)
+        y = wkv7_step(state, r, w, k, v, -kk, kk * a, w_is_decay=False)
+        out = self._post(y.view(r.shape), r, k, v, g)
+        return out[:, 0], x, state, v_first[:, 0]
+
+
+class RWKV_CMix_x070(nn.Module):
+    """Channel mixing (model.py:243-263)."""
+
+    def __init__(self, config: RWKVConfig, layer_id: int):
+        super().__init__()
+        self.config, self.layer_id = config, layer_id
+        C = config.n_embd
+        self.x_k = nn.Parameter(torch.zeros(1, 1, C))
+        self.key = nn.Linear(C, config.dim_ffn, bias=False)
+        self.value = nn.Linear(config.dim_ffn, C, bias=False)
+
+    def forward(self, x):
+        xx = time_shift(x) - x
+        k = x + xx * self.x_k
+        k = torch.relu(self.key(k)) ** 2
+        return self.value(k)
+
+    def forward_rnn(self, x, x_prev):
+        """model.py:498-506 (batched)."""
+        xx = x_prev - x
+        k = x + xx * self.x_k.view(-1)
+        k = torch.relu(self.key(k)) ** 2
+        return self.value(k), x
+
+
+class Block(nn.Module):
+    """LayerNorm -> TimeMix -> LayerNorm -> ChannelMix / LoRA-MoE (model.py:266-327)."""
+
+    def __init__(self, config: RWKVConfig, layer_id: int):
+        super().__init__()
+        self.config, self.layer_id = config, layer_id
+        self.is_moe = False
+        C = config.n_embd
+        if layer_id == 0:
+            self.ln0 = nn.LayerNorm(C)
+        self.ln1 = nn.LayerNorm(C)
+        self.ln2 = nn.LayerNorm(C)
+        self.att = RWKV_Tmix_x070(config, layer_id)
+        use_moe = config.moe_num_experts > 0 and (not config.moe_layers or layer_id in config.moe_layers)
+        if use_moe:
+            if config.moe_mode != "lora":
+                raise NotImplementedError("full-expert MoE_CMix is not implemented")
+            from .moe import LoRAMoE_CMix
+
+            self.is_moe = True
+            self.ffn = LoRAMoE_CMix(RWKV_CMix_x070(config, layer_id), config.moe_num_experts,
+                                    config.moe_lora_rank, config.moe_top_k)
+        else:
+            self.ffn = RWKV_CMix_x070(config, layer_id)
+
+    def forward(self, x, v_first, s0=None, return_state=False):
+        if self.layer_id == 0:
+            x = self.ln0(x)
+        x1 = self.ln1(x)
+        res = self.att(x1, v_first, s0=s0, return_state=return_state)
+        x_attn, v_first = res[0], res[1]
+        x = x + x_attn
+        x2 = self.ln2(x)
+        extra = {}
+        if return_state:
+            extra = {"att_x_prev": x1[:, -1], "att_state": res[2], "ffn_x_prev": x2[:, -1]}
+        if self.is_moe:
+            ffn_out, aux, z = self.ffn(x2)
+            x = x + ffn_out
+            return x, v_first, (aux, z, self.ffn.orthogonal_loss()), extra
+        x = x + self.ffn(x2)
+        return x, v_first, None, extra
+
+
+class RWKV(nn.Module):
+    """RWKV-v7 language model (model.py:330-431)."""
+
+    def __init__(self, config: RWKVConfig):
+        super().__init__()
+        self.config = config
+        self.emb = nn.Embedding(config.vocab_size, config.n_embd)
+        self.blocks = nn.ModuleList([Block(config, i) for i in range(config.n_layer)])
+        self.ln_out = nn.LayerNorm(config.n_embd)
+        self.head = nn.Linear(config.n_embd, config.vocab_size, bias=False)
+
+    def _run(self, idx, return_state=False):
+        x = self.emb(idx)
+        v_first = torch.zeros_like(x)
+        aux_loss = torch.zeros((), device=x.device, dtype=torch.float32)
+        cfg = self.config
+        states = []
+        for blk in self.blocks:
+            x, v_first, moe, extra = blk(x, v_first, return_state=return_state)
+            if moe is not None:
+                aux, z, ortho = moe
+                aux_loss = aux_loss + cfg.moe_aux_loss_coeff * aux + cfg.moe_z_loss_coeff * z \
+                    + cfg.moe_ortho_coeff * ortho
+            if return_state:
+                states.append(extra)
+        x = self.ln_out(x)
+        return self.head(x), aux_loss, states
+
+    def forward(self, idx):
+        """GPT mode: idx (B, T) -> (logits (B, T, V), aux_loss)  (model.py:346-375)."""
+        logits, aux, _ = self._run(idx)
+        return logits, aux
+
+    def forward_with_state(self, idx):
+        """GPT-mode prefill that also returns the RNN state after the last token,
+        as a list of per-layer dicts {att_x_prev (B,C), att_state (B,H,N,N) fp32,
+        ffn_x_prev (B,C)} for :meth:`forward_rnn_batch`."""
+        logits, aux, states = self._run(idx, return_state=True)
+        return logits, aux, states
+
+    # ---- RNN mode --------------------------------------------------------
+    def init_state(self, batch: int | None = None):
+        """Zero state.  ``batch=None``: the reference's flat list layout
+        [att_x_prev (C), att_state (H,N,N), ffn_x_prev (C)] * n_layer (model.py:423-431);
+        otherwise per-layer dicts with a leading batch dimension."""
+        cfg = self.config
+        dev = self.emb.weight.device
+        dt = self.emb.weight.dtype
+        C, H, N = cfg.n_embd, cfg.n_head, cfg.head_size
+        if batch is None:
+            st = []
+            for _ in range(cfg.n_layer):
+                st += [torch.zeros(C, device=dev, dtype=dt),
+                       torch.zeros(H, N, N, device=dev, dtype=torch.float32),
+                       torch.zeros(C, device=dev, dtype=dt)]
+            return st
+        return [{"att_x_prev": torch.zeros(batch, C, device=dev, dtype=dt),
+                 "att_state": torch.zeros(batch, H, N, N, device=dev, dtype=torch.float32),
+                 "ffn_x_prev": torch.zeros(batch, C, device=dev, dtype=dt)} for _ in range(cfg.n_layer)]
+
+    def forward_rnn_batch(self, tokens: torch.Tensor, states: list):
+        """One decode step for a batch of sequences: tokens (Bs,) -> logits (Bs, V).
+        ``states`` (per-layer dicts) is updated in place."""
+        x = self.emb(tokens)
+        v_first = torch.zeros_like(x)
+        for i, blk in enumerate(self.blocks):
+            if i == 0:
+                x = blk.ln0(x)
+            xx = blk.ln1(x)
+            st = states[i]
+            out, st["att_x_prev"], st["att_state"], v_first = blk.att.forward_rnn(
+                xx, st["att_x_prev"], v_first, st["att_state"])
+            x = x + out
+            xx = blk.ln2(x)
+            if blk.is_moe:
+                # the reference's RNN path cannot run MoE layers (model.py:498-506 reads
+                # ffn.x_k / ffn.key); here the LoRA-MoE layer runs on the single token
+                ffn = blk.ffn
+                base, _ = ffn.base.forward_rnn(xx, st["ffn_x_prev"])
+                delta = _moe_rnn(ffn, xx)
+                st["ffn_x_prev"] = xx
+                x = x + base + delta
+            else:
+                out, st["ffn_x_prev"] = blk.ffn.forward_rnn(xx, st["ffn_x_prev"])
+                x = x + out
+        x = self.ln_out(x)
+        return self.head(x)
+
+    def forward_rnn(self, token: int, state: list):
+        """Mirror of model.py:377-421 for one sequence: returns (logits (V,), state)."""
+        cfg = self.config
+        states = []
+        for i in range(cfg.n_layer):
+            states.append({"att_x_prev": state[3 * i].view(1, -1),
+                           "att_state": state[3 * i + 1].view(1, cfg.n_head, cfg.head_size, cfg.head_size).contiguous(),
+                           "ffn_x_prev": state[3 * i + 2].view(1, -1)})
+        tok = torch.tensor([int(token)], device=self.emb.weight.device)
+        logits = self.forward_rnn_batch(tok, states)
+        new = []
+        for st in states:
+            new += [st["att_x_prev"].view(-1), st["att_state"].view(cfg.n_head, cfg.head_size, cfg.head_size),
+                    st["ffn_x_prev"].view(-1)]
+        return logits.view(-1), new
+
+
+def _moe_rnn(ffn, x):
+    from .moe import lora_combine, lora_down, permute, router_forward
+
+    r = router_forward(x.contiguous(), ffn.router.gate.weight, ffn.top_k, ffn.router.bias)
+    perm, inv, off = permute(r["inds"], ffn.n_experts)
+    h = lora_down(x.contiguous(), ffn.lora_A.detach(), perm, off, ffn.top_k)
+    return lora_combine(None, h, ffn.lora_B.detach(), r["inds"], r["scores"], inv)
+
+
+# ---------------------------------------------------------------------------
+# Weight init (rwkv_mlx/train.py:209-310)
+# ---------------------------------------------------------------------------
+def _ortho(shape, scale, gen, device):
+    rows, cols = shape
+    flat = torch.randn(rows, cols, generator=gen, device=device, dtype=torch.float32)
+    q, _ = torch.linalg.qr(flat if rows >= cols else flat.T)
+    q = q.T if rows < cols else q
+    q = q[:rows, :cols]
+    gain = math.sqrt(rows / cols) if rows > cols else 1.0
+    return q * gain * scale
+
+
+@torch.no_grad()
+def init_weights(model: RWKV, seed: int = 0):
+    """Random init following train.py:209-310 (fp32 values)."""
+    cfg = model.config
+    C, H, N, L = cfg.n_embd, cfg.n_head, cfg.head_size, cfg.n_layer
+    dev = model.emb.weight.device
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    model.emb.weight.uniform_(-1e-4, 1e-4, generator=gen)
+    V = cfg.vocab_size
+    h_scale = 0.5 * math.sqrt(V / C) if V > C else 0.5
+    model.head.weight.copy_(_ortho(model.head.weight.shape, h_scale, gen, dev))
+    ar = torch.arange(C, device=dev, dtype=torch.float32)
+    for lid, blk in enumerate(model.blocks):
+        att = blk.att
+        r01 = lid / (L - 1) if L > 1 else 0.0
+        r1a0 = 1.0 - lid / L
+        ddd = ar / C
+        att.x_r.copy_((1.0 - ddd ** (0.2 * r1a0)).view(1, 1, C))
+        att.x_w.copy_((1.0 - ddd ** (0.9 * r1a0)).view(1, 1, C))
+        att.x_k.copy_((1.0 - ddd ** (0.7 * r1a0)).view(1, 1, C))
+        att.x_v.copy_((1.0 - ddd ** (0.7 * r1a0)).view(1, 1, C))
+        att.x_a.copy_((1.0 - ddd ** (0.9 * r1a0)).view(1, 1, C))
+        att.x_g.copy_((1.0 - ddd ** (0.2 * r1a0)).view(1, 1, C))
+        linear = ar / (C - 1) - 0.5
+        n = torch.arange(C, device=dev, dtype=torch.float32) % N
+        zig = (n - (N - 1) / 2) / ((N - 1) / 2)
+        zig = zig * zig.abs()
+        www = -6 + 6 * (ar / (C - 1)) ** (1 + r01 ** 0.3)
+        att.w0.copy_((www + 0.5 + zig * 2.5).view(1, 1, C))
+        att.w1.zero_()
+        att.w2.copy_(_ortho(att.w2.shape, 0.1, gen, dev))
+        att.a0.copy_((-0.19 + zig * 0.3 + linear * 0.4).view(1, 1, C))
+        att.a1.zero_()
+        att.a2.copy_(_ortho(att.a2.shape, 0.1, gen, dev))
+        att.v0.copy_((0.73 - linear * 0.4).view(1, 1, C))
+        att.v1.zero_()
+        att.v2.copy_(_ortho(att.v2.shape, 0.1, gen, dev))
+        att.g1.zero_()
+        att.g2.copy_(_ortho(att.g2.shape, 0.1, gen, dev))
+        att.k_k.copy_((0.71 - linear * 0.1).view(1, 1, C))
+        att.k_a.fill_(1.02)
+        att.r_k.fill_(-0.04)
+        att.receptance.weight.copy_(_ortho(att.receptance.weight.shape, 1.0, gen, dev))
+        att.key.weight.copy_(_ortho(att.key.weight.shape, 0.1, gen, dev))
+        att.value.weight.copy_(_ortho(att.value.weight.shape, 1.0, gen, dev))
+        att.output.weight.zero_()
+        att.ln_x.weight.fill_(((1 + lid) / L) ** 0.7)
+        ffn = blk.ffn.base if blk.is_moe else blk.ffn
+        ffn.x_k.copy_((1.0 - ddd ** ((1.0 - lid / L) ** 4)).view(1, 1, C))
+        ffn.key.weight.copy_(_ortho(ffn.key.weight.shape, 1.0, gen, dev))
+        ffn.value.weight.zero_()
+    return model
+
+
+def cast_for_inference(model: RWKV, dtype=torch.float16) -> RWKV:
+    """Cast every parameter to ``dtype`` except the decay biases ``w0`` (kept fp32,
+    as the reference's converter does, convert.py:80-91)."""
+    for name, p in model.named_parameters():
+        if name.endswith(".w0"):
+            p.data = p.data.float()
+        else:
+            p.data = p.data.to(dtype)
+    return model

@@ -1,0 +1,140 @@
+"""LoRA-MoE CUDA kernels vs the numpy oracle of rwkv_mlx/moe.py (need a B200).
+
+Routing indices and the permutation are compared bit-exactly; the router is fed
+identical fp32 logits on both sides (the GPU's own logits) so that GEMM rounding
+cannot flip a near-tie.  Float outputs: relative-to-RMS 2e-3 for fp16.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import moe_oracle as mo
+from tests.inputs import rel_rms
+
+pytestmark = pytest.mark.gpu
+
+
+def _x(ntok, C, seed, dt=torch.float16):
+    rng = np.random.default_rng(seed)
+    return torch.tensor(rng.standard_normal((ntok, C)), dtype=dt, device="cuda")
+
+
+@pytest.mark.parametrize("E,k,with_bias", [(8, 2, False), (8, 2, True), (4, 1, False), (16, 3, False), (32, 4, True)])
+def test_router_bit_exact_indices(E, k, with_bias):
+    from rwkv_mlx_b200.moe import router_forward
+
+    ntok, C = 3000, 768
+    x = _x(ntok, C, E * 10 + k)
+    rng = np.random.default_rng(E)
+    gw = torch.tensor(rng.standard_normal((E, C)) * 0.02, dtype=torch.float32, device="cuda")
+    bias = torch.tensor(rng.normal(0, 1.5, E), dtype=torch.float32, device="cuda") if with_bias else None
+    r = router_forward(x, gw, k, bias, want_logits=True)
+    torch.cuda.synchronize()
+    lg = r["logits"].cpu().numpy()
+    # logits themselves: fp32 GEMM, different summation order
+    ref_lg = mo.gate_logits(x.cpu().numpy(), gw.cpu().numpy(), None if bias is None else bias.cpu().numpy())
+    assert np.max(np.abs(lg - ref_lg)) < 1e-4 * max(1.0, np.abs(ref_lg).max())
+    inds, scores, aux, z, f = mo.router(None, None, k, logits=lg)
+    np.testing.assert_array_equal(r["inds"].cpu().numpy(), inds)
+    assert rel_rms(r["scores"].double().cpu().numpy(), scores) < 2e-3
+    assert abs(float(r["aux"]) - aux) < 1e-4 * max(1, abs(aux))
+    assert abs(float(r["z"]) - z) < 1e-4 * max(1, abs(z))
+    np.testing.assert_allclose(r["f"].cpu().numpy(), f, rtol=1e-6)
+    np.testing.assert_array_equal(r["counts"].cpu().numpy(), np.bincount(inds.reshape(-1), minlength=E))
+
+
+def test_router_ties_go_to_lower_id():
+    from rwkv_mlx_b200.moe import router_forward
+
+    C, E = 64, 8
+    x = torch.zeros(40, C, dtype=torch.float16, device="cuda")
+    x[20:] = 1.0
+    gw = torch.zeros(E, C, device="cuda")
+    gw[5] = 1.0 / C
+    gw[6] = 1.0 / C  # experts 5 and 6 tie for tokens 20..39
+    r = router_forward(x, gw, 2)
+    inds = r["inds"].cpu().numpy()
+    assert (inds[:20] == [0, 1]).all()  # all logits 0: lowest ids
+    assert (inds[20:] == [5, 6]).all()
+
+
+@pytest.mark.parametrize("ntok,k,E", [(1, 1, 8), (5000, 2, 8), (4097, 3, 5), (70000, 2, 64)])
+def test_permute_bit_exact(ntok, k, E):
+    from rwkv_mlx_b200.moe import permute
+
+    rng = np.random.default_rng(ntok)
+    # skewed load, empty experts included
+    p = rng.dirichlet(np.ones(E) * 0.3)
+    inds = rng.choice(E, size=(ntok, k), p=p).astype(np.int32)
+    perm, inv, off = permute(torch.tensor(inds, device="cuda"), E)
+    flat = inds.reshape(-1)
+    ref_perm = np.argsort(flat, kind="stable")
+    np.testing.assert_array_equal(perm.cpu().numpy(), ref_perm)
+    ref_inv = np.empty_like(ref_perm)
+    ref_inv[ref_perm] = np.arange(len(ref_perm))
+    np.testing.assert_array_equal(inv.cpu().numpy(), ref_inv)
+    np.testing.assert_array_equal(off.cpu().numpy(), np.concatenate([[0], np.cumsum(np.bincount(flat, minlength=E))]))
+
+
+@pytest.mark.parametrize("R", [8, 16, 32])
+def test_lora_down_and_combine(R):
+    from rwkv_mlx_b200.moe import lora_combine, lora_down, permute, router_forward
+
+    ntok, C, E, k = 2000, 768, 8, 2
+    x = _x(ntok, C, 3)
+    rng = np.random.default_rng(R)
+    A = torch.tensor(rng.normal(0, 0.02, (E, C, R)), dtype=torch.float16, device="cuda")
+    Bw = torch.tensor(rng.normal(0, 0.02, (E, R, C)), dtype=torch.float16, device="cuda")
+    gw = torch.tensor(rng.standard_normal((E, C)) * 0.02, dtype=torch.float32, device="cuda")
+    base = _x(ntok, C, 4)
+    r = router_forward(x, gw, k)
+    perm, inv, off = permute(r["inds"], E)
+    h = lora_down(x, A, perm, off, k)
+    out = lora_combine(base, h, Bw, r["inds"], r["scores"], inv)
+    torch.cuda.synchronize()
+    xn, An, Bn = x.double().cpu().numpy(), A.double().cpu().numpy(), Bw.double().cpu().numpy()
+    inds, sc = r["inds"].cpu().numpy(), r["scores"].double().cpu().numpy()
+    # h in sorted order
+    ent = perm.cpu().numpy()
+    tok = ent // k
+    e_of = inds.reshape(-1)[ent]
+    h_ref = np.einsum("pc,pcr->pr", xn[tok], An[e_of])
+    assert rel_rms(h.cpu().numpy(), h_ref) < 1e-5
+    ref = base.double().cpu().numpy() + mo.lora_moe_delta(xn, An, Bn, inds, sc)
+    assert rel_rms(out.double().cpu().numpy(), ref) < 2e-3
+
+
+def test_lora_moe_cmix_module_matches_oracle():
+    from rwkv_mlx_b200.model import RWKV_CMix_x070, RWKVConfig
+    from rwkv_mlx_b200.moe import LoRAMoE_CMix
+
+    torch.manual_seed(0)
+    cfg = RWKVConfig(n_layer=2, n_embd=256, dim_ffn=512)
+    base = RWKV_CMix_x070(cfg, 1).cuda()
+    with torch.no_grad():
+        base.x_k.uniform_(0, 1)
+        base.key.weight.normal_(0, 0.05)
+        base.value.weight.normal_(0, 0.05)
+    m = LoRAMoE_CMix(base, n_experts=8, lora_rank=16, top_k=2).cuda()
+    with torch.no_grad():
+        m.lora_A.normal_(0, 0.02)
+        m.lora_B.normal_(0, 0.02)
+        m.router.gate.weight.normal_(0, 0.05)
+    m = m.half()
+    x = torch.randn(2, 64, 256, device="cuda").half()
+    with torch.no_grad():
+        out, aux, z = m(x)
+        lg = (x.float().reshape(-1, 256) @ m.router.gate.weight.float().T).cpu().numpy()
+    xn = x.double().cpu().numpy()
+    base_ref = mo.cmix(xn, base.x_k.double().cpu().numpy(), base.key.weight.double().cpu().numpy(),
+                       base.value.weight.double().cpu().numpy())
+    inds, sc, aux_r, z_r, _ = mo.router(None, None, 2, logits=lg)
+    ref = base_ref + mo.lora_moe_delta(xn, m.lora_A.double().cpu().numpy(), m.lora_B.double().cpu().numpy(),
+                                       inds.reshape(2, 64, 2), sc.reshape(2, 64, 2))
+    assert rel_rms(out.double().cpu().numpy(), ref) < 3e-3
+    assert abs(float(aux) - aux_r) < 1e-3
+    assert abs(float(z) - z_r) < 1e-3 * max(1, z_r)
+    ol = m.orthogonal_loss()
+    ol_ref = mo.orthogonal_loss(m.lora_A.double().cpu().numpy())
+    assert abs(float(ol) - ol_ref) < 1e-3 * max(1e-6, ol_ref)

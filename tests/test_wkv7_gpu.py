@@ -1,0 +1,169 @@
+"""WKV-7 CUDA kernels vs the float64 oracle (parity tests proper; need a B200).
+
+Tolerances are relative to the RMS of the oracle output:
+  fp32 inputs 2e-5, fp16 inputs 2e-3 (the north-star bound for fp16 inputs with
+  fp32 state), bf16 inputs 6e-3 (bf16 output rounding alone is ~2e-3).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import wkv7_oracle as wo
+from tests.inputs import rel_rms, wkv_inputs
+
+pytestmark = pytest.mark.gpu
+
+TOL = {torch.float32: 2e-5, torch.float16: 2e-3, torch.bfloat16: 6e-3}
+
+
+def _dev(x, dt):
+    return torch.tensor(np.ascontiguousarray(x), dtype=dt, device="cuda")
+
+
+def _bt(x):  # (B,T,H,N) -> (B,T,C)
+    return x.reshape(x.shape[0], x.shape[1], -1)
+
+
+def _rounded(inp, dt, w_dt=None):
+    """Device tensors in dt (w in w_dt) and the float64 values they hold."""
+    dev, host = {}, {}
+    for n, x in inp.items():
+        t = _dev(_bt(x), w_dt if (n == "w" and w_dt is not None) else dt)
+        dev[n] = t
+        host[n] = t.double().cpu().numpy().reshape(x.shape)
+    return dev, host
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("B,T,H", [(1, 256, 4), (2, 100, 3), (1, 17, 1)])
+def test_forward_matches_oracle(dt, B, T, H):
+    from rwkv_mlx_b200 import wkv7
+
+    d, h = _rounded(wkv_inputs(B, T, H, seed=B * 1000 + T), dt)
+    y, s, sa = wkv7.wkv7_forward(d["r"], d["w"], d["k"], d["v"], d["a"], d["b"])
+    torch.cuda.synchronize()
+    ye, sae, _, states = wo.wkv7_forward_exact(h["r"], h["w"], h["k"], h["v"], h["a"], h["b"], keep_states=True)
+    assert rel_rms(y.double().cpu().numpy(), _bt(ye)) < TOL[dt]
+    assert rel_rms(sa.cpu().numpy(), sae) < max(TOL[dt], 1e-5)
+    if T >= 16:
+        ck = wo.checkpoints_from_states(states, 16).reshape(-1)
+        assert rel_rms(s.cpu().numpy(), ck) < 1e-5
+
+
+def test_forward_fp32_decay_with_fp16_inputs():
+    """w in fp32 with the other inputs in fp16 (what the model feeds)."""
+    from rwkv_mlx_b200 import wkv7
+
+    d, h = _rounded(wkv_inputs(2, 128, 2, seed=7), torch.float16, w_dt=torch.float32)
+    assert d["w"].dtype == torch.float32
+    y = wkv7.wkv7(d["r"], d["w"], d["k"], d["v"], d["a"], d["b"])
+    ye = wo.wkv7_forward_exact(h["r"], h["w"], h["k"], h["v"], h["a"], h["b"])[0]
+    assert rel_rms(y.double().cpu().numpy(), _bt(ye)) < TOL[torch.float16]
+
+
+def test_state_in_out_composes():
+    """Running T as two halves with the state handed over equals one pass."""
+    from rwkv_mlx_b200 import wkv7
+
+    d, h = _rounded(wkv_inputs(2, 96, 2, seed=3), torch.float32)
+    y, sT = wkv7.wkv7_with_state(d["r"], d["w"], d["k"], d["v"], d["a"], d["b"])
+    half = {n: t[:, :40] for n, t in d.items()}
+    rest = {n: t[:, 40:] for n, t in d.items()}
+    y1, s1 = wkv7.wkv7_with_state(half["r"], half["w"], half["k"], half["v"], half["a"], half["b"])
+    y2, s2 = wkv7.wkv7_with_state(rest["r"], rest["w"], rest["k"], rest["v"], rest["a"], rest["b"], s0=s1)
+    torch.testing.assert_close(torch.cat([y1, y2], 1), y, rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(s2, sT, rtol=1e-5, atol=1e-5)
+    _, _, sTe, _ = wo.wkv7_forward_exact(h["r"], h["w"], h["k"], h["v"], h["a"], h["b"])
+    assert rel_rms(sT.cpu().numpy(), sTe) < 1e-5
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.float16])
+@pytest.mark.parametrize("B,T,H", [(1, 256, 4), (2, 72, 2), (1, 9, 1)])
+def test_backward_matches_exact_oracle(dt, B, T, H):
+    from rwkv_mlx_b200 import wkv7
+
+    inp = wkv_inputs(B, T, H, seed=11 + T)
+    d, h = _rounded(inp, dt)
+    y, s, sa = wkv7.wkv7_forward(d["r"], d["w"], d["k"], d["v"], d["a"], d["b"])
+    grads = wkv7.wkv7_backward(d["r"], d["w"], d["k"], d["v"], d["a"], d["b"], d["dy"], s, sa)
+    torch.cuda.synchronize()
+    ge = wo.wkv7_backward_exact(h["r"], h["w"], h["k"], h["v"], h["a"], h["b"], h["dy"])
+    for name, g, e in zip(["dr", "dw", "dk", "dv", "da", "db"], grads, ge[:6]):
+        err = rel_rms(g.double().cpu().numpy(), _bt(e))
+        assert err < TOL[dt], f"{name}: {err}"
+
+
+def test_autograd_function_and_state_grads():
+    from rwkv_mlx_b200 import wkv7
+
+    d, h = _rounded(wkv_inputs(1, 48, 2, seed=5), torch.float32)
+    leaves = {n: d[n].clone().requires_grad_(True) for n in "rwkvab"}
+    y = wkv7.wkv7_recurrent(*[leaves[n] for n in "rwkvab"])
+    y.backward(d["dy"])
+    ge = wo.wkv7_backward_exact(h["r"], h["w"], h["k"], h["v"], h["a"], h["b"], h["dy"])
+    for n, e in zip("rwkvab", ge[:6]):
+        assert rel_rms(leaves[n].grad.double().cpu().numpy(), _bt(e)) < 2e-5, n
+
+
+def test_backward_with_initial_state_and_state_grad():
+    from rwkv_mlx_b200 import wkv7
+
+    B, T, H = 1, 40, 2
+    d, h = _rounded(wkv_inputs(B, T, H, seed=21), torch.float32)
+    rng = np.random.default_rng(1)
+    s0 = rng.standard_normal((B, H, 64, 64)) * 0.3
+    dsT = rng.standard_normal((B, H, 64, 64)) * 0.1
+    s0d, dsTd = _dev(s0, torch.float32), _dev(dsT, torch.float32)
+    _, ck, _, _ = wkv7._fwd(d["r"], d["w"], d["k"], d["v"], d["a"], d["b"], s0=s0d)
+    grads, ds0 = wkv7._bwd(d["r"], d["w"], d["k"], d["v"], d["a"], d["b"], d["dy"], ck,
+                           s0=s0d, dsT=dsTd, want_ds0=True)
+    ge = wo.wkv7_backward_exact(h["r"], h["w"], h["k"], h["v"], h["a"], h["b"], h["dy"], s0=s0, dsT=dsT)
+    for name, g, e in zip(["dr", "dw", "dk", "dv", "da", "db"], grads, ge[:6]):
+        assert rel_rms(g.double().cpu().numpy(), _bt(e)) < 2e-5, name
+    assert rel_rms(ds0.cpu().numpy(), ge[6]) < 2e-5
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.float16])
+def test_step_matches_oracle(dt):
+    from rwkv_mlx_b200 import wkv7
+
+    rng = np.random.default_rng(4)
+    Bs, H = 5, 3
+    S0 = rng.standard_normal((Bs, H, 64, 64))
+    inp = {n: rng.standard_normal((Bs, H, 64)) for n in "rkv"}
+    kk = rng.standard_normal((Bs, H, 64))
+    kk /= np.linalg.norm(kk, axis=-1, keepdims=True)
+    inp["a"], inp["b"] = -kk, kk * 0.6
+    inp["w"] = np.exp(-0.606531 / (1 + np.exp(-rng.standard_normal((Bs, H, 64)))))
+    S = _dev(S0, torch.float32)
+    d = {n: _dev(x.reshape(Bs, -1), dt) for n, x in inp.items()}
+    dw32 = _dev(inp["w"].reshape(Bs, -1), torch.float32)
+    hv = {n: d[n].double().cpu().numpy().reshape(Bs, H, 64) for n in d}
+    y = wkv7.wkv7_step(S, d["r"], dw32, d["k"], d["v"], d["a"], d["b"], w_is_decay=True)
+    ye, Se = wo.wkv7_step_exact(S0, hv["r"], inp["w"], hv["k"], hv["v"], hv["a"], hv["b"])
+    assert rel_rms(S.cpu().numpy(), Se) < 1e-6
+    assert rel_rms(y.double().cpu().numpy().reshape(Bs, H, 64), ye) < TOL[dt]
+
+
+def test_step_chain_equals_forward():
+    """T single steps (log-log w) reproduce the sequence kernel's y and final state."""
+    from rwkv_mlx_b200 import wkv7
+
+    B, T, H = 3, 20, 2
+    d, _ = _rounded(wkv_inputs(B, T, H, seed=9), torch.float32)
+    y, sT = wkv7.wkv7_with_state(d["r"], d["w"], d["k"], d["v"], d["a"], d["b"])
+    S = torch.zeros(B, H, 64, 64, device="cuda")
+    ys = []
+    for t in range(T):
+        ys.append(wkv7.wkv7_step(S, *[d[n][:, t] for n in "rwkvab"], w_is_decay=False))
+    torch.testing.assert_close(torch.stack(ys, 1), y, rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(S, sT, rtol=1e-4, atol=1e-4)
+
+
+def test_bad_head_size_raises():
+    from rwkv_mlx_b200 import wkv7
+
+    x = torch.zeros(1, 4, 96, device="cuda")
+    with pytest.raises(AssertionError):
+        wkv7.wkv7_recurrent(x, x, x, x, x, x, head_size=32)

@@ -49,6 +49,13 @@ typedef enum { RWKV_F32 = 0, RWKV_F16 = 1, RWKV_BF16 = 2 } rwkv_dtype;
 const char* rwkv_last_error(void);
 /* ABI version of this header (bumped on any signature change). */
 int rwkv_abi_version(void);
+/* Error word set by a kernel that gave up a bounded wait (0 = none).  Reads the
+ * device word synchronously; `clear` resets it.  Negative on a CUDA error. */
+int rwkv_device_error(int clear);
+/* Select the WKV-7 kernels: 0 automatic (chunked tensor-core kernels when all
+ * per-token inputs are 16-byte aligned), 1 step-sequential kernels, 2 chunked.
+ * Process-wide; meant for testing one implementation against the other. */
+int rwkv_set_wkv_impl(int impl);
 
 /* ------------------------------------------------------------------------ */
 /* WKV-7 forward.

@@ -35,6 +35,8 @@ _SZ = ctypes.c_size_t
 SIGNATURES = {
     "rwkv_last_error": (ctypes.c_char_p, []),
     "rwkv_abi_version": (_I, []),
+    "rwkv_device_error": (_I, [_I]),
+    "rwkv_set_wkv_impl": (_I, [_I]),
     "rwkv_wkv7_forward": (_I, [_P] * 11 + [_I] * 7 + [_P]),
     "rwkv_wkv7_backward": (_I, [_P] * 17 + [_I] * 7 + [_P]),
     "rwkv_wkv7_step": (_I, [_P] * 8 + [_I] * 6 + [_P]),

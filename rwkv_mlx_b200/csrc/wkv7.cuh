@@ -21,6 +21,9 @@ struct WkvBwdArgs {
 };
 
 int wkv7_fwd_seq(const WkvFwdArgs& p, cudaStream_t st);
+int wkv7_fwd_chunk(const WkvFwdArgs& p, cudaStream_t st);
+int read_device_error(int clear);
+extern int g_wkv_impl;  // 0 auto, 1 step-sequential kernels, 2 chunked kernels
 int wkv7_bwd_seq(const WkvBwdArgs& p, cudaStream_t st);
 int wkv7_step_launch(float* S, const void* r, const void* w, const void* k, const void* v,
                      const void* a, const void* b, void* y, int Bs, int H, int dtype, int w_dtype,

@@ -4,6 +4,22 @@
 
 using namespace rwkv;
 
+namespace rwkv {
+int g_wkv_impl = 0;
+}
+
+static bool inputs_aligned16(const void* const* ps, int n) {
+    for (int i = 0; i < n; i++)
+        if (!aligned(ps[i], 16)) return false;
+    return true;
+}
+
+extern "C" int rwkv_set_wkv_impl(int impl) {
+    if (impl < 0 || impl > 2) return RWKV_ERR_ARG;
+    g_wkv_impl = impl;
+    return RWKV_OK;
+}
+
 static int check_dims(int B, int T, int H, int N, int dtype) {
     if (N != 64) return RWKV_ERR_HEAD_SIZE;
     if (B <= 0 || T <= 0 || H <= 0) return RWKV_ERR_SHAPE;
@@ -21,7 +37,9 @@ extern "C" int rwkv_wkv7_forward(const void* r, const void* w, const void* k, co
     if (!r || !w || !k || !v || !a || !b || !y) return RWKV_ERR_ARG;
     if (ckpt && (ckpt_len < 16 || ckpt_len % 16)) return RWKV_ERR_ARG;
     WkvFwdArgs p{r, w, k, v, a, b, s0, y, sT, ckpt, sa, B, T, H, dtype, w_dtype, ckpt ? ckpt_len : 16};
-    return wkv7_fwd_seq(p, (cudaStream_t)stream);
+    const void* ins[6] = {r, w, k, v, a, b};
+    if (g_wkv_impl == 1 || !inputs_aligned16(ins, 6)) return wkv7_fwd_seq(p, (cudaStream_t)stream);
+    return wkv7_fwd_chunk(p, (cudaStream_t)stream);
 }
 
 extern "C" int rwkv_wkv7_backward(const void* r, const void* w, const void* k, const void* v,

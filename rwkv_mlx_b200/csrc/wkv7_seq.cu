@@ -176,7 +176,8 @@ __global__ void __launch_bounds__(64, 1)
     const int nchunks = (T_ + ckpt_len - 1) / ckpt_len;
     for (int c = nchunks - 1; c >= 0; c--) {
         const int cs = c * ckpt_len, ce = min(T_, cs + ckpt_len);
-        const float* start = (c == 0) ? s0 : ckpt + ((size_t)bh * nck + (c - 1)) * N * N;
+        const float* start = (c == 0) ? (s0 ? s0 + (size_t)bh * N * N : nullptr)
+                                      : ckpt + ((size_t)bh * nck + (c - 1)) * N * N;
         const int nsub = (ce - cs + SC - 1) / SC;
         for (int p = nsub - 1; p >= 0; p--) {
             const int ps = cs + p * SC, n = min(SC, ce - ps);

@@ -127,14 +127,14 @@ def test_lora_moe_cmix_module_matches_oracle():
         out, aux, z = m(x)
         lg = (x.float().reshape(-1, 256) @ m.router.gate.weight.float().T).cpu().numpy()
     xn = x.double().cpu().numpy()
-    base_ref = mo.cmix(xn, base.x_k.double().cpu().numpy(), base.key.weight.double().cpu().numpy(),
-                       base.value.weight.double().cpu().numpy())
+    npy = lambda t: t.detach().double().cpu().numpy()
+    base_ref = mo.cmix(xn, npy(base.x_k), npy(base.key.weight), npy(base.value.weight))
     inds, sc, aux_r, z_r, _ = mo.router(None, None, 2, logits=lg)
-    ref = base_ref + mo.lora_moe_delta(xn, m.lora_A.double().cpu().numpy(), m.lora_B.double().cpu().numpy(),
-                                       inds.reshape(2, 64, 2), sc.reshape(2, 64, 2))
+    ref = base_ref + mo.lora_moe_delta(xn, npy(m.lora_A), npy(m.lora_B), inds.reshape(2, 64, 2),
+                                       sc.reshape(2, 64, 2))
     assert rel_rms(out.double().cpu().numpy(), ref) < 3e-3
     assert abs(float(aux) - aux_r) < 1e-3
     assert abs(float(z) - z_r) < 1e-3 * max(1, z_r)
     ol = m.orthogonal_loss()
-    ol_ref = mo.orthogonal_loss(m.lora_A.double().cpu().numpy())
+    ol_ref = mo.orthogonal_loss(npy(m.lora_A))
     assert abs(float(ol) - ol_ref) < 1e-3 * max(1e-6, ol_ref)

@@ -167,3 +167,62 @@ def test_bad_head_size_raises():
     x = torch.zeros(1, 4, 96, device="cuda")
     with pytest.raises(AssertionError):
         wkv7.wkv7_recurrent(x, x, x, x, x, x, head_size=32)
+
+
+def _set_impl(i):
+    from rwkv_mlx_b200 import _native
+
+    assert _native.lib().rwkv_set_wkv_impl(i) == 0
+
+
+@pytest.mark.parametrize("B,T,H", [(2, 64, 3), (1, 333, 2), (3, 16, 1)])
+def test_chunked_and_sequential_kernels_agree(B, T, H):
+    from rwkv_mlx_b200 import _native, wkv7
+
+    d, h = _rounded(wkv_inputs(B, T, H, seed=T + 17), torch.float32)
+    outs = {}
+    try:
+        for impl in (1, 2):
+            _set_impl(impl)
+            outs[impl] = wkv7._fwd(d["r"], d["w"], d["k"], d["v"], d["a"], d["b"], want_ckpt=True,
+                                   want_sa=True, want_state=True)
+    finally:
+        _set_impl(0)
+    torch.cuda.synchronize()
+    assert _native.lib().rwkv_device_error(1) == 0
+    ye, sae, sTe, st = wo.wkv7_forward_exact(h["r"], h["w"], h["k"], h["v"], h["a"], h["b"], keep_states=True)
+    for impl, (y, ck, sa, sT) in outs.items():
+        assert rel_rms(y.cpu().numpy(), _bt(ye)) < 2e-3, impl  # chunked: TF32 operands
+        assert rel_rms(sa.cpu().numpy(), sae) < 2e-3, impl
+        assert rel_rms(sT.cpu().numpy(), sTe) < 2e-3, impl
+        if T >= 16:
+            assert rel_rms(ck.cpu().numpy(), wo.checkpoints_from_states(st, 16).reshape(-1)) < 2e-3, impl
+
+
+def test_chunked_kernel_extreme_decays():
+    """Per-step decays down to exp(-exp(3)) ~ 2e-9: chunks whose cumulative decay
+    leaves the factored range take the element-wise path and stay exact."""
+    from rwkv_mlx_b200 import _native, wkv7
+
+    d, h = _rounded(wkv_inputs(1, 80, 2, seed=8, w_lo=-1.0, w_hi=3.0), torch.float32)
+    y = wkv7.wkv7(d["r"], d["w"], d["k"], d["v"], d["a"], d["b"])
+    torch.cuda.synchronize()
+    assert _native.lib().rwkv_device_error(1) == 0
+    ye = wo.wkv7_forward_exact(h["r"], h["w"], h["k"], h["v"], h["a"], h["b"])[0]
+    assert rel_rms(y.cpu().numpy(), _bt(ye)) < 2e-3
+
+
+def test_misaligned_inputs_use_the_sequential_kernel():
+    from rwkv_mlx_b200 import wkv7
+
+    B, T, H = 1, 40, 1
+    d, h = _rounded(wkv_inputs(B, T, H, seed=12), torch.float32)
+    # storage offset of one element: not 16-byte aligned
+    shifted = {}
+    for n in "rwkvab":
+        buf = torch.empty(d[n].numel() + 1, device="cuda", dtype=torch.float32)
+        buf[1:] = d[n].reshape(-1)
+        shifted[n] = buf[1:].view(B, T, H * 64)
+    y = wkv7.wkv7(*[shifted[n] for n in "rwkvab"])
+    ye = wo.wkv7_forward_exact(h["r"], h["w"], h["k"], h["v"], h["a"], h["b"])[0]
+    assert rel_rms(y.cpu().numpy(), _bt(ye)) < 2e-5

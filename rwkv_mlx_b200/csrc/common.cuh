@@ -5,7 +5,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#include "../../include/rwkv_b200.h"
+#include "rwkv_b200.h"
 
 namespace rwkv {
 

@@ -125,12 +125,43 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src, bool vali
 __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
+// Raw input ring: per chunk, rows of r, k, v, a, b (dtype T) then w (dtype TW), each
+// row padded by 16 bytes so that 16-byte reads of 8 consecutive rows hit distinct banks.
 template <typename T, typename TW>
 struct Raw {
     static constexpr int ROWB = N * sizeof(T), ROWBW = N * sizeof(TW);
-    static constexpr int ARR = L * ROWB, ARRW = L * ROWBW;
-    static constexpr int BYTES = 5 * ARR + ARRW;  // r,k,v,a,b then w
+    static constexpr int PITCH = ROWB + 16, PITCHW = ROWBW + 16;
+    static constexpr int ARR = L * PITCH, ARRW = L * PITCHW;
+    static constexpr int BYTES = 5 * ARR + ARRW;
+    static constexpr int PPR = ROWB / 16, PPRW = ROWBW / 16;     // 16-byte pieces per row
+    static constexpr int PIECES = 5 * L * PPR + L * PPRW;
+    static constexpr int PER_THREAD = (PIECES + 127) / 128;
 };
+
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+constexpr float LOG2E = 1.4426950408889634f;
+
+// 8 consecutive values starting at a 16-byte aligned shared address, as floats.
+template <typename T>
+__device__ __forceinline__ void lds8(const unsigned char* p, float (&o)[8]) {
+    if constexpr (sizeof(T) == 4) {
+        const float4 x0 = *reinterpret_cast<const float4*>(p), x1 = *reinterpret_cast<const float4*>(p + 16);
+        o[0] = x0.x, o[1] = x0.y, o[2] = x0.z, o[3] = x0.w, o[4] = x1.x, o[5] = x1.y, o[6] = x1.z, o[7] = x1.w;
+    } else {
+        const uint4 x = *reinterpret_cast<const uint4*>(p);
+        const T* h = reinterpret_cast<const T*>(&x);
+#pragma unroll
+        for (int q = 0; q < 8; q++) o[q] = to_f32(h[q]);
+    }
+}
+__device__ __forceinline__ void sts8(float* p, const float (&o)[8]) {
+    *reinterpret_cast<float4*>(p) = make_float4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<float4*>(p + 4) = make_float4(o[4], o[5], o[6], o[7]);
+}
 
 enum { BAR_PREP = 1, BAR_STATE = 2 };
 
@@ -166,26 +197,40 @@ __global__ void __launch_bounds__(NT, 1)
     if (tid >= 128) {
         // ===================== prep warps =====================
         const int pt = tid - 128, pw = pt >> 5, lane = pt & 31, g = lane >> 2, tg = lane & 3;
-        const int j = pt & 63, hh = pt >> 6;
 
+        // each thread's 16-byte pieces of a chunk, fixed across chunks
+        const char* psrc[R::PER_THREAD];
+        uint32_t pdst[R::PER_THREAD];
+        int prow[R::PER_THREAD];
+#pragma unroll
+        for (int i = 0; i < R::PER_THREAD; i++) {
+            const int q = pt + 128 * i;
+            if (q < 5 * L * R::PPR) {
+                const int arr = q / (L * R::PPR), rem = q % (L * R::PPR), row = rem / R::PPR, pc = rem % R::PPR;
+                const T* src = arr == 0 ? r : arr == 1 ? k : arr == 2 ? v : arr == 3 ? a : b;
+                psrc[i] = reinterpret_cast<const char*>(src + base + (size_t)row * tstride) + pc * 16;
+                pdst[i] = arr * R::ARR + row * R::PITCH + pc * 16;
+                prow[i] = row;
+            } else if (q < R::PIECES) {
+                const int q2 = q - 5 * L * R::PPR, row = q2 / R::PPRW, pc = q2 % R::PPRW;
+                psrc[i] = reinterpret_cast<const char*>(w + base + (size_t)row * tstride) + pc * 16;
+                pdst[i] = 5 * R::ARR + row * R::PITCHW + pc * 16;
+                prow[i] = row;
+            } else {
+                psrc[i] = nullptr, pdst[i] = 0, prow[i] = -1;
+            }
+        }
         auto issue = [&](int c) {
             unsigned char* dst = rawbuf + (size_t)(c & 1) * R::BYTES;
             const int t0 = c * L;
-            // r, k, v, a, b
-            const T* srcs[5] = {r, k, v, a, b};
-            constexpr int PPR = R::ROWB / 16;  // 16-byte pieces per row
-            for (int q = pt; q < 5 * L * PPR; q += 128) {
-                const int arr = q / (L * PPR), rem = q % (L * PPR), row = rem / PPR, pc = rem % PPR;
-                const bool ok = (t0 + row) < T_;
-                const T* src = srcs[arr] + (ok ? base + (size_t)(t0 + row) * tstride : 0) + pc * (16 / sizeof(T));
-                cp_async16(dst + arr * R::ARR + row * R::ROWB + pc * 16, src, ok);
-            }
-            constexpr int PPRW = R::ROWBW / 16;
-            for (int q = pt; q < L * PPRW; q += 128) {
-                const int row = q / PPRW, pc = q % PPRW;
-                const bool ok = (t0 + row) < T_;
-                const TW* src = w + (ok ? base + (size_t)(t0 + row) * tstride : 0) + pc * (16 / sizeof(TW));
-                cp_async16(dst + 5 * R::ARR + row * R::ROWBW + pc * 16, src, ok);
+#pragma unroll
+            for (int i = 0; i < R::PER_THREAD; i++) {
+                if (prow[i] < 0) continue;
+                const bool ok = (t0 + prow[i]) < T_;
+                const size_t step = (size_t)t0 * tstride;
+                const char* src = ok ? psrc[i] + step * (pdst[i] >= 5u * R::ARR ? sizeof(TW) : sizeof(T))
+                                     : psrc[i];
+                cp_async16(dst + pdst[i], src, ok);
             }
         };
 
@@ -201,55 +246,67 @@ __global__ void __launch_bounds__(NT, 1)
             if (c >= 2) bad = !mbar_wait(&sm.empty[s], ((c >> 1) + 1) & 1, &sm.abort);
             if (group_sync_or(BAR_PREP, bad)) break;
 
-            // ---- P1: cumulative log decay and decayed factors ----
+            // ---- P1: cumulative log2 decay and decayed factors ----
+            // thread = (row t, 8 consecutive columns); the scan over t runs across the
+            // 16 lanes that share a column group
             const unsigned char* raw = rawbuf + (size_t)s * R::BYTES;
-            const T* rr = reinterpret_cast<const T*>(raw);
-            const T* rk = reinterpret_cast<const T*>(raw + R::ARR);
-            const T* rv = reinterpret_cast<const T*>(raw + 2 * R::ARR);
-            const T* ra = reinterpret_cast<const T*>(raw + 3 * R::ARR);
-            const T* rb = reinterpret_cast<const T*>(raw + 4 * R::ARR);
-            const TW* rw = reinterpret_cast<const TW*>(raw + 5 * R::ARR);
-            const int tvalid = T_ - c * L;
-            float cs[8];
-            float acc = 0.f;
+            const int t = lane & 15, cg = 2 * pw + (lane >> 4), j0 = 8 * cg;
+            const bool tok = t < T_ - c * L;
+            float wv[8], cs[8], cp[8], cl[8];
+            lds8<TW>(raw + 5 * R::ARR + t * R::PITCHW + j0 * sizeof(TW), wv);
+#pragma unroll
+            for (int q = 0; q < 8; q++) cs[q] = tok ? -ex2(wv[q] * LOG2E) * LOG2E : 0.f;
+#pragma unroll
+            for (int o = 1; o < 16; o <<= 1) {
+#pragma unroll
+                for (int q = 0; q < 8; q++) {
+                    const float u = __shfl_up_sync(0xffffffffu, cs[q], o, 16);
+                    if (t >= o) cs[q] += u;
+                }
+            }
+            bool ext = false;
 #pragma unroll
             for (int q = 0; q < 8; q++) {
-                const int t = 8 * hh + q;
-                const float lw = (t < tvalid) ? -expf(to_f32(rw[t * N + j])) : 0.f;
-                acc += lw;
-                cs[q] = acc;
+                const float u = __shfl_up_sync(0xffffffffu, cs[q], 1, 16);
+                cp[q] = t ? u : 0.f;
+                cl[q] = __shfl_sync(0xffffffffu, cs[q], 15, 16);
+                ext |= cl[q] < -115.f;  // cumulative decay below e^-80
             }
-            if (hh == 0) sm.Cs[8][j] = acc;  // c_7
-            group_sync(BAR_PREP);
-            const float off = hh ? sm.Cs[8][j] : 0.f;
+            float xr[8], xk[8], xv[8], xa[8], xb[8], o1[8], o2[8];
+            lds8<T>(raw + 0 * R::ARR + t * R::PITCH + j0 * sizeof(T), xr);
+            lds8<T>(raw + 1 * R::ARR + t * R::PITCH + j0 * sizeof(T), xk);
+            lds8<T>(raw + 2 * R::ARR + t * R::PITCH + j0 * sizeof(T), xv);
+            lds8<T>(raw + 3 * R::ARR + t * R::PITCH + j0 * sizeof(T), xa);
+            lds8<T>(raw + 4 * R::ARR + t * R::PITCH + j0 * sizeof(T), xb);
+            float ec[8], ei[8], eL[8];
 #pragma unroll
             for (int q = 0; q < 8; q++) {
-                cs[q] += off;
-                sm.Cs[8 * hh + q + 1][j] = cs[q];
+                ec[q] = ex2(cs[q]);
+                ei[q] = ex2(-cs[q]);
+                eL[q] = ex2(cl[q] - cs[q]);
             }
-            if (hh == 0) sm.Cs[0][j] = 0.f;
-            const bool extreme = group_sync_or(BAR_PREP, hh == 1 && cs[7] < -80.f);
-            const float cL = sm.Cs[L][j];
-            float eprev = hh ? expf(off) : 1.f;
 #pragma unroll
-            for (int q = 0; q < 8; q++) {
-                const int t = 8 * hh + q;
-                const float ec = expf(cs[q]);
-                const float ei = expf(-cs[q]);
-                const float eL = expf(cL - cs[q]);
-                const float av = to_f32(ra[t * N + j]), rv_ = to_f32(rr[t * N + j]);
-                const float bv = to_f32(rb[t * N + j]), kv = to_f32(rk[t * N + j]);
-                sm.At[t][j] = tf32f(av * eprev);
-                sm.Rt[t][j] = tf32f(rv_ * ec);
-                sm.Bh[t][j] = tf32f(bv * ei);
-                sm.Kh[t][j] = tf32f(kv * ei);
-                stg.Bb[t][j] = tf32f(bv * eL);
-                stg.Kb[t][j] = tf32f(kv * eL);
-                stg.V[t][j] = tf32f(to_f32(rv[t * N + j]));
-                eprev = ec;
+            for (int q = 0; q < 8; q++) o1[q] = tf32f(xa[q] * ex2(cp[q])), o2[q] = tf32f(xr[q] * ec[q]);
+            sts8(&sm.At[t][j0], o1);
+            sts8(&sm.Rt[t][j0], o2);
+#pragma unroll
+            for (int q = 0; q < 8; q++) o1[q] = tf32f(xb[q] * ei[q]), o2[q] = tf32f(xk[q] * ei[q]);
+            sts8(&sm.Bh[t][j0], o1);
+            sts8(&sm.Kh[t][j0], o2);
+#pragma unroll
+            for (int q = 0; q < 8; q++) o1[q] = tf32f(xb[q] * eL[q]), o2[q] = tf32f(xk[q] * eL[q]);
+            sts8(&stg.Bb[t][j0], o1);
+            sts8(&stg.Kb[t][j0], o2);
+#pragma unroll
+            for (int q = 0; q < 8; q++) o1[q] = tf32f(xv[q]);
+            sts8(&stg.V[t][j0], o1);
+            sts8(&sm.Cs[t + 1][j0], cs);  // log2 units, used by the element-wise path
+            if (t == 0) {
+#pragma unroll
+                for (int q = 0; q < 8; q++) sm.Cs[0][j0 + q] = 0.f;
             }
-            if (hh == 1) stg.GL[j] = expf(cL);
-            group_sync(BAR_PREP);
+            if (t == 15) sts8(&stg.GL[j0], ec);
+            const bool extreme = group_sync_or(BAR_PREP, ext);
 
             // ---- P2: intra-chunk matrices ----
             if (!extreme) {
@@ -282,19 +339,19 @@ __global__ void __launch_bounds__(NT, 1)
             } else {
                 // element-wise from exponent differences (all exponents <= 0)
                 for (int e = pt; e < 4 * L * L; e += 128) {
-                    const int which = e / (L * L), t = (e / L) % L, sidx = e % L;
+                    const int which = e / (L * L), tt = (e / L) % L, sidx = e % L;
                     const bool strict = which < 2;
                     float val = 0.f;
-                    if (strict ? (sidx < t) : (sidx <= t)) {
-                        const T* lhs = (which < 2) ? ra : rr;
-                        const T* rhs = (which & 1) ? rk : rb;
-                        const float* cl = (which < 2) ? sm.Cs[t] : sm.Cs[t + 1];
-                        const float* cr = sm.Cs[sidx + 1];
+                    if (strict ? (sidx < tt) : (sidx <= tt)) {
+                        const T* lhs = reinterpret_cast<const T*>(raw + (which < 2 ? 3 : 0) * R::ARR + tt * R::PITCH);
+                        const T* rhs = reinterpret_cast<const T*>(raw + ((which & 1) ? 1 : 4) * R::ARR + sidx * R::PITCH);
+                        const float* cl2 = (which < 2) ? sm.Cs[tt] : sm.Cs[tt + 1];
+                        const float* cr2 = sm.Cs[sidx + 1];
                         for (int jj = 0; jj < N; jj++)
-                            val = fmaf(to_f32(lhs[t * N + jj]) * to_f32(rhs[sidx * N + jj]), expf(cl[jj] - cr[jj]), val);
+                            val = fmaf(to_f32(lhs[jj]) * to_f32(rhs[jj]), exp2f(cl2[jj] - cr2[jj]), val);
                     }
                     float(*Mo)[LDM] = which == 0 ? sm.Mab : which == 1 ? sm.Mak : which == 2 ? sm.Mrb : sm.Mrk;
-                    Mo[t][sidx] = which == 0 ? val : tf32f(val);
+                    Mo[tt][sidx] = which == 0 ? val : tf32f(val);
                 }
             }
             group_sync(BAR_PREP);

@@ -1,5 +1,8 @@
 """The RWKV-v7 model shell on the B200 kernels vs the CPU restatement of
-rwkv_mlx/model.py (GPT mode, RNN mode, prefill->decode hand-over).  Needs a GPU."""
+rwkv_mlx/model.py (GPT mode, RNN mode, prefill->decode hand-over).  Needs a GPU.
+
+GPT mode runs the chunked WKV-7 kernel (TF32 operands): 2e-3 relative-to-RMS on
+the logits.  RNN mode runs the fp32 step kernel: 1e-4."""
 
 import numpy as np
 import pytest
@@ -41,7 +44,7 @@ def test_gpt_forward_matches_cpu_restatement(groupnorm):
     with torch.no_grad():
         logits, aux = m(idx)
     ref, aux_r = mo.forward(_sd(m), cfg, idx.cpu(), wkv="exact", dtype=torch.float64)
-    assert rel_rms(logits.double().cpu().numpy(), ref.numpy()) < 1e-4
+    assert rel_rms(logits.double().cpu().numpy(), ref.numpy()) < 2e-3
     assert float(aux) == 0.0 and aux_r == 0.0
 
 
@@ -51,7 +54,7 @@ def test_gpt_forward_with_lora_moe_matches_cpu_restatement():
     with torch.no_grad():
         logits, aux = m(idx)
     ref, aux_r = mo.forward(_sd(m), cfg, idx.cpu(), wkv="exact", dtype=torch.float64)
-    assert rel_rms(logits.double().cpu().numpy(), ref.numpy()) < 1e-3
+    assert rel_rms(logits.double().cpu().numpy(), ref.numpy()) < 2e-3
     assert abs(float(aux) - aux_r) < 1e-4 * max(1.0, abs(aux_r))
 
 
@@ -79,7 +82,7 @@ def test_prefill_state_then_decode_equals_gpt_forward():
         for t in range(24, 30):
             outs.append(m.forward_rnn_batch(idx[:, t], states))
     dec = torch.stack(outs, 1)
-    assert rel_rms(dec.double().cpu().numpy(), full[:, 24:].double().cpu().numpy()) < 1e-4
+    assert rel_rms(dec.double().cpu().numpy(), full[:, 24:].double().cpu().numpy()) < 2e-3
 
 
 def test_fp16_model_close_to_fp32():

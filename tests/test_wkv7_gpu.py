@@ -1,8 +1,10 @@
 """WKV-7 CUDA kernels vs the float64 oracle (parity tests proper; need a B200).
 
-Tolerances are relative to the RMS of the oracle output:
-  fp32 inputs 2e-5, fp16 inputs 2e-3 (the north-star bound for fp16 inputs with
-  fp32 state), bf16 inputs 6e-3 (bf16 output rounding alone is ~2e-3).
+Tolerances are relative to the RMS of the oracle output.  The step-sequential
+kernels compute in fp32 throughout: fp32 inputs 2e-5.  The chunked tensor-core
+kernels use TF32 operands (fp32 accumulate, fp32 state): 2e-3 for fp32 and fp16
+inputs (the north-star bound for fp16 inputs with fp32 state).  bf16 inputs 6e-3
+(bf16 output rounding alone is ~2e-3).
 """
 
 import numpy as np
@@ -14,7 +16,8 @@ from tests.inputs import rel_rms, wkv_inputs
 
 pytestmark = pytest.mark.gpu
 
-TOL = {torch.float32: 2e-5, torch.float16: 2e-3, torch.bfloat16: 6e-3}
+TOL = {torch.float32: 2e-3, torch.float16: 2e-3, torch.bfloat16: 6e-3}  # default (chunked) path
+TOL_SEQ = {torch.float32: 2e-5, torch.float16: 2e-3, torch.bfloat16: 6e-3}
 
 
 def _dev(x, dt):
@@ -35,20 +38,26 @@ def _rounded(inp, dt, w_dt=None):
     return dev, host
 
 
+@pytest.mark.parametrize("impl", [1, 2])
 @pytest.mark.parametrize("dt", [torch.float32, torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("B,T,H", [(1, 256, 4), (2, 100, 3), (1, 17, 1)])
-def test_forward_matches_oracle(dt, B, T, H):
+def test_forward_matches_oracle(dt, B, T, H, impl):
     from rwkv_mlx_b200 import wkv7
 
     d, h = _rounded(wkv_inputs(B, T, H, seed=B * 1000 + T), dt)
-    y, s, sa = wkv7.wkv7_forward(d["r"], d["w"], d["k"], d["v"], d["a"], d["b"])
-    torch.cuda.synchronize()
+    _set_impl(impl)
+    try:
+        y, s, sa = wkv7.wkv7_forward(d["r"], d["w"], d["k"], d["v"], d["a"], d["b"])
+        torch.cuda.synchronize()
+    finally:
+        _set_impl(0)
+    tol = (TOL_SEQ if impl == 1 else TOL)[dt]
     ye, sae, _, states = wo.wkv7_forward_exact(h["r"], h["w"], h["k"], h["v"], h["a"], h["b"], keep_states=True)
-    assert rel_rms(y.double().cpu().numpy(), _bt(ye)) < TOL[dt]
-    assert rel_rms(sa.cpu().numpy(), sae) < max(TOL[dt], 1e-5)
+    assert rel_rms(y.double().cpu().numpy(), _bt(ye)) < tol
+    assert rel_rms(sa.cpu().numpy(), sae) < max(tol, 1e-5)
     if T >= 16:
         ck = wo.checkpoints_from_states(states, 16).reshape(-1)
-        assert rel_rms(s.cpu().numpy(), ck) < 1e-5
+        assert rel_rms(s.cpu().numpy(), ck) < max(tol, 1e-5)
 
 
 def test_forward_fp32_decay_with_fp16_inputs():
@@ -72,10 +81,10 @@ def test_state_in_out_composes():
     rest = {n: t[:, 40:] for n, t in d.items()}
     y1, s1 = wkv7.wkv7_with_state(half["r"], half["w"], half["k"], half["v"], half["a"], half["b"])
     y2, s2 = wkv7.wkv7_with_state(rest["r"], rest["w"], rest["k"], rest["v"], rest["a"], rest["b"], s0=s1)
-    torch.testing.assert_close(torch.cat([y1, y2], 1), y, rtol=1e-5, atol=1e-5)
-    torch.testing.assert_close(s2, sT, rtol=1e-5, atol=1e-5)
-    _, _, sTe, _ = wo.wkv7_forward_exact(h["r"], h["w"], h["k"], h["v"], h["a"], h["b"])
-    assert rel_rms(sT.cpu().numpy(), sTe) < 1e-5
+    ye, _, sTe, _ = wo.wkv7_forward_exact(h["r"], h["w"], h["k"], h["v"], h["a"], h["b"])
+    assert rel_rms(torch.cat([y1, y2], 1).cpu().numpy(), _bt(ye)) < TOL[torch.float32]
+    assert rel_rms(s2.cpu().numpy(), sTe) < TOL[torch.float32]
+    assert rel_rms(sT.cpu().numpy(), sTe) < TOL[torch.float32]
 
 
 @pytest.mark.parametrize("dt", [torch.float32, torch.float16])
@@ -103,7 +112,7 @@ def test_autograd_function_and_state_grads():
     y.backward(d["dy"])
     ge = wo.wkv7_backward_exact(h["r"], h["w"], h["k"], h["v"], h["a"], h["b"], h["dy"])
     for n, e in zip("rwkvab", ge[:6]):
-        assert rel_rms(leaves[n].grad.double().cpu().numpy(), _bt(e)) < 2e-5, n
+        assert rel_rms(leaves[n].grad.double().cpu().numpy(), _bt(e)) < TOL[torch.float32], n
 
 
 def test_backward_with_initial_state_and_state_grad():
@@ -120,8 +129,8 @@ def test_backward_with_initial_state_and_state_grad():
                            s0=s0d, dsT=dsTd, want_ds0=True)
     ge = wo.wkv7_backward_exact(h["r"], h["w"], h["k"], h["v"], h["a"], h["b"], h["dy"], s0=s0, dsT=dsT)
     for name, g, e in zip(["dr", "dw", "dk", "dv", "da", "db"], grads, ge[:6]):
-        assert rel_rms(g.double().cpu().numpy(), _bt(e)) < 2e-5, name
-    assert rel_rms(ds0.cpu().numpy(), ge[6]) < 2e-5
+        assert rel_rms(g.double().cpu().numpy(), _bt(e)) < TOL[torch.float32], name
+    assert rel_rms(ds0.cpu().numpy(), ge[6]) < TOL[torch.float32]
 
 
 @pytest.mark.parametrize("dt", [torch.float32, torch.float16])
@@ -157,8 +166,8 @@ def test_step_chain_equals_forward():
     ys = []
     for t in range(T):
         ys.append(wkv7.wkv7_step(S, *[d[n][:, t] for n in "rwkvab"], w_is_decay=False))
-    torch.testing.assert_close(torch.stack(ys, 1), y, rtol=1e-4, atol=1e-4)
-    torch.testing.assert_close(S, sT, rtol=1e-4, atol=1e-4)
+    assert rel_rms(torch.stack(ys, 1).cpu().numpy(), y.cpu().numpy()) < TOL[torch.float32]
+    assert rel_rms(S.cpu().numpy(), sT.cpu().numpy()) < TOL[torch.float32]
 
 
 def test_bad_head_size_raises():

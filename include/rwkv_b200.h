@@ -121,6 +121,25 @@ int rwkv_moe_router(const void* x, const float* gate_w, const float* bias, float
                     void* workspace, size_t workspace_bytes, int ntok, int C, int E,
                     int topk, int dtype, void* stream);
 
+/* Same as rwkv_moe_router, but allocates nothing and takes no workspace.
+ * No counterpart in the reference: it exists for callers that cannot allocate
+ * device memory -- an FFI binding that holds only the buffers a framework handed
+ * it, or a serving loop that reserves all device memory at start-up and must not
+ * allocate later (cudaMalloc can synchronise the device and fails once memory is
+ * reserved).  Its scratch is a file-scope device array of
+ * rwkv_moe_router_noalloc_scratch_bytes() bytes (~301 KB), held by every GPU that
+ * loads this library until the process exits.  Limit: E <= 32 (any ntok).
+ * The first call on a device looks up that array's device address with the
+ * device current; make that first call before any stream capture.  All calls
+ * on a device share the array (it keeps the last call's contents; nothing in it
+ * needs to start at zero), so calls that overlap on the same GPU, e.g. on two
+ * streams, race: serialize them. */
+size_t rwkv_moe_router_noalloc_scratch_bytes(void);
+int rwkv_moe_router_noalloc(const void* x, const float* gate_w, const float* bias,
+                            float* logits, int32_t* inds, void* scores, float* stats,
+                            int32_t* counts, int ntok, int C, int E, int topk, int dtype,
+                            void* stream);
+
 /* Stable counting sort of the (token, slot) routing entries by expert.
  * The reference has no counterpart (it loops densely over all experts,
  * moe.py:139-145); this builds the dispatch order its output is invariant to.

@@ -42,6 +42,8 @@ SIGNATURES = {
     "rwkv_wkv7_step": (_I, [_P] * 8 + [_I] * 6 + [_P]),
     "rwkv_moe_router_workspace_size": (_SZ, [_I, _I]),
     "rwkv_moe_router": (_I, [_P] * 9 + [_SZ] + [_I] * 5 + [_P]),
+    "rwkv_moe_router_noalloc_scratch_bytes": (_SZ, []),
+    "rwkv_moe_router_noalloc": (_I, [_P] * 8 + [_I] * 5 + [_P]),
     "rwkv_moe_permute_workspace_size": (_SZ, [_I, _I]),
     "rwkv_moe_permute": (_I, [_P] * 5 + [_SZ] + [_I] * 3 + [_P]),
     "rwkv_moe_lora_down": (_I, [_P] * 5 + [_I] * 6 + [_P]),
@@ -86,7 +88,7 @@ def lib() -> ctypes.CDLL:
 # kernels that entry point enqueues).  bench.py reads it to report gpu_launches.
 KERNELS_PER_CALL = {
     "rwkv_wkv7_forward": 1, "rwkv_wkv7_backward": 1, "rwkv_wkv7_step": 1,
-    "rwkv_moe_router": 2, "rwkv_moe_permute": 3, "rwkv_moe_lora_down": 1,
+    "rwkv_moe_router": 2, "rwkv_moe_router_noalloc": 2, "rwkv_moe_permute": 3, "rwkv_moe_lora_down": 1,
     "rwkv_moe_lora_combine": 1, "rwkv_moe_ortho_loss": 1,
 }
 launch_count = 0

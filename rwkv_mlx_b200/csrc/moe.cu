@@ -499,3 +499,82 @@ extern "C" int rwkv_moe_ortho_loss(const void* A, float* out, int E, int C, int 
     RWKV_DISPATCH_DTYPE(dtype, T, moe_ortho_kernel<T><<<1, threads, 0, st>>>((const T*)A, out, E, C, R));
     return check_launch();
 }
+
+// ===========================================================================
+// Router entry point that allocates nothing.
+//
+// Some callers cannot allocate device memory: an FFI binding that only holds the
+// device buffers a framework handed it (and has no allocator of its own), or a
+// serving loop that reserves all device memory at start-up and must not allocate
+// afterwards (cudaMalloc can synchronise the device and fails once the memory is
+// reserved).  rwkv_moe_router_noalloc runs the same kernels as rwkv_moe_router,
+// with its per-CTA partial sums in the file-scope device array below instead of a
+// caller-provided workspace.
+// ===========================================================================
+#include <mutex>
+
+namespace rwkv {
+constexpr int NOALLOC_MAX_E = 32;
+constexpr size_t NOALLOC_SCRATCH_BYTES =
+    ((size_t)ROUTER_MAX_CTAS * (NOALLOC_MAX_E + 1) * sizeof(float) + 255) / 256 * 256 +
+    ((size_t)ROUTER_MAX_CTAS * NOALLOC_MAX_E * sizeof(int32_t) + 255) / 256 * 256;
+// ~301 KB, held by every GPU that loads this library until the process exits.
+static __device__ __align__(256) unsigned char g_router_scratch[NOALLOC_SCRATCH_BYTES];
+
+static std::mutex g_scratch_mu;
+static void* g_scratch_addr[128];
+
+// Device address of g_router_scratch on the current device.  The host-side name
+// is only a stand-in, so the address is looked up once per device, with that
+// device current, the first time the entry point runs on it.
+static int router_scratch_address(void** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return set_cuda_error(e);
+    if (dev < 0 || dev >= 128) return RWKV_ERR_ARG;
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    if (!g_scratch_addr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_router_scratch);
+        if (e != cudaSuccess) return set_cuda_error(e);
+        g_scratch_addr[dev] = p;
+    }
+    *out = g_scratch_addr[dev];
+    return RWKV_OK;
+}
+}  // namespace rwkv
+
+extern "C" size_t rwkv_moe_router_noalloc_scratch_bytes(void) { return rwkv::NOALLOC_SCRATCH_BYTES; }
+
+extern "C" int rwkv_moe_router_noalloc(const void* x, const float* gate_w, const float* bias,
+                                       float* logits, int32_t* inds, void* scores, float* stats,
+                                       int32_t* counts, int ntok, int C, int E, int topk,
+                                       int dtype, void* stream) {
+    if (ntok <= 0 || C <= 0 || E <= 0 || E > NOALLOC_MAX_E || topk <= 0 || topk > E || topk > 8)
+        return RWKV_ERR_SHAPE;
+    if (C % 8) return RWKV_ERR_SHAPE;
+    if ((size_t)E * C * sizeof(float) > 200 * 1024) return RWKV_ERR_SHAPE;
+    if (!x || !gate_w || !inds || !scores || !stats) return RWKV_ERR_ARG;
+    if (!aligned(x, 16)) return RWKV_ERR_ALIGN;
+    if (rwkv_moe_router_workspace_size(ntok, E) > NOALLOC_SCRATCH_BYTES) return RWKV_ERR_WORKSPACE;
+    void* scratch = nullptr;
+    int rc = router_scratch_address(&scratch);
+    if (rc) return rc;
+    const int nb = router_ctas(ntok);
+    // every partial is written by its CTA before the finalize kernel reads it, so
+    // nothing left in the array by an earlier call needs clearing
+    float* pf = (float*)scratch;
+    int32_t* pc = (int32_t*)((char*)scratch + align_up((size_t)nb * (E + 1) * sizeof(float), 256));
+    cudaStream_t st = (cudaStream_t)stream;
+    RWKV_DISPATCH_DTYPE(dtype, T, {
+        if (E <= 8)
+            rc = launch_router<T, 8>(x, gate_w, bias, logits, inds, scores, pf, pc, ntok, C, E, topk, st);
+        else if (E <= 16)
+            rc = launch_router<T, 16>(x, gate_w, bias, logits, inds, scores, pf, pc, ntok, C, E, topk, st);
+        else
+            rc = launch_router<T, 32>(x, gate_w, bias, logits, inds, scores, pf, pc, ntok, C, E, topk, st);
+    });
+    if (rc) return rc;
+    moe_router_finalize_kernel<<<1, 64, 0, st>>>(pf, pc, nb, ntok, E, topk, stats, counts);
+    return check_launch();
+}

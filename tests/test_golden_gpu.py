@@ -1,0 +1,130 @@
+"""The B200 path reproduces golden vectors computed by the reference's own code
+(tests/golden/make_golden.py).  Tolerance 2e-3 relative to RMS (north star) unless
+stated; routing compared as expert sets (the reference's slot order is unspecified)."""
+
+import numpy as np
+import pytest
+import torch
+
+from tests.golden.golden import golden, model_params, tiny_config, wkv_c1_inputs
+from tests.inputs import rel_rms
+
+pytestmark = pytest.mark.gpu
+
+
+def _dev(x, dt=torch.float32):
+    return torch.tensor(np.ascontiguousarray(x), dtype=dt, device="cuda")
+
+
+def _bt(x):
+    return x.reshape(x.shape[0], x.shape[1], -1)
+
+
+def test_wkv_config1_matches_reference():
+    from rwkv_mlx_b200 import wkv7
+
+    G = golden()
+    d = wkv_c1_inputs()
+    args = [_dev(_bt(d[n])) for n in "rwkvab"]
+    y, s, sa = wkv7.wkv7_forward(*args)
+    grads = wkv7.wkv7_backward(*args, _dev(_bt(d["dy"])), s, sa)
+    torch.cuda.synchronize()
+    assert rel_rms(y.cpu().numpy(), G["wkv_c1_y"]) < 2e-3
+    assert rel_rms(sa.cpu().numpy(), G["wkv_c1_sa"]) < 2e-3
+    for n, g in zip(["dr", "dw", "dk", "dv", "da", "db"], grads):
+        assert rel_rms(g.cpu().numpy(), G["wkv_c1_" + n]) < 2e-3, n
+
+
+def test_wkv_fp16_matches_reference_kernel():
+    from rwkv_mlx_b200 import wkv7
+
+    G = golden()
+    args = [_dev(G["wkv_h_in_" + n], torch.float16) for n in "rwkvab"]
+    y, s, sa = wkv7.wkv7_forward(*args)
+    grads = wkv7.wkv7_backward(*args, _dev(G["wkv_h_in_dy"], torch.float16), s, sa)
+    torch.cuda.synchronize()
+    assert rel_rms(y.double().cpu().numpy(), G["wkv_h_y"].astype(np.float64)) < 2e-3
+    assert rel_rms(s.cpu().numpy(), G["wkv_h_s"]) < 2e-3
+    for n, g in zip(["dr", "dw", "dk", "dv", "da", "db"], grads):
+        assert rel_rms(g.double().cpu().numpy(), G["wkv_h_" + n].astype(np.float64)) < 3e-3, n
+
+
+def _model(prefix, seed, moe=False):
+    from rwkv_mlx_b200.model import RWKV, RWKVConfig
+
+    cfg = RWKVConfig(**tiny_config(moe))
+    m = RWKV(cfg).cuda()
+    P = model_params(prefix, seed)
+    sd = m.state_dict()
+    assert set(P) == set(sd), set(P) ^ set(sd)  # same parameter names as the reference
+    m.load_state_dict({k: torch.tensor(v).view(sd[k].shape) for k, v in P.items()})
+    return cfg, m.eval()
+
+
+def test_model_gpt_and_rnn_modes_match_reference():
+    G = golden()
+    cfg, m = _model("model", 2)
+    with torch.no_grad():
+        logits, aux = m(_dev(G["model_idx"], torch.long))
+        assert rel_rms(logits.cpu().numpy(), G["model_logits"]) < 2e-3
+        st = m.init_state()
+        for i, tok in enumerate(G["model_rnn_tokens"]):
+            lg, st = m.forward_rnn(int(tok), st)
+            assert rel_rms(lg.cpu().numpy(), G["model_rnn_logits"][i]) < 1e-4
+    for i in range(len(st)):
+        assert rel_rms(st[i].cpu().numpy(), G[f"model_rnn_state_{i}"]) < 1e-4
+
+
+def test_time_mixing_rnn_step_matches_reference():
+    G = golden()
+    cfg, m = _model("model", 2)
+    att = m.blocks[1].att
+    S = _dev(G["rnn_S"]).view(1, 2, 64, 64).contiguous()
+    with torch.no_grad():
+        out, _, S, _ = att.forward_rnn(_dev(G["rnn_x"]).view(1, -1), _dev(G["rnn_xprev"]).view(1, -1),
+                                       _dev(G["rnn_vfirst"]).view(1, -1), S)
+    assert rel_rms(out.cpu().numpy().reshape(-1), G["rnn_out"]) < 1e-4
+    assert rel_rms(S.cpu().numpy().reshape(2, 64, 64), G["rnn_Snew"]) < 1e-5
+
+
+def test_router_and_lora_moe_match_reference():
+    from rwkv_mlx_b200.model import RWKV_CMix_x070, RWKVConfig
+    from rwkv_mlx_b200.moe import LoRAMoE_CMix, Router
+
+    G = golden()
+    router = Router(64, 8, 2).cuda()
+    with torch.no_grad():
+        router.gate.weight.copy_(_dev(G["router_w"]))
+        inds, scores, aux, z = router(_dev(G["router_x"]))
+    inds, scores = inds.cpu().numpy().reshape(-1, 2), scores.cpu().numpy().reshape(-1, 2)
+    ref_inds, ref_sc = G["router_inds"].reshape(-1, 2), G["router_scores"].reshape(-1, 2)
+    for t in range(inds.shape[0]):
+        assert set(inds[t]) == set(ref_inds[t])
+        for slot in range(2):
+            assert abs(scores[t, slot] - ref_sc[t][list(ref_inds[t]).index(inds[t, slot])]) < 1e-5
+    assert abs(float(aux) - float(G["router_aux"])) < 1e-5
+    assert abs(float(z) - float(G["router_z"])) < 1e-4
+
+    base = RWKV_CMix_x070(RWKVConfig(n_layer=2, n_embd=64, dim_ffn=128), 1).cuda()
+    moe = LoRAMoE_CMix(base, 8, 16, 2).cuda()
+    with torch.no_grad():
+        base.x_k.copy_(_dev(G["moe_xk"]))
+        base.key.weight.copy_(_dev(G["moe_key"]))
+        base.value.weight.copy_(_dev(G["moe_value"]))
+        moe.lora_A.copy_(_dev(G["moe_A"]))
+        moe.lora_B.copy_(_dev(G["moe_B"]))
+        moe.router.gate.weight.copy_(_dev(G["moe_gate"]))
+        out, aux, z = moe(_dev(G["moe_x"]))
+        ortho = moe.orthogonal_loss()
+    assert rel_rms(out.cpu().numpy(), G["moe_out"]) < 1e-4
+    assert abs(float(aux) - float(G["moe_aux"])) < 1e-5 and abs(float(z) - float(G["moe_z"])) < 1e-4
+    assert abs(float(ortho) - float(G["moe_ortho"])) < 1e-4 * float(G["moe_ortho"])
+
+
+def test_model_with_lora_moe_matches_reference():
+    G = golden()
+    cfg, m = _model("modelmoe", 4, moe=True)
+    with torch.no_grad():
+        logits, aux = m(_dev(G["modelmoe_idx"], torch.long))
+    assert rel_rms(logits.cpu().numpy(), G["modelmoe_logits"]) < 2e-3
+    assert abs(float(aux) - float(G["modelmoe_aux"])) < 1e-4 * max(1.0, abs(float(G["modelmoe_aux"])))

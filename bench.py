@@ -322,6 +322,130 @@ def run_wkv(args, ws, rank, dev, backward=False):
             "clocks": clocks}
 
 
+def run_moe(args, ws, rank, dev):
+    """One LoRA-MoE ChannelMix layer: D=768, hidden 3072, E=8,
+    r=16, top-2, 65536 tokens per GPU, per-expert logit bias N(0, 1.5); each rank
+    routes its own tokens over a replica of the experts (no collective)."""
+    from rwkv_mlx_b200 import _native
+    from rwkv_mlx_b200.model import RWKV_CMix_x070, RWKVConfig
+    from rwkv_mlx_b200.moe import LoRAMoE_CMix
+
+    ep = args.ep and ws > 1
+    ntok, C = args.moe_tokens, 768
+    g = torch.Generator(device=dev).manual_seed(7 + rank)
+    cfg = RWKVConfig(n_embd=C, dim_ffn=3072)
+    gw = torch.Generator(device=dev).manual_seed(7)  # same weights on every rank
+    with torch.device(dev):
+        base = RWKV_CMix_x070(cfg, 1)
+        if ep:
+            from rwkv_mlx_b200.ep import ExpertParallelLoRAMoE
+
+            layer = ExpertParallelLoRAMoE(base, n_experts=8, lora_rank=16, top_k=2)
+        else:
+            layer = LoRAMoE_CMix(base, n_experts=8, lora_rank=16, top_k=2)
+    with torch.no_grad():
+        base.x_k.uniform_(0, 1, generator=gw)
+        base.key.weight.normal_(0, C ** -0.5, generator=gw)
+        base.value.weight.normal_(0, 3072 ** -0.5, generator=gw)
+        A = torch.randn(8, C, 16, device=dev, generator=gw) * 0.02
+        Bw = torch.randn(8, 16, C, device=dev, generator=gw) * 0.02
+        if ep:
+            layer.load_experts(A, Bw)
+        else:
+            layer.lora_A.copy_(A)
+            layer.lora_B.copy_(Bw)
+        layer.router.gate.weight.normal_(0, C ** -0.5, generator=gw)
+    layer = layer.half()
+    layer.router.bias = torch.randn(8, device=dev, generator=gw) * 1.5
+    x = torch.randn(1, ntok, C, device=dev, generator=g).half()
+
+    def step():
+        with torch.no_grad():
+            return layer(x)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    l0 = _native.launch_count
+    barrier(ws)
+    clk = ClockSampler(dev)
+    ms = cuda_timed(step, args.steps)
+    clocks = clk.stop()
+    launches = _native.launch_count - l0
+    ms = max_over_ranks(ms, ws)
+    # MoE-path kernels alone (router, permute, down, combine) on the same tokens
+    from rwkv_mlx_b200.moe import lora_combine, lora_down, permute, router_forward
+
+    x2 = x.view(ntok, C)
+    with torch.no_grad():
+        base_out = base(x).view(ntok, C)
+
+    def moe_only():
+        r = router_forward(x2, layer.router.gate.weight, 2, layer.router.bias)
+        perm, inv, off = permute(r["inds"], 8)
+        h = lora_down(x2, A.half(), perm, off, 2)
+        return lora_combine(base_out, h, Bw.half(), r["inds"], r["scores"], inv)
+
+    for _ in range(args.warmup):
+        moe_only()
+    moe_ms = cuda_timed(moe_only, args.steps)  # local kernels on this rank's tokens (also under --ep)
+    hbm, _, src = peaks()
+    algo = ntok * (3 * C * 2 + 2 * (4 + 2))  # x read, base read, out write, inds+scores
+    gbs = algo / (moe_ms / 1e3) / 1e9
+    return {"metric": "LoRA-MoE ChannelMix tok/s", "value": ntok * ws / (ms / 1e3), "unit": "tok/s",
+            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp16 (fp32 router)", "data": "synthetic",
+            "config": {"workload": "LoRA-MoE CMix D768 F3072 E8 r16 top2 (BASELINE configs[3])",
+                       "tokens_per_gpu": ntok,
+                       "parallelism": f"ep{ws} (NCCL all-to-all)" if ep else f"dp{ws} (experts replicated)",
+                       "l2": "x and outputs (3 x 100 MB) larger than L2"},
+            "gpu_launches": launches,
+            "roofline": {"kernel": "MoE path (router+permute+lora_down+combine)", "bound": "hbm", "achieved": gbs,
+                         "peak": hbm, "unit": "GB/s", "frac": gbs / hbm, "traffic": None, "launch_ms": moe_ms,
+                         "algorithmic_bytes": algo, "peak_source": src},
+            "clocks": clocks}
+
+
+def run_decode(args, ws, rank, dev):
+    """Batched RNN-mode decode: L12 D768, 256 sequences per GPU whose
+    state comes from a 512-token GPT-mode prefill, greedy steps; tok/s over all ranks."""
+    from rwkv_mlx_b200 import _native
+
+    Bs, P = args.decode_seqs, args.decode_prompt
+    cfg, model = build_model(dev, CFG_L12, seed=0)
+    g = torch.Generator(device=dev).manual_seed(99 + rank)
+    prompt = torch.randint(0, 65536, (Bs, P), device=dev, generator=g)
+    with torch.no_grad():
+        logits, _, states = model.forward_with_state(prompt)
+        tok = logits[:, -1].argmax(-1)
+        del logits
+
+    def step():
+        nonlocal tok
+        with torch.no_grad():
+            lg = model.forward_rnn_batch(tok, states)
+            tok = lg.argmax(-1)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    l0 = _native.launch_count
+    barrier(ws)
+    clk = ClockSampler(dev)
+    ms = cuda_timed(step, args.steps)
+    clocks = clk.stop()
+    launches = _native.launch_count - l0
+    ms = max_over_ranks(ms, ws)
+    hbm, _, src = peaks()
+    # the state step kernel's bytes: state read+write + 7 vectors per (seq, head), 12 layers
+    return {"metric": "decode tok/s (L12 D768, 256 seqs)", "value": Bs * ws / (ms / 1e3), "unit": "tok/s",
+            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp16 (fp32 state)", "data": "synthetic",
+            "config": {"workload": "RNN-mode greedy decode (BASELINE configs[2])", "seqs_per_gpu": Bs,
+                       "prompt": P, "parallelism": f"dp{ws}"},
+            "gpu_launches": launches, "clocks": clocks}
+
+
 def run_reference(args):
     """CPU restatement of the reference path, rank 0 only."""
     rank = int(os.environ.get("RANK", "0"))
@@ -344,7 +468,11 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="prefill", choices=["prefill", "wkv_fwd", "wkv_bwd"])
+    ap.add_argument("--workload", default="prefill", choices=["prefill", "wkv_fwd", "wkv_bwd", "moe", "decode"])
+    ap.add_argument("--moe-tokens", type=int, default=65536)
+    ap.add_argument("--ep", action="store_true", help="moe workload: expert-parallel over the ranks")
+    ap.add_argument("--decode-seqs", type=int, default=256)
+    ap.add_argument("--decode-prompt", type=int, default=512)
     ap.add_argument("--batch", type=int, default=8)
     ap.add_argument("--seq", type=int, default=4096)
     ap.add_argument("--cpu-sample-tokens", type=int, default=128)
@@ -362,6 +490,10 @@ def main():
     torch.cuda.set_device(dev)
     if args.workload == "prefill":
         line = run_prefill(args, ws, rank, dev)
+    elif args.workload == "moe":
+        line = run_moe(args, ws, rank, dev)
+    elif args.workload == "decode":
+        line = run_decode(args, ws, rank, dev)
     else:
         line = run_wkv(args, ws, rank, dev, backward=args.workload == "wkv_bwd")
     if rank == 0 and ws == 1 and not args.no_cpu_baseline and args.workload == "prefill":

@@ -170,6 +170,23 @@ int rwkv_moe_lora_combine(const void* base, const float* h, const void* B,
                           void* out, int ntok, int C, int R, int E, int topk, int dtype,
                           void* stream);
 
+/* Expert-parallel dispatch / combine helpers (no counterpart in the reference,
+ * which runs on one device; they move the routed rows of moe.py:139-145 between
+ * GPUs and back).
+ * gather_rows:  rows[p] = x[perm[p] / topk]          (C * sizeof(dtype) % 16 == 0)
+ * lora_up:      y[dst] = h[p] @ B[e(p)], e(p) from offsets, dst = out_index[p] (or p
+ *               when out_index is NULL); h (n, R) fp32, B (E, R, C), y (n, C) dtype.
+ * combine_rows: out[t] = base[t] + sum_s scores[t,s] * rows[inv[t*topk + s]]
+ *               (base may be NULL or equal to out).                            */
+int rwkv_moe_gather_rows(const void* x, const int32_t* perm, void* rows, int n, int C, int topk,
+                         int dtype, void* stream);
+int rwkv_moe_lora_up(const float* h, const void* B, const int32_t* offsets,
+                     const int32_t* out_index, void* y, int n, int C, int R, int E, int dtype,
+                     void* stream);
+int rwkv_moe_combine_rows(const void* base, const void* rows, const void* scores,
+                          const int32_t* inv, void* out, int ntok, int C, int topk, int dtype,
+                          void* stream);
+
 /* sum_{i<j} ||A_i^T A_j||_F^2 over the expert down-projections
  * (LoRAMoE_CMix.orthogonal_loss, moe.py:149-163).  A (E, C, R) dtype;
  * out: one fp32 scalar.  R <= 64.                                          */

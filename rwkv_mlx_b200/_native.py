@@ -49,6 +49,9 @@ SIGNATURES = {
     "rwkv_moe_lora_down": (_I, [_P] * 5 + [_I] * 6 + [_P]),
     "rwkv_moe_lora_combine": (_I, [_P] * 7 + [_I] * 6 + [_P]),
     "rwkv_moe_ortho_loss": (_I, [_P] * 2 + [_I] * 4 + [_P]),
+    "rwkv_moe_gather_rows": (_I, [_P] * 3 + [_I] * 4 + [_P]),
+    "rwkv_moe_lora_up": (_I, [_P] * 5 + [_I] * 5 + [_P]),
+    "rwkv_moe_combine_rows": (_I, [_P] * 5 + [_I] * 4 + [_P]),
 }
 
 _lib = None
@@ -89,7 +92,8 @@ def lib() -> ctypes.CDLL:
 KERNELS_PER_CALL = {
     "rwkv_wkv7_forward": 1, "rwkv_wkv7_backward": 1, "rwkv_wkv7_step": 1,
     "rwkv_moe_router": 2, "rwkv_moe_router_noalloc": 2, "rwkv_moe_permute": 3, "rwkv_moe_lora_down": 1,
-    "rwkv_moe_lora_combine": 1, "rwkv_moe_ortho_loss": 1,
+    "rwkv_moe_lora_combine": 1, "rwkv_moe_ortho_loss": 1, "rwkv_moe_gather_rows": 1,
+    "rwkv_moe_lora_up": 1, "rwkv_moe_combine_rows": 1,
 }
 launch_count = 0
 

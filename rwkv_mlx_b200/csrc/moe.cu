@@ -364,6 +364,68 @@ __global__ void __launch_bounds__(1024)
     }
 }
 
+// ---------------------------------------------------------------------------
+// Expert-parallel helpers: dispatch gather, per-entry up-projection, combine of rows.
+// ---------------------------------------------------------------------------
+// rows[p] = x[perm[p] / topk]; one warp per row, 16-byte vectors.
+template <typename T>
+__global__ void __launch_bounds__(256)
+    moe_gather_rows_kernel(const T* __restrict__ x, const int32_t* __restrict__ perm,
+                           T* __restrict__ rows, int n, int C, int topk) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nv = C * (int)sizeof(T) / 16;
+    for (int p = blockIdx.x * 8 + warp; p < n; p += gridDim.x * 8) {
+        const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)(perm[p] / topk) * C);
+        uint4* dst = reinterpret_cast<uint4*>(rows + (size_t)p * C);
+        for (int i = lane; i < nv; i += 32) dst[i] = src[i];
+    }
+}
+
+// y[dst(p)] = h[p] @ B[e(p)], e(p) from offsets, dst(p) = out_index ? out_index[p] : p.
+template <typename T, int R>
+__global__ void __launch_bounds__(256)
+    moe_lora_up_kernel(const float* __restrict__ h, const T* __restrict__ B,
+                       const int32_t* __restrict__ offsets, const int32_t* __restrict__ out_index,
+                       T* __restrict__ y, int n, int C, int E) {
+    __shared__ int offs[257];
+    for (int i = threadIdx.x; i <= E; i += blockDim.x) offs[i] = offsets[i];
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int p = blockIdx.x * 8 + warp; p < n; p += gridDim.x * 8) {
+        int e = 0;
+        while (e + 1 < E && offs[e + 1] <= p) e++;
+        float hv[R];
+#pragma unroll
+        for (int q = 0; q < R; q++) hv[q] = h[(size_t)p * R + q];
+        const T* Be = B + (size_t)e * R * C;
+        T* out = y + (size_t)(out_index ? out_index[p] : p) * C;
+        for (int c = lane; c < C; c += 32) {
+            float d = 0.f;
+#pragma unroll
+            for (int q = 0; q < R; q++) d = fmaf(hv[q], to_f32(Be[(size_t)q * C + c]), d);
+            out[c] = from_f32<T>(d);
+        }
+    }
+}
+
+// out[t] = base[t] + sum_s scores[t, s] * rows[inv[t * topk + s]]
+template <typename T>
+__global__ void __launch_bounds__(256)
+    moe_combine_rows_kernel(const T* base, const T* __restrict__ rows, const T* __restrict__ scores,
+                            const int32_t* __restrict__ inv, T* out, int ntok, int C, int topk) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int t = blockIdx.x * 8 + warp; t < ntok; t += gridDim.x * 8) {
+        for (int c = lane; c < C; c += 32) {
+            float o = base ? to_f32(base[(size_t)t * C + c]) : 0.f;
+            for (int s = 0; s < topk; s++) {
+                const int ent = t * topk + s;
+                o = fmaf(to_f32(scores[ent]), to_f32(rows[(size_t)inv[ent] * C + c]), o);
+            }
+            out[(size_t)t * C + c] = from_f32<T>(o);
+        }
+    }
+}
+
 }  // namespace rwkv
 
 // ===========================================================================
@@ -576,5 +638,50 @@ extern "C" int rwkv_moe_router_noalloc(const void* x, const float* gate_w, const
     });
     if (rc) return rc;
     moe_router_finalize_kernel<<<1, 64, 0, st>>>(pf, pc, nb, ntok, E, topk, stats, counts);
+    return check_launch();
+}
+
+static int ep_grid(int n) { return (n + 7) / 8 < 148 * 16 ? (n + 7) / 8 : 148 * 16; }
+
+extern "C" int rwkv_moe_gather_rows(const void* x, const int32_t* perm, void* rows, int n, int C,
+                                    int topk, int dtype, void* stream) {
+    if (n <= 0 || C <= 0 || topk <= 0) return RWKV_ERR_SHAPE;
+    if (!x || !perm || !rows) return RWKV_ERR_ARG;
+    if (!aligned(x, 16) || !aligned(rows, 16)) return RWKV_ERR_ALIGN;
+    cudaStream_t st = (cudaStream_t)stream;
+    RWKV_DISPATCH_DTYPE(dtype, T, {
+        if ((C * (int)sizeof(T)) % 16) return RWKV_ERR_SHAPE;
+        moe_gather_rows_kernel<T><<<ep_grid(n), 256, 0, st>>>((const T*)x, perm, (T*)rows, n, C, topk);
+    });
+    return check_launch();
+}
+
+extern "C" int rwkv_moe_lora_up(const float* h, const void* B, const int32_t* offsets,
+                                const int32_t* out_index, void* y, int n, int C, int R, int E,
+                                int dtype, void* stream) {
+    if (n <= 0 || C <= 0 || E <= 0 || E > 256) return RWKV_ERR_SHAPE;
+    if (R != 8 && R != 16 && R != 32) return RWKV_ERR_SHAPE;
+    if (!h || !B || !offsets || !y) return RWKV_ERR_ARG;
+    cudaStream_t st = (cudaStream_t)stream;
+    const int grid = ep_grid(n);
+    RWKV_DISPATCH_DTYPE(dtype, T, {
+        switch (R) {
+            case 8: moe_lora_up_kernel<T, 8><<<grid, 256, 0, st>>>(h, (const T*)B, offsets, out_index, (T*)y, n, C, E); break;
+            case 16: moe_lora_up_kernel<T, 16><<<grid, 256, 0, st>>>(h, (const T*)B, offsets, out_index, (T*)y, n, C, E); break;
+            default: moe_lora_up_kernel<T, 32><<<grid, 256, 0, st>>>(h, (const T*)B, offsets, out_index, (T*)y, n, C, E); break;
+        }
+    });
+    return check_launch();
+}
+
+extern "C" int rwkv_moe_combine_rows(const void* base, const void* rows, const void* scores,
+                                     const int32_t* inv, void* out, int ntok, int C, int topk,
+                                     int dtype, void* stream) {
+    if (ntok <= 0 || C <= 0 || topk <= 0) return RWKV_ERR_SHAPE;
+    if (!rows || !scores || !inv || !out) return RWKV_ERR_ARG;
+    cudaStream_t st = (cudaStream_t)stream;
+    RWKV_DISPATCH_DTYPE(dtype, T, moe_combine_rows_kernel<T><<<ep_grid(ntok), 256, 0, st>>>(
+                                      (const T*)base, (const T*)rows, (const T*)scores, inv, (T*)out,
+                                      ntok, C, topk));
     return check_launch();
 }

@@ -193,6 +193,42 @@ int rwkv_moe_combine_rows(const void* base, const void* rows, const void* scores
 int rwkv_moe_ortho_loss(const void* A, float* out, int E, int C, int R, int dtype,
                         void* stream);
 
+/* ------------------------------------------------------------------------ */
+/* Fused element-wise kernels of the block around WKV-7 (the callers defined in
+ * rwkv_mlx/model.py:187-263, 312-327).  Activations (rows = B*T, C) in dtype.
+ *
+ * rwkv_lerp: out[m] = x + (shift(x) - x) * mix[m] for m < M, shift along T with a
+ *   zero first row per sequence (model.py:67-75, 188-196, 260-261); mix (M, C);
+ *   out (M, rows, C).  C * sizeof(dtype) % 16 == 0.
+ * rwkv_tmix_mid (model.py:200-226): with wl = tanh(xw@w1)@w2, al = (xa@a1)@a2,
+ *   vl = (xv@v1)@v2 already computed,
+ *     w_out = -softplus(-(w0 + wl)) - 0.5                (fp32; w0 fp32)
+ *     v_out = v + (v_first - v) * sigmoid(v0 + vl)       (v if layer0)
+ *     a     = sigmoid(a0 + al)
+ *     kk    = normalize_per_64(k * k_k)                  (eps 1e-12)
+ *     k_out = k * (1 + (a - 1) * k_a);  a_out = -kk;  b_out = kk * a
+ * rwkv_tmix_post (model.py:229-239): out = (GroupNorm(y) + bonus * v) * g with
+ *   GroupNorm over H groups (per_head = 0: MLX's default grouping, channel c in
+ *   group c % H; per_head = 1: contiguous groups), weight ln_w, bias ln_b, eps;
+ *   bonus per head = sum(r * k * r_k).
+ * rwkv_relu_sq: x = relu(x)^2 in place (model.py:262).
+ * rwkv_add_layernorm: x_out = x + delta (skipped when delta is NULL);
+ *   y = LayerNorm(x_out) with weight w, bias b, eps (model.py:315-326). */
+int rwkv_lerp(const void* x, const void* mix, void* out, int M, long long rows, int T, int C,
+              int dtype, void* stream);
+int rwkv_tmix_mid(const void* k, const void* v, const void* wl, const void* al, const void* vl,
+                  const void* v_first, const float* w0, const void* a0, const void* v0,
+                  const void* k_k, const void* k_a, float* w_out, void* k_out, void* v_out,
+                  void* a_out, void* b_out, long long rows, int C, int layer0, int dtype,
+                  void* stream);
+int rwkv_tmix_post(const void* y, const void* r, const void* k, const void* v, const void* g,
+                   const void* ln_w, const void* ln_b, const void* r_k, void* out, long long rows,
+                   int C, int H, float eps, int per_head, int dtype, void* stream);
+int rwkv_relu_sq(void* x, long long n, int dtype, void* stream);
+int rwkv_add_layernorm(const void* x, const void* delta, const void* w, const void* b,
+                       void* x_out, void* y, long long rows, int C, float eps, int dtype,
+                       void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,317 @@
+// Fused element-wise kernels of the RWKV-v7 block around the WKV-7 and GEMM calls
+// (the callers of the hot path, rwkv_mlx/model.py:187-263).  Each replaces a chain
+// of separate element-wise passes over (B*T, C) activations with one pass.
+//
+//   lerp         : out[m] = x + (shift(x) - x) * mix[m]      (model.py:188-196, :260-261)
+//   tmix_mid     : decay w, value residual, ICLR a, kk normalisation, k scaling,
+//                  WKV's a/b inputs                          (model.py:200-226)
+//   tmix_post    : GroupNorm (MLX strided or per-head groups), bonus, gate (model.py:229-239)
+//   relu_sq      : relu(x)^2 in place                        (model.py:262)
+//   add_layernorm: x += delta; y = LayerNorm(x)              (model.py:315-326)
+// Arithmetic is fp32; inputs/outputs in the activation dtype (w in fp32).
+#include "common.cuh"
+
+namespace rwkv {
+
+template <typename T>
+struct Vec {
+    static constexpr int N = 16 / sizeof(T);
+    uint4 raw;
+    __device__ __forceinline__ void load(const T* p) { raw = *reinterpret_cast<const uint4*>(p); }
+    __device__ __forceinline__ void store(T* p) const { *reinterpret_cast<uint4*>(p) = raw; }
+    __device__ __forceinline__ float get(int i) const { return to_f32(reinterpret_cast<const T*>(&raw)[i]); }
+    __device__ __forceinline__ void set(int i, float v) { reinterpret_cast<T*>(&raw)[i] = from_f32<T>(v); }
+    __device__ __forceinline__ void zero() { raw = make_uint4(0, 0, 0, 0); }
+};
+
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(256)
+    lerp_kernel(const T* __restrict__ x, const T* __restrict__ mix, T* __restrict__ out, int M,
+                long long rows, int Tlen, int C) {
+    constexpr int V = Vec<T>::N;
+    const int nv = C / V;
+    const long long total = rows * nv;
+    for (long long q = blockIdx.x * (long long)blockDim.x + threadIdx.x; q < total;
+         q += (long long)gridDim.x * blockDim.x) {
+        const long long row = q / nv;
+        const int c0 = (int)(q % nv) * V;
+        Vec<T> xv, pv;
+        xv.load(x + row * C + c0);
+        if (row % Tlen) pv.load(x + (row - 1) * C + c0);
+        else pv.zero();
+        float xf[V], dx[V];
+#pragma unroll
+        for (int i = 0; i < V; i++) xf[i] = xv.get(i), dx[i] = pv.get(i) - xf[i];
+        for (int m = 0; m < M; m++) {
+            Vec<T> mv, ov;
+            mv.load(mix + (size_t)m * C + c0);
+#pragma unroll
+            for (int i = 0; i < V; i++) ov.set(i, fmaf(dx[i], mv.get(i), xf[i]));
+            ov.store(out + ((size_t)m * rows + row) * C + c0);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// one warp per (row, head of 64 channels); lane owns channels 2*lane, 2*lane+1
+template <typename T>
+__global__ void __launch_bounds__(256)
+    tmix_mid_kernel(const T* __restrict__ k, const T* __restrict__ v, const T* __restrict__ wl,
+                    const T* __restrict__ al, const T* __restrict__ vl, const T* __restrict__ vfirst,
+                    const float* __restrict__ w0, const T* __restrict__ a0, const T* __restrict__ v0,
+                    const T* __restrict__ kkp, const T* __restrict__ kap, float* __restrict__ w_out,
+                    T* __restrict__ k_out, T* __restrict__ v_out, T* __restrict__ a_out,
+                    T* __restrict__ b_out, long long rows, int C, int layer0) {
+    const int H = C / 64;
+    const long long units = rows * H;
+    const int lane = threadIdx.x & 31;
+    for (long long u = (blockIdx.x * (long long)blockDim.x + threadIdx.x) / 32; u < units;
+         u += (long long)gridDim.x * blockDim.x / 32) {
+        const long long row = u / H;
+        const int c = (int)(u % H) * 64 + 2 * lane;
+        const size_t o = row * C + c;
+        float kv[2], vv[2], av[2], kk[2], ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < 2; i++) {
+            const float z = w0[c + i] + to_f32(wl[o + i]);
+            // -softplus(-z) - 0.5, softplus(s) = max(s, 0) + log1p(exp(-|s|))
+            const float s = -z;
+            w_out[o + i] = -(fmaxf(s, 0.f) + log1pf(expf(-fabsf(s)))) - 0.5f;
+            kv[i] = to_f32(k[o + i]);
+            vv[i] = to_f32(v[o + i]);
+            if (!layer0) {
+                const float gte = 1.f / (1.f + expf(-(to_f32(v0[c + i]) + to_f32(vl[o + i]))));
+                vv[i] = fmaf(to_f32(vfirst[o + i]) - vv[i], gte, vv[i]);
+            }
+            av[i] = 1.f / (1.f + expf(-(to_f32(a0[c + i]) + to_f32(al[o + i]))));
+            kk[i] = kv[i] * to_f32(kkp[c + i]);
+            ss = fmaf(kk[i], kk[i], ss);
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+        const float inv = 1.f / (sqrtf(ss) + 1e-12f);
+#pragma unroll
+        for (int i = 0; i < 2; i++) {
+            const float kn = kk[i] * inv;
+            k_out[o + i] = from_f32<T>(kv[i] * fmaf(av[i] - 1.f, to_f32(kap[c + i]), 1.f));
+            v_out[o + i] = from_f32<T>(vv[i]);
+            a_out[o + i] = from_f32<T>(-kn);
+            b_out[o + i] = from_f32<T>(kn * av[i]);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// one warp per row; deterministic group / head reductions through a per-warp
+// [32][H+1] partial-sum table (lane-private rows, summed in lane order)
+template <typename T>
+__global__ void __launch_bounds__(128)
+    tmix_post_kernel(const T* __restrict__ y, const T* __restrict__ r, const T* __restrict__ k,
+                     const T* __restrict__ v, const T* __restrict__ g, const T* __restrict__ lnw,
+                     const T* __restrict__ lnb, const T* __restrict__ rk, T* __restrict__ out,
+                     long long rows, int C, int H, float eps, int per_head) {
+    extern __shared__ float sm_post[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int LDP = H + 1;
+    float* part = sm_post + (size_t)warp * (32 * LDP + 3 * H);
+    float* mean = part + 32 * LDP;
+    float* rstd = mean + H;
+    float* hdot = rstd + H;
+    const int gsz = C / H, N = C / H;
+    auto grp = [&](int c) { return per_head ? c / gsz : c % H; };
+    auto reduce_to = [&](float* dst) {
+        __syncwarp();
+        for (int gi = lane; gi < H; gi += 32) {
+            float s = 0.f;
+            for (int l = 0; l < 32; l++) s += part[l * LDP + gi];
+            dst[gi] = s;
+        }
+        __syncwarp();
+    };
+    for (long long row = blockIdx.x * 4LL + warp; row < rows; row += gridDim.x * 4LL) {
+        const size_t base = row * C;
+        for (int gi = 0; gi < H; gi++) part[lane * LDP + gi] = 0.f;
+        for (int c = lane; c < C; c += 32) part[lane * LDP + grp(c)] += to_f32(y[base + c]);
+        reduce_to(mean);
+        for (int gi = lane; gi < H; gi += 32) mean[gi] /= (float)gsz;
+        __syncwarp();
+        for (int gi = 0; gi < H; gi++) part[lane * LDP + gi] = 0.f;
+        for (int c = lane; c < C; c += 32) {
+            const float d = to_f32(y[base + c]) - mean[grp(c)];
+            part[lane * LDP + grp(c)] += d * d;
+        }
+        reduce_to(rstd);
+        for (int gi = lane; gi < H; gi += 32) rstd[gi] = rsqrtf(rstd[gi] / (float)gsz + eps);
+        __syncwarp();
+        for (int gi = 0; gi < H; gi++) part[lane * LDP + gi] = 0.f;
+        for (int c = lane; c < C; c += 32)
+            part[lane * LDP + c / N] += to_f32(r[base + c]) * to_f32(k[base + c]) * to_f32(rk[c]);
+        reduce_to(hdot);
+        for (int c = lane; c < C; c += 32) {
+            const int gi = grp(c);
+            float o = (to_f32(y[base + c]) - mean[gi]) * rstd[gi] * to_f32(lnw[c]) + to_f32(lnb[c]);
+            o = fmaf(hdot[c / N], to_f32(v[base + c]), o);
+            out[base + c] = from_f32<T>(o * to_f32(g[base + c]));
+        }
+        __syncwarp();
+    }
+}
+
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(256) relu_sq_kernel(T* __restrict__ x, long long nvec) {
+    constexpr int V = Vec<T>::N;
+    for (long long q = blockIdx.x * (long long)blockDim.x + threadIdx.x; q < nvec;
+         q += (long long)gridDim.x * blockDim.x) {
+        Vec<T> a;
+        a.load(x + q * V);
+#pragma unroll
+        for (int i = 0; i < V; i++) {
+            const float f = fmaxf(a.get(i), 0.f);
+            a.set(i, f * f);
+        }
+        a.store(x + q * V);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// one warp per row: x_out = x (+ delta); y = (x_out - mean) / sqrt(var + eps) * w + b
+template <typename T>
+__global__ void __launch_bounds__(256)
+    add_layernorm_kernel(const T* x, const T* __restrict__ delta, const T* __restrict__ w,
+                         const T* __restrict__ b, T* x_out, T* __restrict__ y, long long rows, int C,
+                         float eps) {
+    constexpr int V = Vec<T>::N;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nv = C / V;
+    for (long long row = blockIdx.x * 8LL + warp; row < rows; row += gridDim.x * 8LL) {
+        const size_t base = row * C;
+        float s = 0.f;
+        for (int q = lane; q < nv; q += 32) {
+            Vec<T> a;
+            a.load(x + base + q * V);
+            if (delta) {
+                Vec<T> d;
+                d.load(delta + base + q * V);
+#pragma unroll
+                for (int i = 0; i < V; i++) a.set(i, a.get(i) + d.get(i));
+                a.store(x_out + base + q * V);
+            }
+#pragma unroll
+            for (int i = 0; i < V; i++) s += a.get(i);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        const float mean = s / (float)C;
+        const T* src = delta ? x_out : x;
+        __syncwarp();
+        float s2 = 0.f;
+        for (int q = lane; q < nv; q += 32) {
+            Vec<T> a;
+            a.load(src + base + q * V);
+#pragma unroll
+            for (int i = 0; i < V; i++) {
+                const float d = a.get(i) - mean;
+                s2 = fmaf(d, d, s2);
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+        const float rs = rsqrtf(s2 / (float)C + eps);
+        for (int q = lane; q < nv; q += 32) {
+            Vec<T> a, wv, bv, o;
+            a.load(src + base + q * V);
+            wv.load(w + q * V);
+            bv.load(b + q * V);
+#pragma unroll
+            for (int i = 0; i < V; i++) o.set(i, fmaf((a.get(i) - mean) * rs, wv.get(i), bv.get(i)));
+            o.store(y + base + q * V);
+        }
+    }
+}
+
+static int grid_for(long long work, int per_block) {
+    long long g = (work + per_block - 1) / per_block;
+    return (int)(g < 148 * 32 ? (g > 0 ? g : 1) : 148 * 32);
+}
+
+}  // namespace rwkv
+
+using namespace rwkv;
+
+extern "C" int rwkv_lerp(const void* x, const void* mix, void* out, int M, long long rows, int T,
+                         int C, int dtype, void* stream) {
+    if (M <= 0 || rows <= 0 || T <= 0 || C <= 0) return RWKV_ERR_SHAPE;
+    if (!x || !mix || !out) return RWKV_ERR_ARG;
+    if (!aligned(x, 16) || !aligned(mix, 16) || !aligned(out, 16)) return RWKV_ERR_ALIGN;
+    cudaStream_t st = (cudaStream_t)stream;
+    RWKV_DISPATCH_DTYPE(dtype, T_, {
+        if (C % Vec<T_>::N) return RWKV_ERR_SHAPE;
+        lerp_kernel<T_><<<grid_for(rows * (C / Vec<T_>::N), 256), 256, 0, st>>>(
+            (const T_*)x, (const T_*)mix, (T_*)out, M, rows, T, C);
+    });
+    return check_launch();
+}
+
+extern "C" int rwkv_tmix_mid(const void* k, const void* v, const void* wl, const void* al,
+                             const void* vl, const void* v_first, const float* w0, const void* a0,
+                             const void* v0, const void* k_k, const void* k_a, float* w_out,
+                             void* k_out, void* v_out, void* a_out, void* b_out, long long rows,
+                             int C, int layer0, int dtype, void* stream) {
+    if (rows <= 0 || C <= 0 || C % 64) return RWKV_ERR_SHAPE;
+    if (!k || !v || !wl || !al || !w0 || !a0 || !k_k || !k_a || !w_out || !k_out || !v_out || !a_out || !b_out)
+        return RWKV_ERR_ARG;
+    if (!layer0 && (!vl || !v_first || !v0)) return RWKV_ERR_ARG;
+    cudaStream_t st = (cudaStream_t)stream;
+    RWKV_DISPATCH_DTYPE(dtype, T_, tmix_mid_kernel<T_><<<grid_for(rows * (C / 64), 8), 256, 0, st>>>(
+                                       (const T_*)k, (const T_*)v, (const T_*)wl, (const T_*)al, (const T_*)vl,
+                                       (const T_*)v_first, w0, (const T_*)a0, (const T_*)v0, (const T_*)k_k,
+                                       (const T_*)k_a, w_out, (T_*)k_out, (T_*)v_out, (T_*)a_out, (T_*)b_out,
+                                       rows, C, layer0));
+    return check_launch();
+}
+
+extern "C" int rwkv_tmix_post(const void* y, const void* r, const void* k, const void* v,
+                              const void* g, const void* ln_w, const void* ln_b, const void* r_k,
+                              void* out, long long rows, int C, int H, float eps, int per_head,
+                              int dtype, void* stream) {
+    if (rows <= 0 || C <= 0 || H <= 0 || H > 64 || C % H) return RWKV_ERR_SHAPE;
+    if (!y || !r || !k || !v || !g || !ln_w || !ln_b || !r_k || !out) return RWKV_ERR_ARG;
+    cudaStream_t st = (cudaStream_t)stream;
+    const size_t smem = 4 * (size_t)(32 * (H + 1) + 3 * H) * sizeof(float);
+    RWKV_DISPATCH_DTYPE(dtype, T_, tmix_post_kernel<T_><<<grid_for(rows, 4), 128, smem, st>>>(
+                                       (const T_*)y, (const T_*)r, (const T_*)k, (const T_*)v, (const T_*)g,
+                                       (const T_*)ln_w, (const T_*)ln_b, (const T_*)r_k, (T_*)out, rows, C, H, eps,
+                                       per_head));
+    return check_launch();
+}
+
+extern "C" int rwkv_relu_sq(void* x, long long n, int dtype, void* stream) {
+    if (n <= 0) return RWKV_ERR_SHAPE;
+    if (!x) return RWKV_ERR_ARG;
+    if (!aligned(x, 16)) return RWKV_ERR_ALIGN;
+    cudaStream_t st = (cudaStream_t)stream;
+    RWKV_DISPATCH_DTYPE(dtype, T_, {
+        if (n % Vec<T_>::N) return RWKV_ERR_SHAPE;
+        relu_sq_kernel<T_><<<grid_for(n / Vec<T_>::N, 256), 256, 0, st>>>((T_*)x, n / Vec<T_>::N);
+    });
+    return check_launch();
+}
+
+extern "C" int rwkv_add_layernorm(const void* x, const void* delta, const void* w, const void* b,
+                                  void* x_out, void* y, long long rows, int C, float eps, int dtype,
+                                  void* stream) {
+    if (rows <= 0 || C <= 0) return RWKV_ERR_SHAPE;
+    if (!x || !w || !b || !y || (delta && !x_out)) return RWKV_ERR_ARG;
+    const void* ps[6] = {x, delta, w, b, x_out, y};
+    for (const void* p : ps)
+        if (p && !aligned(p, 16)) return RWKV_ERR_ALIGN;
+    cudaStream_t st = (cudaStream_t)stream;
+    RWKV_DISPATCH_DTYPE(dtype, T_, {
+        if (C % Vec<T_>::N) return RWKV_ERR_SHAPE;
+        add_layernorm_kernel<T_><<<grid_for(rows, 8), 256, 0, st>>>((const T_*)x, (const T_*)delta, (const T_*)w,
+                                                                    (const T_*)b, (T_*)x_out, (T_*)y, rows, C, eps);
+    });
+    return check_launch();
+}

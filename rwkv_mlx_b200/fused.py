@@ -1,0 +1,74 @@
+"""Python front-ends of the fused element-wise kernels (csrc/fused.cu).
+
+They replace chains of separate torch element-wise passes in the block around the
+WKV-7 call (rwkv_mlx/model.py:187-263, 312-327); see include/rwkv_b200.h for the
+exact formulas.  Activations are contiguous CUDA tensors (B, T, C) or (rows, C).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _native as nat
+
+
+def _call(name, *args):
+    rc = getattr(nat.lib(), name)(*args)
+    nat.check(rc, name)
+
+
+def lerp(x: torch.Tensor, mix: torch.Tensor, T: int) -> torch.Tensor:
+    """x (..., C) with rows grouped in sequences of length T; mix (M, C) -> (M, rows, C)."""
+    C = x.shape[-1]
+    x = x.contiguous()
+    rows = x.numel() // C
+    mix = mix.to(x.dtype).contiguous().view(-1, C)
+    out = torch.empty((mix.shape[0], rows, C), device=x.device, dtype=x.dtype)
+    _call("rwkv_lerp", nat.ptr(x), nat.ptr(mix), nat.ptr(out), mix.shape[0], rows, T, C, nat.dtype_code(x),
+          nat.stream_ptr(x.device))
+    return out
+
+
+def tmix_mid(k, v, wl, al, vl, v_first, w0, a0, v0, k_k, k_a, layer0: bool):
+    C = k.shape[-1]
+    rows = k.numel() // C
+    dt = k.dtype
+    c = lambda t: None if t is None else t.to(dt).contiguous()
+    w_out = torch.empty(k.shape, device=k.device, dtype=torch.float32)
+    k_out, v_out, a_out, b_out = (torch.empty_like(k) for _ in range(4))
+    args = [c(k), c(v), c(wl), c(al), c(vl), c(v_first)]
+    _call("rwkv_tmix_mid", *[nat.ptr(t) for t in args], nat.ptr(w0.float().contiguous()), nat.ptr(c(a0)),
+          nat.ptr(c(v0)), nat.ptr(c(k_k)), nat.ptr(c(k_a)), nat.ptr(w_out), nat.ptr(k_out), nat.ptr(v_out),
+          nat.ptr(a_out), nat.ptr(b_out), rows, C, 1 if layer0 else 0, nat.dtype_code(k), nat.stream_ptr(k.device))
+    return w_out, k_out, v_out, a_out, b_out
+
+
+def tmix_post(y, r, k, v, g, ln_w, ln_b, r_k, H: int, eps: float, per_head: bool):
+    C = y.shape[-1]
+    rows = y.numel() // C
+    dt = y.dtype
+    c = lambda t: t.to(dt).contiguous()
+    out = torch.empty_like(y)
+    _call("rwkv_tmix_post", nat.ptr(c(y)), nat.ptr(c(r)), nat.ptr(c(k)), nat.ptr(c(v)), nat.ptr(c(g)),
+          nat.ptr(c(ln_w)), nat.ptr(c(ln_b)), nat.ptr(c(r_k)), nat.ptr(out), rows, C, H, float(eps),
+          1 if per_head else 0, nat.dtype_code(y), nat.stream_ptr(y.device))
+    return out
+
+
+def relu_sq_(x: torch.Tensor) -> torch.Tensor:
+    _call("rwkv_relu_sq", nat.ptr(x), x.numel(), nat.dtype_code(x), nat.stream_ptr(x.device))
+    return x
+
+
+def add_layernorm(x, delta, w, b, eps: float = 1e-5):
+    """Returns (x + delta, LayerNorm(x + delta)); with delta None returns (x, LayerNorm(x))."""
+    C = x.shape[-1]
+    rows = x.numel() // C
+    x = x.contiguous()
+    y = torch.empty_like(x)
+    x_out = torch.empty_like(x) if delta is not None else None
+    d = None if delta is None else delta.to(x.dtype).contiguous()
+    _call("rwkv_add_layernorm", nat.ptr(x), nat.ptr(d), nat.ptr(w.to(x.dtype).contiguous()),
+          nat.ptr(b.to(x.dtype).contiguous()), nat.ptr(x_out), nat.ptr(y), rows, C, float(eps), nat.dtype_code(x),
+          nat.stream_ptr(x.device))
+    return (x_out if delta is not None else x), y

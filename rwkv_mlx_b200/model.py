@@ -29,6 +29,7 @@ import torch
 import torch.nn.functional as F
 from torch import nn
 
+from . import fused as fz
 from .wkv7 import wkv7_recurrent, wkv7_step, wkv7_with_state
 
 
@@ -56,6 +57,7 @@ class RWKVConfig:
     moe_z_loss_coeff: float = 0.001
     moe_ortho_coeff: float = 0.001
     groupnorm: str = "mlx"
+    fused: bool = True  # fused element-wise kernels around WKV (False: op-by-op torch path)
 
     def __post_init__(self):
         if self.dim_att <= 0:
@@ -166,7 +168,38 @@ class RWKV_Tmix_x070(nn.Module):
         y = y + bonus
         return self.output((y * g).to(self.output.weight.dtype))
 
+    def _forward_fused(self, x, v_first, s0, return_state):
+        B, T, C = x.shape
+        H, N = self.n_head, self.head_size
+        mix = torch.cat([self.x_r, self.x_k, self.x_v, self.x_w, self.x_a, self.x_g]).view(6, C)
+        X = fz.lerp(x, mix, T)  # (6, B*T, C): r, k, v, w, a, g inputs
+        rkv = torch.bmm(X[0:3], torch.stack([self.receptance.weight, self.key.weight, self.value.weight]).transpose(1, 2))
+        r, k, v = rkv[0], rkv[1], rkv[2]
+        xv, xw, xa, xg = X[2], X[3], X[4], X[5]
+        wl = torch.tanh(xw @ self.w1) @ self.w2
+        al = (xa @ self.a1) @ self.a2
+        layer0 = self.layer_id == 0
+        vl = None if layer0 else (xv @ self.v1) @ self.v2
+        g = torch.sigmoid(xg @ self.g1) @ self.g2
+        vf = None if layer0 else v_first.reshape(B * T, C)
+        w, k2, v2, a_in, b_in = fz.tmix_mid(k, v, wl, al, vl, vf, self.w0.view(-1), self.a0.view(-1),
+                                             self.v0.view(-1), self.k_k.view(-1), self.k_a.view(-1), layer0)
+        sh = (B, T, C)
+        r, w, k2, v2, a_in, b_in = (t.view(sh) for t in (r, w, k2, v2, a_in, b_in))
+        if layer0:
+            v_first = v2
+        if return_state or s0 is not None:
+            y, sT = wkv7_with_state(r, w, k2, v2, a_in, b_in, s0=s0, head_size=N)
+        else:
+            y, sT = wkv7_recurrent(r, w, k2, v2, a_in, b_in, N), None
+        pre = fz.tmix_post(y, r, k2, v2, g.view(sh), self.ln_x.weight, self.ln_x.bias, self.r_k, H,
+                           self.ln_x.eps, self.config.groupnorm != "mlx")
+        out = self.output(pre)
+        return (out, v_first, sT) if return_state else (out, v_first)
+
     def forward(self, x, v_first, s0=None, return_state=False):
+        if self.config.fused and not torch.is_grad_enabled() and x.is_cuda:
+            return self._forward_fused(x, v_first, s0, return_state)
         xx = time_shift(x) - x
         r, w, k, v, a, g, kk, v_first = self._project(x, xx, v_first)
         if return_state or s0 is not None:
@@ -202,6 +235,9 @@ class RWKV_CMix_x070(nn.Module):
         self.value = nn.Linear(config.dim_ffn, C, bias=False)
 
     def forward(self, x):
+        if self.config.fused and not torch.is_grad_enabled() and x.is_cuda:
+            k = fz.lerp(x, self.x_k.view(1, -1), x.shape[1])[0].view(x.shape)
+            return self.value(fz.relu_sq_(self.key(k)))
         xx = time_shift(x) - x
         k = x + xx * self.x_k
         k = torch.relu(self.key(k)) ** 2
@@ -240,6 +276,23 @@ class Block(nn.Module):
         else:
             self.ffn = RWKV_CMix_x070(config, layer_id)
 
+    def forward_fused(self, x, pending, v_first, return_state=False):
+        """Block with the residual adds folded into the LayerNorm passes: ``pending``
+        is the previous block's ChannelMix output, not yet added to ``x``.  Returns
+        (x, pending_ffn_out, v_first, moe_losses, extra)."""
+        if self.layer_id == 0:
+            _, x = fz.add_layernorm(x, None, self.ln0.weight, self.ln0.bias, self.ln0.eps)
+        x, x1 = fz.add_layernorm(x, pending, self.ln1.weight, self.ln1.bias, self.ln1.eps)
+        res = self.att(x1, v_first, return_state=return_state)
+        x, x2 = fz.add_layernorm(x, res[0], self.ln2.weight, self.ln2.bias, self.ln2.eps)
+        extra = {}
+        if return_state:
+            extra = {"att_x_prev": x1[:, -1], "att_state": res[2], "ffn_x_prev": x2[:, -1]}
+        if self.is_moe:
+            ffn_out, aux, z = self.ffn(x2)
+            return x, ffn_out, res[1], (aux, z, self.ffn.orthogonal_loss()), extra
+        return x, self.ffn(x2), res[1], None, extra
+
     def forward(self, x, v_first, s0=None, return_state=False):
         if self.layer_id == 0:
             x = self.ln0(x)
@@ -276,6 +329,18 @@ class RWKV(nn.Module):
         aux_loss = torch.zeros((), device=x.device, dtype=torch.float32)
         cfg = self.config
         states = []
+        if cfg.fused and not torch.is_grad_enabled() and x.is_cuda:
+            pending = None
+            for blk in self.blocks:
+                x, pending, v_first, moe, extra = blk.forward_fused(x, pending, v_first, return_state)
+                if moe is not None:
+                    aux, z, ortho = moe
+                    aux_loss = aux_loss + cfg.moe_aux_loss_coeff * aux + cfg.moe_z_loss_coeff * z \
+                        + cfg.moe_ortho_coeff * ortho
+                if return_state:
+                    states.append(extra)
+            _, x = fz.add_layernorm(x, pending, self.ln_out.weight, self.ln_out.bias, self.ln_out.eps)
+            return self.head(x), aux_loss, states
         for blk in self.blocks:
             x, v_first, moe, extra = blk(x, v_first, return_state=return_state)
             if moe is not None:

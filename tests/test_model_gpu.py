@@ -96,3 +96,38 @@ def test_fp16_model_close_to_fp32():
         assert m.blocks[0].att.w0.dtype == torch.float32
         out, _ = m(idx)
     assert rel_rms(out.double().cpu().numpy(), ref.double().cpu().numpy()) < 2e-2
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16])
+def test_fused_path_matches_op_by_op_path(dtype):
+    """The fused element-wise kernels give the same logits as the op-by-op torch path."""
+    from rwkv_mlx_b200.model import cast_for_inference
+
+    for moe in (False, True):
+        cfg, m = _tiny(moe=moe)
+        if dtype == torch.float16:
+            cast_for_inference(m, torch.float16)
+        idx = torch.randint(0, cfg.vocab_size, (2, 48), device="cuda")
+        with torch.no_grad():
+            cfg.fused = True
+            a, aux_a = m(idx)
+            cfg.fused = False
+            b, aux_b = m(idx)
+            cfg.fused = True
+        tol = 1e-4 if dtype == torch.float32 else 3e-3
+        assert rel_rms(a.double().cpu().numpy(), b.double().cpu().numpy()) < tol, moe
+        assert abs(float(aux_a) - float(aux_b)) < 1e-4 * max(1.0, abs(float(aux_b)))
+
+
+def test_fused_per_head_groupnorm_and_state_output():
+    cfg, m = _tiny(groupnorm="per_head")
+    idx = torch.randint(0, cfg.vocab_size, (2, 40), device="cuda")
+    with torch.no_grad():
+        la, _, sa = m.forward_with_state(idx)
+        cfg.fused = False
+        lb, _, sb = m.forward_with_state(idx)
+        cfg.fused = True
+    assert rel_rms(la.cpu().numpy(), lb.cpu().numpy()) < 1e-4
+    for x, y in zip(sa, sb):
+        for key in x:
+            assert rel_rms(x[key].float().cpu().numpy(), y[key].float().cpu().numpy()) < 1e-4, key

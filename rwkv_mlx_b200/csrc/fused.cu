@@ -54,7 +54,8 @@ __global__ void __launch_bounds__(256)
 }
 
 // ---------------------------------------------------------------------------
-// one warp per (row, head of 64 channels); lane owns channels 2*lane, 2*lane+1
+// Vectorised: each lane owns V consecutive channels (one 16-byte vector); the 64
+// channels of a head are 64/V consecutive lanes, reduced with xor shuffles.
 template <typename T>
 __global__ void __launch_bounds__(256)
     tmix_mid_kernel(const T* __restrict__ k, const T* __restrict__ v, const T* __restrict__ wl,
@@ -63,96 +64,138 @@ __global__ void __launch_bounds__(256)
                     const T* __restrict__ kkp, const T* __restrict__ kap, float* __restrict__ w_out,
                     T* __restrict__ k_out, T* __restrict__ v_out, T* __restrict__ a_out,
                     T* __restrict__ b_out, long long rows, int C, int layer0) {
-    const int H = C / 64;
-    const long long units = rows * H;
-    const int lane = threadIdx.x & 31;
-    for (long long u = (blockIdx.x * (long long)blockDim.x + threadIdx.x) / 32; u < units;
-         u += (long long)gridDim.x * blockDim.x / 32) {
-        const long long row = u / H;
-        const int c = (int)(u % H) * 64 + 2 * lane;
-        const size_t o = row * C + c;
-        float kv[2], vv[2], av[2], kk[2], ss = 0.f;
+    constexpr int V = Vec<T>::N, LPH = 64 / V;  // lanes per head
+    const long long nvec = rows * (C / V);
+    for (long long q = blockIdx.x * (long long)blockDim.x + threadIdx.x; q - (threadIdx.x & 31) < nvec;
+         q += (long long)gridDim.x * blockDim.x) {
+        const bool live = q < nvec;
+        const long long row = live ? q / (C / V) : 0;
+        const int c0 = live ? (int)(q % (C / V)) * V : 0;
+        const size_t o = row * C + c0;
+        float kv[V], vv[V], av[V], kk[V], ss = 0.f;
+        if (live) {
+            Vec<T> K, Vv, WL, AL, A0, KK, KA;
+            K.load(k + o), Vv.load(v + o), WL.load(wl + o), AL.load(al + o);
+            A0.load(a0 + c0), KK.load(kkp + c0), KA.load(kap + c0);
+            float wo[V];
 #pragma unroll
-        for (int i = 0; i < 2; i++) {
-            const float z = w0[c + i] + to_f32(wl[o + i]);
-            // -softplus(-z) - 0.5, softplus(s) = max(s, 0) + log1p(exp(-|s|))
-            const float s = -z;
-            w_out[o + i] = -(fmaxf(s, 0.f) + log1pf(expf(-fabsf(s)))) - 0.5f;
-            kv[i] = to_f32(k[o + i]);
-            vv[i] = to_f32(v[o + i]);
-            if (!layer0) {
-                const float gte = 1.f / (1.f + expf(-(to_f32(v0[c + i]) + to_f32(vl[o + i]))));
-                vv[i] = fmaf(to_f32(vfirst[o + i]) - vv[i], gte, vv[i]);
+            for (int i = 0; i < V; i++) {
+                const float s = -(w0[c0 + i] + WL.get(i));
+                wo[i] = -(fmaxf(s, 0.f) + __logf(1.f + __expf(-fabsf(s)))) - 0.5f;
+                kv[i] = K.get(i);
+                vv[i] = Vv.get(i);
+                av[i] = 1.f / (1.f + __expf(-(A0.get(i) + AL.get(i))));
+                kk[i] = kv[i] * KK.get(i);
+                ss = fmaf(kk[i], kk[i], ss);
             }
-            av[i] = 1.f / (1.f + expf(-(to_f32(a0[c + i]) + to_f32(al[o + i]))));
-            kk[i] = kv[i] * to_f32(kkp[c + i]);
-            ss = fmaf(kk[i], kk[i], ss);
+#pragma unroll
+            for (int i = 0; i < V; i += 4)
+                *reinterpret_cast<float4*>(w_out + o + i) = make_float4(wo[i], wo[i + 1], wo[i + 2], wo[i + 3]);
+            if (!layer0) {
+                Vec<T> VL, VF, V0;
+                VL.load(vl + o), VF.load(vfirst + o), V0.load(v0 + c0);
+#pragma unroll
+                for (int i = 0; i < V; i++) {
+                    const float gte = 1.f / (1.f + __expf(-(V0.get(i) + VL.get(i))));
+                    vv[i] = fmaf(VF.get(i) - vv[i], gte, vv[i]);
+                }
+            }
+            Vec<T> KA2 = KA;
+#pragma unroll
+            for (int i = 0; i < V; i++) kv[i] = kv[i] * fmaf(av[i] - 1.f, KA2.get(i), 1.f);
         }
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-        const float inv = 1.f / (sqrtf(ss) + 1e-12f);
+        for (int off = 1; off < LPH; off <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+        if (live) {
+            const float inv = 1.f / (sqrtf(ss) + 1e-12f);
+            Vec<T> KO, VO, AO, BO;
 #pragma unroll
-        for (int i = 0; i < 2; i++) {
-            const float kn = kk[i] * inv;
-            k_out[o + i] = from_f32<T>(kv[i] * fmaf(av[i] - 1.f, to_f32(kap[c + i]), 1.f));
-            v_out[o + i] = from_f32<T>(vv[i]);
-            a_out[o + i] = from_f32<T>(-kn);
-            b_out[o + i] = from_f32<T>(kn * av[i]);
+            for (int i = 0; i < V; i++) {
+                const float kn = kk[i] * inv;
+                KO.set(i, kv[i]), VO.set(i, vv[i]), AO.set(i, -kn), BO.set(i, kn * av[i]);
+            }
+            KO.store(k_out + o), VO.store(v_out + o), AO.store(a_out + o), BO.store(b_out + o);
         }
     }
 }
 
 // ---------------------------------------------------------------------------
-// one warp per row; deterministic group / head reductions through a per-warp
-// [32][H+1] partial-sum table (lane-private rows, summed in lane order)
+// One warp per row.  The row of y is staged in shared memory (fp32); group
+// statistics: lane g sums its group's C/H members (fixed order, deterministic);
+// head bonus dots: per-vector partials reduced over the 64/V lanes of a head.
 template <typename T>
 __global__ void __launch_bounds__(128)
     tmix_post_kernel(const T* __restrict__ y, const T* __restrict__ r, const T* __restrict__ k,
                      const T* __restrict__ v, const T* __restrict__ g, const T* __restrict__ lnw,
                      const T* __restrict__ lnb, const T* __restrict__ rk, T* __restrict__ out,
                      long long rows, int C, int H, float eps, int per_head) {
+    constexpr int V = Vec<T>::N, LPH = 64 / V;
     extern __shared__ float sm_post[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int LDP = H + 1;
-    float* part = sm_post + (size_t)warp * (32 * LDP + 3 * H);
-    float* mean = part + 32 * LDP;
+    float* ys = sm_post + (size_t)warp * (C + 2 * H);
+    float* mean = ys + C;
     float* rstd = mean + H;
-    float* hdot = rstd + H;
-    const int gsz = C / H, N = C / H;
-    auto grp = [&](int c) { return per_head ? c / gsz : c % H; };
-    auto reduce_to = [&](float* dst) {
-        __syncwarp();
-        for (int gi = lane; gi < H; gi += 32) {
-            float s = 0.f;
-            for (int l = 0; l < 32; l++) s += part[l * LDP + gi];
-            dst[gi] = s;
-        }
-        __syncwarp();
-    };
+    const int gsz = C / H, nv = C / V;
     for (long long row = blockIdx.x * 4LL + warp; row < rows; row += gridDim.x * 4LL) {
         const size_t base = row * C;
-        for (int gi = 0; gi < H; gi++) part[lane * LDP + gi] = 0.f;
-        for (int c = lane; c < C; c += 32) part[lane * LDP + grp(c)] += to_f32(y[base + c]);
-        reduce_to(mean);
-        for (int gi = lane; gi < H; gi += 32) mean[gi] /= (float)gsz;
-        __syncwarp();
-        for (int gi = 0; gi < H; gi++) part[lane * LDP + gi] = 0.f;
-        for (int c = lane; c < C; c += 32) {
-            const float d = to_f32(y[base + c]) - mean[grp(c)];
-            part[lane * LDP + grp(c)] += d * d;
+        // stage y, bonus dot partials per vector
+        // every lane runs NJ vector slots; a head's 64/V lanes are all live or all idle
+        // because C is a multiple of 64
+        const int NJ = (nv + 31) / 32;  // <= 8 (checked on launch)
+        float hd[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            if (j >= NJ) break;
+            const int qv = lane + 32 * j;
+            float d = 0.f;
+            if (qv < nv) {
+                Vec<T> Y, R, K, RK;
+                Y.load(y + base + qv * V), R.load(r + base + qv * V), K.load(k + base + qv * V), RK.load(rk + qv * V);
+#pragma unroll
+                for (int i = 0; i < V; i++) {
+                    ys[qv * V + i] = Y.get(i);
+                    d = fmaf(R.get(i) * K.get(i), RK.get(i), d);
+                }
+            }
+#pragma unroll
+            for (int off = 1; off < LPH; off <<= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
+            hd[j] = d;
         }
-        reduce_to(rstd);
-        for (int gi = lane; gi < H; gi += 32) rstd[gi] = rsqrtf(rstd[gi] / (float)gsz + eps);
         __syncwarp();
-        for (int gi = 0; gi < H; gi++) part[lane * LDP + gi] = 0.f;
-        for (int c = lane; c < C; c += 32)
-            part[lane * LDP + c / N] += to_f32(r[base + c]) * to_f32(k[base + c]) * to_f32(rk[c]);
-        reduce_to(hdot);
-        for (int c = lane; c < C; c += 32) {
-            const int gi = grp(c);
-            float o = (to_f32(y[base + c]) - mean[gi]) * rstd[gi] * to_f32(lnw[c]) + to_f32(lnb[c]);
-            o = fmaf(hdot[c / N], to_f32(v[base + c]), o);
-            out[base + c] = from_f32<T>(o * to_f32(g[base + c]));
+        for (int gi = lane; gi < H; gi += 32) {
+            float s1 = 0.f;
+            if (per_head) {
+                for (int m = 0; m < gsz; m++) s1 += ys[gi * gsz + m];
+            } else {
+                for (int m = 0; m < gsz; m++) s1 += ys[gi + H * m];
+            }
+            const float mu = s1 / (float)gsz;
+            float s2 = 0.f;
+            if (per_head) {
+                for (int m = 0; m < gsz; m++) { const float dd = ys[gi * gsz + m] - mu; s2 = fmaf(dd, dd, s2); }
+            } else {
+                for (int m = 0; m < gsz; m++) { const float dd = ys[gi + H * m] - mu; s2 = fmaf(dd, dd, s2); }
+            }
+            mean[gi] = mu;
+            rstd[gi] = rsqrtf(s2 / (float)gsz + eps);
+        }
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            if (j >= NJ) break;
+            const int qv = lane + 32 * j;
+            if (qv >= nv) continue;
+            Vec<T> Vv, G, W, Bb, O;
+            Vv.load(v + base + qv * V), G.load(g + base + qv * V), W.load(lnw + qv * V), Bb.load(lnb + qv * V);
+#pragma unroll
+            for (int i = 0; i < V; i++) {
+                const int c = qv * V + i;
+                const int gi = per_head ? c / gsz : c % H;
+                float o = fmaf((ys[c] - mean[gi]) * rstd[gi], W.get(i), Bb.get(i));
+                o = fmaf(hd[j], Vv.get(i), o);
+                O.set(i, o * G.get(i));
+            }
+            O.store(out + base + qv * V);
         }
         __syncwarp();
     }
@@ -260,11 +303,16 @@ extern "C" int rwkv_tmix_mid(const void* k, const void* v, const void* wl, const
                              void* k_out, void* v_out, void* a_out, void* b_out, long long rows,
                              int C, int layer0, int dtype, void* stream) {
     if (rows <= 0 || C <= 0 || C % 64) return RWKV_ERR_SHAPE;
+    {
+        const void* ps[16] = {k, v, wl, al, vl, v_first, w0, a0, v0, k_k, k_a, w_out, k_out, v_out, a_out, b_out};
+        for (const void* p : ps)
+            if (p && !aligned(p, 16)) return RWKV_ERR_ALIGN;
+    }
     if (!k || !v || !wl || !al || !w0 || !a0 || !k_k || !k_a || !w_out || !k_out || !v_out || !a_out || !b_out)
         return RWKV_ERR_ARG;
     if (!layer0 && (!vl || !v_first || !v0)) return RWKV_ERR_ARG;
     cudaStream_t st = (cudaStream_t)stream;
-    RWKV_DISPATCH_DTYPE(dtype, T_, tmix_mid_kernel<T_><<<grid_for(rows * (C / 64), 8), 256, 0, st>>>(
+    RWKV_DISPATCH_DTYPE(dtype, T_, tmix_mid_kernel<T_><<<grid_for(rows * (C / Vec<T_>::N), 256), 256, 0, st>>>(
                                        (const T_*)k, (const T_*)v, (const T_*)wl, (const T_*)al, (const T_*)vl,
                                        (const T_*)v_first, w0, (const T_*)a0, (const T_*)v0, (const T_*)k_k,
                                        (const T_*)k_a, w_out, (T_*)k_out, (T_*)v_out, (T_*)a_out, (T_*)b_out,
@@ -276,10 +324,19 @@ extern "C" int rwkv_tmix_post(const void* y, const void* r, const void* k, const
                               const void* g, const void* ln_w, const void* ln_b, const void* r_k,
                               void* out, long long rows, int C, int H, float eps, int per_head,
                               int dtype, void* stream) {
-    if (rows <= 0 || C <= 0 || H <= 0 || H > 64 || C % H) return RWKV_ERR_SHAPE;
+    if (rows <= 0 || C <= 0 || H <= 0 || C % H || C / H != 64) return RWKV_ERR_SHAPE;
     if (!y || !r || !k || !v || !g || !ln_w || !ln_b || !r_k || !out) return RWKV_ERR_ARG;
+    {
+        const void* ps[9] = {y, r, k, v, g, ln_w, ln_b, r_k, out};
+        for (const void* p : ps)
+            if (!aligned(p, 16)) return RWKV_ERR_ALIGN;
+    }
     cudaStream_t st = (cudaStream_t)stream;
-    const size_t smem = 4 * (size_t)(32 * (H + 1) + 3 * H) * sizeof(float);
+    const size_t smem = 4 * (size_t)(C + 2 * H) * sizeof(float);
+    {
+        const int V = dtype == RWKV_F32 ? 4 : 8;
+        if (C / V > 8 * 32) return RWKV_ERR_SHAPE;  // <= 8 vectors per lane
+    }
     RWKV_DISPATCH_DTYPE(dtype, T_, tmix_post_kernel<T_><<<grid_for(rows, 4), 128, smem, st>>>(
                                        (const T_*)y, (const T_*)r, (const T_*)k, (const T_*)v, (const T_*)g,
                                        (const T_*)ln_w, (const T_*)ln_b, (const T_*)r_k, (T_*)out, rows, C, H, eps,

@@ -413,18 +413,22 @@ def run_decode(args, ws, rank, dev):
 
     Bs, P = args.decode_seqs, args.decode_prompt
     cfg, model = build_model(dev, CFG_L12, seed=0)
+    l0_build = None
     g = torch.Generator(device=dev).manual_seed(99 + rank)
     prompt = torch.randint(0, 65536, (Bs, P), device=dev, generator=g)
     with torch.no_grad():
         logits, _, states = model.forward_with_state(prompt)
         tok = logits[:, -1].argmax(-1)
         del logits
+    from rwkv_mlx_b200.model import DecodeGraph
+
+    l_pre = _native.launch_count
+    graph = DecodeGraph(model, states, tok, warmup=0)
+    l_graph = _native.launch_count
+    l0_build = l_pre  # launches recorded once in the graph, replayed per step
 
     def step():
-        nonlocal tok
-        with torch.no_grad():
-            lg = model.forward_rnn_batch(tok, states)
-            tok = lg.argmax(-1)
+        graph.step()
 
     for _ in range(args.warmup):
         step()
@@ -434,7 +438,7 @@ def run_decode(args, ws, rank, dev):
     clk = ClockSampler(dev)
     ms = cuda_timed(step, args.steps)
     clocks = clk.stop()
-    launches = _native.launch_count - l0
+    launches = (l_graph - l0_build) * args.steps  # our kernels captured per step x replays
     ms = max_over_ranks(ms, ws)
     hbm, _, src = peaks()
     # the state step kernel's bytes: state read+write + 7 vectors per (seq, head), 12 layers
@@ -442,7 +446,7 @@ def run_decode(args, ws, rank, dev):
             "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "fp16 (fp32 state)", "data": "synthetic",
             "config": {"workload": "RNN-mode greedy decode (BASELINE configs[2])", "seqs_per_gpu": Bs,
-                       "prompt": P, "parallelism": f"dp{ws}"},
+                       "prompt": P, "parallelism": f"dp{ws}", "cuda_graph": True},
             "gpu_launches": launches, "clocks": clocks}
 
 

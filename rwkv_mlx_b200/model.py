@@ -386,7 +386,8 @@ class RWKV(nn.Module):
 
     def forward_rnn_batch(self, tokens: torch.Tensor, states: list):
         """One decode step for a batch of sequences: tokens (Bs,) -> logits (Bs, V).
-        ``states`` (per-layer dicts) is updated in place."""
+        ``states`` (per-layer dicts) is updated in place: every state tensor keeps its
+        storage, so a step can be captured in a CUDA graph (see :class:`DecodeGraph`)."""
         x = self.emb(tokens)
         v_first = torch.zeros_like(x)
         for i, blk in enumerate(self.blocks):
@@ -394,8 +395,8 @@ class RWKV(nn.Module):
                 x = blk.ln0(x)
             xx = blk.ln1(x)
             st = states[i]
-            out, st["att_x_prev"], st["att_state"], v_first = blk.att.forward_rnn(
-                xx, st["att_x_prev"], v_first, st["att_state"])
+            out, _, _, v_first = blk.att.forward_rnn(xx, st["att_x_prev"], v_first, st["att_state"])
+            st["att_x_prev"].copy_(xx)
             x = x + out
             xx = blk.ln2(x)
             if blk.is_moe:
@@ -404,11 +405,11 @@ class RWKV(nn.Module):
                 ffn = blk.ffn
                 base, _ = ffn.base.forward_rnn(xx, st["ffn_x_prev"])
                 delta = _moe_rnn(ffn, xx)
-                st["ffn_x_prev"] = xx
                 x = x + base + delta
             else:
-                out, st["ffn_x_prev"] = blk.ffn.forward_rnn(xx, st["ffn_x_prev"])
+                out, _ = blk.ffn.forward_rnn(xx, st["ffn_x_prev"])
                 x = x + out
+            st["ffn_x_prev"].copy_(xx)
         x = self.ln_out(x)
         return self.head(x)
 
@@ -427,6 +428,42 @@ class RWKV(nn.Module):
             new += [st["att_x_prev"].view(-1), st["att_state"].view(cfg.n_head, cfg.head_size, cfg.head_size),
                     st["ffn_x_prev"].view(-1)]
         return logits.view(-1), new
+
+
+class DecodeGraph:
+    """Greedy batched decode step captured once in a CUDA graph and replayed.
+
+    ``states`` (from :meth:`RWKV.init_state` / :meth:`RWKV.forward_with_state`) and the
+    token buffer keep their storage across steps; :meth:`step` replays the graph:
+    logits = forward_rnn_batch(tokens, states); tokens = argmax(logits)."""
+
+    def __init__(self, model: "RWKV", states: list, tokens: torch.Tensor, warmup: int = 2):
+        self.model, self.states = model, states
+        self.tokens = tokens.clone()
+        # states must own contiguous storage the graph can update in place
+        for st in states:
+            for k_ in st:
+                st[k_] = st[k_].contiguous().clone()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side), torch.no_grad():
+            saved = [{k_: v.clone() for k_, v in st.items()} for st in states]
+            tok0 = self.tokens.clone()
+            for _ in range(warmup):
+                self.model.forward_rnn_batch(self.tokens, states)
+            for st, sv in zip(states, saved):  # warm-up must not advance the sequences
+                for k_ in st:
+                    st[k_].copy_(sv[k_])
+            self.tokens.copy_(tok0)
+        torch.cuda.current_stream().wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph), torch.no_grad():
+            self.logits = self.model.forward_rnn_batch(self.tokens, states)
+            self.tokens.copy_(self.logits.argmax(-1))
+
+    def step(self):
+        self.graph.replay()
+        return self.tokens
 
 
 def _moe_rnn(ffn, x):

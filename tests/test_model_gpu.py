@@ -131,3 +131,23 @@ def test_fused_per_head_groupnorm_and_state_output():
     for x, y in zip(sa, sb):
         for key in x:
             assert rel_rms(x[key].float().cpu().numpy(), y[key].float().cpu().numpy()) < 1e-4, key
+
+
+def test_decode_graph_matches_eager_decode():
+    from rwkv_mlx_b200.model import DecodeGraph
+
+    cfg, m = _tiny()
+    idx = torch.randint(0, cfg.vocab_size, (4, 20), device="cuda")
+    with torch.no_grad():
+        _, _, st_a = m.forward_with_state(idx)
+        _, _, st_b = m.forward_with_state(idx)
+        tok = idx[:, -1].clone()
+        eager = []
+        t = tok.clone()
+        for _ in range(5):
+            t = m.forward_rnn_batch(t, st_a).argmax(-1)
+            eager.append(t.clone())
+    g = DecodeGraph(m, st_b, tok)
+    graphed = [g.step().clone() for _ in range(5)]
+    for a, b in zip(eager, graphed):
+        assert torch.equal(a, b)

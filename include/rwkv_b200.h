@@ -52,9 +52,11 @@ int rwkv_abi_version(void);
 /* Error word set by a kernel that gave up a bounded wait (0 = none).  Reads the
  * device word synchronously; `clear` resets it.  Negative on a CUDA error. */
 int rwkv_device_error(int clear);
-/* Select the WKV-7 kernels: 0 automatic (chunked tensor-core kernels when all
- * per-token inputs are 16-byte aligned), 1 step-sequential kernels, 2 chunked.
- * Process-wide; meant for testing one implementation against the other. */
+/* Select the WKV-7 forward kernel: 0 automatic (with all per-token inputs 16-byte
+ * aligned: the tcgen05 kernel for fp16/bf16 activations, the mma.sync kernel for
+ * fp32; otherwise the step-sequential kernel), 1 step-sequential, 2 chunked on
+ * mma.sync, 3 chunked on tcgen05 (fp16/bf16 only).  Process-wide; meant for testing
+ * one implementation against another. */
 int rwkv_set_wkv_impl(int impl);
 
 /* ------------------------------------------------------------------------ */

@@ -22,8 +22,11 @@ struct WkvBwdArgs {
 
 int wkv7_fwd_seq(const WkvFwdArgs& p, cudaStream_t st);
 int wkv7_fwd_chunk(const WkvFwdArgs& p, cudaStream_t st);
+int wkv7_fwd_tc(const WkvFwdArgs& p, cudaStream_t st);
+bool wkv7_tc_supported(int dtype);
+int read_device_error_tc(int clear);
 int read_device_error(int clear);
-extern int g_wkv_impl;  // 0 auto, 1 step-sequential kernels, 2 chunked kernels
+extern int g_wkv_impl;  // 0 auto, 1 step-sequential, 2 chunked (mma.sync), 3 chunked (tcgen05)
 int wkv7_bwd_seq(const WkvBwdArgs& p, cudaStream_t st);
 int wkv7_step_launch(float* S, const void* r, const void* w, const void* k, const void* v,
                      const void* a, const void* b, void* y, int Bs, int H, int dtype, int w_dtype,

@@ -15,7 +15,7 @@ static bool inputs_aligned16(const void* const* ps, int n) {
 }
 
 extern "C" int rwkv_set_wkv_impl(int impl) {
-    if (impl < 0 || impl > 2) return RWKV_ERR_ARG;
+    if (impl < 0 || impl > 3) return RWKV_ERR_ARG;
     g_wkv_impl = impl;
     return RWKV_OK;
 }
@@ -39,6 +39,11 @@ extern "C" int rwkv_wkv7_forward(const void* r, const void* w, const void* k, co
     WkvFwdArgs p{r, w, k, v, a, b, s0, y, sT, ckpt, sa, B, T, H, dtype, w_dtype, ckpt ? ckpt_len : 16};
     const void* ins[6] = {r, w, k, v, a, b};
     if (g_wkv_impl == 1 || !inputs_aligned16(ins, 6)) return wkv7_fwd_seq(p, (cudaStream_t)stream);
+    if (g_wkv_impl == 2) return wkv7_fwd_chunk(p, (cudaStream_t)stream);
+    if (g_wkv_impl == 3 || wkv7_tc_supported(dtype)) {
+        if (!wkv7_tc_supported(dtype)) return RWKV_ERR_DTYPE;
+        return wkv7_fwd_tc(p, (cudaStream_t)stream);
+    }
     return wkv7_fwd_chunk(p, (cudaStream_t)stream);
 }
 

@@ -38,12 +38,15 @@ def _rounded(inp, dt, w_dt=None):
     return dev, host
 
 
-@pytest.mark.parametrize("impl", [1, 2])
+@pytest.mark.parametrize("impl", [1, 2, 3])
 @pytest.mark.parametrize("dt", [torch.float32, torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("B,T,H", [(1, 256, 4), (2, 100, 3), (1, 17, 1)])
 def test_forward_matches_oracle(dt, B, T, H, impl):
+    """impl 1: step-sequential, 2: chunked on mma.sync, 3: chunked on tcgen05 (fp16/bf16)."""
     from rwkv_mlx_b200 import wkv7
 
+    if impl == 3 and dt == torch.float32:
+        pytest.skip("the tcgen05 kernel takes fp16/bf16 activations")
     d, h = _rounded(wkv_inputs(B, T, H, seed=B * 1000 + T), dt)
     _set_impl(impl)
     try:
@@ -184,7 +187,7 @@ def _set_impl(i):
     assert _native.lib().rwkv_set_wkv_impl(i) == 0
 
 
-@pytest.mark.parametrize("B,T,H", [(2, 64, 3), (1, 333, 2), (3, 16, 1)])
+@pytest.mark.parametrize("B,T,H", [(2, 64, 3), (1, 333, 2), (3, 16, 1), (1, 1, 1)])
 def test_chunked_and_sequential_kernels_agree(B, T, H):
     from rwkv_mlx_b200 import _native, wkv7
 
@@ -235,3 +238,28 @@ def test_misaligned_inputs_use_the_sequential_kernel():
     y = wkv7.wkv7(*[shifted[n] for n in "rwkvab"])
     ye = wo.wkv7_forward_exact(h["r"], h["w"], h["k"], h["v"], h["a"], h["b"])[0]
     assert rel_rms(y.cpu().numpy(), _bt(ye)) < 2e-5
+
+
+@pytest.mark.parametrize("T", [16, 48, 333, 1024])
+def test_tcgen05_kernel_with_state_and_checkpoints(T):
+    """tcgen05 forward with an initial state, final state, sa and 16-step snapshots (fp16)."""
+    from rwkv_mlx_b200 import _native, wkv7
+
+    B, H = 2, 3
+    d, h = _rounded(wkv_inputs(B, T, H, seed=T), torch.float16, w_dt=torch.float32)
+    rng = np.random.default_rng(T)
+    s0 = rng.standard_normal((B, H, 64, 64)) * 0.5
+    _set_impl(3)
+    try:
+        y, ck, sa, sT = wkv7._fwd(d["r"], d["w"], d["k"], d["v"], d["a"], d["b"], s0=_dev(s0, torch.float32),
+                                  want_ckpt=True, want_sa=True, want_state=True)
+        torch.cuda.synchronize()
+    finally:
+        _set_impl(0)
+    assert _native.lib().rwkv_device_error(1) == 0
+    ye, sae, sTe, st = wo.wkv7_forward_exact(h["r"], h["w"], h["k"], h["v"], h["a"], h["b"], s0=s0, keep_states=True)
+    assert rel_rms(y.double().cpu().numpy(), _bt(ye)) < 2e-3
+    assert rel_rms(sa.cpu().numpy(), sae) < 2e-3
+    assert rel_rms(sT.cpu().numpy(), sTe) < 2e-3
+    if T >= 16:
+        assert rel_rms(ck.cpu().numpy(), wo.checkpoints_from_states(st, 16).reshape(-1)) < 2e-3

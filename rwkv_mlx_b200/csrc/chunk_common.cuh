@@ -8,10 +8,11 @@ namespace ck {
 constexpr int N = 64, L = 16, LD4 = 68, LD8 = 72, LDM = 20;
 constexpr long long WAIT_CYCLES = 4000000000LL;  // ~2 s: far above any legitimate wait
 
+// Round to the 10-bit TF32 mantissa, ties away from zero, in two integer ops (an add
+// carries into the exponent exactly as rounding up should).  Finite inputs only: the
+// operands here are products of bounded activations and decay factors.
 __device__ __forceinline__ uint32_t tf32(float x) {
-    uint32_t r;
-    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-    return r;
+    return (__float_as_uint(x) + 0x1000u) & 0xFFFFE000u;
 }
 __device__ __forceinline__ float tf32f(float x) { return __uint_as_float(tf32(x)); }
 __device__ __forceinline__ uint32_t fbits(float x) { return __float_as_uint(x); }

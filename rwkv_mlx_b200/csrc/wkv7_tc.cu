@@ -1,17 +1,19 @@
 // WKV-7 forward with the state products on the 5th-generation tensor cores:
-// tcgen05.mma (kind::tf32, M=64) with operands in shared memory (K-major, no swizzle)
-// and accumulators in tensor memory.  Same chunk algebra as wkv7_chunk.cu (L = 16):
+// tcgen05.mma (kind::tf32, M=64) with accumulators in tensor memory.  Same chunk
+// algebra as wkv7_chunk.cu (L = 16):
 //
-//   D1 = [U | Y]^T = S0 [Wu; Wy]^T + I [Ui; Yi]^T        (M=64 values, N=32, K=64+64)
+//   D1 = [U | Y]^T = S0 [Wu; Wy]^T + [Ui; Yi]^T          (M=64 values, N=32, K=64)
 //   D2 = S_L       = S0 diag(GL) + V^T Kb + U^T Bb        (M=64 values, N=64 keys, K=16+16)
 //
-// The fp32 state lives in tensor memory (D2) for the whole sequence.  Per chunk the
-// 4 state warps scale it by the chunk decay (tcgen05.ld/st), one thread issues the
-// MMAs, and the warps read U and Y back from D1.  Two groups of 4 "prep" warps compute
-// the inputs-only chunk operands (decay factors, intra-chunk products on mma.sync,
-// triangular solve) for alternating chunks, writing them straight into the UMMA
-// operand layout; the hand-offs are mbarriers with bounded waits (a CTA that gives up
-// sets the device error word and exits, it never traps).
+// The fp32 state lives in tensor memory (D2) for the whole sequence and is itself the
+// A operand of D1 (A read from tensor memory, B = [Wu; Wy] K-major in shared memory).
+// Per chunk the 4 state warps preload the intra-chunk part [Ui; Yi]^T into D1, one
+// thread issues the 8 K-steps of D1 as two independent accumulation chains, the warps
+// scale D2 by the chunk decay and read U and Y back, then D2 takes the rank-32 update.
+// Two groups of 4 "prep" warps compute the inputs-only chunk operands (decay factors,
+// intra-chunk products on mma.sync, triangular solve) for alternating chunks, writing
+// them straight into the UMMA operand layout; the hand-offs are mbarriers with bounded
+// waits (a CTA that gives up sets the device error word and exits, it never traps).
 //
 // Supported for fp16 / bf16 activations (w in the activation dtype or fp32); fp32
 // activations use the mma.sync kernel (their input staging does not fit next to this
@@ -40,11 +42,10 @@ constexpr int SBO_K64 = 16 * KLBO, SBO_K32 = 8 * KLBO, SBO_K16 = 4 * KLBO;
 constexpr int SZ_WB = 4 * SBO_K64;  // 32 rows x K=64
 constexpr int SZ_BK = 8 * SBO_K32;  // 64 rows x K=32
 constexpr int SZ_VT = 8 * SBO_K16;  // 64 rows x K=16
-constexpr int SZ_S = 8 * SBO_K64;   // 64 rows x K=64
 
 struct __align__(128) Stage {
     unsigned char WB[SZ_WB];  // B of D1: rows t' (0-15 Wu, 16-31 Wy), K = key
-    unsigned char UY[SZ_WB];  // B of D1 identity part: rows t' (0-15 Ui, 16-31 Yi), K = value
+    unsigned char UY[SZ_WB];  // intra-chunk part of D1: rows t' (0-15 Ui, 16-31 Yi), K = value
     unsigned char BK[SZ_BK];  // B of D2: rows key, K = t' (0-15 Bb, 16-31 Kb)
     unsigned char VT[SZ_VT];  // A of D2 (V part): rows value, K = t
     float GL[N];              // decay of the whole chunk per key
@@ -58,8 +59,6 @@ struct __align__(16) PrepScratch {
 };
 struct __align__(128) Smem {
     Stage st[2];
-    unsigned char S0A[SZ_S];  // A of D1: state rows value, K = key
-    unsigned char IDA[SZ_S];  // A of D1 identity part
     unsigned char UTA[SZ_VT]; // A of D2 (U part): rows value, K = t
     float Yb[L][LD8];
     PrepScratch ps[2];
@@ -83,6 +82,14 @@ __device__ __forceinline__ void umma(uint32_t d, uint64_t a, uint64_t b, uint32_
         "{ .reg .pred p; setp.ne.b32 p, %4, 0; "
         "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %6, %7, %8}, p; }" ::"r"(d),
         "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(0), "r"(0), "r"(0), "r"(0)
+        : "memory");
+}
+// same, A (M x K, fp32 columns) read from tensor memory
+__device__ __forceinline__ void umma_ts(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{ .reg .pred p; setp.ne.b32 p, %4, 0; "
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p; }" ::"r"(d),
+        "r"(a), "l"(b), "r"(idesc), "r"(acc), "r"(0), "r"(0), "r"(0), "r"(0)
         : "memory");
 }
 __device__ __forceinline__ void umma_commit(unsigned long long* bar) {
@@ -412,62 +419,66 @@ __global__ void __launch_bounds__(NT, 1)
         asm volatile("cp.async.wait_all;" ::: "memory");
     } else {
         // ===================== state warps =====================
+        // TMEM columns: [0,64) D2 = state, [64,96) D1a, [96,128) D1b (D1 = D1a + D1b).
         const int tw = warp, lane = tid & 31;
         const bool live = lane < 16;              // M=64 accumulators use lanes 0-15 of each subpartition
         const int row = 16 * tw + lane;            // state row (value index) held by this thread
+        const int rowc = 16 * tw + (lane & 15);    // in-range row for the idle lanes' loads
         const uint32_t lane_base = (uint32_t)(32 * tw) << 16;
-        const uint32_t tD2 = tmem + lane_base, tD1 = tmem + lane_base + 64;
-        float S[N];
+        const uint32_t tD2 = tmem + lane_base, tD1a = tD2 + 64, tD1b = tD2 + 96;
         {
+            float S[N];
             const float* p = (s0 && live) ? s0 + ((size_t)bh * N + row) * N : nullptr;
 #pragma unroll
             for (int j = 0; j < N; j++) S[j] = p ? p[j] : 0.f;
-            for (int e = tid; e < N * N; e += 128) {
-                const int rr = e / N, kk = e % N;
-                *reinterpret_cast<float*>(sm.IDA + kmaj(rr, kk, SBO_K64)) = rr == kk ? 1.f : 0.f;
-            }
-            if (live) {
 #pragma unroll
-                for (int j = 0; j < N; j += 4) st4(sm.S0A + kmaj(row, j, SBO_K64), S[j], S[j + 1], S[j + 2], S[j + 3]);
-            }
-            proxy_fence();
+            for (int j = 0; j < N; j += 16) tmem_st16(tD2 + j, &S[j]);
+            tmem_wait_st();
         }
-        group_sync(BAR_STATE);
         for (int c = 0; c < nchunks; c++) {
             const int s = c & 1;
             Stage& stg = sm.st[s];
             const bool bad = !mbar_wait(&sm.full[s], (c >> 1) & 1, &sm.abort, &g_device_error_tc);
             if (group_sync_or(BAR_STATE, bad)) break;
-            // state * chunk decay -> D2
+            {  // D1a <- [Ui; Yi]^T (row `row`, columns t')
+                float pre[2 * L];
 #pragma unroll
-            for (int j = 0; j < N; j++) S[j] *= stg.GL[j];
-#pragma unroll
-            for (int j = 0; j < N; j += 16) tmem_st16(tD2 + j, &S[j]);
-            tmem_wait_st();
+                for (int tt = 0; tt < 2 * L; tt++) pre[tt] = *reinterpret_cast<const float*>(stg.UY + kmaj(tt, rowc, SBO_K64));
+                tmem_st16(tD1a, pre);
+                tmem_st16(tD1a + 16, pre + 16);
+                tmem_wait_st();
+            }
             tc_fence_before();
             group_sync(BAR_STATE);
             tc_fence_after();
             if (tid == 0) {
-                const uint32_t i1 = idesc_tf32(64, 32), i2 = idesc_tf32(64, 64);
-                const uint32_t aS = smem_u32(sm.S0A), aI = smem_u32(sm.IDA), bW = smem_u32(stg.WB),
-                               bU = smem_u32(stg.UY), aV = smem_u32(stg.VT), bK = smem_u32(stg.BK);
+                const uint32_t i1 = idesc_tf32(64, 32), bW = smem_u32(stg.WB);
 #pragma unroll
                 for (int ks = 0; ks < 8; ks++)
-                    umma(tmem + 64, umma_desc(aS + 2 * ks * KLBO, SBO_K64), umma_desc(bW + 2 * ks * KLBO, SBO_K64), i1, ks);
-#pragma unroll
-                for (int ks = 0; ks < 8; ks++)
-                    umma(tmem + 64, umma_desc(aI + 2 * ks * KLBO, SBO_K64), umma_desc(bU + 2 * ks * KLBO, SBO_K64), i1, 1);
-#pragma unroll
-                for (int ks = 0; ks < 2; ks++)
-                    umma(tmem, umma_desc(aV + 2 * ks * KLBO, SBO_K16), umma_desc(bK + (4 + 2 * ks) * KLBO, SBO_K32), i2, 1);
+                    umma_ts((ks & 1) ? tmem + 96 : tmem + 64, tmem + 8 * ks, umma_desc(bW + 2 * ks * KLBO, SBO_K64), i1,
+                            (ks & 1) ? (ks > 1) : 1);
                 umma_commit(&sm.mma1);
             }
-            bool bad2 = !mbar_wait(&sm.mma1, c & 1, &sm.abort, &g_device_error_tc);
+            const bool bad2 = !mbar_wait(&sm.mma1, c & 1, &sm.abort, &g_device_error_tc);
             tc_fence_after();
-            float u[L], yv[L];
-            tmem_ld16(tD1, u);
-            tmem_ld16(tD1 + 16, yv);
+            float S[N], u[L], yv[L], u2[L], y2[L];
+#pragma unroll
+            for (int j = 0; j < N; j += 16) tmem_ld16(tD2 + j, &S[j]);
+            tmem_ld16(tD1a, u);
+            tmem_ld16(tD1a + 16, yv);
+            tmem_ld16(tD1b, u2);
+            tmem_ld16(tD1b + 16, y2);
             tmem_wait_ld();
+            // state * chunk decay -> D2
+#pragma unroll
+            for (int j = 0; j < N; j += 4) {
+                const float4 gl = *reinterpret_cast<const float4*>(&stg.GL[j]);
+                S[j] *= gl.x, S[j + 1] *= gl.y, S[j + 2] *= gl.z, S[j + 3] *= gl.w;
+            }
+#pragma unroll
+            for (int j = 0; j < N; j += 16) tmem_st16(tD2 + j, &S[j]);
+#pragma unroll
+            for (int tt = 0; tt < L; tt++) u[tt] += u2[tt], yv[tt] += y2[tt];
             if (live) {
 #pragma unroll
                 for (int tt = 0; tt < L; tt += 4) st4(sm.UTA + kmaj(row, tt, SBO_K16), u[tt], u[tt + 1], u[tt + 2], u[tt + 3]);
@@ -479,51 +490,64 @@ __global__ void __launch_bounds__(NT, 1)
                         if (c * L + tt < T_) sa_out[base + (size_t)(c * L + tt) * tstride + row] = u[tt];
                 }
             }
+            tmem_wait_st();
             proxy_fence();
             tc_fence_before();
             if (group_sync_or(BAR_STATE, bad2)) break;
             tc_fence_after();
             if (tid == 0) {
                 const uint32_t i2 = idesc_tf32(64, 64);
-                const uint32_t aU = smem_u32(sm.UTA), bK = smem_u32(stg.BK);
+                const uint32_t aU = smem_u32(sm.UTA), aV = smem_u32(stg.VT), bK = smem_u32(stg.BK);
+#pragma unroll
+                for (int ks = 0; ks < 2; ks++)
+                    umma(tmem, umma_desc(aV + 2 * ks * KLBO, SBO_K16), umma_desc(bK + (4 + 2 * ks) * KLBO, SBO_K32), i2, 1);
 #pragma unroll
                 for (int ks = 0; ks < 2; ks++)
                     umma(tmem, umma_desc(aU + 2 * ks * KLBO, SBO_K16), umma_desc(bK + 2 * ks * KLBO, SBO_K32), i2, 1);
                 umma_commit(&sm.mma2);
             }
-            {  // y rows of this chunk, coalesced
+            {  // y rows of this chunk: 8 consecutive values per thread, one 16-byte store
                 const int rr = tid >> 3, c8 = (tid & 7) * 8, t = c * L + rr;
                 if (t < T_) {
-                    const size_t off = base + (size_t)t * tstride + c8;
-#pragma unroll
-                    for (int q = 0; q < 8; q++) y[off + q] = from_f32<T>(sm.Yb[rr][c8 + q]);
+                    const float4 f0 = *reinterpret_cast<const float4*>(&sm.Yb[rr][c8]);
+                    const float4 f1 = *reinterpret_cast<const float4*>(&sm.Yb[rr][c8 + 4]);
+                    uint4 pk;
+                    T* pe = reinterpret_cast<T*>(&pk);
+                    pe[0] = from_f32<T>(f0.x), pe[1] = from_f32<T>(f0.y), pe[2] = from_f32<T>(f0.z), pe[3] = from_f32<T>(f0.w);
+                    pe[4] = from_f32<T>(f1.x), pe[5] = from_f32<T>(f1.y), pe[6] = from_f32<T>(f1.z), pe[7] = from_f32<T>(f1.w);
+                    *reinterpret_cast<uint4*>(y + base + (size_t)t * tstride + c8) = pk;
                 }
             }
             const bool bad3 = !mbar_wait(&sm.mma2, c & 1, &sm.abort, &g_device_error_tc);
             tc_fence_after();
+            if (ckpt) {
+                const int tend = (c + 1) * L;
+                if (tend <= T_ && tend % ckpt_len == 0) {
 #pragma unroll
-            for (int j = 0; j < N; j += 16) tmem_ld16(tD2 + j, &S[j]);
-            tmem_wait_ld();
-            if (live) {
-#pragma unroll
-                for (int j = 0; j < N; j += 4) st4(sm.S0A + kmaj(row, j, SBO_K64), S[j], S[j + 1], S[j + 2], S[j + 3]);
-                if (ckpt) {
-                    const int tend = (c + 1) * L;
-                    if (tend <= T_ && tend % ckpt_len == 0) {
+                    for (int j = 0; j < N; j += 16) tmem_ld16(tD2 + j, &S[j]);
+                    tmem_wait_ld();
+                    if (live) {
                         float* p = ckpt + (((size_t)bh * nck + tend / ckpt_len - 1) * N + row) * N;
 #pragma unroll
                         for (int j = 0; j < N; j += 4) *reinterpret_cast<float4*>(p + j) = make_float4(S[j], S[j + 1], S[j + 2], S[j + 3]);
                     }
                 }
             }
-            proxy_fence();
+            tc_fence_before();
             mbar_arrive(&sm.empty[s]);
             if (group_sync_or(BAR_STATE, bad3)) break;  // uniform decision for the whole group
         }
-        if (sT && live && !sm.abort) {
-            float* p = sT + ((size_t)bh * N + row) * N;
+        if (sT && !group_sync_or(BAR_STATE, sm.abort != 0)) {
+            tc_fence_after();
+            float S[N];
 #pragma unroll
-            for (int j = 0; j < N; j += 4) *reinterpret_cast<float4*>(p + j) = make_float4(S[j], S[j + 1], S[j + 2], S[j + 3]);
+            for (int j = 0; j < N; j += 16) tmem_ld16(tD2 + j, &S[j]);
+            tmem_wait_ld();
+            if (live) {
+                float* p = sT + ((size_t)bh * N + row) * N;
+#pragma unroll
+                for (int j = 0; j < N; j += 4) *reinterpret_cast<float4*>(p + j) = make_float4(S[j], S[j + 1], S[j + 2], S[j + 3]);
+            }
         }
     }
     tc_fence_before();

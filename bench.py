@@ -373,18 +373,17 @@ def run_moe(args, ws, rank, dev):
     clocks = clk.stop()
     launches = _native.launch_count - l0
     ms = max_over_ranks(ms, ws)
-    # MoE-path kernels alone (router, permute, down, combine) on the same tokens
-    from rwkv_mlx_b200.moe import lora_combine, lora_down, permute, router_forward
+    # MoE-path kernels alone (router + fused adapter apply, the module's path) on the same tokens
+    from rwkv_mlx_b200.moe import lora_apply, router_forward
 
     x2 = x.view(ntok, C)
     with torch.no_grad():
         base_out = base(x).view(ntok, C)
+    Ah, Bh = A.half(), Bw.half()
 
     def moe_only():
         r = router_forward(x2, layer.router.gate.weight, 2, layer.router.bias)
-        perm, inv, off = permute(r["inds"], 8)
-        h = lora_down(x2, A.half(), perm, off, 2)
-        return lora_combine(base_out, h, Bw.half(), r["inds"], r["scores"], inv)
+        return lora_apply(x2, base_out, Ah, Bh, r["inds"], r["scores"])
 
     for _ in range(args.warmup):
         moe_only()
@@ -400,7 +399,7 @@ def run_moe(args, ws, rank, dev):
                        "parallelism": f"ep{ws} (NCCL all-to-all)" if ep else f"dp{ws} (experts replicated)",
                        "l2": "x and outputs (3 x 100 MB) larger than L2"},
             "gpu_launches": launches,
-            "roofline": {"kernel": "MoE path (router+permute+lora_down+combine)", "bound": "hbm", "achieved": gbs,
+            "roofline": {"kernel": "MoE path (router + fused lora_apply)", "bound": "hbm", "achieved": gbs,
                          "peak": hbm, "unit": "GB/s", "frac": gbs / hbm, "traffic": None, "launch_ms": moe_ms,
                          "algorithmic_bytes": algo, "peak_source": src},
             "clocks": clocks}

@@ -172,6 +172,20 @@ int rwkv_moe_lora_combine(const void* base, const float* h, const void* B,
                           void* out, int ntok, int C, int R, int E, int topk, int dtype,
                           void* stream);
 
+/* Fused adapter apply (replaces the two products of moe.py:142 and the weighted
+ * sum of moe.py:143-147 in one pass over the tokens):
+ *   out[t] = base[t] + sum_s scores[t,s] * ((x[t] @ A[e]) @ B[e]),  e = inds[t,s]
+ * Dense over the E*R adapter columns on the tensor cores with the unselected
+ * experts masked to 0, which is the reference's own dense formulation.  fp16 / bf16
+ * only; needs C % 64 == 0, R % 8 == 0, E*R in {32, 64, 128}, topk <= min(E, 8)
+ * (rwkv_moe_lora_apply_supported says whether a shape qualifies).  base and scores
+ * may be NULL (zeros / all 1); base may equal out.  x (ntok, C), A (E, C, R),
+ * B (E, R, C), out (ntok, C) in dtype; inds (ntok, topk) int32.           */
+int rwkv_moe_lora_apply_supported(int C, int R, int E, int topk, int dtype);
+int rwkv_moe_lora_apply(const void* x, const void* base, const void* A, const void* B,
+                        const int32_t* inds, const void* scores, void* out, int ntok, int C,
+                        int R, int E, int topk, int dtype, void* stream);
+
 /* Expert-parallel dispatch / combine helpers (no counterpart in the reference,
  * which runs on one device; they move the routed rows of moe.py:139-145 between
  * GPUs and back).

@@ -48,6 +48,8 @@ SIGNATURES = {
     "rwkv_moe_permute": (_I, [_P] * 5 + [_SZ] + [_I] * 3 + [_P]),
     "rwkv_moe_lora_down": (_I, [_P] * 5 + [_I] * 6 + [_P]),
     "rwkv_moe_lora_combine": (_I, [_P] * 7 + [_I] * 6 + [_P]),
+    "rwkv_moe_lora_apply_supported": (_I, [_I] * 5),
+    "rwkv_moe_lora_apply": (_I, [_P] * 7 + [_I] * 6 + [_P]),
     "rwkv_moe_ortho_loss": (_I, [_P] * 2 + [_I] * 4 + [_P]),
     "rwkv_moe_gather_rows": (_I, [_P] * 3 + [_I] * 4 + [_P]),
     "rwkv_moe_lora_up": (_I, [_P] * 5 + [_I] * 5 + [_P]),
@@ -97,7 +99,7 @@ def lib() -> ctypes.CDLL:
 KERNELS_PER_CALL = {
     "rwkv_wkv7_forward": 1, "rwkv_wkv7_backward": 1, "rwkv_wkv7_step": 1,
     "rwkv_moe_router": 2, "rwkv_moe_router_noalloc": 2, "rwkv_moe_permute": 3, "rwkv_moe_lora_down": 1,
-    "rwkv_moe_lora_combine": 1, "rwkv_moe_ortho_loss": 1, "rwkv_moe_gather_rows": 1,
+    "rwkv_moe_lora_combine": 1, "rwkv_moe_lora_apply": 1, "rwkv_moe_ortho_loss": 1, "rwkv_moe_gather_rows": 1,
     "rwkv_moe_lora_up": 1, "rwkv_moe_combine_rows": 1, "rwkv_lerp": 1, "rwkv_tmix_mid": 1,
     "rwkv_tmix_post": 1, "rwkv_relu_sq": 1, "rwkv_add_layernorm": 1,
 }
@@ -124,6 +126,10 @@ def stream_ptr(device=None):
 
 
 def dtype_code(t: torch.Tensor) -> int:
-    if t.dtype not in DTYPE_CODE:
-        raise RwkvNativeError(f"unsupported dtype {t.dtype}")
-    return DTYPE_CODE[t.dtype]
+    return dtype_code_of(t.dtype)
+
+
+def dtype_code_of(dt: torch.dtype) -> int:
+    if dt not in DTYPE_CODE:
+        raise RwkvNativeError(f"unsupported dtype {dt}")
+    return DTYPE_CODE[dt]

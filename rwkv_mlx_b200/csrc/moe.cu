@@ -10,6 +10,7 @@
 //   moe_combine    : out[t] = base[t] + sum_slot score * (h @ B[e]).
 //   moe_ortho      : sum_{i<j} ||A_i^T A_j||_F^2 (moe.py:149-163).
 #include <cfloat>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -28,6 +29,11 @@ __host__ __device__ inline int router_ctas(int ntok) {
 // ---------------------------------------------------------------------------
 // Router
 // ---------------------------------------------------------------------------
+// One warp routes 32 / EM tokens per pass (EM = expert count rounded up to 8, 16 or
+// 32): every gate weight read from shared memory serves all of them.  The 32 partial
+// logits per lane (token t, expert e at index t * EM + e) are summed over the warp
+// by a transpose-reduce (31 shuffles), which leaves lane (t, e) with logit e of
+// token t; softmax statistics and top-k then run inside groups of EM lanes.
 template <typename T, int EM>
 __global__ void __launch_bounds__(ROUTER_WARPS * 32)
     moe_router_kernel(const T* __restrict__ x, const float* __restrict__ gate_w,
@@ -35,6 +41,7 @@ __global__ void __launch_bounds__(ROUTER_WARPS * 32)
                       int32_t* __restrict__ inds, T* __restrict__ scores,
                       float* __restrict__ part_f, int32_t* __restrict__ part_c, int ntok, int C,
                       int E, int topk) {
+    constexpr int TPW = 32 / EM;
     extern __shared__ float wsm[];  // [E][C] gate weights
     __shared__ float red_f[ROUTER_WARPS][EM + 1];
     __shared__ int red_c[ROUTER_WARPS][EM];
@@ -42,137 +49,204 @@ __global__ void __launch_bounds__(ROUTER_WARPS * 32)
     for (int i = tid; i < E * C; i += blockDim.x) wsm[i] = gate_w[i];
     __syncthreads();
 
-    float acc_p = 0.f, acc_z = 0.f;  // lane e: sum of p_e; lane 0: sum of lse^2
-    int acc_c = 0;                   // lane e: count of expert e
-    const float lbias = (bias && lane < E) ? bias[lane] : 0.f;
+    const int grp = lane / EM, el = lane % EM;  // token slot of the pass, expert of this lane
+    const bool evalid = el < E;
+    float acc_p = 0.f, acc_z = 0.f;  // lane (t, e): sum of p_e; lanes e == 0: sum of lse^2
+    int acc_c = 0;                   // lane (t, e): count of expert e
+    const float lbias = (bias && evalid) ? bias[el] : 0.f;
     const int nvec = C / 8;
-    for (int tok = blockIdx.x * ROUTER_WARPS + warp; tok < ntok; tok += gridDim.x * ROUTER_WARPS) {
-        float acc[EM];
+    const int stride = gridDim.x * ROUTER_WARPS * TPW;
+    for (int tb = (blockIdx.x * ROUTER_WARPS + warp) * TPW; tb < ntok; tb += stride) {
+        float v[32];
 #pragma unroll
-        for (int e = 0; e < EM; e++) acc[e] = 0.f;
-        const T* xr = x + (size_t)tok * C;
+        for (int i = 0; i < 32; i++) v[i] = 0.f;
         for (int vi = lane; vi < nvec; vi += 32) {
-            float xf[8];
-            if constexpr (sizeof(T) == 2) {
-                uint4 raw = *reinterpret_cast<const uint4*>(xr + vi * 8);
-                const T* h = reinterpret_cast<const T*>(&raw);
+            float xf[TPW][8];
 #pragma unroll
-                for (int q = 0; q < 8; q++) xf[q] = to_f32(h[q]);
-            } else {
-                float4 r0 = *reinterpret_cast<const float4*>(xr + vi * 8);
-                float4 r1 = *reinterpret_cast<const float4*>(xr + vi * 8 + 4);
-                xf[0] = r0.x, xf[1] = r0.y, xf[2] = r0.z, xf[3] = r0.w;
-                xf[4] = r1.x, xf[5] = r1.y, xf[6] = r1.z, xf[7] = r1.w;
+            for (int t = 0; t < TPW; t++) {
+                const int tok = tb + t;
+                if (tok < ntok) {
+                    const T* xr = x + (size_t)tok * C + vi * 8;
+                    if constexpr (sizeof(T) == 2) {
+                        const uint4 raw = *reinterpret_cast<const uint4*>(xr);
+                        const T* h = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+                        for (int q = 0; q < 8; q++) xf[t][q] = to_f32(h[q]);
+                    } else {
+                        const float4 r0 = *reinterpret_cast<const float4*>(xr);
+                        const float4 r1 = *reinterpret_cast<const float4*>(xr + 4);
+                        xf[t][0] = r0.x, xf[t][1] = r0.y, xf[t][2] = r0.z, xf[t][3] = r0.w;
+                        xf[t][4] = r1.x, xf[t][5] = r1.y, xf[t][6] = r1.z, xf[t][7] = r1.w;
+                    }
+                } else {
+#pragma unroll
+                    for (int q = 0; q < 8; q++) xf[t][q] = 0.f;
+                }
             }
 #pragma unroll
             for (int e = 0; e < EM; e++) {
                 if (e < E) {
-                    const float* wr = wsm + e * C + vi * 8;
+                    const float4 w0 = *reinterpret_cast<const float4*>(wsm + e * C + vi * 8);
+                    const float4 w1 = *reinterpret_cast<const float4*>(wsm + e * C + vi * 8 + 4);
 #pragma unroll
-                    for (int q = 0; q < 8; q++) acc[e] = fmaf(xf[q], wr[q], acc[e]);
+                    for (int t = 0; t < TPW; t++) {
+                        float a_ = v[t * EM + e];
+                        a_ = fmaf(xf[t][0], w0.x, a_), a_ = fmaf(xf[t][1], w0.y, a_);
+                        a_ = fmaf(xf[t][2], w0.z, a_), a_ = fmaf(xf[t][3], w0.w, a_);
+                        a_ = fmaf(xf[t][4], w1.x, a_), a_ = fmaf(xf[t][5], w1.y, a_);
+                        a_ = fmaf(xf[t][6], w1.z, a_), a_ = fmaf(xf[t][7], w1.w, a_);
+                        v[t * EM + e] = a_;
+                    }
                 }
             }
         }
-        // butterfly: every lane ends with every logit
+        // transpose-reduce: after the step with offset o a lane keeps the half of its
+        // values whose index bit o matches its own lane bit
 #pragma unroll
-        for (int e = 0; e < EM; e++) {
-            if (e < E) {
+        for (int o = 16; o >= 1; o >>= 1) {
+            const bool up = lane & o;
 #pragma unroll
-                for (int o = 16; o > 0; o >>= 1) acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], o);
+            for (int i = 0; i < o; i++) {
+                const float send = up ? v[i] : v[i + o];
+                const float keep = up ? v[i + o] : v[i];
+                v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
             }
         }
-        float my = -FLT_MAX;
-#pragma unroll
-        for (int e = 0; e < EM; e++)
-            if (e == lane) my = acc[e];
-        const bool valid = lane < E;
-        float lg = valid ? my + lbias : -INFINITY;
-        if (logits && valid) logits[(size_t)tok * E + lane] = lg;
+        const int tok = tb + grp;
+        const bool tvalid = tok < ntok, valid = evalid && tvalid;
+        const float lg = evalid ? v[0] + lbias : -INFINITY;
+        if (logits && valid) logits[(size_t)tok * E + el] = lg;
 
-        // full softmax statistics (max-stabilised log-sum-exp)
+        // full softmax statistics (max-stabilised log-sum-exp) within the group
         float m = lg;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        float ex = valid ? expf(lg - m) : 0.f;
+        for (int o = EM / 2; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        const float ex = evalid ? expf(lg - m) : 0.f;
         float se = ex;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) se += __shfl_xor_sync(0xffffffffu, se, o);
+        for (int o = EM / 2; o > 0; o >>= 1) se += __shfl_xor_sync(0xffffffffu, se, o);
         if (valid) acc_p += ex / se;
         const float lse = m + logf(se);
-        if (lane == 0) acc_z = fmaf(lse, lse, acc_z);
+        if (el == 0 && tvalid) acc_z = fmaf(lse, lse, acc_z);
 
-        // warp top-k: repeated argmax, ties to the lower expert id
-        bool taken = !valid;
-        float sel0 = 0.f, denom = 0.f;
-        float my_sel_logit = 0.f;
+        // top-k by repeated argmax, ties to the lower expert id
+        bool taken = !evalid;
+        float sel0 = 0.f, denom = 0.f, my_sel_logit = 0.f;
         int my_slot = -1;
         for (int kk = 0; kk < topk; kk++) {
             float bv = taken ? -INFINITY : lg;
-            int bi = taken ? 0x7fffffff : lane;
+            int bi = taken ? 0x7fffffff : el;
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
+            for (int o = EM / 2; o > 0; o >>= 1) {
                 const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
                 const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
                 if (ov > bv || (ov == bv && oi < bi)) bv = ov, bi = oi;
             }
             if (kk == 0) sel0 = bv;
             denom += expf(bv - sel0);
-            if (lane == bi) {
+            if (el == bi) {
                 taken = true;
                 my_slot = kk;
                 my_sel_logit = bv;
             }
-            if (lane == 0) inds[(size_t)tok * topk + kk] = bi;
+            if (el == 0 && tvalid) inds[(size_t)tok * topk + kk] = bi;
         }
-        if (my_slot >= 0) {
+        if (my_slot >= 0 && tvalid) {
             scores[(size_t)tok * topk + my_slot] = from_f32<T>(expf(my_sel_logit - sel0) / denom);
             acc_c += 1;
         }
     }
+    // sum over the token slots of the warp (lanes with the same expert)
+#pragma unroll
+    for (int o = EM; o < 32; o <<= 1) {
+        acc_p += __shfl_xor_sync(0xffffffffu, acc_p, o);
+        acc_c += __shfl_xor_sync(0xffffffffu, acc_c, o);
+        acc_z += __shfl_xor_sync(0xffffffffu, acc_z, o);
+    }
     if (lane < EM) {
-        red_f[warp][lane] = (lane < E) ? acc_p : 0.f;
-        red_c[warp][lane] = (lane < E) ? acc_c : 0;
+        red_f[warp][lane] = evalid ? acc_p : 0.f;
+        red_c[warp][lane] = evalid ? acc_c : 0;
     }
     if (lane == 0) red_f[warp][EM] = acc_z;
     __syncthreads();
     if (tid < E) {
-        float s = 0.f;
+        float s_ = 0.f;
         int c = 0;
-        for (int w = 0; w < ROUTER_WARPS; w++) s += red_f[w][tid], c += red_c[w][tid];
-        part_f[(size_t)blockIdx.x * (E + 1) + tid] = s;
+        for (int w = 0; w < ROUTER_WARPS; w++) s_ += red_f[w][tid], c += red_c[w][tid];
+        part_f[(size_t)blockIdx.x * (E + 1) + tid] = s_;
         part_c[(size_t)blockIdx.x * E + tid] = c;
     }
     if (tid == 0) {
-        float s = 0.f;
-        for (int w = 0; w < ROUTER_WARPS; w++) s += red_f[w][EM];
-        part_f[(size_t)blockIdx.x * (E + 1) + E] = s;
+        float s_ = 0.f;
+        for (int w = 0; w < ROUTER_WARPS; w++) s_ += red_f[w][EM];
+        part_f[(size_t)blockIdx.x * (E + 1) + E] = s_;
     }
 }
 
-__global__ void moe_router_finalize_kernel(const float* __restrict__ part_f,
-                                           const int32_t* __restrict__ part_c, int nblk, int ntok,
-                                           int E, int topk, float* __restrict__ stats,
-                                           int32_t* __restrict__ counts) {
-    __shared__ float fp[64];
-    const int e = threadIdx.x;
-    if (e < E) {
-        float p = 0.f;
-        long long c = 0;
-        for (int b = 0; b < nblk; b++) p += part_f[(size_t)b * (E + 1) + e], c += part_c[(size_t)b * E + e];
-        const float pe = p / (float)ntok;
-        const float fe = (float)c / ((float)ntok * (float)topk);
-        stats[2 + e] = fe;
-        fp[e] = fe * pe;
-        if (counts) counts[e] = (int32_t)c;
+// Fixed-order (deterministic) reduction of the per-CTA partials: thread t sums CTAs
+// t, t + 256, ..., then warps and finally 8 warp totals, always in the same order.
+constexpr int FIN_THREADS = 256, FIN_MAXE = 32;
+__global__ void __launch_bounds__(FIN_THREADS)
+    moe_router_finalize_kernel(const float* __restrict__ part_f, const int32_t* __restrict__ part_c,
+                               int nblk, int ntok, int E, int topk, float* __restrict__ stats,
+                               int32_t* __restrict__ counts) {
+    __shared__ float wf[FIN_THREADS / 32][FIN_MAXE + 1];
+    __shared__ int wc[FIN_THREADS / 32][FIN_MAXE];
+    __shared__ float fp[FIN_MAXE];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    float p[FIN_MAXE + 1];
+    int c[FIN_MAXE];
+#pragma unroll
+    for (int q = 0; q <= FIN_MAXE; q++) p[q] = 0.f;
+#pragma unroll
+    for (int q = 0; q < FIN_MAXE; q++) c[q] = 0;
+    for (int b = tid; b < nblk; b += FIN_THREADS) {
+#pragma unroll
+        for (int q = 0; q <= FIN_MAXE; q++)
+            if (q <= E) p[q] += part_f[(size_t)b * (E + 1) + q];
+#pragma unroll
+        for (int q = 0; q < FIN_MAXE; q++)
+            if (q < E) c[q] += part_c[(size_t)b * E + q];
+    }
+#pragma unroll
+    for (int q = 0; q <= FIN_MAXE; q++) {
+        if (q <= E) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) p[q] += __shfl_xor_sync(0xffffffffu, p[q], o);
+            if (lane == 0) wf[warp][q] = p[q];
+        }
+    }
+#pragma unroll
+    for (int q = 0; q < FIN_MAXE; q++) {
+        if (q < E) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) c[q] += __shfl_xor_sync(0xffffffffu, c[q], o);
+            if (lane == 0) wc[warp][q] = c[q];
+        }
     }
     __syncthreads();
-    if (e == 0) {
+    if (tid <= E) {
+        float sp = 0.f;
+        long long sc = 0;
+        for (int w = 0; w < FIN_THREADS / 32; w++) {
+            sp += wf[w][tid];
+            if (tid < E) sc += wc[w][tid];
+        }
+        if (tid < E) {
+            const float pe = sp / (float)ntok;
+            const float fe = (float)sc / ((float)ntok * (float)topk);
+            stats[2 + tid] = fe;
+            fp[tid] = fe * pe;
+            if (counts) counts[tid] = (int32_t)sc;
+        } else {
+            stats[1] = sp / (float)ntok;
+        }
+    }
+    __syncthreads();
+    if (tid == 0) {
         float aux = 0.f;
         for (int i = 0; i < E; i++) aux += fp[i];
-        float z = 0.f;
-        for (int b = 0; b < nblk; b++) z += part_f[(size_t)b * (E + 1) + E];
         stats[0] = (float)E * aux;
-        stats[1] = z / (float)ntok;
     }
 }
 
@@ -426,6 +500,214 @@ __global__ void __launch_bounds__(256)
     }
 }
 
+// ---------------------------------------------------------------------------
+// Fused adapter apply (tensor cores):  out[t] = base[t] + sum_s scores[t,s] * (x[t] @ A[e]) @ B[e]
+// with e = inds[t,s].  Per tile of 64 tokens (4 warps x 16), dense over all E*R adapter
+// columns on mma.sync m16n8k16 (fp32 accumulate): H = X @ [A_0 | ... | A_E-1] in
+// K-slices of 64 channels, H masked and scaled by the routing scores (0 for experts a
+// token did not select, as in the reference's dense sum), then OUT = base + H @ [B_0; ...]
+// in N-slices of 64 channels.  H goes from the accumulators straight into the A
+// fragments of the second product (rounded to the activation dtype).  x and base are
+// read once and nothing per entry goes through global memory.  Weight slices are
+// staged with cp.async in their natural layouts and read with ldmatrix(.trans).
+// ---------------------------------------------------------------------------
+namespace apply {
+constexpr int TM = 64, KS = 64, NTH = 128;
+__device__ __forceinline__ uint32_t su32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+__device__ __forceinline__ void cp16(void* dst, const void* src, bool ok) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(su32(dst)), "l"(src), "r"(ok ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void ldm_x4(uint32_t (&r)[4], const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(su32(p)));
+}
+__device__ __forceinline__ void ldm_x4_t(uint32_t (&r)[4], const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(su32(p)));
+}
+template <typename T>
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    if constexpr (std::is_same<T, __half>::value)
+        asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                     : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                     : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    else
+        asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                     : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                     : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+    T h[2] = {from_f32<T>(lo), from_f32<T>(hi)};
+    return *reinterpret_cast<uint32_t*>(h);
+}
+template <int EN>
+struct Geo {
+    static constexpr int XP = KS * 2 + 16;  // X slice row pitch (bytes): TM rows x KS channels
+    static constexpr int AP = EN * 2 + 16;  // A slice row pitch: KS channels x EN columns
+    static constexpr int BP = KS * 2 + 16;  // B slice row pitch: EN rows x KS channels
+    static constexpr int OP = KS * 2 + 16;  // base / out slice row pitch: TM rows x KS channels
+    static constexpr int XS = TM * XP, AS = KS * AP, BS = EN * BP, OS = TM * OP;
+    static constexpr int STAGE = (XS + AS) > (BS + OS) ? (XS + AS) : (BS + OS);
+    static constexpr int SMEM = 2 * STAGE;
+};
+}  // namespace apply
+
+template <typename T, int EN>
+__global__ void __launch_bounds__(apply::NTH)
+    moe_lora_apply_kernel(const T* __restrict__ x, const T* __restrict__ base, const T* __restrict__ A,
+                          const T* __restrict__ B, const int32_t* __restrict__ inds,
+                          const T* __restrict__ scores, T* __restrict__ out, int ntok, int C, int R, int E,
+                          int topk) {
+    using namespace apply;
+    using G = Geo<EN>;
+    extern __shared__ __align__(16) unsigned char smem_apply[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, tg = lane & 3;
+    const int t0 = blockIdx.x * TM;
+    const int nsl = C / KS;
+    const int RP = R / 8;  // 16-byte pieces per adapter row
+
+    auto load_down = [&](int sl, int buf) {
+        unsigned char* xs = smem_apply + buf * G::STAGE;
+        unsigned char* as = xs + G::XS;
+        const int c0 = sl * KS;
+        for (int p = tid; p < TM * (KS / 8); p += NTH) {
+            const int row = p / (KS / 8), pc = p % (KS / 8), tok = t0 + row;
+            const bool ok = tok < ntok;
+            cp16(xs + row * G::XP + pc * 16, x + (size_t)(ok ? tok : 0) * C + c0 + pc * 8, ok);
+        }
+        for (int p = tid; p < E * KS * RP; p += NTH) {
+            const int e = p / (KS * RP), rem = p % (KS * RP), c = rem / RP, qp = rem % RP;
+            cp16(as + c * G::AP + (e * R + qp * 8) * 2, A + ((size_t)e * C + c0 + c) * R + qp * 8, true);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    auto load_up = [&](int sl, int buf) {
+        unsigned char* bs = smem_apply + buf * G::STAGE;
+        unsigned char* os = bs + G::BS;
+        const int c0 = sl * KS;
+        for (int p = tid; p < EN * (KS / 8); p += NTH) {
+            const int row = p / (KS / 8), pc = p % (KS / 8);
+            cp16(bs + row * G::BP + pc * 16, B + (size_t)row * C + c0 + pc * 8, true);
+        }
+        for (int p = tid; p < TM * (KS / 8); p += NTH) {  // base slice (zeros when there is no base)
+            const int row = p / (KS / 8), pc = p % (KS / 8), tok = t0 + row;
+            const bool ok = base && tok < ntok;
+            cp16(os + row * G::OP + pc * 16, ok ? base + (size_t)tok * C + c0 + pc * 8 : x, ok);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+
+    // ---- H = X @ Acat ----
+    float acc[EN / 8][4];
+#pragma unroll
+    for (int i = 0; i < EN / 8; i++) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+    load_down(0, 0);
+    for (int sl = 0; sl < nsl; sl++) {
+        if (sl + 1 < nsl) {
+            load_down(sl + 1, (sl + 1) & 1);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        __syncthreads();
+        const unsigned char* xs = smem_apply + (sl & 1) * G::STAGE;
+        const unsigned char* as = xs + G::XS;
+#pragma unroll
+        for (int kk = 0; kk < KS / 16; kk++) {
+            uint32_t af[4];
+            ldm_x4(af, xs + (16 * warp + (lane & 15)) * G::XP + (kk * 16 + (lane >> 4) * 8) * 2);
+#pragma unroll
+            for (int n2 = 0; n2 < EN / 16; n2++) {
+                uint32_t bq[4];
+                ldm_x4_t(bq, as + (kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * G::AP + (n2 * 16 + (lane >> 4) * 8) * 2);
+                mma16816<T>(acc[2 * n2], af, bq[0], bq[1]);
+                mma16816<T>(acc[2 * n2 + 1], af, bq[2], bq[3]);
+            }
+        }
+        __syncthreads();
+    }
+    load_up(0, 0);  // overlaps the routing mask below
+
+    // ---- routing mask / scores: column n belongs to expert n / R ----
+#pragma unroll
+    for (int hr = 0; hr < 2; hr++) {
+        const int tok = t0 + 16 * warp + g + 8 * hr;
+        int es[8];
+        float ss[8];
+        const int kq = tok < ntok ? topk : 0;
+        for (int s = 0; s < 8; s++) {
+            es[s] = s < kq ? inds[(size_t)tok * topk + s] : -1;
+            ss[s] = s < kq ? (scores ? to_f32(scores[(size_t)tok * topk + s]) : 1.f) : 0.f;
+        }
+#pragma unroll
+        for (int nt = 0; nt < EN / 8; nt++) {
+            const int e = (nt * 8) / R;
+            float gsc = 0.f;
+#pragma unroll
+            for (int s = 0; s < 8; s++) gsc += es[s] == e ? ss[s] : 0.f;
+            acc[nt][2 * hr] *= gsc;
+            acc[nt][2 * hr + 1] *= gsc;
+        }
+    }
+    uint32_t ha[EN / 16][4];
+#pragma unroll
+    for (int kk = 0; kk < EN / 16; kk++) {
+        ha[kk][0] = pack2<T>(acc[2 * kk][0], acc[2 * kk][1]);
+        ha[kk][1] = pack2<T>(acc[2 * kk][2], acc[2 * kk][3]);
+        ha[kk][2] = pack2<T>(acc[2 * kk + 1][0], acc[2 * kk + 1][1]);
+        ha[kk][3] = pack2<T>(acc[2 * kk + 1][2], acc[2 * kk + 1][3]);
+    }
+
+    // ---- OUT = base + Hg @ Bcat ----
+    for (int sl = 0; sl < nsl; sl++) {
+        if (sl + 1 < nsl) {
+            load_up(sl + 1, (sl + 1) & 1);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        __syncthreads();
+        const unsigned char* bs = smem_apply + (sl & 1) * G::STAGE;
+        float o[KS / 8][4];
+#pragma unroll
+        for (int i = 0; i < KS / 8; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < EN / 16; kk++) {
+#pragma unroll
+            for (int n2 = 0; n2 < KS / 16; n2++) {
+                uint32_t bq[4];
+                ldm_x4_t(bq, bs + (kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * G::BP + (n2 * 16 + (lane >> 4) * 8) * 2);
+                mma16816<T>(o[2 * n2], ha[kk], bq[0], bq[1]);
+                mma16816<T>(o[2 * n2 + 1], ha[kk], bq[2], bq[3]);
+            }
+        }
+        // out = base + o, formed in the base slice (this warp's 16 rows), then stored
+        // with 16-byte writes
+        unsigned char* os = smem_apply + (sl & 1) * G::STAGE + G::BS;
+#pragma unroll
+        for (int hr = 0; hr < 2; hr++) {
+            unsigned char* orow = os + (16 * warp + g + 8 * hr) * G::OP;
+#pragma unroll
+            for (int nt = 0; nt < KS / 8; nt++) {
+                uint32_t* pp = reinterpret_cast<uint32_t*>(orow + (nt * 8 + 2 * tg) * 2);
+                const uint32_t bb = *pp;
+                const T* bp = reinterpret_cast<const T*>(&bb);
+                *pp = pack2<T>(o[nt][2 * hr] + to_f32(bp[0]), o[nt][2 * hr + 1] + to_f32(bp[1]));
+            }
+        }
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < (16 * KS / 8) / 32; i++) {
+            const int q = lane + 32 * i, row = 16 * warp + q / (KS / 8), pc = q % (KS / 8), tok = t0 + row;
+            if (tok < ntok)
+                *reinterpret_cast<uint4*>(out + (size_t)tok * C + sl * KS + pc * 8) =
+                    *reinterpret_cast<const uint4*>(os + row * G::OP + pc * 16);
+        }
+        __syncthreads();
+    }
+}
+
 }  // namespace rwkv
 
 // ===========================================================================
@@ -480,7 +762,7 @@ extern "C" int rwkv_moe_router(const void* x, const float* gate_w, const float* 
             rc = launch_router<T, 32>(x, gate_w, bias, logits, inds, scores, pf, pc, ntok, C, E, topk, st);
     });
     if (rc) return rc;
-    moe_router_finalize_kernel<<<1, 64, 0, st>>>(pf, pc, nb, ntok, E, topk, stats, counts);
+    moe_router_finalize_kernel<<<1, FIN_THREADS, 0, st>>>(pf, pc, nb, ntok, E, topk, stats, counts);
     return check_launch();
 }
 
@@ -550,6 +832,48 @@ extern "C" int rwkv_moe_lora_combine(const void* base, const float* h, const voi
         }
     });
     return check_launch();
+}
+
+template <typename T, int EN>
+static int launch_apply(const void* x, const void* base, const void* A, const void* B, const int32_t* inds,
+                        const void* scores, void* out, int ntok, int C, int R, int E, int topk, cudaStream_t st) {
+    auto kern = moe_lora_apply_kernel<T, EN>;
+    const int smem = apply::Geo<EN>::SMEM;
+    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (err != cudaSuccess) return set_cuda_error(err);
+    const int grid = (ntok + apply::TM - 1) / apply::TM;
+    kern<<<grid, apply::NTH, smem, st>>>((const T*)x, (const T*)base, (const T*)A, (const T*)B, inds, (const T*)scores,
+                                         (T*)out, ntok, C, R, E, topk);
+    return check_launch();
+}
+template <typename T>
+static int launch_apply_en(const void* x, const void* base, const void* A, const void* B, const int32_t* inds,
+                           const void* scores, void* out, int ntok, int C, int R, int E, int topk, cudaStream_t st) {
+    switch (E * R) {
+        case 32: return launch_apply<T, 32>(x, base, A, B, inds, scores, out, ntok, C, R, E, topk, st);
+        case 64: return launch_apply<T, 64>(x, base, A, B, inds, scores, out, ntok, C, R, E, topk, st);
+        default: return launch_apply<T, 128>(x, base, A, B, inds, scores, out, ntok, C, R, E, topk, st);
+    }
+}
+
+extern "C" int rwkv_moe_lora_apply_supported(int C, int R, int E, int topk, int dtype) {
+    const int en = E * R;
+    return (dtype == RWKV_F16 || dtype == RWKV_BF16) && C > 0 && C % 64 == 0 && R > 0 && R % 8 == 0 &&
+           (en == 32 || en == 64 || en == 128) && topk > 0 && topk <= 8 && topk <= E;
+}
+
+extern "C" int rwkv_moe_lora_apply(const void* x, const void* base, const void* A, const void* B,
+                                   const int32_t* inds, const void* scores, void* out, int ntok, int C,
+                                   int R, int E, int topk, int dtype, void* stream) {
+    if (ntok <= 0) return 0;
+    if (dtype != RWKV_F16 && dtype != RWKV_BF16) return RWKV_ERR_DTYPE;
+    if (!rwkv_moe_lora_apply_supported(C, R, E, topk, dtype)) return RWKV_ERR_SHAPE;
+    if (!x || !A || !B || !inds || !out) return RWKV_ERR_ARG;
+    if (!aligned(x, 16) || !aligned(A, 16) || !aligned(B, 16) || !aligned(out, 16) || (base && !aligned(base, 16)))
+        return RWKV_ERR_ALIGN;
+    cudaStream_t st = (cudaStream_t)stream;
+    if (dtype == RWKV_F16) return launch_apply_en<__half>(x, base, A, B, inds, scores, out, ntok, C, R, E, topk, st);
+    return launch_apply_en<__nv_bfloat16>(x, base, A, B, inds, scores, out, ntok, C, R, E, topk, st);
 }
 
 extern "C" int rwkv_moe_ortho_loss(const void* A, float* out, int E, int C, int R, int dtype,
@@ -637,7 +961,7 @@ extern "C" int rwkv_moe_router_noalloc(const void* x, const float* gate_w, const
             rc = launch_router<T, 32>(x, gate_w, bias, logits, inds, scores, pf, pc, ntok, C, E, topk, st);
     });
     if (rc) return rc;
-    moe_router_finalize_kernel<<<1, 64, 0, st>>>(pf, pc, nb, ntok, E, topk, stats, counts);
+    moe_router_finalize_kernel<<<1, FIN_THREADS, 0, st>>>(pf, pc, nb, ntok, E, topk, stats, counts);
     return check_launch();
 }
 

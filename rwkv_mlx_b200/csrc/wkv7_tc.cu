@@ -1,19 +1,24 @@
 // WKV-7 forward with the state products on the 5th-generation tensor cores:
-// tcgen05.mma (kind::tf32, M=64) with accumulators in tensor memory.  Same chunk
-// algebra as wkv7_chunk.cu (L = 16):
+// tcgen05.mma (kind::tf32, M=64) with accumulators in tensor memory.  Chunk algebra
+// (L = 16, same quantities as wkv7_chunk.cu):
 //
-//   D1 = [U | Y]^T = S0 [Wu; Wy]^T + [Ui; Yi]^T          (M=64 values, N=32, K=64)
-//   D2 = S_L       = S0 diag(GL) + V^T Kb + U^T Bb        (M=64 values, N=64 keys, K=16+16)
+//   S_L        = S0 diag(GL) + Q + S0 P,   P = Wu^T Bb,  Q = Ui^T Bb + V^T Kb
+//   [U | Y]^T  = [Ui | Yi]^T + S0 [Wu; Wy]^T,  [Ui | Yi]^T = [Ui^T | V^T] [[I, Mrb^T]; [0, Mrk^T]]
 //
-// The fp32 state lives in tensor memory (D2) for the whole sequence and is itself the
-// A operand of D1 (A read from tensor memory, B = [Wu; Wy] K-major in shared memory).
-// Per chunk the 4 state warps preload the intra-chunk part [Ui; Yi]^T into D1, one
-// thread issues the 8 K-steps of D1 as two independent accumulation chains, the warps
-// scale D2 by the chunk decay and read U and Y back, then D2 takes the rank-32 update.
-// Two groups of 4 "prep" warps compute the inputs-only chunk operands (decay factors,
-// intra-chunk products on mma.sync, triangular solve) for alternating chunks, writing
-// them straight into the UMMA operand layout; the hand-offs are mbarriers with bounded
-// waits (a CTA that gives up sets the device error word and exits, it never traps).
+// Only S0 P depends on the previous chunk, so the serial chain per chunk is one
+// 8-step MMA (M=64 values, N=64 keys, K=64) whose A operand, the fp32 state, is read
+// straight from tensor memory.  Everything else is built from the inputs alone:
+// two groups of 4 "prep" warps take alternating chunks and produce P, GL, Wu/Wy
+// (UMMA K-major operands in shared memory) and issue the Q and [Ui | Yi] products
+// into tensor memory themselves.  The 4 state warps, per chunk, write
+// S0 diag(GL) + Q (exact fp32 diagonal part) into the next state buffer, one thread
+// issues S0 P into it together with S0 [Wu; Wy]^T into the chunk's [U | Y] buffer,
+// and while those run the warps store y and sa of the previous chunk.  Hand-offs
+// are mbarriers with bounded waits (a CTA that gives up sets the device error word
+// and exits, it never traps).
+//
+// Tensor memory (512 columns): state ping-pong [0,128), Q per stage [128,256),
+// [U | Y] for chunk mod 4 [256,384).
 //
 // Supported for fp16 / bf16 activations (w in the activation dtype or fp32); fp32
 // activations use the mma.sync kernel (their input staging does not fit next to this
@@ -38,31 +43,35 @@ constexpr int KLBO = 144;  // bytes between K-adjacent core matrices (16 B pad: 
 __host__ __device__ constexpr int kmaj(int r, int k, int sbo) {
     return (r & 7) * 16 + (r >> 3) * sbo + (k >> 2) * KLBO + (k & 3) * 4;
 }
-constexpr int SBO_K64 = 16 * KLBO, SBO_K32 = 8 * KLBO, SBO_K16 = 4 * KLBO;
+constexpr int SBO_K64 = 16 * KLBO, SBO_K32 = 8 * KLBO;
 constexpr int SZ_WB = 4 * SBO_K64;  // 32 rows x K=64
-constexpr int SZ_BK = 8 * SBO_K32;  // 64 rows x K=32
-constexpr int SZ_VT = 8 * SBO_K16;  // 64 rows x K=16
+constexpr int SZ_PL = 8 * SBO_K64;  // 64 rows x K=64
+constexpr int SZ_AQ = 8 * SBO_K32;  // 64 rows x K=32
+constexpr int SZ_BY = 4 * SBO_K32;  // 32 rows x K=32
+
+constexpr uint32_t COL_S = 0, COL_Q = 128, COL_D1 = 256, TMEM_COLS = 512;
 
 struct __align__(128) Stage {
-    unsigned char WB[SZ_WB];  // B of D1: rows t' (0-15 Wu, 16-31 Wy), K = key
-    unsigned char UY[SZ_WB];  // intra-chunk part of D1: rows t' (0-15 Ui, 16-31 Yi), K = value
-    unsigned char BK[SZ_BK];  // B of D2: rows key, K = t' (0-15 Bb, 16-31 Kb)
-    unsigned char VT[SZ_VT];  // A of D2 (V part): rows value, K = t
+    unsigned char WB[SZ_WB];  // B of [U|Y] (state part): rows t' (0-15 Wu, 16-31 Wy), K = key
+    unsigned char PL[SZ_PL];  // B of S0 P: rows output key j', K = key j (P[j][j'])
+    unsigned char AQ[SZ_AQ];  // A of Q and [Ui|Yi]: rows value, K = t' (0-15 Ui^T, 16-31 V^T)
+    unsigned char BK[SZ_AQ];  // B of Q: rows key, K = t' (0-15 Bb, 16-31 Kb)
+    unsigned char BY[SZ_BY];  // B of [Ui|Yi]: rows 0-15 [I | 0], rows 16-31 [Mrb | Mrk]
     float GL[N];              // decay of the whole chunk per key
 };
 struct __align__(16) PrepScratch {
-    float At[L][LD4], Rt[L][LD4], Bh[L][LD4], Kh[L][LD4];
+    float At[L][LD4], Rt[L][LD4], Bh[L][LD4], Kh[L][LD4];  // Bh, Kh hold Bb, Kb after P2
     float Mab[L][LDM], Mak[L][LDM], Mrb[L][LDM], Mrk[L][LDM];
     float MakV[L][LD8];
     float Vs[L][LD8];
     float Cs[L + 1][N];  // cumulative log2 decay, Cs[0] = 0
+    float GL[N];
 };
 struct __align__(128) Smem {
     Stage st[2];
-    unsigned char UTA[SZ_VT]; // A of D2 (U part): rows value, K = t
     float Yb[L][LD8];
     PrepScratch ps[2];
-    unsigned long long full[2], empty[2], mma1, mma2;
+    unsigned long long full[2], qready[2], empty[2], mma;
     uint32_t tmem_base;
     int abort;
 };
@@ -151,18 +160,18 @@ __global__ void __launch_bounds__(NT, 1)
     const int nck = ckpt ? T_ / ckpt_len : 0;
 
     if (warp == 0) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 128;" ::"r"(
-                         smem_u32(&sm.tmem_base))
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(&sm.tmem_base)), "n"(TMEM_COLS)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     if (tid == 32) {
-        mbar_init(&sm.full[0], 128);
-        mbar_init(&sm.full[1], 128);
-        mbar_init(&sm.empty[0], 128);
-        mbar_init(&sm.empty[1], 128);
-        mbar_init(&sm.mma1, 1);
-        mbar_init(&sm.mma2, 1);
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&sm.full[i], 128);
+            mbar_init(&sm.qready[i], 1);
+            mbar_init(&sm.empty[i], 128);
+        }
+        mbar_init(&sm.mma, 1);
         sm.abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -172,7 +181,7 @@ __global__ void __launch_bounds__(NT, 1)
     const uint32_t tmem = sm.tmem_base;
 
     if (warp >= 4) {
-        // ===================== prep groups =====================
+        // ===================== prep groups: chunks g_, g_ + 2, ... into stage g_ =====================
         const int g_ = (warp - 4) >> 2;
         const int pt = tid - 128 - 128 * g_, pw = pt >> 5, lane = pt & 31, g = lane >> 2, tg = lane & 3;
         const int BAR = BAR_PREP0 + g_;
@@ -213,18 +222,26 @@ __global__ void __launch_bounds__(NT, 1)
             }
             cp_commit();
         };
+        auto ldB = [&](const unsigned char* src, int kk, int nn) {
+            return fbits(*reinterpret_cast<const float*>(src + kmaj(kk, nn, SBO_K64)));
+        };
+
+        // rows 0-15 of BY: [I | 0] (constant; made visible to the tensor cores by the
+        // proxy fence before the first MMA issue)
+        for (int e = pt; e < L * 2 * L; e += 128) {
+            const int rr = e / (2 * L), kk = e % (2 * L);
+            *reinterpret_cast<float*>(stg.BY + kmaj(rr, kk, SBO_K32)) = rr == kk ? 1.f : 0.f;
+        }
 
         if (g_ < nchunks) issue(g_);
         for (int c = g_; c < nchunks; c += 2) {
             asm volatile("cp.async.wait_all;" ::: "memory");
-            bool bad = false;
-            if (c >= 2) bad = !mbar_wait(&sm.empty[g_], ((c >> 1) + 1) & 1, &sm.abort, &g_device_error_tc);
-            if (group_sync_or(BAR, bad)) break;
+            group_sync(BAR);
 
-            // ---- P1: cumulative log2 decay, decayed factors, operands ----
+            // ---- P1: cumulative log2 decay, decayed factors ----
             const int t = lane & 15, cg = 2 * pw + (lane >> 4), j0 = 8 * cg;
             const bool tok = t < T_ - c * L;
-            float wv[8], cs[8], cp[8], cl[8];
+            float wv[8], cs[8], cl[8], ec[8], ei[8], ep[8];
             lds8<TW>(raw + 5 * R::ARR + t * R::PITCHW + j0 * sizeof(TW), wv);
 #pragma unroll
             for (int q = 0; q < 8; q++) cs[q] = tok ? -ex2(wv[q] * LOG2E) * LOG2E : 0.f;
@@ -239,48 +256,48 @@ __global__ void __launch_bounds__(NT, 1)
             bool ext = false;
 #pragma unroll
             for (int q = 0; q < 8; q++) {
-                const float u = __shfl_up_sync(0xffffffffu, cs[q], 1, 16);
-                cp[q] = t ? u : 0.f;
-                cl[q] = __shfl_sync(0xffffffffu, cs[q], 15, 16);
-                ext |= cl[q] < -115.f;  // cumulative decay below e^-80
-            }
-            float xr[8], xk[8], xv[8], xa[8], xb[8], o1[8], o2[8];
-            lds8<T>(raw + 0 * R::ARR + t * R::PITCH + j0 * sizeof(T), xr);
-            lds8<T>(raw + 1 * R::ARR + t * R::PITCH + j0 * sizeof(T), xk);
-            lds8<T>(raw + 2 * R::ARR + t * R::PITCH + j0 * sizeof(T), xv);
-            lds8<T>(raw + 3 * R::ARR + t * R::PITCH + j0 * sizeof(T), xa);
-            lds8<T>(raw + 4 * R::ARR + t * R::PITCH + j0 * sizeof(T), xb);
-            float ec[8], ei[8], eL[8];
-#pragma unroll
-            for (int q = 0; q < 8; q++) {
                 ec[q] = ex2(cs[q]);
                 ei[q] = ex2(-cs[q]);
-                eL[q] = ex2(cl[q] - cs[q]);
+                cl[q] = __shfl_sync(0xffffffffu, cs[q], 15, 16);
+                const float up = __shfl_up_sync(0xffffffffu, ec[q], 1, 16);
+                ep[q] = t ? up : 1.f;
+                ext |= cl[q] < -115.f;  // cumulative decay below e^-80
             }
+            float bb[8], kb[8];
+            {
+                float xr[8], xk[8], xv[8], xa[8], xb[8], o1[8], o2[8];
+                lds8<T>(raw + 0 * R::ARR + t * R::PITCH + j0 * sizeof(T), xr);
+                lds8<T>(raw + 1 * R::ARR + t * R::PITCH + j0 * sizeof(T), xk);
+                lds8<T>(raw + 2 * R::ARR + t * R::PITCH + j0 * sizeof(T), xv);
+                lds8<T>(raw + 3 * R::ARR + t * R::PITCH + j0 * sizeof(T), xa);
+                lds8<T>(raw + 4 * R::ARR + t * R::PITCH + j0 * sizeof(T), xb);
 #pragma unroll
-            for (int q = 0; q < 8; q++) o1[q] = tf32f(xa[q] * ex2(cp[q])), o2[q] = tf32f(xr[q] * ec[q]);
-            sts8(&ps.At[t][j0], o1);
-            sts8(&ps.Rt[t][j0], o2);
+                for (int q = 0; q < 8; q++) o1[q] = tf32f(xa[q] * ep[q]), o2[q] = tf32f(xr[q] * ec[q]);
+                sts8(&ps.At[t][j0], o1);
+                sts8(&ps.Rt[t][j0], o2);
 #pragma unroll
-            for (int q = 0; q < 8; q++) o1[q] = tf32f(xb[q] * ei[q]), o2[q] = tf32f(xk[q] * ei[q]);
-            sts8(&ps.Bh[t][j0], o1);
-            sts8(&ps.Kh[t][j0], o2);
+                for (int q = 0; q < 8; q++) o1[q] = tf32f(xb[q] * ei[q]), o2[q] = tf32f(xk[q] * ei[q]);
+                sts8(&ps.Bh[t][j0], o1);
+                sts8(&ps.Kh[t][j0], o2);
+                // factors to the chunk end: 2^(cL - c_t) (the product form overflows only
+                // where the chunk's decay is extreme; those keys take the direct form)
+                float eL[8];
 #pragma unroll
-            for (int q = 0; q < 8; q++) {
-                const int key = j0 + q;
-                *reinterpret_cast<float*>(stg.BK + kmaj(key, t, SBO_K32)) = tf32f(xb[q] * eL[q]);
-                *reinterpret_cast<float*>(stg.BK + kmaj(key, L + t, SBO_K32)) = tf32f(xk[q] * eL[q]);
-                const float vq = tf32f(xv[q]);
-                o1[q] = vq;
-                *reinterpret_cast<float*>(stg.VT + kmaj(key, t, SBO_K16)) = vq;  // key index = value index
+                for (int q = 0; q < 8; q++) eL[q] = __shfl_sync(0xffffffffu, ec[q], 15, 16) * ei[q];
+                if (ext) {
+#pragma unroll
+                    for (int q = 0; q < 8; q++) eL[q] = ex2(cl[q] - cs[q]);
+                }
+#pragma unroll
+                for (int q = 0; q < 8; q++) bb[q] = tf32f(xb[q] * eL[q]), kb[q] = tf32f(xk[q] * eL[q]), o1[q] = tf32f(xv[q]);
+                sts8(&ps.Vs[t][j0], o1);
             }
-            sts8(&ps.Vs[t][j0], o1);
             sts8(&ps.Cs[t + 1][j0], cs);
             if (t == 0) {
 #pragma unroll
                 for (int q = 0; q < 8; q++) ps.Cs[0][j0 + q] = 0.f;
             }
-            if (t == 15) sts8(&stg.GL[j0], ec);
+            if (t == 15) sts8(&ps.GL[j0], ec);
             const bool extreme = group_sync_or(BAR, ext);
 
             // ---- P2: intra-chunk matrices ----
@@ -330,6 +347,8 @@ __global__ void __launch_bounds__(NT, 1)
             }
             group_sync(BAR);
             if (c + 2 < nchunks) issue(c + 2);  // raw staging is free from here on
+            sts8(&ps.Bh[t][j0], bb);           // Bh, Kh are dead: keep Bb, Kb there
+            sts8(&ps.Kh[t][j0], kb);
 
             // ---- P3: MakV = Mak V ----
             {
@@ -354,30 +373,49 @@ __global__ void __launch_bounds__(NT, 1)
             }
             group_sync(BAR);
 
-            // ---- P4: X = (I - Mab)^-1 [At | MakV] -> Wu (WB rows 0-15), Ui (UY rows 0-15) ----
-            {
-                float x[L];
-                const bool left = pt < 64;
-                const int col = left ? pt : pt - 64;
+            // ---- P4: X = (I - Mab)^-1 [At | MakV]: Wu (left threads) or Ui (right threads), one column each ----
+            const bool left = pt < 64;
+            const int col = left ? pt : pt - 64;
+            float x[L];
 #pragma unroll
-                for (int tt = 0; tt < L; tt++) {
-                    float accx = left ? ps.At[tt][col] : ps.MakV[tt][col];
+            for (int tt = 0; tt < L; tt++) {
+                float accx = left ? ps.At[tt][col] : ps.MakV[tt][col];
 #pragma unroll
-                    for (int s2 = 0; s2 < tt; s2++) accx = fmaf(ps.Mab[tt][s2], x[s2], accx);
-                    x[tt] = accx;
+                for (int s2 = 0; s2 < tt; s2++) accx = fmaf(ps.Mab[tt][s2], x[s2], accx);
+                x[tt] = accx;
+            }
+
+            // ---- the stage is free once the state warps are done with chunk c - 2 ----
+            bool bad = false;
+            if (c >= 2) bad = !mbar_wait(&sm.empty[g_], ((c >> 1) + 1) & 1, &sm.abort, &g_device_error_tc);
+            if (group_sync_or(BAR, bad)) break;
+            tc_fence_after();
+
+            // ---- B1: Wu -> WB rows 0-15, V^T and Ui^T -> AQ, Bb and Kb -> BK, GL ----
+            if (left) {
+#pragma unroll
+                for (int tt = 0; tt < L; tt++) *reinterpret_cast<float*>(stg.WB + kmaj(tt, col, SBO_K64)) = tf32f(x[tt]);
+#pragma unroll
+                for (int tt = 0; tt < L; tt += 4) {
+                    *reinterpret_cast<float4*>(stg.AQ + kmaj(col, L + tt, SBO_K32)) =
+                        make_float4(ps.Vs[tt][col], ps.Vs[tt + 1][col], ps.Vs[tt + 2][col], ps.Vs[tt + 3][col]);
+                    *reinterpret_cast<float4*>(stg.BK + kmaj(col, tt, SBO_K32)) =
+                        make_float4(ps.Bh[tt][col], ps.Bh[tt + 1][col], ps.Bh[tt + 2][col], ps.Bh[tt + 3][col]);
                 }
-                unsigned char* dst = left ? stg.WB : stg.UY;
+            } else {
 #pragma unroll
-                for (int tt = 0; tt < L; tt++) *reinterpret_cast<float*>(dst + kmaj(tt, col, SBO_K64)) = tf32f(x[tt]);
+                for (int tt = 0; tt < L; tt += 4) {
+                    st4(stg.AQ + kmaj(col, tt, SBO_K32), x[tt], x[tt + 1], x[tt + 2], x[tt + 3]);
+                    *reinterpret_cast<float4*>(stg.BK + kmaj(col, L + tt, SBO_K32)) =
+                        make_float4(ps.Kh[tt][col], ps.Kh[tt + 1][col], ps.Kh[tt + 2][col], ps.Kh[tt + 3][col]);
+                }
+                stg.GL[col] = ps.GL[col];
             }
             group_sync(BAR);
 
-            // ---- P5: Wy = Rt + Mrb Wu (WB rows 16-31); Yi = Mrb Ui + Mrk V (UY rows 16-31) ----
+            // ---- B2: Wy = Rt + Mrb Wu -> WB rows 16-31; [Mrb | Mrk] -> BY rows 16-31; P = Wu^T Bb -> PL ----
             {
-                auto ldB = [&](const unsigned char* src, int kk, int nn) {
-                    return fbits(*reinterpret_cast<const float*>(src + kmaj(kk, nn, SBO_K64)));
-                };
-                float wy[2][4], yi[2][4] = {};
+                float wy[2][4];
 #pragma unroll
                 for (int nt = 0; nt < 2; nt++) {
                     const int n0 = 16 * pw + 8 * nt + 2 * tg;
@@ -393,160 +431,193 @@ __global__ void __launch_bounds__(NT, 1)
                     for (int nt = 0; nt < 2; nt++) {
                         const int n0 = 16 * pw + 8 * nt;
                         mma8(wy[nt], a0, a1, a2, a3, ldB(stg.WB, k0 + tg, n0 + g), ldB(stg.WB, k0 + tg + 4, n0 + g));
-                        mma8(yi[nt], a0, a1, a2, a3, ldB(stg.UY, k0 + tg, n0 + g), ldB(stg.UY, k0 + tg + 4, n0 + g));
-                    }
-                    const uint32_t c0 = fbits(ps.Mrk[g][k0 + tg]), c1 = fbits(ps.Mrk[g + 8][k0 + tg]);
-                    const uint32_t c2 = fbits(ps.Mrk[g][k0 + tg + 4]), c3 = fbits(ps.Mrk[g + 8][k0 + tg + 4]);
-#pragma unroll
-                    for (int nt = 0; nt < 2; nt++) {
-                        const int n0 = 16 * pw + 8 * nt;
-                        mma8(yi[nt], c0, c1, c2, c3, fbits(ps.Vs[k0 + tg][n0 + g]), fbits(ps.Vs[k0 + tg + 4][n0 + g]));
                     }
                 }
 #pragma unroll
                 for (int nt = 0; nt < 2; nt++) {
 #pragma unroll
                     for (int e = 0; e < 4; e++) {
-                        const int tt = L + g + (e >> 1) * 8, col = 16 * pw + 8 * nt + 2 * tg + (e & 1);
-                        *reinterpret_cast<float*>(stg.WB + kmaj(tt, col, SBO_K64)) = tf32f(wy[nt][e]);
-                        *reinterpret_cast<float*>(stg.UY + kmaj(tt, col, SBO_K64)) = tf32f(yi[nt][e]);
+                        const int tt = L + g + (e >> 1) * 8, cc = 16 * pw + 8 * nt + 2 * tg + (e & 1);
+                        *reinterpret_cast<float*>(stg.WB + kmaj(tt, cc, SBO_K64)) = tf32f(wy[nt][e]);
                     }
                 }
             }
-            proxy_fence();  // make the operand stores visible to the tensor cores
+            {
+                const int tp = pt >> 3, kq = (pt & 7) * 4;
+                const float* src = kq < L ? &ps.Mrb[tp][kq] : &ps.Mrk[tp][kq - L];
+                *reinterpret_cast<float4*>(stg.BY + kmaj(L + tp, kq, SBO_K32)) = *reinterpret_cast<const float4*>(src);
+            }
+            {
+                // P[j][j'] = sum_t Wu[t][j] Bb[t][j']; row j' (= 16 pw + ...) of the K-major operand
+                float pl[8][4] = {};
+                const int m0 = 16 * pw;
+#pragma unroll
+                for (int ks = 0; ks < 2; ks++) {
+                    const int k0 = 8 * ks;
+                    const uint32_t a0 = fbits(ps.Bh[k0 + tg][m0 + g]), a1 = fbits(ps.Bh[k0 + tg][m0 + g + 8]);
+                    const uint32_t a2 = fbits(ps.Bh[k0 + tg + 4][m0 + g]), a3 = fbits(ps.Bh[k0 + tg + 4][m0 + g + 8]);
+#pragma unroll
+                    for (int nt = 0; nt < 8; nt++)
+                        mma8(pl[nt], a0, a1, a2, a3, ldB(stg.WB, k0 + tg, 8 * nt + g), ldB(stg.WB, k0 + tg + 4, 8 * nt + g));
+                }
+#pragma unroll
+                for (int nt = 0; nt < 8; nt++) {
+                    const int jj = 8 * nt + 2 * tg;
+                    *reinterpret_cast<float2*>(stg.PL + kmaj(m0 + g, jj, SBO_K64)) = make_float2(tf32f(pl[nt][0]), tf32f(pl[nt][1]));
+                    *reinterpret_cast<float2*>(stg.PL + kmaj(m0 + g + 8, jj, SBO_K64)) = make_float2(tf32f(pl[nt][2]), tf32f(pl[nt][3]));
+                }
+            }
+
+            // ---- B3: Q and [Ui | Yi] on the tensor cores; hand the chunk over ----
+            proxy_fence();  // operand stores -> async proxy
+            group_sync(BAR);
+            if (pt == 0) {
+                tc_fence_after();
+                const uint32_t i64 = idesc_tf32(64, 64), i32 = idesc_tf32(64, 32);
+                const uint32_t aQ = smem_u32(stg.AQ), bK = smem_u32(stg.BK), bY = smem_u32(stg.BY);
+                const uint32_t dQ = tmem + COL_Q + 64 * g_, dY = tmem + COL_D1 + 32 * (c & 3);
+#pragma unroll
+                for (int ks = 0; ks < 4; ks++) {
+                    umma(dQ, umma_desc(aQ + 2 * ks * KLBO, SBO_K32), umma_desc(bK + 2 * ks * KLBO, SBO_K32), i64, ks > 0);
+                    umma(dY, umma_desc(aQ + 2 * ks * KLBO, SBO_K32), umma_desc(bY + 2 * ks * KLBO, SBO_K32), i32, ks > 0);
+                }
+                umma_commit(&sm.qready[g_]);
+            }
             mbar_arrive(&sm.full[g_]);
         }
         asm volatile("cp.async.wait_all;" ::: "memory");
     } else {
         // ===================== state warps =====================
-        // TMEM columns: [0,64) D2 = state, [64,96) D1a, [96,128) D1b (D1 = D1a + D1b).
         const int tw = warp, lane = tid & 31;
         const bool live = lane < 16;              // M=64 accumulators use lanes 0-15 of each subpartition
         const int row = 16 * tw + lane;            // state row (value index) held by this thread
-        const int rowc = 16 * tw + (lane & 15);    // in-range row for the idle lanes' loads
-        const uint32_t lane_base = (uint32_t)(32 * tw) << 16;
-        const uint32_t tD2 = tmem + lane_base, tD1a = tD2 + 64, tD1b = tD2 + 96;
-        {
-            float S[N];
-            const float* p = (s0 && live) ? s0 + ((size_t)bh * N + row) * N : nullptr;
-#pragma unroll
-            for (int j = 0; j < N; j++) S[j] = p ? p[j] : 0.f;
-#pragma unroll
-            for (int j = 0; j < N; j += 16) tmem_st16(tD2 + j, &S[j]);
-            tmem_wait_st();
-        }
-        for (int c = 0; c < nchunks; c++) {
-            const int s = c & 1;
-            Stage& stg = sm.st[s];
-            const bool bad = !mbar_wait(&sm.full[s], (c >> 1) & 1, &sm.abort, &g_device_error_tc);
-            if (group_sync_or(BAR_STATE, bad)) break;
-            {  // D1a <- [Ui; Yi]^T (row `row`, columns t')
-                float pre[2 * L];
-#pragma unroll
-                for (int tt = 0; tt < 2 * L; tt++) pre[tt] = *reinterpret_cast<const float*>(stg.UY + kmaj(tt, rowc, SBO_K64));
-                tmem_st16(tD1a, pre);
-                tmem_st16(tD1a + 16, pre + 16);
-                tmem_wait_st();
-            }
-            tc_fence_before();
-            group_sync(BAR_STATE);
-            tc_fence_after();
-            if (tid == 0) {
-                const uint32_t i1 = idesc_tf32(64, 32), bW = smem_u32(stg.WB);
-#pragma unroll
-                for (int ks = 0; ks < 8; ks++)
-                    umma_ts((ks & 1) ? tmem + 96 : tmem + 64, tmem + 8 * ks, umma_desc(bW + 2 * ks * KLBO, SBO_K64), i1,
-                            (ks & 1) ? (ks > 1) : 1);
-                umma_commit(&sm.mma1);
-            }
-            const bool bad2 = !mbar_wait(&sm.mma1, c & 1, &sm.abort, &g_device_error_tc);
-            tc_fence_after();
-            float S[N], u[L], yv[L], u2[L], y2[L];
-#pragma unroll
-            for (int j = 0; j < N; j += 16) tmem_ld16(tD2 + j, &S[j]);
-            tmem_ld16(tD1a, u);
-            tmem_ld16(tD1a + 16, yv);
-            tmem_ld16(tD1b, u2);
-            tmem_ld16(tD1b + 16, y2);
+        const uint32_t tl = tmem + ((uint32_t)(32 * tw) << 16);
+
+        // y and sa of chunk cc from its [U | Y] buffer
+        auto output = [&](int cc) {
+            float u[L], yv[L];
+            const uint32_t d = tl + COL_D1 + 32 * (cc & 3);
+            tmem_ld16(d, u);
+            tmem_ld16(d + 16, yv);
             tmem_wait_ld();
-            // state * chunk decay -> D2
-#pragma unroll
-            for (int j = 0; j < N; j += 4) {
-                const float4 gl = *reinterpret_cast<const float4*>(&stg.GL[j]);
-                S[j] *= gl.x, S[j + 1] *= gl.y, S[j + 2] *= gl.z, S[j + 3] *= gl.w;
-            }
-#pragma unroll
-            for (int j = 0; j < N; j += 16) tmem_st16(tD2 + j, &S[j]);
-#pragma unroll
-            for (int tt = 0; tt < L; tt++) u[tt] += u2[tt], yv[tt] += y2[tt];
             if (live) {
-#pragma unroll
-                for (int tt = 0; tt < L; tt += 4) st4(sm.UTA + kmaj(row, tt, SBO_K16), u[tt], u[tt + 1], u[tt + 2], u[tt + 3]);
 #pragma unroll
                 for (int tt = 0; tt < L; tt++) sm.Yb[tt][row] = yv[tt];
                 if (sa_out) {
 #pragma unroll
                     for (int tt = 0; tt < L; tt++)
-                        if (c * L + tt < T_) sa_out[base + (size_t)(c * L + tt) * tstride + row] = u[tt];
+                        if (cc * L + tt < T_) sa_out[base + (size_t)(cc * L + tt) * tstride + row] = u[tt];
+                }
+            }
+            group_sync(BAR_STATE);
+            const int rr = tid >> 3, c8 = (tid & 7) * 8, t = cc * L + rr;
+            if (t < T_) {
+                const float4 f0 = *reinterpret_cast<const float4*>(&sm.Yb[rr][c8]);
+                const float4 f1 = *reinterpret_cast<const float4*>(&sm.Yb[rr][c8 + 4]);
+                uint4 pk;
+                T* pe = reinterpret_cast<T*>(&pk);
+                pe[0] = from_f32<T>(f0.x), pe[1] = from_f32<T>(f0.y), pe[2] = from_f32<T>(f0.z), pe[3] = from_f32<T>(f0.w);
+                pe[4] = from_f32<T>(f1.x), pe[5] = from_f32<T>(f1.y), pe[6] = from_f32<T>(f1.z), pe[7] = from_f32<T>(f1.w);
+                *reinterpret_cast<uint4*>(y + base + (size_t)t * tstride + c8) = pk;
+            }
+        };
+        // state buffer `from` (or s0) -> registers; S diag(GL) + Q of chunk cn -> buffer `to`;
+        // checkpoint of the state after chunk cn - 1 when one is due
+        auto advance = [&](uint32_t from, uint32_t to, int cn, bool have_next, bool from_s0) {
+            const int tend = cn * L;
+            const bool save = ckpt && cn > 0 && tend <= T_ && tend % ckpt_len == 0;
+            const Stage& stg = sm.st[cn & 1];
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                float S[32], q[32];
+                if (from_s0) {
+                    const float* p = (s0 && live) ? s0 + ((size_t)bh * N + row) * N + 32 * h : nullptr;
+#pragma unroll
+                    for (int j = 0; j < 32; j++) S[j] = p ? p[j] : 0.f;
+                    tmem_st16(tl + from + 32 * h, S);
+                    tmem_st16(tl + from + 32 * h + 16, S + 16);
+                } else {
+                    tmem_ld16(tl + from + 32 * h, S);
+                    tmem_ld16(tl + from + 32 * h + 16, S + 16);
+                }
+                if (have_next) {
+                    tmem_ld16(tl + COL_Q + 64 * (cn & 1) + 32 * h, q);
+                    tmem_ld16(tl + COL_Q + 64 * (cn & 1) + 32 * h + 16, q + 16);
+                }
+                tmem_wait_ld();
+                if (save && live) {
+                    float* p = ckpt + (((size_t)bh * nck + tend / ckpt_len - 1) * N + row) * N + 32 * h;
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(p + j) = make_float4(S[j], S[j + 1], S[j + 2], S[j + 3]);
+                }
+                if (have_next) {
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4) {
+                        const float4 gl = *reinterpret_cast<const float4*>(&stg.GL[32 * h + j]);
+                        S[j] = fmaf(S[j], gl.x, q[j]), S[j + 1] = fmaf(S[j + 1], gl.y, q[j + 1]);
+                        S[j + 2] = fmaf(S[j + 2], gl.z, q[j + 2]), S[j + 3] = fmaf(S[j + 3], gl.w, q[j + 3]);
+                    }
+                    tmem_st16(tl + to + 32 * h, S);
+                    tmem_st16(tl + to + 32 * h + 16, S + 16);
                 }
             }
             tmem_wait_st();
-            proxy_fence();
+        };
+        auto wait_chunk = [&](int cn) {
+            const uint32_t par = (cn >> 1) & 1;
+            return mbar_wait(&sm.full[cn & 1], par, &sm.abort, &g_device_error_tc) &&
+                   mbar_wait(&sm.qready[cn & 1], par, &sm.abort, &g_device_error_tc);
+        };
+
+        bool ok = true;
+        if (nchunks > 0) {
+            ok = !group_sync_or(BAR_STATE, !wait_chunk(0));
+            tc_fence_after();
+            advance(COL_S, COL_S + 64, 0, ok, true);  // s0 -> buffer 0; S0 diag(GL) + Q -> buffer 1
+        } else {
+            advance(COL_S, COL_S, 0, false, true);
+        }
+        for (int c = 0; ok && c < nchunks; c++) {
+            const uint32_t cur = COL_S + 64 * (c & 1), nxt = COL_S + 64 * ((c + 1) & 1);
             tc_fence_before();
-            if (group_sync_or(BAR_STATE, bad2)) break;
+            group_sync(BAR_STATE);
             tc_fence_after();
             if (tid == 0) {
-                const uint32_t i2 = idesc_tf32(64, 64);
-                const uint32_t aU = smem_u32(sm.UTA), aV = smem_u32(stg.VT), bK = smem_u32(stg.BK);
+                const Stage& stg = sm.st[c & 1];
+                const uint32_t i64 = idesc_tf32(64, 64), i32 = idesc_tf32(64, 32);
+                const uint32_t bP = smem_u32(stg.PL), bW = smem_u32(stg.WB);
+                const uint32_t dY = tmem + COL_D1 + 32 * (c & 3);
 #pragma unroll
-                for (int ks = 0; ks < 2; ks++)
-                    umma(tmem, umma_desc(aV + 2 * ks * KLBO, SBO_K16), umma_desc(bK + (4 + 2 * ks) * KLBO, SBO_K32), i2, 1);
-#pragma unroll
-                for (int ks = 0; ks < 2; ks++)
-                    umma(tmem, umma_desc(aU + 2 * ks * KLBO, SBO_K16), umma_desc(bK + 2 * ks * KLBO, SBO_K32), i2, 1);
-                umma_commit(&sm.mma2);
-            }
-            {  // y rows of this chunk: 8 consecutive values per thread, one 16-byte store
-                const int rr = tid >> 3, c8 = (tid & 7) * 8, t = c * L + rr;
-                if (t < T_) {
-                    const float4 f0 = *reinterpret_cast<const float4*>(&sm.Yb[rr][c8]);
-                    const float4 f1 = *reinterpret_cast<const float4*>(&sm.Yb[rr][c8 + 4]);
-                    uint4 pk;
-                    T* pe = reinterpret_cast<T*>(&pk);
-                    pe[0] = from_f32<T>(f0.x), pe[1] = from_f32<T>(f0.y), pe[2] = from_f32<T>(f0.z), pe[3] = from_f32<T>(f0.w);
-                    pe[4] = from_f32<T>(f1.x), pe[5] = from_f32<T>(f1.y), pe[6] = from_f32<T>(f1.z), pe[7] = from_f32<T>(f1.w);
-                    *reinterpret_cast<uint4*>(y + base + (size_t)t * tstride + c8) = pk;
+                for (int ks = 0; ks < 8; ks++) {
+                    umma_ts(tmem + nxt, tmem + cur + 8 * ks, umma_desc(bP + 2 * ks * KLBO, SBO_K64), i64, 1);
+                    umma_ts(dY, tmem + cur + 8 * ks, umma_desc(bW + 2 * ks * KLBO, SBO_K64), i32, 1);
                 }
+                umma_commit(&sm.mma);
             }
-            const bool bad3 = !mbar_wait(&sm.mma2, c & 1, &sm.abort, &g_device_error_tc);
+            if (c >= 1) output(c - 1);
+            const bool more = c + 1 < nchunks;
+            bool bad = more && !wait_chunk(c + 1);
+            bad |= !mbar_wait(&sm.mma, c & 1, &sm.abort, &g_device_error_tc);
             tc_fence_after();
-            if (ckpt) {
-                const int tend = (c + 1) * L;
-                if (tend <= T_ && tend % ckpt_len == 0) {
-#pragma unroll
-                    for (int j = 0; j < N; j += 16) tmem_ld16(tD2 + j, &S[j]);
-                    tmem_wait_ld();
-                    if (live) {
-                        float* p = ckpt + (((size_t)bh * nck + tend / ckpt_len - 1) * N + row) * N;
-#pragma unroll
-                        for (int j = 0; j < N; j += 4) *reinterpret_cast<float4*>(p + j) = make_float4(S[j], S[j + 1], S[j + 2], S[j + 3]);
-                    }
-                }
-            }
+            advance(nxt, cur, c + 1, more, false);
             tc_fence_before();
-            mbar_arrive(&sm.empty[s]);
-            if (group_sync_or(BAR_STATE, bad3)) break;  // uniform decision for the whole group
+            mbar_arrive(&sm.empty[c & 1]);
+            ok = !group_sync_or(BAR_STATE, bad);  // uniform decision for the whole group
         }
-        if (sT && !group_sync_or(BAR_STATE, sm.abort != 0)) {
-            tc_fence_after();
-            float S[N];
+        if (ok && nchunks > 0) output(nchunks - 1);
+        if (sT && ok) {
+            const uint32_t fin = COL_S + 64 * (nchunks & 1);
 #pragma unroll
-            for (int j = 0; j < N; j += 16) tmem_ld16(tD2 + j, &S[j]);
-            tmem_wait_ld();
-            if (live) {
-                float* p = sT + ((size_t)bh * N + row) * N;
+            for (int h = 0; h < 2; h++) {
+                float S[32];
+                tmem_ld16(tl + fin + 32 * h, S);
+                tmem_ld16(tl + fin + 32 * h + 16, S + 16);
+                tmem_wait_ld();
+                if (live) {
+                    float* p = sT + ((size_t)bh * N + row) * N + 32 * h;
 #pragma unroll
-                for (int j = 0; j < N; j += 4) *reinterpret_cast<float4*>(p + j) = make_float4(S[j], S[j + 1], S[j + 2], S[j + 3]);
+                    for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(p + j) = make_float4(S[j], S[j + 1], S[j + 2], S[j + 3]);
+                }
             }
         }
     }
@@ -554,7 +625,7 @@ __global__ void __launch_bounds__(NT, 1)
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 128;" ::"r"(tmem) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(TMEM_COLS) : "memory");
     }
 }
 

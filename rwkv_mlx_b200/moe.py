@@ -107,6 +107,31 @@ def lora_combine(base2d, h, Bw, inds, scores, inv, out=None):
     return out
 
 
+def lora_apply_supported(C: int, R: int, E: int, top_k: int, dtype: torch.dtype) -> bool:
+    return bool(nat.lib().rwkv_moe_lora_apply_supported(C, R, E, top_k, nat.dtype_code_of(dtype)))
+
+
+def lora_apply(x2d, base2d, A, Bw, inds, scores, out=None):
+    """out = base + sum_s scores[:, s] * (x @ A[e]) @ B[e] in one fused pass (moe.py:142-147)."""
+    ntok, C = x2d.shape
+    E, _, R = A.shape
+    k = inds.shape[1]
+    dt = x2d.dtype
+    if out is None:
+        out = torch.empty((ntok, C), device=x2d.device, dtype=dt)
+    A = A.to(dt).contiguous()
+    Bw = Bw.to(dt).contiguous()
+    base2d = None if base2d is None else base2d.to(dt).contiguous()
+    scores = None if scores is None else scores.to(dt).contiguous()
+    L = nat.lib()
+    with torch.cuda.device(x2d.device):
+        rc = L.rwkv_moe_lora_apply(nat.ptr(x2d.contiguous()), nat.ptr(base2d), nat.ptr(A), nat.ptr(Bw),
+                                   nat.ptr(inds.contiguous()), nat.ptr(scores), nat.ptr(out), ntok, C, R, E, k,
+                                   nat.dtype_code(out), _stream(x2d.device))
+    nat.check(rc, "rwkv_moe_lora_apply")
+    return out
+
+
 def ortho_loss(A: torch.Tensor) -> torch.Tensor:
     E, C, R = A.shape
     A = A.contiguous()
@@ -162,10 +187,14 @@ class LoRAMoE_CMix(nn.Module):
             base_out = self.base(x)
         x2 = x.reshape(B * T, C).contiguous()
         r = router_forward(x2, self.router.gate.weight, self.top_k, self.router.bias)
-        perm, inv, offsets = permute(r["inds"], self.n_experts)
-        h = lora_down(x2, self.lora_A.detach(), perm, offsets, self.top_k)
-        out = lora_combine(base_out.reshape(B * T, C), h, self.lora_B.detach(), r["inds"],
-                           r["scores"], inv)
+        if lora_apply_supported(C, self.lora_rank, self.n_experts, self.top_k, x.dtype):
+            out = lora_apply(x2, base_out.reshape(B * T, C), self.lora_A.detach(), self.lora_B.detach(),
+                             r["inds"], r["scores"])
+        else:  # sorted dispatch: grouped down-projection, then per-token combine
+            perm, inv, offsets = permute(r["inds"], self.n_experts)
+            h = lora_down(x2, self.lora_A.detach(), perm, offsets, self.top_k)
+            out = lora_combine(base_out.reshape(B * T, C), h, self.lora_B.detach(), r["inds"],
+                               r["scores"], inv)
         return out.reshape(B, T, C), r["aux"], r["z"]
 
     def orthogonal_loss(self) -> torch.Tensor:

@@ -17,7 +17,7 @@ pytestmark = pytest.mark.gpu
 
 def _x(ntok, C, seed, dt=torch.float16):
     rng = np.random.default_rng(seed)
-    return torch.tensor(rng.standard_normal((ntok, C)), dtype=dt, device="cuda")
+    return torch.tensor(rng.standard_normal((ntok, C)), dtype=torch.float32, device="cuda").to(dt)
 
 
 @pytest.mark.parametrize("E,k,with_bias", [(8, 2, False), (8, 2, True), (4, 1, False), (16, 3, False), (32, 4, True)])
@@ -138,3 +138,76 @@ def test_lora_moe_cmix_module_matches_oracle():
     ol = m.orthogonal_loss()
     ol_ref = mo.orthogonal_loss(npy(m.lora_A))
     assert abs(float(ol) - ol_ref) < 1e-3 * max(1e-6, ol_ref)
+
+
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("ntok,C,E,R,k,with_base", [(2000, 768, 8, 16, 2, True), (4097, 1024, 4, 8, 1, False),
+                                                    (77, 64, 8, 8, 3, True), (130, 128, 16, 8, 4, True),
+                                                    (65, 768, 2, 16, 2, True)])
+def test_lora_apply_matches_oracle(dt, ntok, C, E, R, k, with_base):
+    """Fused adapter apply (dense over E*R columns, routing mask) vs the float64 sum."""
+    from rwkv_mlx_b200.moe import lora_apply, lora_apply_supported, router_forward
+
+    assert lora_apply_supported(C, R, E, k, dt)
+    x = _x(ntok, C, 5, dt)
+    rng = np.random.default_rng(ntok + C)
+    A = torch.tensor(rng.normal(0, 0.05, (E, C, R)), dtype=dt, device="cuda")
+    Bw = torch.tensor(rng.normal(0, 0.05, (E, R, C)), dtype=dt, device="cuda")
+    gw = torch.tensor(rng.standard_normal((E, C)) * 0.05, dtype=torch.float32, device="cuda")
+    base = _x(ntok, C, 6, dt) if with_base else None
+    r = router_forward(x, gw, k)
+    out = lora_apply(x, base, A, Bw, r["inds"], r["scores"])
+    torch.cuda.synchronize()
+    npy = lambda t: t.double().cpu().numpy()
+    delta = mo.lora_moe_delta(npy(x), npy(A), npy(Bw), r["inds"].cpu().numpy(), npy(r["scores"]))
+    # without a base the delta is checked on its own; with one, the output (which is
+    # rounded to the activation dtype at the magnitude of base + delta)
+    ref = delta + (npy(base) if with_base else 0.0)
+    tol = {torch.float16: 2e-3, torch.bfloat16: 8e-3}[dt] if with_base else {torch.float16: 4e-3, torch.bfloat16: 2e-2}[dt]
+    assert rel_rms(npy(out), ref) < tol
+
+
+def test_lora_apply_in_place_and_no_scores():
+    """out aliasing base, scores NULL (all 1): the EP local step's form."""
+    from rwkv_mlx_b200.moe import lora_apply
+
+    ntok, C, E, R = 300, 256, 8, 16
+    x = _x(ntok, C, 8)
+    rng = np.random.default_rng(9)
+    A = torch.tensor(rng.normal(0, 0.05, (E, C, R)), dtype=torch.float16, device="cuda")
+    Bw = torch.tensor(rng.normal(0, 0.05, (E, R, C)), dtype=torch.float16, device="cuda")
+    inds = torch.tensor(rng.integers(0, E, (ntok, 1)), dtype=torch.int32, device="cuda")
+    base = _x(ntok, C, 10)
+    base_np = base.double().cpu().numpy()
+    out = lora_apply(x, base, A, Bw, inds, None, out=base)
+    torch.cuda.synchronize()
+    assert out.data_ptr() == base.data_ptr()
+    npy = lambda t: t.double().cpu().numpy()
+    delta = mo.lora_moe_delta(npy(x), npy(A), npy(Bw), inds.cpu().numpy(), np.ones((ntok, 1)))
+    assert rel_rms(npy(out), base_np + delta) < 2e-3
+
+
+def test_lora_moe_cmix_unsupported_shape_uses_sorted_dispatch():
+    """E*R = 256 is outside the fused kernel: the module takes the permutation path."""
+    from rwkv_mlx_b200.model import RWKV_CMix_x070, RWKVConfig
+    from rwkv_mlx_b200.moe import LoRAMoE_CMix, lora_apply_supported
+
+    assert not lora_apply_supported(256, 32, 8, 2, torch.float16)
+    torch.manual_seed(1)
+    cfg = RWKVConfig(n_layer=2, n_embd=256, dim_ffn=512)
+    base = RWKV_CMix_x070(cfg, 1).cuda()
+    m = LoRAMoE_CMix(base, n_experts=8, lora_rank=32, top_k=2).cuda()
+    with torch.no_grad():
+        m.lora_B.normal_(0, 0.02)
+        m.router.gate.weight.normal_(0, 0.05)
+    m = m.half()
+    x = torch.randn(2, 40, 256, device="cuda").half()
+    with torch.no_grad():
+        out, _, _ = m(x)
+        lg = (x.float().reshape(-1, 256) @ m.router.gate.weight.float().T).cpu().numpy()
+    npy = lambda t: t.detach().double().cpu().numpy()
+    xn = x.double().cpu().numpy()
+    inds, sc, _, _, _ = mo.router(None, None, 2, logits=lg)
+    ref = mo.cmix(xn, npy(base.x_k), npy(base.key.weight), npy(base.value.weight)) + mo.lora_moe_delta(
+        xn, npy(m.lora_A), npy(m.lora_B), inds.reshape(2, 40, 2), sc.reshape(2, 40, 2))
+    assert rel_rms(out.double().cpu().numpy(), ref) < 3e-3

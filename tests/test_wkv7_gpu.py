@@ -211,17 +211,35 @@ def test_chunked_and_sequential_kernels_agree(B, T, H):
             assert rel_rms(ck.cpu().numpy(), wo.checkpoints_from_states(st, 16).reshape(-1)) < 2e-3, impl
 
 
-def test_chunked_kernel_extreme_decays():
+@pytest.mark.parametrize("dt", [torch.float32, torch.float16])
+def test_chunked_kernel_extreme_decays(dt):
     """Per-step decays down to exp(-exp(3)) ~ 2e-9: chunks whose cumulative decay
-    leaves the factored range take the element-wise path and stay exact."""
+    leaves the factored range take the element-wise path and stay exact (fp32 inputs:
+    mma.sync kernel; fp16: tcgen05 kernel)."""
     from rwkv_mlx_b200 import _native, wkv7
 
-    d, h = _rounded(wkv_inputs(1, 80, 2, seed=8, w_lo=-1.0, w_hi=3.0), torch.float32)
+    d, h = _rounded(wkv_inputs(1, 80, 2, seed=8, w_lo=-1.0, w_hi=3.0), dt, w_dt=torch.float32)
     y = wkv7.wkv7(d["r"], d["w"], d["k"], d["v"], d["a"], d["b"])
     torch.cuda.synchronize()
     assert _native.lib().rwkv_device_error(1) == 0
     ye = wo.wkv7_forward_exact(h["r"], h["w"], h["k"], h["v"], h["a"], h["b"])[0]
-    assert rel_rms(y.cpu().numpy(), _bt(ye)) < 2e-3
+    assert rel_rms(y.double().cpu().numpy(), _bt(ye)) < TOL[dt]
+
+
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16])
+def test_long_sequence_error_stays_bounded(dt):
+    """T = 4096 (256 chunks): TF32 rounding of the chunk operands must not build up
+    along the state chain (slow decays keep old state alive the longest)."""
+    from rwkv_mlx_b200 import _native, wkv7
+
+    d, h = _rounded(wkv_inputs(1, 4096, 2, seed=21, w_lo=-6.0, w_hi=-3.0), dt, w_dt=torch.float32)
+    y, _, sa, sT = wkv7._fwd(d["r"], d["w"], d["k"], d["v"], d["a"], d["b"], want_sa=True, want_state=True)
+    torch.cuda.synchronize()
+    assert _native.lib().rwkv_device_error(1) == 0
+    ye, sae, sTe, _ = wo.wkv7_forward_exact(h["r"], h["w"], h["k"], h["v"], h["a"], h["b"])
+    assert rel_rms(y.double().cpu().numpy(), _bt(ye)) < TOL[dt]
+    assert rel_rms(sa.cpu().numpy(), sae) < 2e-3
+    assert rel_rms(sT.cpu().numpy(), sTe) < 2e-3
 
 
 def test_misaligned_inputs_use_the_sequential_kernel():

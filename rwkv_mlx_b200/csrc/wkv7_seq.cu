@@ -5,7 +5,8 @@
 //                   reads row i of S), so a head is split over 4 CTAs.
 //   wkv7_bwd_seq  : exact backward: each chunk of ckpt_len steps is replayed
 //                   from its checkpoint in sub-chunks of 8 steps whose states are
-//                   kept in shared memory; no division by the decay.
+//                   kept in shared memory; no division by the decay.  256 threads
+//                   per (b, h), each owning a quarter of a row and of a column of dS.
 //   wkv7_step     : one RNN step for a batch of sequences (memory bound).
 //
 // Math (reference rwkv_mlx/kernels/wkv7_metal.py:53-91, model.py:480-483):
@@ -116,13 +117,25 @@ __global__ void __launch_bounds__(RPB * 4)
 // (row-major, rows padded to 65 floats: column reads are conflict-free).
 // ---------------------------------------------------------------------------
 namespace bwdseq {
-constexpr int N = 64, SC = 8, LD = 65, NV = 9;
+// 256 threads per (b, h): thread (i, q) = (tid / 4, tid % 4) owns the strided quarter
+// j = 4 jj + q (jj < 16) of row i of G = dL/dS and of row i of the replayed state, and
+// the strided quarter i' = 4 ii + q of column i of G (G is kept twice, by rows and by
+// columns, so that row sums (dv, dsa) and column sums (dr, dk, db, dw, da) are both
+// thread-local plus a 4-lane shuffle).  Per-step vectors sit in shared memory in the
+// same quarter layout ([q][jj]), so a thread reads its 16 elements as 4 float4.
+constexpr int N = 64, SC = 8, LDS_ = 72, NT = 256, NVEC = 9, NOUT = 6;
 enum { VR = 0, VDEC, VWF, VK, VV, VA, VB, VDY, VU };
-constexpr size_t smem_bytes = ((size_t)(SC + 1) * N * LD + (size_t)NV * SC * N + N) * sizeof(float);
+constexpr int QS = 20;                            // quarter stride (floats): 4 quarters in distinct banks
+constexpr int VROW = 4 * QS;                      // one vector of one step in quarter layout
+constexpr int VSZ = SC * VROW;                    // one vector kind for a sub-chunk
+constexpr int OSZ = SC * N;                       // one gradient kind for a sub-chunk
+constexpr size_t ST_FLOATS = (size_t)(SC + 1) * N * LDS_;
+constexpr size_t smem_bytes = (ST_FLOATS + (size_t)NVEC * VSZ + (size_t)NOUT * OSZ + 2 * VROW) * sizeof(float);
+__device__ __forceinline__ int qidx(int e) { return (e & 3) * QS + (e >> 2); }  // element e -> [q][jj]
 }  // namespace bwdseq
 
 template <typename T, typename TW>
-__global__ void __launch_bounds__(64, 1)
+__global__ void __launch_bounds__(bwdseq::NT, 1)
     wkv7_bwd_seq_kernel(const T* __restrict__ r, const TW* __restrict__ w, const T* __restrict__ k,
                         const T* __restrict__ v, const T* __restrict__ a, const T* __restrict__ b,
                         const T* __restrict__ dy, const float* __restrict__ s0,
@@ -131,48 +144,74 @@ __global__ void __launch_bounds__(64, 1)
                         T* __restrict__ dv, T* __restrict__ da, T* __restrict__ db,
                         float* __restrict__ ds0, int T_, int H, int ckpt_len) {
     using namespace bwdseq;
-    extern __shared__ float smem[];
-    float* st = smem;                          // [SC+1][N][LD]
-    float* vec = st + (SC + 1) * N * LD;       // [NV][SC][N]
-    float* du_s = vec + NV * SC * N;           // [N]
-#define VEC(kind, s, j) vec[((kind) * SC + (s)) * N + (j)]
+    extern __shared__ __align__(16) float smem[];
+    float* st = smem;                 // [SC+1][N][LDS_] replayed states
+    float* vec = st + ST_FLOATS;      // [NVEC][SC][4][QS]
+    float* outs = vec + NVEC * VSZ;   // [NOUT][SC][N] gradients of the sub-chunk (plain layout)
+    float* dus = outs + NOUT * OSZ;   // [2][4][QS] dsa of the current step (double-buffered)
 
-    const int tid = threadIdx.x;
+    const int tid = threadIdx.x, i = tid >> 2, q = tid & 3;
     const int bh = blockIdx.x, bi = bh / H, hi = bh % H;
     const size_t tstride = (size_t)H * N;
     const size_t base = ((size_t)bi * T_ * H + hi) * N;
     const int nck = T_ / ckpt_len;
+    const int iq = qidx(i);
 
-    float Grow[N], Gcol[N];
+    auto V4 = [&](int kind, int s, float (&o)[16]) {
+        const float4* p = reinterpret_cast<const float4*>(vec + kind * VSZ + s * VROW + q * QS);
+#pragma unroll
+        for (int m = 0; m < 4; m++) {
+            const float4 x = p[m];
+            o[4 * m] = x.x, o[4 * m + 1] = x.y, o[4 * m + 2] = x.z, o[4 * m + 3] = x.w;
+        }
+    };
+    auto V1 = [&](int kind, int s) { return vec[kind * VSZ + s * VROW + iq]; };
+
+    float Grow[16], Gcol[16];
     if (dsT) {
         const float* p = dsT + (size_t)bh * N * N;
 #pragma unroll
-        for (int j = 0; j < N; j++) Grow[j] = p[tid * N + j];
-#pragma unroll
-        for (int i = 0; i < N; i++) Gcol[i] = p[i * N + tid];
+        for (int jj = 0; jj < 16; jj++) Grow[jj] = p[i * N + 4 * jj + q], Gcol[jj] = p[(4 * jj + q) * N + i];
     } else {
 #pragma unroll
-        for (int j = 0; j < N; j++) Grow[j] = 0.f, Gcol[j] = 0.f;
+        for (int jj = 0; jj < 16; jj++) Grow[jj] = 0.f, Gcol[jj] = 0.f;
     }
 
     auto stage = [&](int t_begin, int n) {
         __syncthreads();
-        for (int s = 0; s < n; s++) {
-            const size_t off = base + (size_t)(t_begin + s) * tstride + tid;
-            const float wr = ldg_f32(w + off);
-            const float wf = -expf(wr);
-            VEC(VR, s, tid) = ldg_f32(r + off);
-            VEC(VWF, s, tid) = wf;
-            VEC(VDEC, s, tid) = expf(wf);
-            VEC(VK, s, tid) = ldg_f32(k + off);
-            VEC(VV, s, tid) = ldg_f32(v + off);
-            VEC(VA, s, tid) = ldg_f32(a + off);
-            VEC(VB, s, tid) = ldg_f32(b + off);
-            VEC(VDY, s, tid) = ldg_f32(dy + off);
+        for (int e = tid; e < SC * N; e += NT) {
+            const int s = e / N, j = e % N;
+            if (s >= n) continue;
+            const size_t off = base + (size_t)(t_begin + s) * tstride + j;
+            const float wf = -expf(ldg_f32(w + off));
+            const int d = s * VROW + qidx(j);
+            vec[VR * VSZ + d] = ldg_f32(r + off);
+            vec[VWF * VSZ + d] = wf;
+            vec[VDEC * VSZ + d] = expf(wf);
+            vec[VK * VSZ + d] = ldg_f32(k + off);
+            vec[VV * VSZ + d] = ldg_f32(v + off);
+            vec[VA * VSZ + d] = ldg_f32(a + off);
+            vec[VB * VSZ + d] = ldg_f32(b + off);
+            vec[VDY * VSZ + d] = ldg_f32(dy + off);
         }
         __syncthreads();
     };
+    // one forward step of state row i (own quarter); returns sa_i
+    auto fwd_step = [&](int s, float (&S)[16]) {
+        float av[16], bv[16], kv[16], dc[16];
+        V4(VA, s, av), V4(VB, s, bv), V4(VK, s, kv), V4(VDEC, s, dc);
+        float u = 0.f;
+#pragma unroll
+        for (int jj = 0; jj < 16; jj++) u = fmaf(av[jj], S[jj], u);
+        u += __shfl_xor_sync(0xffffffffu, u, 1);
+        u += __shfl_xor_sync(0xffffffffu, u, 2);
+        const float vi = V1(VV, s);
+#pragma unroll
+        for (int jj = 0; jj < 16; jj++) S[jj] = fmaf(S[jj], dc[jj], fmaf(u, bv[jj], vi * kv[jj]));
+        return u;
+    };
 
+    int buf = 0;
     const int nchunks = (T_ + ckpt_len - 1) / ckpt_len;
     for (int c = nchunks - 1; c >= 0; c--) {
         const int cs = c * ckpt_len, ce = min(T_, cs + ckpt_len);
@@ -181,93 +220,118 @@ __global__ void __launch_bounds__(64, 1)
         const int nsub = (ce - cs + SC - 1) / SC;
         for (int p = nsub - 1; p >= 0; p--) {
             const int ps = cs + p * SC, n = min(SC, ce - ps);
-            float Srow[N];
-            if (start) {
+            float S[16];
 #pragma unroll
-                for (int j = 0; j < N; j++) Srow[j] = start[tid * N + j];
-            } else {
-#pragma unroll
-                for (int j = 0; j < N; j++) Srow[j] = 0.f;
-            }
+            for (int jj = 0; jj < 16; jj++) S[jj] = start ? start[i * N + 4 * jj + q] : 0.f;
             // replay the earlier sub-chunks of this chunk (states not kept)
             for (int pp = 0; pp < p; pp++) {
                 stage(cs + pp * SC, SC);
-                for (int s = 0; s < SC; s++) {
-                    float u = 0.f;
-#pragma unroll
-                    for (int j = 0; j < N; j++) u = fmaf(VEC(VA, s, j), Srow[j], u);
-                    const float vi = VEC(VV, s, tid);
-#pragma unroll
-                    for (int j = 0; j < N; j++)
-                        Srow[j] = fmaf(Srow[j], VEC(VDEC, s, j), fmaf(u, VEC(VB, s, j), vi * VEC(VK, s, j)));
-                }
+                for (int s = 0; s < SC; s++) fwd_step(s, S);
             }
             // replay this sub-chunk keeping every state and sa
             stage(ps, n);
 #pragma unroll
-            for (int j = 0; j < N; j++) st[tid * LD + j] = Srow[j];
+            for (int jj = 0; jj < 16; jj++) st[i * LDS_ + 4 * jj + q] = S[jj];
             for (int s = 0; s < n; s++) {
-                float u = 0.f;
+                const float u = fwd_step(s, S);
+                float* dst = st + (size_t)(s + 1) * N * LDS_ + i * LDS_;
 #pragma unroll
-                for (int j = 0; j < N; j++) u = fmaf(VEC(VA, s, j), Srow[j], u);
-                const float vi = VEC(VV, s, tid);
-#pragma unroll
-                for (int j = 0; j < N; j++) {
-                    Srow[j] = fmaf(Srow[j], VEC(VDEC, s, j), fmaf(u, VEC(VB, s, j), vi * VEC(VK, s, j)));
-                    st[((s + 1) * N + tid) * LD + j] = Srow[j];
-                }
-                VEC(VU, s, tid) = u;
+                for (int jj = 0; jj < 16; jj++) dst[4 * jj + q] = S[jj];
+                if (q == 0) vec[VU * VSZ + s * VROW + iq] = u;
             }
             __syncthreads();
             // reverse over the sub-chunk
             for (int s = n - 1; s >= 0; s--) {
-                const float* Sp = st + (size_t)s * N * LD;
-                const float* Sn = st + (size_t)(s + 1) * N * LD;
-                const float dyi = VEC(VDY, s, tid), ri = VEC(VR, s, tid);
+                const float* Sp = st + (size_t)s * N * LDS_;
+                const float* Sn = st + (size_t)(s + 1) * N * LDS_;
+                float rv[16], dyv[16];
+                V4(VR, s, rv), V4(VDY, s, dyv);
+                const float dyi = V1(VDY, s), ri = V1(VR, s);
 #pragma unroll
-                for (int j = 0; j < N; j++) Grow[j] = fmaf(dyi, VEC(VR, s, j), Grow[j]);
+                for (int jj = 0; jj < 16; jj++) Grow[jj] = fmaf(dyi, rv[jj], Grow[jj]);
 #pragma unroll
-                for (int i = 0; i < N; i++) Gcol[i] = fmaf(VEC(VDY, s, i), ri, Gcol[i]);
-                float dr_ = 0.f, dv_ = 0.f, du_ = 0.f, dk_ = 0.f, db_ = 0.f, dD = 0.f;
+                for (int ii = 0; ii < 16; ii++) Gcol[ii] = fmaf(dyv[ii], ri, Gcol[ii]);
+                float dv_ = 0.f, du_ = 0.f, dr_ = 0.f, dk_ = 0.f, db_ = 0.f, dD = 0.f;
+                {
+                    float kv[16], bv[16];
+                    V4(VK, s, kv), V4(VB, s, bv);
 #pragma unroll
-                for (int j = 0; j < N; j++) {
-                    dv_ = fmaf(Grow[j], VEC(VK, s, j), dv_);
-                    du_ = fmaf(Grow[j], VEC(VB, s, j), du_);
+                    for (int jj = 0; jj < 16; jj++) dv_ = fmaf(Grow[jj], kv[jj], dv_), du_ = fmaf(Grow[jj], bv[jj], du_);
+                }
+                {
+                    float vv[16], uv[16];
+                    V4(VV, s, vv), V4(VU, s, uv);
+#pragma unroll
+                    for (int ii = 0; ii < 16; ii++) {
+                        const int row = 4 * ii + q;
+                        dr_ = fmaf(Sn[row * LDS_ + i], dyv[ii], dr_);
+                        dk_ = fmaf(Gcol[ii], vv[ii], dk_);
+                        db_ = fmaf(Gcol[ii], uv[ii], db_);
+                        dD = fmaf(Sp[row * LDS_ + i], Gcol[ii], dD);
+                    }
                 }
 #pragma unroll
-                for (int i = 0; i < N; i++) {
-                    dr_ = fmaf(Sn[i * LD + tid], VEC(VDY, s, i), dr_);
-                    dk_ = fmaf(Gcol[i], VEC(VV, s, i), dk_);
-                    db_ = fmaf(Gcol[i], VEC(VU, s, i), db_);
-                    dD = fmaf(Sp[i * LD + tid], Gcol[i], dD);
+                for (int o = 1; o <= 2; o <<= 1) {
+                    dv_ += __shfl_xor_sync(0xffffffffu, dv_, o);
+                    du_ += __shfl_xor_sync(0xffffffffu, du_, o);
+                    dr_ += __shfl_xor_sync(0xffffffffu, dr_, o);
+                    dk_ += __shfl_xor_sync(0xffffffffu, dk_, o);
+                    db_ += __shfl_xor_sync(0xffffffffu, db_, o);
+                    dD += __shfl_xor_sync(0xffffffffu, dD, o);
                 }
-                du_s[tid] = du_;
+                float* du_s = dus + buf * VROW;
+                if (q == 0) du_s[iq] = du_;
                 __syncthreads();
+                float duv[16];
+                {
+                    const float4* pd = reinterpret_cast<const float4*>(du_s + q * QS);
+#pragma unroll
+                    for (int m = 0; m < 4; m++) {
+                        const float4 x = pd[m];
+                        duv[4 * m] = x.x, duv[4 * m + 1] = x.y, duv[4 * m + 2] = x.z, duv[4 * m + 3] = x.w;
+                    }
+                }
                 float da_ = 0.f;
 #pragma unroll
-                for (int i = 0; i < N; i++) da_ = fmaf(Sp[i * LD + tid], du_s[i], da_);
-                const size_t off = base + (size_t)(ps + s) * tstride + tid;
-                const float deci = VEC(VDEC, s, tid), ai = VEC(VA, s, tid);
-                dr[off] = from_f32<T>(dr_);
-                dw[off] = from_f32<T>(dD * deci * VEC(VWF, s, tid));
-                dk[off] = from_f32<T>(dk_);
-                dv[off] = from_f32<T>(dv_);
-                da[off] = from_f32<T>(da_);
-                db[off] = from_f32<T>(db_);
+                for (int ii = 0; ii < 16; ii++) da_ = fmaf(Sp[(4 * ii + q) * LDS_ + i], duv[ii], da_);
+                da_ += __shfl_xor_sync(0xffffffffu, da_, 1);
+                da_ += __shfl_xor_sync(0xffffffffu, da_, 2);
+                const float deci = V1(VDEC, s), ai = V1(VA, s);
+                if (q == 0) {
+                    outs[0 * OSZ + s * N + i] = dr_;
+                    outs[1 * OSZ + s * N + i] = dD * deci * V1(VWF, s);
+                } else if (q == 1) {
+                    outs[2 * OSZ + s * N + i] = dk_;
+                    outs[3 * OSZ + s * N + i] = dv_;
+                } else if (q == 2) {
+                    outs[4 * OSZ + s * N + i] = da_;
+                    outs[5 * OSZ + s * N + i] = db_;
+                }
+                {
+                    float av[16], dc[16];
+                    V4(VA, s, av), V4(VDEC, s, dc);
 #pragma unroll
-                for (int j = 0; j < N; j++) Grow[j] = fmaf(Grow[j], VEC(VDEC, s, j), du_ * VEC(VA, s, j));
+                    for (int jj = 0; jj < 16; jj++) Grow[jj] = fmaf(Grow[jj], dc[jj], du_ * av[jj]);
+                }
 #pragma unroll
-                for (int i = 0; i < N; i++) Gcol[i] = fmaf(Gcol[i], deci, du_s[i] * ai);
-                __syncthreads();
+                for (int ii = 0; ii < 16; ii++) Gcol[ii] = fmaf(Gcol[ii], deci, duv[ii] * ai);
+                buf ^= 1;
+            }
+            __syncthreads();
+            // the sub-chunk's gradients, coalesced
+            for (int e = tid; e < NOUT * n * N; e += NT) {
+                const int kind = e / (n * N), rem = e % (n * N), s = rem / N, j = rem % N;
+                const size_t off = base + (size_t)(ps + s) * tstride + j;
+                T* dst = kind == 0 ? dr : kind == 1 ? dw : kind == 2 ? dk : kind == 3 ? dv : kind == 4 ? da : db;
+                dst[off] = from_f32<T>(outs[kind * OSZ + s * N + j]);
             }
         }
     }
     if (ds0) {
-        float* p = ds0 + (size_t)bh * N * N + (size_t)tid * N;
+        float* p = ds0 + (size_t)bh * N * N + (size_t)i * N;
 #pragma unroll
-        for (int j = 0; j < N; j++) p[j] = Grow[j];
+        for (int jj = 0; jj < 16; jj++) p[4 * jj + q] = Grow[jj];
     }
-#undef VEC
 }
 
 // ---------------------------------------------------------------------------
@@ -345,7 +409,7 @@ int launch_bwd_seq(const WkvBwdArgs& p, cudaStream_t st) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)bwdseq::smem_bytes);
     if (e != cudaSuccess) return set_cuda_error(e);
-    kern<<<p.B * p.H, 64, bwdseq::smem_bytes, st>>>(
+    kern<<<p.B * p.H, bwdseq::NT, bwdseq::smem_bytes, st>>>(
         (const T*)p.r, (const TW*)p.w, (const T*)p.k, (const T*)p.v, (const T*)p.a, (const T*)p.b,
         (const T*)p.dy, p.s0, p.dsT, p.ckpt, (T*)p.dr, (T*)p.dw, (T*)p.dk, (T*)p.dv, (T*)p.da,
         (T*)p.db, p.ds0, p.T, p.H, p.ckpt_len);

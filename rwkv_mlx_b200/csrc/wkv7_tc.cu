@@ -1,24 +1,22 @@
 // WKV-7 forward with the state products on the 5th-generation tensor cores:
 // tcgen05.mma (kind::tf32, M=64) with accumulators in tensor memory.  Chunk algebra
-// (L = 16, same quantities as wkv7_chunk.cu):
+// (L = 16; decayed factors as in wkv7_chunk.cu), with Inv = (I - Mab)^-1:
 //
-//   S_L        = S0 diag(GL) + Q + S0 P,   P = Wu^T Bb,  Q = Ui^T Bb + V^T Kb
-//   [U | Y]^T  = [Ui | Yi]^T + S0 [Wu; Wy]^T,  [Ui | Yi]^T = [Ui^T | V^T] [[I, Mrb^T]; [0, Mrk^T]]
+//   Wu = Inv At,  Wy = Rt + Mrb Wu,  Gu^T = Inv Mak,  Gy^T = Mrb Gu^T + Mrk,
+//   P = Wu^T Bb,  Kb' = Kb + Gu Bb,
+//   S_L       = S0 diag(GL) + S0 P + V^T Kb'
+//   [U | Y]^T =               S0 [Wu; Wy]^T + V^T [Gu | Gy]
 //
-// Only S0 P depends on the previous chunk, so the serial chain per chunk is one
-// 8-step MMA (M=64 values, N=64 keys, K=64) whose A operand, the fp32 state, is read
-// straight from tensor memory.  Everything else is built from the inputs alone:
-// two groups of 4 "prep" warps take alternating chunks and produce P, GL, Wu/Wy
-// (UMMA K-major operands in shared memory) and issue the Q and [Ui | Yi] products
-// into tensor memory themselves.  The 4 state warps, per chunk, write
-// S0 diag(GL) + Q (exact fp32 diagonal part) into the next state buffer, one thread
-// issues S0 P into it together with S0 [Wu; Wy]^T into the chunk's [U | Y] buffer,
-// and while those run the warps store y and sa of the previous chunk.  Hand-offs
-// are mbarriers with bounded waits (a CTA that gives up sets the device error word
-// and exits, it never traps).
-//
-// Tensor memory (512 columns): state ping-pong [0,128), Q per stage [128,256),
-// [U | Y] for chunk mod 4 [256,384).
+// so both right-hand sides are one product with the state, N = 64 + 32 columns, plus
+// one with V^T (K = 16).  Per chunk one thread issues 2 + 8 MMAs (a tcgen05.mma keeps
+// the tensor pipe ~160 cycles whatever its shape, so the count is what matters) into
+// [S_L | U | Y] held in tensor memory; the A operand of the 8 state steps is the fp32
+// state itself, read from tensor memory.  The 4 state warps preload S0 diag(GL)
+// (exact fp32) and zeros, read S_L back, and store y and sa of the previous chunk
+// while the MMAs run.  Two groups of 4 "prep" warps build the inputs-only operands
+// for alternating chunks (decay scan, intra-chunk products on mma.sync, forward
+// substitution) in the UMMA K-major layout.  Hand-offs are mbarriers with bounded
+// waits (a CTA that gives up sets the device error word and exits, it never traps).
 //
 // Supported for fp16 / bf16 activations (w in the activation dtype or fp32); fp32
 // activations use the mma.sync kernel (their input staging does not fit next to this
@@ -43,35 +41,33 @@ constexpr int KLBO = 144;  // bytes between K-adjacent core matrices (16 B pad: 
 __host__ __device__ constexpr int kmaj(int r, int k, int sbo) {
     return (r & 7) * 16 + (r >> 3) * sbo + (k >> 2) * KLBO + (k & 3) * 4;
 }
-constexpr int SBO_K64 = 16 * KLBO, SBO_K32 = 8 * KLBO;
-constexpr int SZ_WB = 4 * SBO_K64;  // 32 rows x K=64
-constexpr int SZ_PL = 8 * SBO_K64;  // 64 rows x K=64
-constexpr int SZ_AQ = 8 * SBO_K32;  // 64 rows x K=32
-constexpr int SZ_BY = 4 * SBO_K32;  // 32 rows x K=32
-
-constexpr uint32_t COL_S = 0, COL_Q = 128, COL_D1 = 256, TMEM_COLS = 512;
+constexpr int SBO_K64 = 16 * KLBO, SBO_K16 = 4 * KLBO;
+constexpr int SZ_BS = 12 * SBO_K64;  // 96 rows x K=64
+constexpr int SZ_AV = 8 * SBO_K16;   // 64 rows x K=16
+constexpr int SZ_BV = 12 * SBO_K16;  // 96 rows x K=16
+constexpr int NS = 96;               // columns of [S_L | U | Y]
+constexpr int NSTAGE = 3;            // operand stages (2 prep groups: one chunk of slack)
+constexpr uint32_t TMEM_COLS = 256;  // two [S | U | Y] buffers at columns 0 and 128
 
 struct __align__(128) Stage {
-    unsigned char WB[SZ_WB];  // B of [U|Y] (state part): rows t' (0-15 Wu, 16-31 Wy), K = key
-    unsigned char PL[SZ_PL];  // B of S0 P: rows output key j', K = key j (P[j][j'])
-    unsigned char AQ[SZ_AQ];  // A of Q and [Ui|Yi]: rows value, K = t' (0-15 Ui^T, 16-31 V^T)
-    unsigned char BK[SZ_AQ];  // B of Q: rows key, K = t' (0-15 Bb, 16-31 Kb)
-    unsigned char BY[SZ_BY];  // B of [Ui|Yi]: rows 0-15 [I | 0], rows 16-31 [Mrb | Mrk]
+    unsigned char BS[SZ_BS];  // B of the state product: rows 0-63 P^T (row j', K = j), 64-79 Wu, 80-95 Wy (K = key)
+    unsigned char AV[SZ_AV];  // A of the V product: V^T (row value, K = t)
+    unsigned char BV[SZ_BV];  // B of the V product: rows 0-63 Kb'^T (row key), 64-79 Gu^T, 80-95 Gy^T (K = s)
     float GL[N];              // decay of the whole chunk per key
 };
 struct __align__(16) PrepScratch {
     float At[L][LD4], Rt[L][LD4], Bh[L][LD4], Kh[L][LD4];  // Bh, Kh hold Bb, Kb after P2
     float Mab[L][LDM], Mak[L][LDM], Mrb[L][LDM], Mrk[L][LDM];
-    float MakV[L][LD8];
+    float GuT[L][LDM];
     float Vs[L][LD8];
     float Cs[L + 1][N];  // cumulative log2 decay, Cs[0] = 0
     float GL[N];
 };
 struct __align__(128) Smem {
-    Stage st[2];
+    Stage st[NSTAGE];  // chunk c uses stage c % NSTAGE
     float Yb[L][LD8];
     PrepScratch ps[2];
-    unsigned long long full[2], qready[2], empty[2], mma;
+    unsigned long long full[NSTAGE], empty[NSTAGE], mma;
     uint32_t tmem_base;
     int abort;
 };
@@ -166,9 +162,8 @@ __global__ void __launch_bounds__(NT, 1)
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     if (tid == 32) {
-        for (int i = 0; i < 2; i++) {
+        for (int i = 0; i < NSTAGE; i++) {
             mbar_init(&sm.full[i], 128);
-            mbar_init(&sm.qready[i], 1);
             mbar_init(&sm.empty[i], 128);
         }
         mbar_init(&sm.mma, 1);
@@ -186,7 +181,6 @@ __global__ void __launch_bounds__(NT, 1)
         const int pt = tid - 128 - 128 * g_, pw = pt >> 5, lane = pt & 31, g = lane >> 2, tg = lane & 3;
         const int BAR = BAR_PREP0 + g_;
         PrepScratch& ps = sm.ps[g_];
-        Stage& stg = sm.st[g_];
         unsigned char* raw = rawbuf + (size_t)g_ * R::BYTES;
 
         const char* psrc[R::PER_THREAD];
@@ -225,13 +219,6 @@ __global__ void __launch_bounds__(NT, 1)
         auto ldB = [&](const unsigned char* src, int kk, int nn) {
             return fbits(*reinterpret_cast<const float*>(src + kmaj(kk, nn, SBO_K64)));
         };
-
-        // rows 0-15 of BY: [I | 0] (constant; made visible to the tensor cores by the
-        // proxy fence before the first MMA issue)
-        for (int e = pt; e < L * 2 * L; e += 128) {
-            const int rr = e / (2 * L), kk = e % (2 * L);
-            *reinterpret_cast<float*>(stg.BY + kmaj(rr, kk, SBO_K32)) = rr == kk ? 1.f : 0.f;
-        }
 
         if (g_ < nchunks) issue(g_);
         for (int c = g_; c < nchunks; c += 2) {
@@ -350,70 +337,46 @@ __global__ void __launch_bounds__(NT, 1)
             sts8(&ps.Bh[t][j0], bb);           // Bh, Kh are dead: keep Bb, Kb there
             sts8(&ps.Kh[t][j0], kb);
 
-            // ---- P3: MakV = Mak V ----
-            {
-                float acc3[2][4] = {};
-#pragma unroll
-                for (int ks = 0; ks < 2; ks++) {
-                    const int k0 = 8 * ks;
-                    const uint32_t a0 = fbits(ps.Mak[g][k0 + tg]), a1 = fbits(ps.Mak[g + 8][k0 + tg]);
-                    const uint32_t a2 = fbits(ps.Mak[g][k0 + tg + 4]), a3 = fbits(ps.Mak[g + 8][k0 + tg + 4]);
-#pragma unroll
-                    for (int nt = 0; nt < 2; nt++) {
-                        const int n0 = 16 * pw + 8 * nt;
-                        mma8(acc3[nt], a0, a1, a2, a3, fbits(ps.Vs[k0 + tg][n0 + g]), fbits(ps.Vs[k0 + tg + 4][n0 + g]));
-                    }
-                }
-#pragma unroll
-                for (int nt = 0; nt < 2; nt++) {
-                    const int n0 = 16 * pw + 8 * nt + 2 * tg;
-                    *reinterpret_cast<float2*>(&ps.MakV[g][n0]) = make_float2(acc3[nt][0], acc3[nt][1]);
-                    *reinterpret_cast<float2*>(&ps.MakV[g + 8][n0]) = make_float2(acc3[nt][2], acc3[nt][3]);
-                }
-            }
-            group_sync(BAR);
-
-            // ---- P4: X = (I - Mab)^-1 [At | MakV]: Wu (left threads) or Ui (right threads), one column each ----
-            const bool left = pt < 64;
-            const int col = left ? pt : pt - 64;
+            // ---- P4: forward substitution (I - Mab) X = [At | Mak]: Wu (threads 0-63, one key
+            //      column each) and Gu^T (threads 64-79, one column each), column-oriented
+            const int col = pt;
             float x[L];
+            if (pt < N + L) {
 #pragma unroll
-            for (int tt = 0; tt < L; tt++) {
-                float accx = left ? ps.At[tt][col] : ps.MakV[tt][col];
+                for (int tt = 0; tt < L; tt++) x[tt] = pt < N ? ps.At[tt][col] : ps.Mak[tt][col - N];
 #pragma unroll
-                for (int s2 = 0; s2 < tt; s2++) accx = fmaf(ps.Mab[tt][s2], x[s2], accx);
-                x[tt] = accx;
+                for (int s2 = 0; s2 < L - 1; s2++) {
+#pragma unroll
+                    for (int tt = s2 + 1; tt < L; tt++) x[tt] = fmaf(ps.Mab[tt][s2], x[s2], x[tt]);
+                }
+                if (pt >= N) {
+#pragma unroll
+                    for (int tt = 0; tt < L; tt++) ps.GuT[tt][col - N] = tf32f(x[tt]);
+                }
             }
 
             // ---- the stage is free once the state warps are done with chunk c - 2 ----
             bool bad = false;
-            if (c >= 2) bad = !mbar_wait(&sm.empty[g_], ((c >> 1) + 1) & 1, &sm.abort, &g_device_error_tc);
+            const int si = c % NSTAGE;
+            Stage& stg = sm.st[si];
+            if (c >= NSTAGE) bad = !mbar_wait(&sm.empty[si], ((c / NSTAGE) + 1) & 1, &sm.abort, &g_device_error_tc);
             if (group_sync_or(BAR, bad)) break;
-            tc_fence_after();
 
-            // ---- B1: Wu -> WB rows 0-15, V^T and Ui^T -> AQ, Bb and Kb -> BK, GL ----
-            if (left) {
+            // ---- B1: Wu -> BS rows 64-79, V^T -> AV, GL ----
+            if (pt < N) {
 #pragma unroll
-                for (int tt = 0; tt < L; tt++) *reinterpret_cast<float*>(stg.WB + kmaj(tt, col, SBO_K64)) = tf32f(x[tt]);
+                for (int tt = 0; tt < L; tt++) *reinterpret_cast<float*>(stg.BS + kmaj(N + tt, col, SBO_K64)) = tf32f(x[tt]);
 #pragma unroll
-                for (int tt = 0; tt < L; tt += 4) {
-                    *reinterpret_cast<float4*>(stg.AQ + kmaj(col, L + tt, SBO_K32)) =
+                for (int tt = 0; tt < L; tt += 4)
+                    *reinterpret_cast<float4*>(stg.AV + kmaj(col, tt, SBO_K16)) =
                         make_float4(ps.Vs[tt][col], ps.Vs[tt + 1][col], ps.Vs[tt + 2][col], ps.Vs[tt + 3][col]);
-                    *reinterpret_cast<float4*>(stg.BK + kmaj(col, tt, SBO_K32)) =
-                        make_float4(ps.Bh[tt][col], ps.Bh[tt + 1][col], ps.Bh[tt + 2][col], ps.Bh[tt + 3][col]);
-                }
             } else {
-#pragma unroll
-                for (int tt = 0; tt < L; tt += 4) {
-                    st4(stg.AQ + kmaj(col, tt, SBO_K32), x[tt], x[tt + 1], x[tt + 2], x[tt + 3]);
-                    *reinterpret_cast<float4*>(stg.BK + kmaj(col, L + tt, SBO_K32)) =
-                        make_float4(ps.Kh[tt][col], ps.Kh[tt + 1][col], ps.Kh[tt + 2][col], ps.Kh[tt + 3][col]);
-                }
-                stg.GL[col] = ps.GL[col];
+                stg.GL[pt - N] = ps.GL[pt - N];
             }
             group_sync(BAR);
 
-            // ---- B2: Wy = Rt + Mrb Wu -> WB rows 16-31; [Mrb | Mrk] -> BY rows 16-31; P = Wu^T Bb -> PL ----
+            // ---- B2: Wy = Rt + Mrb Wu -> BS rows 80-95; P^T -> BS rows 0-63;
+            //      Kb'^T -> BV rows 0-63; Gu^T, Gy^T -> BV rows 64-95 ----
             {
                 float wy[2][4];
 #pragma unroll
@@ -430,22 +393,17 @@ __global__ void __launch_bounds__(NT, 1)
 #pragma unroll
                     for (int nt = 0; nt < 2; nt++) {
                         const int n0 = 16 * pw + 8 * nt;
-                        mma8(wy[nt], a0, a1, a2, a3, ldB(stg.WB, k0 + tg, n0 + g), ldB(stg.WB, k0 + tg + 4, n0 + g));
+                        mma8(wy[nt], a0, a1, a2, a3, ldB(stg.BS, N + k0 + tg, n0 + g), ldB(stg.BS, N + k0 + tg + 4, n0 + g));
                     }
                 }
 #pragma unroll
                 for (int nt = 0; nt < 2; nt++) {
 #pragma unroll
                     for (int e = 0; e < 4; e++) {
-                        const int tt = L + g + (e >> 1) * 8, cc = 16 * pw + 8 * nt + 2 * tg + (e & 1);
-                        *reinterpret_cast<float*>(stg.WB + kmaj(tt, cc, SBO_K64)) = tf32f(wy[nt][e]);
+                        const int tt = N + L + g + (e >> 1) * 8, cc = 16 * pw + 8 * nt + 2 * tg + (e & 1);
+                        *reinterpret_cast<float*>(stg.BS + kmaj(tt, cc, SBO_K64)) = tf32f(wy[nt][e]);
                     }
                 }
-            }
-            {
-                const int tp = pt >> 3, kq = (pt & 7) * 4;
-                const float* src = kq < L ? &ps.Mrb[tp][kq] : &ps.Mrk[tp][kq - L];
-                *reinterpret_cast<float4*>(stg.BY + kmaj(L + tp, kq, SBO_K32)) = *reinterpret_cast<const float4*>(src);
             }
             {
                 // P[j][j'] = sum_t Wu[t][j] Bb[t][j']; row j' (= 16 pw + ...) of the K-major operand
@@ -458,47 +416,99 @@ __global__ void __launch_bounds__(NT, 1)
                     const uint32_t a2 = fbits(ps.Bh[k0 + tg + 4][m0 + g]), a3 = fbits(ps.Bh[k0 + tg + 4][m0 + g + 8]);
 #pragma unroll
                     for (int nt = 0; nt < 8; nt++)
-                        mma8(pl[nt], a0, a1, a2, a3, ldB(stg.WB, k0 + tg, 8 * nt + g), ldB(stg.WB, k0 + tg + 4, 8 * nt + g));
+                        mma8(pl[nt], a0, a1, a2, a3, ldB(stg.BS, N + k0 + tg, 8 * nt + g), ldB(stg.BS, N + k0 + tg + 4, 8 * nt + g));
                 }
 #pragma unroll
                 for (int nt = 0; nt < 8; nt++) {
                     const int jj = 8 * nt + 2 * tg;
-                    *reinterpret_cast<float2*>(stg.PL + kmaj(m0 + g, jj, SBO_K64)) = make_float2(tf32f(pl[nt][0]), tf32f(pl[nt][1]));
-                    *reinterpret_cast<float2*>(stg.PL + kmaj(m0 + g + 8, jj, SBO_K64)) = make_float2(tf32f(pl[nt][2]), tf32f(pl[nt][3]));
+                    *reinterpret_cast<float2*>(stg.BS + kmaj(m0 + g, jj, SBO_K64)) = make_float2(tf32f(pl[nt][0]), tf32f(pl[nt][1]));
+                    *reinterpret_cast<float2*>(stg.BS + kmaj(m0 + g + 8, jj, SBO_K64)) = make_float2(tf32f(pl[nt][2]), tf32f(pl[nt][3]));
+                }
+            }
+            {
+                // Kb'[s][j] = Kb[s][j] + sum_t' Gu^T[t'][s] Bb[t'][j] for keys j in [16 pw, 16 pw + 16)
+                float kq[2][4];
+#pragma unroll
+                for (int nt = 0; nt < 2; nt++) {
+                    const int n0 = 16 * pw + 8 * nt + 2 * tg;
+                    kq[nt][0] = ps.Kh[g][n0], kq[nt][1] = ps.Kh[g][n0 + 1];
+                    kq[nt][2] = ps.Kh[g + 8][n0], kq[nt][3] = ps.Kh[g + 8][n0 + 1];
+                }
+#pragma unroll
+                for (int ks = 0; ks < 2; ks++) {
+                    const int k0 = 8 * ks;
+                    const uint32_t a0 = fbits(ps.GuT[k0 + tg][g]), a1 = fbits(ps.GuT[k0 + tg][g + 8]);
+                    const uint32_t a2 = fbits(ps.GuT[k0 + tg + 4][g]), a3 = fbits(ps.GuT[k0 + tg + 4][g + 8]);
+#pragma unroll
+                    for (int nt = 0; nt < 2; nt++) {
+                        const int n0 = 16 * pw + 8 * nt;
+                        mma8(kq[nt], a0, a1, a2, a3, fbits(ps.Bh[k0 + tg][n0 + g]), fbits(ps.Bh[k0 + tg + 4][n0 + g]));
+                    }
+                }
+#pragma unroll
+                for (int nt = 0; nt < 2; nt++) {
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        const int ss = g + (e >> 1) * 8, jj = 16 * pw + 8 * nt + 2 * tg + (e & 1);
+                        *reinterpret_cast<float*>(stg.BV + kmaj(jj, ss, SBO_K16)) = tf32f(kq[nt][e]);
+                    }
+                }
+            }
+            if (pw == 0) {
+                // Gy^T[t'][s] = sum_u Mrb[t'][u] Gu^T[u][s] + Mrk[t'][s]
+                float gy[2][4];
+#pragma unroll
+                for (int nt = 0; nt < 2; nt++) {
+                    const int n0 = 8 * nt + 2 * tg;
+                    gy[nt][0] = ps.Mrk[g][n0], gy[nt][1] = ps.Mrk[g][n0 + 1];
+                    gy[nt][2] = ps.Mrk[g + 8][n0], gy[nt][3] = ps.Mrk[g + 8][n0 + 1];
+                }
+#pragma unroll
+                for (int ks = 0; ks < 2; ks++) {
+                    const int k0 = 8 * ks;
+                    const uint32_t a0 = fbits(ps.Mrb[g][k0 + tg]), a1 = fbits(ps.Mrb[g + 8][k0 + tg]);
+                    const uint32_t a2 = fbits(ps.Mrb[g][k0 + tg + 4]), a3 = fbits(ps.Mrb[g + 8][k0 + tg + 4]);
+#pragma unroll
+                    for (int nt = 0; nt < 2; nt++)
+                        mma8(gy[nt], a0, a1, a2, a3, fbits(ps.GuT[k0 + tg][8 * nt + g]), fbits(ps.GuT[k0 + tg + 4][8 * nt + g]));
+                }
+#pragma unroll
+                for (int nt = 0; nt < 2; nt++) {
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        const int tp = g + (e >> 1) * 8, ss = 8 * nt + 2 * tg + (e & 1);
+                        *reinterpret_cast<float*>(stg.BV + kmaj(N + L + tp, ss, SBO_K16)) = tf32f(gy[nt][e]);
+                    }
+                }
+            } else if (pw == 1) {
+#pragma unroll
+                for (int i = 0; i < (L * L) / 32; i++) {
+                    const int q = lane + 32 * i, tp = q / L, ss = q % L;
+                    *reinterpret_cast<float*>(stg.BV + kmaj(N + tp, ss, SBO_K16)) = ps.GuT[tp][ss];
                 }
             }
 
-            // ---- B3: Q and [Ui | Yi] on the tensor cores; hand the chunk over ----
+            // ---- B3: hand the chunk over ----
             proxy_fence();  // operand stores -> async proxy
-            group_sync(BAR);
-            if (pt == 0) {
-                tc_fence_after();
-                const uint32_t i64 = idesc_tf32(64, 64), i32 = idesc_tf32(64, 32);
-                const uint32_t aQ = smem_u32(stg.AQ), bK = smem_u32(stg.BK), bY = smem_u32(stg.BY);
-                const uint32_t dQ = tmem + COL_Q + 64 * g_, dY = tmem + COL_D1 + 32 * (c & 3);
-#pragma unroll
-                for (int ks = 0; ks < 4; ks++) {
-                    umma(dQ, umma_desc(aQ + 2 * ks * KLBO, SBO_K32), umma_desc(bK + 2 * ks * KLBO, SBO_K32), i64, ks > 0);
-                    umma(dY, umma_desc(aQ + 2 * ks * KLBO, SBO_K32), umma_desc(bY + 2 * ks * KLBO, SBO_K32), i32, ks > 0);
-                }
-                umma_commit(&sm.qready[g_]);
-            }
-            mbar_arrive(&sm.full[g_]);
+            mbar_arrive(&sm.full[si]);
         }
         asm volatile("cp.async.wait_all;" ::: "memory");
     } else {
         // ===================== state warps =====================
+        // tensor memory: buffer b at column 128 b holds [S (64) | U (16) | Y (16)]; chunk c
+        // reads the state from buffer c & 1 and accumulates into buffer (c + 1) & 1
         const int tw = warp, lane = tid & 31;
         const bool live = lane < 16;              // M=64 accumulators use lanes 0-15 of each subpartition
         const int row = 16 * tw + lane;            // state row (value index) held by this thread
         const uint32_t tl = tmem + ((uint32_t)(32 * tw) << 16);
+        auto buf = [](int c) { return (uint32_t)(128 * (c & 1)); };
 
-        // y and sa of chunk cc from its [U | Y] buffer
+        // y and sa of chunk cc from its buffer (U at +64, Y at +80)
         auto output = [&](int cc) {
             float u[L], yv[L];
-            const uint32_t d = tl + COL_D1 + 32 * (cc & 3);
+            const uint32_t d = tl + buf(cc + 1) + N;
             tmem_ld16(d, u);
-            tmem_ld16(d + 16, yv);
+            tmem_ld16(d + L, yv);
             tmem_wait_ld();
             if (live) {
 #pragma unroll
@@ -521,30 +531,27 @@ __global__ void __launch_bounds__(NT, 1)
                 *reinterpret_cast<uint4*>(y + base + (size_t)t * tstride + c8) = pk;
             }
         };
-        // state buffer `from` (or s0) -> registers; S diag(GL) + Q of chunk cn -> buffer `to`;
-        // checkpoint of the state after chunk cn - 1 when one is due
-        auto advance = [&](uint32_t from, uint32_t to, int cn, bool have_next, bool from_s0) {
+        // S (state after chunk cn - 1, from tensor memory or s0) -> checkpoint when due;
+        // S diag(GL of chunk cn) and zero [U | Y] -> buffer (cn + 1) & 1
+        auto advance = [&](int cn, bool have_next, bool from_s0) {
             const int tend = cn * L;
             const bool save = ckpt && cn > 0 && tend <= T_ && tend % ckpt_len == 0;
-            const Stage& stg = sm.st[cn & 1];
+            const Stage& stg = sm.st[cn % NSTAGE];
+            const uint32_t from = tl + buf(cn), to = tl + buf(cn + 1);
 #pragma unroll
             for (int h = 0; h < 2; h++) {
-                float S[32], q[32];
+                float S[32];
                 if (from_s0) {
                     const float* p = (s0 && live) ? s0 + ((size_t)bh * N + row) * N + 32 * h : nullptr;
 #pragma unroll
                     for (int j = 0; j < 32; j++) S[j] = p ? p[j] : 0.f;
-                    tmem_st16(tl + from + 32 * h, S);
-                    tmem_st16(tl + from + 32 * h + 16, S + 16);
+                    tmem_st16(from + 32 * h, S);
+                    tmem_st16(from + 32 * h + 16, S + 16);
                 } else {
-                    tmem_ld16(tl + from + 32 * h, S);
-                    tmem_ld16(tl + from + 32 * h + 16, S + 16);
+                    tmem_ld16(from + 32 * h, S);
+                    tmem_ld16(from + 32 * h + 16, S + 16);
+                    tmem_wait_ld();
                 }
-                if (have_next) {
-                    tmem_ld16(tl + COL_Q + 64 * (cn & 1) + 32 * h, q);
-                    tmem_ld16(tl + COL_Q + 64 * (cn & 1) + 32 * h + 16, q + 16);
-                }
-                tmem_wait_ld();
                 if (save && live) {
                     float* p = ckpt + (((size_t)bh * nck + tend / ckpt_len - 1) * N + row) * N + 32 * h;
 #pragma unroll
@@ -554,64 +561,64 @@ __global__ void __launch_bounds__(NT, 1)
 #pragma unroll
                     for (int j = 0; j < 32; j += 4) {
                         const float4 gl = *reinterpret_cast<const float4*>(&stg.GL[32 * h + j]);
-                        S[j] = fmaf(S[j], gl.x, q[j]), S[j + 1] = fmaf(S[j + 1], gl.y, q[j + 1]);
-                        S[j + 2] = fmaf(S[j + 2], gl.z, q[j + 2]), S[j + 3] = fmaf(S[j + 3], gl.w, q[j + 3]);
+                        S[j] *= gl.x, S[j + 1] *= gl.y, S[j + 2] *= gl.z, S[j + 3] *= gl.w;
                     }
-                    tmem_st16(tl + to + 32 * h, S);
-                    tmem_st16(tl + to + 32 * h + 16, S + 16);
+                    tmem_st16(to + 32 * h, S);
+                    tmem_st16(to + 32 * h + 16, S + 16);
                 }
             }
+            if (have_next) {
+                float z[16];
+#pragma unroll
+                for (int j = 0; j < 16; j++) z[j] = 0.f;
+                tmem_st16(to + N, z);
+                tmem_st16(to + N + L, z);
+            }
             tmem_wait_st();
-        };
-        auto wait_chunk = [&](int cn) {
-            const uint32_t par = (cn >> 1) & 1;
-            return mbar_wait(&sm.full[cn & 1], par, &sm.abort, &g_device_error_tc) &&
-                   mbar_wait(&sm.qready[cn & 1], par, &sm.abort, &g_device_error_tc);
         };
 
         bool ok = true;
         if (nchunks > 0) {
-            ok = !group_sync_or(BAR_STATE, !wait_chunk(0));
-            tc_fence_after();
-            advance(COL_S, COL_S + 64, 0, ok, true);  // s0 -> buffer 0; S0 diag(GL) + Q -> buffer 1
+            ok = !group_sync_or(BAR_STATE, !mbar_wait(&sm.full[0], 0, &sm.abort, &g_device_error_tc));
+            advance(0, ok, true);  // s0 -> buffer 0; S0 diag(GL) and zeros -> buffer 1
         } else {
-            advance(COL_S, COL_S, 0, false, true);
+            advance(0, false, true);
         }
         for (int c = 0; ok && c < nchunks; c++) {
-            const uint32_t cur = COL_S + 64 * (c & 1), nxt = COL_S + 64 * ((c + 1) & 1);
             tc_fence_before();
             group_sync(BAR_STATE);
             tc_fence_after();
             if (tid == 0) {
-                const Stage& stg = sm.st[c & 1];
-                const uint32_t i64 = idesc_tf32(64, 64), i32 = idesc_tf32(64, 32);
-                const uint32_t bP = smem_u32(stg.PL), bW = smem_u32(stg.WB);
-                const uint32_t dY = tmem + COL_D1 + 32 * (c & 3);
+                const Stage& stg = sm.st[c % NSTAGE];
+                const uint32_t id = idesc_tf32(64, NS);
+                const uint32_t aV = smem_u32(stg.AV), bV = smem_u32(stg.BV), bS = smem_u32(stg.BS);
+                const uint32_t d = tmem + buf(c + 1), a_ = tmem + buf(c);
 #pragma unroll
-                for (int ks = 0; ks < 8; ks++) {
-                    umma_ts(tmem + nxt, tmem + cur + 8 * ks, umma_desc(bP + 2 * ks * KLBO, SBO_K64), i64, 1);
-                    umma_ts(dY, tmem + cur + 8 * ks, umma_desc(bW + 2 * ks * KLBO, SBO_K64), i32, 1);
-                }
+                for (int ks = 0; ks < 2; ks++)
+                    umma(d, umma_desc(aV + 2 * ks * KLBO, SBO_K16), umma_desc(bV + 2 * ks * KLBO, SBO_K16), id, 1);
+#pragma unroll
+                for (int ks = 0; ks < 8; ks++)
+                    umma_ts(d, a_ + 8 * ks, umma_desc(bS + 2 * ks * KLBO, SBO_K64), id, 1);
                 umma_commit(&sm.mma);
             }
             if (c >= 1) output(c - 1);
             const bool more = c + 1 < nchunks;
-            bool bad = more && !wait_chunk(c + 1);
+            bool bad = more && !mbar_wait(&sm.full[(c + 1) % NSTAGE], ((c + 1) / NSTAGE) & 1, &sm.abort, &g_device_error_tc);
             bad |= !mbar_wait(&sm.mma, c & 1, &sm.abort, &g_device_error_tc);
             tc_fence_after();
-            advance(nxt, cur, c + 1, more, false);
+            advance(c + 1, more, false);
             tc_fence_before();
-            mbar_arrive(&sm.empty[c & 1]);
+            mbar_arrive(&sm.empty[c % NSTAGE]);
             ok = !group_sync_or(BAR_STATE, bad);  // uniform decision for the whole group
         }
         if (ok && nchunks > 0) output(nchunks - 1);
         if (sT && ok) {
-            const uint32_t fin = COL_S + 64 * (nchunks & 1);
+            const uint32_t fin = tl + buf(nchunks);
 #pragma unroll
             for (int h = 0; h < 2; h++) {
                 float S[32];
-                tmem_ld16(tl + fin + 32 * h, S);
-                tmem_ld16(tl + fin + 32 * h + 16, S + 16);
+                tmem_ld16(fin + 32 * h, S);
+                tmem_ld16(fin + 32 * h + 16, S + 16);
                 tmem_wait_ld();
                 if (live) {
                     float* p = sT + ((size_t)bh * N + row) * N + 32 * h;

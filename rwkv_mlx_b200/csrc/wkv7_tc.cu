@@ -1,21 +1,18 @@
 // WKV-7 forward with the state products on the 5th-generation tensor cores:
-// tcgen05.mma (kind::tf32, M=64) with accumulators in tensor memory.  Chunk algebra
-// (L = 16; decayed factors as in wkv7_chunk.cu), with Inv = (I - Mab)^-1:
+// tcgen05.mma (kind::tf32, M=64) with accumulators in tensor memory.  Same chunk
+// algebra as wkv7_chunk.cu (L = 16):
 //
-//   Wu = Inv At,  Wy = Rt + Mrb Wu,  Gu^T = Inv Mak,  Gy^T = Mrb Gu^T + Mrk,
-//   P = Wu^T Bb,  Kb' = Kb + Gu Bb,
-//   S_L       = S0 diag(GL) + S0 P + V^T Kb'
-//   [U | Y]^T =               S0 [Wu; Wy]^T + V^T [Gu | Gy]
+//   D1 = [U | Y]^T = S0 [Wu; Wy]^T + [Ui; Yi]^T          (M=64 values, N=32, K=64)
+//   D2 = S_L       = S0 diag(GL) + V^T Kb + U^T Bb        (M=64 values, N=64 keys, K=16+16)
 //
-// so both right-hand sides are one product with the state, N = 64 + 32 columns, plus
-// one with V^T (K = 16).  Per chunk one thread issues 2 + 8 MMAs (a tcgen05.mma keeps
-// the tensor pipe ~160 cycles whatever its shape, so the count is what matters) into
-// [S_L | U | Y] held in tensor memory; the A operand of the 8 state steps is the fp32
-// state itself, read from tensor memory.  The 4 state warps preload S0 diag(GL)
-// (exact fp32) and zeros, read S_L back, and store y and sa of the previous chunk
-// while the MMAs run.  Two groups of 4 "prep" warps build the inputs-only operands
-// for alternating chunks (decay scan, intra-chunk products on mma.sync, forward
-// substitution) in the UMMA K-major layout.  Hand-offs are mbarriers with bounded
+// The fp32 state lives in tensor memory (D2) for the whole sequence and is itself the
+// A operand of D1 (A read from tensor memory, B = [Wu; Wy] K-major in shared memory).
+// Per chunk the 4 state warps preload the intra-chunk part [Ui; Yi]^T into D1, one
+// thread issues the 8 K-steps of D1 as two independent accumulation chains, the warps
+// scale D2 by the chunk decay and read U and Y back, then D2 takes the rank-32 update.
+// Two groups of 4 "prep" warps compute the inputs-only chunk operands (decay factors,
+// intra-chunk products on mma.sync, triangular solve) for alternating chunks, writing
+// them straight into the UMMA operand layout; the hand-offs are mbarriers with bounded
 // waits (a CTA that gives up sets the device error word and exits, it never traps).
 //
 // Supported for fp16 / bf16 activations (w in the activation dtype or fp32); fp32
@@ -35,39 +32,38 @@ namespace tc {
 using namespace ck;
 
 constexpr int NT = 384;
-constexpr int KLBO = 144;  // bytes between K-adjacent core matrices (16 B pad: conflict-free stores)
+constexpr int KLBO = 144;
+constexpr int NSTAGE = 3;  // operand stages for 2 prep groups: one chunk of slack  // bytes between K-adjacent core matrices (16 B pad: conflict-free stores)
 
 // byte offset of element (row r, column k) of a K-major no-swizzle UMMA operand
 __host__ __device__ constexpr int kmaj(int r, int k, int sbo) {
     return (r & 7) * 16 + (r >> 3) * sbo + (k >> 2) * KLBO + (k & 3) * 4;
 }
-constexpr int SBO_K64 = 16 * KLBO, SBO_K16 = 4 * KLBO;
-constexpr int SZ_BS = 12 * SBO_K64;  // 96 rows x K=64
-constexpr int SZ_AV = 8 * SBO_K16;   // 64 rows x K=16
-constexpr int SZ_BV = 12 * SBO_K16;  // 96 rows x K=16
-constexpr int NS = 96;               // columns of [S_L | U | Y]
-constexpr int NSTAGE = 3;            // operand stages (2 prep groups: one chunk of slack)
-constexpr uint32_t TMEM_COLS = 256;  // two [S | U | Y] buffers at columns 0 and 128
+constexpr int SBO_K64 = 16 * KLBO, SBO_K32 = 8 * KLBO, SBO_K16 = 4 * KLBO;
+constexpr int SZ_WB = 4 * SBO_K64;  // 32 rows x K=64
+constexpr int SZ_BK = 8 * SBO_K32;  // 64 rows x K=32
+constexpr int SZ_VT = 8 * SBO_K16;  // 64 rows x K=16
 
 struct __align__(128) Stage {
-    unsigned char BS[SZ_BS];  // B of the state product: rows 0-63 P^T (row j', K = j), 64-79 Wu, 80-95 Wy (K = key)
-    unsigned char AV[SZ_AV];  // A of the V product: V^T (row value, K = t)
-    unsigned char BV[SZ_BV];  // B of the V product: rows 0-63 Kb'^T (row key), 64-79 Gu^T, 80-95 Gy^T (K = s)
+    unsigned char WB[SZ_WB];  // B of D1: rows t' (0-15 Wu, 16-31 Wy), K = key
+    unsigned char UY[SZ_WB];  // intra-chunk part of D1: rows t' (0-15 Ui, 16-31 Yi), K = value
+    unsigned char BK[SZ_BK];  // B of D2: rows key, K = t' (0-15 Bb, 16-31 Kb)
+    unsigned char VT[SZ_VT];  // A of D2 (V part): rows value, K = t
     float GL[N];              // decay of the whole chunk per key
 };
 struct __align__(16) PrepScratch {
-    float At[L][LD4], Rt[L][LD4], Bh[L][LD4], Kh[L][LD4];  // Bh, Kh hold Bb, Kb after P2
+    float At[L][LD4], Rt[L][LD4], Bh[L][LD4], Kh[L][LD4];
     float Mab[L][LDM], Mak[L][LDM], Mrb[L][LDM], Mrk[L][LDM];
-    float GuT[L][LDM];
+    float MakV[L][LD8];
     float Vs[L][LD8];
     float Cs[L + 1][N];  // cumulative log2 decay, Cs[0] = 0
-    float GL[N];
 };
 struct __align__(128) Smem {
     Stage st[NSTAGE];  // chunk c uses stage c % NSTAGE
+    unsigned char UTA[SZ_VT]; // A of D2 (U part): rows value, K = t
     float Yb[L][LD8];
     PrepScratch ps[2];
-    unsigned long long full[NSTAGE], empty[NSTAGE], mma;
+    unsigned long long full[NSTAGE], empty[NSTAGE], mma1, mma2;
     uint32_t tmem_base;
     int abort;
 };
@@ -156,8 +152,8 @@ __global__ void __launch_bounds__(NT, 1)
     const int nck = ckpt ? T_ / ckpt_len : 0;
 
     if (warp == 0) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                         smem_u32(&sm.tmem_base)), "n"(TMEM_COLS)
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 128;" ::"r"(
+                         smem_u32(&sm.tmem_base))
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -166,7 +162,8 @@ __global__ void __launch_bounds__(NT, 1)
             mbar_init(&sm.full[i], 128);
             mbar_init(&sm.empty[i], 128);
         }
-        mbar_init(&sm.mma, 1);
+        mbar_init(&sm.mma1, 1);
+        mbar_init(&sm.mma2, 1);
         sm.abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -176,7 +173,7 @@ __global__ void __launch_bounds__(NT, 1)
     const uint32_t tmem = sm.tmem_base;
 
     if (warp >= 4) {
-        // ===================== prep groups: chunks g_, g_ + 2, ... into stage g_ =====================
+        // ===================== prep groups =====================
         const int g_ = (warp - 4) >> 2;
         const int pt = tid - 128 - 128 * g_, pw = pt >> 5, lane = pt & 31, g = lane >> 2, tg = lane & 3;
         const int BAR = BAR_PREP0 + g_;
@@ -216,19 +213,20 @@ __global__ void __launch_bounds__(NT, 1)
             }
             cp_commit();
         };
-        auto ldB = [&](const unsigned char* src, int kk, int nn) {
-            return fbits(*reinterpret_cast<const float*>(src + kmaj(kk, nn, SBO_K64)));
-        };
 
         if (g_ < nchunks) issue(g_);
         for (int c = g_; c < nchunks; c += 2) {
             asm volatile("cp.async.wait_all;" ::: "memory");
-            group_sync(BAR);
+            bool bad = false;
+            const int si = c % NSTAGE;
+            Stage& stg = sm.st[si];
+            if (c >= NSTAGE) bad = !mbar_wait(&sm.empty[si], ((c / NSTAGE) + 1) & 1, &sm.abort, &g_device_error_tc);
+            if (group_sync_or(BAR, bad)) break;
 
-            // ---- P1: cumulative log2 decay, decayed factors ----
+            // ---- P1: cumulative log2 decay, decayed factors, operands ----
             const int t = lane & 15, cg = 2 * pw + (lane >> 4), j0 = 8 * cg;
             const bool tok = t < T_ - c * L;
-            float wv[8], cs[8], cl[8], ec[8], ei[8], ep[8];
+            float wv[8], cs[8], cp[8], cl[8];
             lds8<TW>(raw + 5 * R::ARR + t * R::PITCHW + j0 * sizeof(TW), wv);
 #pragma unroll
             for (int q = 0; q < 8; q++) cs[q] = tok ? -ex2(wv[q] * LOG2E) * LOG2E : 0.f;
@@ -243,48 +241,48 @@ __global__ void __launch_bounds__(NT, 1)
             bool ext = false;
 #pragma unroll
             for (int q = 0; q < 8; q++) {
-                ec[q] = ex2(cs[q]);
-                ei[q] = ex2(-cs[q]);
+                const float u = __shfl_up_sync(0xffffffffu, cs[q], 1, 16);
+                cp[q] = t ? u : 0.f;
                 cl[q] = __shfl_sync(0xffffffffu, cs[q], 15, 16);
-                const float up = __shfl_up_sync(0xffffffffu, ec[q], 1, 16);
-                ep[q] = t ? up : 1.f;
                 ext |= cl[q] < -115.f;  // cumulative decay below e^-80
             }
-            float bb[8], kb[8];
-            {
-                float xr[8], xk[8], xv[8], xa[8], xb[8], o1[8], o2[8];
-                lds8<T>(raw + 0 * R::ARR + t * R::PITCH + j0 * sizeof(T), xr);
-                lds8<T>(raw + 1 * R::ARR + t * R::PITCH + j0 * sizeof(T), xk);
-                lds8<T>(raw + 2 * R::ARR + t * R::PITCH + j0 * sizeof(T), xv);
-                lds8<T>(raw + 3 * R::ARR + t * R::PITCH + j0 * sizeof(T), xa);
-                lds8<T>(raw + 4 * R::ARR + t * R::PITCH + j0 * sizeof(T), xb);
+            float xr[8], xk[8], xv[8], xa[8], xb[8], o1[8], o2[8];
+            lds8<T>(raw + 0 * R::ARR + t * R::PITCH + j0 * sizeof(T), xr);
+            lds8<T>(raw + 1 * R::ARR + t * R::PITCH + j0 * sizeof(T), xk);
+            lds8<T>(raw + 2 * R::ARR + t * R::PITCH + j0 * sizeof(T), xv);
+            lds8<T>(raw + 3 * R::ARR + t * R::PITCH + j0 * sizeof(T), xa);
+            lds8<T>(raw + 4 * R::ARR + t * R::PITCH + j0 * sizeof(T), xb);
+            float ec[8], ei[8], eL[8];
 #pragma unroll
-                for (int q = 0; q < 8; q++) o1[q] = tf32f(xa[q] * ep[q]), o2[q] = tf32f(xr[q] * ec[q]);
-                sts8(&ps.At[t][j0], o1);
-                sts8(&ps.Rt[t][j0], o2);
-#pragma unroll
-                for (int q = 0; q < 8; q++) o1[q] = tf32f(xb[q] * ei[q]), o2[q] = tf32f(xk[q] * ei[q]);
-                sts8(&ps.Bh[t][j0], o1);
-                sts8(&ps.Kh[t][j0], o2);
-                // factors to the chunk end: 2^(cL - c_t) (the product form overflows only
-                // where the chunk's decay is extreme; those keys take the direct form)
-                float eL[8];
-#pragma unroll
-                for (int q = 0; q < 8; q++) eL[q] = __shfl_sync(0xffffffffu, ec[q], 15, 16) * ei[q];
-                if (ext) {
-#pragma unroll
-                    for (int q = 0; q < 8; q++) eL[q] = ex2(cl[q] - cs[q]);
-                }
-#pragma unroll
-                for (int q = 0; q < 8; q++) bb[q] = tf32f(xb[q] * eL[q]), kb[q] = tf32f(xk[q] * eL[q]), o1[q] = tf32f(xv[q]);
-                sts8(&ps.Vs[t][j0], o1);
+            for (int q = 0; q < 8; q++) {
+                ec[q] = ex2(cs[q]);
+                ei[q] = ex2(-cs[q]);
+                eL[q] = ex2(cl[q] - cs[q]);
             }
+#pragma unroll
+            for (int q = 0; q < 8; q++) o1[q] = tf32f(xa[q] * ex2(cp[q])), o2[q] = tf32f(xr[q] * ec[q]);
+            sts8(&ps.At[t][j0], o1);
+            sts8(&ps.Rt[t][j0], o2);
+#pragma unroll
+            for (int q = 0; q < 8; q++) o1[q] = tf32f(xb[q] * ei[q]), o2[q] = tf32f(xk[q] * ei[q]);
+            sts8(&ps.Bh[t][j0], o1);
+            sts8(&ps.Kh[t][j0], o2);
+#pragma unroll
+            for (int q = 0; q < 8; q++) {
+                const int key = j0 + q;
+                *reinterpret_cast<float*>(stg.BK + kmaj(key, t, SBO_K32)) = tf32f(xb[q] * eL[q]);
+                *reinterpret_cast<float*>(stg.BK + kmaj(key, L + t, SBO_K32)) = tf32f(xk[q] * eL[q]);
+                const float vq = tf32f(xv[q]);
+                o1[q] = vq;
+                *reinterpret_cast<float*>(stg.VT + kmaj(key, t, SBO_K16)) = vq;  // key index = value index
+            }
+            sts8(&ps.Vs[t][j0], o1);
             sts8(&ps.Cs[t + 1][j0], cs);
             if (t == 0) {
 #pragma unroll
                 for (int q = 0; q < 8; q++) ps.Cs[0][j0 + q] = 0.f;
             }
-            if (t == 15) sts8(&ps.GL[j0], ec);
+            if (t == 15) sts8(&stg.GL[j0], ec);
             const bool extreme = group_sync_or(BAR, ext);
 
             // ---- P2: intra-chunk matrices ----
@@ -334,51 +332,54 @@ __global__ void __launch_bounds__(NT, 1)
             }
             group_sync(BAR);
             if (c + 2 < nchunks) issue(c + 2);  // raw staging is free from here on
-            sts8(&ps.Bh[t][j0], bb);           // Bh, Kh are dead: keep Bb, Kb there
-            sts8(&ps.Kh[t][j0], kb);
 
-            // ---- P4: forward substitution (I - Mab) X = [At | Mak]: Wu (threads 0-63, one key
-            //      column each) and Gu^T (threads 64-79, one column each), column-oriented
-            const int col = pt;
-            float x[L];
-            if (pt < N + L) {
+            // ---- P3: MakV = Mak V ----
+            {
+                float acc3[2][4] = {};
 #pragma unroll
-                for (int tt = 0; tt < L; tt++) x[tt] = pt < N ? ps.At[tt][col] : ps.Mak[tt][col - N];
+                for (int ks = 0; ks < 2; ks++) {
+                    const int k0 = 8 * ks;
+                    const uint32_t a0 = fbits(ps.Mak[g][k0 + tg]), a1 = fbits(ps.Mak[g + 8][k0 + tg]);
+                    const uint32_t a2 = fbits(ps.Mak[g][k0 + tg + 4]), a3 = fbits(ps.Mak[g + 8][k0 + tg + 4]);
 #pragma unroll
-                for (int s2 = 0; s2 < L - 1; s2++) {
-#pragma unroll
-                    for (int tt = s2 + 1; tt < L; tt++) x[tt] = fmaf(ps.Mab[tt][s2], x[s2], x[tt]);
+                    for (int nt = 0; nt < 2; nt++) {
+                        const int n0 = 16 * pw + 8 * nt;
+                        mma8(acc3[nt], a0, a1, a2, a3, fbits(ps.Vs[k0 + tg][n0 + g]), fbits(ps.Vs[k0 + tg + 4][n0 + g]));
+                    }
                 }
-                if (pt >= N) {
 #pragma unroll
-                    for (int tt = 0; tt < L; tt++) ps.GuT[tt][col - N] = tf32f(x[tt]);
+                for (int nt = 0; nt < 2; nt++) {
+                    const int n0 = 16 * pw + 8 * nt + 2 * tg;
+                    *reinterpret_cast<float2*>(&ps.MakV[g][n0]) = make_float2(acc3[nt][0], acc3[nt][1]);
+                    *reinterpret_cast<float2*>(&ps.MakV[g + 8][n0]) = make_float2(acc3[nt][2], acc3[nt][3]);
                 }
-            }
-
-            // ---- the stage is free once the state warps are done with chunk c - 2 ----
-            bool bad = false;
-            const int si = c % NSTAGE;
-            Stage& stg = sm.st[si];
-            if (c >= NSTAGE) bad = !mbar_wait(&sm.empty[si], ((c / NSTAGE) + 1) & 1, &sm.abort, &g_device_error_tc);
-            if (group_sync_or(BAR, bad)) break;
-
-            // ---- B1: Wu -> BS rows 64-79, V^T -> AV, GL ----
-            if (pt < N) {
-#pragma unroll
-                for (int tt = 0; tt < L; tt++) *reinterpret_cast<float*>(stg.BS + kmaj(N + tt, col, SBO_K64)) = tf32f(x[tt]);
-#pragma unroll
-                for (int tt = 0; tt < L; tt += 4)
-                    *reinterpret_cast<float4*>(stg.AV + kmaj(col, tt, SBO_K16)) =
-                        make_float4(ps.Vs[tt][col], ps.Vs[tt + 1][col], ps.Vs[tt + 2][col], ps.Vs[tt + 3][col]);
-            } else {
-                stg.GL[pt - N] = ps.GL[pt - N];
             }
             group_sync(BAR);
 
-            // ---- B2: Wy = Rt + Mrb Wu -> BS rows 80-95; P^T -> BS rows 0-63;
-            //      Kb'^T -> BV rows 0-63; Gu^T, Gy^T -> BV rows 64-95 ----
+            // ---- P4: X = (I - Mab)^-1 [At | MakV] -> Wu (WB rows 0-15), Ui (UY rows 0-15) ----
             {
-                float wy[2][4];
+                float x[L];
+                const bool left = pt < 64;
+                const int col = left ? pt : pt - 64;
+#pragma unroll
+                for (int tt = 0; tt < L; tt++) {
+                    float accx = left ? ps.At[tt][col] : ps.MakV[tt][col];
+#pragma unroll
+                    for (int s2 = 0; s2 < tt; s2++) accx = fmaf(ps.Mab[tt][s2], x[s2], accx);
+                    x[tt] = accx;
+                }
+                unsigned char* dst = left ? stg.WB : stg.UY;
+#pragma unroll
+                for (int tt = 0; tt < L; tt++) *reinterpret_cast<float*>(dst + kmaj(tt, col, SBO_K64)) = tf32f(x[tt]);
+            }
+            group_sync(BAR);
+
+            // ---- P5: Wy = Rt + Mrb Wu (WB rows 16-31); Yi = Mrb Ui + Mrk V (UY rows 16-31) ----
+            {
+                auto ldB = [&](const unsigned char* src, int kk, int nn) {
+                    return fbits(*reinterpret_cast<const float*>(src + kmaj(kk, nn, SBO_K64)));
+                };
+                float wy[2][4], yi[2][4] = {};
 #pragma unroll
                 for (int nt = 0; nt < 2; nt++) {
                     const int n0 = 16 * pw + 8 * nt + 2 * tg;
@@ -393,238 +394,161 @@ __global__ void __launch_bounds__(NT, 1)
 #pragma unroll
                     for (int nt = 0; nt < 2; nt++) {
                         const int n0 = 16 * pw + 8 * nt;
-                        mma8(wy[nt], a0, a1, a2, a3, ldB(stg.BS, N + k0 + tg, n0 + g), ldB(stg.BS, N + k0 + tg + 4, n0 + g));
+                        mma8(wy[nt], a0, a1, a2, a3, ldB(stg.WB, k0 + tg, n0 + g), ldB(stg.WB, k0 + tg + 4, n0 + g));
+                        mma8(yi[nt], a0, a1, a2, a3, ldB(stg.UY, k0 + tg, n0 + g), ldB(stg.UY, k0 + tg + 4, n0 + g));
                     }
-                }
-#pragma unroll
-                for (int nt = 0; nt < 2; nt++) {
-#pragma unroll
-                    for (int e = 0; e < 4; e++) {
-                        const int tt = N + L + g + (e >> 1) * 8, cc = 16 * pw + 8 * nt + 2 * tg + (e & 1);
-                        *reinterpret_cast<float*>(stg.BS + kmaj(tt, cc, SBO_K64)) = tf32f(wy[nt][e]);
-                    }
-                }
-            }
-            {
-                // P[j][j'] = sum_t Wu[t][j] Bb[t][j']; row j' (= 16 pw + ...) of the K-major operand
-                float pl[8][4] = {};
-                const int m0 = 16 * pw;
-#pragma unroll
-                for (int ks = 0; ks < 2; ks++) {
-                    const int k0 = 8 * ks;
-                    const uint32_t a0 = fbits(ps.Bh[k0 + tg][m0 + g]), a1 = fbits(ps.Bh[k0 + tg][m0 + g + 8]);
-                    const uint32_t a2 = fbits(ps.Bh[k0 + tg + 4][m0 + g]), a3 = fbits(ps.Bh[k0 + tg + 4][m0 + g + 8]);
-#pragma unroll
-                    for (int nt = 0; nt < 8; nt++)
-                        mma8(pl[nt], a0, a1, a2, a3, ldB(stg.BS, N + k0 + tg, 8 * nt + g), ldB(stg.BS, N + k0 + tg + 4, 8 * nt + g));
-                }
-#pragma unroll
-                for (int nt = 0; nt < 8; nt++) {
-                    const int jj = 8 * nt + 2 * tg;
-                    *reinterpret_cast<float2*>(stg.BS + kmaj(m0 + g, jj, SBO_K64)) = make_float2(tf32f(pl[nt][0]), tf32f(pl[nt][1]));
-                    *reinterpret_cast<float2*>(stg.BS + kmaj(m0 + g + 8, jj, SBO_K64)) = make_float2(tf32f(pl[nt][2]), tf32f(pl[nt][3]));
-                }
-            }
-            {
-                // Kb'[s][j] = Kb[s][j] + sum_t' Gu^T[t'][s] Bb[t'][j] for keys j in [16 pw, 16 pw + 16)
-                float kq[2][4];
-#pragma unroll
-                for (int nt = 0; nt < 2; nt++) {
-                    const int n0 = 16 * pw + 8 * nt + 2 * tg;
-                    kq[nt][0] = ps.Kh[g][n0], kq[nt][1] = ps.Kh[g][n0 + 1];
-                    kq[nt][2] = ps.Kh[g + 8][n0], kq[nt][3] = ps.Kh[g + 8][n0 + 1];
-                }
-#pragma unroll
-                for (int ks = 0; ks < 2; ks++) {
-                    const int k0 = 8 * ks;
-                    const uint32_t a0 = fbits(ps.GuT[k0 + tg][g]), a1 = fbits(ps.GuT[k0 + tg][g + 8]);
-                    const uint32_t a2 = fbits(ps.GuT[k0 + tg + 4][g]), a3 = fbits(ps.GuT[k0 + tg + 4][g + 8]);
+                    const uint32_t c0 = fbits(ps.Mrk[g][k0 + tg]), c1 = fbits(ps.Mrk[g + 8][k0 + tg]);
+                    const uint32_t c2 = fbits(ps.Mrk[g][k0 + tg + 4]), c3 = fbits(ps.Mrk[g + 8][k0 + tg + 4]);
 #pragma unroll
                     for (int nt = 0; nt < 2; nt++) {
                         const int n0 = 16 * pw + 8 * nt;
-                        mma8(kq[nt], a0, a1, a2, a3, fbits(ps.Bh[k0 + tg][n0 + g]), fbits(ps.Bh[k0 + tg + 4][n0 + g]));
+                        mma8(yi[nt], c0, c1, c2, c3, fbits(ps.Vs[k0 + tg][n0 + g]), fbits(ps.Vs[k0 + tg + 4][n0 + g]));
                     }
                 }
 #pragma unroll
                 for (int nt = 0; nt < 2; nt++) {
 #pragma unroll
                     for (int e = 0; e < 4; e++) {
-                        const int ss = g + (e >> 1) * 8, jj = 16 * pw + 8 * nt + 2 * tg + (e & 1);
-                        *reinterpret_cast<float*>(stg.BV + kmaj(jj, ss, SBO_K16)) = tf32f(kq[nt][e]);
+                        const int tt = L + g + (e >> 1) * 8, col = 16 * pw + 8 * nt + 2 * tg + (e & 1);
+                        *reinterpret_cast<float*>(stg.WB + kmaj(tt, col, SBO_K64)) = tf32f(wy[nt][e]);
+                        *reinterpret_cast<float*>(stg.UY + kmaj(tt, col, SBO_K64)) = tf32f(yi[nt][e]);
                     }
                 }
             }
-            if (pw == 0) {
-                // Gy^T[t'][s] = sum_u Mrb[t'][u] Gu^T[u][s] + Mrk[t'][s]
-                float gy[2][4];
-#pragma unroll
-                for (int nt = 0; nt < 2; nt++) {
-                    const int n0 = 8 * nt + 2 * tg;
-                    gy[nt][0] = ps.Mrk[g][n0], gy[nt][1] = ps.Mrk[g][n0 + 1];
-                    gy[nt][2] = ps.Mrk[g + 8][n0], gy[nt][3] = ps.Mrk[g + 8][n0 + 1];
-                }
-#pragma unroll
-                for (int ks = 0; ks < 2; ks++) {
-                    const int k0 = 8 * ks;
-                    const uint32_t a0 = fbits(ps.Mrb[g][k0 + tg]), a1 = fbits(ps.Mrb[g + 8][k0 + tg]);
-                    const uint32_t a2 = fbits(ps.Mrb[g][k0 + tg + 4]), a3 = fbits(ps.Mrb[g + 8][k0 + tg + 4]);
-#pragma unroll
-                    for (int nt = 0; nt < 2; nt++)
-                        mma8(gy[nt], a0, a1, a2, a3, fbits(ps.GuT[k0 + tg][8 * nt + g]), fbits(ps.GuT[k0 + tg + 4][8 * nt + g]));
-                }
-#pragma unroll
-                for (int nt = 0; nt < 2; nt++) {
-#pragma unroll
-                    for (int e = 0; e < 4; e++) {
-                        const int tp = g + (e >> 1) * 8, ss = 8 * nt + 2 * tg + (e & 1);
-                        *reinterpret_cast<float*>(stg.BV + kmaj(N + L + tp, ss, SBO_K16)) = tf32f(gy[nt][e]);
-                    }
-                }
-            } else if (pw == 1) {
-#pragma unroll
-                for (int i = 0; i < (L * L) / 32; i++) {
-                    const int q = lane + 32 * i, tp = q / L, ss = q % L;
-                    *reinterpret_cast<float*>(stg.BV + kmaj(N + tp, ss, SBO_K16)) = ps.GuT[tp][ss];
-                }
-            }
-
-            // ---- B3: hand the chunk over ----
-            proxy_fence();  // operand stores -> async proxy
+            proxy_fence();  // make the operand stores visible to the tensor cores
             mbar_arrive(&sm.full[si]);
         }
         asm volatile("cp.async.wait_all;" ::: "memory");
     } else {
         // ===================== state warps =====================
-        // tensor memory: buffer b at column 128 b holds [S (64) | U (16) | Y (16)]; chunk c
-        // reads the state from buffer c & 1 and accumulates into buffer (c + 1) & 1
+        // TMEM columns: [0,64) D2 = state, [64,96) D1a, [96,128) D1b (D1 = D1a + D1b).
         const int tw = warp, lane = tid & 31;
         const bool live = lane < 16;              // M=64 accumulators use lanes 0-15 of each subpartition
         const int row = 16 * tw + lane;            // state row (value index) held by this thread
-        const uint32_t tl = tmem + ((uint32_t)(32 * tw) << 16);
-        auto buf = [](int c) { return (uint32_t)(128 * (c & 1)); };
-
-        // y and sa of chunk cc from its buffer (U at +64, Y at +80)
-        auto output = [&](int cc) {
-            float u[L], yv[L];
-            const uint32_t d = tl + buf(cc + 1) + N;
-            tmem_ld16(d, u);
-            tmem_ld16(d + L, yv);
+        const int rowc = 16 * tw + (lane & 15);    // in-range row for the idle lanes' loads
+        const uint32_t lane_base = (uint32_t)(32 * tw) << 16;
+        const uint32_t tD2 = tmem + lane_base, tD1a = tD2 + 64, tD1b = tD2 + 96;
+        {
+            float S[N];
+            const float* p = (s0 && live) ? s0 + ((size_t)bh * N + row) * N : nullptr;
+#pragma unroll
+            for (int j = 0; j < N; j++) S[j] = p ? p[j] : 0.f;
+#pragma unroll
+            for (int j = 0; j < N; j += 16) tmem_st16(tD2 + j, &S[j]);
+            tmem_wait_st();
+        }
+        for (int c = 0; c < nchunks; c++) {
+            const int s = c % NSTAGE;
+            Stage& stg = sm.st[s];
+            const bool bad = !mbar_wait(&sm.full[s], (c / NSTAGE) & 1, &sm.abort, &g_device_error_tc);
+            if (group_sync_or(BAR_STATE, bad)) break;
+            {  // D1a <- [Ui; Yi]^T (row `row`, columns t')
+                float pre[2 * L];
+#pragma unroll
+                for (int tt = 0; tt < 2 * L; tt++) pre[tt] = *reinterpret_cast<const float*>(stg.UY + kmaj(tt, rowc, SBO_K64));
+                tmem_st16(tD1a, pre);
+                tmem_st16(tD1a + 16, pre + 16);
+                tmem_wait_st();
+            }
+            tc_fence_before();
+            group_sync(BAR_STATE);
+            tc_fence_after();
+            if (tid == 0) {
+                const uint32_t i1 = idesc_tf32(64, 32), bW = smem_u32(stg.WB);
+#pragma unroll
+                for (int ks = 0; ks < 8; ks++)
+                    umma_ts((ks & 1) ? tmem + 96 : tmem + 64, tmem + 8 * ks, umma_desc(bW + 2 * ks * KLBO, SBO_K64), i1,
+                            (ks & 1) ? (ks > 1) : 1);
+                umma_commit(&sm.mma1);
+            }
+            const bool bad2 = !mbar_wait(&sm.mma1, c & 1, &sm.abort, &g_device_error_tc);
+            tc_fence_after();
+            float S[N], u[L], yv[L], u2[L], y2[L];
+#pragma unroll
+            for (int j = 0; j < N; j += 16) tmem_ld16(tD2 + j, &S[j]);
+            tmem_ld16(tD1a, u);
+            tmem_ld16(tD1a + 16, yv);
+            tmem_ld16(tD1b, u2);
+            tmem_ld16(tD1b + 16, y2);
             tmem_wait_ld();
+            // state * chunk decay -> D2
+#pragma unroll
+            for (int j = 0; j < N; j += 4) {
+                const float4 gl = *reinterpret_cast<const float4*>(&stg.GL[j]);
+                S[j] *= gl.x, S[j + 1] *= gl.y, S[j + 2] *= gl.z, S[j + 3] *= gl.w;
+            }
+#pragma unroll
+            for (int j = 0; j < N; j += 16) tmem_st16(tD2 + j, &S[j]);
+#pragma unroll
+            for (int tt = 0; tt < L; tt++) u[tt] += u2[tt], yv[tt] += y2[tt];
             if (live) {
+#pragma unroll
+                for (int tt = 0; tt < L; tt += 4) st4(sm.UTA + kmaj(row, tt, SBO_K16), u[tt], u[tt + 1], u[tt + 2], u[tt + 3]);
 #pragma unroll
                 for (int tt = 0; tt < L; tt++) sm.Yb[tt][row] = yv[tt];
                 if (sa_out) {
 #pragma unroll
                     for (int tt = 0; tt < L; tt++)
-                        if (cc * L + tt < T_) sa_out[base + (size_t)(cc * L + tt) * tstride + row] = u[tt];
+                        if (c * L + tt < T_) sa_out[base + (size_t)(c * L + tt) * tstride + row] = u[tt];
                 }
-            }
-            group_sync(BAR_STATE);
-            const int rr = tid >> 3, c8 = (tid & 7) * 8, t = cc * L + rr;
-            if (t < T_) {
-                const float4 f0 = *reinterpret_cast<const float4*>(&sm.Yb[rr][c8]);
-                const float4 f1 = *reinterpret_cast<const float4*>(&sm.Yb[rr][c8 + 4]);
-                uint4 pk;
-                T* pe = reinterpret_cast<T*>(&pk);
-                pe[0] = from_f32<T>(f0.x), pe[1] = from_f32<T>(f0.y), pe[2] = from_f32<T>(f0.z), pe[3] = from_f32<T>(f0.w);
-                pe[4] = from_f32<T>(f1.x), pe[5] = from_f32<T>(f1.y), pe[6] = from_f32<T>(f1.z), pe[7] = from_f32<T>(f1.w);
-                *reinterpret_cast<uint4*>(y + base + (size_t)t * tstride + c8) = pk;
-            }
-        };
-        // S (state after chunk cn - 1, from tensor memory or s0) -> checkpoint when due;
-        // S diag(GL of chunk cn) and zero [U | Y] -> buffer (cn + 1) & 1
-        auto advance = [&](int cn, bool have_next, bool from_s0) {
-            const int tend = cn * L;
-            const bool save = ckpt && cn > 0 && tend <= T_ && tend % ckpt_len == 0;
-            const Stage& stg = sm.st[cn % NSTAGE];
-            const uint32_t from = tl + buf(cn), to = tl + buf(cn + 1);
-#pragma unroll
-            for (int h = 0; h < 2; h++) {
-                float S[32];
-                if (from_s0) {
-                    const float* p = (s0 && live) ? s0 + ((size_t)bh * N + row) * N + 32 * h : nullptr;
-#pragma unroll
-                    for (int j = 0; j < 32; j++) S[j] = p ? p[j] : 0.f;
-                    tmem_st16(from + 32 * h, S);
-                    tmem_st16(from + 32 * h + 16, S + 16);
-                } else {
-                    tmem_ld16(from + 32 * h, S);
-                    tmem_ld16(from + 32 * h + 16, S + 16);
-                    tmem_wait_ld();
-                }
-                if (save && live) {
-                    float* p = ckpt + (((size_t)bh * nck + tend / ckpt_len - 1) * N + row) * N + 32 * h;
-#pragma unroll
-                    for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(p + j) = make_float4(S[j], S[j + 1], S[j + 2], S[j + 3]);
-                }
-                if (have_next) {
-#pragma unroll
-                    for (int j = 0; j < 32; j += 4) {
-                        const float4 gl = *reinterpret_cast<const float4*>(&stg.GL[32 * h + j]);
-                        S[j] *= gl.x, S[j + 1] *= gl.y, S[j + 2] *= gl.z, S[j + 3] *= gl.w;
-                    }
-                    tmem_st16(to + 32 * h, S);
-                    tmem_st16(to + 32 * h + 16, S + 16);
-                }
-            }
-            if (have_next) {
-                float z[16];
-#pragma unroll
-                for (int j = 0; j < 16; j++) z[j] = 0.f;
-                tmem_st16(to + N, z);
-                tmem_st16(to + N + L, z);
             }
             tmem_wait_st();
-        };
-
-        bool ok = true;
-        if (nchunks > 0) {
-            ok = !group_sync_or(BAR_STATE, !mbar_wait(&sm.full[0], 0, &sm.abort, &g_device_error_tc));
-            advance(0, ok, true);  // s0 -> buffer 0; S0 diag(GL) and zeros -> buffer 1
-        } else {
-            advance(0, false, true);
-        }
-        for (int c = 0; ok && c < nchunks; c++) {
+            proxy_fence();
             tc_fence_before();
-            group_sync(BAR_STATE);
+            if (group_sync_or(BAR_STATE, bad2)) break;
             tc_fence_after();
             if (tid == 0) {
-                const Stage& stg = sm.st[c % NSTAGE];
-                const uint32_t id = idesc_tf32(64, NS);
-                const uint32_t aV = smem_u32(stg.AV), bV = smem_u32(stg.BV), bS = smem_u32(stg.BS);
-                const uint32_t d = tmem + buf(c + 1), a_ = tmem + buf(c);
+                const uint32_t i2 = idesc_tf32(64, 64);
+                const uint32_t aU = smem_u32(sm.UTA), aV = smem_u32(stg.VT), bK = smem_u32(stg.BK);
 #pragma unroll
                 for (int ks = 0; ks < 2; ks++)
-                    umma(d, umma_desc(aV + 2 * ks * KLBO, SBO_K16), umma_desc(bV + 2 * ks * KLBO, SBO_K16), id, 1);
+                    umma(tmem, umma_desc(aV + 2 * ks * KLBO, SBO_K16), umma_desc(bK + (4 + 2 * ks) * KLBO, SBO_K32), i2, 1);
 #pragma unroll
-                for (int ks = 0; ks < 8; ks++)
-                    umma_ts(d, a_ + 8 * ks, umma_desc(bS + 2 * ks * KLBO, SBO_K64), id, 1);
-                umma_commit(&sm.mma);
+                for (int ks = 0; ks < 2; ks++)
+                    umma(tmem, umma_desc(aU + 2 * ks * KLBO, SBO_K16), umma_desc(bK + 2 * ks * KLBO, SBO_K32), i2, 1);
+                umma_commit(&sm.mma2);
             }
-            if (c >= 1) output(c - 1);
-            const bool more = c + 1 < nchunks;
-            bool bad = more && !mbar_wait(&sm.full[(c + 1) % NSTAGE], ((c + 1) / NSTAGE) & 1, &sm.abort, &g_device_error_tc);
-            bad |= !mbar_wait(&sm.mma, c & 1, &sm.abort, &g_device_error_tc);
-            tc_fence_after();
-            advance(c + 1, more, false);
-            tc_fence_before();
-            mbar_arrive(&sm.empty[c % NSTAGE]);
-            ok = !group_sync_or(BAR_STATE, bad);  // uniform decision for the whole group
-        }
-        if (ok && nchunks > 0) output(nchunks - 1);
-        if (sT && ok) {
-            const uint32_t fin = tl + buf(nchunks);
-#pragma unroll
-            for (int h = 0; h < 2; h++) {
-                float S[32];
-                tmem_ld16(fin + 32 * h, S);
-                tmem_ld16(fin + 32 * h + 16, S + 16);
-                tmem_wait_ld();
-                if (live) {
-                    float* p = sT + ((size_t)bh * N + row) * N + 32 * h;
-#pragma unroll
-                    for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(p + j) = make_float4(S[j], S[j + 1], S[j + 2], S[j + 3]);
+            {  // y rows of this chunk: 8 consecutive values per thread, one 16-byte store
+                const int rr = tid >> 3, c8 = (tid & 7) * 8, t = c * L + rr;
+                if (t < T_) {
+                    const float4 f0 = *reinterpret_cast<const float4*>(&sm.Yb[rr][c8]);
+                    const float4 f1 = *reinterpret_cast<const float4*>(&sm.Yb[rr][c8 + 4]);
+                    uint4 pk;
+                    T* pe = reinterpret_cast<T*>(&pk);
+                    pe[0] = from_f32<T>(f0.x), pe[1] = from_f32<T>(f0.y), pe[2] = from_f32<T>(f0.z), pe[3] = from_f32<T>(f0.w);
+                    pe[4] = from_f32<T>(f1.x), pe[5] = from_f32<T>(f1.y), pe[6] = from_f32<T>(f1.z), pe[7] = from_f32<T>(f1.w);
+                    *reinterpret_cast<uint4*>(y + base + (size_t)t * tstride + c8) = pk;
                 }
+            }
+            const bool bad3 = !mbar_wait(&sm.mma2, c & 1, &sm.abort, &g_device_error_tc);
+            tc_fence_after();
+            if (ckpt) {
+                const int tend = (c + 1) * L;
+                if (tend <= T_ && tend % ckpt_len == 0) {
+#pragma unroll
+                    for (int j = 0; j < N; j += 16) tmem_ld16(tD2 + j, &S[j]);
+                    tmem_wait_ld();
+                    if (live) {
+                        float* p = ckpt + (((size_t)bh * nck + tend / ckpt_len - 1) * N + row) * N;
+#pragma unroll
+                        for (int j = 0; j < N; j += 4) *reinterpret_cast<float4*>(p + j) = make_float4(S[j], S[j + 1], S[j + 2], S[j + 3]);
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&sm.empty[s]);
+            if (group_sync_or(BAR_STATE, bad3)) break;  // uniform decision for the whole group
+        }
+        if (sT && !group_sync_or(BAR_STATE, sm.abort != 0)) {
+            tc_fence_after();
+            float S[N];
+#pragma unroll
+            for (int j = 0; j < N; j += 16) tmem_ld16(tD2 + j, &S[j]);
+            tmem_wait_ld();
+            if (live) {
+                float* p = sT + ((size_t)bh * N + row) * N;
+#pragma unroll
+                for (int j = 0; j < N; j += 4) *reinterpret_cast<float4*>(p + j) = make_float4(S[j], S[j + 1], S[j + 2], S[j + 3]);
             }
         }
     }
@@ -632,7 +556,7 @@ __global__ void __launch_bounds__(NT, 1)
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(TMEM_COLS) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 128;" ::"r"(tmem) : "memory");
     }
 }
 

@@ -131,10 +131,12 @@ def cuda_timed(fn, steps, stream=None):
     """Run fn() `steps` times between CUDA events on the current stream; ms per step."""
     s = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("timed")  # lets a profiler select the timed launches
     e0.record(s)
     for _ in range(steps):
         fn()
     e1.record(s)
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     return e0.elapsed_time(e1) / steps
 
@@ -476,6 +478,9 @@ def main():
     ap.add_argument("--ep", action="store_true", help="moe workload: expert-parallel over the ranks")
     ap.add_argument("--decode-seqs", type=int, default=256)
     ap.add_argument("--decode-prompt", type=int, default=512)
+    ap.add_argument("--wkv-impl", type=int, default=0, choices=[0, 1, 2, 3],
+                    help="WKV-7 forward kernel: 0 auto (tcgen05 for fp16/bf16), 1 step-sequential, "
+                         "2 mma.sync chunked, 3 tcgen05 chunked")
     ap.add_argument("--batch", type=int, default=8)
     ap.add_argument("--seq", type=int, default=4096)
     ap.add_argument("--cpu-sample-tokens", type=int, default=128)
@@ -491,6 +496,10 @@ def main():
     ws, rank, local = dist_setup()
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    if args.wkv_impl:
+        from rwkv_mlx_b200 import _native
+
+        _native.check(_native.lib().rwkv_set_wkv_impl(args.wkv_impl), "rwkv_set_wkv_impl")
     if args.workload == "prefill":
         line = run_prefill(args, ws, rank, dev)
     elif args.workload == "moe":

@@ -91,6 +91,21 @@ int rwkv_wkv7_backward(const void* r, const void* w, const void* k, const void* 
                        void* dv, void* da, void* db, float* ds0, int B, int T, int H,
                        int N, int dtype, int w_dtype, int ckpt_len, void* stream);
 
+/* WKV-7 backward, chunked (same contract as rwkv_wkv7_backward, replacing the same
+ * reference code, wkv7_metal.py:282-319 and :102-214), with a caller-provided
+ * workspace of rwkv_wkv7_backward_workspace_size(B, T, H, N) bytes (fp32 state
+ * gradients at every 16-step chunk boundary).  Two launches: the adjoint of the
+ * chunk state chain per (b, h), then every chunk's input gradients in parallel.
+ * Needs ckpt_len == 16 (a snapshot at every chunk boundary); other ckpt_len values,
+ * or rwkv_set_wkv_impl(1), run the step-sequential backward of rwkv_wkv7_backward.  */
+size_t rwkv_wkv7_backward_workspace_size(int B, int T, int H, int N);
+int rwkv_wkv7_backward_ws(const void* r, const void* w, const void* k, const void* v,
+                          const void* a, const void* b, const void* dy, const float* s0,
+                          const float* dsT, const float* ckpt, void* dr, void* dw, void* dk,
+                          void* dv, void* da, void* db, float* ds0, int B, int T, int H,
+                          int N, int dtype, int w_dtype, int ckpt_len, void* workspace,
+                          size_t workspace_bytes, void* stream);
+
 /* One RNN-mode step for Bs independent sequences, state updated in place.
  * Replaces the state update of _time_mixing_rnn (rwkv_mlx/model.py:475-483),
  * batched over sequences (the reference runs one sequence per call).

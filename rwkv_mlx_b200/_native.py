@@ -39,6 +39,8 @@ SIGNATURES = {
     "rwkv_set_wkv_impl": (_I, [_I]),
     "rwkv_wkv7_forward": (_I, [_P] * 11 + [_I] * 7 + [_P]),
     "rwkv_wkv7_backward": (_I, [_P] * 17 + [_I] * 7 + [_P]),
+    "rwkv_wkv7_backward_workspace_size": (_SZ, [_I] * 4),
+    "rwkv_wkv7_backward_ws": (_I, [_P] * 17 + [_I] * 7 + [_P, _SZ, _P]),
     "rwkv_wkv7_step": (_I, [_P] * 8 + [_I] * 6 + [_P]),
     "rwkv_moe_router_workspace_size": (_SZ, [_I, _I]),
     "rwkv_moe_router": (_I, [_P] * 9 + [_SZ] + [_I] * 5 + [_P]),
@@ -97,7 +99,7 @@ def lib() -> ctypes.CDLL:
 # Kernel launches issued through this binding (per C-ABI entry point: the number of
 # kernels that entry point enqueues).  bench.py reads it to report gpu_launches.
 KERNELS_PER_CALL = {
-    "rwkv_wkv7_forward": 1, "rwkv_wkv7_backward": 1, "rwkv_wkv7_step": 1,
+    "rwkv_wkv7_forward": 1, "rwkv_wkv7_backward": 1, "rwkv_wkv7_backward_ws": 2, "rwkv_wkv7_step": 1,
     "rwkv_moe_router": 2, "rwkv_moe_router_noalloc": 2, "rwkv_moe_permute": 3, "rwkv_moe_lora_down": 1,
     "rwkv_moe_lora_combine": 1, "rwkv_moe_lora_apply": 1, "rwkv_moe_ortho_loss": 1, "rwkv_moe_gather_rows": 1,
     "rwkv_moe_lora_up": 1, "rwkv_moe_combine_rows": 1, "rwkv_lerp": 1, "rwkv_tmix_mid": 1,

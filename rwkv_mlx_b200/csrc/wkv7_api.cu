@@ -64,6 +64,35 @@ extern "C" int rwkv_wkv7_backward(const void* r, const void* w, const void* k, c
     return wkv7_bwd_seq(p, (cudaStream_t)stream);
 }
 
+extern "C" size_t rwkv_wkv7_backward_workspace_size(int B, int T, int H, int N) {
+    if (check_dims(B, T, H, N, RWKV_F32)) return 0;
+    return wkv7_bwd_chunk_ws_bytes(B, T, H);
+}
+
+extern "C" int rwkv_wkv7_backward_ws(const void* r, const void* w, const void* k, const void* v,
+                                     const void* a, const void* b, const void* dy, const float* s0,
+                                     const float* dsT, const float* ckpt, void* dr, void* dw,
+                                     void* dk, void* dv, void* da, void* db, float* ds0, int B,
+                                     int T, int H, int N, int dtype, int w_dtype, int ckpt_len,
+                                     void* workspace, size_t workspace_bytes, void* stream) {
+    int rc = check_dims(B, T, H, N, dtype);
+    if (rc) return rc;
+    if (!r || !w || !k || !v || !a || !b || !dy || !dr || !dw || !dk || !dv || !da || !db)
+        return RWKV_ERR_ARG;
+    if (ckpt_len < 16 || ckpt_len % 16) return RWKV_ERR_ARG;
+    if (T > ckpt_len && !ckpt) return RWKV_ERR_ARG;
+    WkvBwdArgs p{r, w, k, v, a, b, dy, s0, dsT, ckpt, dr, dw, dk, dv, da, db, ds0,
+                 B, T, H, dtype, w_dtype, ckpt_len};
+    // the chunked backward needs a snapshot at every 16-step chunk boundary and reads
+    // its inputs as 16-byte vectors
+    const void* ins[7] = {r, w, k, v, a, b, dy};
+    const bool al = inputs_aligned16(ins, 7) && aligned(ckpt, 16) && aligned(s0, 16);
+    if (g_wkv_impl == 1 || ckpt_len != 16 || !al) return wkv7_bwd_seq(p, (cudaStream_t)stream);
+    if (!workspace || workspace_bytes < wkv7_bwd_chunk_ws_bytes(B, T, H)) return RWKV_ERR_WORKSPACE;
+    if (!aligned(workspace, 16)) return RWKV_ERR_ALIGN;
+    return wkv7_bwd_chunked(p, (float*)workspace, (cudaStream_t)stream);
+}
+
 extern "C" int rwkv_wkv7_step(float* S, const void* r, const void* w, const void* k,
                               const void* v, const void* a, const void* b, void* y, int Bs, int H,
                               int N, int dtype, int w_dtype, int w_mode, void* stream) {

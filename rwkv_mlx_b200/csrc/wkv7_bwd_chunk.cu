@@ -1,0 +1,563 @@
+// WKV-7 backward, chunked (L = 16 steps per chunk), exact, in two launches.
+//
+// Per chunk, with X = S^T (keys x values) at the chunk start, natural-log cumulative
+// decays c_t, and the decayed factors At = a e^{c_{t-1}}, Rt = r e^{c_t},
+// Bh = b e^{-c_t}, Kh = k e^{-c_t}, Bb = b e^{c_L - c_t}, Kb = k e^{c_L - c_t},
+// GL = e^{c_L}; Mab/Mak strictly and Mrb/Mrk inclusively lower-triangular parts of
+// At Bh^T, At Kh^T, Rt Bh^T, Rt Kh^T:
+//
+//   U   = At X + Mab U + Mak V          (U[t] = S_{t-1} a_t, one row per step)
+//   Y   = Rt X + Mrb U + Mrk V
+//   X_L = GL o X + Bb^T U + Kb^T V
+//
+// Pass 1 (one CTA per (b, h), chunks in reverse) runs the adjoint of the state chain:
+// with Inv = (I - Mab)^-1, Wu = Inv At, Wy = Rt + Mrb Wu,
+//   dX_0 = GL o dX_L + Wu^T (Bb dX_L) + Wy^T dY,
+// writing dX_L of every chunk to the workspace (and dX_0 of chunk 0 as ds0).
+// Pass 2 (one CTA per (b, h, chunk), all chunks at once) forms every input gradient
+// of its chunk from X (the forward's snapshot), dX_L and the inputs:
+//   Lambda = Inv^T (Mrb^T dY + Bb dX_L)                 (adjoint of the solve for U)
+//   dAt = Lambda X^T + dMab Bh + dMak Kh,   dMab = Lambda U^T, dMak = Lambda V^T (strict)
+//   dRt = dY X^T + dMrb Bh + dMrk Kh,       dMrb = dY U^T,     dMrk = dY V^T     (incl.)
+//   dBh = dMab^T At + dMrb^T Rt,  dKh = dMak^T At + dMrk^T Rt
+//   dBb = U dX_L^T,  dKb = V dX_L^T,  dGL = rowsum(dX_L o X)
+//   dV  = Mak^T Lambda + Mrk^T dY + Kb dX_L
+// then the factor chain rule back to r, k, a, b and the reverse cumulative sum of
+// the decay gradients back to w.  All products run on mma.sync with operands split
+// into high and low TF32 parts (three products, fp32-accurate).  Chunks whose
+// cumulative decay falls below e^-80 form the Mab..Mrk products and their gradients
+// element-wise from exponent differences (the factored forms would overflow).
+#include "chunk_common.cuh"
+#include "common.cuh"
+#include "wkv7.cuh"
+
+namespace rwkv {
+namespace bwdc {
+using ck::L;
+using ck::N;
+using ck::mma8;
+using ck::tf32;
+constexpr int NT = 256;
+constexpr int LDC = 68;   // row pitch (floats) of the 16x64 / 64x64 arrays
+constexpr int LM = 20;    // row pitch of the 16x16 arrays
+constexpr float EXT_C = -80.f;
+
+__device__ __forceinline__ void split(float x, uint32_t& hi, uint32_t& lo) {
+    hi = tf32(x);
+    lo = tf32(x - __uint_as_float(hi));
+}
+
+// d (one 16x8 tile) += A(16 x K) B(K x 8); accessors take tile-local indices
+template <typename FA, typename FB>
+__device__ __forceinline__ void tile_mm(float (&d)[4], const FA& A, const FB& B, int K) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, tg = lane & 3;
+    for (int k0 = 0; k0 < K; k0 += 8) {
+        uint32_t ah[4], al[4], bh[2], bl[2];
+        split(A(g, k0 + tg), ah[0], al[0]);
+        split(A(g + 8, k0 + tg), ah[1], al[1]);
+        split(A(g, k0 + tg + 4), ah[2], al[2]);
+        split(A(g + 8, k0 + tg + 4), ah[3], al[3]);
+        split(B(k0 + tg, g), bh[0], bl[0]);
+        split(B(k0 + tg + 4, g), bh[1], bl[1]);
+        mma8(d, al[0], al[1], al[2], al[3], bh[0], bh[1]);
+        mma8(d, ah[0], ah[1], ah[2], ah[3], bl[0], bl[1]);
+        mma8(d, ah[0], ah[1], ah[2], ah[3], bh[0], bh[1]);
+    }
+}
+// C (M x Nn) = A (M x K) B (K x Nn) over the block's warps; out(m, n, v) once per element.
+// The element -> thread mapping depends only on (M, Nn), so successive calls with the
+// same shape may accumulate into the same elements without a barrier.
+template <typename FA, typename FB, typename FO>
+__device__ __forceinline__ void block_mm(int M, int Nn, int K, const FA& A, const FB& B, const FO& out) {
+    const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tg = lane & 3;
+    const int ntl = Nn / 8, tiles = (M / 16) * ntl;
+    for (int tile = warp; tile < tiles; tile += nw) {
+        const int m0 = (tile / ntl) * 16, n0 = (tile % ntl) * 8;
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
+        tile_mm(d, [&](int m, int k) { return A(m0 + m, k); }, [&](int k, int n) { return B(k, n0 + n); }, K);
+        out(m0 + g, n0 + 2 * tg, d[0]);
+        out(m0 + g, n0 + 2 * tg + 1, d[1]);
+        out(m0 + g + 8, n0 + 2 * tg, d[2]);
+        out(m0 + g + 8, n0 + 2 * tg + 1, d[3]);
+    }
+}
+
+// Sum of products over K segments, each with its own accessors: (A_1 B_1 + A_2 B_2 + ...)
+template <typename FA, typename FB>
+struct Seg {
+    FA A;
+    FB B;
+    int K;
+};
+template <typename FA, typename FB>
+__device__ __forceinline__ Seg<FA, FB> seg(const FA& A, const FB& B, int K) {
+    return Seg<FA, FB>{A, B, K};
+}
+template <typename FO, typename... S>
+__device__ __forceinline__ void block_mm_s(int M, int Nn, const FO& out, const S&... segs) {
+    const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tg = lane & 3;
+    const int ntl = Nn / 8, tiles = (M / 16) * ntl;
+    for (int tile = warp; tile < tiles; tile += nw) {
+        const int m0 = (tile / ntl) * 16, n0 = (tile % ntl) * 8;
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
+        (tile_mm(d, [&](int m, int k) { return segs.A(m0 + m, k); }, [&](int k, int n) { return segs.B(k, n0 + n); },
+                 segs.K),
+         ...);
+        out(m0 + g, n0 + 2 * tg, d[0]);
+        out(m0 + g, n0 + 2 * tg + 1, d[1]);
+        out(m0 + g + 8, n0 + 2 * tg, d[2]);
+        out(m0 + g + 8, n0 + 2 * tg + 1, d[3]);
+    }
+}
+
+// nblk independent 16 x Nn products (block b: rows of A(b, m, k), B(b, k, n)), tiles
+// spread over the block's warps; out(b, m, n, v) once per element.
+template <typename FA, typename FB, typename FO>
+__device__ __forceinline__ void block_mm_b(int nblk, int Nn, int K, const FA& A, const FB& B, const FO& out) {
+    const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tg = lane & 3;
+    const int ntl = Nn / 8, tiles = nblk * ntl;
+    for (int tile = warp; tile < tiles; tile += nw) {
+        const int bb = tile / ntl, n0 = (tile % ntl) * 8;
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
+        tile_mm(d, [&](int m, int k) { return A(bb, m, k); }, [&](int k, int n) { return B(bb, k, n0 + n); }, K);
+        out(bb, g, n0 + 2 * tg, d[0]);
+        out(bb, g, n0 + 2 * tg + 1, d[1]);
+        out(bb, g + 8, n0 + 2 * tg, d[2]);
+        out(bb, g + 8, n0 + 2 * tg + 1, d[3]);
+    }
+}
+
+enum { IR = 0, IL, IK, IV, IA, IB, IDY, NIN };  // IL holds l = -exp(w), the natural-log decay
+enum { FAT = 0, FRT, FBH, FKH, FBB, FKB, NF };
+
+// Shared per-chunk front end: inputs -> cumulative decays -> factors -> intra-chunk
+// matrices -> Inv.  `which` selects the matrices needed (bit m for Mab, Mak, Mrb, Mrk).
+struct Front {
+    float in[NIN][L][LDC];
+    float c[L][LDC];
+    float f[NF][L][LDC];
+    float GL[N];
+    float M[4][L][LM];
+    float Inv[L][LM];
+};
+
+// One chunk's inputs: every thread issues at most one 16-byte load per array (all of
+// them before any is used), then converts to fp32 into `in`.  The loads and the
+// stores are split so that a caller can overlap the loads with other work.
+template <typename T, typename TW>
+struct ChunkLoad {
+    static constexpr int VT = 16 / sizeof(T), VW = 16 / sizeof(TW);
+    uint4 raw[NIN];
+    __device__ __forceinline__ static int per_row(int arr) { return N / (arr == IL ? VW : VT); }
+    __device__ __forceinline__ void issue(const T* r, const TW* w, const T* k, const T* v, const T* a, const T* b,
+                                          const T* dy, size_t base, size_t tstride, int t0, int nt, unsigned mask) {
+        const int tid = threadIdx.x;
+#pragma unroll
+        for (int arr = 0; arr < NIN; arr++) {
+            raw[arr] = make_uint4(0, 0, 0, 0);
+            const int pr = per_row(arr), row = tid / pr, col = (tid % pr) * (arr == IL ? VW : VT);
+            if (!((mask >> arr) & 1) || tid >= L * pr || row >= nt) continue;
+            const size_t off = base + (size_t)(t0 + row) * tstride + col;
+            const void* src = arr == IR ? (const void*)(r + off) : arr == IL ? (const void*)(w + off)
+                            : arr == IK ? (const void*)(k + off) : arr == IV ? (const void*)(v + off)
+                            : arr == IA ? (const void*)(a + off) : arr == IB ? (const void*)(b + off)
+                            : (const void*)(dy + off);
+            raw[arr] = __ldg(reinterpret_cast<const uint4*>(src));
+        }
+    }
+    __device__ __forceinline__ void store(Front& fr, int nt, unsigned mask) const {
+        const int tid = threadIdx.x;
+#pragma unroll
+        for (int arr = 0; arr < NIN; arr++) {
+            const int pr = per_row(arr), row = tid / pr;
+            if (!((mask >> arr) & 1) || tid >= L * pr) continue;
+            if (arr == IL) {
+                const TW* e = reinterpret_cast<const TW*>(&raw[arr]);
+                const int col = (tid % pr) * VW;
+#pragma unroll
+                for (int i = 0; i < VW; i++) fr.in[IL][row][col + i] = row < nt ? -expf(to_f32(e[i])) : 0.f;
+            } else {
+                const T* e = reinterpret_cast<const T*>(&raw[arr]);
+                const int col = (tid % pr) * VT;
+#pragma unroll
+                for (int i = 0; i < VT; i++) fr.in[arr][row][col + i] = to_f32(e[i]);
+            }
+        }
+    }
+};
+
+__device__ __forceinline__ void cp16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+                 : "memory");
+}
+// 64 x 64 fp32 matrix (row-major in global memory) into smem rows of pitch LDC
+__device__ __forceinline__ void cp_mat(float (*dst)[LDC], const float* src) {
+    for (int e = threadIdx.x; e < N * N / 4; e += NT) cp16(&dst[e / 16][(e % 16) * 4], src + 4 * e);
+}
+
+// returns the CTA-uniform "extreme decay" flag
+__device__ int front_factors(Front& fr) {
+    const int tid = threadIdx.x;
+    int ext = 0;
+    if (tid < N) {
+        float s = 0.f;
+#pragma unroll
+        for (int t = 0; t < L; t++) s += fr.in[IL][t][tid], fr.c[t][tid] = s;
+        ext = s < EXT_C;
+        fr.GL[tid] = expf(s);
+    }
+    ext = __syncthreads_or(ext);
+    for (int e = tid; e < L * N; e += NT) {
+        const int t = e / N, j = e % N;
+        const float cp = t ? fr.c[t - 1][j] : 0.f, ct = fr.c[t][j], cl = fr.c[L - 1][j];
+        fr.f[FAT][t][j] = fr.in[IA][t][j] * expf(cp);
+        fr.f[FRT][t][j] = fr.in[IR][t][j] * expf(ct);
+        const float eb = expf(cl - ct);
+        fr.f[FBB][t][j] = fr.in[IB][t][j] * eb;
+        fr.f[FKB][t][j] = fr.in[IK][t][j] * eb;
+        if (!ext) {
+            const float ei = expf(-ct);
+            fr.f[FBH][t][j] = fr.in[IB][t][j] * ei;
+            fr.f[FKH][t][j] = fr.in[IK][t][j] * ei;
+        }
+    }
+    __syncthreads();
+    return ext;
+}
+
+// Mab, Mak (strict) and Mrb, Mrk (inclusive) for the matrices selected in `which`
+__device__ void front_matrices(Front& fr, int ext, unsigned which) {
+    if (!ext) {
+        int ms[4], nb = 0;
+        for (int m = 0; m < 4; m++)
+            if ((which >> m) & 1) ms[nb++] = m;
+        block_mm_b(nb, L, N,
+                   [&](int bb, int t, int j) { return (&fr.f[ms[bb] < 2 ? FAT : FRT][0][0])[t * LDC + j]; },
+                   [&](int bb, int j, int s) { return (&fr.f[(ms[bb] & 1) ? FKH : FBH][0][0])[s * LDC + j]; },
+                   [&](int bb, int t, int s, float val) {
+                       const int m = ms[bb];
+                       fr.M[m][t][s] = (m < 2 ? s < t : s <= t) ? val : 0.f;
+                   });
+    }
+    for (int m = 0; m < 4; m++) {
+        if (!((which >> m) & 1)) continue;
+        const bool strict = m < 2;
+        if (ext) {
+            for (int e = threadIdx.x; e < L * L; e += NT) {
+                const int t = e / L, s = e % L;
+                float val = 0.f;
+                if (strict ? s < t : s <= t) {
+                    const float* xs = m < 2 ? fr.in[IA][t] : fr.in[IR][t];
+                    const float* ys = (m & 1) ? fr.in[IK][s] : fr.in[IB][s];
+                    const float* cx = m < 2 ? (t ? fr.c[t - 1] : nullptr) : fr.c[t];
+                    for (int j = 0; j < N; j++) val = fmaf(xs[j] * ys[j], expf((cx ? cx[j] : 0.f) - fr.c[s][j]), val);
+                }
+                fr.M[m][t][s] = val;
+            }
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x < L) {  // Inv = (I - Mab)^-1, one column per thread
+        const int cc = threadIdx.x;
+        float x[L];
+#pragma unroll
+        for (int t = 0; t < L; t++) x[t] = t == cc ? 1.f : 0.f;
+#pragma unroll
+        for (int s = 0; s < L - 1; s++) {
+#pragma unroll
+            for (int t = s + 1; t < L; t++) x[t] = fmaf(fr.M[0][t][s], x[s], x[t]);
+        }
+#pragma unroll
+        for (int t = 0; t < L; t++) fr.Inv[t][cc] = x[t];
+    }
+    __syncthreads();
+}
+
+// ---------------------------------------------------------------------------
+// Pass 1: adjoint of the state chain.
+struct P1Smem {
+    Front fr;
+    float WU[L][LDC], WY[L][LDC], DU[L][LDC];
+    float D[N][LDC];  // dX_L [key][value]
+};
+
+template <typename T, typename TW>
+__global__ void __launch_bounds__(NT, 1)
+    wkv7_bwd_chain_kernel(const T* __restrict__ r, const TW* __restrict__ w, const T* __restrict__ a,
+                          const T* __restrict__ b, const T* __restrict__ dy, const float* __restrict__ dsT,
+                          float* __restrict__ dxl, float* __restrict__ ds0, int T_, int H) {
+    extern __shared__ __align__(16) unsigned char smem_p1[];
+    P1Smem& sm = *reinterpret_cast<P1Smem*>(smem_p1);
+    Front& fr = sm.fr;
+    const int tid = threadIdx.x, bh = blockIdx.x, bi = bh / H, hi = bh % H;
+    const size_t tstride = (size_t)H * N, base = ((size_t)bi * T_ * H + hi) * N;
+    const int nch = (T_ + L - 1) / L;
+    for (int e = tid; e < N * N; e += NT) {  // D = dsT^T
+        const int vv = e / N, j = e % N;
+        sm.D[j][vv] = dsT ? dsT[(size_t)bh * N * N + e] : 0.f;
+    }
+    constexpr unsigned MASK1 = (1u << IR) | (1u << IL) | (1u << IA) | (1u << IB) | (1u << IDY);
+    ChunkLoad<T, TW> ld;
+    ld.issue(r, w, nullptr, nullptr, a, b, dy, base, tstride, (nch - 1) * L, min(L, T_ - (nch - 1) * L), MASK1);
+    for (int c = nch - 1; c >= 0; c--) {
+        __syncthreads();
+        ld.store(fr, min(L, T_ - c * L), MASK1);
+        if (c > 0) ld.issue(r, w, nullptr, nullptr, a, b, dy, base, tstride, (c - 1) * L, L, MASK1);  // next chunk
+        __syncthreads();
+        const int ext = front_factors(fr);
+        front_matrices(fr, ext, 0b0101);  // Mab, Mrb
+        block_mm(L, N, L, [&](int t, int s) { return fr.Inv[t][s]; }, [&](int s, int j) { return fr.f[FAT][s][j]; },
+                 [&](int t, int j, float val) { sm.WU[t][j] = val; });
+        __syncthreads();
+        block_mm(L, N, L, [&](int t, int s) { return fr.M[2][t][s]; }, [&](int s, int j) { return sm.WU[s][j]; },
+                 [&](int t, int j, float val) { sm.WY[t][j] = fr.f[FRT][t][j] + val; });
+        block_mm(L, N, N, [&](int t, int j) { return fr.f[FBB][t][j]; }, [&](int j, int vv) { return sm.D[j][vv]; },
+                 [&](int t, int vv, float val) { sm.DU[t][vv] = val; });
+        float* out = dxl + ((size_t)bh * nch + c) * N * N;
+        for (int e = tid; e < N * N / 4; e += NT)
+            *reinterpret_cast<float4*>(out + 4 * e) = *reinterpret_cast<const float4*>(&sm.D[e / 16][(e % 16) * 4]);
+        __syncthreads();
+        block_mm_s(N, N, [&](int j, int vv, float val) { sm.D[j][vv] = fmaf(fr.GL[j], sm.D[j][vv], val); },
+                   seg([&](int j, int t) { return sm.WU[t][j]; }, [&](int t, int vv) { return sm.DU[t][vv]; }, L),
+                   seg([&](int j, int t) { return sm.WY[t][j]; }, [&](int t, int vv) { return fr.in[IDY][t][vv]; }, L));
+    }
+    __syncthreads();
+    if (ds0) {
+        for (int e = tid; e < N * N; e += NT) ds0[(size_t)bh * N * N + e] = sm.D[e % N][e / N];
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Pass 2: every input gradient of one chunk.
+struct P2Smem {
+    Front fr;
+    float Sv[N][LDC];  // state at the chunk start, [value][key] (X = Sv^T)
+    float D[N][LDC];  // dX_L, [key][value]
+    float U[L][LDC], G[L][LDC], Lam[L][LDC];
+    float dM[4][L][LM];
+    float dA[L][LDC], dR[L][LDC], dB[L][LDC], dK[L][LDC], dV[L][LDC];
+    float dC[L][LDC];   // d/dc_t from terms at index t
+    float dCp[L][LDC];  // d/dc_{t-1} from terms at index t
+    float Q[L][LDC];    // d/dc_L from terms at index t
+    float dGL[N];
+};
+
+template <typename T, typename TW>
+__global__ void __launch_bounds__(NT, 1)
+    wkv7_bwd_chunk_kernel(const T* __restrict__ r, const TW* __restrict__ w, const T* __restrict__ k,
+                          const T* __restrict__ v, const T* __restrict__ a, const T* __restrict__ b,
+                          const T* __restrict__ dy, const float* __restrict__ s0, const float* __restrict__ ckpt,
+                          const float* __restrict__ dxl, T* __restrict__ dr, T* __restrict__ dw, T* __restrict__ dk,
+                          T* __restrict__ dv, T* __restrict__ da, T* __restrict__ db, int T_, int H) {
+    extern __shared__ __align__(16) unsigned char smem_p2[];
+    P2Smem& sm = *reinterpret_cast<P2Smem*>(smem_p2);
+    Front& fr = sm.fr;
+    const int tid = threadIdx.x, c = blockIdx.x, bh = blockIdx.y, bi = bh / H, hi = bh % H;
+    const size_t tstride = (size_t)H * N, base = ((size_t)bi * T_ * H + hi) * N;
+    const int nch = gridDim.x, t0 = c * L, nt = min(L, T_ - t0);
+
+    {
+        const float* S = c == 0 ? (s0 ? s0 + (size_t)bh * N * N : nullptr) : ckpt + ((size_t)bh * (T_ / L) + c - 1) * N * N;
+        if (S) {
+            cp_mat(sm.Sv, S);
+        } else {
+            for (int e = tid; e < N * LDC; e += NT) (&sm.Sv[0][0])[e] = 0.f;
+        }
+        cp_mat(sm.D, dxl + ((size_t)bh * nch + c) * N * N);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        ChunkLoad<T, TW> ld;
+        ld.issue(r, w, k, v, a, b, dy, base, tstride, t0, nt, 0x7f);
+        ld.store(fr, nt, 0x7f);
+        for (int e = tid; e < L * LDC; e += NT) {
+            (&sm.dA[0][0])[e] = 0.f, (&sm.dR[0][0])[e] = 0.f, (&sm.dB[0][0])[e] = 0.f, (&sm.dK[0][0])[e] = 0.f;
+            (&sm.dC[0][0])[e] = 0.f, (&sm.dCp[0][0])[e] = 0.f, (&sm.Q[0][0])[e] = 0.f;
+        }
+        asm volatile("cp.async.wait_all;" ::: "memory");
+    }
+    __syncthreads();
+    const int ext = front_factors(fr);
+    front_matrices(fr, ext, 0b1111);
+    const auto& F = fr.f;
+    const auto& IN = fr.in;
+
+    // U = Inv (At X + Mak V)
+    block_mm_s(L, N, [&](int t, int vv, float val) { sm.G[t][vv] = val; },
+               seg([&](int t, int j) { return F[FAT][t][j]; }, [&](int j, int vv) { return sm.Sv[vv][j]; }, N),
+               seg([&](int t, int s) { return fr.M[1][t][s]; }, [&](int s, int vv) { return IN[IV][s][vv]; }, L));
+    __syncthreads();
+    block_mm(L, N, L, [&](int t, int s) { return fr.Inv[t][s]; }, [&](int s, int vv) { return sm.G[s][vv]; },
+             [&](int t, int vv, float val) { sm.U[t][vv] = val; });
+    // external gradient of U: Mrb^T dY + Bb dX_L
+    block_mm_s(L, N, [&](int t, int vv, float val) { sm.Lam[t][vv] = val; },
+               seg([&](int t, int s) { return fr.M[2][s][t]; }, [&](int s, int vv) { return IN[IDY][s][vv]; }, L),
+               seg([&](int t, int j) { return F[FBB][t][j]; }, [&](int j, int vv) { return sm.D[j][vv]; }, N));
+    __syncthreads();
+    // Lambda = Inv^T (...)  (into G, free after U)
+    block_mm(L, N, L, [&](int t, int s) { return fr.Inv[s][t]; }, [&](int s, int vv) { return sm.Lam[s][vv]; },
+             [&](int t, int vv, float val) { sm.G[t][vv] = val; });
+    __syncthreads();
+    const auto& Lam = sm.G;
+    // gradients of the intra-chunk matrices (4 stacked 16x16 products)
+    block_mm_b(4, L, N,
+               [&](int bb, int t, int vv) { return (bb < 2 ? &Lam[0][0] : &IN[IDY][0][0])[t * LDC + vv]; },
+               [&](int bb, int vv, int s) { return ((bb & 1) ? &IN[IV][0][0] : &sm.U[0][0])[s * LDC + vv]; },
+               [&](int bb, int t, int s, float val) { sm.dM[bb][t][s] = (bb < 2 ? s < t : s <= t) ? val : 0.f; });
+    // dV = Mak^T Lambda + Mrk^T dY + Kb dX_L
+    block_mm_s(L, N, [&](int s, int vv, float val) { sm.dV[s][vv] = val; },
+               seg([&](int s, int t) { return fr.M[1][t][s]; }, [&](int t, int vv) { return Lam[t][vv]; }, L),
+               seg([&](int s, int t) { return fr.M[3][t][s]; }, [&](int t, int vv) { return IN[IDY][t][vv]; }, L),
+               seg([&](int s, int j) { return F[FKB][s][j]; }, [&](int j, int vv) { return sm.D[j][vv]; }, N));
+    if (tid < N) {
+        float sdg = 0.f;
+        for (int vv = 0; vv < N; vv++) sdg = fmaf(sm.D[tid][vv], sm.Sv[vv][tid], sdg);
+        sm.dGL[tid] = sdg * fr.GL[tid];
+    }
+    __syncthreads();
+    // Factor gradients.  Every call below is 16 x 64 with the same element -> thread
+    // mapping, so each thread accumulates only its own elements: no barriers needed.
+    {
+        auto outA = [&](int t, int j, float val) {  // dAt: At = a e^{c_{t-1}}
+            const float cp = t ? fr.c[t - 1][j] : 0.f;
+            sm.dA[t][j] += val * expf(cp);
+            sm.dCp[t][j] += val * F[FAT][t][j];
+        };
+        auto outR = [&](int t, int j, float val) {  // dRt: Rt = r e^{c_t}
+            sm.dR[t][j] += val * expf(fr.c[t][j]);
+            sm.dC[t][j] += val * F[FRT][t][j];
+        };
+        auto sA = seg([&](int t, int vv) { return Lam[t][vv]; }, [&](int vv, int j) { return sm.Sv[vv][j]; }, N);
+        auto sR = seg([&](int t, int vv) { return IN[IDY][t][vv]; }, [&](int vv, int j) { return sm.Sv[vv][j]; }, N);
+        if (!ext) {
+            auto bh = [&](int s, int j) { return F[FBH][s][j]; };
+            auto kh = [&](int s, int j) { return F[FKH][s][j]; };
+            block_mm_s(L, N, outA, sA, seg([&](int t, int s) { return sm.dM[0][t][s]; }, bh, L),
+                       seg([&](int t, int s) { return sm.dM[1][t][s]; }, kh, L));
+            block_mm_s(L, N, outR, sR, seg([&](int t, int s) { return sm.dM[2][t][s]; }, bh, L),
+                       seg([&](int t, int s) { return sm.dM[3][t][s]; }, kh, L));
+        } else {
+            block_mm_s(L, N, outA, sA);
+            block_mm_s(L, N, outR, sR);
+        }
+    }
+    block_mm(L, N, N, [&](int t, int vv) { return sm.U[t][vv]; }, [&](int vv, int j) { return sm.D[j][vv]; },
+             [&](int t, int j, float val) {  // dBb: Bb = b e^{c_L - c_t}
+                 const float q = val * F[FBB][t][j];
+                 sm.dB[t][j] += val * expf(fr.c[L - 1][j] - fr.c[t][j]);
+                 sm.dC[t][j] -= q;
+                 sm.Q[t][j] += q;
+             });
+    block_mm(L, N, N, [&](int t, int vv) { return IN[IV][t][vv]; }, [&](int vv, int j) { return sm.D[j][vv]; },
+             [&](int t, int j, float val) {  // dKb: Kb = k e^{c_L - c_t}
+                 const float q = val * F[FKB][t][j];
+                 sm.dK[t][j] += val * expf(fr.c[L - 1][j] - fr.c[t][j]);
+                 sm.dC[t][j] -= q;
+                 sm.Q[t][j] += q;
+             });
+    if (!ext) {
+        auto at = [&](int t, int j) { return F[FAT][t][j]; };
+        auto rt = [&](int t, int j) { return F[FRT][t][j]; };
+        block_mm_s(
+            L, N,
+            [&](int s, int j, float val) {  // dBh = dMab^T At + dMrb^T Rt
+                sm.dB[s][j] += val * expf(-fr.c[s][j]);
+                sm.dC[s][j] -= val * F[FBH][s][j];
+            },
+            seg([&](int s, int t) { return sm.dM[0][t][s]; }, at, L), seg([&](int s, int t) { return sm.dM[2][t][s]; }, rt, L));
+        block_mm_s(
+            L, N,
+            [&](int s, int j, float val) {  // dKh = dMak^T At + dMrk^T Rt
+                sm.dK[s][j] += val * expf(-fr.c[s][j]);
+                sm.dC[s][j] -= val * F[FKH][s][j];
+            },
+            seg([&](int s, int t) { return sm.dM[1][t][s]; }, at, L), seg([&](int s, int t) { return sm.dM[3][t][s]; }, rt, L));
+    } else {
+        // element-wise: each term x_t y_s e^{c_p - c_s} (p = t-1 for Mab/Mak, t for Mrb/Mrk);
+        // thread (i, j) forms the a/r terms of row i and the b/k terms of column i
+        __syncthreads();
+        for (int e = tid; e < L * N; e += NT) {
+            const int i = e / N, j = e % N;
+            const float ci = fr.c[i][j], cpi = i ? fr.c[i - 1][j] : 0.f;
+            float ga = 0.f, gr = 0.f, gb = 0.f, gk = 0.f;
+            for (int s = 0; s < L; s++) {
+                const float cs = fr.c[s][j];
+                if (s < i) ga = fmaf(sm.dM[0][i][s] * IN[IB][s][j] + sm.dM[1][i][s] * IN[IK][s][j], expf(cpi - cs), ga);
+                if (s <= i) gr = fmaf(sm.dM[2][i][s] * IN[IB][s][j] + sm.dM[3][i][s] * IN[IK][s][j], expf(ci - cs), gr);
+            }
+            for (int t = 0; t < L; t++) {
+                const float ct = fr.c[t][j], cpt = t ? fr.c[t - 1][j] : 0.f;
+                if (t > i) {
+                    const float e1 = expf(cpt - ci) * IN[IA][t][j];
+                    gb = fmaf(sm.dM[0][t][i], e1, gb);
+                    gk = fmaf(sm.dM[1][t][i], e1, gk);
+                }
+                if (t >= i) {
+                    const float e2 = expf(ct - ci) * IN[IR][t][j];
+                    gb = fmaf(sm.dM[2][t][i], e2, gb);
+                    gk = fmaf(sm.dM[3][t][i], e2, gk);
+                }
+            }
+            sm.dA[i][j] += ga;
+            sm.dCp[i][j] += ga * IN[IA][i][j];
+            sm.dR[i][j] += gr;
+            sm.dC[i][j] += gr * IN[IR][i][j] - gb * IN[IB][i][j] - gk * IN[IK][i][j];
+            sm.dB[i][j] += gb;
+            sm.dK[i][j] += gk;
+        }
+    }
+    __syncthreads();
+    // decay: l_t = -exp(w_t); d l_tau = sum_{t >= tau} dc_t + dc_L;  dw = dl * l
+    if (tid < N) {
+        const int j = tid;
+        float dcl = sm.dGL[j];
+        for (int t = 0; t < L; t++) dcl += sm.Q[t][j];
+        float acc = dcl;
+        for (int t = L - 1; t >= 0; t--) {
+            acc += sm.dC[t][j] + (t + 1 < L ? sm.dCp[t + 1][j] : 0.f);
+            sm.Q[t][j] = acc * IN[IL][t][j];  // dw_t
+        }
+    }
+    __syncthreads();
+    for (int e = tid; e < nt * N; e += NT) {
+        const int t = e / N, j = e % N;
+        const size_t off = base + (size_t)(t0 + t) * tstride + j;
+        dr[off] = from_f32<T>(sm.dR[t][j]);
+        dw[off] = from_f32<T>(sm.Q[t][j]);
+        dk[off] = from_f32<T>(sm.dK[t][j]);
+        dv[off] = from_f32<T>(sm.dV[t][j]);
+        da[off] = from_f32<T>(sm.dA[t][j]);
+        db[off] = from_f32<T>(sm.dB[t][j]);
+    }
+}
+
+}  // namespace bwdc
+
+size_t wkv7_bwd_chunk_ws_bytes(int B, int T, int H) {
+    return (size_t)B * H * ((T + bwdc::L - 1) / bwdc::L) * bwdc::N * bwdc::N * sizeof(float);
+}
+
+template <typename T, typename TW>
+static int launch_bwd_chunked(const WkvBwdArgs& p, float* ws, cudaStream_t st) {
+    using namespace bwdc;
+    auto k1 = wkv7_bwd_chain_kernel<T, TW>;
+    auto k2 = wkv7_bwd_chunk_kernel<T, TW>;
+    const int s1 = (int)sizeof(P1Smem), s2 = (int)sizeof(P2Smem);
+    cudaError_t e = cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, s1);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, s2);
+    if (e != cudaSuccess) return set_cuda_error(e);
+    const int nch = (p.T + L - 1) / L;
+    k1<<<p.B * p.H, NT, s1, st>>>((const T*)p.r, (const TW*)p.w, (const T*)p.a, (const T*)p.b, (const T*)p.dy, p.dsT,
+                                  ws, p.ds0, p.T, p.H);
+    int rc = check_launch();
+    if (rc) return rc;
+    k2<<<dim3(nch, p.B * p.H), NT, s2, st>>>((const T*)p.r, (const TW*)p.w, (const T*)p.k, (const T*)p.v,
+                                             (const T*)p.a, (const T*)p.b, (const T*)p.dy, p.s0, p.ckpt, ws,
+                                             (T*)p.dr, (T*)p.dw, (T*)p.dk, (T*)p.dv, (T*)p.da, (T*)p.db, p.T, p.H);
+    return check_launch();
+}
+
+int wkv7_bwd_chunked(const WkvBwdArgs& p, float* ws, cudaStream_t st) {
+    RWKV_DISPATCH_DTYPE_W(p.dtype, p.w_dtype, T, TW, return launch_bwd_chunked<T, TW>(p, ws, st));
+    return RWKV_OK;
+}
+
+}  // namespace rwkv

@@ -114,13 +114,15 @@ def _bwd(r, w, k, v, a, b, dy, ckpt, head_size=64, s0=None, dsT=None, want_ds0=F
         if ckpt.numel() != B * H * (T // ckpt_len) * 64 * 64:
             raise ValueError("checkpoint buffer does not match (B, H, T // ckpt_len, 64, 64)")
     L = nat.lib()
+    ws_bytes = L.rwkv_wkv7_backward_workspace_size(B, T, H, 64)
+    ws = torch.empty(max(1, (ws_bytes + 3) // 4), device=dev, dtype=torch.float32)
     with torch.cuda.device(dev):
-        rc = L.rwkv_wkv7_backward(
+        rc = L.rwkv_wkv7_backward_ws(
             nat.ptr(r), nat.ptr(w), nat.ptr(k), nat.ptr(v), nat.ptr(a), nat.ptr(b), nat.ptr(dy),
             nat.ptr(s0), nat.ptr(dsT), nat.ptr(ckpt) if (ckpt is not None and ckpt.numel()) else None,
             *[nat.ptr(g) for g in grads], nat.ptr(ds0), B, T, H, 64, nat.dtype_code(r),
-            nat.dtype_code(w), ckpt_len, nat.stream_ptr(dev))
-    nat.check(rc, "rwkv_wkv7_backward")
+            nat.dtype_code(w), ckpt_len, nat.ptr(ws), ws_bytes, nat.stream_ptr(dev))
+    nat.check(rc, "rwkv_wkv7_backward_ws")
     if w.dtype != r.dtype:
         pass  # dw is produced in r.dtype like the reference (wkv7_metal.py:317)
     return tuple(grads), ds0

@@ -51,6 +51,7 @@ __device__ __forceinline__ void split(float x, uint32_t& hi, uint32_t& lo) {
 template <typename FA, typename FB>
 __device__ __forceinline__ void tile_mm(float (&d)[4], const FA& A, const FB& B, int K) {
     const int lane = threadIdx.x & 31, g = lane >> 2, tg = lane & 3;
+    float e[4] = {0.f, 0.f, 0.f, 0.f};  // correction terms: a separate chain from d
     for (int k0 = 0; k0 < K; k0 += 8) {
         uint32_t ah[4], al[4], bh[2], bl[2];
         split(A(g, k0 + tg), ah[0], al[0]);
@@ -59,10 +60,12 @@ __device__ __forceinline__ void tile_mm(float (&d)[4], const FA& A, const FB& B,
         split(A(g + 8, k0 + tg + 4), ah[3], al[3]);
         split(B(k0 + tg, g), bh[0], bl[0]);
         split(B(k0 + tg + 4, g), bh[1], bl[1]);
-        mma8(d, al[0], al[1], al[2], al[3], bh[0], bh[1]);
-        mma8(d, ah[0], ah[1], ah[2], ah[3], bl[0], bl[1]);
+        mma8(e, al[0], al[1], al[2], al[3], bh[0], bh[1]);
+        mma8(e, ah[0], ah[1], ah[2], ah[3], bl[0], bl[1]);
         mma8(d, ah[0], ah[1], ah[2], ah[3], bh[0], bh[1]);
     }
+#pragma unroll
+    for (int i = 0; i < 4; i++) d[i] += e[i];
 }
 // C (M x Nn) = A (M x K) B (K x Nn) over the block's warps; out(m, n, v) once per element.
 // The element -> thread mapping depends only on (M, Nn), so successive calls with the

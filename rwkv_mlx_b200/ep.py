@@ -8,7 +8,7 @@ combines them with the router scores and the frozen base output:
 
     router -> stable sort of the entries by expert (= by destination rank)
     -> all_to_all of counts -> all_to_all of rows and expert ids
-    -> local sort by expert -> grouped x @ A_e -> (h @ B_e) written back in arrival order
+    -> local adapters (fused x @ A_e @ B_e per row, or sorted + grouped for other shapes)
     -> all_to_all back -> out[t] = base[t] + sum_slot score * row
 
 The aux and z losses are reduced over ranks exactly (sums of the per-rank partial
@@ -49,6 +49,15 @@ class GpuOps:
     @staticmethod
     def lora_down(rows, A, perm, offsets):
         return gpu_moe.lora_down(rows, A, perm, offsets, 1)
+
+    @staticmethod
+    def apply_local(rows, A, Bw, e_loc):
+        """rows[i] @ A[e] @ B[e] with e = e_loc[i] in one fused pass, or None when the shape
+        is outside the fused kernel (then the sorted path runs)."""
+        E, C, R = A.shape
+        if not gpu_moe.lora_apply_supported(C, R, E, 1, rows.dtype):
+            return None
+        return gpu_moe.lora_apply(rows, None, A, Bw, e_loc, None)
 
     @staticmethod
     def lora_up(h, Bw, offsets, out_index, dtype):
@@ -135,10 +144,14 @@ class ExpertParallelLoRAMoE(nn.Module):
         x_recv = _a2a(x2.new_empty((n_recv, C)), x_send, rc, sc, g)
         e_recv = _a2a(e_send.new_empty((n_recv,)), e_send, rc, sc, g)
         if n_recv:
-            e_loc = (e_recv - self.rank * El).reshape(-1, 1).contiguous()
-            perm2, _, off2 = ops.permute(e_loc, El)
-            h = ops.lora_down(x_recv, self.lora_A.detach(), perm2, off2)
-            y_recv = ops.lora_up(h, self.lora_B.detach(), off2, perm2, x.dtype)
+            e_loc = (e_recv - self.rank * El).reshape(-1, 1).to(torch.int32).contiguous()
+            y_recv = None
+            if hasattr(ops, "apply_local"):
+                y_recv = ops.apply_local(x_recv, self.lora_A.detach().to(x.dtype), self.lora_B.detach().to(x.dtype), e_loc)
+            if y_recv is None:  # sorted by local expert: grouped down, then up in arrival order
+                perm2, _, off2 = ops.permute(e_loc, El)
+                h = ops.lora_down(x_recv, self.lora_A.detach(), perm2, off2)
+                y_recv = ops.lora_up(h, self.lora_B.detach(), off2, perm2, x.dtype)
         else:
             y_recv = x2.new_empty((0, C))
         y_back = _a2a(x2.new_empty((n_send, C)), y_recv, sc, rc, g)
@@ -146,7 +159,8 @@ class ExpertParallelLoRAMoE(nn.Module):
 
         # aux / z over the whole (all-rank) batch
         p_loc = torch.softmax(r["logits"].float(), -1).sum(0)
-        f_cnt = torch.bincount(inds.reshape(-1).long(), minlength=E).to(p_loc.dtype)
+        cnt = r.get("counts")  # per-expert counts from the router (no device -> host sync)
+        f_cnt = (cnt if cnt is not None else torch.bincount(inds.reshape(-1).long(), minlength=E)).to(p_loc.dtype)
         z_sum = r["z"].float() * ntok
         red = torch.cat([p_loc, f_cnt, z_sum.reshape(1), torch.tensor([float(ntok)], device=p_loc.device)])
         dist.all_reduce(red, group=g)

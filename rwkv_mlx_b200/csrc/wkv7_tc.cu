@@ -43,10 +43,11 @@ constexpr int SBO_K64 = 16 * KLBO, SBO_K32 = 8 * KLBO, SBO_K16 = 4 * KLBO;
 constexpr int SZ_WB = 4 * SBO_K64;  // 32 rows x K=64
 constexpr int SZ_BK = 8 * SBO_K32;  // 64 rows x K=32
 constexpr int SZ_VT = 8 * SBO_K16;  // 64 rows x K=16
+constexpr int SZ_BY = 4 * SBO_K16;  // 32 rows x K=16
 
 struct __align__(128) Stage {
     unsigned char WB[SZ_WB];  // B of D1: rows t' (0-15 Wu, 16-31 Wy), K = key
-    unsigned char UY[SZ_WB];  // intra-chunk part of D1: rows t' (0-15 Ui, 16-31 Yi), K = value
+    unsigned char BY[SZ_BY];  // B of the intra-chunk part V^T [Gu | Gy]: rows t' (0-15 Gu^T, 16-31 Gy^T), K = s
     unsigned char BK[SZ_BK];  // B of D2: rows key, K = t' (0-15 Bb, 16-31 Kb)
     unsigned char VT[SZ_VT];  // A of D2 (V part): rows value, K = t
     float GL[N];              // decay of the whole chunk per key
@@ -54,8 +55,7 @@ struct __align__(128) Stage {
 struct __align__(16) PrepScratch {
     float At[L][LD4], Rt[L][LD4], Bh[L][LD4], Kh[L][LD4];
     float Mab[L][LDM], Mak[L][LDM], Mrb[L][LDM], Mrk[L][LDM];
-    float MakV[L][LD8];
-    float Vs[L][LD8];
+    float GuT[L][LDM];  // (I - Mab)^-1 Mak
     float Cs[L + 1][N];  // cumulative log2 decay, Cs[0] = 0
 };
 struct __align__(128) Smem {
@@ -276,7 +276,6 @@ __global__ void __launch_bounds__(NT, 1)
                 o1[q] = vq;
                 *reinterpret_cast<float*>(stg.VT + kmaj(key, t, SBO_K16)) = vq;  // key index = value index
             }
-            sts8(&ps.Vs[t][j0], o1);
             sts8(&ps.Cs[t + 1][j0], cs);
             if (t == 0) {
 #pragma unroll
@@ -333,53 +332,35 @@ __global__ void __launch_bounds__(NT, 1)
             group_sync(BAR);
             if (c + 2 < nchunks) issue(c + 2);  // raw staging is free from here on
 
-            // ---- P3: MakV = Mak V ----
-            {
-                float acc3[2][4] = {};
-#pragma unroll
-                for (int ks = 0; ks < 2; ks++) {
-                    const int k0 = 8 * ks;
-                    const uint32_t a0 = fbits(ps.Mak[g][k0 + tg]), a1 = fbits(ps.Mak[g + 8][k0 + tg]);
-                    const uint32_t a2 = fbits(ps.Mak[g][k0 + tg + 4]), a3 = fbits(ps.Mak[g + 8][k0 + tg + 4]);
-#pragma unroll
-                    for (int nt = 0; nt < 2; nt++) {
-                        const int n0 = 16 * pw + 8 * nt;
-                        mma8(acc3[nt], a0, a1, a2, a3, fbits(ps.Vs[k0 + tg][n0 + g]), fbits(ps.Vs[k0 + tg + 4][n0 + g]));
-                    }
-                }
-#pragma unroll
-                for (int nt = 0; nt < 2; nt++) {
-                    const int n0 = 16 * pw + 8 * nt + 2 * tg;
-                    *reinterpret_cast<float2*>(&ps.MakV[g][n0]) = make_float2(acc3[nt][0], acc3[nt][1]);
-                    *reinterpret_cast<float2*>(&ps.MakV[g + 8][n0]) = make_float2(acc3[nt][2], acc3[nt][3]);
-                }
-            }
-            group_sync(BAR);
-
-            // ---- P4: X = (I - Mab)^-1 [At | MakV] -> Wu (WB rows 0-15), Ui (UY rows 0-15) ----
-            {
+            // ---- P4: forward substitution (I - Mab) X = [At | Mak]: Wu -> WB rows 0-15
+            //      (threads 0-63, one key column each), Gu^T (threads 64-79) ----
+            if (pt < N + L) {
                 float x[L];
-                const bool left = pt < 64;
-                const int col = left ? pt : pt - 64;
+                const bool left = pt < N;
+                const int col = left ? pt : pt - N;
 #pragma unroll
                 for (int tt = 0; tt < L; tt++) {
-                    float accx = left ? ps.At[tt][col] : ps.MakV[tt][col];
+                    float accx = left ? ps.At[tt][col] : ps.Mak[tt][col];
 #pragma unroll
                     for (int s2 = 0; s2 < tt; s2++) accx = fmaf(ps.Mab[tt][s2], x[s2], accx);
                     x[tt] = accx;
                 }
-                unsigned char* dst = left ? stg.WB : stg.UY;
+                if (left) {
 #pragma unroll
-                for (int tt = 0; tt < L; tt++) *reinterpret_cast<float*>(dst + kmaj(tt, col, SBO_K64)) = tf32f(x[tt]);
+                    for (int tt = 0; tt < L; tt++) *reinterpret_cast<float*>(stg.WB + kmaj(tt, col, SBO_K64)) = tf32f(x[tt]);
+                } else {
+#pragma unroll
+                    for (int tt = 0; tt < L; tt++) ps.GuT[tt][col] = tf32f(x[tt]);
+                }
             }
             group_sync(BAR);
 
-            // ---- P5: Wy = Rt + Mrb Wu (WB rows 16-31); Yi = Mrb Ui + Mrk V (UY rows 16-31) ----
+            // ---- P5: Wy = Rt + Mrb Wu (WB rows 16-31); Gu^T, Gy^T = Mrb Gu^T + Mrk (BY) ----
             {
                 auto ldB = [&](const unsigned char* src, int kk, int nn) {
                     return fbits(*reinterpret_cast<const float*>(src + kmaj(kk, nn, SBO_K64)));
                 };
-                float wy[2][4], yi[2][4] = {};
+                float wy[2][4];
 #pragma unroll
                 for (int nt = 0; nt < 2; nt++) {
                     const int n0 = 16 * pw + 8 * nt + 2 * tg;
@@ -395,14 +376,6 @@ __global__ void __launch_bounds__(NT, 1)
                     for (int nt = 0; nt < 2; nt++) {
                         const int n0 = 16 * pw + 8 * nt;
                         mma8(wy[nt], a0, a1, a2, a3, ldB(stg.WB, k0 + tg, n0 + g), ldB(stg.WB, k0 + tg + 4, n0 + g));
-                        mma8(yi[nt], a0, a1, a2, a3, ldB(stg.UY, k0 + tg, n0 + g), ldB(stg.UY, k0 + tg + 4, n0 + g));
-                    }
-                    const uint32_t c0 = fbits(ps.Mrk[g][k0 + tg]), c1 = fbits(ps.Mrk[g + 8][k0 + tg]);
-                    const uint32_t c2 = fbits(ps.Mrk[g][k0 + tg + 4]), c3 = fbits(ps.Mrk[g + 8][k0 + tg + 4]);
-#pragma unroll
-                    for (int nt = 0; nt < 2; nt++) {
-                        const int n0 = 16 * pw + 8 * nt;
-                        mma8(yi[nt], c0, c1, c2, c3, fbits(ps.Vs[k0 + tg][n0 + g]), fbits(ps.Vs[k0 + tg + 4][n0 + g]));
                     }
                 }
 #pragma unroll
@@ -411,7 +384,38 @@ __global__ void __launch_bounds__(NT, 1)
                     for (int e = 0; e < 4; e++) {
                         const int tt = L + g + (e >> 1) * 8, col = 16 * pw + 8 * nt + 2 * tg + (e & 1);
                         *reinterpret_cast<float*>(stg.WB + kmaj(tt, col, SBO_K64)) = tf32f(wy[nt][e]);
-                        *reinterpret_cast<float*>(stg.UY + kmaj(tt, col, SBO_K64)) = tf32f(yi[nt][e]);
+                    }
+                }
+                if (pw == 0) {
+                    float gy[2][4];
+#pragma unroll
+                    for (int nt = 0; nt < 2; nt++) {
+                        const int n0 = 8 * nt + 2 * tg;
+                        gy[nt][0] = ps.Mrk[g][n0], gy[nt][1] = ps.Mrk[g][n0 + 1];
+                        gy[nt][2] = ps.Mrk[g + 8][n0], gy[nt][3] = ps.Mrk[g + 8][n0 + 1];
+                    }
+#pragma unroll
+                    for (int ks = 0; ks < 2; ks++) {
+                        const int k0 = 8 * ks;
+                        const uint32_t a0 = fbits(ps.Mrb[g][k0 + tg]), a1 = fbits(ps.Mrb[g + 8][k0 + tg]);
+                        const uint32_t a2 = fbits(ps.Mrb[g][k0 + tg + 4]), a3 = fbits(ps.Mrb[g + 8][k0 + tg + 4]);
+#pragma unroll
+                        for (int nt = 0; nt < 2; nt++)
+                            mma8(gy[nt], a0, a1, a2, a3, fbits(ps.GuT[k0 + tg][8 * nt + g]), fbits(ps.GuT[k0 + tg + 4][8 * nt + g]));
+                    }
+#pragma unroll
+                    for (int nt = 0; nt < 2; nt++) {
+#pragma unroll
+                        for (int e = 0; e < 4; e++) {
+                            const int tp = g + (e >> 1) * 8, ss = 8 * nt + 2 * tg + (e & 1);
+                            *reinterpret_cast<float*>(stg.BY + kmaj(L + tp, ss, SBO_K16)) = tf32f(gy[nt][e]);
+                        }
+                    }
+                } else if (pw == 1) {
+#pragma unroll
+                    for (int i = 0; i < (L * L) / 32; i++) {
+                        const int q = lane + 32 * i, tp = q / L, ss = q % L;
+                        *reinterpret_cast<float*>(stg.BY + kmaj(tp, ss, SBO_K16)) = ps.GuT[tp][ss];
                     }
                 }
             }
@@ -425,7 +429,6 @@ __global__ void __launch_bounds__(NT, 1)
         const int tw = warp, lane = tid & 31;
         const bool live = lane < 16;              // M=64 accumulators use lanes 0-15 of each subpartition
         const int row = 16 * tw + lane;            // state row (value index) held by this thread
-        const int rowc = 16 * tw + (lane & 15);    // in-range row for the idle lanes' loads
         const uint32_t lane_base = (uint32_t)(32 * tw) << 16;
         const uint32_t tD2 = tmem + lane_base, tD1a = tD2 + 64, tD1b = tD2 + 96;
         {
@@ -442,19 +445,14 @@ __global__ void __launch_bounds__(NT, 1)
             Stage& stg = sm.st[s];
             const bool bad = !mbar_wait(&sm.full[s], (c / NSTAGE) & 1, &sm.abort, &g_device_error_tc);
             if (group_sync_or(BAR_STATE, bad)) break;
-            {  // D1a <- [Ui; Yi]^T (row `row`, columns t')
-                float pre[2 * L];
-#pragma unroll
-                for (int tt = 0; tt < 2 * L; tt++) pre[tt] = *reinterpret_cast<const float*>(stg.UY + kmaj(tt, rowc, SBO_K64));
-                tmem_st16(tD1a, pre);
-                tmem_st16(tD1a + 16, pre + 16);
-                tmem_wait_st();
-            }
-            tc_fence_before();
-            group_sync(BAR_STATE);
             tc_fence_after();
             if (tid == 0) {
-                const uint32_t i1 = idesc_tf32(64, 32), bW = smem_u32(stg.WB);
+                // D1a = V^T [Gu | Gy] (intra-chunk part), then + S0 [Wu; Wy]^T over two chains
+                const uint32_t i1 = idesc_tf32(64, 32), bW = smem_u32(stg.WB), aV = smem_u32(stg.VT),
+                               bY = smem_u32(stg.BY);
+#pragma unroll
+                for (int ks = 0; ks < 2; ks++)
+                    umma(tmem + 64, umma_desc(aV + 2 * ks * KLBO, SBO_K16), umma_desc(bY + 2 * ks * KLBO, SBO_K16), i1, ks);
 #pragma unroll
                 for (int ks = 0; ks < 8; ks++)
                     umma_ts((ks & 1) ? tmem + 96 : tmem + 64, tmem + 8 * ks, umma_desc(bW + 2 * ks * KLBO, SBO_K64), i1,

@@ -247,6 +247,11 @@ int rwkv_moe_ortho_loss(const void* A, float* out, int E, int C, int R, int dtyp
  *   y = LayerNorm(x_out) with weight w, bias b, eps (model.py:315-326). */
 int rwkv_lerp(const void* x, const void* mix, void* out, int M, long long rows, int T, int C,
               int dtype, void* stream);
+/* rwkv_lerp_prev: rwkv_lerp whose shift at the first row of sequence s takes
+ * prev[s] (rows / T, C) instead of zeros: the RNN-mode token shift with the stored
+ * previous token (model.py:449-455, 498-501); prev NULL = rwkv_lerp.                 */
+int rwkv_lerp_prev(const void* x, const void* prev, const void* mix, void* out, int M,
+                   long long rows, int T, int C, int dtype, void* stream);
 int rwkv_tmix_mid(const void* k, const void* v, const void* wl, const void* al, const void* vl,
                   const void* v_first, const float* w0, const void* a0, const void* v0,
                   const void* k_k, const void* k_a, float* w_out, void* k_out, void* v_out,

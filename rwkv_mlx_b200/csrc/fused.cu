@@ -27,8 +27,8 @@ struct Vec {
 // ---------------------------------------------------------------------------
 template <typename T>
 __global__ void __launch_bounds__(256)
-    lerp_kernel(const T* __restrict__ x, const T* __restrict__ mix, T* __restrict__ out, int M,
-                long long rows, int Tlen, int C) {
+    lerp_kernel(const T* __restrict__ x, const T* __restrict__ prev, const T* __restrict__ mix,
+                T* __restrict__ out, int M, long long rows, int Tlen, int C) {
     constexpr int V = Vec<T>::N;
     const int nv = C / V;
     const long long total = rows * nv;
@@ -39,6 +39,7 @@ __global__ void __launch_bounds__(256)
         Vec<T> xv, pv;
         xv.load(x + row * C + c0);
         if (row % Tlen) pv.load(x + (row - 1) * C + c0);
+        else if (prev) pv.load(prev + (row / Tlen) * C + c0);  // the token before this sequence
         else pv.zero();
         float xf[V], dx[V];
 #pragma unroll
@@ -283,18 +284,24 @@ static int grid_for(long long work, int per_block) {
 
 using namespace rwkv;
 
-extern "C" int rwkv_lerp(const void* x, const void* mix, void* out, int M, long long rows, int T,
-                         int C, int dtype, void* stream) {
-    if (M <= 0 || rows <= 0 || T <= 0 || C <= 0) return RWKV_ERR_SHAPE;
+extern "C" int rwkv_lerp_prev(const void* x, const void* prev, const void* mix, void* out, int M,
+                              long long rows, int T, int C, int dtype, void* stream) {
+    if (M <= 0 || rows <= 0 || T <= 0 || C <= 0 || rows % T) return RWKV_ERR_SHAPE;
     if (!x || !mix || !out) return RWKV_ERR_ARG;
-    if (!aligned(x, 16) || !aligned(mix, 16) || !aligned(out, 16)) return RWKV_ERR_ALIGN;
+    if (!aligned(x, 16) || !aligned(mix, 16) || !aligned(out, 16) || (prev && !aligned(prev, 16)))
+        return RWKV_ERR_ALIGN;
     cudaStream_t st = (cudaStream_t)stream;
     RWKV_DISPATCH_DTYPE(dtype, T_, {
         if (C % Vec<T_>::N) return RWKV_ERR_SHAPE;
         lerp_kernel<T_><<<grid_for(rows * (C / Vec<T_>::N), 256), 256, 0, st>>>(
-            (const T_*)x, (const T_*)mix, (T_*)out, M, rows, T, C);
+            (const T_*)x, (const T_*)prev, (const T_*)mix, (T_*)out, M, rows, T, C);
     });
     return check_launch();
+}
+
+extern "C" int rwkv_lerp(const void* x, const void* mix, void* out, int M, long long rows, int T,
+                         int C, int dtype, void* stream) {
+    return rwkv_lerp_prev(x, nullptr, mix, out, M, rows, T, C, dtype, stream);
 }
 
 extern "C" int rwkv_tmix_mid(const void* k, const void* v, const void* wl, const void* al,

@@ -17,15 +17,21 @@ def _call(name, *args):
     nat.check(rc, name)
 
 
-def lerp(x: torch.Tensor, mix: torch.Tensor, T: int) -> torch.Tensor:
-    """x (..., C) with rows grouped in sequences of length T; mix (M, C) -> (M, rows, C)."""
+def lerp(x: torch.Tensor, mix: torch.Tensor, T: int, prev: torch.Tensor = None) -> torch.Tensor:
+    """x (..., C) with rows grouped in sequences of length T; mix (M, C) -> (M, rows, C).
+    ``prev`` (rows / T, C): the token before each sequence (zeros when None)."""
     C = x.shape[-1]
     x = x.contiguous()
     rows = x.numel() // C
     mix = mix.to(x.dtype).contiguous().view(-1, C)
     out = torch.empty((mix.shape[0], rows, C), device=x.device, dtype=x.dtype)
-    _call("rwkv_lerp", nat.ptr(x), nat.ptr(mix), nat.ptr(out), mix.shape[0], rows, T, C, nat.dtype_code(x),
-          nat.stream_ptr(x.device))
+    if prev is None:
+        _call("rwkv_lerp", nat.ptr(x), nat.ptr(mix), nat.ptr(out), mix.shape[0], rows, T, C, nat.dtype_code(x),
+              nat.stream_ptr(x.device))
+    else:
+        prev = prev.to(x.dtype).contiguous()
+        _call("rwkv_lerp_prev", nat.ptr(x), nat.ptr(prev), nat.ptr(mix), nat.ptr(out), mix.shape[0], rows, T, C,
+              nat.dtype_code(x), nat.stream_ptr(x.device))
     return out
 
 

@@ -209,6 +209,31 @@ class RWKV_Tmix_x070(nn.Module):
         out = self._post(y, r, k, v, g)
         return (out, v_first, sT) if return_state else (out, v_first)
 
+    def _forward_rnn_fused(self, x, x_prev, v_first, state):
+        """forward_rnn on the fused kernels: x, x_prev (Bs, C); v_first (Bs, C) or None for
+        layer 0.  Returns (out (Bs, C), v_first)."""
+        Bs, C = x.shape
+        H = self.n_head
+        mix = torch.cat([self.x_r, self.x_k, self.x_v, self.x_w, self.x_a, self.x_g]).view(6, C)
+        X = fz.lerp(x, mix, 1, prev=x_prev)  # (6, Bs, C)
+        rkv = torch.bmm(X[0:3], torch.stack([self.receptance.weight, self.key.weight, self.value.weight]).transpose(1, 2))
+        r, k, v = rkv[0], rkv[1], rkv[2]
+        xv, xw, xa, xg = X[2], X[3], X[4], X[5]
+        wl = torch.tanh(xw @ self.w1) @ self.w2
+        al = (xa @ self.a1) @ self.a2
+        layer0 = self.layer_id == 0
+        vl = None if layer0 else (xv @ self.v1) @ self.v2
+        g = torch.sigmoid(xg @ self.g1) @ self.g2
+        w, k2, v2, a_in, b_in = fz.tmix_mid(k, v, wl, al, vl, None if layer0 else v_first, self.w0.view(-1),
+                                             self.a0.view(-1), self.v0.view(-1), self.k_k.view(-1),
+                                             self.k_a.view(-1), layer0)
+        if layer0:
+            v_first = v2
+        y = wkv7_step(state, r, w, k2, v2, a_in, b_in, w_is_decay=False)
+        pre = fz.tmix_post(y, r, k2, v2, g, self.ln_x.weight, self.ln_x.bias, self.r_k, H, self.ln_x.eps,
+                           self.config.groupnorm != "mlx")
+        return self.output(pre), v_first
+
     def forward_rnn(self, x, x_prev, v_first, state):
         """Batched RNN step (model.py:441-495): x, x_prev (Bs, C); state (Bs,H,N,N)
         fp32 updated in place.  Returns (out, x, state, v_first)."""
@@ -242,6 +267,10 @@ class RWKV_CMix_x070(nn.Module):
         k = x + xx * self.x_k
         k = torch.relu(self.key(k)) ** 2
         return self.value(k)
+
+    def forward_rnn_fused(self, x, x_prev):
+        k = fz.lerp(x, self.x_k.view(1, -1), 1, prev=x_prev)[0]
+        return self.value(fz.relu_sq_(self.key(k)))
 
     def forward_rnn(self, x, x_prev):
         """model.py:498-506 (batched)."""
@@ -389,6 +418,8 @@ class RWKV(nn.Module):
         ``states`` (per-layer dicts) is updated in place: every state tensor keeps its
         storage, so a step can be captured in a CUDA graph (see :class:`DecodeGraph`)."""
         x = self.emb(tokens)
+        if self.config.fused and not torch.is_grad_enabled() and x.is_cuda:
+            return self._forward_rnn_batch_fused(x, states)
         v_first = torch.zeros_like(x)
         for i, blk in enumerate(self.blocks):
             if i == 0:
@@ -411,6 +442,26 @@ class RWKV(nn.Module):
                 x = x + out
             st["ffn_x_prev"].copy_(xx)
         x = self.ln_out(x)
+        return self.head(x)
+
+    def _forward_rnn_batch_fused(self, x, states):
+        """forward_rnn_batch with the residual adds folded into the LayerNorm passes."""
+        v_first, pending = None, None
+        for i, blk in enumerate(self.blocks):
+            if i == 0:
+                _, x = fz.add_layernorm(x, None, blk.ln0.weight, blk.ln0.bias, blk.ln0.eps)
+            x, xx = fz.add_layernorm(x, pending, blk.ln1.weight, blk.ln1.bias, blk.ln1.eps)
+            st = states[i]
+            out, v_first = blk.att._forward_rnn_fused(xx, st["att_x_prev"], v_first, st["att_state"])
+            st["att_x_prev"].copy_(xx)
+            x, xx = fz.add_layernorm(x, out, blk.ln2.weight, blk.ln2.bias, blk.ln2.eps)
+            if blk.is_moe:
+                ffn = blk.ffn
+                pending = ffn.base.forward_rnn_fused(xx, st["ffn_x_prev"]) + _moe_rnn(ffn, xx)
+            else:
+                pending = blk.ffn.forward_rnn_fused(xx, st["ffn_x_prev"])
+            st["ffn_x_prev"].copy_(xx)
+        _, x = fz.add_layernorm(x, pending, self.ln_out.weight, self.ln_out.bias, self.ln_out.eps)
         return self.head(x)
 
     def forward_rnn(self, token: int, state: list):
@@ -467,9 +518,12 @@ class DecodeGraph:
 
 
 def _moe_rnn(ffn, x):
-    from .moe import lora_combine, lora_down, permute, router_forward
+    from .moe import lora_apply, lora_apply_supported, lora_combine, lora_down, permute, router_forward
 
     r = router_forward(x.contiguous(), ffn.router.gate.weight, ffn.top_k, ffn.router.bias)
+    C = x.shape[-1]
+    if lora_apply_supported(C, ffn.lora_rank, ffn.n_experts, ffn.top_k, x.dtype):
+        return lora_apply(x.contiguous(), None, ffn.lora_A.detach(), ffn.lora_B.detach(), r["inds"], r["scores"])
     perm, inv, off = permute(r["inds"], ffn.n_experts)
     h = lora_down(x.contiguous(), ffn.lora_A.detach(), perm, off, ffn.top_k)
     return lora_combine(None, h, ffn.lora_B.detach(), r["inds"], r["scores"], inv)

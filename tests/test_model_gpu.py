@@ -151,3 +151,32 @@ def test_decode_graph_matches_eager_decode():
     graphed = [g.step().clone() for _ in range(5)]
     for a, b in zip(eager, graphed):
         assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16])
+def test_fused_rnn_step_matches_op_by_op(dtype):
+    """RNN-mode batched step on the fused kernels (lerp with the stored previous token,
+    TimeMix mid/post, relu^2, add+LayerNorm) equals the op-by-op path, states included."""
+    from rwkv_mlx_b200.model import cast_for_inference
+
+    for moe in (False, True):
+        cfg, m = _tiny(moe=moe)
+        if dtype == torch.float16:
+            cast_for_inference(m, torch.float16)
+        idx = torch.randint(0, cfg.vocab_size, (3, 20), device="cuda")
+        with torch.no_grad():
+            _, _, st_a = m.forward_with_state(idx)
+            _, _, st_b = m.forward_with_state(idx)
+            tok = idx[:, -1]
+            for _ in range(4):
+                cfg.fused = True
+                la = m.forward_rnn_batch(tok, st_a)
+                cfg.fused = False
+                lb = m.forward_rnn_batch(tok, st_b)
+                cfg.fused = True
+                tol = 1e-4 if dtype == torch.float32 else 3e-3
+                assert rel_rms(la.double().cpu().numpy(), lb.double().cpu().numpy()) < tol, moe
+                tok = lb.argmax(-1)
+        for x, y in zip(st_a, st_b):
+            for key in x:
+                assert rel_rms(x[key].float().cpu().numpy(), y[key].float().cpu().numpy()) < 1e-2, key

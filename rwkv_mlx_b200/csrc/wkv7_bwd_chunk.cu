@@ -47,21 +47,29 @@ __device__ __forceinline__ void split(float x, uint32_t& hi, uint32_t& lo) {
     lo = tf32(x - __uint_as_float(hi));
 }
 
-// d (one 16x8 tile) += A(16 x K) B(K x 8); accessors take tile-local indices
-template <typename FA, typename FB>
+// d (one 16x8 tile) += A(16 x K) B(K x 8); accessors take tile-local indices.  AX / BX:
+// the operand's values are exactly representable in TF32 (16-bit inputs), so its low
+// part is zero and the product that uses it is skipped.
+template <bool AX = false, bool BX = false, typename FA, typename FB>
 __device__ __forceinline__ void tile_mm(float (&d)[4], const FA& A, const FB& B, int K) {
     const int lane = threadIdx.x & 31, g = lane >> 2, tg = lane & 3;
     float e[4] = {0.f, 0.f, 0.f, 0.f};  // correction terms: a separate chain from d
     for (int k0 = 0; k0 < K; k0 += 8) {
         uint32_t ah[4], al[4], bh[2], bl[2];
-        split(A(g, k0 + tg), ah[0], al[0]);
-        split(A(g + 8, k0 + tg), ah[1], al[1]);
-        split(A(g, k0 + tg + 4), ah[2], al[2]);
-        split(A(g + 8, k0 + tg + 4), ah[3], al[3]);
-        split(B(k0 + tg, g), bh[0], bl[0]);
-        split(B(k0 + tg + 4, g), bh[1], bl[1]);
-        mma8(e, al[0], al[1], al[2], al[3], bh[0], bh[1]);
-        mma8(e, ah[0], ah[1], ah[2], ah[3], bl[0], bl[1]);
+        const float av[4] = {A(g, k0 + tg), A(g + 8, k0 + tg), A(g, k0 + tg + 4), A(g + 8, k0 + tg + 4)};
+        const float bv[2] = {B(k0 + tg, g), B(k0 + tg + 4, g)};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            if (AX) ah[i] = __float_as_uint(av[i]), al[i] = 0u;
+            else split(av[i], ah[i], al[i]);
+        }
+#pragma unroll
+        for (int i = 0; i < 2; i++) {
+            if (BX) bh[i] = __float_as_uint(bv[i]), bl[i] = 0u;
+            else split(bv[i], bh[i], bl[i]);
+        }
+        if (!AX) mma8(e, al[0], al[1], al[2], al[3], bh[0], bh[1]);
+        if (!BX) mma8(e, ah[0], ah[1], ah[2], ah[3], bl[0], bl[1]);
         mma8(d, ah[0], ah[1], ah[2], ah[3], bh[0], bh[1]);
     }
 #pragma unroll
@@ -86,15 +94,16 @@ __device__ __forceinline__ void block_mm(int M, int Nn, int K, const FA& A, cons
 }
 
 // Sum of products over K segments, each with its own accessors: (A_1 B_1 + A_2 B_2 + ...)
-template <typename FA, typename FB>
+template <bool AX_, bool BX_, typename FA, typename FB>
 struct Seg {
+    static constexpr bool AX = AX_, BX = BX_;
     FA A;
     FB B;
     int K;
 };
-template <typename FA, typename FB>
-__device__ __forceinline__ Seg<FA, FB> seg(const FA& A, const FB& B, int K) {
-    return Seg<FA, FB>{A, B, K};
+template <bool AX = false, bool BX = false, typename FA, typename FB>
+__device__ __forceinline__ Seg<AX, BX, FA, FB> seg(const FA& A, const FB& B, int K) {
+    return Seg<AX, BX, FA, FB>{A, B, K};
 }
 template <typename FO, typename... S>
 __device__ __forceinline__ void block_mm_s(int M, int Nn, const FO& out, const S&... segs) {
@@ -103,8 +112,8 @@ __device__ __forceinline__ void block_mm_s(int M, int Nn, const FO& out, const S
     for (int tile = warp; tile < tiles; tile += nw) {
         const int m0 = (tile / ntl) * 16, n0 = (tile % ntl) * 8;
         float d[4] = {0.f, 0.f, 0.f, 0.f};
-        (tile_mm(d, [&](int m, int k) { return segs.A(m0 + m, k); }, [&](int k, int n) { return segs.B(k, n0 + n); },
-                 segs.K),
+        (tile_mm<S::AX, S::BX>(d, [&](int m, int k) { return segs.A(m0 + m, k); },
+                               [&](int k, int n) { return segs.B(k, n0 + n); }, segs.K),
          ...);
         out(m0 + g, n0 + 2 * tg, d[0]);
         out(m0 + g, n0 + 2 * tg + 1, d[1]);
@@ -115,14 +124,23 @@ __device__ __forceinline__ void block_mm_s(int M, int Nn, const FO& out, const S
 
 // nblk independent 16 x Nn products (block b: rows of A(b, m, k), B(b, k, n)), tiles
 // spread over the block's warps; out(b, m, n, v) once per element.
+// With `exact` set, block 1's B, block 2's A and both operands of block 3 are taken as
+// exactly representable in TF32 (the layout of the stacked gradient products below).
 template <typename FA, typename FB, typename FO>
-__device__ __forceinline__ void block_mm_b(int nblk, int Nn, int K, const FA& A, const FB& B, const FO& out) {
+__device__ __forceinline__ void block_mm_b(int nblk, int Nn, int K, const FA& A, const FB& B, const FO& out,
+                                           bool exact = false) {
     const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tg = lane & 3;
     const int ntl = Nn / 8, tiles = nblk * ntl;
     for (int tile = warp; tile < tiles; tile += nw) {
         const int bb = tile / ntl, n0 = (tile % ntl) * 8;
         float d[4] = {0.f, 0.f, 0.f, 0.f};
-        tile_mm(d, [&](int m, int k) { return A(bb, m, k); }, [&](int k, int n) { return B(bb, k, n0 + n); }, K);
+        auto a_ = [&](int m, int k) { return A(bb, m, k); };
+        auto b_ = [&](int k, int n) { return B(bb, k, n0 + n); };
+        const int kind = exact ? bb : 0;
+        if (kind == 1) tile_mm<false, true>(d, a_, b_, K);
+        else if (kind == 2) tile_mm<true, false>(d, a_, b_, K);
+        else if (kind == 3) tile_mm<true, true>(d, a_, b_, K);
+        else tile_mm(d, a_, b_, K);
         out(bb, g, n0 + 2 * tg, d[0]);
         out(bb, g, n0 + 2 * tg + 1, d[1]);
         out(bb, g + 8, n0 + 2 * tg, d[2]);
@@ -322,7 +340,8 @@ __global__ void __launch_bounds__(NT, 1)
         __syncthreads();
         block_mm_s(N, N, [&](int j, int vv, float val) { sm.D[j][vv] = fmaf(fr.GL[j], sm.D[j][vv], val); },
                    seg([&](int j, int t) { return sm.WU[t][j]; }, [&](int t, int vv) { return sm.DU[t][vv]; }, L),
-                   seg([&](int j, int t) { return sm.WY[t][j]; }, [&](int t, int vv) { return fr.in[IDY][t][vv]; }, L));
+                   seg<false, sizeof(T) == 2>([&](int j, int t) { return sm.WY[t][j]; },
+                                              [&](int t, int vv) { return fr.in[IDY][t][vv]; }, L));
     }
     __syncthreads();
     if (ds0) {
@@ -382,17 +401,18 @@ __global__ void __launch_bounds__(NT, 1)
     front_matrices(fr, ext, 0b1111);
     const auto& F = fr.f;
     const auto& IN = fr.in;
+    constexpr bool EXI = sizeof(T) == 2;  // 16-bit v and dy are exact in TF32
 
     // U = Inv (At X + Mak V)
     block_mm_s(L, N, [&](int t, int vv, float val) { sm.G[t][vv] = val; },
                seg([&](int t, int j) { return F[FAT][t][j]; }, [&](int j, int vv) { return sm.Sv[vv][j]; }, N),
-               seg([&](int t, int s) { return fr.M[1][t][s]; }, [&](int s, int vv) { return IN[IV][s][vv]; }, L));
+               seg<false, EXI>([&](int t, int s) { return fr.M[1][t][s]; }, [&](int s, int vv) { return IN[IV][s][vv]; }, L));
     __syncthreads();
     block_mm(L, N, L, [&](int t, int s) { return fr.Inv[t][s]; }, [&](int s, int vv) { return sm.G[s][vv]; },
              [&](int t, int vv, float val) { sm.U[t][vv] = val; });
     // external gradient of U: Mrb^T dY + Bb dX_L
     block_mm_s(L, N, [&](int t, int vv, float val) { sm.Lam[t][vv] = val; },
-               seg([&](int t, int s) { return fr.M[2][s][t]; }, [&](int s, int vv) { return IN[IDY][s][vv]; }, L),
+               seg<false, EXI>([&](int t, int s) { return fr.M[2][s][t]; }, [&](int s, int vv) { return IN[IDY][s][vv]; }, L),
                seg([&](int t, int j) { return F[FBB][t][j]; }, [&](int j, int vv) { return sm.D[j][vv]; }, N));
     __syncthreads();
     // Lambda = Inv^T (...)  (into G, free after U)
@@ -404,11 +424,12 @@ __global__ void __launch_bounds__(NT, 1)
     block_mm_b(4, L, N,
                [&](int bb, int t, int vv) { return (bb < 2 ? &Lam[0][0] : &IN[IDY][0][0])[t * LDC + vv]; },
                [&](int bb, int vv, int s) { return ((bb & 1) ? &IN[IV][0][0] : &sm.U[0][0])[s * LDC + vv]; },
-               [&](int bb, int t, int s, float val) { sm.dM[bb][t][s] = (bb < 2 ? s < t : s <= t) ? val : 0.f; });
+               [&](int bb, int t, int s, float val) { sm.dM[bb][t][s] = (bb < 2 ? s < t : s <= t) ? val : 0.f; },
+               EXI);
     // dV = Mak^T Lambda + Mrk^T dY + Kb dX_L
     block_mm_s(L, N, [&](int s, int vv, float val) { sm.dV[s][vv] = val; },
                seg([&](int s, int t) { return fr.M[1][t][s]; }, [&](int t, int vv) { return Lam[t][vv]; }, L),
-               seg([&](int s, int t) { return fr.M[3][t][s]; }, [&](int t, int vv) { return IN[IDY][t][vv]; }, L),
+               seg<false, EXI>([&](int s, int t) { return fr.M[3][t][s]; }, [&](int t, int vv) { return IN[IDY][t][vv]; }, L),
                seg([&](int s, int j) { return F[FKB][s][j]; }, [&](int j, int vv) { return sm.D[j][vv]; }, N));
     if (tid < N) {
         float sdg = 0.f;
@@ -429,7 +450,7 @@ __global__ void __launch_bounds__(NT, 1)
             sm.dC[t][j] += val * F[FRT][t][j];
         };
         auto sA = seg([&](int t, int vv) { return Lam[t][vv]; }, [&](int vv, int j) { return sm.Sv[vv][j]; }, N);
-        auto sR = seg([&](int t, int vv) { return IN[IDY][t][vv]; }, [&](int vv, int j) { return sm.Sv[vv][j]; }, N);
+        auto sR = seg<EXI, false>([&](int t, int vv) { return IN[IDY][t][vv]; }, [&](int vv, int j) { return sm.Sv[vv][j]; }, N);
         if (!ext) {
             auto bh = [&](int s, int j) { return F[FBH][s][j]; };
             auto kh = [&](int s, int j) { return F[FKH][s][j]; };
@@ -449,13 +470,14 @@ __global__ void __launch_bounds__(NT, 1)
                  sm.dC[t][j] -= q;
                  sm.Q[t][j] += q;
              });
-    block_mm(L, N, N, [&](int t, int vv) { return IN[IV][t][vv]; }, [&](int vv, int j) { return sm.D[j][vv]; },
-             [&](int t, int j, float val) {  // dKb: Kb = k e^{c_L - c_t}
-                 const float q = val * F[FKB][t][j];
-                 sm.dK[t][j] += val * expf(fr.c[L - 1][j] - fr.c[t][j]);
-                 sm.dC[t][j] -= q;
-                 sm.Q[t][j] += q;
-             });
+    block_mm_s(L, N,
+               [&](int t, int j, float val) {  // dKb: Kb = k e^{c_L - c_t}
+                   const float q = val * F[FKB][t][j];
+                   sm.dK[t][j] += val * expf(fr.c[L - 1][j] - fr.c[t][j]);
+                   sm.dC[t][j] -= q;
+                   sm.Q[t][j] += q;
+               },
+               seg<EXI, false>([&](int t, int vv) { return IN[IV][t][vv]; }, [&](int vv, int j) { return sm.D[j][vv]; }, N));
     if (!ext) {
         auto at = [&](int t, int j) { return F[FAT][t][j]; };
         auto rt = [&](int t, int j) { return F[FRT][t][j]; };

@@ -440,10 +440,11 @@ __global__ void __launch_bounds__(NT, 1)
             for (int j = 0; j < N; j += 16) tmem_st16(tD2 + j, &S[j]);
             tmem_wait_st();
         }
+        bool bad_prev = false;  // a wait of the previous chunk gave up (voted on below)
         for (int c = 0; c < nchunks; c++) {
             const int s = c % NSTAGE;
             Stage& stg = sm.st[s];
-            const bool bad = !mbar_wait(&sm.full[s], (c / NSTAGE) & 1, &sm.abort, &g_device_error_tc);
+            const bool bad = bad_prev || !mbar_wait(&sm.full[s], (c / NSTAGE) & 1, &sm.abort, &g_device_error_tc);
             if (group_sync_or(BAR_STATE, bad)) break;
             tc_fence_after();
             if (tid == 0) {
@@ -535,8 +536,9 @@ __global__ void __launch_bounds__(NT, 1)
             }
             tc_fence_before();
             mbar_arrive(&sm.empty[s]);
-            if (group_sync_or(BAR_STATE, bad3)) break;  // uniform decision for the whole group
+            bad_prev = bad3;  // the next chunk's first barrier decides for the whole group
         }
+        if (group_sync_or(BAR_STATE, bad_prev)) sm.abort = 1;
         if (sT && !group_sync_or(BAR_STATE, sm.abort != 0)) {
             tc_fence_after();
             float S[N];

@@ -478,6 +478,16 @@ __global__ void __launch_bounds__(NT, 1)
             }
 #pragma unroll
             for (int j = 0; j < N; j += 16) tmem_st16(tD2 + j, &S[j]);
+            tmem_wait_st();
+            tc_fence_before();
+            group_sync(BAR_STATE);
+            tc_fence_after();
+            if (tid == 0) {  // V^T Kb needs only the rescaled state: start it while U is staged
+                const uint32_t i2 = idesc_tf32(64, 64), aV = smem_u32(stg.VT), bK = smem_u32(stg.BK);
+#pragma unroll
+                for (int ks = 0; ks < 2; ks++)
+                    umma(tmem, umma_desc(aV + 2 * ks * KLBO, SBO_K16), umma_desc(bK + (4 + 2 * ks) * KLBO, SBO_K32), i2, 1);
+            }
 #pragma unroll
             for (int tt = 0; tt < L; tt++) u[tt] += u2[tt], yv[tt] += y2[tt];
             if (live) {
@@ -498,10 +508,7 @@ __global__ void __launch_bounds__(NT, 1)
             tc_fence_after();
             if (tid == 0) {
                 const uint32_t i2 = idesc_tf32(64, 64);
-                const uint32_t aU = smem_u32(sm.UTA), aV = smem_u32(stg.VT), bK = smem_u32(stg.BK);
-#pragma unroll
-                for (int ks = 0; ks < 2; ks++)
-                    umma(tmem, umma_desc(aV + 2 * ks * KLBO, SBO_K16), umma_desc(bK + (4 + 2 * ks) * KLBO, SBO_K32), i2, 1);
+                const uint32_t aU = smem_u32(sm.UTA), bK = smem_u32(stg.BK);
 #pragma unroll
                 for (int ks = 0; ks < 2; ks++)
                     umma(tmem, umma_desc(aU + 2 * ks * KLBO, SBO_K16), umma_desc(bK + 2 * ks * KLBO, SBO_K32), i2, 1);

@@ -9,7 +9,7 @@ its own batch (data-parallel replicas, no collective on the data path); `value`
 is the tokens all ranks processed per second (weak scaling).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload prefill|wkv_fwd|wkv_bwd|decode|moe]
+                    [--workload prefill|wkv_fwd|wkv_bwd|decode|moe|moe_full]
 
 Multi-GPU: launched by torch.distributed.run (RANK/LOCAL_RANK/WORLD_SIZE from the
 environment).  `--impl reference` times the CPU restatement of the reference
@@ -407,6 +407,60 @@ def run_moe(args, ws, rank, dev):
             "clocks": clocks}
 
 
+def run_moe_full(args, ws, rank, dev):
+    """One full-expert MoE ChannelMix layer (MoE_CMix, moe.py:170-242) at the config-4
+    shapes: D=768, hidden 3072, E=8 full experts, top-2, 65536 tokens per GPU, per-expert
+    logit bias N(0, 1.5); experts replicated on every rank (no collective)."""
+    from rwkv_mlx_b200 import _native
+    from rwkv_mlx_b200.model import RWKVConfig
+    from rwkv_mlx_b200.moe import MoE_CMix
+
+    ntok, C, F, E, k = args.moe_tokens, 768, 3072, 8, 2
+    g = torch.Generator(device=dev).manual_seed(7 + rank)
+    gw = torch.Generator(device=dev).manual_seed(7)
+    with torch.device(dev):
+        layer = MoE_CMix(RWKVConfig(n_embd=C, dim_ffn=F), 1, E, k)
+    with torch.no_grad():
+        layer.x_k.uniform_(0, 1, generator=gw)
+        layer.expert_key.normal_(0, C ** -0.5, generator=gw)
+        layer.expert_val.normal_(0, F ** -0.5, generator=gw)
+        layer.router.gate.weight.normal_(0, C ** -0.5, generator=gw)
+    layer = layer.half()
+    layer.router.bias = torch.randn(E, device=dev, generator=gw) * 1.5
+    seq = 4096
+    x = torch.randn(ntok // seq, seq, C, device=dev, generator=g).half()
+
+    def step():
+        with torch.no_grad():
+            return layer(x)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    l0 = _native.launch_count
+    barrier(ws)
+    clk = ClockSampler(dev)
+    ms = cuda_timed(step, args.steps)
+    clocks = clk.stop()
+    launches = _native.launch_count - l0
+    ms = max_over_ranks(ms, ws)
+    _, tflops, src = peaks()
+    flop = ntok * k * 4 * C * F  # two products of 2*C*F flops per routed (token, expert)
+    achieved = flop / (ms / 1e3) / 1e12
+    return {"metric": "full-expert MoE ChannelMix tok/s", "value": ntok * ws / (ms / 1e3), "unit": "tok/s",
+            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp16 (fp32 router, fp32 accumulate)",
+            "data": "synthetic",
+            "config": {"workload": "MoE_CMix D768 F3072 E8 top2, config-4 shapes", "tokens_per_gpu": ntok,
+                       "parallelism": f"dp{ws} (experts replicated)",
+                       "l2": "x, routed rows and key activations (0.8 GB) larger than L2"},
+            "gpu_launches": launches,
+            "roofline": {"kernel": "whole layer (expert GEMMs on cuBLAS dominate)", "bound": "tensor",
+                         "achieved": achieved, "peak": tflops, "unit": "TFLOP/s", "frac": achieved / tflops,
+                         "traffic": None, "algorithmic_flop": flop, "peak_source": src},
+            "clocks": clocks}
+
+
 def run_decode(args, ws, rank, dev):
     """Batched RNN-mode decode: L12 D768, 256 sequences per GPU whose
     state comes from a 512-token GPT-mode prefill, greedy steps; tok/s over all ranks."""
@@ -473,7 +527,8 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="prefill", choices=["prefill", "wkv_fwd", "wkv_bwd", "moe", "decode"])
+    ap.add_argument("--workload", default="prefill",
+                    choices=["prefill", "wkv_fwd", "wkv_bwd", "moe", "moe_full", "decode"])
     ap.add_argument("--moe-tokens", type=int, default=65536)
     ap.add_argument("--ep", action="store_true", help="moe workload: expert-parallel over the ranks")
     ap.add_argument("--decode-seqs", type=int, default=256)
@@ -504,6 +559,8 @@ def main():
         line = run_prefill(args, ws, rank, dev)
     elif args.workload == "moe":
         line = run_moe(args, ws, rank, dev)
+    elif args.workload == "moe_full":
+        line = run_moe_full(args, ws, rank, dev)
     elif args.workload == "decode":
         line = run_decode(args, ws, rank, dev)
     else:

@@ -218,6 +218,20 @@ int rwkv_moe_combine_rows(const void* base, const void* rows, const void* scores
                           const int32_t* inv, void* out, int ntok, int C, int topk, int dtype,
                           void* stream);
 
+/* Full-expert dispatch (MoE_CMix.__call__, moe.py:231-236, replaces the per-expert
+ * token shift and lerp of the dense loop): for sorted position p (rwkv_moe_permute)
+ * with tok = perm[p] / topk and e its expert (offsets),
+ *   rows[p] = x[tok] + (x_prev - x[tok]) * x_k[e]
+ * x_prev = x[tok - 1] inside a sequence of T tokens, prev[tok / T] for the first token
+ * of a sequence (prev NULL: zeros, the reference's _time_shift; T = 1 with prev =
+ * the stored previous token gives RNN mode).  x (ntok, C), prev (ntok / T, C),
+ * x_k (E, C), rows (n = ntok * topk, C), all in dtype, 16-byte aligned,
+ * C * sizeof(dtype) % 16 == 0.
+ * The expert products then run on rows [offsets[e], offsets[e+1]). */
+int rwkv_moe_expert_mix_rows(const void* x, const void* prev, const void* x_k,
+                             const int32_t* perm, const int32_t* offsets, void* rows, int n,
+                             int T, int C, int topk, int E, int dtype, void* stream);
+
 /* sum_{i<j} ||A_i^T A_j||_F^2 over the expert down-projections
  * (LoRAMoE_CMix.orthogonal_loss, moe.py:149-163).  A (E, C, R) dtype;
  * out: one fp32 scalar.  R <= 64.                                          */

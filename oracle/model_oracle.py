@@ -5,7 +5,8 @@ may use this.  It restates rwkv_mlx/model.py with torch CPU tensors:
 
   * ``forward``      : RWKV.__call__ (model.py:346-375) -> (logits, aux_loss), with
                        Block (:312-327), RWKV_Tmix_x070 (:182-240), RWKV_CMix_x070
-                       (:259-263) and LoRAMoE_CMix (moe.py:129-147)
+                       (:259-263), LoRAMoE_CMix (moe.py:129-147) and MoE_CMix
+                       (moe.py:226-242)
   * ``forward_rnn``  : RWKV.forward_rnn (model.py:377-421) with _time_mixing_rnn
                        (:441-495) and _channel_mixing_rnn (:498-506)
 
@@ -107,6 +108,15 @@ def _lora_moe(p, pre, x, cfg):
     return out, aux, z, ortho
 
 
+def _full_moe(p, pre, x, cfg):
+    B, T, C = x.shape
+    xn = x.reshape(B * T, C).double().numpy()
+    inds, scores, aux, z, _ = moe_oracle.router(xn, p[pre + "router.gate.weight"].numpy(), cfg.moe_top_k)
+    out = moe_oracle.full_moe(x.double().numpy(), p[pre + "x_k"].double().numpy(), p[pre + "expert_key"].double().numpy(),
+                              p[pre + "expert_val"].double().numpy(), inds.reshape(B, T, -1), scores.reshape(B, T, -1))
+    return torch.from_numpy(out).to(x.dtype), aux, z, 0.0  # no orthogonality loss (moe.py:241-242)
+
+
 def _is_moe(cfg, i):
     return cfg.moe_num_experts > 0 and (not cfg.moe_layers or i in cfg.moe_layers)
 
@@ -127,7 +137,8 @@ def forward(p, cfg, idx, wkv="port", dtype=torch.float32):
         x = x + xa
         x2 = _ln(x, p[pre + "ln2.weight"], p[pre + "ln2.bias"])
         if _is_moe(cfg, i):
-            out, aux, z, ortho = _lora_moe(p, pre + "ffn.", x2, cfg)
+            moe = _lora_moe if getattr(cfg, "moe_mode", "lora") == "lora" else _full_moe
+            out, aux, z, ortho = moe(p, pre + "ffn.", x2, cfg)
             aux_total += cfg.moe_aux_loss_coeff * aux + cfg.moe_z_loss_coeff * z + cfg.moe_ortho_coeff * ortho
             x = x + out
         else:

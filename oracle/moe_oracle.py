@@ -8,6 +8,11 @@ Restates rwkv_mlx/moe.py in numpy (float64 unless stated):
   * ``lora_moe``        : LoRAMoE_CMix.__call__ delta (moe.py:129-147), dense over
                           experts exactly as the reference loops
   * ``orthogonal_loss`` : LoRAMoE_CMix.orthogonal_loss (moe.py:149-163)
+  * ``full_moe``        : MoE_CMix.__call__ output (moe.py:226-242), dense over the
+                          E full experts exactly as the reference loops
+  * ``full_moe_step``   : one RNN-mode token through the same experts (the
+                          reference's forward_rnn has no MoE branch; this applies
+                          _channel_mixing_rnn, model.py:498-506, per expert)
   * ``cmix``            : RWKV_CMix_x070.__call__ (model.py:259-263), the frozen base
 
 Pinned against the reference's own moe.py / model.py code by
@@ -94,3 +99,32 @@ def cmix(x, x_k, key_w, value_w):
     kin = x + xx * np.asarray(x_k, np.float64).reshape(1, 1, -1)
     k = np.maximum(kin @ np.asarray(key_w, np.float64).T, 0.0) ** 2
     return k @ np.asarray(value_w, np.float64).T
+
+
+def full_moe(x, x_k, key, val, inds, scores):
+    """MoE_CMix output (moe.py:226-242) for x (B, T, C): per expert e,
+    k_e = x + (shift(x) - x) * x_k[e]; out_e = relu(k_e @ key[e]^T)^2 @ val[e]^T;
+    out = sum_e w_e * out_e with w_e = sum_slots where(inds == e, scores, 0).
+    x_k (E, 1, 1, C), key (E, D, C), val (E, C, D); inds / scores (B, T, k)."""
+    x = np.asarray(x, np.float64)
+    xx = time_shift(x) - x
+    out = np.zeros_like(x)
+    for e in range(key.shape[0]):
+        ke = x + xx * np.asarray(x_k[e], np.float64).reshape(1, 1, -1)
+        ke = np.maximum(ke @ np.asarray(key[e], np.float64).T, 0.0) ** 2
+        oe = ke @ np.asarray(val[e], np.float64).T
+        w_e = np.where(inds == e, scores, 0.0).sum(-1, keepdims=True)
+        out = out + w_e * oe
+    return out
+
+
+def full_moe_step(x, x_prev, x_k, key, val, inds, scores):
+    """One token per row: x, x_prev (n, C); inds / scores (n, k)."""
+    x = np.asarray(x, np.float64)
+    d = np.asarray(x_prev, np.float64) - x
+    out = np.zeros_like(x)
+    for e in range(key.shape[0]):
+        ke = x + d * np.asarray(x_k[e], np.float64).reshape(1, -1)
+        oe = np.maximum(ke @ np.asarray(key[e], np.float64).T, 0.0) ** 2 @ np.asarray(val[e], np.float64).T
+        out = out + np.where(inds == e, scores, 0.0).sum(-1, keepdims=True) * oe
+    return out

@@ -455,6 +455,51 @@ __global__ void __launch_bounds__(256)
     }
 }
 
+// Full-expert dispatch (MoE_CMix, moe.py:231-236): for sorted position p with
+// tok = perm[p] / topk and expert e(p) (from offsets),
+//   rows[p] = x[tok] + (x_prev(tok) - x[tok]) * x_k[e(p)]
+// where x_prev(tok) is the previous token of the same sequence (sequences of T tokens),
+// or prev[tok / T] (NULL: zeros) for the first token.  One warp per row, one 16-byte
+// vector per lane step; fp32 arithmetic, one rounding.
+template <typename T>
+__global__ void __launch_bounds__(256)
+    moe_expert_mix_rows_kernel(const T* __restrict__ x, const T* __restrict__ prev, const T* __restrict__ x_k,
+                               const int32_t* __restrict__ perm, const int32_t* __restrict__ offsets,
+                               T* __restrict__ rows, int n, int T_, int C, int topk, int E) {
+    constexpr int V = 16 / sizeof(T);
+    __shared__ int offs[257];
+    for (int i = threadIdx.x; i <= E; i += blockDim.x) offs[i] = offsets[i];
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nv = C / V;
+    for (int p = blockIdx.x * 8 + warp; p < n; p += gridDim.x * 8) {
+        int e = 0;
+        while (e + 1 < E && offs[e + 1] <= p) e++;
+        const int tok = perm[p] / topk;
+        const T* xr = x + (size_t)tok * C;
+        const T* pr = (tok % T_) ? xr - C : (prev ? prev + (size_t)(tok / T_) * C : nullptr);
+        const T* mr = x_k + (size_t)e * C;
+        T* out = rows + (size_t)p * C;
+        for (int i = lane; i < nv; i += 32) {
+            const uint4 xv = reinterpret_cast<const uint4*>(xr)[i];
+            const uint4 mv = reinterpret_cast<const uint4*>(mr)[i];
+            uint4 pv = make_uint4(0, 0, 0, 0);
+            if (pr) pv = reinterpret_cast<const uint4*>(pr)[i];
+            const T* xe = reinterpret_cast<const T*>(&xv);
+            const T* me = reinterpret_cast<const T*>(&mv);
+            const T* pe = reinterpret_cast<const T*>(&pv);
+            uint4 ov;
+            T* oe = reinterpret_cast<T*>(&ov);
+#pragma unroll
+            for (int q = 0; q < V; q++) {
+                const float xf = to_f32(xe[q]);
+                oe[q] = from_f32<T>(fmaf(to_f32(pe[q]) - xf, to_f32(me[q]), xf));
+            }
+            reinterpret_cast<uint4*>(out)[i] = ov;
+        }
+    }
+}
+
 // y[dst(p)] = h[p] @ B[e(p)], e(p) from offsets, dst(p) = out_index ? out_index[p] : p.
 template <typename T, int R>
 __global__ void __launch_bounds__(256)
@@ -1007,5 +1052,22 @@ extern "C" int rwkv_moe_combine_rows(const void* base, const void* rows, const v
     RWKV_DISPATCH_DTYPE(dtype, T, moe_combine_rows_kernel<T><<<ep_grid(ntok), 256, 0, st>>>(
                                       (const T*)base, (const T*)rows, (const T*)scores, inv, (T*)out,
                                       ntok, C, topk));
+    return check_launch();
+}
+
+extern "C" int rwkv_moe_expert_mix_rows(const void* x, const void* prev, const void* x_k,
+                                        const int32_t* perm, const int32_t* offsets, void* rows,
+                                        int n, int Tseq, int C, int topk, int E, int dtype,
+                                        void* stream) {
+    if (n <= 0 || Tseq <= 0 || C <= 0 || topk <= 0 || E <= 0 || E > 256) return RWKV_ERR_SHAPE;
+    if (!x || !x_k || !perm || !offsets || !rows) return RWKV_ERR_ARG;
+    if (!aligned(x, 16) || !aligned(x_k, 16) || !aligned(rows, 16) || (prev && !aligned(prev, 16)))
+        return RWKV_ERR_ALIGN;
+    cudaStream_t st = (cudaStream_t)stream;
+    RWKV_DISPATCH_DTYPE(dtype, T, {
+        if ((C * (int)sizeof(T)) % 16) return RWKV_ERR_SHAPE;
+        moe_expert_mix_rows_kernel<T><<<ep_grid(n), 256, 0, st>>>((const T*)x, (const T*)prev, (const T*)x_k, perm,
+                                                                  offsets, (T*)rows, n, Tseq, C, topk, E);
+    });
     return check_launch();
 }

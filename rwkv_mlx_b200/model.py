@@ -295,13 +295,16 @@ class Block(nn.Module):
         self.att = RWKV_Tmix_x070(config, layer_id)
         use_moe = config.moe_num_experts > 0 and (not config.moe_layers or layer_id in config.moe_layers)
         if use_moe:
-            if config.moe_mode != "lora":
-                raise NotImplementedError("full-expert MoE_CMix is not implemented")
-            from .moe import LoRAMoE_CMix
-
             self.is_moe = True
-            self.ffn = LoRAMoE_CMix(RWKV_CMix_x070(config, layer_id), config.moe_num_experts,
-                                    config.moe_lora_rank, config.moe_top_k)
+            if config.moe_mode == "lora":
+                from .moe import LoRAMoE_CMix
+
+                self.ffn = LoRAMoE_CMix(RWKV_CMix_x070(config, layer_id), config.moe_num_experts,
+                                        config.moe_lora_rank, config.moe_top_k)
+            else:  # "full": E independent ChannelMix experts (model.py:306-308)
+                from .moe import MoE_CMix
+
+                self.ffn = MoE_CMix(config, layer_id, config.moe_num_experts, config.moe_top_k)
         else:
             self.ffn = RWKV_CMix_x070(config, layer_id)
 
@@ -430,7 +433,9 @@ class RWKV(nn.Module):
             st["att_x_prev"].copy_(xx)
             x = x + out
             xx = blk.ln2(x)
-            if blk.is_moe:
+            if blk.is_moe and not hasattr(blk.ffn, "base"):  # full experts
+                x = x + blk.ffn.forward_rnn(xx, st["ffn_x_prev"])
+            elif blk.is_moe:
                 # the reference's RNN path cannot run MoE layers (model.py:498-506 reads
                 # ffn.x_k / ffn.key); here the LoRA-MoE layer runs on the single token
                 ffn = blk.ffn
@@ -455,7 +460,9 @@ class RWKV(nn.Module):
             out, v_first = blk.att._forward_rnn_fused(xx, st["att_x_prev"], v_first, st["att_state"])
             st["att_x_prev"].copy_(xx)
             x, xx = fz.add_layernorm(x, out, blk.ln2.weight, blk.ln2.bias, blk.ln2.eps)
-            if blk.is_moe:
+            if blk.is_moe and not hasattr(blk.ffn, "base"):  # full experts
+                pending = blk.ffn.forward_rnn(xx, st["ffn_x_prev"])
+            elif blk.is_moe:
                 ffn = blk.ffn
                 pending = ffn.base.forward_rnn_fused(xx, st["ffn_x_prev"]) + _moe_rnn(ffn, xx)
             else:
@@ -589,8 +596,18 @@ def init_weights(model: RWKV, seed: int = 0):
         att.value.weight.copy_(_ortho(att.value.weight.shape, 1.0, gen, dev))
         att.output.weight.zero_()
         att.ln_x.weight.fill_(((1 + lid) / L) ** 0.7)
+        xk = (1.0 - ddd ** ((1.0 - lid / L) ** 4)).view(1, 1, C)
+        if blk.is_moe and not hasattr(blk.ffn, "base"):
+            # full experts: the ChannelMix schedule for every expert's x_k, orthogonal keys
+            # scaled by sqrt(D / C) and zero values as MoE_CMix.__init__ (moe.py:196-215)
+            ffn = blk.ffn
+            ffn.x_k.copy_(xk.expand_as(ffn.x_k[0]).unsqueeze(0).expand_as(ffn.x_k))
+            for e in range(ffn.n_experts):
+                ffn.expert_key[e].copy_(_ortho(ffn.expert_key[e].shape, 1.0, gen, dev))
+            ffn.expert_val.zero_()
+            continue
         ffn = blk.ffn.base if blk.is_moe else blk.ffn
-        ffn.x_k.copy_((1.0 - ddd ** ((1.0 - lid / L) ** 4)).view(1, 1, C))
+        ffn.x_k.copy_(xk)
         ffn.key.weight.copy_(_ortho(ffn.key.weight.shape, 1.0, gen, dev))
         ffn.value.weight.zero_()
     return model

@@ -5,6 +5,8 @@ Reference (rwkv_mlx/moe.py):
     (:35-86)                                              -> :class:`Router`
   * ``LoRAMoE_CMix(base, n_experts, lora_rank, top_k)(x) -> (out, aux, z)`` and
     ``.orthogonal_loss()`` (:93-163)                      -> :class:`LoRAMoE_CMix`
+  * ``MoE_CMix(config, layer_id, n_experts, top_k)(x) -> (out, aux, z)`` and
+    ``.orthogonal_loss()`` (:170-242)                     -> :class:`MoE_CMix`
 
 The reference evaluates every expert densely for every token and masks the
 result (moe.py:138-145).  Here the routed (token, slot) entries are sorted by
@@ -14,15 +16,24 @@ up-projection, score weighting and residual add are fused in one combine pass
 (``rwkv_moe_lora_combine``).  Top-k ties go to the lower expert id; slots are in
 descending logit order (the reference's argpartition leaves both unspecified).
 
+The full-expert ``MoE_CMix`` uses the same sorted dispatch: one kernel builds every
+routed row with its expert's token-shift mix (``rwkv_moe_expert_mix_rows``), the two
+products of each expert run as library GEMMs (cuBLAS) on that expert's contiguous row
+range with the squared ReLU applied in place between them (``rwkv_relu_sq``), and
+``rwkv_moe_combine_rows`` forms the score-weighted sum per token.
+
 These modules compute the forward pass only (no autograd through the kernels).
 """
 
 from __future__ import annotations
 
+import math
+
 import torch
 from torch import nn
 
 from . import _native as nat
+from .fused import relu_sq_
 
 
 def _stream(dev):
@@ -144,6 +155,36 @@ def ortho_loss(A: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def expert_mix_rows(x2d, prev, x_k, perm, offsets, T: int, top_k: int):
+    """rows[p] = x[tok] + (x_prev - x[tok]) * x_k[e(p)] for the sorted routing entries
+    (moe.py:231-233); x_prev from the same sequence of T tokens, else ``prev``."""
+    ntok, C = x2d.shape
+    E = x_k.shape[0]
+    n = perm.numel()
+    rows = torch.empty((n, C), device=x2d.device, dtype=x2d.dtype)
+    xk = x_k.reshape(E, C).to(x2d.dtype).contiguous()
+    prev = None if prev is None else prev.to(x2d.dtype).contiguous()
+    L = nat.lib()
+    with torch.cuda.device(x2d.device):
+        rc = L.rwkv_moe_expert_mix_rows(nat.ptr(x2d), nat.ptr(prev), nat.ptr(xk), nat.ptr(perm), nat.ptr(offsets),
+                                        nat.ptr(rows), n, T, C, top_k, E, nat.dtype_code(x2d), _stream(x2d.device))
+    nat.check(rc, "rwkv_moe_expert_mix_rows")
+    return rows
+
+
+def combine_rows(base2d, rows, scores, inv, ntok: int):
+    """out[t] = base[t] + sum_s scores[t, s] * rows[inv[t * k + s]] (base may be None)."""
+    k = scores.shape[-1]
+    C = rows.shape[1]
+    out = torch.empty((ntok, C), device=rows.device, dtype=rows.dtype)
+    L = nat.lib()
+    with torch.cuda.device(rows.device):
+        rc = L.rwkv_moe_combine_rows(nat.ptr(base2d), nat.ptr(rows), nat.ptr(scores.contiguous()), nat.ptr(inv),
+                                     nat.ptr(out), ntok, C, k, nat.dtype_code(out), _stream(rows.device))
+    nat.check(rc, "rwkv_moe_combine_rows")
+    return out
+
+
 class Router(nn.Module):
     """Token router (moe.py:35-86): linear gate in fp32 -> top-k + aux losses.
 
@@ -199,3 +240,74 @@ class LoRAMoE_CMix(nn.Module):
 
     def orthogonal_loss(self) -> torch.Tensor:
         return ortho_loss(self.lora_A.detach())
+
+
+class MoE_CMix(nn.Module):
+    """Sparse MoE ChannelMix with E full experts and top-k routing (moe.py:170-242).
+
+    Each expert is a ChannelMix (token shift -> lerp with its own ``x_k`` -> key ->
+    squared ReLU -> value); out = sum over the selected experts of score * expert(x).
+    Parameter names, shapes and init follow the reference: ``router.gate.weight``
+    (E, C), ``x_k`` (E, 1, 1, C) zeros, ``expert_key`` (E, D, C) orthogonal scaled by
+    sqrt(D / C), ``expert_val`` (E, C, D) zeros.  The reference evaluates every expert
+    for every token (moe.py:230-239); here only the routed (token, expert) rows are
+    computed (see the module docstring)."""
+
+    def __init__(self, config, layer_id: int, n_experts: int, top_k: int = 2):
+        super().__init__()
+        self.n_experts, self.top_k, self.layer_id = n_experts, top_k, layer_id
+        C, D = config.n_embd, config.dim_ffn
+        self.router = Router(C, n_experts, top_k)
+        self.x_k = nn.Parameter(torch.zeros(n_experts, 1, 1, C))
+        key = []
+        for _ in range(n_experts):
+            q, _ = torch.linalg.qr(torch.randn(D, C) if D >= C else torch.randn(C, D))
+            q = q if D >= C else q.T
+            key.append(q[:D, :C] * math.sqrt(D / C))
+        self.expert_key = nn.Parameter(torch.stack(key))
+        self.expert_val = nn.Parameter(torch.zeros(n_experts, C, D))
+
+    def _experts(self, x2d: torch.Tensor, prev, T: int):
+        """(ntok, C) tokens in sequences of T (prev: the token before each sequence,
+        or None) -> (out (ntok, C), router result)."""
+        ntok, C = x2d.shape
+        E, k = self.n_experts, self.top_k
+        D = self.expert_key.shape[1]
+        dt = x2d.dtype
+        r = router_forward(x2d, self.router.gate.weight, k, self.router.bias)
+        perm, inv, offsets = permute(r["inds"], E)
+        rows = expert_mix_rows(x2d, prev, self.x_k.detach(), perm, offsets, T, k)
+        # one device -> host read of the E+1 offsets: the library GEMMs below are sized
+        # on the host, one pair per expert over its contiguous rows
+        offs = offsets.tolist()
+        wk = self.expert_key.detach().to(dt)
+        wv = self.expert_val.detach().to(dt)
+        h = torch.empty((rows.shape[0], D), device=x2d.device, dtype=dt)
+        o = torch.empty_like(rows)
+        for e in range(E):
+            a, b = offs[e], offs[e + 1]
+            if b > a:
+                torch.mm(rows[a:b], wk[e].t(), out=h[a:b])
+        relu_sq_(h)
+        for e in range(E):
+            a, b = offs[e], offs[e + 1]
+            if b > a:
+                torch.mm(h[a:b], wv[e].t(), out=o[a:b])
+        return combine_rows(None, o, r["scores"], inv, ntok), r
+
+    def forward(self, x: torch.Tensor):
+        """x (B, T, C) -> (out (B, T, C), aux_loss, z_loss)  (moe.py:224-239)."""
+        B, T, C = x.shape
+        out, r = self._experts(x.reshape(B * T, C).contiguous(), None, T)
+        return out.reshape(B, T, C), r["aux"], r["z"]
+
+    def forward_rnn(self, x: torch.Tensor, x_prev: torch.Tensor) -> torch.Tensor:
+        """One token per sequence: x, x_prev (Bs, C) -> (Bs, C).  The reference's RNN
+        mode has no MoE branch; this is the ChannelMix RNN step (model.py:498-506) per
+        selected expert, weighted like the GPT-mode output."""
+        out, _ = self._experts(x.contiguous(), x_prev, 1)
+        return out
+
+    def orthogonal_loss(self) -> torch.Tensor:
+        """No orthogonality loss for full experts (moe.py:241-242)."""
+        return torch.zeros((), device=self.x_k.device, dtype=torch.float32)

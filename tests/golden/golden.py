@@ -38,8 +38,10 @@ def model_params(prefix, seed):
     return P
 
 
-def tiny_config(moe=False):
+def tiny_config(moe=False, full=False):
     kw = dict(n_layer=2, n_embd=128, vocab_size=256, dim_ffn=256)
     if moe:
         kw.update(moe_num_experts=4, moe_top_k=2, moe_lora_rank=8)
+    if full:
+        kw.update(moe_num_experts=4, moe_top_k=2, moe_mode="full")
     return kw

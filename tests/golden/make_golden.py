@@ -172,6 +172,32 @@ def main():
     logits2, aux2 = m2(idx2)
     G["modelmoe_idx"], G["modelmoe_logits"], G["modelmoe_aux"] = idx2, logits2, np.array(aux2)
 
+    # ---- full-expert MoE_CMix (moe.py:170-242) ----
+    fcfg = ref_model.RWKVConfig(n_layer=2, n_embd=64, dim_ffn=128)
+    fm = ref_moe.MoE_CMix(fcfg, 1, n_experts=4, top_k=2)
+    fm.x_k = rng.uniform(0, 1, (4, 1, 1, 64)).astype(np.float32)
+    fm.expert_key = (rng.standard_normal((4, 128, 64)) / 8).astype(np.float32)
+    fm.expert_val = (rng.standard_normal((4, 64, 128)) / 11).astype(np.float32)
+    fm.router.gate.weight = (rng.standard_normal((4, 64)) * 0.3).astype(np.float32)
+    xf = rng.standard_normal((2, 24, 64)).astype(np.float32)
+    outf, auxf, zf = fm(xf)
+    G.update(fullmoe_xk=fm.x_k, fullmoe_key=fm.expert_key, fullmoe_val=fm.expert_val,
+             fullmoe_gate=fm.router.gate.weight, fullmoe_x=xf, fullmoe_out=outf,
+             fullmoe_aux=np.array(auxf), fullmoe_z=np.array(zf))
+
+    # ---- tiny model with full-expert MoE in every layer ----
+    cfg3 = ref_model.RWKVConfig(n_layer=2, n_embd=128, vocab_size=256, dim_ffn=256, moe_num_experts=4,
+                                moe_top_k=2, moe_mode="full")
+    m3 = ref_model.RWKV(cfg3)
+    spec3 = spec_of(m3, nn)
+    P3 = random_params(spec3, seed=5)
+    set_params(m3, P3)
+    G["modelfull_spec_names"], G["modelfull_spec_shapes"] = spec_arrays(spec3)
+    G["modelfull_params_sha256"] = params_sha256(P3)
+    idx3 = rng.integers(0, 256, (2, 24)).astype(np.int32)
+    logits3, aux3 = m3(idx3)
+    G["modelfull_idx"], G["modelfull_logits"], G["modelfull_aux"] = idx3, logits3, np.array(aux3)
+
     out_path = HERE / "reference_golden.npz"
     np.savez_compressed(out_path, **{k: np.asarray(v) for k, v in G.items()})
     print(f"wrote {out_path} ({out_path.stat().st_size / 1e6:.2f} MB, {len(G)} arrays)")

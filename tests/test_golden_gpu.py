@@ -49,10 +49,10 @@ def test_wkv_fp16_matches_reference_kernel():
         assert rel_rms(g.double().cpu().numpy(), G["wkv_h_" + n].astype(np.float64)) < 3e-3, n
 
 
-def _model(prefix, seed, moe=False):
+def _model(prefix, seed, moe=False, full=False):
     from rwkv_mlx_b200.model import RWKV, RWKVConfig
 
-    cfg = RWKVConfig(**tiny_config(moe))
+    cfg = RWKVConfig(**tiny_config(moe, full))
     m = RWKV(cfg).cuda()
     P = model_params(prefix, seed)
     sd = m.state_dict()
@@ -128,3 +128,31 @@ def test_model_with_lora_moe_matches_reference():
         logits, aux = m(_dev(G["modelmoe_idx"], torch.long))
     assert rel_rms(logits.cpu().numpy(), G["modelmoe_logits"]) < 2e-3
     assert abs(float(aux) - float(G["modelmoe_aux"])) < 1e-4 * max(1.0, abs(float(G["modelmoe_aux"])))
+
+
+def test_full_expert_moe_matches_reference():
+    """MoE_CMix (moe.py:170-242) on the reference module's own output."""
+    from rwkv_mlx_b200.model import RWKVConfig
+    from rwkv_mlx_b200.moe import MoE_CMix
+
+    G = golden()
+    fm = MoE_CMix(RWKVConfig(n_layer=2, n_embd=64, dim_ffn=128), 1, 4, 2).cuda()
+    with torch.no_grad():
+        fm.x_k.copy_(_dev(G["fullmoe_xk"]))
+        fm.expert_key.copy_(_dev(G["fullmoe_key"]))
+        fm.expert_val.copy_(_dev(G["fullmoe_val"]))
+        fm.router.gate.weight.copy_(_dev(G["fullmoe_gate"]))
+        out, aux, z = fm(_dev(G["fullmoe_x"]))
+        ortho = fm.orthogonal_loss()
+    assert rel_rms(out.cpu().numpy(), G["fullmoe_out"]) < 1e-4
+    assert abs(float(aux) - float(G["fullmoe_aux"])) < 1e-5 and abs(float(z) - float(G["fullmoe_z"])) < 1e-4
+    assert float(ortho) == 0.0
+
+
+def test_model_with_full_expert_moe_matches_reference():
+    G = golden()
+    cfg, m = _model("modelfull", 5, full=True)
+    with torch.no_grad():
+        logits, aux = m(_dev(G["modelfull_idx"], torch.long))
+    assert rel_rms(logits.cpu().numpy(), G["modelfull_logits"]) < 2e-3
+    assert abs(float(aux) - float(G["modelfull_aux"])) < 1e-4 * max(1.0, abs(float(G["modelfull_aux"])))

@@ -93,3 +93,26 @@ def test_model_with_lora_moe():
                                        dtype=torch.float64)
     assert rel_rms(logits.numpy(), G["modelmoe_logits"]) < 1e-5
     assert abs(aux - float(G["modelmoe_aux"])) < 1e-5 * max(1.0, abs(aux))
+
+
+def test_full_expert_moe():
+    """MoE_CMix (moe.py:226-242): the dense expert loop of the oracle against the
+    reference module's own output."""
+    G = golden()
+    x = G["fullmoe_x"].astype(np.float64)
+    lg = moe_oracle.gate_logits(x.reshape(-1, 64), G["fullmoe_gate"])
+    inds, scores, aux, z, _ = moe_oracle.router(None, None, 2, logits=lg)
+    out = moe_oracle.full_moe(x, G["fullmoe_xk"], G["fullmoe_key"], G["fullmoe_val"], inds.reshape(2, 24, 2),
+                              scores.reshape(2, 24, 2))
+    assert rel_rms(out, G["fullmoe_out"]) < 1e-5
+    assert abs(aux - float(G["fullmoe_aux"])) < 1e-5 and abs(z - float(G["fullmoe_z"])) < 1e-4
+
+
+def test_model_with_full_expert_moe():
+    G = golden()
+    cfg = RWKVConfig(**tiny_config(full=True))
+    P = _sd(model_params("modelfull", seed=5))
+    logits, aux = model_oracle.forward(P, cfg, torch.tensor(G["modelfull_idx"]).long(), wkv="exact",
+                                       dtype=torch.float64)
+    assert rel_rms(logits.numpy(), G["modelfull_logits"]) < 1e-5
+    assert abs(aux - float(G["modelfull_aux"])) < 1e-5 * max(1.0, abs(aux))

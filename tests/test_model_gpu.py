@@ -14,12 +14,14 @@ from tests.inputs import rel_rms
 pytestmark = pytest.mark.gpu
 
 
-def _tiny(moe=False, groupnorm="mlx"):
+def _tiny(moe=False, groupnorm="mlx", full=False):
     from rwkv_mlx_b200.model import RWKV, RWKVConfig, init_weights
 
     kw = dict(n_layer=2, n_embd=128, vocab_size=512, dim_ffn=256, groupnorm=groupnorm)
     if moe:
         kw.update(moe_num_experts=4, moe_top_k=2, moe_lora_rank=8)
+    if full:
+        kw.update(moe_num_experts=4, moe_top_k=2, moe_mode="full")
     cfg = RWKVConfig(**kw)
     torch.manual_seed(0)
     m = RWKV(cfg).cuda()
@@ -58,6 +60,16 @@ def test_gpt_forward_with_lora_moe_matches_cpu_restatement():
     assert abs(float(aux) - aux_r) < 1e-4 * max(1.0, abs(aux_r))
 
 
+def test_gpt_forward_with_full_expert_moe_matches_cpu_restatement():
+    cfg, m = _tiny(full=True)
+    idx = torch.randint(0, cfg.vocab_size, (2, 32), device="cuda")
+    with torch.no_grad():
+        logits, aux = m(idx)
+    ref, aux_r = mo.forward(_sd(m), cfg, idx.cpu(), wkv="exact", dtype=torch.float64)
+    assert rel_rms(logits.double().cpu().numpy(), ref.numpy()) < 2e-3
+    assert abs(float(aux) - aux_r) < 1e-4 * max(1.0, abs(aux_r))
+
+
 def test_rnn_mode_matches_cpu_restatement():
     cfg, m = _tiny()
     st_g = m.init_state()
@@ -70,10 +82,11 @@ def test_rnn_mode_matches_cpu_restatement():
         assert rel_rms(lg.double().cpu().numpy(), lc.numpy()) < 1e-4
 
 
-def test_prefill_state_then_decode_equals_gpt_forward():
+@pytest.mark.parametrize("moe", ["none", "lora", "full"])
+def test_prefill_state_then_decode_equals_gpt_forward(moe):
     """Prefill 24 tokens in GPT mode with state output, decode 6 more in RNN mode
     (batched): logits equal a GPT-mode pass over all 30 tokens."""
-    cfg, m = _tiny()
+    cfg, m = _tiny(moe=moe == "lora", full=moe == "full")
     idx = torch.randint(0, cfg.vocab_size, (3, 30), device="cuda")
     with torch.no_grad():
         full, _ = m(idx)

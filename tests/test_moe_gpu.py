@@ -211,3 +211,67 @@ def test_lora_moe_cmix_unsupported_shape_uses_sorted_dispatch():
     ref = mo.cmix(xn, npy(base.x_k), npy(base.key.weight), npy(base.value.weight)) + mo.lora_moe_delta(
         xn, npy(m.lora_A), npy(m.lora_B), inds.reshape(2, 40, 2), sc.reshape(2, 40, 2))
     assert rel_rms(out.double().cpu().numpy(), ref) < 3e-3
+
+
+def _full_moe(C, D, E, k, dt, seed):
+    from rwkv_mlx_b200.model import RWKVConfig
+    from rwkv_mlx_b200.moe import MoE_CMix
+
+    torch.manual_seed(seed)
+    fm = MoE_CMix(RWKVConfig(n_layer=2, n_embd=C, dim_ffn=D), 1, E, k).cuda()
+    rng = np.random.default_rng(seed)
+    with torch.no_grad():
+        fm.x_k.copy_(torch.tensor(rng.uniform(0, 1, (E, 1, 1, C))))
+        fm.expert_key.copy_(torch.tensor(rng.standard_normal((E, D, C)) / np.sqrt(C)))
+        fm.expert_val.copy_(torch.tensor(rng.standard_normal((E, C, D)) / np.sqrt(D)))
+        fm.router.gate.weight.copy_(torch.tensor(rng.standard_normal((E, C)) * 0.05))
+    return fm.to(dt)
+
+
+def _full_moe_oracle(fm, x, inds, scores):
+    g = lambda t: t.detach().double().cpu().numpy()
+    return mo.full_moe(g(x), g(fm.x_k), g(fm.expert_key), g(fm.expert_val), inds, scores)
+
+
+# float tolerance, relative to RMS: every intermediate (mixed rows, key activations,
+# their squares, expert outputs) is rounded to the activation dtype once
+_TOL = {torch.float16: 4e-3, torch.bfloat16: 3e-2, torch.float32: 1e-4}
+
+
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("B,T,C,D,E,k", [(2, 300, 256, 512, 4, 2), (3, 77, 128, 384, 8, 1), (1, 1, 64, 128, 5, 3),
+                                         (4, 129, 768, 3072, 8, 2)])
+def test_full_moe_cmix_matches_oracle(dt, B, T, C, D, E, k):
+    """MoE_CMix on the sorted dispatch vs the reference's dense expert loop (moe.py:226-239),
+    the oracle routed with the GPU's own fp32 logits (identical inputs on both sides)."""
+    from rwkv_mlx_b200.moe import router_forward
+
+    fm = _full_moe(C, D, E, k, dt, seed=B * 1000 + T)
+    x = _x(B * T, C, seed=T, dt=dt).view(B, T, C)
+    with torch.no_grad():
+        out, aux, z = fm(x)
+        r = router_forward(x.view(B * T, C), fm.router.gate.weight, k, want_logits=True)
+    torch.cuda.synchronize()
+    inds, scores, aux_o, z_o, _ = mo.router(None, None, k, logits=r["logits"].cpu().numpy())
+    np.testing.assert_array_equal(r["inds"].cpu().numpy(), inds)
+    ref = _full_moe_oracle(fm, x, inds.reshape(B, T, k), r["scores"].double().cpu().numpy().reshape(B, T, k))
+    assert rel_rms(out.double().cpu().numpy(), ref) < _TOL[dt]
+    assert abs(float(aux) - aux_o) < 1e-4 and abs(float(z) - z_o) < 1e-3 * max(1.0, z_o)
+
+
+def test_full_moe_cmix_rnn_step_matches_oracle():
+    """One token per sequence with the stored previous token (RNN mode)."""
+    from rwkv_mlx_b200.moe import router_forward
+
+    Bs, C, D, E, k = 37, 256, 512, 8, 2
+    fm = _full_moe(C, D, E, k, torch.float16, seed=11)
+    x, xp = _x(Bs, C, seed=1), _x(Bs, C, seed=2)
+    with torch.no_grad():
+        out = fm.forward_rnn(x, xp)
+        r = router_forward(x, fm.router.gate.weight, k, want_logits=True)
+    torch.cuda.synchronize()
+    inds, _, _, _, _ = mo.router(None, None, k, logits=r["logits"].cpu().numpy())
+    g = lambda t: t.detach().double().cpu().numpy()
+    ref = mo.full_moe_step(g(x), g(xp), g(fm.x_k), g(fm.expert_key), g(fm.expert_val), inds,
+                           r["scores"].double().cpu().numpy())
+    assert rel_rms(out.double().cpu().numpy(), ref) < _TOL[torch.float16]

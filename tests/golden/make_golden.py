@@ -18,7 +18,13 @@ Cases (all seeded):
   router_*   Router(64, 8, 2) on x (2, 16, 64).
   moe_*      LoRAMoE_CMix(base C=64 F=128, E=8, r=16, k=2) forward + orthogonal_loss.
   model_*    RWKV L2 D128 (vocab 256, ffn 256): GPT-mode logits (B=2, T=32) and six
-             RNN-mode steps; modelmoe_* the same model with LoRA-MoE in every layer.
+             RNN-mode steps; modelmoe_* the same model with LoRA-MoE in every layer,
+             modelfull_* with full-expert MoE_CMix in every layer.
+  fullmoe_*  MoE_CMix(C=64, F=128, E=4, k=2) forward.
+  loss_*     l2_wrap_loss and l2_wrap_loss_masked (train.py:317-362).
+  conv_*     convert_pytorch_to_mlx (convert.py:16-141) on a PyTorch-layout state dict of
+             the tiny model: names, shapes, dtypes and SHA-256 of every converted tensor,
+             and the inferred config.
              Model parameters are drawn by tests/golden/params.py from the stored
              (name, shape) spec and seed; their SHA-256 is stored.
 """
@@ -60,6 +66,12 @@ def set_params(model, params):
         old = getattr(obj, parts[-1])
         assert old.shape == val.shape, (name, old.shape, val.shape)
         setattr(obj, parts[-1], val.astype(np.float32))
+
+
+def ref_mx_load(path):
+    import mlx.core as mx
+
+    return mx.load(path)
 
 
 def spec_of(model, nn):
@@ -197,6 +209,39 @@ def main():
     idx3 = rng.integers(0, 256, (2, 24)).astype(np.int32)
     logits3, aux3 = m3(idx3)
     G["modelfull_idx"], G["modelfull_logits"], G["modelfull_aux"] = idx3, logits3, np.array(aux3)
+
+    # ---- loss: l2_wrap_loss / l2_wrap_loss_masked (train.py:317-362) ----
+    from rwkv_mlx import train as ref_train
+
+    lg = (3 * rng.standard_normal((2, 12, 50))).astype(np.float32)
+    tg = rng.integers(0, 50, (2, 12)).astype(np.int32)
+    mk = (rng.uniform(0, 1, (2, 12)) < 0.6).astype(np.float32)
+    G.update(loss_logits=lg, loss_targets=tg, loss_mask=mk,
+             loss_l2wrap=np.array(ref_train.l2_wrap_loss(lg, tg)),
+             loss_l2wrap_masked=np.array(ref_train.l2_wrap_loss_masked(lg, tg, mk)))
+
+    # ---- checkpoint conversion: convert_pytorch_to_mlx (convert.py:16-141) on a
+    # PyTorch-layout state dict (1-D mixing vectors, no layer-0 v0/v1/v2) ----
+    import json
+    import tempfile
+
+    import torch
+
+    from rwkv_mlx import convert as ref_convert
+    from tests.golden.params import pth_state_dict
+
+    sd = pth_state_dict(spec, seed=6)
+    with tempfile.TemporaryDirectory() as td:
+        torch.save(sd, f"{td}/m.pth")
+        conf = ref_convert.convert_pytorch_to_mlx(f"{td}/m.pth", f"{td}/out", "float16")
+        conv = ref_mx_load(f"{td}/out/model.safetensors")
+    names = sorted(conv)
+    G["conv_names"] = np.array(names)
+    G["conv_shapes"] = np.array([list(conv[n].shape) + [-1] * (4 - conv[n].ndim) for n in names], np.int64)
+    G["conv_dtypes"] = np.array([str(conv[n].dtype) for n in names])
+    G["conv_sha256"] = np.stack([np.frombuffer(hashlib.sha256(np.ascontiguousarray(conv[n]).tobytes()).digest(),
+                                               np.uint8) for n in names])
+    G["conv_config"] = np.array(json.dumps(conf, sort_keys=True))
 
     out_path = HERE / "reference_golden.npz"
     np.savez_compressed(out_path, **{k: np.asarray(v) for k, v in G.items()})

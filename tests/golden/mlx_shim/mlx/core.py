@@ -63,6 +63,18 @@ def take_along_axis(a, idx, axis):
     return np.take_along_axis(a, idx.astype(np.int64), axis=axis)
 
 
+def save_safetensors(path, arrays):
+    from safetensors.numpy import save_file
+
+    save_file({k: np.ascontiguousarray(v) for k, v in arrays.items()}, str(path))
+
+
+def load(path):
+    from safetensors.numpy import load_file
+
+    return load_file(str(path))
+
+
 def stop_gradient(x):
     return x
 

@@ -73,3 +73,22 @@ def softplus(x):
 
 def relu(x):
     return np.maximum(x, 0)
+
+
+class losses:
+    """mlx.nn.losses subset."""
+
+    @staticmethod
+    def cross_entropy(logits, targets, reduction="none"):
+        """-log softmax(logits)[target] per row (MLX's documented definition, class
+        axis last), then the reduction ("none" | "mean" | "sum")."""
+        lg = np.asarray(logits, np.float64)
+        m = lg.max(axis=-1, keepdims=True)
+        lse = (m + np.log(np.exp(lg - m).sum(axis=-1, keepdims=True)))[..., 0]
+        tgt = np.take_along_axis(lg, np.asarray(targets).astype(np.int64)[..., None], axis=-1)[..., 0]
+        loss = (lse - tgt).astype(np.asarray(logits).dtype)
+        if reduction == "mean":
+            return loss.mean()
+        if reduction == "sum":
+            return loss.sum()
+        return loss

@@ -58,3 +58,23 @@ def spec_arrays(spec):
 
 def spec_from_arrays(names, shapes):
     return [(str(n), tuple(int(x) for x in s if x >= 0)) for n, s in zip(names, shapes)]
+
+
+RESHAPE_1D = {"x_r", "x_w", "x_k", "x_v", "x_a", "x_g", "w0", "a0", "v0", "k_k", "k_a"}
+
+
+def pth_state_dict(spec, seed):
+    """A PyTorch-layout RWKV-7 state dict for the model spec: the values of
+    random_params(spec, seed), mixing vectors and biases of shape (1, 1, C) stored
+    1-D, and layer 0 without att.v0 / v1 / v2 (the layout convert.py reads)."""
+    import torch
+
+    P = random_params(spec, seed)
+    sd = {}
+    for n, v in P.items():
+        if n in ("blocks.0.att.v0", "blocks.0.att.v1", "blocks.0.att.v2"):
+            continue
+        if n.split(".")[-1] in RESHAPE_1D and v.ndim == 3:
+            v = v.reshape(-1)
+        sd[n] = torch.tensor(v)
+    return sd

@@ -156,3 +156,20 @@ def test_model_with_full_expert_moe_matches_reference():
         logits, aux = m(_dev(G["modelfull_idx"], torch.long))
     assert rel_rms(logits.cpu().numpy(), G["modelfull_logits"]) < 2e-3
     assert abs(float(aux) - float(G["modelfull_aux"])) < 1e-4 * max(1.0, abs(float(G["modelfull_aux"])))
+
+
+def test_converted_pytorch_checkpoint_runs_like_the_reference(tmp_path):
+    """A PyTorch-layout RWKV-7 state dict (1-D mixing vectors, no layer-0 v0/v1/v2) of
+    the golden model goes through the converter and the loader; the loaded model gives
+    the reference model's logits."""
+    from rwkv_mlx_b200 import checkpoint as ck
+    from tests.golden.params import pth_state_dict, spec_from_arrays
+
+    G = golden()
+    sd = pth_state_dict(spec_from_arrays(G["model_spec_names"], G["model_spec_shapes"]), seed=2)
+    torch.save(sd, tmp_path / "m.pth")
+    ck.convert_pth(tmp_path / "m.pth", tmp_path / "out", "float32")
+    m = ck.load_model(tmp_path / "out", device="cuda", dtype=torch.float32).eval()
+    with torch.no_grad():
+        logits, _ = m(_dev(G["model_idx"], torch.long))
+    assert rel_rms(logits.cpu().numpy(), G["model_logits"]) < 2e-3

@@ -279,6 +279,32 @@ int rwkv_add_layernorm(const void* x, const void* delta, const void* w, const vo
                        void* x_out, void* y, long long rows, int C, float eps, int dtype,
                        void* stream);
 
+/* ------------------------------------------------------------------------ */
+/* Training loss (l2_wrap_loss / l2_wrap_loss_masked, train.py:317-362) over
+ * vocabulary chunks, so that a fused head + loss never holds the full logits.
+ *
+ * rwkv_ce_chunk: for token i (row i of `logits`, row stride `ld` elements), the
+ *   columns [col0, col0 + ncols) of the vocabulary: updates the token's state
+ *   float4 {running max m, sum of exp(l - m), target logit, first argmax (int bits)}
+ *   (first != 0 starts it).  targets int32 in [0, V); state 16-byte aligned.
+ * rwkv_ce_finalize: out fp32[4] = {loss, cross-entropy term, L2 term, denominator}:
+ *   loss = sum_i w_i (log s_i + m_i - target logit_i) / den + l2_factor * 0.5 * sum_i m_i^2
+ *   with w = mask (den = sum(mask) + 1e-9, train.py:355-356) or 1 (den = ntok).
+ *   l2_factor = 1e-4 / (B * T) (train.py:332).
+ * rwkv_ce_chunk_grad: d loss / d logits for a chunk times the device scalar *g:
+ *   *g * w_i / den * (softmax_ij - [j = target_i]) + *g * l2_factor * m_i * [j = argmax_i]
+ *   written to dlogits (row stride ld_out), in dtype; with scaled = 0 the values are
+ *   multiplied by den / *g (O(1) entries for 16-bit types; the caller scales the
+ *   products it forms from them by *g / den).                                */
+int rwkv_ce_chunk(const void* logits, long long ld, const int32_t* targets, float* state, int ntok,
+                  int col0, int ncols, int first, int dtype, void* stream);
+int rwkv_ce_finalize(const float* state, const float* mask, float l2_factor, float* out, int ntok,
+                     void* stream);
+int rwkv_ce_chunk_grad(const void* logits, long long ld, const int32_t* targets, const float* state,
+                       const float* mask, const float* out, const float* g, float l2_factor,
+                       int scaled, void* dlogits, long long ld_out, int ntok, int col0, int ncols,
+                       int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -57,6 +57,10 @@ SIGNATURES = {
     "rwkv_moe_lora_up": (_I, [_P] * 5 + [_I] * 5 + [_P]),
     "rwkv_moe_combine_rows": (_I, [_P] * 5 + [_I] * 4 + [_P]),
     "rwkv_moe_expert_mix_rows": (_I, [_P] * 6 + [_I] * 6 + [_P]),
+    "rwkv_ce_chunk": (_I, [_P, ctypes.c_longlong, _P, _P] + [_I] * 5 + [_P]),
+    "rwkv_ce_finalize": (_I, [_P, _P, ctypes.c_float, _P, _I, _P]),
+    "rwkv_ce_chunk_grad": (_I, [_P, ctypes.c_longlong] + [_P] * 5 + [ctypes.c_float, _I, _P, ctypes.c_longlong]
+                           + [_I] * 4 + [_P]),
     "rwkv_lerp": (_I, [_P] * 3 + [_I, ctypes.c_longlong, _I, _I, _I, _P]),
     "rwkv_lerp_prev": (_I, [_P] * 4 + [_I, ctypes.c_longlong, _I, _I, _I, _P]),
     "rwkv_tmix_mid": (_I, [_P] * 16 + [ctypes.c_longlong, _I, _I, _I, _P]),
@@ -106,6 +110,7 @@ KERNELS_PER_CALL = {
     "rwkv_moe_lora_combine": 1, "rwkv_moe_lora_apply": 1, "rwkv_moe_ortho_loss": 1, "rwkv_moe_gather_rows": 1,
     "rwkv_moe_lora_up": 1, "rwkv_moe_combine_rows": 1, "rwkv_lerp": 1, "rwkv_lerp_prev": 1, "rwkv_tmix_mid": 1,
     "rwkv_tmix_post": 1, "rwkv_relu_sq": 1, "rwkv_add_layernorm": 1, "rwkv_moe_expert_mix_rows": 1,
+    "rwkv_ce_chunk": 1, "rwkv_ce_finalize": 1, "rwkv_ce_chunk_grad": 1,
 }
 launch_count = 0
 

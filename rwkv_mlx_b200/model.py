@@ -355,7 +355,7 @@ class RWKV(nn.Module):
         self.ln_out = nn.LayerNorm(config.n_embd)
         self.head = nn.Linear(config.n_embd, config.vocab_size, bias=False)
 
-    def _run(self, idx, return_state=False):
+    def _run(self, idx, return_state=False, head=True):
         x = self.emb(idx)
         v_first = torch.zeros_like(x)
         aux_loss = torch.zeros((), device=x.device, dtype=torch.float32)
@@ -372,7 +372,7 @@ class RWKV(nn.Module):
                 if return_state:
                     states.append(extra)
             _, x = fz.add_layernorm(x, pending, self.ln_out.weight, self.ln_out.bias, self.ln_out.eps)
-            return self.head(x), aux_loss, states
+            return (self.head(x) if head else x), aux_loss, states
         for blk in self.blocks:
             x, v_first, moe, extra = blk(x, v_first, return_state=return_state)
             if moe is not None:
@@ -382,12 +382,22 @@ class RWKV(nn.Module):
             if return_state:
                 states.append(extra)
         x = self.ln_out(x)
-        return self.head(x), aux_loss, states
+        return (self.head(x) if head else x), aux_loss, states
 
     def forward(self, idx):
         """GPT mode: idx (B, T) -> (logits (B, T, V), aux_loss)  (model.py:346-375)."""
         logits, aux, _ = self._run(idx)
         return logits, aux
+
+    def forward_loss(self, idx, targets, mask=None, chunk: int = 8192):
+        """The reference's training objective (train.py:483-489):
+        ``l2_wrap_loss(logits, targets)`` (masked when ``mask`` is given) + the MoE aux
+        loss, with the output head fused into the loss so the (B, T, V) logits are never
+        held (``loss.head_l2_wrap_loss``)."""
+        from .loss import head_l2_wrap_loss
+
+        x, aux, _ = self._run(idx, head=False)
+        return head_l2_wrap_loss(x, self.head.weight, targets, mask, chunk) + aux
 
     def forward_with_state(self, idx):
         """GPT-mode prefill that also returns the RNN state after the last token,

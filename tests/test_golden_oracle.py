@@ -116,3 +116,15 @@ def test_model_with_full_expert_moe():
                                        dtype=torch.float64)
     assert rel_rms(logits.numpy(), G["modelfull_logits"]) < 1e-5
     assert abs(aux - float(G["modelfull_aux"])) < 1e-5 * max(1.0, abs(aux))
+
+
+def test_l2_wrap_losses():
+    """train.py:317-362 restated in torch float64 against the reference functions."""
+    from oracle import loss_oracle
+
+    G = golden()
+    lg = torch.tensor(G["loss_logits"], dtype=torch.float64)
+    tg = torch.tensor(G["loss_targets"])
+    mk = torch.tensor(G["loss_mask"], dtype=torch.float64)
+    assert abs(float(loss_oracle.l2_wrap_loss(lg, tg)) - float(G["loss_l2wrap"])) < 1e-5
+    assert abs(float(loss_oracle.l2_wrap_loss_masked(lg, tg, mk)) - float(G["loss_l2wrap_masked"])) < 1e-5

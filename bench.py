@@ -9,7 +9,7 @@ its own batch (data-parallel replicas, no collective on the data path); `value`
 is the tokens all ranks processed per second (weak scaling).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload prefill|wkv_fwd|wkv_bwd|decode|moe|moe_full]
+                    [--workload prefill|wkv_fwd|wkv_bwd|decode|moe|moe_full|head_loss]
 
 Multi-GPU: launched by torch.distributed.run (RANK/LOCAL_RANK/WORLD_SIZE from the
 environment).  `--impl reference` times the CPU restatement of the reference
@@ -461,6 +461,57 @@ def run_moe_full(args, ws, rank, dev):
             "clocks": clocks}
 
 
+def run_head_loss(args, ws, rank, dev):
+    """Output head + training loss (train.py:317-334, 483-489) at the prefill shapes of
+    hidden states (B=8, T=4096, C=768) fp16, head (65568, 768),
+    uniform-random targets; forward and backward of the fused head + loss (the logits
+    are formed and consumed one 8192-column vocabulary chunk at a time)."""
+    from rwkv_mlx_b200 import _native
+    from rwkv_mlx_b200.loss import head_l2_wrap_loss
+
+    B, T, C, V = args.batch, args.seq, 768, 65568
+    g = torch.Generator(device=dev).manual_seed(11 + rank)
+    x = torch.randn(B, T, C, device=dev, generator=g).half().requires_grad_(True)
+    w = (torch.randn(V, C, device=dev, generator=g) * C ** -0.5).half().requires_grad_(True)
+    tg = torch.randint(0, V, (B, T), device=dev, generator=g)
+
+    def step():
+        x.grad = None
+        w.grad = None
+        loss = head_l2_wrap_loss(x, w, tg)
+        loss.backward()
+        return loss
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    torch.cuda.reset_peak_memory_stats(dev)
+    base_mem = torch.cuda.memory_allocated(dev)
+    l0 = _native.launch_count
+    barrier(ws)
+    clk = ClockSampler(dev)
+    ms = cuda_timed(step, args.steps)
+    clocks = clk.stop()
+    launches = _native.launch_count - l0
+    peak_extra = torch.cuda.max_memory_allocated(dev) - base_mem
+    ms = max_over_ranks(ms, ws)
+    _, tflops, src = peaks()
+    n = B * T
+    flop = 3 * 2 * n * V * C  # logits, d/dx, d/dW (the backward's recomputed logits not credited)
+    achieved = flop / (ms / 1e3) / 1e12
+    return {"metric": "fused head + l2_wrap_loss fwd+bwd tok/s", "value": n * ws / (ms / 1e3), "unit": "tok/s",
+            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp16 (fp32 softmax statistics)", "data": "synthetic",
+            "config": {"workload": f"head+loss B={B} T={T} C={C} V={V}, chunk 8192",
+                       "full_logits_bytes": n * V * 2, "peak_extra_bytes": int(peak_extra),
+                       "l2": "logit chunks (0.5 GB) larger than L2"},
+            "gpu_launches": launches,
+            "roofline": {"kernel": "whole head + loss (GEMMs on cuBLAS dominate)", "bound": "tensor",
+                         "achieved": achieved, "peak": tflops, "unit": "TFLOP/s", "frac": achieved / tflops,
+                         "traffic": None, "algorithmic_flop": flop, "peak_source": src},
+            "clocks": clocks}
+
+
 def run_decode(args, ws, rank, dev):
     """Batched RNN-mode decode: L12 D768, 256 sequences per GPU whose
     state comes from a 512-token GPT-mode prefill, greedy steps; tok/s over all ranks."""
@@ -528,7 +579,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="prefill",
-                    choices=["prefill", "wkv_fwd", "wkv_bwd", "moe", "moe_full", "decode"])
+                    choices=["prefill", "wkv_fwd", "wkv_bwd", "moe", "moe_full", "head_loss", "decode"])
     ap.add_argument("--moe-tokens", type=int, default=65536)
     ap.add_argument("--ep", action="store_true", help="moe workload: expert-parallel over the ranks")
     ap.add_argument("--decode-seqs", type=int, default=256)
@@ -561,6 +612,8 @@ def main():
         line = run_moe(args, ws, rank, dev)
     elif args.workload == "moe_full":
         line = run_moe_full(args, ws, rank, dev)
+    elif args.workload == "head_loss":
+        line = run_head_loss(args, ws, rank, dev)
     elif args.workload == "decode":
         line = run_decode(args, ws, rank, dev)
     else:

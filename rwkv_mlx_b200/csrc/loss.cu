@@ -39,19 +39,42 @@ template <typename T>
 __global__ void __launch_bounds__(WARPS * 32)
     ce_chunk_kernel(const T* __restrict__ logits, long long ld, const int32_t* __restrict__ targets,
                     float4* __restrict__ state, int ntok, int col0, int ncols, int first) {
+    constexpr int V = 16 / sizeof(T);
+    const bool vec = ((reinterpret_cast<uintptr_t>(logits) | (uintptr_t)(ld * sizeof(T))) % 16 == 0) && ncols % V == 0;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int i = blockIdx.x * WARPS + warp; i < ntok; i += gridDim.x * WARPS) {
         const T* row = logits + (size_t)i * ld;
         float m = -INFINITY, s = 0.f;
         int am = 0x7fffffff;
-        for (int j = lane; j < ncols; j += 32) {
-            const float l = to_f32(row[j]);
-            if (l > m) {
-                s = s * __expf(m - l) + 1.f;
-                m = l;
-                am = col0 + j;
-            } else {
-                s += __expf(l - m);
+        if (vec) {  // one 16-byte vector of V columns per lane step
+            for (int j = lane * V; j < ncols; j += 32 * V) {
+                const uint4 raw = *reinterpret_cast<const uint4*>(row + j);
+                const T* e = reinterpret_cast<const T*>(&raw);
+                float l[V], lm = -INFINITY;
+                int li = 0;
+#pragma unroll
+                for (int q = 0; q < V; q++) {
+                    l[q] = to_f32(e[q]);
+                    if (l[q] > lm) lm = l[q], li = q;
+                }
+                if (lm > m) {
+                    s *= __expf(m - lm);
+                    m = lm;
+                    am = col0 + j + li;
+                }
+#pragma unroll
+                for (int q = 0; q < V; q++) s += __expf(l[q] - m);
+            }
+        } else {
+            for (int j = lane; j < ncols; j += 32) {
+                const float l = to_f32(row[j]);
+                if (l > m) {
+                    s = s * __expf(m - l) + 1.f;
+                    m = l;
+                    am = col0 + j;
+                } else {
+                    s += __expf(l - m);
+                }
             }
         }
 #pragma unroll
@@ -121,6 +144,10 @@ __global__ void __launch_bounds__(WARPS * 32)
                          const float4* __restrict__ state, const float* __restrict__ mask,
                          const float* __restrict__ out, const float* __restrict__ g, float l2_factor, int scaled,
                          T* dlogits, long long ld_out, int ntok, int col0, int ncols) {  // may alias logits
+    constexpr int V = 16 / sizeof(T);
+    const bool vec = ((reinterpret_cast<uintptr_t>(logits) | reinterpret_cast<uintptr_t>(dlogits) |
+                       (uintptr_t)(ld * sizeof(T)) | (uintptr_t)(ld_out * sizeof(T))) % 16 == 0) &&
+                     ncols % V == 0;
     const float gv = *g, den = out[3];
     const float c1 = scaled ? gv / den : 1.f, c2 = scaled ? gv * l2_factor : l2_factor * den;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -132,10 +159,26 @@ __global__ void __launch_bounds__(WARPS * 32)
         const float l2g = c2 * st.x;
         const T* row = logits + (size_t)i * ld;
         T* drow = dlogits + (size_t)i * ld_out;
-        for (int j = lane; j < ncols; j += 32) {
-            float d = a * (__expf(to_f32(row[j]) - lse) - (j == tg ? 1.f : 0.f));
-            if (j == am) d += l2g;
-            drow[j] = from_f32<T>(d);
+        if (vec) {
+            for (int j = lane * V; j < ncols; j += 32 * V) {
+                const uint4 raw = *reinterpret_cast<const uint4*>(row + j);
+                const T* e = reinterpret_cast<const T*>(&raw);
+                uint4 o;
+                T* oe = reinterpret_cast<T*>(&o);
+#pragma unroll
+                for (int q = 0; q < V; q++) {
+                    float d = a * (__expf(to_f32(e[q]) - lse) - (j + q == tg ? 1.f : 0.f));
+                    if (j + q == am) d += l2g;
+                    oe[q] = from_f32<T>(d);
+                }
+                *reinterpret_cast<uint4*>(drow + j) = o;
+            }
+        } else {
+            for (int j = lane; j < ncols; j += 32) {
+                float d = a * (__expf(to_f32(row[j]) - lse) - (j == tg ? 1.f : 0.f));
+                if (j == am) d += l2g;
+                drow[j] = from_f32<T>(d);
+            }
         }
     }
 }

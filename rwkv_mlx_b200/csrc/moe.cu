@@ -527,20 +527,50 @@ __global__ void __launch_bounds__(256)
     }
 }
 
-// out[t] = base[t] + sum_s scores[t, s] * rows[inv[t * topk + s]]
+// out[t] = base[t] + sum_s scores[t, s] * rows[inv[t * topk + s]]; one warp per token,
+// one 16-byte vector per lane step when every row is 16-byte aligned (vec), else scalar.
 template <typename T>
 __global__ void __launch_bounds__(256)
     moe_combine_rows_kernel(const T* base, const T* __restrict__ rows, const T* __restrict__ scores,
-                            const int32_t* __restrict__ inv, T* out, int ntok, int C, int topk) {
+                            const int32_t* __restrict__ inv, T* out, int ntok, int C, int topk, int vec) {
+    constexpr int V = 16 / sizeof(T);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int t = blockIdx.x * 8 + warp; t < ntok; t += gridDim.x * 8) {
-        for (int c = lane; c < C; c += 32) {
-            float o = base ? to_f32(base[(size_t)t * C + c]) : 0.f;
-            for (int s = 0; s < topk; s++) {
-                const int ent = t * topk + s;
-                o = fmaf(to_f32(scores[ent]), to_f32(rows[(size_t)inv[ent] * C + c]), o);
+        if (vec) {
+            for (int i = lane; i < C / V; i += 32) {
+                float o[V];
+                if (base) {
+                    const uint4 bv = reinterpret_cast<const uint4*>(base + (size_t)t * C)[i];
+                    const T* be = reinterpret_cast<const T*>(&bv);
+#pragma unroll
+                    for (int q = 0; q < V; q++) o[q] = to_f32(be[q]);
+                } else {
+#pragma unroll
+                    for (int q = 0; q < V; q++) o[q] = 0.f;
+                }
+                for (int s = 0; s < topk; s++) {
+                    const int ent = t * topk + s;
+                    const float sc = to_f32(scores[ent]);
+                    const uint4 rv = reinterpret_cast<const uint4*>(rows + (size_t)inv[ent] * C)[i];
+                    const T* re = reinterpret_cast<const T*>(&rv);
+#pragma unroll
+                    for (int q = 0; q < V; q++) o[q] = fmaf(sc, to_f32(re[q]), o[q]);
+                }
+                uint4 ov;
+                T* oe = reinterpret_cast<T*>(&ov);
+#pragma unroll
+                for (int q = 0; q < V; q++) oe[q] = from_f32<T>(o[q]);
+                reinterpret_cast<uint4*>(out + (size_t)t * C)[i] = ov;
             }
-            out[(size_t)t * C + c] = from_f32<T>(o);
+        } else {
+            for (int c = lane; c < C; c += 32) {
+                float o = base ? to_f32(base[(size_t)t * C + c]) : 0.f;
+                for (int s = 0; s < topk; s++) {
+                    const int ent = t * topk + s;
+                    o = fmaf(to_f32(scores[ent]), to_f32(rows[(size_t)inv[ent] * C + c]), o);
+                }
+                out[(size_t)t * C + c] = from_f32<T>(o);
+            }
         }
     }
 }
@@ -1049,9 +1079,13 @@ extern "C" int rwkv_moe_combine_rows(const void* base, const void* rows, const v
     if (ntok <= 0 || C <= 0 || topk <= 0) return RWKV_ERR_SHAPE;
     if (!rows || !scores || !inv || !out) return RWKV_ERR_ARG;
     cudaStream_t st = (cudaStream_t)stream;
-    RWKV_DISPATCH_DTYPE(dtype, T, moe_combine_rows_kernel<T><<<ep_grid(ntok), 256, 0, st>>>(
-                                      (const T*)base, (const T*)rows, (const T*)scores, inv, (T*)out,
-                                      ntok, C, topk));
+    RWKV_DISPATCH_DTYPE(dtype, T, {
+        const int vec = (C * (int)sizeof(T)) % 16 == 0 && aligned(rows, 16) && aligned(out, 16) &&
+                        (!base || aligned(base, 16));
+        moe_combine_rows_kernel<T><<<ep_grid(ntok), 256, 0, st>>>((const T*)base, (const T*)rows,
+                                                                  (const T*)scores, inv, (T*)out, ntok, C,
+                                                                  topk, vec);
+    });
     return check_launch();
 }
 

@@ -125,7 +125,7 @@ __global__ void __launch_bounds__(256)
 // statistics: lane g sums its group's C/H members (fixed order, deterministic);
 // head bonus dots: per-vector partials reduced over the 64/V lanes of a head.
 template <typename T>
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(128, 10)  // <= 48 registers: 40 warps per SM hide the loads
     tmix_post_kernel(const T* __restrict__ y, const T* __restrict__ r, const T* __restrict__ k,
                      const T* __restrict__ v, const T* __restrict__ g, const T* __restrict__ lnw,
                      const T* __restrict__ lnb, const T* __restrict__ rk, T* __restrict__ out,

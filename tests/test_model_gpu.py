@@ -14,10 +14,10 @@ from tests.inputs import rel_rms
 pytestmark = pytest.mark.gpu
 
 
-def _tiny(moe=False, groupnorm="mlx", full=False):
+def _tiny(moe=False, groupnorm="mlx", full=False, n_embd=128):
     from rwkv_mlx_b200.model import RWKV, RWKVConfig, init_weights
 
-    kw = dict(n_layer=2, n_embd=128, vocab_size=512, dim_ffn=256, groupnorm=groupnorm)
+    kw = dict(n_layer=2, n_embd=n_embd, vocab_size=512, dim_ffn=256, groupnorm=groupnorm)
     if moe:
         kw.update(moe_num_experts=4, moe_top_k=2, moe_lora_rank=8)
     if full:
@@ -130,6 +130,23 @@ def test_fused_path_matches_op_by_op_path(dtype):
         tol = 1e-4 if dtype == torch.float32 else 3e-3
         assert rel_rms(a.double().cpu().numpy(), b.double().cpu().numpy()) < tol, moe
         assert abs(float(aux_a) - float(aux_b)) < 1e-4 * max(1.0, abs(float(aux_b)))
+
+
+@pytest.mark.parametrize("groupnorm", ["mlx", "per_head"])
+def test_fused_path_with_an_odd_head_count(groupnorm):
+    """C = 192 (3 heads): the fused kernels' per-warp staging and group statistics on a
+    head count that is not a multiple of 2, against the op-by-op path and the oracle."""
+    cfg, m = _tiny(groupnorm=groupnorm, n_embd=192)
+    idx = torch.randint(0, cfg.vocab_size, (2, 40), device="cuda")
+    with torch.no_grad():
+        cfg.fused = True
+        a, _ = m(idx)
+        cfg.fused = False
+        b, _ = m(idx)
+        cfg.fused = True
+    assert rel_rms(a.double().cpu().numpy(), b.double().cpu().numpy()) < 1e-4
+    ref, _ = mo.forward(_sd(m), cfg, idx.cpu(), wkv="exact", dtype=torch.float64)
+    assert rel_rms(a.double().cpu().numpy(), ref.numpy()) < 2e-3
 
 
 def test_fused_per_head_groupnorm_and_state_output():

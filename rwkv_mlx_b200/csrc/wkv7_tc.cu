@@ -22,6 +22,7 @@
 
 #include "chunk_common.cuh"
 #include "common.cuh"
+#include "tc_common.cuh"
 #include "wkv7.cuh"
 
 namespace rwkv {
@@ -30,15 +31,10 @@ __device__ int g_device_error_tc;
 
 namespace tc {
 using namespace ck;
+using namespace tcc;
 
 constexpr int NT = 384;
-constexpr int KLBO = 144;
-constexpr int NSTAGE = 3;  // operand stages for 2 prep groups: one chunk of slack  // bytes between K-adjacent core matrices (16 B pad: conflict-free stores)
-
-// byte offset of element (row r, column k) of a K-major no-swizzle UMMA operand
-__host__ __device__ constexpr int kmaj(int r, int k, int sbo) {
-    return (r & 7) * 16 + (r >> 3) * sbo + (k >> 2) * KLBO + (k & 3) * 4;
-}
+constexpr int NSTAGE = 3;  // operand stages for 2 prep groups: one chunk of slack
 constexpr int SBO_K64 = 16 * KLBO, SBO_K32 = 8 * KLBO, SBO_K16 = 4 * KLBO;
 constexpr int SZ_WB = 4 * SBO_K64;  // 32 rows x K=64
 constexpr int SZ_BK = 8 * SBO_K32;  // 64 rows x K=32
@@ -69,63 +65,6 @@ struct __align__(128) Smem {
 };
 
 enum { BAR_STATE = 1, BAR_PREP0 = 2 };  // BAR_PREP0 + g for prep group g
-
-// ---- tcgen05 helpers -------------------------------------------------------
-__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t sbo) {
-    return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)((KLBO >> 4) & 0x3FFF) << 16) |
-           ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46);
-}
-__host__ __device__ constexpr uint32_t idesc_tf32(int M, int Nn) {
-    return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(Nn >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
-}
-__device__ __forceinline__ void umma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-    asm volatile(
-        "{ .reg .pred p; setp.ne.b32 p, %4, 0; "
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %6, %7, %8}, p; }" ::"r"(d),
-        "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(0), "r"(0), "r"(0), "r"(0)
-        : "memory");
-}
-// same, A (M x K, fp32 columns) read from tensor memory
-__device__ __forceinline__ void umma_ts(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-    asm volatile(
-        "{ .reg .pred p; setp.ne.b32 p, %4, 0; "
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p; }" ::"r"(d),
-        "r"(a), "l"(b), "r"(idesc), "r"(acc), "r"(0), "r"(0), "r"(0), "r"(0)
-        : "memory");
-}
-__device__ __forceinline__ void umma_commit(unsigned long long* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                     smem_u32(bar))
-                 : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void proxy_fence() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
-    uint32_t r[16];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-#pragma unroll
-    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
-}
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float* v) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
-            taddr),
-        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
-        "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
-        "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
-        "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
-        "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
-        "r"(__float_as_uint(v[15]))
-        : "memory");
-}
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 __device__ __forceinline__ void st4(unsigned char* p, float a, float b, float c, float d) {
     *reinterpret_cast<float4*>(p) = make_float4(tf32f(a), tf32f(b), tf32f(c), tf32f(d));

@@ -281,3 +281,29 @@ def test_tcgen05_kernel_with_state_and_checkpoints(T):
     assert rel_rms(sT.cpu().numpy(), sTe) < 2e-3
     if T >= 16:
         assert rel_rms(ck.cpu().numpy(), wo.checkpoints_from_states(st, 16).reshape(-1)) < 2e-3
+
+
+@pytest.mark.parametrize("scale_s,scale_v,scale_ab", [(3e4, 300.0, 1.0), (1e-6, 1e-4, 1.0), (1.0, 1.0, 1.4)])
+def test_tcgen05_kernel_across_ranges(scale_s, scale_v, scale_ab):
+    """fp16 activations with states far outside the fp16 range (entries ~1e5), tiny
+    states, and larger |a|, |b| (larger triangular-solve entries): the state and the
+    TF32 operands are fp32-ranged, so accuracy does not depend on the magnitudes."""
+    from rwkv_mlx_b200 import _native, wkv7
+
+    B, T, H = 2, 160, 2
+    inp = wkv_inputs(B, T, H, seed=31)
+    inp["v"] = inp["v"] * scale_v
+    inp["a"] = inp["a"] * scale_ab
+    inp["b"] = inp["b"] * scale_ab
+    d, h = _rounded(inp, torch.float16, w_dt=torch.float32)
+    rng = np.random.default_rng(5)
+    s0 = rng.standard_normal((B, H, 64, 64)) * scale_s
+    y, _, sa, sT = wkv7._fwd(d["r"], d["w"], d["k"], d["v"], d["a"], d["b"], s0=_dev(s0, torch.float32),
+                             want_sa=True, want_state=True)
+    torch.cuda.synchronize()
+    assert _native.lib().rwkv_device_error(1) == 0
+    ye, sae, sTe, _ = wo.wkv7_forward_exact(h["r"], h["w"], h["k"], h["v"], h["a"], h["b"], s0=s0)
+    if np.abs(ye).max() < 6e4:  # y itself is an fp16 output
+        assert rel_rms(y.double().cpu().numpy(), _bt(ye)) < 2e-3
+    assert rel_rms(sa.cpu().numpy(), sae) < 2e-3
+    assert rel_rms(sT.cpu().numpy(), sTe) < 2e-3

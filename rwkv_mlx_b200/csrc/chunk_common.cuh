@@ -69,6 +69,19 @@ __device__ __forceinline__ bool group_sync_or(int id, bool v) {
 __device__ __forceinline__ void group_sync(int id) {
     asm volatile("bar.sync %0, 128;" ::"r"(id) : "memory");
 }
+// Named barriers over `n` threads (a multiple of 32): wait, or wait and OR a predicate.
+__device__ __forceinline__ void bar_sync_n(int id, int n) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+__device__ __forceinline__ bool bar_or_n(int id, int n, bool v) {
+    uint32_t r;
+    asm volatile(
+        "{ .reg .pred p, q; setp.ne.u32 q, %1, 0; bar.red.or.pred p, %2, %3, q; selp.u32 %0, 1, 0, p; }"
+        : "=r"(r)
+        : "r"((uint32_t)v), "r"(id), "r"(n)
+        : "memory");
+    return r != 0;
+}
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),

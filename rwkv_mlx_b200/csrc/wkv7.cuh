@@ -25,6 +25,7 @@ int wkv7_fwd_chunk(const WkvFwdArgs& p, cudaStream_t st);
 int wkv7_fwd_tc(const WkvFwdArgs& p, cudaStream_t st);
 bool wkv7_tc_supported(int dtype);
 int read_device_error_tc(int clear);
+int read_device_error_bwd(int clear);
 int read_device_error(int clear);
 extern int g_wkv_impl;  // 0 auto, 1 step-sequential, 2 chunked (mma.sync), 3 chunked (tcgen05)
 int wkv7_bwd_seq(const WkvBwdArgs& p, cudaStream_t st);

@@ -13,7 +13,8 @@
 // Pass 1 (one CTA per (b, h), chunks in reverse) runs the adjoint of the state chain:
 // with Inv = (I - Mab)^-1, Wu = Inv At, Wy = Rt + Mrb Wu,
 //   dX_0 = GL o dX_L + Wu^T (Bb dX_L) + Wy^T dY,
-// writing dX_L of every chunk to the workspace (and dX_0 of chunk 0 as ds0).
+// writing dX_L of every chunk to the workspace (and dX_0 of chunk 0 as ds0); two warp
+// groups build Wu, Wy, Bb, dY, GL for alternating chunks while eight warps run the chain.
 // Pass 2 (one CTA per (b, h, chunk), all chunks at once) forms every input gradient
 // of its chunk from X (the forward's snapshot), dX_L and the inputs:
 //   Lambda = Inv^T (Mrb^T dY + Bb dX_L)                 (adjoint of the solve for U)
@@ -295,58 +296,255 @@ __device__ void front_matrices(Front& fr, int ext, unsigned which) {
 }
 
 // ---------------------------------------------------------------------------
-// Pass 1: adjoint of the state chain.
-struct P1Smem {
-    Front fr;
-    float WU[L][LDC], WY[L][LDC], DU[L][LDC];
-    float D[N][LDC];  // dX_L [key][value]
+// Pass 1, warp-specialized.  The chain itself needs per chunk only Wu, Wy, Bb, dY and
+// GL, all functions of the inputs: two "prep" groups of 4 warps build them for
+// alternating chunks into a 3-stage ring (inputs streamed with cp.async one own chunk
+// ahead), while 8 "chain" warps run dX_0 = GL o dX_L + Wu^T (Bb dX_L) + Wy^T dY.
+// Wu = (I - Mab)^-1 At comes from a forward substitution in fp32 (one key column per
+// thread); the products run on mma.sync with 3xTF32 operands as elsewhere here.
+namespace p1 {
+constexpr int NTH = 512, NSTAGE = 3, NCW = 8;  // 8 chain warps, then two prep groups of 4 warps
+enum { BAR_CHAIN = 1, BAR_PREP0 = 2 };
+enum { PR = 0, PL, PA, PB, PD, NP };  // inputs kept per chunk: r, l = -exp(w), a, b, dy
+struct Stage {
+    float WU[L][LDC], WY[L][LDC], BB[L][LDC], DY[L][LDC];
+    float GL[N];
+};
+template <typename T, typename TW>
+struct RawIn {  // one chunk's raw inputs as cp.async deposits them: r, a, b, dy (T), w (TW)
+    static constexpr int ROW = N * sizeof(T), ROWW = N * sizeof(TW);
+    static constexpr int PR_ = ROW / 16, PRW = ROWW / 16;  // 16-byte pieces per row
+    static constexpr int BYTES = 4 * L * ROW + L * ROWW;
+};
+struct Prep {
+    float in[NP][L][LDC];
+    float c[L][LDC];
+    float At[L][LDC], Rt[L][LDC], Bh[L][LDC];
+    float M[2][L][LM];  // Mab (strict), Mrb (inclusive)
+};
+struct Warps {
+    int w, n;  // this warp's index within its group, warps in the group
 };
 
+// C (M x Nn) = sum over segments A_i B_i, tiles over the group's warps (see block_mm_s)
+template <typename FO, typename... S>
+__device__ __forceinline__ void gmm(Warps wp, int M, int Nn, const FO& out, const S&... segs) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, tg = lane & 3;
+    const int ntl = Nn / 8, tiles = (M / 16) * ntl;
+    for (int tile = wp.w; tile < tiles; tile += wp.n) {
+        const int m0 = (tile / ntl) * 16, n0 = (tile % ntl) * 8;
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
+        (tile_mm<S::AX, S::BX>(d, [&](int m, int k) { return segs.A(m0 + m, k); },
+                               [&](int k, int n) { return segs.B(k, n0 + n); }, segs.K),
+         ...);
+        out(m0 + g, n0 + 2 * tg, d[0]);
+        out(m0 + g, n0 + 2 * tg + 1, d[1]);
+        out(m0 + g + 8, n0 + 2 * tg, d[2]);
+        out(m0 + g + 8, n0 + 2 * tg + 1, d[3]);
+    }
+}
+
+__device__ __forceinline__ void cp16z(unsigned char* dst, const void* src, bool ok) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+                 "l"(src), "r"(ok ? 16 : 0)
+                 : "memory");
+}
+}  // namespace p1
+
 template <typename T, typename TW>
-__global__ void __launch_bounds__(NT, 1)
-    wkv7_bwd_chain_kernel(const T* __restrict__ r, const TW* __restrict__ w, const T* __restrict__ a,
-                          const T* __restrict__ b, const T* __restrict__ dy, const float* __restrict__ dsT,
-                          float* __restrict__ dxl, float* __restrict__ ds0, int T_, int H) {
-    extern __shared__ __align__(16) unsigned char smem_p1[];
-    P1Smem& sm = *reinterpret_cast<P1Smem*>(smem_p1);
-    Front& fr = sm.fr;
-    const int tid = threadIdx.x, bh = blockIdx.x, bi = bh / H, hi = bh % H;
+struct P1WSmem {
+    p1::Stage st[p1::NSTAGE];
+    p1::Prep pg[2];
+    unsigned char raw[2][p1::RawIn<T, TW>::BYTES];
+    float D[N][LDC];  // dX_L [key][value]
+    float DU[L][LDC];
+    unsigned long long full[p1::NSTAGE], empty[p1::NSTAGE];
+    int abort;
+};
+
+__device__ int g_device_error_bwd;
+
+template <typename T, typename TW>
+__global__ void __launch_bounds__(p1::NTH, 1)
+    wkv7_bwd_chain_ws_kernel(const T* __restrict__ r, const TW* __restrict__ w, const T* __restrict__ a,
+                             const T* __restrict__ b, const T* __restrict__ dy, const float* __restrict__ dsT,
+                             float* __restrict__ dxl, float* __restrict__ ds0, int T_, int H) {
+    using namespace p1;
+    using RI = RawIn<T, TW>;
+    extern __shared__ __align__(16) unsigned char smem_p1w[];
+    P1WSmem<T, TW>& sm = *reinterpret_cast<P1WSmem<T, TW>*>(smem_p1w);
+    const int tid = threadIdx.x, warp = tid >> 5, bh = blockIdx.x, bi = bh / H, hi = bh % H;
     const size_t tstride = (size_t)H * N, base = ((size_t)bi * T_ * H + hi) * N;
     const int nch = (T_ + L - 1) / L;
-    for (int e = tid; e < N * N; e += NT) {  // D = dsT^T
-        const int vv = e / N, j = e % N;
-        sm.D[j][vv] = dsT ? dsT[(size_t)bh * N * N + e] : 0.f;
-    }
-    constexpr unsigned MASK1 = (1u << IR) | (1u << IL) | (1u << IA) | (1u << IB) | (1u << IDY);
-    ChunkLoad<T, TW> ld;
-    ld.issue(r, w, nullptr, nullptr, a, b, dy, base, tstride, (nch - 1) * L, min(L, T_ - (nch - 1) * L), MASK1);
-    for (int c = nch - 1; c >= 0; c--) {
-        __syncthreads();
-        ld.store(fr, min(L, T_ - c * L), MASK1);
-        if (c > 0) ld.issue(r, w, nullptr, nullptr, a, b, dy, base, tstride, (c - 1) * L, L, MASK1);  // next chunk
-        __syncthreads();
-        const int ext = front_factors(fr);
-        front_matrices(fr, ext, 0b0101);  // Mab, Mrb
-        block_mm(L, N, L, [&](int t, int s) { return fr.Inv[t][s]; }, [&](int s, int j) { return fr.f[FAT][s][j]; },
-                 [&](int t, int j, float val) { sm.WU[t][j] = val; });
-        __syncthreads();
-        block_mm(L, N, L, [&](int t, int s) { return fr.M[2][t][s]; }, [&](int s, int j) { return sm.WU[s][j]; },
-                 [&](int t, int j, float val) { sm.WY[t][j] = fr.f[FRT][t][j] + val; });
-        block_mm(L, N, N, [&](int t, int j) { return fr.f[FBB][t][j]; }, [&](int j, int vv) { return sm.D[j][vv]; },
-                 [&](int t, int vv, float val) { sm.DU[t][vv] = val; });
-        float* out = dxl + ((size_t)bh * nch + c) * N * N;
-        for (int e = tid; e < N * N / 4; e += NT)
-            *reinterpret_cast<float4*>(out + 4 * e) = *reinterpret_cast<const float4*>(&sm.D[e / 16][(e % 16) * 4]);
-        __syncthreads();
-        block_mm_s(N, N, [&](int j, int vv, float val) { sm.D[j][vv] = fmaf(fr.GL[j], sm.D[j][vv], val); },
-                   seg([&](int j, int t) { return sm.WU[t][j]; }, [&](int t, int vv) { return sm.DU[t][vv]; }, L),
-                   seg<false, sizeof(T) == 2>([&](int j, int t) { return sm.WY[t][j]; },
-                                              [&](int t, int vv) { return fr.in[IDY][t][vv]; }, L));
+    constexpr bool EXI = sizeof(T) == 2;  // 16-bit dy is exact in TF32
+
+    if (tid == 0) {
+        for (int i = 0; i < NSTAGE; i++) ck::mbar_init(&sm.full[i], 128), ck::mbar_init(&sm.empty[i], 32 * NCW);
+        sm.abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
-    if (ds0) {
-        for (int e = tid; e < N * N; e += NT) ds0[(size_t)bh * N * N + e] = sm.D[e % N][e / N];
+
+    if (warp >= NCW) {
+        // ===================== prep groups =====================
+        const int g_ = (warp - NCW) >> 2, pt = tid - 32 * NCW - 128 * g_, lane = pt & 31;
+        const Warps wp{pt >> 5, 4};
+        const int BAR = BAR_PREP0 + g_;
+        Prep& pg = sm.pg[g_];
+        unsigned char* raw = sm.raw[g_];
+        auto issue = [&](int ii) {  // raw inputs of processing index ii (chunk nch - 1 - ii)
+            const int t0 = (nch - 1 - ii) * L, nt = min(L, T_ - t0);
+            constexpr int NTP = 4 * L * RI::PR_, ALL = NTP + L * RI::PRW;
+            for (int q = pt; q < ALL; q += 128) {
+                const void* src;
+                unsigned char* dst;
+                bool ok;
+                if (q < NTP) {
+                    const int arr = q / (L * RI::PR_), rem = q % (L * RI::PR_), row = rem / RI::PR_, pc = rem % RI::PR_;
+                    const T* ab = arr == 0 ? r : arr == 1 ? a : arr == 2 ? b : dy;
+                    ok = row < nt;
+                    src = ok ? (const void*)(ab + base + (size_t)(t0 + row) * tstride + pc * (16 / sizeof(T))) : (const void*)ab;
+                    dst = raw + arr * (L * RI::ROW) + row * RI::ROW + pc * 16;
+                } else {
+                    const int q2 = q - NTP, row = q2 / RI::PRW, pc = q2 % RI::PRW;
+                    ok = row < nt;
+                    src = ok ? (const void*)(w + base + (size_t)(t0 + row) * tstride + pc * (16 / sizeof(TW))) : (const void*)w;
+                    dst = raw + 4 * (L * RI::ROW) + row * RI::ROWW + pc * 16;
+                }
+                cp16z(dst, src, ok);
+            }
+            asm volatile("cp.async.commit_group;" ::: "memory");
+        };
+        if (g_ < nch) issue(g_);
+        for (int i = g_; i < nch; i += 2) {
+            asm volatile("cp.async.wait_all;" ::: "memory");
+            const int s = i % NSTAGE, c = nch - 1 - i, nt = min(L, T_ - c * L);
+            Stage& stg = sm.st[s];
+            const bool bad = i >= NSTAGE && !ck::mbar_wait(&sm.empty[s], ((i / NSTAGE) + 1) & 1, &sm.abort, &g_device_error_bwd);
+            if (ck::group_sync_or(BAR, bad)) break;
+            // raw -> fp32 (l = -exp(w); rows past the sequence end are zero)
+            for (int e = pt; e < L * N; e += 128) {
+                const int t = e / N, j = e % N;
+                const T* rt = reinterpret_cast<const T*>(raw);
+                pg.in[PR][t][j] = to_f32(rt[0 * L * N + t * N + j]);
+                pg.in[PA][t][j] = to_f32(rt[1 * L * N + t * N + j]);
+                pg.in[PB][t][j] = to_f32(rt[2 * L * N + t * N + j]);
+                pg.in[PD][t][j] = to_f32(rt[3 * L * N + t * N + j]);
+                const TW* wt = reinterpret_cast<const TW*>(raw + 4 * (L * RI::ROW));
+                pg.in[PL][t][j] = t < nt ? -ck::ex2(to_f32(wt[t * N + j]) * ck::LOG2E) : 0.f;
+            }
+            ck::group_sync(BAR);
+            if (i + 2 < nch) issue(i + 2);  // the raw buffer is free again
+            // cumulative decays, GL
+            int ext = 0;
+            if (pt < N) {
+                float sum = 0.f;
+#pragma unroll
+                for (int t = 0; t < L; t++) sum += pg.in[PL][t][pt], pg.c[t][pt] = sum;
+                ext = sum < EXT_C;
+                stg.GL[pt] = ck::ex2(sum * ck::LOG2E);
+            }
+            ext = ck::group_sync_or(BAR, ext);
+            // decayed factors; Bb and dY go straight to the stage
+            for (int e = pt; e < L * N; e += 128) {
+                const int t = e / N, j = e % N;
+                const float cp = t ? pg.c[t - 1][j] : 0.f, ct = pg.c[t][j], cl = pg.c[L - 1][j];
+                pg.At[t][j] = pg.in[PA][t][j] * ck::ex2(cp * ck::LOG2E);
+                pg.Rt[t][j] = pg.in[PR][t][j] * ck::ex2(ct * ck::LOG2E);
+                stg.BB[t][j] = pg.in[PB][t][j] * ck::ex2((cl - ct) * ck::LOG2E);
+                if (!ext) pg.Bh[t][j] = pg.in[PB][t][j] * ck::ex2(-ct * ck::LOG2E);
+                stg.DY[t][j] = pg.in[PD][t][j];
+            }
+            ck::group_sync(BAR);
+            // Mab (strict) and Mrb (inclusive): 4 tiles of 16 x 8, one per warp
+            if (!ext) {
+                const int which = wp.w >> 1, n0 = (wp.w & 1) * 8, g = lane >> 2, tg = lane & 3;
+                float d[4] = {0.f, 0.f, 0.f, 0.f};
+                const float(*X)[LDC] = which ? pg.Rt : pg.At;
+                tile_mm(d, [&](int m, int k) { return X[m][k]; }, [&](int k, int n) { return pg.Bh[n0 + n][k]; }, N);
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    const int tt = g + (q >> 1) * 8, ss = n0 + 2 * tg + (q & 1);
+                    pg.M[which][tt][ss] = (which ? ss <= tt : ss < tt) ? d[q] : 0.f;
+                }
+            } else {  // from exponent differences: the factored forms would overflow
+                for (int e = pt; e < 2 * L * L; e += 128) {
+                    const int which = e / (L * L), tt = (e / L) % L, ss = e % L;
+                    float val = 0.f;
+                    if (which ? ss <= tt : ss < tt) {
+                        const float* xs = which ? pg.in[PR][tt] : pg.in[PA][tt];
+                        const float* cx = which ? pg.c[tt] : (tt ? pg.c[tt - 1] : nullptr);
+                        for (int j = 0; j < N; j++)
+                            val = fmaf(xs[j] * pg.in[PB][ss][j], expf((cx ? cx[j] : 0.f) - pg.c[ss][j]), val);
+                    }
+                    pg.M[which][tt][ss] = val;
+                }
+            }
+            ck::group_sync(BAR);
+            // Wu = (I - Mab)^-1 At by forward substitution, one key column per thread
+            if (pt < N) {
+                float x[L];
+#pragma unroll
+                for (int tt = 0; tt < L; tt++) {
+                    float acc = pg.At[tt][pt];
+#pragma unroll
+                    for (int s2 = 0; s2 < tt; s2++) acc = fmaf(pg.M[0][tt][s2], x[s2], acc);
+                    x[tt] = acc;
+                    stg.WU[tt][pt] = acc;
+                }
+            }
+            ck::group_sync(BAR);
+            // Wy = Rt + Mrb Wu
+            gmm(wp, L, N, [&](int t, int j, float val) { stg.WY[t][j] = pg.Rt[t][j] + val; },
+                seg([&](int t, int s2) { return pg.M[1][t][s2]; }, [&](int s2, int j) { return stg.WU[s2][j]; }, L));
+            ck::mbar_arrive(&sm.full[s]);
+        }
+        asm volatile("cp.async.wait_all;" ::: "memory");
+    } else {
+        // ===================== chain warps =====================
+        const Warps wp{warp, NCW};
+        for (int e = tid; e < N * N; e += 32 * NCW) {  // D = dsT^T
+            const int vv = e / N, j = e % N;
+            sm.D[j][vv] = dsT ? dsT[(size_t)bh * N * N + e] : 0.f;
+        }
+        bool failed = false;
+        for (int i = 0; i < nch; i++) {
+            const int c = nch - 1 - i, s = i % NSTAGE;
+            const Stage& stg = sm.st[s];
+            const bool bad = !ck::mbar_wait(&sm.full[s], (i / NSTAGE) & 1, &sm.abort, &g_device_error_bwd);
+            if (ck::bar_or_n(BAR_CHAIN, 32 * NCW, bad)) {
+                failed = true;
+                break;
+            }
+            gmm(wp, L, N, [&](int t, int vv, float val) { sm.DU[t][vv] = val; },
+                seg([&](int t, int j) { return stg.BB[t][j]; }, [&](int j, int vv) { return sm.D[j][vv]; }, N));
+            float* out = dxl + ((size_t)bh * nch + c) * N * N;
+            for (int e = tid; e < N * N / 4; e += 32 * NCW)
+                *reinterpret_cast<float4*>(out + 4 * e) = *reinterpret_cast<const float4*>(&sm.D[e / 16][(e % 16) * 4]);
+            ck::bar_sync_n(BAR_CHAIN, 32 * NCW);
+            gmm(wp, N, N, [&](int j, int vv, float val) { sm.D[j][vv] = fmaf(stg.GL[j], sm.D[j][vv], val); },
+                seg([&](int j, int t) { return stg.WU[t][j]; }, [&](int t, int vv) { return sm.DU[t][vv]; }, L),
+                seg<false, EXI>([&](int j, int t) { return stg.WY[t][j]; }, [&](int t, int vv) { return stg.DY[t][vv]; }, L));
+            ck::mbar_arrive(&sm.empty[s]);
+        }
+        if (failed && tid == 0) sm.abort = 1;
+        ck::bar_sync_n(BAR_CHAIN, 32 * NCW);
+        if (!failed && ds0) {
+            for (int e = tid; e < N * N; e += 32 * NCW) ds0[(size_t)bh * N * N + e] = sm.D[e % N][e / N];
+        }
     }
+}
+
+int read_error_word(int clear) {
+    int v = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&v, g_device_error_bwd, sizeof(int));
+    if (e != cudaSuccess) return -set_cuda_error(e);
+    if (clear && v) {
+        const int z = 0;
+        e = cudaMemcpyToSymbol(g_device_error_bwd, &z, sizeof(int));
+        if (e != cudaSuccess) return -set_cuda_error(e);
+    }
+    return v;
 }
 
 // ---------------------------------------------------------------------------
@@ -563,15 +761,15 @@ size_t wkv7_bwd_chunk_ws_bytes(int B, int T, int H) {
 template <typename T, typename TW>
 static int launch_bwd_chunked(const WkvBwdArgs& p, float* ws, cudaStream_t st) {
     using namespace bwdc;
-    auto k1 = wkv7_bwd_chain_kernel<T, TW>;
+    auto k1 = wkv7_bwd_chain_ws_kernel<T, TW>;
     auto k2 = wkv7_bwd_chunk_kernel<T, TW>;
-    const int s1 = (int)sizeof(P1Smem), s2 = (int)sizeof(P2Smem);
+    const int s1 = (int)sizeof(P1WSmem<T, TW>), s2 = (int)sizeof(P2Smem);
     cudaError_t e = cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, s1);
     if (e == cudaSuccess) e = cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, s2);
     if (e != cudaSuccess) return set_cuda_error(e);
     const int nch = (p.T + L - 1) / L;
-    k1<<<p.B * p.H, NT, s1, st>>>((const T*)p.r, (const TW*)p.w, (const T*)p.a, (const T*)p.b, (const T*)p.dy, p.dsT,
-                                  ws, p.ds0, p.T, p.H);
+    k1<<<p.B * p.H, p1::NTH, s1, st>>>((const T*)p.r, (const TW*)p.w, (const T*)p.a, (const T*)p.b, (const T*)p.dy,
+                                       p.dsT, ws, p.ds0, p.T, p.H);
     int rc = check_launch();
     if (rc) return rc;
     k2<<<dim3(nch, p.B * p.H), NT, s2, st>>>((const T*)p.r, (const TW*)p.w, (const T*)p.k, (const T*)p.v,
@@ -579,6 +777,8 @@ static int launch_bwd_chunked(const WkvBwdArgs& p, float* ws, cudaStream_t st) {
                                              (T*)p.dr, (T*)p.dw, (T*)p.dk, (T*)p.dv, (T*)p.da, (T*)p.db, p.T, p.H);
     return check_launch();
 }
+
+int read_device_error_bwd(int clear) { return bwdc::read_error_word(clear); }
 
 int wkv7_bwd_chunked(const WkvBwdArgs& p, float* ws, cudaStream_t st) {
     RWKV_DISPATCH_DTYPE_W(p.dtype, p.w_dtype, T, TW, return launch_bwd_chunked<T, TW>(p, ws, st));

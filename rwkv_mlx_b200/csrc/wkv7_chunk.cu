@@ -510,8 +510,10 @@ int read_device_error(int clear) {
 }  // namespace rwkv
 
 extern "C" int rwkv_device_error(int clear) {
-    const int a = rwkv::read_device_error(clear), b = rwkv::read_device_error_tc(clear);
+    const int a = rwkv::read_device_error(clear), b = rwkv::read_device_error_tc(clear),
+              c = rwkv::read_device_error_bwd(clear);
     if (a < 0) return a;
     if (b < 0) return b;
-    return a | b;
+    if (c < 0) return c;
+    return a | b | c;
 }

@@ -51,7 +51,7 @@ def test_head_loss_and_gradients_match_oracle(dt, masked, B, T, V, C, chunk):
     ref = lo.l2_wrap_loss_masked(lg, tg.cpu(), mk.cpu().double()) if masked else lo.l2_wrap_loss(lg, tg.cpu())
     ref.backward()
     tol = 1e-5 if dt == torch.float32 else 2e-2
-    assert abs(float(loss.detach()) - float(ref)) < tol * max(1.0, abs(float(ref)))
+    assert abs(float(loss.detach()) - float(ref.detach())) < tol * max(1.0, abs(float(ref.detach())))
     gtol = 1e-4 if dt == torch.float32 else 3e-2
     assert rel_rms(xg.grad.double().cpu().numpy(), xd.grad.numpy()) < gtol
     assert rel_rms(wg.grad.double().cpu().numpy(), wd.grad.numpy()) < gtol
@@ -69,7 +69,7 @@ def test_loss_on_logits_and_its_gradient(dt):
     ld = lg.detach().double().cpu().requires_grad_(True)
     ref = lo.l2_wrap_loss(ld, tg.cpu())
     ref.backward()
-    assert abs(float(loss.detach()) - float(ref)) < 1e-5 * abs(float(ref))
+    assert abs(float(loss.detach()) - float(ref.detach())) < 1e-5 * abs(float(ref.detach()))
     assert rel_rms(lg.grad.double().cpu().numpy(), ld.grad.numpy()) < (1e-5 if dt == torch.float32 else 5e-3)
 
 

@@ -121,11 +121,12 @@ __global__ void __launch_bounds__(256)
 }
 
 // ---------------------------------------------------------------------------
-// One warp per row.  The row of y is staged in shared memory (fp32); group
-// statistics: lane g sums its group's C/H members (fixed order, deterministic);
+// One warp per row.  The row of y is staged in shared memory (fp32, 16-byte stores);
+// group statistics: MLX strided groups -- lane g sums its group's C/H members; per-head
+// groups -- the lanes holding a head reduce with shuffles (fixed order, deterministic);
 // head bonus dots: per-vector partials reduced over the 64/V lanes of a head.
 template <typename T>
-__global__ void __launch_bounds__(128, 10)  // <= 48 registers: 40 warps per SM hide the loads
+__global__ void __launch_bounds__(128, 8)  // <= 64 registers: 32 warps per SM
     tmix_post_kernel(const T* __restrict__ y, const T* __restrict__ r, const T* __restrict__ k,
                      const T* __restrict__ v, const T* __restrict__ g, const T* __restrict__ lnw,
                      const T* __restrict__ lnb, const T* __restrict__ rk, T* __restrict__ out,
@@ -133,7 +134,7 @@ __global__ void __launch_bounds__(128, 10)  // <= 48 registers: 40 warps per SM 
     constexpr int V = Vec<T>::N, LPH = 64 / V;
     extern __shared__ float sm_post[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float* ys = sm_post + (size_t)warp * (C + 2 * H);
+    float* ys = sm_post + (size_t)warp * (((C + 2 * H) + 3) & ~3);  // 16-byte aligned per warp
     float* mean = ys + C;
     float* rstd = mean + H;
     const int gsz = C / H, nv = C / V;
@@ -153,34 +154,55 @@ __global__ void __launch_bounds__(128, 10)  // <= 48 registers: 40 warps per SM 
                 Vec<T> Y, R, K, RK;
                 Y.load(y + base + qv * V), R.load(r + base + qv * V), K.load(k + base + qv * V), RK.load(rk + qv * V);
 #pragma unroll
-                for (int i = 0; i < V; i++) {
-                    ys[qv * V + i] = Y.get(i);
-                    d = fmaf(R.get(i) * K.get(i), RK.get(i), d);
-                }
+                for (int i = 0; i < V; i += 4)  // 16-byte stores: a lane's V values are contiguous
+                    *reinterpret_cast<float4*>(&ys[qv * V + i]) = make_float4(Y.get(i), Y.get(i + 1), Y.get(i + 2), Y.get(i + 3));
+#pragma unroll
+                for (int i = 0; i < V; i++) d = fmaf(R.get(i) * K.get(i), RK.get(i), d);
             }
 #pragma unroll
             for (int off = 1; off < LPH; off <<= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
             hd[j] = d;
         }
         __syncwarp();
-        for (int gi = lane; gi < H; gi += 32) {
-            float s1 = 0.f;
-            if (per_head) {
-                for (int m = 0; m < gsz; m++) s1 += ys[gi * gsz + m];
-            } else {
+        float hm[8], hr[8];  // per-head grouping: the vector's head statistics, in registers
+        if (per_head) {
+            // a head's 64 channels are the 64/V vectors of LPH consecutive lanes: sums over
+            // the lane's own values, then xor shuffles within those lanes (fixed order)
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                if (j >= NJ) break;
+                const int qv = lane + 32 * j;
+                float s1 = 0.f;
+                if (qv < nv) {
+#pragma unroll
+                    for (int i = 0; i < V; i++) s1 += ys[qv * V + i];
+                }
+#pragma unroll
+                for (int off = 1; off < LPH; off <<= 1) s1 += __shfl_xor_sync(0xffffffffu, s1, off);
+                const float mu = s1 * (1.f / 64.f);
+                float s2 = 0.f;
+                if (qv < nv) {
+#pragma unroll
+                    for (int i = 0; i < V; i++) { const float dd = ys[qv * V + i] - mu; s2 = fmaf(dd, dd, s2); }
+                }
+#pragma unroll
+                for (int off = 1; off < LPH; off <<= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, off);
+                hm[j] = mu;
+                hr[j] = rsqrtf(s2 * (1.f / 64.f) + eps);
+            }
+        } else {
+            // MLX strided grouping (channel c in group c % H): one lane per group
+            for (int gi = lane; gi < H; gi += 32) {
+                float s1 = 0.f;
                 for (int m = 0; m < gsz; m++) s1 += ys[gi + H * m];
-            }
-            const float mu = s1 / (float)gsz;
-            float s2 = 0.f;
-            if (per_head) {
-                for (int m = 0; m < gsz; m++) { const float dd = ys[gi * gsz + m] - mu; s2 = fmaf(dd, dd, s2); }
-            } else {
+                const float mu = s1 / (float)gsz;
+                float s2 = 0.f;
                 for (int m = 0; m < gsz; m++) { const float dd = ys[gi + H * m] - mu; s2 = fmaf(dd, dd, s2); }
+                mean[gi] = mu;
+                rstd[gi] = rsqrtf(s2 / (float)gsz + eps);
             }
-            mean[gi] = mu;
-            rstd[gi] = rsqrtf(s2 / (float)gsz + eps);
+            __syncwarp();
         }
-        __syncwarp();
 #pragma unroll
         for (int j = 0; j < 8; j++) {
             if (j >= NJ) break;
@@ -188,13 +210,29 @@ __global__ void __launch_bounds__(128, 10)  // <= 48 registers: 40 warps per SM 
             if (qv >= nv) continue;
             Vec<T> Vv, G, W, Bb, O;
             Vv.load(v + base + qv * V), G.load(g + base + qv * V), W.load(lnw + qv * V), Bb.load(lnb + qv * V);
+            float yv[V];
 #pragma unroll
-            for (int i = 0; i < V; i++) {
-                const int c = qv * V + i;
-                const int gi = per_head ? c / gsz : c % H;
-                float o = fmaf((ys[c] - mean[gi]) * rstd[gi], W.get(i), Bb.get(i));
-                o = fmaf(hd[j], Vv.get(i), o);
-                O.set(i, o * G.get(i));
+            for (int i = 0; i < V; i += 4) {
+                const float4 q4 = *reinterpret_cast<const float4*>(&ys[qv * V + i]);
+                yv[i] = q4.x, yv[i + 1] = q4.y, yv[i + 2] = q4.z, yv[i + 3] = q4.w;
+            }
+            if (per_head) {
+#pragma unroll
+                for (int i = 0; i < V; i++) {
+                    float o = fmaf((yv[i] - hm[j]) * hr[j], W.get(i), Bb.get(i));
+                    o = fmaf(hd[j], Vv.get(i), o);
+                    O.set(i, o * G.get(i));
+                }
+            } else {
+                // group of channel c = c % H: one modulo per vector, then increments
+                int gi = (qv * V) % H;
+#pragma unroll
+                for (int i = 0; i < V; i++) {
+                    float o = fmaf((yv[i] - mean[gi]) * rstd[gi], W.get(i), Bb.get(i));
+                    o = fmaf(hd[j], Vv.get(i), o);
+                    O.set(i, o * G.get(i));
+                    if (++gi == H) gi = 0;
+                }
             }
             O.store(out + base + qv * V);
         }
@@ -339,7 +377,7 @@ extern "C" int rwkv_tmix_post(const void* y, const void* r, const void* k, const
             if (!aligned(p, 16)) return RWKV_ERR_ALIGN;
     }
     cudaStream_t st = (cudaStream_t)stream;
-    const size_t smem = 4 * (size_t)(C + 2 * H) * sizeof(float);
+    const size_t smem = 4 * (size_t)(((C + 2 * H) + 3) & ~3) * sizeof(float);
     {
         const int V = dtype == RWKV_F32 ? 4 : 8;
         if (C / V > 8 * 32) return RWKV_ERR_SHAPE;  // <= 8 vectors per lane

@@ -136,6 +136,22 @@ class RWKV_Tmix_x070(nn.Module):
         self.value = nn.Linear(C, C, bias=False)
         self.output = nn.Linear(C, C, bias=False)
         self.ln_x = GroupNormMLX(H, C, eps=64e-5, mode=config.groupnorm)
+        self._packed, self._packed_key = None, None
+
+    def _packed_weights(self):
+        """The six token-shift mixes as one (6, C) tensor and W_r, W_k, W_v stacked for one
+        batched product, rebuilt only when a parameter changes (storage, dtype or an
+        in-place update), so inference steps launch no copies for them."""
+        ps = (self.x_r, self.x_k, self.x_v, self.x_w, self.x_a, self.x_g,
+              self.receptance.weight, self.key.weight, self.value.weight)
+        key = tuple((p.data_ptr(), p.dtype, p._version) for p in ps)
+        if self._packed_key != key:
+            C = self.x_r.shape[-1]
+            with torch.no_grad():
+                mix = torch.cat([p.detach() for p in ps[:6]]).view(6, C)
+                wrkv = torch.stack([p.detach() for p in ps[6:]]).transpose(1, 2)
+            self._packed, self._packed_key = (mix, wrkv), key
+        return self._packed
 
     def _project(self, x, xx, v_first):
         """Shared by GPT and RNN mode: returns r, w(log-log), k, v, a, g, kk, v_first."""
@@ -171,9 +187,9 @@ class RWKV_Tmix_x070(nn.Module):
     def _forward_fused(self, x, v_first, s0, return_state):
         B, T, C = x.shape
         H, N = self.n_head, self.head_size
-        mix = torch.cat([self.x_r, self.x_k, self.x_v, self.x_w, self.x_a, self.x_g]).view(6, C)
+        mix, wrkv = self._packed_weights()
         X = fz.lerp(x, mix, T)  # (6, B*T, C): r, k, v, w, a, g inputs
-        rkv = torch.bmm(X[0:3], torch.stack([self.receptance.weight, self.key.weight, self.value.weight]).transpose(1, 2))
+        rkv = torch.bmm(X[0:3], wrkv)
         r, k, v = rkv[0], rkv[1], rkv[2]
         xv, xw, xa, xg = X[2], X[3], X[4], X[5]
         wl = torch.tanh(xw @ self.w1) @ self.w2
@@ -214,9 +230,9 @@ class RWKV_Tmix_x070(nn.Module):
         layer 0.  Returns (out (Bs, C), v_first)."""
         Bs, C = x.shape
         H = self.n_head
-        mix = torch.cat([self.x_r, self.x_k, self.x_v, self.x_w, self.x_a, self.x_g]).view(6, C)
+        mix, wrkv = self._packed_weights()
         X = fz.lerp(x, mix, 1, prev=x_prev)  # (6, Bs, C)
-        rkv = torch.bmm(X[0:3], torch.stack([self.receptance.weight, self.key.weight, self.value.weight]).transpose(1, 2))
+        rkv = torch.bmm(X[0:3], wrkv)
         r, k, v = rkv[0], rkv[1], rkv[2]
         xv, xw, xa, xg = X[2], X[3], X[4], X[5]
         wl = torch.tanh(xw @ self.w1) @ self.w2

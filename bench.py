@@ -93,7 +93,7 @@ class ClockSampler:
             self.fh = open(self.out, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", uuid, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=self.fh, stderr=subprocess.DEVNULL)
+                 "-lms", "50"], stdout=self.fh, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
 

@@ -93,3 +93,22 @@ def test_model_forward_loss_equals_loss_on_full_logits():
         logits, aux = m(idx)
         full = l2_wrap_loss(logits, tg) + aux
     assert abs(float(fused) - float(full)) < 1e-5 * abs(float(full))
+
+
+def test_masked_loss_with_an_empty_mask_is_the_l2_term():
+    """mask all zero: the cross-entropy term is 0 / (0 + 1e-9) = 0 (train.py:355-356) and
+    the loss is the L2 max-logit term alone; its gradient flows only through the maxima."""
+    from rwkv_mlx_b200.loss import head_l2_wrap_loss
+
+    x, w, tg, _ = _case(2, 20, 500, 64, torch.float32, seed=9)
+    mk = torch.zeros(2, 20, device="cuda")
+    xg, wg = x.clone().requires_grad_(True), w.clone().requires_grad_(True)
+    loss = head_l2_wrap_loss(xg, wg, tg, mk, chunk=128)
+    loss.backward()
+    xd = x.double().cpu().requires_grad_(True)
+    wd = w.double().cpu().requires_grad_(True)
+    ref = lo.l2_wrap_loss_masked(xd @ wd.T, tg.cpu(), mk.cpu().double())
+    ref.backward()
+    assert abs(float(loss.detach()) - float(ref.detach())) < 1e-6 * max(1.0, abs(float(ref.detach())))
+    assert rel_rms(xg.grad.double().cpu().numpy(), xd.grad.numpy()) < 1e-4
+    assert rel_rms(wg.grad.double().cpu().numpy(), wd.grad.numpy()) < 1e-4

@@ -52,6 +52,7 @@ SIGNATURES = {
     "rwkv_moe_lora_combine": (_I, [_P] * 7 + [_I] * 6 + [_P]),
     "rwkv_moe_lora_apply_supported": (_I, [_I] * 5),
     "rwkv_moe_lora_apply": (_I, [_P] * 7 + [_I] * 6 + [_P]),
+    "rwkv_moe_set_apply_impl": (_I, [_I]),
     "rwkv_moe_ortho_loss": (_I, [_P] * 2 + [_I] * 4 + [_P]),
     "rwkv_moe_gather_rows": (_I, [_P] * 3 + [_I] * 4 + [_P]),
     "rwkv_moe_lora_up": (_I, [_P] * 5 + [_I] * 5 + [_P]),

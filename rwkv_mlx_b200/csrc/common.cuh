@@ -30,6 +30,7 @@ __device__ __forceinline__ float ldg_f32(const T* p) { return to_f32(__ldg(p)); 
 // Record the CUDA error text for rwkv_last_error() and map to a status.
 int set_cuda_error(cudaError_t e);
 int check_launch();
+int set_error(int code, const char* msg);  // records msg for rwkv_last_error()
 
 inline bool aligned(const void* p, size_t n) { return (reinterpret_cast<uintptr_t>(p) % n) == 0; }
 

@@ -17,7 +17,7 @@
 namespace rwkv {
 
 constexpr int ROUTER_WARPS = 8;
-constexpr int ROUTER_MAX_CTAS = 148 * 8;
+constexpr int ROUTER_MAX_CTAS = 148 * 2;  // resident at once: the gate weights are staged once per CTA
 constexpr int PERM_TILE = 2048;
 constexpr int PERM_THREADS = 256;
 
@@ -42,11 +42,25 @@ __global__ void __launch_bounds__(ROUTER_WARPS * 32)
                       float* __restrict__ part_f, int32_t* __restrict__ part_c, int ntok, int C,
                       int E, int topk) {
     constexpr int TPW = 32 / EM;
-    extern __shared__ float wsm[];  // [E][C] gate weights
+    extern __shared__ __align__(16) float wsm[];  // [E][C] gate weights (two planes per expert)
     __shared__ float red_f[ROUTER_WARPS][EM + 1];
     __shared__ int red_c[ROUTER_WARPS][EM];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    for (int i = tid; i < E * C; i += blockDim.x) wsm[i] = gate_w[i];
+    // expert e's weights as two planes of C / 2: plane p holds, for each 8-column
+    // vector vi, columns 8 vi + 4 p .. 8 vi + 4 p + 3, so that the lanes of a warp
+    // (consecutive vi) read consecutive 16-byte words (no bank conflicts)
+    if ((reinterpret_cast<uintptr_t>(gate_w) & 15) == 0) {
+        for (int i = tid * 4; i < E * C; i += blockDim.x * 4) {
+            const int e = i / C, c = i - e * C;
+            *reinterpret_cast<float4*>(wsm + e * C + ((c >> 2) & 1) * (C >> 1) + (c >> 3) * 4) =
+                *reinterpret_cast<const float4*>(gate_w + i);
+        }
+    } else {
+        for (int i = tid; i < E * C; i += blockDim.x) {
+            const int e = i / C, c = i - e * C;
+            wsm[e * C + ((c >> 2) & 1) * (C >> 1) + (c >> 3) * 4 + (c & 3)] = gate_w[i];
+        }
+    }
     __syncthreads();
 
     const int grp = lane / EM, el = lane % EM;  // token slot of the pass, expert of this lane
@@ -86,8 +100,8 @@ __global__ void __launch_bounds__(ROUTER_WARPS * 32)
 #pragma unroll
             for (int e = 0; e < EM; e++) {
                 if (e < E) {
-                    const float4 w0 = *reinterpret_cast<const float4*>(wsm + e * C + vi * 8);
-                    const float4 w1 = *reinterpret_cast<const float4*>(wsm + e * C + vi * 8 + 4);
+                    const float4 w0 = *reinterpret_cast<const float4*>(wsm + e * C + vi * 4);
+                    const float4 w1 = *reinterpret_cast<const float4*>(wsm + e * C + (C >> 1) + vi * 4);
 #pragma unroll
                     for (int t = 0; t < TPW; t++) {
                         float a_ = v[t * EM + e];
@@ -931,6 +945,19 @@ static int launch_apply_en(const void* x, const void* base, const void* A, const
     }
 }
 
+namespace rwkv {
+template <typename T>
+int moe_lora_apply_tc(const void* x, const void* base, const void* A, const void* B, const int32_t* inds,
+                      const void* scores, void* out, int ntok, int C, int R, int E, int topk, cudaStream_t st);
+static int g_apply_impl = 0;  // 0 automatic (tcgen05), 1 mma.sync, 2 tcgen05
+}  // namespace rwkv
+
+extern "C" int rwkv_moe_set_apply_impl(int impl) {
+    if (impl < 0 || impl > 2) return RWKV_ERR_ARG;
+    g_apply_impl = impl;
+    return RWKV_OK;
+}
+
 extern "C" int rwkv_moe_lora_apply_supported(int C, int R, int E, int topk, int dtype) {
     const int en = E * R;
     return (dtype == RWKV_F16 || dtype == RWKV_BF16) && C > 0 && C % 64 == 0 && R > 0 && R % 8 == 0 &&
@@ -947,8 +974,12 @@ extern "C" int rwkv_moe_lora_apply(const void* x, const void* base, const void* 
     if (!aligned(x, 16) || !aligned(A, 16) || !aligned(B, 16) || !aligned(out, 16) || (base && !aligned(base, 16)))
         return RWKV_ERR_ALIGN;
     cudaStream_t st = (cudaStream_t)stream;
-    if (dtype == RWKV_F16) return launch_apply_en<__half>(x, base, A, B, inds, scores, out, ntok, C, R, E, topk, st);
-    return launch_apply_en<__nv_bfloat16>(x, base, A, B, inds, scores, out, ntok, C, R, E, topk, st);
+    if (g_apply_impl == 1) {
+        if (dtype == RWKV_F16) return launch_apply_en<__half>(x, base, A, B, inds, scores, out, ntok, C, R, E, topk, st);
+        return launch_apply_en<__nv_bfloat16>(x, base, A, B, inds, scores, out, ntok, C, R, E, topk, st);
+    }
+    if (dtype == RWKV_F16) return moe_lora_apply_tc<__half>(x, base, A, B, inds, scores, out, ntok, C, R, E, topk, st);
+    return moe_lora_apply_tc<__nv_bfloat16>(x, base, A, B, inds, scores, out, ntok, C, R, E, topk, st);
 }
 
 extern "C" int rwkv_moe_ortho_loss(const void* A, float* out, int E, int C, int R, int dtype,

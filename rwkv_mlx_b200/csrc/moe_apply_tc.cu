@@ -1,0 +1,419 @@
+// Fused LoRA-MoE adapter apply on the 5th-generation tensor cores (tcgen05) with TMA:
+//
+//   out = base + sum_s scores[:, s] * (x @ A[e_s]) @ B[e_s]        (rwkv_mlx/moe.py:142-147)
+//
+// with the E adapters concatenated: Acat = [A_0 | ... | A_{E-1}] (C x EN, EN = E * R) and
+// Bcat = [B_0; ...; B_{E-1}] (EN x C).  Per tile of 128 tokens (one TMEM lane each):
+//   down   D1 = X Acat            M = 128, N = EN, K = C in slices of 64 channels
+//   route  H  = T(D1 * g)         g[token, e * R + r] = the token's score for expert e
+//                                 (0 for experts it was not routed to), rounded to the
+//                                 activation type as the reference's fp16 product is
+//   up     D2 = H Bcat            M = 128, N = 64 channels per chunk, K = EN
+//   out    = T(base + D2)
+//
+// Data movement is all TMA (no multicast): x, base and out move as 128-byte-swizzled
+// 64-channel x 128-token boxes, Bcat slices as 128-byte-swizzled 64-channel x EN boxes
+// (the MN-major operand layout of the up MMA), and Acat slices through a 4-d view of A
+// (E, C, R) whose box lands directly in the no-swizzle MN-major layout of the down MMA.
+// The CTA is persistent over tiles and warp-specialised:
+//   warp 4 lane 0   producer: a ring of NS stages, one "job" per stage (a down slice:
+//                   X + Acat; an up chunk: Bcat + base), armed with expect_tx;
+//   warp 5 lane 0   MMA issuer: commits each job to the stage's barrier (down) or to the
+//                   up accumulator's barrier (two TMEM buffers of 64 columns);
+//   warps 0-3       epilogue: H per tile (TMEM -> routing scale -> shared memory), and per
+//                   up chunk TMEM + base -> out in place in the stage, stored by TMA.
+// Every wait is bounded: a wait that gives up sets the CTA's abort flag and the device
+// error word, and every role leaves its loop.
+#include <cuda.h>
+
+#include <mutex>
+
+#include "tc_common.cuh"
+
+namespace rwkv {
+
+__device__ int g_device_error_moe;  // set by a kernel that gave up a bounded wait
+
+namespace atc {
+using namespace tcc;
+
+constexpr int TM = 128;  // tokens per tile
+constexpr int KS = 64;   // channels per down slice (one 128-byte swizzle row of x)
+constexpr int NC = 64;   // channels per up chunk
+constexpr int NEPI = 128;
+constexpr int NTH = NEPI + 64;  // epilogue warps 0-3, producer warp 4, MMA warp 5
+constexpr int NS = 5;           // ring stages
+constexpr int BAR_EPI = 1;      // named barrier of the epilogue warps
+constexpr int X_BYTES = TM * KS * 2;  // 128 rows x 128 bytes, swizzled
+constexpr int O_BYTES = TM * NC * 2;
+constexpr int H_LBO = (TM / 8) * 128;  // H: K-major, no swizzle, 8-row groups adjacent
+
+template <int EN>
+struct Geo {
+    static constexpr int A_BYTES = KS * EN * 2;  // MN-major: K groups 128 B apart, N groups 1024 B
+    static constexpr int B_BYTES = EN * NC * 2;  // EN rows x 128 bytes, swizzled
+    static constexpr int P1 = X_BYTES + A_BYTES, P2 = B_BYTES + O_BYTES;
+    static constexpr int STAGE = ((P1 > P2 ? P1 : P2) + 1023) / 1024 * 1024;
+    static constexpr int H_BYTES = (EN / 8) * H_LBO;
+    static constexpr int CTRL = 1024;
+    static constexpr int SMEM = 1024 /* alignment slack */ + CTRL + H_BYTES + NS * STAGE;
+    static_assert(SMEM <= 227 * 1024, "shared memory");
+    static_assert(EN % 32 == 0 && EN + 2 * NC <= 256, "TMEM columns");
+};
+struct Ctrl {
+    unsigned long long full[NS];   // stage landed (producer expect_tx + TMA bytes)
+    unsigned long long empty[NS];  // stage free (MMA commit of a down slice / epilogue of an up chunk)
+    unsigned long long d2_full[2], d2_empty[2];  // up-projection accumulators (double buffer)
+    unsigned long long d1_full, h_full;          // down-projection done / H written
+    uint32_t tmem_base;
+    int abort;
+};
+
+// 128-byte-swizzled (layout type 2) shared-memory descriptor
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    return umma_desc_ls(saddr, lbo, sbo) | (2ull << 61);
+}
+
+__device__ __forceinline__ void expect_tx(unsigned long long* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(ck::smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* m, int x, int y, unsigned long long* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            ck::smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(m)), "r"(x), "r"(y), "r"(ck::smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* m, int x, int y, int z, int w,
+                                            unsigned long long* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(
+            ck::smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(m)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(ck::smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* m, int x, int y, const void* src) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                     reinterpret_cast<uint64_t>(m)),
+                 "r"(x), "r"(y), "r"(ck::smem_u32(src))
+                 : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+}  // namespace atc
+
+template <typename T, int EN>
+__global__ void __launch_bounds__(atc::NTH, 1)
+    moe_lora_apply_tc_kernel(const __grid_constant__ CUtensorMap mx, const __grid_constant__ CUtensorMap ma,
+                             const __grid_constant__ CUtensorMap mb, const __grid_constant__ CUtensorMap mbase,
+                             const __grid_constant__ CUtensorMap mout, int has_base,
+                             const int32_t* __restrict__ inds, const T* __restrict__ scores, int ntok, int C,
+                             int R, int topk) {
+    using namespace atc;
+    using G = Geo<EN>;
+    constexpr bool BF = std::is_same<T, __nv_bfloat16>::value;
+    constexpr uint32_t IDESC_DOWN = idesc_16(TM, EN, BF, false, true);
+    constexpr uint32_t IDESC_UP = idesc_16(TM, NC, BF, false, true);
+
+    extern __shared__ __align__(1024) unsigned char smem_atc_raw[];
+    // the swizzled tiles need 1024-byte alignment of the shared-memory address
+    const uint32_t raw_addr = ck::smem_u32(smem_atc_raw);
+    unsigned char* smem = smem_atc_raw + (((raw_addr + 1023) & ~1023u) - raw_addr);
+    Ctrl& cs = *reinterpret_cast<Ctrl*>(smem);
+    unsigned char* hs = smem + G::CTRL;
+    unsigned char* ring = hs + G::H_BYTES;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int nsl = C / KS, nch = C / NC, jpt = nsl + nch;
+    const int ntiles = (ntok + TM - 1) / TM;
+    const int my_tiles = (int)blockIdx.x < ntiles ? (ntiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    const int njobs = my_tiles * jpt;
+
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(
+                         ck::smem_u32(&cs.tmem_base))
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    if (tid == NEPI) {
+        for (int i = 0; i < NS; i++) ck::mbar_init(&cs.full[i], 1), ck::mbar_init(&cs.empty[i], 1);
+        for (int i = 0; i < 2; i++) ck::mbar_init(&cs.d2_full[i], 1), ck::mbar_init(&cs.d2_empty[i], NEPI);
+        ck::mbar_init(&cs.d1_full, 1);
+        ck::mbar_init(&cs.h_full, NEPI);
+        cs.abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = cs.tmem_base;
+    auto tile0 = [&](int lt) { return ((int)blockIdx.x + lt * (int)gridDim.x) * TM; };
+    int* err = &g_device_error_moe;
+
+    if (warp == NEPI / 32) {
+        // ============ producer: TMA of job g into stage g % NS ============
+        if (lane == 0) {
+            for (int g = 0; g < njobs; g++) {
+                const int s = g % NS;
+                if (g >= NS && !ck::mbar_wait(&cs.empty[s], ((g / NS) + 1) & 1, &cs.abort, err)) break;
+                const int lt = g / jpt, jj = g - lt * jpt, t0 = tile0(lt);
+                unsigned char* st = ring + s * G::STAGE;
+                if (jj < nsl) {
+                    expect_tx(&cs.full[s], X_BYTES + G::A_BYTES);
+                    tma_load_2d(st, &mx, jj * KS, t0, &cs.full[s]);
+                    tma_load_4d(st + X_BYTES, &ma, 0, jj * KS, 0, 0, &cs.full[s]);
+                } else {
+                    const int cj = (jj - nsl) * NC;
+                    expect_tx(&cs.full[s], G::B_BYTES + (has_base ? O_BYTES : 0));
+                    tma_load_2d(st, &mb, cj, 0, &cs.full[s]);
+                    if (has_base) tma_load_2d(st + G::B_BYTES, &mbase, cj, t0, &cs.full[s]);
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp == NEPI / 32 + 1) {
+        // ============ MMA issuer ============
+        if (lane == 0) {
+            int q = 0;  // up chunks issued so far (TMEM buffer q & 1, use q >> 1)
+            for (int g = 0; g < njobs; g++) {
+                const int s = g % NS, lt = g / jpt, jj = g - lt * jpt;
+                if (!ck::mbar_wait(&cs.full[s], (g / NS) & 1, &cs.abort, err)) break;
+                if (jj == nsl && !ck::mbar_wait(&cs.h_full, lt & 1, &cs.abort, err)) break;
+                if (jj >= nsl && q >= 2 && !ck::mbar_wait(&cs.d2_empty[q & 1], ((q >> 1) + 1) & 1, &cs.abort, err))
+                    break;
+                tc_fence_after();
+                const uint32_t st = ck::smem_u32(ring + s * G::STAGE);
+                if (jj < nsl) {
+                    // A = x slice (K-major, 128-byte swizzle: K step = 32 bytes within the row),
+                    // B = Acat slice (MN-major, no swizzle: K groups 128 B, N groups 1024 B)
+#pragma unroll
+                    for (int kk = 0; kk < KS / 16; kk++)
+                        umma16(tmem, desc_sw128(st + kk * 32, 16, 1024),
+                               umma_desc_ls(st + X_BYTES + kk * 256, 128, 1024), IDESC_DOWN,
+                               (jj > 0 || kk > 0) ? 1u : 0u);
+                    umma_commit(&cs.empty[s]);
+                    if (jj == nsl - 1) umma_commit(&cs.d1_full);
+                } else {
+                    // A = H (K-major, no swizzle), B = Bcat slice (MN-major, 128-byte swizzle:
+                    // 8 K rows of 128 bytes per 1024-byte group)
+                    const uint32_t h = ck::smem_u32(hs), d2 = tmem + EN + (q & 1) * NC;
+#pragma unroll
+                    for (int kk = 0; kk < EN / 16; kk++)
+                        umma16(d2, umma_desc_ls(h + 2 * kk * H_LBO, H_LBO, 128), desc_sw128(st + kk * 2048, 8192, 1024),
+                               IDESC_UP, kk > 0 ? 1u : 0u);
+                    umma_commit(&cs.d2_full[q & 1]);
+                    q++;
+                }
+            }
+        }
+        __syncwarp();
+    } else {
+        // ============ epilogue warps 0-3: H per tile, out per up chunk ============
+        const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
+        const int row = tid;  // token row of the tile = TMEM lane
+        int q = 0, pend = -1;  // up chunks done; stage of the last store still reading smem (row 0)
+        bool bad = false;
+        for (int lt = 0; lt < my_tiles && !bad; lt++) {
+            const int t0 = tile0(lt), tok = t0 + row;
+            {
+                const int kq = tok < ntok ? topk : 0;
+                int es[8];
+                float ss[8];
+#pragma unroll
+                for (int s = 0; s < 8; s++) {
+                    es[s] = s < kq ? inds[(size_t)tok * topk + s] : -1;
+                    ss[s] = s < kq ? (scores ? to_f32(scores[(size_t)tok * topk + s]) : 1.f) : 0.f;
+                }
+                bad = ck::bar_or_n(BAR_EPI, NEPI, !ck::mbar_wait(&cs.d1_full, lt & 1, &cs.abort, err));
+                if (bad) break;  // the vote keeps the 128 threads together for the named barriers
+                tc_fence_after();
+#pragma unroll
+                for (int h0 = 0; h0 < EN; h0 += 32) {
+                    float v[32];
+                    tmem_ld16(tmem + lane_base + h0, v);
+                    tmem_ld16(tmem + lane_base + h0 + 16, v + 16);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int c = 0; c < 32; c += 8) {
+                        const int col = h0 + c, e = col / R;
+                        float gs = 0.f;
+#pragma unroll
+                        for (int s = 0; s < 8; s++) gs += es[s] == e ? ss[s] : 0.f;
+                        uint4 pk;
+                        T* pe = reinterpret_cast<T*>(&pk);
+#pragma unroll
+                        for (int u = 0; u < 8; u++) pe[u] = from_f32<T>(v[c + u] * gs);
+                        *reinterpret_cast<uint4*>(hs + row * 16 + (col >> 3) * H_LBO) = pk;
+                    }
+                }
+                proxy_fence();
+                tc_fence_before();
+                ck::mbar_arrive(&cs.h_full);
+            }
+            for (int j = 0; j < nch; j++, q++) {
+                const int g = lt * jpt + nsl + j, s = g % NS;
+                unsigned char* os = ring + s * G::STAGE + G::B_BYTES;
+                bad = !ck::mbar_wait(&cs.d2_full[q & 1], (q >> 1) & 1, &cs.abort, err) ||
+                      !ck::mbar_wait(&cs.full[s], (g / NS) & 1, &cs.abort, err);
+                bad = ck::bar_or_n(BAR_EPI, NEPI, bad);
+                if (bad) break;
+                tc_fence_after();
+                float v[NC];
+                const uint32_t ta = tmem + lane_base + EN + (q & 1) * NC;
+#pragma unroll
+                for (int c = 0; c < NC; c += 16) tmem_ld16(ta + c, v + c);
+                tmem_wait_ld();
+                tc_fence_before();
+                ck::mbar_arrive(&cs.d2_empty[q & 1]);
+                // this row of the 128-byte-swizzled base / out box: 16-byte piece c sits at c ^ (row % 8)
+                unsigned char* orow = os + row * 128;
+#pragma unroll
+                for (int c = 0; c < NC / 8; c++) {
+                    unsigned char* pp = orow + ((c ^ (row & 7)) << 4);
+                    uint4 raw = has_base ? *reinterpret_cast<const uint4*>(pp) : make_uint4(0u, 0u, 0u, 0u);
+                    T* e = reinterpret_cast<T*>(&raw);
+#pragma unroll
+                    for (int u = 0; u < 8; u++) e[u] = from_f32<T>(v[8 * c + u] + to_f32(e[u]));
+                    *reinterpret_cast<uint4*>(pp) = raw;
+                }
+                proxy_fence();  // the TMA store reads these bytes through the async proxy
+                ck::bar_sync_n(BAR_EPI, NEPI);
+                if (row == 0) {
+                    tma_store_2d(&mout, j * NC, t0, os);  // rows past ntok are not written
+                    if (j + 1 < nch) {
+                        bulk_wait_read<1>();  // the previous chunk's store has read its stage
+                        if (pend >= 0) ck::mbar_arrive(&cs.empty[pend]);
+                        pend = s;
+                    } else {  // last chunk of the tile: release both now (the next tile's
+                        bulk_wait_read<0>();  // down slices may need these stages)
+                        if (pend >= 0) ck::mbar_arrive(&cs.empty[pend]);
+                        ck::mbar_arrive(&cs.empty[s]);
+                        pend = -1;
+                    }
+                }
+            }
+        }
+        if (row == 0) bulk_wait_all();
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem) : "memory");
+    }
+}
+
+namespace atc {
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link-time
+// dependency on the driver library).
+static EncodeFn encoder() {
+    static EncodeFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeFn>(p);
+    });
+    return fn;
+}
+
+// Tensor map of rank `rank` over `base` (dims[0] contiguous; strides in bytes for
+// dims 1..rank-1), box `box`, zero fill out of bounds.
+static int make_map(CUtensorMap* m, bool bf16, const void* base, int rank, const cuuint64_t* dims,
+                    const cuuint64_t* strides, const cuuint32_t* box, bool swizzle128) {
+    EncodeFn enc = encoder();
+    if (!enc) return set_error(RWKV_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+    const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    const CUresult r = enc(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                           (cuuint32_t)rank, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(RWKV_ERR_CUDA, "cuTensorMapEncodeTiled rejected a tensor map");
+    return RWKV_OK;
+}
+}  // namespace atc
+
+template <typename T, int EN>
+static int launch_apply_tc(const void* x, const void* base, const void* A, const void* B, const int32_t* inds,
+                           const void* scores, void* out, int ntok, int C, int R, int topk, cudaStream_t st) {
+    using namespace atc;
+    constexpr bool BF = std::is_same<T, __nv_bfloat16>::value;
+    const int E = EN / R, rp = R / 8;
+    alignas(64) CUtensorMap mx, ma, mb, mbase, mout;
+    const cuuint64_t row_stride[1] = {(cuuint64_t)C * 2};
+    {  // x, base, out: (ntok, C) row-major; box 64 channels x 128 tokens, 128-byte swizzle
+        const cuuint64_t dims[2] = {(cuuint64_t)C, (cuuint64_t)ntok};
+        const cuuint32_t box[2] = {(cuuint32_t)KS, (cuuint32_t)TM};
+        int rc = make_map(&mx, BF, x, 2, dims, row_stride, box, true);
+        if (!rc) rc = make_map(&mout, BF, out, 2, dims, row_stride, box, true);
+        if (!rc) rc = make_map(&mbase, BF, base ? base : x, 2, dims, row_stride, box, true);
+        if (rc) return rc;
+    }
+    {  // A (E, C, R) as (8 values, C, R / 8 pieces, E): one box is a 64-channel Acat slice
+        // in MN-major core matrices (8 channels x 16 bytes), N group e * R / 8 + piece
+        const cuuint64_t dims[4] = {8, (cuuint64_t)C, (cuuint64_t)rp, (cuuint64_t)E};
+        const cuuint64_t strides[3] = {(cuuint64_t)R * 2, 16, (cuuint64_t)C * R * 2};
+        const cuuint32_t box[4] = {8, (cuuint32_t)KS, (cuuint32_t)rp, (cuuint32_t)E};
+        const int rc = make_map(&ma, BF, A, 4, dims, strides, box, false);
+        if (rc) return rc;
+    }
+    {  // B (E, R, C) = Bcat (EN, C): box 64 channels x EN rows, 128-byte swizzle
+        const cuuint64_t dims[2] = {(cuuint64_t)C, (cuuint64_t)EN};
+        const cuuint32_t box[2] = {(cuuint32_t)NC, (cuuint32_t)EN};
+        const int rc = make_map(&mb, BF, B, 2, dims, row_stride, box, true);
+        if (rc) return rc;
+    }
+    auto kern = moe_lora_apply_tc_kernel<T, EN>;
+    const int smem = Geo<EN>::SMEM;
+    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (err != cudaSuccess) return set_cuda_error(err);
+    int dev = 0, nsm = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    const int ntiles = (ntok + TM - 1) / TM;
+    const int grid = ntiles < nsm ? ntiles : nsm;  // persistent: one CTA per SM
+    kern<<<grid, NTH, smem, st>>>(mx, ma, mb, mbase, mout, base ? 1 : 0, inds, (const T*)scores, ntok, C, R, topk);
+    return check_launch();
+}
+
+template <typename T>
+int moe_lora_apply_tc(const void* x, const void* base, const void* A, const void* B, const int32_t* inds,
+                      const void* scores, void* out, int ntok, int C, int R, int E, int topk, cudaStream_t st) {
+    switch (E * R) {
+        case 32: return launch_apply_tc<T, 32>(x, base, A, B, inds, scores, out, ntok, C, R, topk, st);
+        case 64: return launch_apply_tc<T, 64>(x, base, A, B, inds, scores, out, ntok, C, R, topk, st);
+        case 128: return launch_apply_tc<T, 128>(x, base, A, B, inds, scores, out, ntok, C, R, topk, st);
+        default: return RWKV_ERR_SHAPE;
+    }
+}
+template int moe_lora_apply_tc<__half>(const void*, const void*, const void*, const void*, const int32_t*,
+                                       const void*, void*, int, int, int, int, int, cudaStream_t);
+template int moe_lora_apply_tc<__nv_bfloat16>(const void*, const void*, const void*, const void*,
+                                              const int32_t*, const void*, void*, int, int, int, int, int,
+                                              cudaStream_t);
+
+int read_device_error_moe(int clear) {
+    int v = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&v, g_device_error_moe, sizeof(int));
+    if (e != cudaSuccess) return -set_cuda_error(e);
+    if (clear && v) {
+        const int z = 0;
+        e = cudaMemcpyToSymbol(g_device_error_moe, &z, sizeof(int));
+        if (e != cudaSuccess) return -set_cuda_error(e);
+    }
+    return v;
+}
+
+}  // namespace rwkv

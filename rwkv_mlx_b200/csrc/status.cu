@@ -14,6 +14,11 @@ int set_cuda_error(cudaError_t e) {
 }
 
 int check_launch() { return set_cuda_error(cudaGetLastError()); }
+
+int set_error(int code, const char* msg) {
+    snprintf(g_err, sizeof(g_err), "%s", msg);
+    return code;
+}
 }  // namespace rwkv
 
 extern "C" const char* rwkv_last_error(void) { return rwkv::g_err; }

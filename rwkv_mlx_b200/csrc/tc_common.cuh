@@ -25,6 +25,20 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t sbo) {
     return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)((KLBO >> 4) & 0x3FFF) << 16) |
            ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46);
 }
+// No-swizzle descriptor with an explicit K-direction core-matrix stride (lbo) and
+// M/N-direction stride (sbo), for K-major and MN-major operands alike.  A K-major
+// core matrix is 8 M/N rows x 16 bytes of K; an MN-major one is 8 K rows x 16 bytes
+// of M/N; either is 128 contiguous bytes.
+__device__ __forceinline__ uint64_t umma_desc_ls(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46);
+}
+// kind::f16 instruction descriptor: fp32 accumulate, A and B both fp16 or both bf16,
+// each K-major or MN-major.
+__host__ __device__ constexpr uint32_t idesc_16(int M, int Nn, bool bf16, bool a_mn, bool b_mn) {
+    return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | ((a_mn ? 1u : 0u) << 15) |
+           ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(Nn >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
 // Instruction descriptors: fp32 accumulate, A and B K-major, M x N.
 __host__ __device__ constexpr uint32_t idesc_tf32(int M, int Nn) {
     return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(Nn >> 3) << 17) | ((uint32_t)(M >> 4) << 24);

@@ -27,6 +27,7 @@ bool wkv7_tc_supported(int dtype);
 int read_device_error_tc(int clear);
 int read_device_error_bwd(int clear);
 int read_device_error(int clear);
+int read_device_error_moe(int clear);
 extern int g_wkv_impl;  // 0 auto, 1 step-sequential, 2 chunked (mma.sync), 3 chunked (tcgen05)
 int wkv7_bwd_seq(const WkvBwdArgs& p, cudaStream_t st);
 size_t wkv7_bwd_chunk_ws_bytes(int B, int T, int H);

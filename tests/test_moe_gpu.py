@@ -140,12 +140,23 @@ def test_lora_moe_cmix_module_matches_oracle():
     assert abs(float(ol) - ol_ref) < 1e-3 * max(1e-6, ol_ref)
 
 
+@pytest.fixture(params=[2, 1], ids=["tcgen05", "mma_sync"])
+def apply_impl(request):
+    """Run a test on each kernel of rwkv_moe_lora_apply (process-wide switch, reset after)."""
+    from rwkv_mlx_b200 import _native
+
+    assert _native.lib().rwkv_moe_set_apply_impl(request.param) == 0
+    yield request.param
+    assert _native.lib().rwkv_moe_set_apply_impl(0) == 0
+
+
 @pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("ntok,C,E,R,k,with_base", [(2000, 768, 8, 16, 2, True), (4097, 1024, 4, 8, 1, False),
                                                     (77, 64, 8, 8, 3, True), (130, 128, 16, 8, 4, True),
-                                                    (65, 768, 2, 16, 2, True)])
-def test_lora_apply_matches_oracle(dt, ntok, C, E, R, k, with_base):
-    """Fused adapter apply (dense over E*R columns, routing mask) vs the float64 sum."""
+                                                    (65, 768, 2, 16, 2, True), (40000, 768, 8, 16, 2, True)])
+def test_lora_apply_matches_oracle(apply_impl, dt, ntok, C, E, R, k, with_base):
+    """Fused adapter apply (dense over E*R columns, routing mask) vs the float64 sum;
+    40000 tokens = 313 tiles of 128, more than one per SM for the persistent kernel."""
     from rwkv_mlx_b200.moe import lora_apply, lora_apply_supported, router_forward
 
     assert lora_apply_supported(C, R, E, k, dt)
@@ -165,9 +176,12 @@ def test_lora_apply_matches_oracle(dt, ntok, C, E, R, k, with_base):
     ref = delta + (npy(base) if with_base else 0.0)
     tol = {torch.float16: 2e-3, torch.bfloat16: 8e-3}[dt] if with_base else {torch.float16: 4e-3, torch.bfloat16: 2e-2}[dt]
     assert rel_rms(npy(out), ref) < tol
+    from rwkv_mlx_b200 import _native
+
+    assert _native.lib().rwkv_device_error(1) == 0
 
 
-def test_lora_apply_in_place_and_no_scores():
+def test_lora_apply_in_place_and_no_scores(apply_impl):
     """out aliasing base, scores NULL (all 1): the EP local step's form."""
     from rwkv_mlx_b200.moe import lora_apply
 

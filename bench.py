@@ -385,7 +385,7 @@ def run_moe(args, ws, rank, dev):
 
     def moe_only():
         r = router_forward(x2, layer.router.gate.weight, 2, layer.router.bias)
-        return lora_apply(x2, base_out, Ah, Bh, r["inds"], r["scores"])
+        return lora_apply(x2, base_out, Ah, Bh, r["inds"], r["scores"], out=base_out)  # as the module does
 
     for _ in range(args.warmup):
         moe_only()

@@ -9,19 +9,23 @@
 //                                 (0 for experts it was not routed to), rounded to the
 //                                 activation type as the reference's fp16 product is
 //   up     D2 = H Bcat            M = 128, N = 64 channels per chunk, K = EN
-//   out    = T(base + D2)
+//   out    = T(base + D2), or, when out is base, out += T(D2) by a TMA reduce-add store
+//          (base is then never loaded into the SM: the add happens in L2)
 //
 // Data movement is all TMA (no multicast): x, base and out move as 128-byte-swizzled
 // 64-channel x 128-token boxes, Bcat slices as 128-byte-swizzled 64-channel x EN boxes
 // (the MN-major operand layout of the up MMA), and Acat slices through a 4-d view of A
 // (E, C, R) whose box lands directly in the no-swizzle MN-major layout of the down MMA.
 // The CTA is persistent over tiles and warp-specialised:
-//   warp 4 lane 0   producer: a ring of NS stages, one "job" per stage (a down slice:
-//                   X + Acat; an up chunk: Bcat + base), armed with expect_tx;
-//   warp 5 lane 0   MMA issuer: commits each job to the stage's barrier (down) or to the
-//                   up accumulator's barrier (two TMEM buffers of 64 columns);
-//   warps 0-3       epilogue: H per tile (TMEM -> routing scale -> shared memory), and per
-//                   up chunk TMEM + base -> out in place in the stage, stored by TMA.
+//   warp 4 lane 0   producer: one "job" (a down slice: x + Acat slices; an up chunk: Bcat +
+//                   base slices) per stage of two rings, activations (NA deep: they come
+//                   from HBM) and adapter slices (NW deep: L2), armed with expect_tx;
+//   warp 5 lane 0   MMA issuer: commits each job to its stages' barriers and to the up
+//                   accumulator's barrier; TMEM holds two D1 accumulators (EN columns
+//                   each: tiles alternate), two up accumulators of 64 columns and H
+//                   (EN / 2 columns of packed 16-bit pairs, the A operand of the up MMA);
+//   warps 0-3       epilogue: H per tile (TMEM -> routing scale -> TMEM), and per up chunk
+//                   TMEM + base -> out in place in the activation stage, stored by TMA.
 // Every wait is bounded: a wait that gives up sets the CTA's abort flag and the device
 // error word, and every role leaves its loop.
 #include <cuda.h>
@@ -40,31 +44,32 @@ using namespace tcc;
 constexpr int TM = 128;  // tokens per tile
 constexpr int KS = 64;   // channels per down slice (one 128-byte swizzle row of x)
 constexpr int NC = 64;   // channels per up chunk
-constexpr int NEPI = 128;
-constexpr int NTH = NEPI + 64;  // epilogue warps 0-3, producer warp 4, MMA warp 5
-constexpr int NS = 5;           // ring stages
+constexpr int NEPI = 256;       // epilogue warps 0-7: warps w and w + 4 share TMEM lanes 32 (w % 4) ..
+constexpr int NTH = NEPI + 96;  // producer warp 8, MMA warp 9, store warp 10
+constexpr int NA = 10, NW = 4;  // stages of the activation ring (x / base+out) and the adapter ring
 constexpr int BAR_EPI = 1;      // named barrier of the epilogue warps
 constexpr int X_BYTES = TM * KS * 2;  // 128 rows x 128 bytes, swizzled
 constexpr int O_BYTES = TM * NC * 2;
-constexpr int H_LBO = (TM / 8) * 128;  // H: K-major, no swizzle, 8-row groups adjacent
 
 template <int EN>
 struct Geo {
     static constexpr int A_BYTES = KS * EN * 2;  // MN-major: K groups 128 B apart, N groups 1024 B
     static constexpr int B_BYTES = EN * NC * 2;  // EN rows x 128 bytes, swizzled
-    static constexpr int P1 = X_BYTES + A_BYTES, P2 = B_BYTES + O_BYTES;
-    static constexpr int STAGE = ((P1 > P2 ? P1 : P2) + 1023) / 1024 * 1024;
-    static constexpr int H_BYTES = (EN / 8) * H_LBO;
+    static constexpr int W_STAGE = ((A_BYTES > B_BYTES ? A_BYTES : B_BYTES) + 1023) / 1024 * 1024;
+    static constexpr int A_STAGE = X_BYTES;      // = O_BYTES
     static constexpr int CTRL = 1024;
-    static constexpr int SMEM = 1024 /* alignment slack */ + CTRL + H_BYTES + NS * STAGE;
+    static constexpr int SMEM = 1024 /* alignment slack */ + CTRL + NA * A_STAGE + NW * W_STAGE;
+    // TMEM columns: two D1 accumulators (tiles alternate), two up accumulators, H
+    static constexpr int T_D2 = 2 * EN, T_H = 2 * EN + 2 * NC;
     static_assert(SMEM <= 227 * 1024, "shared memory");
-    static_assert(EN % 32 == 0 && EN + 2 * NC <= 256, "TMEM columns");
+    static_assert(EN % 32 == 0 && T_H + EN / 2 <= 512, "TMEM columns");
 };
 struct Ctrl {
-    unsigned long long full[NS];   // stage landed (producer expect_tx + TMA bytes)
-    unsigned long long empty[NS];  // stage free (MMA commit of a down slice / epilogue of an up chunk)
+    unsigned long long full_a[NA], empty_a[NA];  // activation stages: landed / free
+    unsigned long long full_w[NW], empty_w[NW];  // adapter stages
     unsigned long long d2_full[2], d2_empty[2];  // up-projection accumulators (double buffer)
     unsigned long long d1_full, h_full;          // down-projection done / H written
+    unsigned long long out_full[2], out_empty[2];  // out box of an up chunk ready / taken by the store warp
     uint32_t tmem_base;
     int abort;
 };
@@ -93,6 +98,14 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* m, int
         "l"(reinterpret_cast<uint64_t>(m)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(ck::smem_u32(bar))
         : "memory");
 }
+// out += box (element-wise add in the memory system, in the tensor map's type)
+__device__ __forceinline__ void tma_add_2d(const CUtensorMap* m, int x, int y, const void* src) {
+    asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                     reinterpret_cast<uint64_t>(m)),
+                 "r"(x), "r"(y), "r"(ck::smem_u32(src))
+                 : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* m, int x, int y, const void* src) {
     asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
                      reinterpret_cast<uint64_t>(m)),
@@ -106,13 +119,34 @@ __device__ __forceinline__ void bulk_wait_read() {
 }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
+// Job order of a CTA with nt tiles and n slices (= chunks) per tile: the down slices of
+// tile 0, then pairs (down slice j of tile t + 1, up chunk j of tile t), then the up
+// chunks of the last tile.  The up epilogues of one tile so overlap the loads and MMAs
+// of the next tile's down projection (into the other D1 accumulator).
+struct Job {
+    bool down;
+    int t, j;
+};
+__device__ __forceinline__ Job job_of(int g, int n, int nt) {
+    if (g < n) return {true, 0, g};
+    const int h = g - n, mid = (nt - 1) * 2 * n;
+    if (h < mid) {
+        const int pr = h >> 1;
+        return (h & 1) ? Job{false, pr / n, pr % n} : Job{true, pr / n + 1, pr % n};
+    }
+    return {false, nt - 1, h - mid};
+}
+__device__ __forceinline__ int up_job_index(int t, int j, int n, int nt) {
+    return t < nt - 1 ? n + t * 2 * n + 2 * j + 1 : n + (nt - 1) * 2 * n + j;
+}
+
 }  // namespace atc
 
 template <typename T, int EN>
 __global__ void __launch_bounds__(atc::NTH, 1)
     moe_lora_apply_tc_kernel(const __grid_constant__ CUtensorMap mx, const __grid_constant__ CUtensorMap ma,
                              const __grid_constant__ CUtensorMap mb, const __grid_constant__ CUtensorMap mbase,
-                             const __grid_constant__ CUtensorMap mout, int has_base,
+                             const __grid_constant__ CUtensorMap mout, int has_base, int accum,
                              const int32_t* __restrict__ inds, const T* __restrict__ scores, int ntok, int C,
                              int R, int topk) {
     using namespace atc;
@@ -126,25 +160,27 @@ __global__ void __launch_bounds__(atc::NTH, 1)
     const uint32_t raw_addr = ck::smem_u32(smem_atc_raw);
     unsigned char* smem = smem_atc_raw + (((raw_addr + 1023) & ~1023u) - raw_addr);
     Ctrl& cs = *reinterpret_cast<Ctrl*>(smem);
-    unsigned char* hs = smem + G::CTRL;
-    unsigned char* ring = hs + G::H_BYTES;
+    unsigned char* ring_a = smem + G::CTRL;
+    unsigned char* ring_w = ring_a + NA * G::A_STAGE;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int nsl = C / KS, nch = C / NC, jpt = nsl + nch;
+    const int nsl = C / KS, nch = C / NC;  // equal: KS == NC
     const int ntiles = (ntok + TM - 1) / TM;
     const int my_tiles = (int)blockIdx.x < ntiles ? (ntiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-    const int njobs = my_tiles * jpt;
+    const int njobs = my_tiles * (nsl + nch);
 
     if (warp == 0) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(
                          ck::smem_u32(&cs.tmem_base))
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     if (tid == NEPI) {
-        for (int i = 0; i < NS; i++) ck::mbar_init(&cs.full[i], 1), ck::mbar_init(&cs.empty[i], 1);
+        for (int i = 0; i < NA; i++) ck::mbar_init(&cs.full_a[i], 1), ck::mbar_init(&cs.empty_a[i], 1);
+        for (int i = 0; i < NW; i++) ck::mbar_init(&cs.full_w[i], 1), ck::mbar_init(&cs.empty_w[i], 1);
         for (int i = 0; i < 2; i++) ck::mbar_init(&cs.d2_full[i], 1), ck::mbar_init(&cs.d2_empty[i], NEPI);
         ck::mbar_init(&cs.d1_full, 1);
         ck::mbar_init(&cs.h_full, NEPI);
+        for (int i = 0; i < 2; i++) ck::mbar_init(&cs.out_full[i], 1), ck::mbar_init(&cs.out_empty[i], 1);
         cs.abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -153,25 +189,38 @@ __global__ void __launch_bounds__(atc::NTH, 1)
     tc_fence_after();
     const uint32_t tmem = cs.tmem_base;
     auto tile0 = [&](int lt) { return ((int)blockIdx.x + lt * (int)gridDim.x) * TM; };
+    // Slice / chunk j of a tile's sequence is channel block (j + tile) % nsl: CTAs working
+    // on neighbouring tiles at the same time then read different adapter slices, instead
+    // of all SMs requesting the same few L2 lines at once.
+    auto blk = [&](int lt, int j) {
+        const int r = j + ((int)blockIdx.x + lt * (int)gridDim.x) % nsl;
+        return r >= nsl ? r - nsl : r;
+    };
     int* err = &g_device_error_moe;
 
     if (warp == NEPI / 32) {
-        // ============ producer: TMA of job g into stage g % NS ============
+        // ============ producer: TMA of job g into activation stage g % NA, adapter stage g % NW ============
         if (lane == 0) {
             for (int g = 0; g < njobs; g++) {
-                const int s = g % NS;
-                if (g >= NS && !ck::mbar_wait(&cs.empty[s], ((g / NS) + 1) & 1, &cs.abort, err)) break;
-                const int lt = g / jpt, jj = g - lt * jpt, t0 = tile0(lt);
-                unsigned char* st = ring + s * G::STAGE;
-                if (jj < nsl) {
-                    expect_tx(&cs.full[s], X_BYTES + G::A_BYTES);
-                    tma_load_2d(st, &mx, jj * KS, t0, &cs.full[s]);
-                    tma_load_4d(st + X_BYTES, &ma, 0, jj * KS, 0, 0, &cs.full[s]);
+                const int sa = g % NA, sw = g % NW;
+                if (g >= NA && !ck::mbar_wait(&cs.empty_a[sa], ((g / NA) + 1) & 1, &cs.abort, err)) break;
+                if (g >= NW && !ck::mbar_wait(&cs.empty_w[sw], ((g / NW) + 1) & 1, &cs.abort, err)) break;
+                const Job jb = job_of(g, nsl, my_tiles);
+                const int t0 = tile0(jb.t);
+                unsigned char* sta = ring_a + sa * G::A_STAGE;
+                unsigned char* stw = ring_w + sw * G::W_STAGE;
+                if (jb.down) {
+                    expect_tx(&cs.full_w[sw], G::A_BYTES);
+                    tma_load_4d(stw, &ma, 0, blk(jb.t, jb.j) * KS, 0, 0, &cs.full_w[sw]);
+                    expect_tx(&cs.full_a[sa], X_BYTES);
+                    tma_load_2d(sta, &mx, blk(jb.t, jb.j) * KS, t0, &cs.full_a[sa]);
                 } else {
-                    const int cj = (jj - nsl) * NC;
-                    expect_tx(&cs.full[s], G::B_BYTES + (has_base ? O_BYTES : 0));
-                    tma_load_2d(st, &mb, cj, 0, &cs.full[s]);
-                    if (has_base) tma_load_2d(st + G::B_BYTES, &mbase, cj, t0, &cs.full[s]);
+                    const int cj = blk(jb.t, jb.j) * NC;
+                    expect_tx(&cs.full_w[sw], G::B_BYTES);
+                    tma_load_2d(stw, &mb, cj, 0, &cs.full_w[sw]);
+                    const bool ld = has_base && !accum;  // accumulating into out = base: nothing to load
+                    expect_tx(&cs.full_a[sa], ld ? O_BYTES : 0);
+                    if (ld) tma_load_2d(sta, &mbase, cj, t0, &cs.full_a[sa]);
                 }
             }
         }
@@ -181,42 +230,76 @@ __global__ void __launch_bounds__(atc::NTH, 1)
         if (lane == 0) {
             int q = 0;  // up chunks issued so far (TMEM buffer q & 1, use q >> 1)
             for (int g = 0; g < njobs; g++) {
-                const int s = g % NS, lt = g / jpt, jj = g - lt * jpt;
-                if (!ck::mbar_wait(&cs.full[s], (g / NS) & 1, &cs.abort, err)) break;
-                if (jj == nsl && !ck::mbar_wait(&cs.h_full, lt & 1, &cs.abort, err)) break;
-                if (jj >= nsl && q >= 2 && !ck::mbar_wait(&cs.d2_empty[q & 1], ((q >> 1) + 1) & 1, &cs.abort, err))
+                const int sa = g % NA, sw = g % NW;
+                const Job jb = job_of(g, nsl, my_tiles);
+                if (!ck::mbar_wait(&cs.full_w[sw], (g / NW) & 1, &cs.abort, err)) break;
+                if (jb.down && !ck::mbar_wait(&cs.full_a[sa], (g / NA) & 1, &cs.abort, err)) break;
+                if (!jb.down && jb.j == 0 && !ck::mbar_wait(&cs.h_full, jb.t & 1, &cs.abort, err)) break;
+                if (!jb.down && q >= 2 && !ck::mbar_wait(&cs.d2_empty[q & 1], ((q >> 1) + 1) & 1, &cs.abort, err))
                     break;
                 tc_fence_after();
-                const uint32_t st = ck::smem_u32(ring + s * G::STAGE);
-                if (jj < nsl) {
+                const uint32_t stw = ck::smem_u32(ring_w + sw * G::W_STAGE);
+                if (jb.down) {
                     // A = x slice (K-major, 128-byte swizzle: K step = 32 bytes within the row),
                     // B = Acat slice (MN-major, no swizzle: K groups 128 B, N groups 1024 B)
+                    const uint32_t sta = ck::smem_u32(ring_a + sa * G::A_STAGE);
 #pragma unroll
                     for (int kk = 0; kk < KS / 16; kk++)
-                        umma16(tmem, desc_sw128(st + kk * 32, 16, 1024),
-                               umma_desc_ls(st + X_BYTES + kk * 256, 128, 1024), IDESC_DOWN,
-                               (jj > 0 || kk > 0) ? 1u : 0u);
-                    umma_commit(&cs.empty[s]);
-                    if (jj == nsl - 1) umma_commit(&cs.d1_full);
+                        umma16(tmem + (jb.t & 1) * EN, desc_sw128(sta + kk * 32, 16, 1024),
+                               umma_desc_ls(stw + kk * 256, 128, 1024), IDESC_DOWN, (jb.j > 0 || kk > 0) ? 1u : 0u);
+                    umma_commit(&cs.empty_a[sa]);
+                    umma_commit(&cs.empty_w[sw]);
+                    if (jb.j == nsl - 1) umma_commit(&cs.d1_full);
                 } else {
-                    // A = H (K-major, no swizzle), B = Bcat slice (MN-major, 128-byte swizzle:
-                    // 8 K rows of 128 bytes per 1024-byte group)
-                    const uint32_t h = ck::smem_u32(hs), d2 = tmem + EN + (q & 1) * NC;
+                    // A = H in TMEM (8 columns per K step of 16), B = Bcat slice (MN-major,
+                    // 128-byte swizzle: 8 K rows of 128 bytes per 1024-byte group)
+                    const uint32_t d2 = tmem + G::T_D2 + (q & 1) * NC;
 #pragma unroll
                     for (int kk = 0; kk < EN / 16; kk++)
-                        umma16(d2, umma_desc_ls(h + 2 * kk * H_LBO, H_LBO, 128), desc_sw128(st + kk * 2048, 8192, 1024),
-                               IDESC_UP, kk > 0 ? 1u : 0u);
+                        umma16_ts(d2, tmem + G::T_H + kk * 8, desc_sw128(stw + kk * 2048, 8192, 1024), IDESC_UP,
+                                  kk > 0 ? 1u : 0u);
+                    umma_commit(&cs.empty_w[sw]);
                     umma_commit(&cs.d2_full[q & 1]);
                     q++;
                 }
             }
         }
         __syncwarp();
+    } else if (warp == NEPI / 32 + 2) {
+        // ============ store warp: out boxes -> global (TMA store, or reduce-add into out = base) ============
+        if (lane == 0) {
+            int q = 0, p1 = 0, p2 = 0;  // act stages of the stores of chunks q - 1, q - 2 (released once read)
+            for (int lt = 0; lt < my_tiles; lt++) {
+                const int t0 = tile0(lt);
+                bool bad = false;
+                for (int j = 0; j < nch; j++, q++) {
+                    const int sa = up_job_index(lt, j, nsl, my_tiles) % NA;
+                    if (!ck::mbar_wait(&cs.out_full[q & 1], (q >> 1) & 1, &cs.abort, err)) {
+                        bad = true;
+                        break;
+                    }
+                    ck::mbar_arrive(&cs.out_empty[q & 1]);
+                    const unsigned char* os = ring_a + sa * G::A_STAGE;
+                    if (accum)
+                        tma_add_2d(&mout, blk(lt, j) * NC, t0, os);  // out (= base) += T(D2)
+                    else
+                        tma_store_2d(&mout, blk(lt, j) * NC, t0, os);  // rows past ntok are not written
+                    bulk_wait_read<2>();  // the store of chunk q - 2 has read its box
+                    if (q >= 2) ck::mbar_arrive(&cs.empty_a[p2]);
+                    p2 = p1;
+                    p1 = sa;
+                }
+                if (bad) break;
+            }
+            bulk_wait_all();
+        }
+        __syncwarp();
     } else {
-        // ============ epilogue warps 0-3: H per tile, out per up chunk ============
-        const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
-        const int row = tid;  // token row of the tile = TMEM lane
-        int q = 0, pend = -1;  // up chunks done; stage of the last store still reading smem (row 0)
+        // ============ epilogue warps 0-7: H per tile, out per up chunk ============
+        const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
+        const int row = 32 * (warp & 3) + lane;  // token row of the tile = TMEM lane
+        const int hf = warp >> 2;                // which half of the columns this thread handles
+        int q = 0;                               // up chunks done (TMEM buffer q & 1)
         bool bad = false;
         for (int lt = 0; lt < my_tiles && !bad; lt++) {
             const int t0 = tile0(lt), tok = t0 + row;
@@ -230,82 +313,74 @@ __global__ void __launch_bounds__(atc::NTH, 1)
                     ss[s] = s < kq ? (scores ? to_f32(scores[(size_t)tok * topk + s]) : 1.f) : 0.f;
                 }
                 bad = ck::bar_or_n(BAR_EPI, NEPI, !ck::mbar_wait(&cs.d1_full, lt & 1, &cs.abort, err));
-                if (bad) break;  // the vote keeps the 128 threads together for the named barriers
+                if (bad) break;  // the vote keeps the threads together for the named barriers
                 tc_fence_after();
 #pragma unroll
-                for (int h0 = 0; h0 < EN; h0 += 32) {
-                    float v[32];
-                    tmem_ld16(tmem + lane_base + h0, v);
-                    tmem_ld16(tmem + lane_base + h0 + 16, v + 16);
+                for (int h0 = hf * (EN / 2); h0 < (hf + 1) * (EN / 2); h0 += 16) {
+                    float v[16];
+                    uint32_t hp[8];
+                    tmem_ld16(tmem + lane_base + (lt & 1) * EN + h0, v);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int c = 0; c < 32; c += 8) {
-                        const int col = h0 + c, e = col / R;
+                    for (int c = 0; c < 16; c += 8) {
+                        const int e = (h0 + c) / R;
                         float gs = 0.f;
 #pragma unroll
                         for (int s = 0; s < 8; s++) gs += es[s] == e ? ss[s] : 0.f;
-                        uint4 pk;
-                        T* pe = reinterpret_cast<T*>(&pk);
 #pragma unroll
-                        for (int u = 0; u < 8; u++) pe[u] = from_f32<T>(v[c + u] * gs);
-                        *reinterpret_cast<uint4*>(hs + row * 16 + (col >> 3) * H_LBO) = pk;
+                        for (int u = 0; u < 8; u += 2) {
+                            T pr[2] = {from_f32<T>(v[c + u] * gs), from_f32<T>(v[c + u + 1] * gs)};
+                            hp[(c + u) / 2] = *reinterpret_cast<const uint32_t*>(pr);
+                        }
                     }
+                    tmem_st8(tmem + lane_base + G::T_H + h0 / 2, hp);
                 }
-                proxy_fence();
+                tmem_wait_st();
                 tc_fence_before();
                 ck::mbar_arrive(&cs.h_full);
             }
             for (int j = 0; j < nch; j++, q++) {
-                const int g = lt * jpt + nsl + j, s = g % NS;
-                unsigned char* os = ring + s * G::STAGE + G::B_BYTES;
+                const int g = up_job_index(lt, j, nsl, my_tiles), sa = g % NA;
+                unsigned char* os = ring_a + sa * G::A_STAGE;  // base slice, then out in place
                 bad = !ck::mbar_wait(&cs.d2_full[q & 1], (q >> 1) & 1, &cs.abort, err) ||
-                      !ck::mbar_wait(&cs.full[s], (g / NS) & 1, &cs.abort, err);
+                      !ck::mbar_wait(&cs.full_a[sa], (g / NA) & 1, &cs.abort, err);
                 bad = ck::bar_or_n(BAR_EPI, NEPI, bad);
                 if (bad) break;
                 tc_fence_after();
-                float v[NC];
-                const uint32_t ta = tmem + lane_base + EN + (q & 1) * NC;
-#pragma unroll
-                for (int c = 0; c < NC; c += 16) tmem_ld16(ta + c, v + c);
+                float v[32];
+                const uint32_t ta = tmem + lane_base + G::T_D2 + (q & 1) * NC + hf * 32;
+                tmem_ld16(ta, v);
+                tmem_ld16(ta + 16, v + 16);
                 tmem_wait_ld();
                 tc_fence_before();
                 ck::mbar_arrive(&cs.d2_empty[q & 1]);
                 // this row of the 128-byte-swizzled base / out box: 16-byte piece c sits at c ^ (row % 8)
                 unsigned char* orow = os + row * 128;
 #pragma unroll
-                for (int c = 0; c < NC / 8; c++) {
+                for (int c4 = 0; c4 < 4; c4++) {
+                    const int c = hf * 4 + c4;
                     unsigned char* pp = orow + ((c ^ (row & 7)) << 4);
-                    uint4 raw = has_base ? *reinterpret_cast<const uint4*>(pp) : make_uint4(0u, 0u, 0u, 0u);
+                    uint4 raw = (has_base && !accum) ? *reinterpret_cast<const uint4*>(pp) : make_uint4(0u, 0u, 0u, 0u);
                     T* e = reinterpret_cast<T*>(&raw);
 #pragma unroll
-                    for (int u = 0; u < 8; u++) e[u] = from_f32<T>(v[8 * c + u] + to_f32(e[u]));
+                    for (int u = 0; u < 8; u++) e[u] = from_f32<T>(v[8 * c4 + u] + to_f32(e[u]));
                     *reinterpret_cast<uint4*>(pp) = raw;
                 }
                 proxy_fence();  // the TMA store reads these bytes through the async proxy
                 ck::bar_sync_n(BAR_EPI, NEPI);
-                if (row == 0) {
-                    tma_store_2d(&mout, j * NC, t0, os);  // rows past ntok are not written
-                    if (j + 1 < nch) {
-                        bulk_wait_read<1>();  // the previous chunk's store has read its stage
-                        if (pend >= 0) ck::mbar_arrive(&cs.empty[pend]);
-                        pend = s;
-                    } else {  // last chunk of the tile: release both now (the next tile's
-                        bulk_wait_read<0>();  // down slices may need these stages)
-                        if (pend >= 0) ck::mbar_arrive(&cs.empty[pend]);
-                        ck::mbar_arrive(&cs.empty[s]);
-                        pend = -1;
-                    }
+                if (tid == 0) {  // hand the box to the store warp
+                    if (q >= 2 && !ck::mbar_wait(&cs.out_empty[q & 1], ((q >> 1) + 1) & 1, &cs.abort, err)) bad = true;
+                    ck::mbar_arrive(&cs.out_full[q & 1]);
                 }
             }
         }
-        if (row == 0) bulk_wait_all();
     }
 
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
     }
 }
 
@@ -384,7 +459,9 @@ static int launch_apply_tc(const void* x, const void* base, const void* A, const
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
     const int ntiles = (ntok + TM - 1) / TM;
     const int grid = ntiles < nsm ? ntiles : nsm;  // persistent: one CTA per SM
-    kern<<<grid, NTH, smem, st>>>(mx, ma, mb, mbase, mout, base ? 1 : 0, inds, (const T*)scores, ntok, C, R, topk);
+    const int accum = base != nullptr && base == out;
+    kern<<<grid, NTH, smem, st>>>(mx, ma, mb, mbase, mout, base ? 1 : 0, accum, inds, (const T*)scores, ntok, C, R,
+                                  topk);
     return check_launch();
 }
 

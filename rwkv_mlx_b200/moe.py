@@ -229,8 +229,8 @@ class LoRAMoE_CMix(nn.Module):
         x2 = x.reshape(B * T, C).contiguous()
         r = router_forward(x2, self.router.gate.weight, self.top_k, self.router.bias)
         if lora_apply_supported(C, self.lora_rank, self.n_experts, self.top_k, x.dtype):
-            out = lora_apply(x2, base_out.reshape(B * T, C), self.lora_A.detach(), self.lora_B.detach(),
-                             r["inds"], r["scores"])
+            b2 = base_out.reshape(B * T, C)  # a temporary: the adapters are added into it in place
+            out = lora_apply(x2, b2, self.lora_A.detach(), self.lora_B.detach(), r["inds"], r["scores"], out=b2)
         else:  # sorted dispatch: grouped down-projection, then per-token combine
             perm, inv, offsets = permute(r["inds"], self.n_experts)
             h = lora_down(x2, self.lora_A.detach(), perm, offsets, self.top_k)

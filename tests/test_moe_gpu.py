@@ -181,24 +181,31 @@ def test_lora_apply_matches_oracle(apply_impl, dt, ntok, C, E, R, k, with_base):
     assert _native.lib().rwkv_device_error(1) == 0
 
 
-def test_lora_apply_in_place_and_no_scores(apply_impl):
-    """out aliasing base, scores NULL (all 1): the EP local step's form."""
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("ntok,C,E,R,k,with_scores", [(300, 256, 8, 16, 1, False), (5000, 768, 8, 16, 2, True),
+                                                      (333, 64, 4, 8, 2, True)])
+def test_lora_apply_in_place(apply_impl, dt, ntok, C, E, R, k, with_scores):
+    """out aliasing base (the tcgen05 kernel then adds into out in L2 with TMA
+    reduce-add stores); scores NULL (all 1) is the EP local step's form."""
+    from rwkv_mlx_b200 import _native
     from rwkv_mlx_b200.moe import lora_apply
 
-    ntok, C, E, R = 300, 256, 8, 16
-    x = _x(ntok, C, 8)
-    rng = np.random.default_rng(9)
-    A = torch.tensor(rng.normal(0, 0.05, (E, C, R)), dtype=torch.float16, device="cuda")
-    Bw = torch.tensor(rng.normal(0, 0.05, (E, R, C)), dtype=torch.float16, device="cuda")
-    inds = torch.tensor(rng.integers(0, E, (ntok, 1)), dtype=torch.int32, device="cuda")
-    base = _x(ntok, C, 10)
+    x = _x(ntok, C, 8, dt)
+    rng = np.random.default_rng(9 + ntok)
+    A = torch.tensor(rng.normal(0, 0.05, (E, C, R)), dtype=dt, device="cuda")
+    Bw = torch.tensor(rng.normal(0, 0.05, (E, R, C)), dtype=dt, device="cuda")
+    inds = torch.tensor(np.argsort(rng.random((ntok, E)), axis=1)[:, :k], dtype=torch.int32, device="cuda")
+    sc = torch.tensor(rng.random((ntok, k)), dtype=dt, device="cuda") if with_scores else None
+    base = _x(ntok, C, 10, dt)
     base_np = base.double().cpu().numpy()
-    out = lora_apply(x, base, A, Bw, inds, None, out=base)
+    out = lora_apply(x, base, A, Bw, inds, sc, out=base)
     torch.cuda.synchronize()
     assert out.data_ptr() == base.data_ptr()
     npy = lambda t: t.double().cpu().numpy()
-    delta = mo.lora_moe_delta(npy(x), npy(A), npy(Bw), inds.cpu().numpy(), np.ones((ntok, 1)))
-    assert rel_rms(npy(out), base_np + delta) < 2e-3
+    delta = mo.lora_moe_delta(npy(x), npy(A), npy(Bw), inds.cpu().numpy(),
+                              npy(sc) if with_scores else np.ones((ntok, k)))
+    assert rel_rms(npy(out), base_np + delta) < {torch.float16: 2e-3, torch.bfloat16: 8e-3}[dt]
+    assert _native.lib().rwkv_device_error(1) == 0
 
 
 def test_lora_moe_cmix_unsupported_shape_uses_sorted_dispatch():

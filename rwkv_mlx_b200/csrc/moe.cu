@@ -199,7 +199,8 @@ __global__ void __launch_bounds__(ROUTER_WARPS * 32)
 
 // Fixed-order (deterministic) reduction of the per-CTA partials: thread t sums CTAs
 // t, t + 256, ..., then warps and finally 8 warp totals, always in the same order.
-constexpr int FIN_THREADS = 256, FIN_MAXE = 32;
+constexpr int FIN_THREADS = 256;
+template <int FIN_MAXE>  // expert count rounded up to 8, 16 or 32
 __global__ void __launch_bounds__(FIN_THREADS)
     moe_router_finalize_kernel(const float* __restrict__ part_f, const int32_t* __restrict__ part_c,
                                int nblk, int ntok, int E, int topk, float* __restrict__ stats,
@@ -642,6 +643,222 @@ struct Geo {
 };
 }  // namespace apply
 
+// Router on the tensor cores for 16-bit x (mma.sync m16n8k16, fp32 accumulate; the GEMM
+// is 16 tokens x E experts x C per warp and memory-bound, so the legacy MMA suffices).
+// The fp32 gate weights are split into 16-bit terms W = W0 + W1 / S + W2 / S^2 (S = 2^11
+// and two terms for fp16, S = 2^8 and three terms for bf16), each term with its own fp32
+// accumulator: x is exact in its own type and every 16-bit x 16-bit product is exact in
+// fp32, so the logits carry fp32-level rounding like the FMA kernel's.  Within every
+// 32-column block the K order is permuted identically for x and W (the fragment slots of
+// thread t of a quad are columns 8t .. 8t+7), so each operand load is one 16-byte vector.
+// Thread (g, t) of a warp holds the logits of tokens g and g + 8 of its 16 for experts
+// 8n + 2t and 8n + 2t + 1; softmax statistics and top-k (ties to the lower expert id) run
+// over the quad.
+__host__ __device__ inline int router_mma_rs(int C) {  // W row stride (elements): 64 B mod 128 B
+    return (((C * 2 + 127) / 128) * 128 + 64) / 2;
+}
+template <typename T>
+__host__ __device__ constexpr int router_mma_terms() { return sizeof(T) == 2 && !std::is_same<T, __nv_bfloat16>::value ? 2 : 3; }
+
+template <typename T, int NT>
+__global__ void __launch_bounds__(ROUTER_WARPS * 32)
+    moe_router_mma_kernel(const T* __restrict__ x, const float* __restrict__ gate_w,
+                          const float* __restrict__ bias, float* __restrict__ logits,
+                          int32_t* __restrict__ inds, T* __restrict__ scores, float* __restrict__ part_f,
+                          int32_t* __restrict__ part_c, int ntok, int C, int E, int topk) {
+    constexpr int NTERM = router_mma_terms<T>();
+    constexpr float SC = NTERM == 2 ? 2048.f : 256.f;
+    constexpr int EM = NT * 8, NO = 2 * NT;  // padded experts; experts owned per thread
+    extern __shared__ __align__(16) unsigned char wsm_raw[];
+    T* wsm = reinterpret_cast<T*>(wsm_raw);  // [NTERM][EM][RS]
+    __shared__ float red_f[ROUTER_WARPS][EM + 1];
+    __shared__ int red_c[ROUTER_WARPS][EM];
+    const int RS = router_mma_rs(C), CP = RS;  // columns past C are zero
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+    // split weights, 4 columns per step (C % 8 == 0: a group of 4 is all in or all out)
+    const bool al16 = (reinterpret_cast<uintptr_t>(gate_w) & 15) == 0;
+    const int cq = CP / 4;
+#pragma unroll 4
+    for (int i = tid; i < EM * cq; i += blockDim.x) {
+        const int e = i / cq, c = 4 * (i - e * cq);
+        float w[4] = {0.f, 0.f, 0.f, 0.f};
+        if (e < E && c < C) {
+            const float* src = gate_w + (size_t)e * C + c;
+            if (al16) {
+                const float4 v = __ldg(reinterpret_cast<const float4*>(src));
+                w[0] = v.x, w[1] = v.y, w[2] = v.z, w[3] = v.w;
+            } else {
+                w[0] = src[0], w[1] = src[1], w[2] = src[2], w[3] = src[3];
+            }
+        }
+        T t0[4], t1[4], t2[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            t0[u] = from_f32<T>(w[u]);
+            const float r1 = (w[u] - to_f32(t0[u])) * SC;  // exact: t0 is w rounded
+            t1[u] = from_f32<T>(r1);
+            t2[u] = from_f32<T>((r1 - to_f32(t1[u])) * SC);
+        }
+        *reinterpret_cast<uint2*>(wsm + (size_t)e * RS + c) = *reinterpret_cast<const uint2*>(t0);
+        *reinterpret_cast<uint2*>(wsm + (size_t)(EM + e) * RS + c) = *reinterpret_cast<const uint2*>(t1);
+        if constexpr (NTERM == 3)
+            *reinterpret_cast<uint2*>(wsm + (size_t)(2 * EM + e) * RS + c) = *reinterpret_cast<const uint2*>(t2);
+    }
+    __syncthreads();
+
+    float acc_p[NO], acc_z = 0.f;
+    int acc_c[NO];
+    float lb[NO];
+#pragma unroll
+    for (int o = 0; o < NO; o++) {
+        const int e = 8 * (o >> 1) + 2 * t + (o & 1);
+        acc_p[o] = 0.f, acc_c[o] = 0;
+        lb[o] = (bias && e < E) ? bias[e] : 0.f;
+    }
+    const int stride = gridDim.x * ROUTER_WARPS * 16;
+    for (int tb = (blockIdx.x * ROUTER_WARPS + warp) * 16; tb < ntok; tb += stride) {
+        float d[NTERM][NT][4];
+#pragma unroll
+        for (int m = 0; m < NTERM; m++)
+#pragma unroll
+            for (int n = 0; n < NT; n++) d[m][n][0] = d[m][n][1] = d[m][n][2] = d[m][n][3] = 0.f;
+        const int r0 = tb + g, r1 = tb + g + 8;
+        const T* x0 = x + (size_t)(r0 < ntok ? r0 : 0) * C;
+        const T* x1 = x + (size_t)(r1 < ntok ? r1 : 0) * C;
+        constexpr int KB = 8;  // 32-column blocks whose x is loaded as one batch (16 loads in flight)
+        for (int kb0 = 0; kb0 < C; kb0 += 32 * KB) {
+            uint4 a_lo[KB], a_hi[KB];
+#pragma unroll
+            for (int u = 0; u < KB; u++) {
+                const int col = kb0 + 32 * u + 8 * t;
+                const bool in = col < C;  // C % 8 == 0: a 16-byte piece is all in or all out
+                const uint4 z4 = make_uint4(0u, 0u, 0u, 0u);
+                a_lo[u] = (in && r0 < ntok) ? __ldg(reinterpret_cast<const uint4*>(x0 + col)) : z4;
+                a_hi[u] = (in && r1 < ntok) ? __ldg(reinterpret_cast<const uint4*>(x1 + col)) : z4;
+            }
+#pragma unroll
+            for (int u = 0; u < KB; u++) {
+                const int col = kb0 + 32 * u + 8 * t;
+                if (kb0 + 32 * u >= C) break;
+                const uint32_t A0[4] = {a_lo[u].x, a_hi[u].x, a_lo[u].y, a_hi[u].y};  // columns 8t .. 8t+3
+                const uint32_t A1[4] = {a_lo[u].z, a_hi[u].z, a_lo[u].w, a_hi[u].w};  // columns 8t+4 .. 8t+7
+#pragma unroll
+                for (int m = 0; m < NTERM; m++)
+#pragma unroll
+                    for (int n = 0; n < NT; n++) {
+                        const uint4 b = *reinterpret_cast<const uint4*>(wsm + (size_t)(m * EM + 8 * n + g) * RS + col);
+                        apply::mma16816<T>(d[m][n], A0, b.x, b.y);
+                        apply::mma16816<T>(d[m][n], A1, b.z, b.w);
+                    }
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const int tok = tb + g + 8 * h;
+            const bool tvalid = tok < ntok;
+            float lg[NO];
+            bool ev[NO];
+#pragma unroll
+            for (int o = 0; o < NO; o++) {
+                const int n = o >> 1, i = o & 1, e = 8 * n + 2 * t + i;
+                float v = d[NTERM - 1][n][2 * h + i];
+#pragma unroll
+                for (int m = NTERM - 2; m >= 0; m--) v = d[m][n][2 * h + i] + v * (1.f / SC);
+                ev[o] = e < E;
+                lg[o] = ev[o] ? v + lb[o] : -INFINITY;
+                if (logits && tvalid && ev[o]) logits[(size_t)tok * E + e] = lg[o];
+            }
+            // full softmax statistics (max-stabilised log-sum-exp) over the quad
+            float m = -INFINITY;
+#pragma unroll
+            for (int o = 0; o < NO; o++) m = fmaxf(m, lg[o]);
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+            float ex[NO], se = 0.f;
+#pragma unroll
+            for (int o = 0; o < NO; o++) ex[o] = ev[o] ? expf(lg[o] - m) : 0.f, se += ex[o];
+            se += __shfl_xor_sync(0xffffffffu, se, 1);
+            se += __shfl_xor_sync(0xffffffffu, se, 2);
+            if (tvalid) {
+#pragma unroll
+                for (int o = 0; o < NO; o++) acc_p[o] += ev[o] ? ex[o] / se : 0.f;
+            }
+            const float lse = m + logf(se);
+            if (t == 0 && tvalid) acc_z = fmaf(lse, lse, acc_z);
+
+            // top-k by repeated argmax over the quad, ties to the lower expert id
+            bool taken[NO];
+            int slot[NO];
+#pragma unroll
+            for (int o = 0; o < NO; o++) taken[o] = !ev[o], slot[o] = -1;
+            float sel0 = 0.f, denom = 0.f;
+            for (int kk = 0; kk < topk; kk++) {
+                float bv = -INFINITY;
+                int bi = 0x7fffffff;
+#pragma unroll
+                for (int o = 0; o < NO; o++) {
+                    const int e = 8 * (o >> 1) + 2 * t + (o & 1);
+                    if (!taken[o] && (lg[o] > bv || (lg[o] == bv && e < bi))) bv = lg[o], bi = e;
+                }
+#pragma unroll
+                for (int s = 1; s <= 2; s <<= 1) {
+                    const float ov = __shfl_xor_sync(0xffffffffu, bv, s);
+                    const int oi = __shfl_xor_sync(0xffffffffu, bi, s);
+                    if (ov > bv || (ov == bv && oi < bi)) bv = ov, bi = oi;
+                }
+                if (kk == 0) sel0 = bv;
+                denom += expf(bv - sel0);
+#pragma unroll
+                for (int o = 0; o < NO; o++)
+                    if (8 * (o >> 1) + 2 * t + (o & 1) == bi) taken[o] = true, slot[o] = kk;
+                if (t == 0 && tvalid) inds[(size_t)tok * topk + kk] = bi;
+            }
+            if (tvalid) {
+#pragma unroll
+                for (int o = 0; o < NO; o++)
+                    if (slot[o] >= 0) {
+                        scores[(size_t)tok * topk + slot[o]] = from_f32<T>(expf(lg[o] - sel0) / denom);
+                        acc_c[o] += 1;
+                    }
+            }
+        }
+    }
+    // per expert over the 8 token groups of the warp, then over the warps of the CTA
+#pragma unroll
+    for (int s = 4; s < 32; s <<= 1) {
+#pragma unroll
+        for (int o = 0; o < NO; o++) {
+            acc_p[o] += __shfl_xor_sync(0xffffffffu, acc_p[o], s);
+            acc_c[o] += __shfl_xor_sync(0xffffffffu, acc_c[o], s);
+        }
+    }
+#pragma unroll
+    for (int s = 1; s < 32; s <<= 1) acc_z += __shfl_xor_sync(0xffffffffu, acc_z, s);
+    if (g == 0) {
+#pragma unroll
+        for (int o = 0; o < NO; o++) {
+            const int e = 8 * (o >> 1) + 2 * t + (o & 1);
+            red_f[warp][e] = acc_p[o];
+            red_c[warp][e] = acc_c[o];
+        }
+    }
+    if (lane == 0) red_f[warp][EM] = acc_z;
+    __syncthreads();
+    if (tid < E) {
+        float s_ = 0.f;
+        int c = 0;
+        for (int w = 0; w < ROUTER_WARPS; w++) s_ += red_f[w][tid], c += red_c[w][tid];
+        part_f[(size_t)blockIdx.x * (E + 1) + tid] = s_;
+        part_c[(size_t)blockIdx.x * E + tid] = c;
+    }
+    if (tid == 0) {
+        float s_ = 0.f;
+        for (int w = 0; w < ROUTER_WARPS; w++) s_ += red_f[w][EM];
+        part_f[(size_t)blockIdx.x * (E + 1) + E] = s_;
+    }
+}
+
+
 template <typename T, int EN>
 __global__ void __launch_bounds__(apply::NTH)
     moe_lora_apply_kernel(const T* __restrict__ x, const T* __restrict__ base, const T* __restrict__ A,
@@ -817,13 +1034,35 @@ static int launch_router(const void* x, const float* gw, const float* bias, floa
                          int32_t* inds, void* scores, float* pf, int32_t* pc, int ntok, int C,
                          int E, int topk, cudaStream_t st) {
     const int nb = router_ctas(ntok);
+    if constexpr (sizeof(T) == 2) {  // tensor-core kernel when its split weights fit
+        const size_t smem_mma = (size_t)router_mma_terms<T>() * EM * router_mma_rs(C) * sizeof(T);
+        if (smem_mma <= 200 * 1024) {
+            auto kern = moe_router_mma_kernel<T, EM / 8>;
+            cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_mma);
+            if (err != cudaSuccess) return set_cuda_error(err);
+            kern<<<nb, ROUTER_WARPS * 32, smem_mma, st>>>((const T*)x, gw, bias, logits, inds, (T*)scores, pf, pc,
+                                                          ntok, C, E, topk);
+            return check_launch();
+        }
+    }
     const size_t smem = (size_t)E * C * sizeof(float);
+    if (smem > 200 * 1024) return RWKV_ERR_SHAPE;
     auto kern = moe_router_kernel<T, EM>;
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (err != cudaSuccess) return set_cuda_error(err);
     kern<<<nb, ROUTER_WARPS * 32, smem, st>>>((const T*)x, gw, bias, logits, inds, (T*)scores, pf,
                                               pc, ntok, C, E, topk);
     return check_launch();
+}
+
+static void launch_finalize(const float* pf, const int32_t* pc, int nb, int ntok, int E, int topk, float* stats,
+                            int32_t* counts, cudaStream_t st) {
+    if (E <= 8)
+        moe_router_finalize_kernel<8><<<1, FIN_THREADS, 0, st>>>(pf, pc, nb, ntok, E, topk, stats, counts);
+    else if (E <= 16)
+        moe_router_finalize_kernel<16><<<1, FIN_THREADS, 0, st>>>(pf, pc, nb, ntok, E, topk, stats, counts);
+    else
+        moe_router_finalize_kernel<32><<<1, FIN_THREADS, 0, st>>>(pf, pc, nb, ntok, E, topk, stats, counts);
 }
 
 extern "C" int rwkv_moe_router(const void* x, const float* gate_w, const float* bias,
@@ -833,7 +1072,6 @@ extern "C" int rwkv_moe_router(const void* x, const float* gate_w, const float* 
     if (ntok <= 0 || C <= 0 || E <= 0 || E > 32 || topk <= 0 || topk > E || topk > 8)
         return RWKV_ERR_SHAPE;
     if (C % 8) return RWKV_ERR_SHAPE;
-    if ((size_t)E * C * sizeof(float) > 200 * 1024) return RWKV_ERR_SHAPE;
     if (!x || !gate_w || !inds || !scores || !stats || !workspace) return RWKV_ERR_ARG;
     if (!aligned(x, 16)) return RWKV_ERR_ALIGN;
     if (workspace_bytes < rwkv_moe_router_workspace_size(ntok, E)) return RWKV_ERR_WORKSPACE;
@@ -851,7 +1089,7 @@ extern "C" int rwkv_moe_router(const void* x, const float* gate_w, const float* 
             rc = launch_router<T, 32>(x, gate_w, bias, logits, inds, scores, pf, pc, ntok, C, E, topk, st);
     });
     if (rc) return rc;
-    moe_router_finalize_kernel<<<1, FIN_THREADS, 0, st>>>(pf, pc, nb, ntok, E, topk, stats, counts);
+    launch_finalize(pf, pc, nb, ntok, E, topk, stats, counts, st);
     return check_launch();
 }
 
@@ -1045,7 +1283,6 @@ extern "C" int rwkv_moe_router_noalloc(const void* x, const float* gate_w, const
     if (ntok <= 0 || C <= 0 || E <= 0 || E > NOALLOC_MAX_E || topk <= 0 || topk > E || topk > 8)
         return RWKV_ERR_SHAPE;
     if (C % 8) return RWKV_ERR_SHAPE;
-    if ((size_t)E * C * sizeof(float) > 200 * 1024) return RWKV_ERR_SHAPE;
     if (!x || !gate_w || !inds || !scores || !stats) return RWKV_ERR_ARG;
     if (!aligned(x, 16)) return RWKV_ERR_ALIGN;
     if (rwkv_moe_router_workspace_size(ntok, E) > NOALLOC_SCRATCH_BYTES) return RWKV_ERR_WORKSPACE;
@@ -1067,7 +1304,7 @@ extern "C" int rwkv_moe_router_noalloc(const void* x, const float* gate_w, const
             rc = launch_router<T, 32>(x, gate_w, bias, logits, inds, scores, pf, pc, ntok, C, E, topk, st);
     });
     if (rc) return rc;
-    moe_router_finalize_kernel<<<1, FIN_THREADS, 0, st>>>(pf, pc, nb, ntok, E, topk, stats, counts);
+    launch_finalize(pf, pc, nb, ntok, E, topk, stats, counts, st);
     return check_launch();
 }
 

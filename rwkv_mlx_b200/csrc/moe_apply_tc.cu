@@ -12,20 +12,26 @@
 //   out    = T(base + D2), or, when out is base, out += T(D2) by a TMA reduce-add store
 //          (base is then never loaded into the SM: the add happens in L2)
 //
-// Data movement is all TMA (no multicast): x, base and out move as 128-byte-swizzled
-// 64-channel x 128-token boxes, Bcat slices as 128-byte-swizzled 64-channel x EN boxes
-// (the MN-major operand layout of the up MMA), and Acat slices through a 4-d view of A
-// (E, C, R) whose box lands directly in the no-swizzle MN-major layout of the down MMA.
-// The CTA is persistent over tiles and warp-specialised:
-//   warp 4 lane 0   producer: one "job" (a down slice: x + Acat slices; an up chunk: Bcat +
-//                   base slices) per stage of two rings, activations (NA deep: they come
-//                   from HBM) and adapter slices (NW deep: L2), armed with expect_tx;
-//   warp 5 lane 0   MMA issuer: commits each job to its stages' barriers and to the up
+// Data movement is all TMA, each CTA loading its own boxes: x, base and out move as
+// 128-byte-swizzled 64-channel x 128-token boxes, Bcat slices as 128-byte-swizzled
+// 64-channel x EN boxes (the MN-major operand layout of the up MMA), and Acat slices
+// through a 4-d view of A (E, C, R) whose box lands directly in the no-swizzle MN-major
+// layout of the down MMA.  The CTA is persistent over tiles and warp-specialised:
+//   warp 8 lane 0   producer: one "job" (a down slice: x + Acat slices; an up chunk: Bcat +
+//                   base slices) per stage of two rings, activations (NA deep: HBM) and
+//                   adapter slices (NW deep: L2), armed with expect_tx;
+//   warp 9 lane 0   MMA issuer: commits each job to its stages' barriers and to the up
 //                   accumulator's barrier; TMEM holds two D1 accumulators (EN columns
 //                   each: tiles alternate), two up accumulators of 64 columns and H
 //                   (EN / 2 columns of packed 16-bit pairs, the A operand of the up MMA);
-//   warps 0-3       epilogue: H per tile (TMEM -> routing scale -> TMEM), and per up chunk
-//                   TMEM + base -> out in place in the activation stage, stored by TMA.
+//   warps 0-7       epilogue: H per tile (TMEM -> routing scale -> TMEM), and per up chunk
+//                   TMEM + base -> out in place in the activation stage (warps w and
+//                   w + 4 share TMEM lanes 32 (w % 4) .. and split the columns);
+//   warp 10 lane 0  store warp: TMA store (or reduce-add) of each finished out box, and
+//                   release of its stage once the store has read it.
+// Jobs interleave the up chunks of one tile with the down slices of the next, and a
+// tile's slices start at channel block (tile mod C / 64), so that the SMs do not all
+// read the same adapter slice from L2 at the same moment.
 // Every wait is bounded: a wait that gives up sets the CTA's abort flag and the device
 // error word, and every role leaves its loop.
 #include <cuda.h>

@@ -20,12 +20,16 @@ def _x(ntok, C, seed, dt=torch.float16):
     return torch.tensor(rng.standard_normal((ntok, C)), dtype=torch.float32, device="cuda").to(dt)
 
 
+@pytest.mark.parametrize("dt,C", [(torch.float16, 768), (torch.bfloat16, 768), (torch.float32, 768),
+                                  (torch.float16, 72), (torch.bfloat16, 264)])
 @pytest.mark.parametrize("E,k,with_bias", [(8, 2, False), (8, 2, True), (4, 1, False), (16, 3, False), (32, 4, True)])
-def test_router_bit_exact_indices(E, k, with_bias):
+def test_router_bit_exact_indices(dt, C, E, k, with_bias):
+    """16-bit x: tensor-core kernel with split gate weights (C = 72, 264: partial
+    32-column blocks and load batches); fp32 x: the FMA kernel."""
     from rwkv_mlx_b200.moe import router_forward
 
-    ntok, C = 3000, 768
-    x = _x(ntok, C, E * 10 + k)
+    ntok = 3000
+    x = _x(ntok, C, E * 10 + k, dt)
     rng = np.random.default_rng(E)
     gw = torch.tensor(rng.standard_normal((E, C)) * 0.02, dtype=torch.float32, device="cuda")
     bias = torch.tensor(rng.normal(0, 1.5, E), dtype=torch.float32, device="cuda") if with_bias else None
@@ -33,7 +37,7 @@ def test_router_bit_exact_indices(E, k, with_bias):
     torch.cuda.synchronize()
     lg = r["logits"].cpu().numpy()
     # logits themselves: fp32 GEMM, different summation order
-    ref_lg = mo.gate_logits(x.cpu().numpy(), gw.cpu().numpy(), None if bias is None else bias.cpu().numpy())
+    ref_lg = mo.gate_logits(x.float().cpu().numpy(), gw.cpu().numpy(), None if bias is None else bias.cpu().numpy())
     assert np.max(np.abs(lg - ref_lg)) < 1e-4 * max(1.0, np.abs(ref_lg).max())
     inds, scores, aux, z, f = mo.router(None, None, k, logits=lg)
     np.testing.assert_array_equal(r["inds"].cpu().numpy(), inds)

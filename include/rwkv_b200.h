@@ -144,7 +144,7 @@ int rwkv_moe_router(const void* x, const float* gate_w, const float* bias, float
  * it, or a serving loop that reserves all device memory at start-up and must not
  * allocate later (cudaMalloc can synchronise the device and fails once memory is
  * reserved).  Its scratch is a file-scope device array of
- * rwkv_moe_router_noalloc_scratch_bytes() bytes (~301 KB), held by every GPU that
+ * rwkv_moe_router_noalloc_scratch_bytes() bytes (~75 KB), held by every GPU that
  * loads this library until the process exits.  Limit: E <= 32 (any ntok).
  * The first call on a device looks up that array's device address with the
  * device current; make that first call before any stream capture.  All calls

@@ -1248,7 +1248,7 @@ constexpr int NOALLOC_MAX_E = 32;
 constexpr size_t NOALLOC_SCRATCH_BYTES =
     ((size_t)ROUTER_MAX_CTAS * (NOALLOC_MAX_E + 1) * sizeof(float) + 255) / 256 * 256 +
     ((size_t)ROUTER_MAX_CTAS * NOALLOC_MAX_E * sizeof(int32_t) + 255) / 256 * 256;
-// ~301 KB, held by every GPU that loads this library until the process exits.
+// ~75 KB, held by every GPU that loads this library until the process exits.
 static __device__ __align__(256) unsigned char g_router_scratch[NOALLOC_SCRATCH_BYTES];
 
 static std::mutex g_scratch_mu;

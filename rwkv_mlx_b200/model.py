@@ -137,6 +137,7 @@ class RWKV_Tmix_x070(nn.Module):
         self.output = nn.Linear(C, C, bias=False)
         self.ln_x = GroupNormMLX(H, C, eps=64e-5, mode=config.groupnorm)
         self._packed, self._packed_key = None, None
+        self._lora, self._lora_key = None, None
 
     def _packed_weights(self):
         """The six token-shift mixes as one (6, C) tensor and W_r, W_k, W_v stacked for one
@@ -152,6 +153,35 @@ class RWKV_Tmix_x070(nn.Module):
                 wrkv = torch.stack([p.detach() for p in ps[6:]]).transpose(1, 2)
             self._packed, self._packed_key = (mix, wrkv), key
         return self._packed
+
+    def _packed_lora(self):
+        """The four LoRA pairs in the order of the mixes v, w, a, g (slices 2..5 of the
+        packed mixes), zero-padded to one rank, stacked for two batched products:
+        (4, C, D) and (4, D, C).  Zero padding is exact: padded first-stage columns are 0,
+        and the padded second-stage rows are 0 whatever tanh / sigmoid makes of them."""
+        ps = (self.v1, self.w1, self.a1, self.g1, self.v2, self.w2, self.a2, self.g2)
+        key = tuple((p.data_ptr(), p.dtype, p._version) for p in ps)
+        if self._lora_key != key:
+            C = self.v1.shape[0]
+            D = max(p.shape[1] for p in ps[:4])
+            with torch.no_grad():
+                w1 = torch.zeros(4, C, D, device=self.v1.device, dtype=self.v1.dtype)
+                w2 = torch.zeros(4, D, C, device=self.v1.device, dtype=self.v1.dtype)
+                for i in range(4):
+                    w1[i, :, : ps[i].shape[1]] = ps[i].detach()
+                    w2[i, : ps[4 + i].shape[0]] = ps[4 + i].detach()
+            self._lora, self._lora_key = (w1, w2), key
+        return self._lora
+
+    def _lora_products(self, X):
+        """wl, al, vl, g of the fused paths from the mixes X (6, rows, C) in two batched
+        products (4 launches instead of 10)."""
+        w1, w2 = self._packed_lora()
+        h = torch.bmm(X[2:6], w1)  # (4, rows, D): v, w, a, g
+        torch.tanh_(h[1])
+        torch.sigmoid_(h[3])
+        o = torch.bmm(h, w2)
+        return o[1], o[2], o[0], o[3]
 
     def _project(self, x, xx, v_first):
         """Shared by GPT and RNN mode: returns r, w(log-log), k, v, a, g, kk, v_first."""
@@ -191,12 +221,10 @@ class RWKV_Tmix_x070(nn.Module):
         X = fz.lerp(x, mix, T)  # (6, B*T, C): r, k, v, w, a, g inputs
         rkv = torch.bmm(X[0:3], wrkv)
         r, k, v = rkv[0], rkv[1], rkv[2]
-        xv, xw, xa, xg = X[2], X[3], X[4], X[5]
-        wl = torch.tanh(xw @ self.w1) @ self.w2
-        al = (xa @ self.a1) @ self.a2
+        wl, al, vl, g = self._lora_products(X)
         layer0 = self.layer_id == 0
-        vl = None if layer0 else (xv @ self.v1) @ self.v2
-        g = torch.sigmoid(xg @ self.g1) @ self.g2
+        if layer0:
+            vl = None
         vf = None if layer0 else v_first.reshape(B * T, C)
         w, k2, v2, a_in, b_in = fz.tmix_mid(k, v, wl, al, vl, vf, self.w0.view(-1), self.a0.view(-1),
                                              self.v0.view(-1), self.k_k.view(-1), self.k_a.view(-1), layer0)
@@ -234,12 +262,10 @@ class RWKV_Tmix_x070(nn.Module):
         X = fz.lerp(x, mix, 1, prev=x_prev)  # (6, Bs, C)
         rkv = torch.bmm(X[0:3], wrkv)
         r, k, v = rkv[0], rkv[1], rkv[2]
-        xv, xw, xa, xg = X[2], X[3], X[4], X[5]
-        wl = torch.tanh(xw @ self.w1) @ self.w2
-        al = (xa @ self.a1) @ self.a2
+        wl, al, vl, g = self._lora_products(X)
         layer0 = self.layer_id == 0
-        vl = None if layer0 else (xv @ self.v1) @ self.v2
-        g = torch.sigmoid(xg @ self.g1) @ self.g2
+        if layer0:
+            vl = None
         w, k2, v2, a_in, b_in = fz.tmix_mid(k, v, wl, al, vl, None if layer0 else v_first, self.w0.view(-1),
                                              self.a0.view(-1), self.v0.view(-1), self.k_k.view(-1),
                                              self.k_a.view(-1), layer0)

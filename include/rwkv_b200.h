@@ -271,6 +271,12 @@ int rwkv_lerp(const void* x, const void* mix, void* out, int M, long long rows, 
  * previous token (model.py:449-455, 498-501); prev NULL = rwkv_lerp.                 */
 int rwkv_lerp_prev(const void* x, const void* prev, const void* mix, void* out, int M,
                    long long rows, int T, int C, int dtype, void* stream);
+/* rwkv_lerp_prev that also stores each sequence's last x row into prev_out (rows / T, C):
+ * the token-shift state of an RNN step, written by the same pass that reads the old
+ * state.  prev_out may be prev only when T == 1 (decode: each thread reads its vector of
+ * the old state before it overwrites it); otherwise RWKV_ERR_ARG. */
+int rwkv_lerp_prev_state(const void* x, const void* prev, const void* mix, void* out, void* prev_out, int M,
+                         long long rows, int T, int C, int dtype, void* stream);
 int rwkv_tmix_mid(const void* k, const void* v, const void* wl, const void* al, const void* vl,
                   const void* v_first, const float* w0, const void* a0, const void* v0,
                   const void* k_k, const void* k_a, float* w_out, void* k_out, void* v_out,

@@ -27,8 +27,8 @@ struct Vec {
 // ---------------------------------------------------------------------------
 template <typename T>
 __global__ void __launch_bounds__(256)
-    lerp_kernel(const T* __restrict__ x, const T* __restrict__ prev, const T* __restrict__ mix,
-                T* __restrict__ out, int M, long long rows, int Tlen, int C) {
+    lerp_kernel(const T* __restrict__ x, const T* prev, const T* __restrict__ mix, T* __restrict__ out,
+                T* prev_out, int M, long long rows, int Tlen, int C) {  // prev_out may be prev when Tlen = 1
     constexpr int V = Vec<T>::N;
     const int nv = C / V;
     const long long total = rows * nv;
@@ -51,6 +51,9 @@ __global__ void __launch_bounds__(256)
             for (int i = 0; i < V; i++) ov.set(i, fmaf(dx[i], mv.get(i), xf[i]));
             ov.store(out + ((size_t)m * rows + row) * C + c0);
         }
+        // the sequence's last token becomes its next shift state (this thread read the
+        // same vector of prev above when Tlen = 1)
+        if (prev_out && row % Tlen == Tlen - 1) xv.store(prev_out + (row / Tlen) * C + c0);
     }
 }
 
@@ -322,19 +325,31 @@ static int grid_for(long long work, int per_block) {
 
 using namespace rwkv;
 
-extern "C" int rwkv_lerp_prev(const void* x, const void* prev, const void* mix, void* out, int M,
-                              long long rows, int T, int C, int dtype, void* stream) {
+static int lerp_launch(const void* x, const void* prev, const void* mix, void* out, void* prev_out, int M,
+                       long long rows, int T, int C, int dtype, void* stream) {
     if (M <= 0 || rows <= 0 || T <= 0 || C <= 0 || rows % T) return RWKV_ERR_SHAPE;
     if (!x || !mix || !out) return RWKV_ERR_ARG;
-    if (!aligned(x, 16) || !aligned(mix, 16) || !aligned(out, 16) || (prev && !aligned(prev, 16)))
+    if (prev_out && prev_out == prev && T != 1) return RWKV_ERR_ARG;  // other threads read prev
+    if (!aligned(x, 16) || !aligned(mix, 16) || !aligned(out, 16) || (prev && !aligned(prev, 16)) ||
+        (prev_out && !aligned(prev_out, 16)))
         return RWKV_ERR_ALIGN;
     cudaStream_t st = (cudaStream_t)stream;
     RWKV_DISPATCH_DTYPE(dtype, T_, {
         if (C % Vec<T_>::N) return RWKV_ERR_SHAPE;
         lerp_kernel<T_><<<grid_for(rows * (C / Vec<T_>::N), 256), 256, 0, st>>>(
-            (const T_*)x, (const T_*)prev, (const T_*)mix, (T_*)out, M, rows, T, C);
+            (const T_*)x, (const T_*)prev, (const T_*)mix, (T_*)out, (T_*)prev_out, M, rows, T, C);
     });
     return check_launch();
+}
+
+extern "C" int rwkv_lerp_prev(const void* x, const void* prev, const void* mix, void* out, int M,
+                              long long rows, int T, int C, int dtype, void* stream) {
+    return lerp_launch(x, prev, mix, out, nullptr, M, rows, T, C, dtype, stream);
+}
+
+extern "C" int rwkv_lerp_prev_state(const void* x, const void* prev, const void* mix, void* out, void* prev_out,
+                                    int M, long long rows, int T, int C, int dtype, void* stream) {
+    return lerp_launch(x, prev, mix, out, prev_out, M, rows, T, C, dtype, stream);
 }
 
 extern "C" int rwkv_lerp(const void* x, const void* mix, void* out, int M, long long rows, int T,

@@ -17,21 +17,29 @@ def _call(name, *args):
     nat.check(rc, name)
 
 
-def lerp(x: torch.Tensor, mix: torch.Tensor, T: int, prev: torch.Tensor = None) -> torch.Tensor:
+def lerp(x: torch.Tensor, mix: torch.Tensor, T: int, prev: torch.Tensor = None,
+         prev_out: torch.Tensor = None) -> torch.Tensor:
     """x (..., C) with rows grouped in sequences of length T; mix (M, C) -> (M, rows, C).
-    ``prev`` (rows / T, C): the token before each sequence (zeros when None)."""
+    ``prev`` (rows / T, C): the token before each sequence (zeros when None).
+    ``prev_out`` (rows / T, C): receives each sequence's last row of x, the next shift
+    state (may be ``prev`` when T == 1: an RNN state updated in place)."""
     C = x.shape[-1]
     x = x.contiguous()
     rows = x.numel() // C
     mix = mix.to(x.dtype).contiguous().view(-1, C)
     out = torch.empty((mix.shape[0], rows, C), device=x.device, dtype=x.dtype)
-    if prev is None:
+    if prev is not None:
+        prev = prev.to(x.dtype).contiguous()  # a copy only for another dtype / layout
+    direct = prev_out is not None and prev_out.dtype == x.dtype and prev_out.is_contiguous()
+    if prev is None and prev_out is None:
         _call("rwkv_lerp", nat.ptr(x), nat.ptr(mix), nat.ptr(out), mix.shape[0], rows, T, C, nat.dtype_code(x),
               nat.stream_ptr(x.device))
     else:
-        prev = prev.to(x.dtype).contiguous()
-        _call("rwkv_lerp_prev", nat.ptr(x), nat.ptr(prev), nat.ptr(mix), nat.ptr(out), mix.shape[0], rows, T, C,
-              nat.dtype_code(x), nat.stream_ptr(x.device))
+        _call("rwkv_lerp_prev_state", nat.ptr(x), nat.ptr(prev), nat.ptr(mix), nat.ptr(out),
+              nat.ptr(prev_out if direct else None), mix.shape[0], rows, T, C, nat.dtype_code(x),
+              nat.stream_ptr(x.device))
+    if prev_out is not None and not direct:
+        prev_out.copy_(x.view(rows // T, T, C)[:, -1].reshape(prev_out.shape))
     return out
 
 

@@ -253,13 +253,14 @@ class RWKV_Tmix_x070(nn.Module):
         out = self._post(y, r, k, v, g)
         return (out, v_first, sT) if return_state else (out, v_first)
 
-    def _forward_rnn_fused(self, x, x_prev, v_first, state):
+    def _forward_rnn_fused(self, x, x_prev, v_first, state, update_prev=False):
         """forward_rnn on the fused kernels: x, x_prev (Bs, C); v_first (Bs, C) or None for
         layer 0.  Returns (out (Bs, C), v_first)."""
         Bs, C = x.shape
         H = self.n_head
         mix, wrkv = self._packed_weights()
-        X = fz.lerp(x, mix, 1, prev=x_prev)  # (6, Bs, C)
+        # (6, Bs, C); with update_prev the same pass stores x as the next shift state
+        X = fz.lerp(x, mix, 1, prev=x_prev, prev_out=x_prev if update_prev else None)
         rkv = torch.bmm(X[0:3], wrkv)
         r, k, v = rkv[0], rkv[1], rkv[2]
         wl, al, vl, g = self._lora_products(X)
@@ -310,8 +311,8 @@ class RWKV_CMix_x070(nn.Module):
         k = torch.relu(self.key(k)) ** 2
         return self.value(k)
 
-    def forward_rnn_fused(self, x, x_prev):
-        k = fz.lerp(x, self.x_k.view(1, -1), 1, prev=x_prev)[0]
+    def forward_rnn_fused(self, x, x_prev, update_prev=False):
+        k = fz.lerp(x, self.x_k.view(1, -1), 1, prev=x_prev, prev_out=x_prev if update_prev else None)[0]
         return self.value(fz.relu_sq_(self.key(k)))
 
     def forward_rnn(self, x, x_prev):
@@ -509,8 +510,8 @@ class RWKV(nn.Module):
                 _, x = fz.add_layernorm(x, None, blk.ln0.weight, blk.ln0.bias, blk.ln0.eps)
             x, xx = fz.add_layernorm(x, pending, blk.ln1.weight, blk.ln1.bias, blk.ln1.eps)
             st = states[i]
-            out, v_first = blk.att._forward_rnn_fused(xx, st["att_x_prev"], v_first, st["att_state"])
-            st["att_x_prev"].copy_(xx)
+            out, v_first = blk.att._forward_rnn_fused(xx, st["att_x_prev"], v_first, st["att_state"],
+                                                      update_prev=True)
             x, xx = fz.add_layernorm(x, out, blk.ln2.weight, blk.ln2.bias, blk.ln2.eps)
             if blk.is_moe and not hasattr(blk.ffn, "base"):  # full experts
                 pending = blk.ffn.forward_rnn(xx, st["ffn_x_prev"])
@@ -518,7 +519,8 @@ class RWKV(nn.Module):
                 ffn = blk.ffn
                 pending = ffn.base.forward_rnn_fused(xx, st["ffn_x_prev"]) + _moe_rnn(ffn, xx)
             else:
-                pending = blk.ffn.forward_rnn_fused(xx, st["ffn_x_prev"])
+                pending = blk.ffn.forward_rnn_fused(xx, st["ffn_x_prev"], update_prev=True)
+                continue
             st["ffn_x_prev"].copy_(xx)
         _, x = fz.add_layernorm(x, pending, self.ln_out.weight, self.ln_out.bias, self.ln_out.eps)
         return self.head(x)

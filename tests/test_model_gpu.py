@@ -210,3 +210,22 @@ def test_fused_rnn_step_matches_op_by_op(dtype):
         for x, y in zip(st_a, st_b):
             for key in x:
                 assert rel_rms(x[key].float().cpu().numpy(), y[key].float().cpu().numpy()) < 1e-2, key
+
+
+@pytest.mark.parametrize("dt,T", [(torch.float16, 1), (torch.float32, 1), (torch.bfloat16, 7)])
+def test_lerp_writes_the_next_shift_state(dt, T):
+    """rwkv_lerp_prev_state: the mixes as rwkv_lerp_prev computes them, and each sequence's
+    last row stored as the next state (in place over the old state when T == 1)."""
+    from rwkv_mlx_b200 import fused as fz
+
+    rows, C = 21 * T, 768
+    g = torch.Generator(device="cuda").manual_seed(T)
+    x = torch.randn(rows, C, device="cuda", generator=g).to(dt)
+    mix = torch.rand(6, C, device="cuda", generator=g).to(dt)
+    state = torch.randn(rows // T, C, device="cuda", generator=g).to(dt)
+    ref = fz.lerp(x, mix, T, prev=state.clone())
+    dest = state if T == 1 else torch.empty_like(state)
+    out = fz.lerp(x, mix, T, prev=state, prev_out=dest)
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)
+    assert torch.equal(dest, x.view(rows // T, T, C)[:, -1])

@@ -286,6 +286,9 @@ int rwkv_tmix_post(const void* y, const void* r, const void* k, const void* v, c
                    const void* ln_w, const void* ln_b, const void* r_k, void* out, long long rows,
                    int C, int H, float eps, int per_head, int dtype, void* stream);
 int rwkv_relu_sq(void* x, long long n, int dtype, void* stream);
+/* In place on h (4, n) (the stacked first-stage TimeMix LoRA products v, w, a, g):
+ * tanh on h[1], sigmoid on h[3] (model.py:204, :212); h[0], h[2] untouched. */
+int rwkv_lora_act(void* h, long long n, int dtype, void* stream);
 int rwkv_add_layernorm(const void* x, const void* delta, const void* w, const void* b,
                        void* x_out, void* y, long long rows, int C, float eps, int dtype,
                        void* stream);

@@ -244,6 +244,27 @@ __global__ void __launch_bounds__(128, 8)  // <= 64 registers: 32 warps per SM
 }
 
 // ---------------------------------------------------------------------------
+// The activations between the two stages of the stacked TimeMix LoRA products, h (4, n):
+// tanh on slice 1 (decay), sigmoid on slice 3 (gate), slices 0 and 2 untouched
+// (model.py:204, :212).  One launch instead of two.
+template <typename T>
+__global__ void __launch_bounds__(256) lora_act_kernel(T* __restrict__ h, long long nvec) {
+    constexpr int V = Vec<T>::N;
+    for (long long q = blockIdx.x * (long long)blockDim.x + threadIdx.x; q < 2 * nvec;
+         q += (long long)gridDim.x * blockDim.x) {
+        const bool gate = q >= nvec;
+        T* p = h + ((gate ? 3 : 1) * nvec + (gate ? q - nvec : q)) * V;
+        Vec<T> a;
+        a.load(p);
+#pragma unroll
+        for (int i = 0; i < V; i++) {
+            const float f = a.get(i);
+            a.set(i, gate ? 1.f / (1.f + expf(-f)) : tanhf(f));
+        }
+        a.store(p);
+    }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(256) relu_sq_kernel(T* __restrict__ x, long long nvec) {
     constexpr int V = Vec<T>::N;
@@ -412,6 +433,18 @@ extern "C" int rwkv_relu_sq(void* x, long long n, int dtype, void* stream) {
     RWKV_DISPATCH_DTYPE(dtype, T_, {
         if (n % Vec<T_>::N) return RWKV_ERR_SHAPE;
         relu_sq_kernel<T_><<<grid_for(n / Vec<T_>::N, 256), 256, 0, st>>>((T_*)x, n / Vec<T_>::N);
+    });
+    return check_launch();
+}
+
+extern "C" int rwkv_lora_act(void* h, long long n, int dtype, void* stream) {
+    if (n <= 0) return RWKV_ERR_SHAPE;
+    if (!h) return RWKV_ERR_ARG;
+    if (!aligned(h, 16)) return RWKV_ERR_ALIGN;
+    cudaStream_t st = (cudaStream_t)stream;
+    RWKV_DISPATCH_DTYPE(dtype, T_, {
+        if (n % Vec<T_>::N) return RWKV_ERR_SHAPE;
+        lora_act_kernel<T_><<<grid_for(2 * (n / Vec<T_>::N), 256), 256, 0, st>>>((T_*)h, n / Vec<T_>::N);
     });
     return check_launch();
 }

@@ -69,6 +69,12 @@ def tmix_post(y, r, k, v, g, ln_w, ln_b, r_k, H: int, eps: float, per_head: bool
     return out
 
 
+def lora_act_(h: torch.Tensor) -> torch.Tensor:
+    """In place on the stacked LoRA hidden h (4, rows, D): tanh on h[1], sigmoid on h[3]."""
+    _call("rwkv_lora_act", nat.ptr(h), h[0].numel(), nat.dtype_code(h), nat.stream_ptr(h.device))
+    return h
+
+
 def relu_sq_(x: torch.Tensor) -> torch.Tensor:
     _call("rwkv_relu_sq", nat.ptr(x), x.numel(), nat.dtype_code(x), nat.stream_ptr(x.device))
     return x

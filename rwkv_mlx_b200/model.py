@@ -175,11 +175,9 @@ class RWKV_Tmix_x070(nn.Module):
 
     def _lora_products(self, X):
         """wl, al, vl, g of the fused paths from the mixes X (6, rows, C) in two batched
-        products (4 launches instead of 10)."""
+        products (3 launches instead of 10)."""
         w1, w2 = self._packed_lora()
-        h = torch.bmm(X[2:6], w1)  # (4, rows, D): v, w, a, g
-        torch.tanh_(h[1])
-        torch.sigmoid_(h[3])
+        h = fz.lora_act_(torch.bmm(X[2:6], w1))  # (4, rows, D): v, tanh(w), a, sigmoid(g)
         o = torch.bmm(h, w2)
         return o[1], o[2], o[0], o[3]
 

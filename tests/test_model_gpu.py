@@ -229,3 +229,19 @@ def test_lerp_writes_the_next_shift_state(dt, T):
     torch.cuda.synchronize()
     assert torch.equal(out, ref)
     assert torch.equal(dest, x.view(rows // T, T, C)[:, -1])
+
+
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16, torch.float32])
+def test_lora_act_matches_torch(dt):
+    """One-launch tanh (slice 1) / sigmoid (slice 3) of the stacked LoRA hidden."""
+    from rwkv_mlx_b200 import fused as fz
+
+    h = (3 * torch.randn(4, 300, 128, device="cuda", generator=torch.Generator(device="cuda").manual_seed(1))).to(dt)
+    ref = h.clone()
+    ref[1] = torch.tanh(ref[1].float()).to(dt)
+    ref[3] = torch.sigmoid(ref[3].float()).to(dt)
+    fz.lora_act_(h)
+    torch.cuda.synchronize()
+    assert torch.equal(h[0], ref[0]) and torch.equal(h[2], ref[2])
+    tol = {torch.float16: 1e-3, torch.bfloat16: 8e-3, torch.float32: 1e-6}[dt]
+    assert (h.float() - ref.float()).abs().max().item() <= tol

@@ -289,6 +289,9 @@ int rwkv_relu_sq(void* x, long long n, int dtype, void* stream);
 /* In place on h (4, n) (the stacked first-stage TimeMix LoRA products v, w, a, g):
  * tanh on h[1], sigmoid on h[3] (model.py:204, :212); h[0], h[2] untouched. */
 int rwkv_lora_act(void* h, long long n, int dtype, void* stream);
+/* Greedy decoding's next token (the batched decode graph): out[row] = index of the first
+ * maximum of x[row, 0:V] (row stride ld), as torch.argmax, in int64. */
+int rwkv_argmax_rows(const void* x, long long ld, long long rows, int V, int64_t* out, int dtype, void* stream);
 int rwkv_add_layernorm(const void* x, const void* delta, const void* w, const void* b,
                        void* x_out, void* y, long long rows, int C, float eps, int dtype,
                        void* stream);

@@ -69,6 +69,7 @@ SIGNATURES = {
     "rwkv_tmix_post": (_I, [_P] * 9 + [ctypes.c_longlong, _I, _I, ctypes.c_float, _I, _I, _P]),
     "rwkv_relu_sq": (_I, [_P, ctypes.c_longlong, _I, _P]),
     "rwkv_lora_act": (_I, [_P, ctypes.c_longlong, _I, _P]),
+    "rwkv_argmax_rows": (_I, [_P, ctypes.c_longlong, ctypes.c_longlong, _I, _P, _I, _P]),
     "rwkv_add_layernorm": (_I, [_P] * 6 + [ctypes.c_longlong, _I, ctypes.c_float, _I, _P]),
 }
 
@@ -112,7 +113,7 @@ KERNELS_PER_CALL = {
     "rwkv_moe_router": 2, "rwkv_moe_router_noalloc": 2, "rwkv_moe_permute": 3, "rwkv_moe_lora_down": 1,
     "rwkv_moe_lora_combine": 1, "rwkv_moe_lora_apply": 1, "rwkv_moe_ortho_loss": 1, "rwkv_moe_gather_rows": 1,
     "rwkv_moe_lora_up": 1, "rwkv_moe_combine_rows": 1, "rwkv_lerp": 1, "rwkv_lerp_prev": 1, "rwkv_lerp_prev_state": 1, "rwkv_tmix_mid": 1,
-    "rwkv_tmix_post": 1, "rwkv_relu_sq": 1, "rwkv_lora_act": 1, "rwkv_add_layernorm": 1, "rwkv_moe_expert_mix_rows": 1,
+    "rwkv_tmix_post": 1, "rwkv_relu_sq": 1, "rwkv_lora_act": 1, "rwkv_argmax_rows": 1, "rwkv_add_layernorm": 1, "rwkv_moe_expert_mix_rows": 1,
     "rwkv_ce_chunk": 1, "rwkv_ce_finalize": 1, "rwkv_ce_chunk_grad": 1,
 }
 launch_count = 0

@@ -337,6 +337,54 @@ __global__ void __launch_bounds__(256)
     }
 }
 
+// ---------------------------------------------------------------------------
+// Greedy decoding's argmax over each row of the logits (first index of the maximum, as
+// torch.argmax), written as int64 token ids: one CTA per row, 16-byte vectors.
+template <typename T>
+__global__ void __launch_bounds__(256)
+    argmax_rows_kernel(const T* __restrict__ x, long long ld, long long rows, int V, int64_t* __restrict__ out) {
+    constexpr int NV = Vec<T>::N;
+    __shared__ float sv[8];
+    __shared__ int si[8];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const bool vec = ((reinterpret_cast<uintptr_t>(x) | (uintptr_t)(ld * sizeof(T))) % 16 == 0) && V % NV == 0;
+    for (long long row = blockIdx.x; row < rows; row += gridDim.x) {
+        const T* p = x + row * ld;
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+        if (vec) {
+            for (int j = tid * NV; j < V; j += 256 * NV) {
+                Vec<T> a;
+                a.load(p + j);
+#pragma unroll
+                for (int i = 0; i < NV; i++) {
+                    const float f = a.get(i);
+                    if (f > bv) bv = f, bi = j + i;  // ascending within the thread: first index kept
+                }
+            }
+        } else {
+            for (int j = tid; j < V; j += 256) {
+                const float f = to_f32(p[j]);
+                if (f > bv) bv = f, bi = j;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) bv = ov, bi = oi;
+        }
+        if (lane == 0) sv[warp] = bv, si[warp] = bi;
+        __syncthreads();
+        if (tid == 0) {
+            for (int w = 1; w < 8; w++)
+                if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) bv = sv[w], bi = si[w];
+            out[row] = bi == 0x7fffffff ? 0 : bi;
+        }
+        __syncthreads();
+    }
+}
+
 static int grid_for(long long work, int per_block) {
     long long g = (work + per_block - 1) / per_block;
     return (int)(g < 148 * 32 ? (g > 0 ? g : 1) : 148 * 32);
@@ -463,5 +511,15 @@ extern "C" int rwkv_add_layernorm(const void* x, const void* delta, const void* 
         add_layernorm_kernel<T_><<<grid_for(rows, 8), 256, 0, st>>>((const T_*)x, (const T_*)delta, (const T_*)w,
                                                                     (const T_*)b, (T_*)x_out, (T_*)y, rows, C, eps);
     });
+    return check_launch();
+}
+
+extern "C" int rwkv_argmax_rows(const void* x, long long ld, long long rows, int V, int64_t* out, int dtype,
+                                void* stream) {
+    if (rows <= 0 || V <= 0 || ld < V) return RWKV_ERR_SHAPE;
+    if (!x || !out) return RWKV_ERR_ARG;
+    cudaStream_t st = (cudaStream_t)stream;
+    const int grid = rows < 148 * 16 ? (int)rows : 148 * 16;
+    RWKV_DISPATCH_DTYPE(dtype, T_, argmax_rows_kernel<T_><<<grid, 256, 0, st>>>((const T_*)x, ld, rows, V, out));
     return check_launch();
 }

@@ -92,3 +92,15 @@ def add_layernorm(x, delta, w, b, eps: float = 1e-5):
           nat.ptr(b.to(x.dtype).contiguous()), nat.ptr(x_out), nat.ptr(y), rows, C, float(eps), nat.dtype_code(x),
           nat.stream_ptr(x.device))
     return (x_out if delta is not None else x), y
+
+
+def argmax_rows(x: torch.Tensor, out: torch.Tensor = None) -> torch.Tensor:
+    """torch.argmax(x, -1) for 2-d x (first index of the maximum), int64, into ``out``."""
+    rows, V = x.shape
+    if x.stride(1) != 1:
+        x = x.contiguous()
+    if out is None:
+        out = torch.empty(rows, device=x.device, dtype=torch.int64)
+    _call("rwkv_argmax_rows", nat.ptr(x), x.stride(0), rows, V, nat.ptr(out), nat.dtype_code(x),
+          nat.stream_ptr(x.device))
+    return out

@@ -569,7 +569,10 @@ class DecodeGraph:
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph), torch.no_grad():
             self.logits = self.model.forward_rnn_batch(self.tokens, states)
-            self.tokens.copy_(self.logits.argmax(-1))
+            if self.tokens.dtype == torch.int64 and self.tokens.is_contiguous() and self.logits.dim() == 2:
+                fz.argmax_rows(self.logits, out=self.tokens)  # one launch, straight into the token buffer
+            else:
+                self.tokens.copy_(self.logits.argmax(-1))
 
     def step(self):
         self.graph.replay()

@@ -245,3 +245,18 @@ def test_lora_act_matches_torch(dt):
     assert torch.equal(h[0], ref[0]) and torch.equal(h[2], ref[2])
     tol = {torch.float16: 1e-3, torch.bfloat16: 8e-3, torch.float32: 1e-6}[dt]
     assert (h.float() - ref.float()).abs().max().item() <= tol
+
+
+@pytest.mark.parametrize("dt,V", [(torch.float16, 65536), (torch.bfloat16, 1000), (torch.float32, 777)])
+def test_argmax_rows_matches_torch(dt, V):
+    """Row argmax for greedy decoding: first index of the maximum, ties included."""
+    from rwkv_mlx_b200 import fused as fz
+
+    g = torch.Generator(device="cuda").manual_seed(V)
+    x = torch.randn(37, V, device="cuda", generator=g).to(dt)
+    x[5, :] = 1.0  # all tied: index 0
+    x[6, V // 3] = x[6, 2 * V // 3] = x[6].max() + 1  # two tied maxima: the first
+    got = fz.argmax_rows(x)
+    torch.cuda.synchronize()
+    assert torch.equal(got, x.argmax(-1))
+    assert got[5].item() == 0 and got[6].item() == V // 3

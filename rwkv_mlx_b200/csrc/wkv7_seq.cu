@@ -347,6 +347,11 @@ __global__ void __launch_bounds__(256)
     __shared__ float sv[N];
     const int bh = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const size_t vbase = (size_t)bh * N;
+    // the state rows first: their loads overlap the small per-token loads and the barrier
+    float2* Sb = reinterpret_cast<float2*>(S + (size_t)bh * N * N);
+    float2 s[8];
+#pragma unroll
+    for (int rr = 0; rr < 8; rr++) s[rr] = Sb[(warp * 8 + rr) * (N / 2) + lane];
     if (tid < N) sv[tid] = ldg_f32(v + vbase + tid);
     const int j0 = 2 * lane;
     float2 rj, dj, kj, aj, bj;
@@ -358,11 +363,7 @@ __global__ void __launch_bounds__(256)
     if (w_mode == 0) dj.x = expf(-expf(dj.x)), dj.y = expf(-expf(dj.y));
     __syncthreads();
 
-    float2* Sb = reinterpret_cast<float2*>(S + (size_t)bh * N * N);
-    float2 s[8];
     float u[8], yp[8];
-#pragma unroll
-    for (int rr = 0; rr < 8; rr++) s[rr] = Sb[(warp * 8 + rr) * (N / 2) + lane];
 #pragma unroll
     for (int rr = 0; rr < 8; rr++) u[rr] = fmaf(s[rr].x, aj.x, s[rr].y * aj.y);
 #pragma unroll

@@ -59,6 +59,20 @@ def _chunk_grad(logits2d, ld, targets, state, mask, out, g, l2_factor, scaled, d
     nat.check(rc, "rwkv_ce_chunk_grad")
 
 
+_FP32_OUT = [True]  # the GEMM with a 16-bit product and an fp32 output is available
+
+
+def _accumulate_fp32(acc, a, b):
+    """acc (fp32) + a @ b for 16-bit a, b: one GEMM accumulating into fp32 where the
+    library offers it, else the product in a's type added in fp32."""
+    if _FP32_OUT[0]:
+        try:
+            return torch.addmm(acc, a, b, out_dtype=torch.float32)
+        except (RuntimeError, TypeError, NotImplementedError):
+            _FP32_OUT[0] = False
+    return acc.add_(torch.mm(a, b).float())
+
+
 class _LossOnLogits(torch.autograd.Function):
     @staticmethod
     def forward(ctx, logits2d, targets, mask, l2_factor):
@@ -107,7 +121,7 @@ class _HeadLoss(torch.autograd.Function):
             lg = torch.mm(x2d, weight[c0:c1].t())
             # unscaled d loss / d logits (O(1) entries); g / den is applied to the products
             _chunk_grad(lg, c1 - c0, targets, state, ctx.mask, out, g, ctx.l2_factor, False, lg, c0, c1 - c0)
-            dx.add_(torch.mm(lg, weight[c0:c1]).float())
+            dx = _accumulate_fp32(dx, lg, weight[c0:c1])
             dw[c0:c1] = torch.mm(lg.t(), x2d)
         s = g / out[3]
         dx.mul_(s)

@@ -385,6 +385,69 @@ __global__ void __launch_bounds__(256)
     }
 }
 
+// add_layernorm with the row held in registers (NVL 16-byte vectors per lane, C <= 256 V):
+// one read of x / delta instead of three passes, the same summation order and roundings
+// as add_layernorm_kernel (identical results); in decode every pass was a memory round trip.
+template <typename T, int NVL>
+__global__ void __launch_bounds__(256)
+    add_layernorm_reg_kernel(const T* x, const T* __restrict__ delta, const T* __restrict__ w,
+                             const T* __restrict__ b, T* x_out, T* __restrict__ y, long long rows, int C,
+                             float eps) {
+    constexpr int V = Vec<T>::N;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nv = C / V;
+    for (long long row = blockIdx.x * 8LL + warp; row < rows; row += gridDim.x * 8LL) {
+        const size_t base = row * C;
+        float a[NVL][V];
+        float s = 0.f;
+#pragma unroll
+        for (int j = 0; j < NVL; j++) {
+            const int q = lane + 32 * j;
+            if (q < nv) {
+                Vec<T> xv;
+                xv.load(x + base + q * V);
+                if (delta) {
+                    Vec<T> d;
+                    d.load(delta + base + q * V);
+#pragma unroll
+                    for (int i = 0; i < V; i++) xv.set(i, xv.get(i) + d.get(i));
+                    xv.store(x_out + base + q * V);
+                }
+#pragma unroll
+                for (int i = 0; i < V; i++) a[j][i] = xv.get(i), s += a[j][i];
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        const float mean = s / (float)C;
+        float s2 = 0.f;
+#pragma unroll
+        for (int j = 0; j < NVL; j++)
+            if (lane + 32 * j < nv) {
+#pragma unroll
+                for (int i = 0; i < V; i++) {
+                    const float d = a[j][i] - mean;
+                    s2 = fmaf(d, d, s2);
+                }
+            }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+        const float rs = rsqrtf(s2 / (float)C + eps);
+#pragma unroll
+        for (int j = 0; j < NVL; j++) {
+            const int q = lane + 32 * j;
+            if (q < nv) {
+                Vec<T> wv, bv, o;
+                wv.load(w + q * V);
+                bv.load(b + q * V);
+#pragma unroll
+                for (int i = 0; i < V; i++) o.set(i, fmaf((a[j][i] - mean) * rs, wv.get(i), bv.get(i)));
+                o.store(y + base + q * V);
+            }
+        }
+    }
+}
+
 static int grid_for(long long work, int per_block) {
     long long g = (work + per_block - 1) / per_block;
     return (int)(g < 148 * 32 ? (g > 0 ? g : 1) : 148 * 32);
@@ -508,8 +571,19 @@ extern "C" int rwkv_add_layernorm(const void* x, const void* delta, const void* 
     cudaStream_t st = (cudaStream_t)stream;
     RWKV_DISPATCH_DTYPE(dtype, T_, {
         if (C % Vec<T_>::N) return RWKV_ERR_SHAPE;
-        add_layernorm_kernel<T_><<<grid_for(rows, 8), 256, 0, st>>>((const T_*)x, (const T_*)delta, (const T_*)w,
-                                                                    (const T_*)b, (T_*)x_out, (T_*)y, rows, C, eps);
+        const int nvl = (C / Vec<T_>::N + 31) / 32;
+        auto reg = [&](auto kern) {
+            kern<<<grid_for(rows, 8), 256, 0, st>>>((const T_*)x, (const T_*)delta, (const T_*)w, (const T_*)b,
+                                                    (T_*)x_out, (T_*)y, rows, C, eps);
+        };
+        if (nvl <= 1) reg(add_layernorm_reg_kernel<T_, 1>);
+        else if (nvl <= 2) reg(add_layernorm_reg_kernel<T_, 2>);
+        else if (nvl <= 3) reg(add_layernorm_reg_kernel<T_, 3>);
+        else if (nvl <= 4) reg(add_layernorm_reg_kernel<T_, 4>);
+        else if (nvl <= 8) reg(add_layernorm_reg_kernel<T_, 8>);
+        else
+            add_layernorm_kernel<T_><<<grid_for(rows, 8), 256, 0, st>>>(
+                (const T_*)x, (const T_*)delta, (const T_*)w, (const T_*)b, (T_*)x_out, (T_*)y, rows, C, eps);
     });
     return check_launch();
 }

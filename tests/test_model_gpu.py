@@ -260,3 +260,23 @@ def test_argmax_rows_matches_torch(dt, V):
     torch.cuda.synchronize()
     assert torch.equal(got, x.argmax(-1))
     assert got[5].item() == 0 and got[6].item() == V // 3
+
+
+@pytest.mark.parametrize("dt,C,with_delta", [(torch.float16, 768, True), (torch.bfloat16, 64, False),
+                                             (torch.float32, 2048, True), (torch.float16, 4096, True)])
+def test_add_layernorm_matches_torch(dt, C, with_delta):
+    """Residual add + LayerNorm (registers for C <= 256 vectors, three passes beyond)."""
+    from rwkv_mlx_b200 import fused as fz
+
+    g = torch.Generator(device="cuda").manual_seed(C)
+    x = torch.randn(333, C, device="cuda", generator=g).to(dt)
+    d = torch.randn(333, C, device="cuda", generator=g).to(dt) if with_delta else None
+    w = (1 + 0.1 * torch.randn(C, device="cuda", generator=g)).to(dt)
+    b = (0.1 * torch.randn(C, device="cuda", generator=g)).to(dt)
+    xs, y = fz.add_layernorm(x, d, w, b, 1e-5)
+    torch.cuda.synchronize()
+    ref_x = (x + d) if with_delta else x
+    assert torch.equal(xs, ref_x)
+    ref_y = torch.nn.functional.layer_norm(ref_x.float(), (C,), w.float(), b.float(), 1e-5)
+    tol = {torch.float16: 4e-3, torch.bfloat16: 3e-2, torch.float32: 1e-5}[dt]
+    assert (y.float() - ref_y).abs().max().item() < tol

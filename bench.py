@@ -402,7 +402,8 @@ def run_moe(args, ws, rank, dev):
                        "l2": "x and outputs (3 x 100 MB) larger than L2"},
             "gpu_launches": launches,
             "roofline": {"kernel": "MoE path (router + fused lora_apply)", "bound": "hbm", "achieved": gbs,
-                         "peak": hbm, "unit": "GB/s", "frac": gbs / hbm, "traffic": None, "launch_ms": moe_ms,
+                         "peak": hbm, "unit": "GB/s", "frac": gbs / hbm, "traffic": traffic_for("moe_path", ntok, 1, 1),
+                         "launch_ms": moe_ms,
                          "algorithmic_bytes": algo, "peak_source": src},
             "clocks": clocks}
 

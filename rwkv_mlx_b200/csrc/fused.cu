@@ -196,13 +196,22 @@ __global__ void __launch_bounds__(128, 8)  // <= 64 registers: 32 warps per SM
         } else {
             // MLX strided grouping (channel c in group c % H): one lane per group
             for (int gi = lane; gi < H; gi += 32) {
-                float s1 = 0.f;
-                for (int m = 0; m < gsz; m++) s1 += ys[gi + H * m];
-                const float mu = s1 / (float)gsz;
-                float s2 = 0.f;
-                for (int m = 0; m < gsz; m++) { const float dd = ys[gi + H * m] - mu; s2 = fmaf(dd, dd, s2); }
+                // four independent partial sums (gsz = 64 is a multiple of 4): the serial
+                // shared-memory chain is a quarter as long
+                float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+                for (int m = 0; m < gsz; m += 4) {
+                    a0 += ys[gi + H * m], a1 += ys[gi + H * (m + 1)];
+                    a2 += ys[gi + H * (m + 2)], a3 += ys[gi + H * (m + 3)];
+                }
+                const float mu = ((a0 + a1) + (a2 + a3)) / (float)gsz;
+                a0 = a1 = a2 = a3 = 0.f;
+                for (int m = 0; m < gsz; m += 4) {
+                    const float d0 = ys[gi + H * m] - mu, d1 = ys[gi + H * (m + 1)] - mu;
+                    const float d2 = ys[gi + H * (m + 2)] - mu, d3 = ys[gi + H * (m + 3)] - mu;
+                    a0 = fmaf(d0, d0, a0), a1 = fmaf(d1, d1, a1), a2 = fmaf(d2, d2, a2), a3 = fmaf(d3, d3, a3);
+                }
                 mean[gi] = mu;
-                rstd[gi] = rsqrtf(s2 / (float)gsz + eps);
+                rstd[gi] = rsqrtf(((a0 + a1) + (a2 + a3)) / (float)gsz + eps);
             }
             __syncwarp();
         }

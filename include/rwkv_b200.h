@@ -200,10 +200,11 @@ int rwkv_moe_lora_apply_supported(int C, int R, int E, int topk, int dtype);
 int rwkv_moe_lora_apply(const void* x, const void* base, const void* A, const void* B,
                         const int32_t* inds, const void* scores, void* out, int ntok, int C,
                         int R, int E, int topk, int dtype, void* stream);
-/* Select the kernel of rwkv_moe_lora_apply: 0 automatic (= 2), 1 mma.sync (64-token
- * tiles, two passes per tile), 2 tcgen05 (persistent, 128-token tiles, operands
- * staged by cp.async into the tensor cores' shared-memory layouts, accumulators in
- * tensor memory).  Process-wide; meant for testing one against the other. */
+/* Select the kernel of rwkv_moe_lora_apply: 0 automatic (2, or 1 when the driver cannot
+ * build TMA tensor maps), 1 mma.sync (64-token tiles, two passes per tile), 2 tcgen05
+ * (persistent, warp-specialised, 128-token tiles, operands moved by TMA into the tensor
+ * cores' shared-memory layouts, accumulators in tensor memory).  Process-wide; meant for
+ * testing one against the other. */
 int rwkv_moe_set_apply_impl(int impl);
 
 /* Expert-parallel dispatch / combine helpers (no counterpart in the reference,

@@ -1216,8 +1216,13 @@ extern "C" int rwkv_moe_lora_apply(const void* x, const void* base, const void* 
         if (dtype == RWKV_F16) return launch_apply_en<__half>(x, base, A, B, inds, scores, out, ntok, C, R, E, topk, st);
         return launch_apply_en<__nv_bfloat16>(x, base, A, B, inds, scores, out, ntok, C, R, E, topk, st);
     }
-    if (dtype == RWKV_F16) return moe_lora_apply_tc<__half>(x, base, A, B, inds, scores, out, ntok, C, R, E, topk, st);
-    return moe_lora_apply_tc<__nv_bfloat16>(x, base, A, B, inds, scores, out, ntok, C, R, E, topk, st);
+    const int rc = dtype == RWKV_F16
+                       ? moe_lora_apply_tc<__half>(x, base, A, B, inds, scores, out, ntok, C, R, E, topk, st)
+                       : moe_lora_apply_tc<__nv_bfloat16>(x, base, A, B, inds, scores, out, ntok, C, R, E, topk, st);
+    if (rc != -100) return rc;  // -100: no tensor maps on this driver (nothing was launched)
+    if (g_apply_impl == 2) return RWKV_ERR_CUDA;  // the tcgen05 kernel was asked for explicitly
+    if (dtype == RWKV_F16) return launch_apply_en<__half>(x, base, A, B, inds, scores, out, ntok, C, R, E, topk, st);
+    return launch_apply_en<__nv_bfloat16>(x, base, A, B, inds, scores, out, ntok, C, R, E, topk, st);
 }
 
 extern "C" int rwkv_moe_ortho_loss(const void* A, float* out, int E, int C, int R, int dtype,

@@ -391,6 +391,9 @@ __global__ void __launch_bounds__(atc::NTH, 1)
 }
 
 namespace atc {
+// internal status: the tensor maps could not be built (before anything was launched);
+// the automatic kernel choice then runs the mma.sync kernel instead
+constexpr int APPLY_TC_NO_MAPS = -100;
 using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                               const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                               CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -415,14 +418,14 @@ static EncodeFn encoder() {
 static int make_map(CUtensorMap* m, bool bf16, const void* base, int rank, const cuuint64_t* dims,
                     const cuuint64_t* strides, const cuuint32_t* box, bool swizzle128) {
     EncodeFn enc = encoder();
-    if (!enc) return set_error(RWKV_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+    if (!enc) return set_error(APPLY_TC_NO_MAPS, "cuTensorMapEncodeTiled is not available");
     const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
     const CUresult r = enc(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
                            (cuuint32_t)rank, const_cast<void*>(base), dims, strides, box, estr,
                            CU_TENSOR_MAP_INTERLEAVE_NONE,
                            swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return set_error(RWKV_ERR_CUDA, "cuTensorMapEncodeTiled rejected a tensor map");
+    if (r != CUDA_SUCCESS) return set_error(APPLY_TC_NO_MAPS, "cuTensorMapEncodeTiled rejected a tensor map");
     return RWKV_OK;
 }
 }  // namespace atc

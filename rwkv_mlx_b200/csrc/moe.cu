@@ -1,9 +1,13 @@
 // LoRA-MoE ChannelMix kernels (reference rwkv_mlx/moe.py:35-163).
 //
-//   moe_router     : fp32 logits x @ Wg^T (+ optional bias), warp-level top-k
-//                    (ties -> lower expert id), softmax over the selected logits,
-//                    per-CTA partial sums for aux / z-loss (moe.py:56-84).
+//   moe_router_mma : fp32-accurate logits x @ Wg^T (+ optional bias) on mma.sync for
+//                    16-bit x (split gate weights), quad-level top-k (ties -> lower
+//                    expert id), softmax over the selected logits, per-CTA partial sums
+//                    for aux / z-loss (moe.py:56-84); moe_router: the same on FMAs for
+//                    fp32 x.
 //   moe_finalize   : deterministic (fixed-order) reduction of those partials.
+//   moe_lora_apply : the fused adapter apply on mma.sync (the tcgen05 + TMA kernel that
+//                    runs by default is in moe_apply_tc.cu).
 //   moe_count / moe_scan / moe_scatter : stable counting sort of the
 //                    (token, slot) entries by expert -> perm, inv, offsets.
 //   moe_lora_down  : h[p] = x[token(p)] @ A[e(p)]  for every sorted entry p.

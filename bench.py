@@ -25,6 +25,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 from datetime import timedelta
 from pathlib import Path
@@ -86,10 +87,10 @@ class ClockSampler:
 
     def __init__(self, dev):
         self.proc = None
-        self.out = ROOT / "gpurun_out" / f"clocks_{os.getpid()}.csv"
+        self.tmp = tempfile.TemporaryDirectory(prefix="rwkv_bench_clocks_")
+        self.out = Path(self.tmp.name) / "clocks.csv"
         try:
             uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
-            self.out.parent.mkdir(exist_ok=True)
             self.fh = open(self.out, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", uuid, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
@@ -99,6 +100,7 @@ class ClockSampler:
 
     def stop(self):
         if self.proc is None:
+            self.tmp.cleanup()
             return None
         time.sleep(0.25)
         self.proc.terminate()
@@ -121,6 +123,7 @@ class ClockSampler:
             for n, v in zip(names, parts[3:7]):
                 if v.lower() == "active":
                     reasons.add(n)
+        self.tmp.cleanup()
         if not sm:
             return None
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons),

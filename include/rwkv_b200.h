@@ -146,8 +146,9 @@ int rwkv_moe_router(const void* x, const float* gate_w, const float* bias, float
  * reserved).  Its scratch is a file-scope device array of
  * rwkv_moe_router_noalloc_scratch_bytes() bytes (~75 KB), held by every GPU that
  * loads this library until the process exits.  Limit: E <= 32 (any ntok).
- * The first call on a device looks up that array's device address with the
- * device current; make that first call before any stream capture.  All calls
+ * The first call in a CUDA context looks up that array's device address with
+ * the device current (again after a cudaDeviceReset, which makes a new
+ * context); make that first call before any stream capture.  All calls
  * on a device share the array (it keeps the last call's contents; nothing in it
  * needs to start at zero), so calls that overlap on the same GPU, e.g. on two
  * streams, race: serialize them. */

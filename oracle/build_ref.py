@@ -15,7 +15,8 @@ here, so this script:
 3. compiles the result with g++ into ``oracle/_ref/`` (git-ignored; it travels to
    the GPU box with the rest of the tree, which needs no reference sources).
 
-Run from this container: ``python oracle/build_ref.py``.  Outputs:
+The reference checkout is read from ``$RWKV_MLX_REFERENCE`` (default: a directory
+named ``reference`` beside this repository).  Run: ``python oracle/build_ref.py``.  Outputs:
 ``oracle/_ref/manifest.json`` plus one ``.so`` per (kernel, dtype).
 """
 
@@ -23,6 +24,7 @@ from __future__ import annotations
 
 import ast
 import json
+import os
 import sys
 from pathlib import Path
 
@@ -32,7 +34,8 @@ HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE.parent))
 from oracle.metal_cpu import build_kernel  # noqa: E402
 
-REF_FILE = Path("/root/reference/rwkv_mlx/kernels/wkv7_metal.py")
+REF_ROOT = Path(os.environ.get("RWKV_MLX_REFERENCE", str(HERE.parent.parent / "reference")))
+REF_FILE = REF_ROOT / "rwkv_mlx" / "kernels" / "wkv7_metal.py"
 OUT = HERE / "_ref"
 
 FWD_IN = ["r", "w", "k", "v", "a", "b", "wkv_H", "wkv_T"]

@@ -31,6 +31,11 @@ __device__ __forceinline__ float ldg_f32(const T* p) { return to_f32(__ldg(p)); 
 int set_cuda_error(cudaError_t e);
 int check_launch();
 int set_error(int code, const char* msg);  // records msg for rwkv_last_error()
+void clear_error();                        // rwkv_last_error() reads "no error" again
+
+// Internal status of the tcgen05 LoRA-MoE apply launcher: the tensor maps could not be
+// built (nothing was launched), so the automatic kernel choice may fall back.
+constexpr int APPLY_TC_NO_MAPS = -100;
 
 inline bool aligned(const void* p, size_t n) { return (reinterpret_cast<uintptr_t>(p) % n) == 0; }
 

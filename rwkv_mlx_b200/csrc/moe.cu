@@ -1223,8 +1223,9 @@ extern "C" int rwkv_moe_lora_apply(const void* x, const void* base, const void* 
     const int rc = dtype == RWKV_F16
                        ? moe_lora_apply_tc<__half>(x, base, A, B, inds, scores, out, ntok, C, R, E, topk, st)
                        : moe_lora_apply_tc<__nv_bfloat16>(x, base, A, B, inds, scores, out, ntok, C, R, E, topk, st);
-    if (rc != -100) return rc;  // -100: no tensor maps on this driver (nothing was launched)
+    if (rc != APPLY_TC_NO_MAPS) return rc;  // launched (or failed after launching)
     if (g_apply_impl == 2) return RWKV_ERR_CUDA;  // the tcgen05 kernel was asked for explicitly
+    clear_error();  // the fallback below succeeds or records its own error
     if (dtype == RWKV_F16) return launch_apply_en<__half>(x, base, A, B, inds, scores, out, ntok, C, R, E, topk, st);
     return launch_apply_en<__nv_bfloat16>(x, base, A, B, inds, scores, out, ntok, C, R, E, topk, st);
 }
@@ -1250,6 +1251,8 @@ extern "C" int rwkv_moe_ortho_loss(const void* A, float* out, int E, int C, int 
 // with its per-CTA partial sums in the file-scope device array below instead of a
 // caller-provided workspace.
 // ===========================================================================
+#include <cuda.h>
+
 #include <mutex>
 
 namespace rwkv {
@@ -1260,25 +1263,65 @@ constexpr size_t NOALLOC_SCRATCH_BYTES =
 // ~75 KB, held by every GPU that loads this library until the process exits.
 static __device__ __align__(256) unsigned char g_router_scratch[NOALLOC_SCRATCH_BYTES];
 
+// The address is cached per CUDA context, keyed by the context's unique ID
+// (cuCtxGetId): a context that is destroyed and created again (cudaDeviceReset, or the
+// primary context released and retained) loads this module again at a new address and
+// gets a new ID, so the lookup runs again instead of handing out a stale pointer.
 static std::mutex g_scratch_mu;
-static void* g_scratch_addr[128];
+constexpr int SCRATCH_CACHE = 64;
+static unsigned long long g_scratch_ctx[SCRATCH_CACHE];
+static void* g_scratch_addr[SCRATCH_CACHE];
+static int g_scratch_n = 0;
 
-// Device address of g_router_scratch on the current device.  The host-side name
-// is only a stand-in, so the address is looked up once per device, with that
-// device current, the first time the entry point runs on it.
-static int router_scratch_address(void** out) {
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return set_cuda_error(e);
-    if (dev < 0 || dev >= 128) return RWKV_ERR_ARG;
-    std::lock_guard<std::mutex> lk(g_scratch_mu);
-    if (!g_scratch_addr[dev]) {
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+
+// ID of the calling thread's current context (0 if it cannot be read: no caching then).
+static unsigned long long current_context_id() {
+    static CtxGetCurrentFn get_cur = nullptr;
+    static CtxGetIdFn get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
         void* p = nullptr;
-        e = cudaGetSymbolAddress(&p, g_router_scratch);
-        if (e != cudaSuccess) return set_cuda_error(e);
-        g_scratch_addr[dev] = p;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_cur = reinterpret_cast<CtxGetCurrentFn>(p);
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<CtxGetIdFn>(p);
+    });
+    CUcontext ctx = nullptr;
+    unsigned long long id = 0;
+    if (!get_cur || !get_id || get_cur(&ctx) != CUDA_SUCCESS || !ctx || get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+    return id;
+}
+
+// Device address of g_router_scratch in the current context.  The host-side name is
+// only a stand-in, so the address is looked up with the device current, the first
+// time the entry point runs in that context (the lookup also makes the runtime bind
+// the device's context to the calling thread if it was not yet).
+static int router_scratch_address(void** out) {
+    unsigned long long id = current_context_id();
+    {
+        std::lock_guard<std::mutex> lk(g_scratch_mu);
+        for (int i = 0; id && i < g_scratch_n; i++)
+            if (g_scratch_ctx[i] == id) {
+                *out = g_scratch_addr[i];
+                return RWKV_OK;
+            }
     }
-    *out = g_scratch_addr[dev];
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_router_scratch);
+    if (e != cudaSuccess) return set_cuda_error(e);
+    id = current_context_id();  // the context is current now
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    if (id && g_scratch_n < SCRATCH_CACHE) {
+        g_scratch_ctx[g_scratch_n] = id;
+        g_scratch_addr[g_scratch_n] = p;
+        g_scratch_n++;
+    }
+    *out = p;
     return RWKV_OK;
 }
 }  // namespace rwkv

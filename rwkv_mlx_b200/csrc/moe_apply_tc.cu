@@ -391,9 +391,8 @@ __global__ void __launch_bounds__(atc::NTH, 1)
 }
 
 namespace atc {
-// internal status: the tensor maps could not be built (before anything was launched);
-// the automatic kernel choice then runs the mma.sync kernel instead
-constexpr int APPLY_TC_NO_MAPS = -100;
+// APPLY_TC_NO_MAPS (common.cuh): the tensor maps could not be built (before anything
+// was launched); the automatic kernel choice then runs the mma.sync kernel instead
 using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                               const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                               CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);

@@ -19,6 +19,8 @@ int set_error(int code, const char* msg) {
     snprintf(g_err, sizeof(g_err), "%s", msg);
     return code;
 }
+
+void clear_error() { snprintf(g_err, sizeof(g_err), "%s", "no error"); }
 }  // namespace rwkv
 
 extern "C" const char* rwkv_last_error(void) { return rwkv::g_err; }

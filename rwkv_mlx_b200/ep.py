@@ -123,6 +123,7 @@ class ExpertParallelLoRAMoE(nn.Module):
         self.lora_B.copy_(B_all[lo:hi])
 
     def forward(self, x: torch.Tensor):
+        gpu_moe.check_forward_only("ExpertParallelLoRAMoE", x, (self.lora_A, self.lora_B, self.router.gate.weight))
         ops, g, k, E, El = self.ops, self.group, self.top_k, self.n_experts, self.local
         B, T, C = x.shape
         ntok = B * T

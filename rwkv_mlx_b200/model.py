@@ -545,7 +545,12 @@ class DecodeGraph:
 
     ``states`` (from :meth:`RWKV.init_state` / :meth:`RWKV.forward_with_state`) and the
     token buffer keep their storage across steps; :meth:`step` replays the graph:
-    logits = forward_rnn_batch(tokens, states); tokens = argmax(logits)."""
+    logits = forward_rnn_batch(tokens, states); tokens = argmax(logits).
+
+    The graph reads the weights as they were packed at capture (the stacked mixes,
+    W_r/W_k/W_v and LoRA pairs are copies).  :meth:`step` therefore checks that no
+    parameter has been updated in place or replaced since the capture and raises if
+    one has: build a new DecodeGraph after loading or changing weights."""
 
     def __init__(self, model: "RWKV", states: list, tokens: torch.Tensor, warmup: int = 2):
         self.model, self.states = model, states
@@ -573,15 +578,57 @@ class DecodeGraph:
                 fz.argmax_rows(self.logits, out=self.tokens)  # one launch, straight into the token buffer
             else:
                 self.tokens.copy_(self.logits.argmax(-1))
+        self._params = list(model.parameters())
+        self._fingerprint = self._weights_fingerprint()
+
+    def _weights_fingerprint(self):
+        return tuple((p.data_ptr(), p._version) for p in self._params)
 
     def step(self):
+        if self._weights_fingerprint() != self._fingerprint:
+            raise RuntimeError("DecodeGraph: a model parameter was updated or replaced after the graph was "
+                               "captured; the graph would decode with stale packed weights. Build a new "
+                               "DecodeGraph.")
         self.graph.replay()
         return self.tokens
 
 
-def _moe_rnn(ffn, x):
-    from .moe import lora_apply, lora_apply_supported, lora_combine, lora_down, permute, router_forward
+# ---------------------------------------------------------------------------
+# The reference's module-level RNN-mode functions (model.py:441-506), same signatures
+# ---------------------------------------------------------------------------
+def _time_mixing_rnn(layer_id: int, H: int, N: int, x: torch.Tensor, x_prev: torch.Tensor,
+                     v_first: torch.Tensor, state: torch.Tensor, att: RWKV_Tmix_x070):
+    """RNN-mode time mixing of one token (model.py:441-495).
 
+    x, x_prev, v_first (C,); state (H, N, N) fp32 -> (out (C,), x, new state (H, N, N),
+    v_first).  Like the reference (immutable MLX arrays) the caller's ``state`` is not
+    modified: the update runs in place on a copy (the batched kernel behind
+    :meth:`RWKV_Tmix_x070.forward_rnn`, one sequence).  For ``layer_id == 0`` the value
+    is returned as the new ``v_first``."""
+    if layer_id != att.layer_id:
+        raise ValueError(f"layer_id={layer_id} but att belongs to layer {att.layer_id}")
+    if H != att.config.n_head or N != att.config.head_size:
+        raise ValueError(f"H={H}, N={N} do not match the layer ({att.config.n_head}, {att.config.head_size})")
+    C = H * N
+    S = state.detach().to(torch.float32).reshape(1, H, N, N).clone()
+    out, _, S, vf = att.forward_rnn(x.reshape(1, C), x_prev.reshape(1, C), v_first.reshape(1, C), S)
+    return out.reshape(C), x, S.reshape(H, N, N), vf.reshape(C)
+
+
+def _channel_mixing_rnn(x: torch.Tensor, x_prev: torch.Tensor, ffn: RWKV_CMix_x070):
+    """RNN-mode channel mixing of one token (model.py:498-506): x, x_prev (C,) ->
+    (out (C,), x).  Like the reference it needs a plain ChannelMix (``ffn.x_k``,
+    ``ffn.key``)."""
+    C = x.shape[-1]
+    out, _ = ffn.forward_rnn(x.reshape(1, C), x_prev.reshape(1, C))
+    return out.reshape(C), x
+
+
+def _moe_rnn(ffn, x):
+    from .moe import (check_forward_only, lora_apply, lora_apply_supported, lora_combine, lora_down, permute,
+                      router_forward)
+
+    check_forward_only("LoRAMoE_CMix", x, (ffn.lora_A, ffn.lora_B, ffn.router.gate.weight))
     r = router_forward(x.contiguous(), ffn.router.gate.weight, ffn.top_k, ffn.router.bias)
     C = x.shape[-1]
     if lora_apply_supported(C, ffn.lora_rank, ffn.n_experts, ffn.top_k, x.dtype):

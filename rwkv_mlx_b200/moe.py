@@ -22,7 +22,11 @@ products of each expert run as library GEMMs (cuBLAS) on that expert's contiguou
 range with the squared ReLU applied in place between them (``rwkv_relu_sq``), and
 ``rwkv_moe_combine_rows`` forms the score-weighted sum per token.
 
-These modules compute the forward pass only (no autograd through the kernels).
+These modules compute the forward pass only (no autograd through the kernels): a call
+with autograd enabled that would need gradients (an input that requires grad, or a
+trainable adapter / router / expert parameter) raises instead of returning values
+that silently carry no gradient.  Run them under ``torch.no_grad()`` /
+``torch.inference_mode()``, or freeze the parameters.
 """
 
 from __future__ import annotations
@@ -38,6 +42,22 @@ from .fused import relu_sq_
 
 def _stream(dev):
     return nat.stream_ptr(dev)
+
+
+def check_forward_only(name: str, x: torch.Tensor, params) -> None:
+    """Raise if autograd would need gradients through these forward-only kernels.
+
+    The reference's module is differentiable (finetune_moe.py trains the adapters and
+    the router through it); these kernels have no backward, so a training call must
+    fail loudly rather than yield zero gradients for the adapters, the router and the
+    layers before it."""
+    if not torch.is_grad_enabled():
+        return
+    if x.requires_grad or any(p.requires_grad for p in params):
+        raise RuntimeError(
+            f"{name}: the CUDA kernels of this module are forward-only (no backward); call it "
+            "under torch.no_grad() / torch.inference_mode(), or freeze its parameters "
+            "(requires_grad_(False)) and pass an input that does not require grad")
 
 
 def router_forward(x2d: torch.Tensor, gate_w: torch.Tensor, top_k: int, bias=None,
@@ -223,6 +243,8 @@ class LoRAMoE_CMix(nn.Module):
         self.router = Router(C, n_experts, top_k)
 
     def forward(self, x: torch.Tensor):
+        # the base is frozen (stop_gradient in moe.py:131); adapters and router are not
+        check_forward_only("LoRAMoE_CMix", x, (self.lora_A, self.lora_B, self.router.gate.weight))
         B, T, C = x.shape
         with torch.no_grad():
             base_out = self.base(x)
@@ -297,6 +319,7 @@ class MoE_CMix(nn.Module):
 
     def forward(self, x: torch.Tensor):
         """x (B, T, C) -> (out (B, T, C), aux_loss, z_loss)  (moe.py:224-239)."""
+        check_forward_only("MoE_CMix", x, self.parameters())
         B, T, C = x.shape
         out, r = self._experts(x.reshape(B * T, C).contiguous(), None, T)
         return out.reshape(B, T, C), r["aux"], r["z"]
@@ -305,6 +328,7 @@ class MoE_CMix(nn.Module):
         """One token per sequence: x, x_prev (Bs, C) -> (Bs, C).  The reference's RNN
         mode has no MoE branch; this is the ChannelMix RNN step (model.py:498-506) per
         selected expert, weighted like the GPT-mode output."""
+        check_forward_only("MoE_CMix", x, self.parameters())
         out, _ = self._experts(x.contiguous(), x_prev, 1)
         return out
 

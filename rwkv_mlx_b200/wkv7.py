@@ -123,8 +123,7 @@ def _bwd(r, w, k, v, a, b, dy, ckpt, head_size=64, s0=None, dsT=None, want_ds0=F
             *[nat.ptr(g) for g in grads], nat.ptr(ds0), B, T, H, 64, nat.dtype_code(r),
             nat.dtype_code(w), ckpt_len, nat.ptr(ws), ws_bytes, nat.stream_ptr(dev))
     nat.check(rc, "rwkv_wkv7_backward_ws")
-    if w.dtype != r.dtype:
-        pass  # dw is produced in r.dtype like the reference (wkv7_metal.py:317)
+    # dw is produced in r.dtype like the reference's (wkv7_metal.py:317), whatever w's dtype
     return tuple(grads), ds0
 
 

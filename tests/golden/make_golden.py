@@ -1,6 +1,7 @@
 """Generate golden vectors by running the reference's own Python code.
 
-Run in a container that has the reference at /root/reference:
+Run where the reference checkout is available, at ``$RWKV_MLX_REFERENCE`` or (the
+default) in a directory named ``reference`` beside this repository:
 
     python tests/golden/make_golden.py
 
@@ -22,6 +23,10 @@ Cases (all seeded):
              modelfull_* with full-expert MoE_CMix in every layer.
   fullmoe_*  MoE_CMix(C=64, F=128, E=4, k=2) forward.
   loss_*     l2_wrap_loss and l2_wrap_loss_masked (train.py:317-362).
+  cmix_rnn_* _channel_mixing_rnn on layer 1 of the tiny model.
+  router4k_* Router(768, 8, 2) on 4096 fp16 tokens (x regenerated from a seed by
+             tests/inputs.router_x, its SHA-256 stored), as BASELINE configs[3]'s router
+             sees them (without the harness's logit bias: the reference router has none).
   conv_*     convert_pytorch_to_mlx (convert.py:16-141) on a PyTorch-layout state dict of
              the tiny model: names, shapes, dtypes and SHA-256 of every converted tensor,
              and the inferred config.
@@ -32,6 +37,7 @@ Cases (all seeded):
 from __future__ import annotations
 
 import hashlib
+import os
 import sys
 from pathlib import Path
 
@@ -39,7 +45,7 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parent.parent
-REF = Path("/root/reference")
+REF = Path(os.environ.get("RWKV_MLX_REFERENCE", str(ROOT.parent / "reference")))
 sys.path.insert(0, str(HERE / "mlx_shim"))
 sys.path.insert(0, str(ROOT))
 sys.path.insert(0, str(REF))
@@ -242,6 +248,24 @@ def main():
     G["conv_sha256"] = np.stack([np.frombuffer(hashlib.sha256(np.ascontiguousarray(conv[n]).tobytes()).digest(),
                                                np.uint8) for n in names])
     G["conv_config"] = np.array(json.dumps(conf, sort_keys=True))
+
+    # ---- cases added later use their own generator (earlier draws stay unchanged) ----
+    from tests.inputs import router_x
+
+    rng2 = np.random.default_rng(21)
+    ffn = m.blocks[1].ffn
+    xc = rng2.standard_normal(128).astype(np.float32)
+    xcp = rng2.standard_normal(128).astype(np.float32)
+    outc, xco = ref_model._channel_mixing_rnn(xc, xcp, ffn)
+    G.update(cmix_rnn_x=xc, cmix_rnn_xprev=xcp, cmix_rnn_out=outc)
+
+    r4 = ref_moe.Router(768, 8, 2)
+    r4.gate.weight = (rng2.standard_normal((8, 768)) / np.sqrt(768)).astype(np.float32)
+    x4 = router_x(4096, 768, seed=22)  # fp16
+    G["router4k_x_sha256"] = np.frombuffer(hashlib.sha256(x4.tobytes()).digest(), np.uint8)
+    i4, s4, a4, z4 = r4(x4.reshape(1, 4096, 768))
+    G.update(router4k_w=r4.gate.weight, router4k_inds=i4, router4k_scores=s4, router4k_aux=np.array(a4),
+             router4k_z=np.array(z4))
 
     out_path = HERE / "reference_golden.npz"
     np.savez_compressed(out_path, **{k: np.asarray(v) for k, v in G.items()})

@@ -29,3 +29,8 @@ def rel_rms(x, ref):
     ref = np.asarray(ref, np.float64)
     den = np.sqrt(np.mean(ref ** 2))
     return float(np.sqrt(np.mean((x - ref) ** 2)) / max(den, 1e-30))
+
+
+def router_x(ntok, C, seed):
+    """Router inputs of BASELINE configs[3]: x ~ N(0, 1) as fp16, (ntok, C)."""
+    return np.random.default_rng(seed).standard_normal((ntok, C)).astype(np.float16)

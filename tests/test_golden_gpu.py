@@ -173,3 +173,52 @@ def test_converted_pytorch_checkpoint_runs_like_the_reference(tmp_path):
     with torch.no_grad():
         logits, _ = m(_dev(G["model_idx"], torch.long))
     assert rel_rms(logits.cpu().numpy(), G["model_logits"]) < 2e-3
+
+
+def test_reference_signature_rnn_functions_match_reference():
+    """_time_mixing_rnn(layer_id, H, N, x, x_prev, v_first, state, att) and
+    _channel_mixing_rnn(x, x_prev, ffn) with the reference's signatures and unbatched
+    shapes (model.py:441-506); the caller's state is left unchanged, as with MLX arrays."""
+    from rwkv_mlx_b200.model import _channel_mixing_rnn, _time_mixing_rnn
+
+    G = golden()
+    cfg, m = _model("model", 2)
+    att, ffn = m.blocks[1].att, m.blocks[1].ffn
+    S = _dev(G["rnn_S"])
+    S_before = S.clone()
+    with torch.no_grad():
+        out, x_ret, S_new, vf = _time_mixing_rnn(1, cfg.n_head, cfg.head_size, _dev(G["rnn_x"]),
+                                                 _dev(G["rnn_xprev"]), _dev(G["rnn_vfirst"]), S, att)
+        cout, cx = _channel_mixing_rnn(_dev(G["cmix_rnn_x"]), _dev(G["cmix_rnn_xprev"]), ffn)
+    assert out.shape == (128,) and S_new.shape == (cfg.n_head, 64, 64) and vf.shape == (128,)
+    assert torch.equal(S, S_before)
+    assert torch.equal(x_ret, _dev(G["rnn_x"]))
+    assert rel_rms(out.cpu().numpy(), G["rnn_out"]) < 1e-4
+    assert rel_rms(S_new.cpu().numpy(), G["rnn_Snew"]) < 1e-5
+    assert torch.equal(vf, _dev(G["rnn_vfirst"]))  # layer 1 keeps v_first
+    assert rel_rms(cout.cpu().numpy(), G["cmix_rnn_out"]) < 1e-4
+    assert torch.equal(cx, _dev(G["cmix_rnn_x"]))
+
+
+def test_router_config4_scale_matches_reference():
+    """Router(768, 8, 2) on 4096 fp16 tokens: expert sets bit-exact with the reference's
+    own router, scores to fp16 rounding, aux and z to fp32 rounding."""
+    from rwkv_mlx_b200.moe import Router
+    from tests.inputs import router_x
+
+    G = golden()
+    router = Router(768, 8, 2).cuda()
+    with torch.no_grad():
+        router.gate.weight.copy_(_dev(G["router4k_w"]))
+        x = torch.tensor(router_x(4096, 768, seed=22), device="cuda").view(1, 4096, 768)
+        inds, scores, aux, z = router(x)
+    inds = inds.cpu().numpy().reshape(-1, 2).astype(np.int64)
+    scores = scores.float().cpu().numpy().reshape(-1, 2)
+    ref_i = G["router4k_inds"].reshape(-1, 2).astype(np.int64)
+    ref_s = G["router4k_scores"].reshape(-1, 2).astype(np.float32)
+    assert (np.sort(inds, -1) == np.sort(ref_i, -1)).all()
+    for slot in range(2):
+        j = np.where(ref_i[:, 0] == inds[:, slot], 0, 1)
+        assert np.abs(scores[:, slot] - ref_s[np.arange(len(j)), j]).max() <= 1e-3
+    assert abs(float(aux) - float(G["router4k_aux"])) < 1e-5
+    assert abs(float(z) - float(G["router4k_z"])) < 1e-4 * max(1.0, float(G["router4k_z"]))

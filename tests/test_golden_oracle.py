@@ -128,3 +128,36 @@ def test_l2_wrap_losses():
     mk = torch.tensor(G["loss_mask"], dtype=torch.float64)
     assert abs(float(loss_oracle.l2_wrap_loss(lg, tg)) - float(G["loss_l2wrap"])) < 1e-5
     assert abs(float(loss_oracle.l2_wrap_loss_masked(lg, tg, mk)) - float(G["loss_l2wrap_masked"])) < 1e-5
+
+
+def test_router_at_config4_scale_matches_reference():
+    """4096 fp16 tokens, E=8, top-2 (moe.py:51-86): the oracle's own float64 logits route
+    every token to the same expert set as the reference's float32 router; the scores,
+    aux and z agree to float32 rounding."""
+    import hashlib
+
+    from tests.inputs import router_x
+
+    G = golden()
+    x = router_x(4096, 768, seed=22)
+    assert np.array_equal(np.frombuffer(hashlib.sha256(x.tobytes()).digest(), np.uint8), G["router4k_x_sha256"])
+    inds, scores, aux, z, _ = moe_oracle.router(x, G["router4k_w"], 2)
+    ref_i = G["router4k_inds"].reshape(-1, 2)
+    ref_s = G["router4k_scores"].reshape(-1, 2).astype(np.float64)
+    assert (np.sort(inds, -1) == np.sort(ref_i.astype(np.int64), -1)).all()
+    for slot in range(2):  # reference slot order is unspecified: match scores by expert
+        j = np.where(ref_i[:, 0] == inds[:, slot], 0, 1)
+        assert np.abs(scores[:, slot] - ref_s[np.arange(len(j)), j]).max() < 1e-3  # fp16 scores
+    assert abs(aux - float(G["router4k_aux"])) < 1e-5
+    assert abs(z - float(G["router4k_z"])) < 1e-4 * max(1.0, z)
+
+
+def test_channel_mixing_rnn_step():
+    """_channel_mixing_rnn (model.py:498-506) of the tiny model's layer 1."""
+    G = golden()
+    P = model_params("model", seed=2)
+    x, xp = G["cmix_rnn_x"].astype(np.float64), G["cmix_rnn_xprev"].astype(np.float64)
+    xk = P["blocks.1.ffn.x_k"].reshape(-1).astype(np.float64)
+    kw, vw = P["blocks.1.ffn.key.weight"].astype(np.float64), P["blocks.1.ffn.value.weight"].astype(np.float64)
+    k = np.maximum(kw @ (x + (xp - x) * xk), 0) ** 2
+    assert rel_rms(vw @ k, G["cmix_rnn_out"]) < 1e-5

@@ -181,6 +181,11 @@ def test_decode_graph_matches_eager_decode():
     graphed = [g.step().clone() for _ in range(5)]
     for a, b in zip(eager, graphed):
         assert torch.equal(a, b)
+    # an in-place weight update after the capture: the graph refuses to replay stale copies
+    with torch.no_grad():
+        m.blocks[0].att.key.weight.mul_(1.0)
+    with pytest.raises(RuntimeError, match="DecodeGraph"):
+        g.step()
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.float16])

@@ -48,6 +48,38 @@ def test_router_bit_exact_indices(dt, C, E, k, with_bias):
     np.testing.assert_array_equal(r["counts"].cpu().numpy(), np.bincount(inds.reshape(-1), minlength=E))
 
 
+def test_router_config4_routing_vs_oracle_own_logits():
+    """BASELINE configs[3]'s router: 65,536 fp16 tokens, C=768, E=8, top-2, per-expert
+    logit bias N(0, 1.5).  The GPU's indices are compared with the oracle routing on its
+    OWN logits (x.astype(f32) @ W^T + bias, moe.py:56, evaluated in float64), not the
+    GPU's.  Any token that differs must be a provable near-tie: the two competing
+    logits differ by less than the worst-case fp32 summation error of a 768-term dot
+    product (768 * 2^-24 * sum |x_i w_i|, plus the bias rounding)."""
+    from rwkv_mlx_b200.moe import router_forward
+
+    ntok, C, E, k = 65536, 768, 8, 2
+    x = _x(ntok, C, 4, torch.float16)
+    rng = np.random.default_rng(5)
+    gw = torch.tensor(rng.standard_normal((E, C)) / np.sqrt(C), dtype=torch.float32, device="cuda")
+    bias = torch.tensor(rng.normal(0, 1.5, E), dtype=torch.float32, device="cuda")
+    r = router_forward(x, gw, k, bias)
+    torch.cuda.synchronize()
+    xn, wn, bn = x.float().cpu().numpy(), gw.cpu().numpy(), bias.cpu().numpy()
+    lg = mo.gate_logits(xn, wn, bn)
+    ref = mo.topk_from_logits(lg, k)
+    got = r["inds"].cpu().numpy().astype(np.int64)
+    bad = np.nonzero((got != ref).any(-1))[0]
+    mag = np.abs(xn.astype(np.float64)) @ np.abs(wn.astype(np.float64)).T  # sum_i |x_i w_ie|
+    bound = C * 2.0 ** -24 * mag + 2.0 ** -24 * np.abs(bn)
+    for t in bad:
+        # the sets differ only where the boundary logits are within the error bound
+        for e_g, e_r in zip(got[t], ref[t]):
+            if e_g != e_r:
+                assert abs(lg[t, e_g] - lg[t, e_r]) <= bound[t, e_g] + bound[t, e_r], (t, e_g, e_r)
+    print(f"config-4 routing: {len(bad)} of {ntok} tokens differ from the oracle (near-ties)")
+    assert len(bad) <= 8
+
+
 def test_router_ties_go_to_lower_id():
     from rwkv_mlx_b200.moe import router_forward
 

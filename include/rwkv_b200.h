@@ -50,8 +50,16 @@ const char* rwkv_last_error(void);
 /* ABI version of this header (bumped on any signature change). */
 int rwkv_abi_version(void);
 /* Error word set by a kernel that gave up a bounded wait (0 = none).  Reads the
- * device word synchronously; `clear` resets it.  Negative on a CUDA error. */
+ * device word synchronously; `clear` resets it.  Negative on a CUDA error.
+ * A CTA of the tcgen05 WKV-7 forward that gives up also fills its outputs (y, sa,
+ * sT, ckpt) with NaN, so an abort never leaves plausible-looking values behind.
+ * No counterpart in the reference (its Metal kernels have no waits). */
 int rwkv_device_error(int clear);
+/* Test hooks, no counterpart in the reference: make every bounded wait of the
+ * tcgen05 WKV-7 forward give up at once (on != 0), exercising its abort path
+ * without any real stall; set the device error word of that kernel directly.  */
+int rwkv_debug_force_wait_timeout(int on);
+int rwkv_debug_set_device_error(int value);
 /* Select the WKV-7 forward kernel: 0 automatic (with all per-token inputs 16-byte
  * aligned: the tcgen05 kernel for fp16/bf16 activations, the mma.sync kernel for
  * fp32; otherwise the step-sequential kernel), 1 step-sequential, 2 chunked on
@@ -77,6 +85,25 @@ int rwkv_wkv7_forward(const void* r, const void* w, const void* k, const void* v
                       const void* a, const void* b, const float* s0, void* y,
                       float* sT, float* ckpt, float* sa, int B, int T, int H, int N,
                       int dtype, int w_dtype, int ckpt_len, void* stream);
+
+/* WKV-7 forward with a caller-provided workspace (same contract and reference code
+ * as rwkv_wkv7_forward, wkv7_metal.py:250-279 and :28-91).  When B*H leaves most
+ * SMs idle, the tcgen05 kernel cuts each sequence into segments of whole 16-step
+ * chunks: a transition pass computes every segment's affine state map
+ * S_end = S_start M + C (a 128-row state [C; M]), a scan composes them into each
+ * segment's initial state, and the forward runs all segments in parallel.  The
+ * workspace holds those maps and states: rwkv_wkv7_forward_workspace_size bytes
+ * (0 when no segmenting happens for these sizes; workspace may then be NULL).  */
+size_t rwkv_wkv7_forward_workspace_size(int B, int T, int H, int N, int dtype);
+int rwkv_wkv7_forward_ws(const void* r, const void* w, const void* k, const void* v,
+                         const void* a, const void* b, const float* s0, void* y,
+                         float* sT, float* ckpt, float* sa, int B, int T, int H, int N,
+                         int dtype, int w_dtype, int ckpt_len, void* workspace,
+                         size_t workspace_bytes, void* stream);
+/* Segments per sequence of rwkv_wkv7_forward_ws: 0 automatic (default), n >= 1
+ * fixed (capped at the chunk count).  Process-wide; meant for testing.  No
+ * counterpart in the reference. */
+int rwkv_set_wkv_segments(int nseg);
 
 /* WKV-7 backward, exact (no division by the decay).
  * Replaces wkv7_metal_backward (wkv7_metal.py:282-319) and the backward kernel

@@ -8,6 +8,8 @@ declared in include/rwkv_b200.h.  Submodules: ``wkv7`` (WKV-7 operators),
 """
 
 from . import wkv7  # noqa: F401
+from ._native import RwkvDeviceError, RwkvNativeError, check_device_error  # noqa: F401
 from .wkv7 import wkv7_backward, wkv7_forward, wkv7_recurrent, wkv7_step, wkv7_with_state  # noqa: F401
 
-__all__ = ["wkv7", "wkv7_forward", "wkv7_backward", "wkv7_recurrent", "wkv7_step", "wkv7_with_state"]
+__all__ = ["wkv7", "wkv7_forward", "wkv7_backward", "wkv7_recurrent", "wkv7_step", "wkv7_with_state",
+           "check_device_error", "RwkvDeviceError", "RwkvNativeError"]

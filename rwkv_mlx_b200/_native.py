@@ -38,6 +38,11 @@ SIGNATURES = {
     "rwkv_device_error": (_I, [_I]),
     "rwkv_set_wkv_impl": (_I, [_I]),
     "rwkv_wkv7_forward": (_I, [_P] * 11 + [_I] * 7 + [_P]),
+    "rwkv_wkv7_forward_workspace_size": (_SZ, [_I] * 5),
+    "rwkv_wkv7_forward_ws": (_I, [_P] * 11 + [_I] * 7 + [_P, _SZ, _P]),
+    "rwkv_set_wkv_segments": (_I, [_I]),
+    "rwkv_debug_force_wait_timeout": (_I, [_I]),
+    "rwkv_debug_set_device_error": (_I, [_I]),
     "rwkv_wkv7_backward": (_I, [_P] * 17 + [_I] * 7 + [_P]),
     "rwkv_wkv7_backward_workspace_size": (_SZ, [_I] * 4),
     "rwkv_wkv7_backward_ws": (_I, [_P] * 17 + [_I] * 7 + [_P, _SZ, _P]),
@@ -80,6 +85,10 @@ class RwkvNativeError(RuntimeError):
     pass
 
 
+class RwkvDeviceError(RwkvNativeError):
+    """A kernel gave up a bounded wait (its outputs were filled with NaN)."""
+
+
 def load(path: Path | None = None) -> ctypes.CDLL:
     """Load the library (no GPU needed to load it)."""
     global _lib
@@ -119,10 +128,10 @@ KERNELS_PER_CALL = {
 launch_count = 0
 
 
-def check(rc: int, what: str) -> None:
+def check(rc: int, what: str, kernels: int | None = None) -> None:
     global launch_count
     if rc == 0:
-        launch_count += KERNELS_PER_CALL.get(what, 0)
+        launch_count += KERNELS_PER_CALL.get(what, 0) if kernels is None else kernels
     if rc != 0:
         msg = STATUS.get(rc, f"status {rc}")
         if rc == 4:
@@ -146,3 +155,14 @@ def dtype_code_of(dt: torch.dtype) -> int:
     if dt not in DTYPE_CODE:
         raise RwkvNativeError(f"unsupported dtype {dt}")
     return DTYPE_CODE[dt]
+
+
+def check_device_error(clear: bool = True) -> None:
+    """Raise :class:`RwkvDeviceError` if a kernel of this library gave up a bounded wait
+    since the last check (reads the device error word: a host synchronisation).  The
+    aborting kernel also fills its outputs with NaN, so results never look valid."""
+    v = lib().rwkv_device_error(1 if clear else 0)
+    if v < 0:
+        raise RwkvNativeError("rwkv_device_error failed: " + (load().rwkv_last_error() or b"").decode())
+    if v:
+        raise RwkvDeviceError(f"a kernel gave up a bounded wait (device error word {v}); its outputs are NaN")

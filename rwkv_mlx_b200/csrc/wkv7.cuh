@@ -22,9 +22,14 @@ struct WkvBwdArgs {
 
 int wkv7_fwd_seq(const WkvFwdArgs& p, cudaStream_t st);
 int wkv7_fwd_chunk(const WkvFwdArgs& p, cudaStream_t st);
-int wkv7_fwd_tc(const WkvFwdArgs& p, cudaStream_t st);
+// tcgen05 forward; nseg > 1 splits each sequence into segments run in parallel
+// (transition launch + scan + forward launch), with ws of wkv7_tc_ws_bytes bytes.
+int wkv7_fwd_tc(const WkvFwdArgs& p, int nseg, float* ws, cudaStream_t st);
+size_t wkv7_tc_ws_bytes(int B, int T, int H, int nseg);
 bool wkv7_tc_supported(int dtype);
 int read_device_error_tc(int clear);
+int set_force_wait_timeout_tc(int on);
+int set_device_error_tc(int value);
 int read_device_error_bwd(int clear);
 int read_device_error(int clear);
 int read_device_error_moe(int clear);

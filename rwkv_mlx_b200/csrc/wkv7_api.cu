@@ -6,6 +6,27 @@ using namespace rwkv;
 
 namespace rwkv {
 int g_wkv_impl = 0;
+int g_wkv_segments = 0;  // 0: automatic segment count for the tcgen05 forward
+
+// Segments per sequence for the tcgen05 forward: only when B*H leaves most SMs idle
+// (a segment costs a transition pass, so fewer than 3 segments gains nothing), and
+// with at least 8 chunks (128 steps) per segment.
+static int auto_segments(int B, int T, int H) {
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const long long units = (long long)B * H;
+    const int nch = (T + 15) / 16;
+    if (units * 3 > sms) return 1;
+    int n = (int)(sms / units);
+    if (n > nch / 8) n = nch / 8;
+    return n >= 3 ? n : 1;
+}
+static int fwd_segments(int B, int T, int H, int dtype) {
+    if (!wkv7_tc_supported(dtype) || (g_wkv_impl != 0 && g_wkv_impl != 3)) return 1;
+    const int nch = (T + 15) / 16;
+    int n = g_wkv_segments > 0 ? g_wkv_segments : auto_segments(B, T, H);
+    return n > nch ? nch : n;
+}
 }
 
 static bool inputs_aligned16(const void* const* ps, int n) {
@@ -28,10 +49,10 @@ static int check_dims(int B, int T, int H, int N, int dtype) {
     return RWKV_OK;
 }
 
-extern "C" int rwkv_wkv7_forward(const void* r, const void* w, const void* k, const void* v,
-                                 const void* a, const void* b, const float* s0, void* y,
-                                 float* sT, float* ckpt, float* sa, int B, int T, int H, int N,
-                                 int dtype, int w_dtype, int ckpt_len, void* stream) {
+static int forward_impl(const void* r, const void* w, const void* k, const void* v, const void* a,
+                        const void* b, const float* s0, void* y, float* sT, float* ckpt, float* sa, int B,
+                        int T, int H, int N, int dtype, int w_dtype, int ckpt_len, int nseg, void* ws,
+                        size_t ws_bytes, void* stream) {
     int rc = check_dims(B, T, H, N, dtype);
     if (rc) return rc;
     if (!r || !w || !k || !v || !a || !b || !y) return RWKV_ERR_ARG;
@@ -42,10 +63,48 @@ extern "C" int rwkv_wkv7_forward(const void* r, const void* w, const void* k, co
     if (g_wkv_impl == 2) return wkv7_fwd_chunk(p, (cudaStream_t)stream);
     if (g_wkv_impl == 3 || wkv7_tc_supported(dtype)) {
         if (!wkv7_tc_supported(dtype)) return RWKV_ERR_DTYPE;
-        return wkv7_fwd_tc(p, (cudaStream_t)stream);
+        const size_t need = wkv7_tc_ws_bytes(B, T, H, nseg);
+        if (need) {
+            if (!ws || ws_bytes < need) return RWKV_ERR_WORKSPACE;
+            if (!aligned(ws, 16)) return RWKV_ERR_ALIGN;
+        }
+        return wkv7_fwd_tc(p, need ? nseg : 1, (float*)ws, (cudaStream_t)stream);
     }
     return wkv7_fwd_chunk(p, (cudaStream_t)stream);
 }
+
+extern "C" int rwkv_wkv7_forward(const void* r, const void* w, const void* k, const void* v,
+                                 const void* a, const void* b, const float* s0, void* y,
+                                 float* sT, float* ckpt, float* sa, int B, int T, int H, int N,
+                                 int dtype, int w_dtype, int ckpt_len, void* stream) {
+    return forward_impl(r, w, k, v, a, b, s0, y, sT, ckpt, sa, B, T, H, N, dtype, w_dtype, ckpt_len, 1, nullptr, 0,
+                        stream);
+}
+
+extern "C" size_t rwkv_wkv7_forward_workspace_size(int B, int T, int H, int N, int dtype) {
+    if (check_dims(B, T, H, N, dtype)) return 0;
+    return wkv7_tc_ws_bytes(B, T, H, fwd_segments(B, T, H, dtype));
+}
+
+extern "C" int rwkv_wkv7_forward_ws(const void* r, const void* w, const void* k, const void* v,
+                                    const void* a, const void* b, const float* s0, void* y,
+                                    float* sT, float* ckpt, float* sa, int B, int T, int H, int N,
+                                    int dtype, int w_dtype, int ckpt_len, void* workspace,
+                                    size_t workspace_bytes, void* stream) {
+    const int nseg = check_dims(B, T, H, N, dtype) ? 1 : fwd_segments(B, T, H, dtype);
+    return forward_impl(r, w, k, v, a, b, s0, y, sT, ckpt, sa, B, T, H, N, dtype, w_dtype, ckpt_len, nseg,
+                        workspace, workspace_bytes, stream);
+}
+
+extern "C" int rwkv_set_wkv_segments(int nseg) {
+    if (nseg < 0) return RWKV_ERR_ARG;
+    g_wkv_segments = nseg;
+    return RWKV_OK;
+}
+
+extern "C" int rwkv_debug_force_wait_timeout(int on) { return set_force_wait_timeout_tc(on); }
+
+extern "C" int rwkv_debug_set_device_error(int value) { return set_device_error_tc(value); }
 
 extern "C" int rwkv_wkv7_backward(const void* r, const void* w, const void* k, const void* v,
                                   const void* a, const void* b, const void* dy, const float* s0,

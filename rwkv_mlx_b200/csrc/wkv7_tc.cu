@@ -1,23 +1,41 @@
 // WKV-7 forward with the state products on the 5th-generation tensor cores:
-// tcgen05.mma (kind::tf32, M=64) with accumulators in tensor memory.  Same chunk
-// algebra as wkv7_chunk.cu (L = 16):
+// tcgen05.mma (kind::tf32) with accumulators in tensor memory.  Same chunk algebra as
+// wkv7_chunk.cu (L = 16 steps per chunk, S0 the state entering the chunk):
 //
-//   D1 = [U | Y]^T = S0 [Wu; Wy]^T + [Ui; Yi]^T          (M=64 values, N=32, K=64)
-//   D2 = S_L       = S0 diag(GL) + V^T Kb + U^T Bb        (M=64 values, N=64 keys, K=16+16)
+//   U^T = S0 Wu^T + Ui^T,  Y^T = S0 Wy^T + Yi^T               (sa and y of the chunk)
+//   S_L = S0 diag(GL) + V^T Kb + U^T Bb
 //
-// The fp32 state lives in tensor memory (D2) for the whole sequence and is itself the
-// A operand of D1 (A read from tensor memory, B = [Wu; Wy] K-major in shared memory).
-// Per chunk the 4 state warps preload the intra-chunk part [Ui; Yi]^T into D1, one
-// thread issues the 8 K-steps of D1 as two independent accumulation chains, the warps
-// scale D2 by the chunk decay and read U and Y back, then D2 takes the rank-32 update.
-// Two groups of 4 "prep" warps compute the inputs-only chunk operands (decay factors,
-// intra-chunk products on mma.sync, triangular solve) for alternating chunks, writing
-// them straight into the UMMA operand layout; the hand-offs are mbarriers with bounded
-// waits (a CTA that gives up sets the device error word and exits, it never traps).
+// with the inputs-only parts Ui^T = V^T Gu, Yi^T = V^T Gy and V^T Kb formed as one
+// product X = V^T [Gu | Gy | Kb] (N = 96).
+//
+// Cost model (measured on B200): a tcgen05.mma blocks the thread that issues it for
+// ~280 cycles with A in shared memory and ~165 with A in tensor memory, whatever its
+// shape, while separate warps issue in parallel.  The serial state chain is therefore
+// arranged around MMA issues, not FLOPs:
+//   * the K = 64 product S0 [Wu; Wy]^T is split over the 4 state warps: warp w issues
+//     the two K-steps of keys 16w..16w+15 into its own accumulator D1_w (A = the state
+//     read from tensor memory), so the chain pays for 2 issues instead of 8;
+//   * X, which needs no state, is issued by the prep group that built the chunk (its
+//     completion is part of the chunk's "full" barrier), off the chain;
+//   * the state warps sum U = sum_w D1_w.u + X.u, write it to tensor memory, form
+//     S0 diag(GL) + V^T Kb in registers (one read-modify-write of the state), and one
+//     thread issues U^T Bb with A = U read from tensor memory (2 issues).
+// Two groups of 4 "prep" warps compute the inputs-only chunk operands (decay scan,
+// intra-chunk products on mma.sync, triangular solve) for alternating chunks, straight
+// into the UMMA operand layouts.  Every wait is a bounded mbarrier wait: a CTA that
+// gives up sets the device error word, waits (bounded) for its own MMAs in flight,
+// fills its outputs with NaN, frees its tensor memory and exits; it never traps.
+//
+// Segments (intra-sequence parallelism for small B*H): the sequence is cut into nseg
+// segments of whole chunks.  A "transition" launch runs each segment s < nseg-1 with a
+// 128-row state [C; M] (C from S = 0, or from s0 for segment 0; M from the identity,
+// no inputs), which gives the segment's affine map S_end = S_start M + C at the cost
+// of the 64-row chain (MMA issues do not depend on M).  wkv7_seg_scan_kernel composes
+// the maps into every segment's initial state, and the forward launch runs all
+// segments in parallel from those states.
 //
 // Supported for fp16 / bf16 activations (w in the activation dtype or fp32); fp32
-// activations use the mma.sync kernel (their input staging does not fit next to this
-// kernel's shared memory).
+// activations use the mma.sync kernel.
 #include <cfloat>
 
 #include "chunk_common.cuh"
@@ -28,6 +46,9 @@
 namespace rwkv {
 
 __device__ int g_device_error_tc;
+// Test hook (rwkv_debug_force_wait_timeout): every bounded wait of these kernels gives
+// up at once, which exercises the abort path without any real stall.
+static __constant__ int c_force_wait_timeout;
 
 namespace tc {
 using namespace ck;
@@ -35,18 +56,22 @@ using namespace tcc;
 
 constexpr int NT = 384;
 constexpr int NSTAGE = 3;  // operand stages for 2 prep groups: one chunk of slack
-constexpr int SBO_K64 = 16 * KLBO, SBO_K32 = 8 * KLBO, SBO_K16 = 4 * KLBO;
-constexpr int SZ_WB = 4 * SBO_K64;  // 32 rows x K=64
-constexpr int SZ_BK = 8 * SBO_K32;  // 64 rows x K=32
-constexpr int SZ_VT = 8 * SBO_K16;  // 64 rows x K=16
-constexpr int SZ_BY = 4 * SBO_K16;  // 32 rows x K=16
+constexpr int SBO_K64 = 16 * KLBO, SBO_K16 = 4 * KLBO;
+constexpr int SZ_WB = 4 * SBO_K64;   // 32 rows x K=64
+constexpr int SZ_BB = 8 * SBO_K16;   // 64 rows x K=16
+constexpr int SZ_BX = 12 * SBO_K16;  // 96 rows x K=16
 
+// Tensor-memory columns: state, the four D1 partial products, U, X per stage.
+constexpr uint32_t COL_S = 0, COL_D1 = 64, COL_U = 192, COL_X = 208;
+constexpr int ROWS_CM = 128;  // rows of a segment's transition output [C; M]
+
+template <int ROWS>
 struct __align__(128) Stage {
-    unsigned char WB[SZ_WB];  // B of D1: rows t' (0-15 Wu, 16-31 Wy), K = key
-    unsigned char BY[SZ_BY];  // B of the intra-chunk part V^T [Gu | Gy]: rows t' (0-15 Gu^T, 16-31 Gy^T), K = s
-    unsigned char BK[SZ_BK];  // B of D2: rows key, K = t' (0-15 Bb, 16-31 Kb)
-    unsigned char VT[SZ_VT];  // A of D2 (V part): rows value, K = t
-    float GL[N];              // decay of the whole chunk per key
+    unsigned char WB[SZ_WB];                  // B of D1: rows t' (0-15 Wu, 16-31 Wy), K = key
+    unsigned char BB[SZ_BB];                  // B of U^T Bb: rows key, K = t
+    unsigned char BX[SZ_BX];                  // B of X: rows 0-15 Gu^T, 16-31 Gy^T, 32-95 Kb (key), K = s
+    unsigned char VT[(ROWS / 8) * SBO_K16];   // A of X: rows value (>= 64: zero), K = t
+    float GL[N];                              // decay of the whole chunk per key
 };
 struct __align__(16) PrepScratch {
     float At[L][LD4], Rt[L][LD4], Bh[L][LD4], Kh[L][LD4];
@@ -54,57 +79,112 @@ struct __align__(16) PrepScratch {
     float GuT[L][LDM];  // (I - Mab)^-1 Mak
     float Cs[L + 1][N];  // cumulative log2 decay, Cs[0] = 0
 };
+template <int ROWS>
 struct __align__(128) Smem {
-    Stage st[NSTAGE];  // chunk c uses stage c % NSTAGE
-    unsigned char UTA[SZ_VT]; // A of D2 (U part): rows value, K = t
+    Stage<ROWS> st[NSTAGE];  // chunk c uses stage c % NSTAGE
     float Yb[L][LD8];
     PrepScratch ps[2];
-    unsigned long long full[NSTAGE], empty[NSTAGE], mma1, mma2;
+    unsigned long long full[NSTAGE], empty[NSTAGE], mma1, mma2, drain[3];
     uint32_t tmem_base;
     int abort;
 };
 
 enum { BAR_STATE = 1, BAR_PREP0 = 2 };  // BAR_PREP0 + g for prep group g
 
-__device__ __forceinline__ void st4(unsigned char* p, float a, float b, float c, float d) {
-    *reinterpret_cast<float4*>(p) = make_float4(tf32f(a), tf32f(b), tf32f(c), tf32f(d));
+struct TcArgs {
+    const void *r, *w, *k, *v, *a, *b;
+    const float* s0;  // initial state of the sequence (B,H,64,64) or null
+    void* y;
+    float *sT, *ckpt, *sa;
+    float* seg_s0;  // forward launch, nseg > 1: state entering segment s >= 1, ((bh*nseg+s)*64+row)*64
+    float* trans;   // transition launch: [C; M] of segment s < nseg-1, ((bh*(nseg-1)+s)*128+row)*64
+    int T, H, ckpt_len, nseg, seg_len;
+};
+
+__device__ __forceinline__ bool wait_tc(unsigned long long* b, uint32_t parity, volatile int* abort) {
+    if (c_force_wait_timeout) {
+        *abort = 1;
+        atomicOr(&g_device_error_tc, 2);
+        return false;
+    }
+    return mbar_wait(b, parity, abort, &g_device_error_tc);
+}
+// Bounded wait that ignores the abort flag: the end-of-kernel drain of a thread's own
+// MMAs (tensor memory may only be freed once nothing writes it any more).
+__device__ __forceinline__ void drain_wait(unsigned long long* b) {
+    const uint32_t a = smem_u32(b);
+    const long long t0 = clock64();
+    while (true) {
+        uint32_t ok;
+        asm volatile(
+            "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+            : "=r"(ok)
+            : "r"(a), "r"(0u)
+            : "memory");
+        if (ok) return;
+        if (clock64() - t0 > WAIT_CYCLES) {
+            atomicOr(&g_device_error_tc, 4);
+            return;
+        }
+    }
 }
 
+template <typename T>
+__device__ __forceinline__ uint4 nan_pack();
+template <>
+__device__ __forceinline__ uint4 nan_pack<__half>() { return make_uint4(0x7E007E00u, 0x7E007E00u, 0x7E007E00u, 0x7E007E00u); }
+template <>
+__device__ __forceinline__ uint4 nan_pack<__nv_bfloat16>() { return make_uint4(0x7FC07FC0u, 0x7FC07FC0u, 0x7FC07FC0u, 0x7FC07FC0u); }
+
 // ---------------------------------------------------------------------------
-template <typename T, typename TW>
-__global__ void __launch_bounds__(NT, 1)
-    wkv7_fwd_tc_kernel(const T* __restrict__ r, const TW* __restrict__ w, const T* __restrict__ k,
-                       const T* __restrict__ v, const T* __restrict__ a, const T* __restrict__ b,
-                       const float* __restrict__ s0, T* __restrict__ y, float* __restrict__ sT,
-                       float* __restrict__ ckpt, float* __restrict__ sa_out, int T_, int H,
-                       int ckpt_len) {
+template <typename T, typename TW, bool TRANS>
+__global__ void __launch_bounds__(NT, 1) wkv7_fwd_tc_kernel(const TcArgs p) {
+    constexpr int ROWS = TRANS ? 128 : 64;
     using R = Raw<T, TW>;
     extern __shared__ __align__(128) unsigned char smem_raw[];
-    Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
-    unsigned char* rawbuf = smem_raw + ((sizeof(Smem) + 127) / 128) * 128;  // [2 groups][R::BYTES]
+    Smem<ROWS>& sm = *reinterpret_cast<Smem<ROWS>*>(smem_raw);
+    unsigned char* rawbuf = smem_raw + ((sizeof(Smem<ROWS>) + 127) / 128) * 128;  // [2 groups][R::BYTES]
 
+    const T* __restrict__ r = (const T*)p.r;
+    const TW* __restrict__ w = (const TW*)p.w;
+    const T* __restrict__ k = (const T*)p.k;
+    const T* __restrict__ v = (const T*)p.v;
+    const T* __restrict__ a = (const T*)p.a;
+    const T* __restrict__ b = (const T*)p.b;
     const int tid = threadIdx.x, warp = tid >> 5;
-    const int bh = blockIdx.x, bi = bh / H, hi = bh % H;
+    const int nsl = TRANS ? p.nseg - 1 : p.nseg;  // segments in this launch
+    const int bh = blockIdx.x / nsl, seg = blockIdx.x % nsl, H = p.H;
+    const int bi = bh / H, hi = bh % H;
+    const int t_begin = seg * p.seg_len;
+    const int nloc = min(p.T, t_begin + p.seg_len) - t_begin;  // steps of this segment
     const size_t tstride = (size_t)H * N;
-    const size_t base = ((size_t)bi * T_ * H + hi) * N;
-    const int nchunks = (T_ + L - 1) / L;
-    const int nck = ckpt ? T_ / ckpt_len : 0;
+    const size_t base = (((size_t)bi * p.T + t_begin) * H + hi) * N;
+    const int nchunks = (nloc + L - 1) / L;
 
     if (warp == 0) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 128;" ::"r"(
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(
                          smem_u32(&sm.tmem_base))
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     if (tid == 32) {
         for (int i = 0; i < NSTAGE; i++) {
-            mbar_init(&sm.full[i], 128);
+            mbar_init(&sm.full[i], 129);  // 128 prep threads + the commit of the X product
             mbar_init(&sm.empty[i], 128);
         }
-        mbar_init(&sm.mma1, 1);
+        mbar_init(&sm.mma1, 4);  // one commit per state warp
         mbar_init(&sm.mma2, 1);
+        mbar_init(&sm.drain[0], 1);
+        mbar_init(&sm.drain[1], 1);
+        mbar_init(&sm.drain[2], 4);
         sm.abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if constexpr (TRANS) {  // rows 64..127 of V^T (the M part has no input) stay zero
+        for (int s = 0; s < NSTAGE; s++)
+            for (int i = tid; i < 8 * SBO_K16 / 16; i += NT)
+                reinterpret_cast<uint4*>(sm.st[s].VT + 8 * SBO_K16)[i] = make_uint4(0, 0, 0, 0);
+        proxy_fence();
     }
     tc_fence_before();
     __syncthreads();
@@ -145,7 +225,7 @@ __global__ void __launch_bounds__(NT, 1)
 #pragma unroll
             for (int i = 0; i < R::PER_THREAD; i++) {
                 if (prow[i] < 0) continue;
-                const bool ok = (t0 + prow[i]) < T_;
+                const bool ok = (t0 + prow[i]) < nloc;
                 const size_t step = (size_t)t0 * tstride;
                 const char* src = ok ? psrc[i] + step * (pdst[i] >= 5u * R::ARR ? sizeof(TW) : sizeof(T)) : psrc[i];
                 cp_async16(raw + pdst[i], src, ok);
@@ -158,13 +238,13 @@ __global__ void __launch_bounds__(NT, 1)
             asm volatile("cp.async.wait_all;" ::: "memory");
             bool bad = false;
             const int si = c % NSTAGE;
-            Stage& stg = sm.st[si];
-            if (c >= NSTAGE) bad = !mbar_wait(&sm.empty[si], ((c / NSTAGE) + 1) & 1, &sm.abort, &g_device_error_tc);
+            Stage<ROWS>& stg = sm.st[si];
+            if (c >= NSTAGE) bad = !wait_tc(&sm.empty[si], ((c / NSTAGE) + 1) & 1, &sm.abort);
             if (group_sync_or(BAR, bad)) break;
 
             // ---- P1: cumulative log2 decay, decayed factors, operands ----
             const int t = lane & 15, cg = 2 * pw + (lane >> 4), j0 = 8 * cg;
-            const bool tok = t < T_ - c * L;
+            const bool tok = t < nloc - c * L;
             float wv[8], cs[8], cp[8], cl[8];
             lds8<TW>(raw + 5 * R::ARR + t * R::PITCHW + j0 * sizeof(TW), wv);
 #pragma unroll
@@ -209,11 +289,9 @@ __global__ void __launch_bounds__(NT, 1)
 #pragma unroll
             for (int q = 0; q < 8; q++) {
                 const int key = j0 + q;
-                *reinterpret_cast<float*>(stg.BK + kmaj(key, t, SBO_K32)) = tf32f(xb[q] * eL[q]);
-                *reinterpret_cast<float*>(stg.BK + kmaj(key, L + t, SBO_K32)) = tf32f(xk[q] * eL[q]);
-                const float vq = tf32f(xv[q]);
-                o1[q] = vq;
-                *reinterpret_cast<float*>(stg.VT + kmaj(key, t, SBO_K16)) = vq;  // key index = value index
+                *reinterpret_cast<float*>(stg.BB + kmaj(key, t, SBO_K16)) = tf32f(xb[q] * eL[q]);
+                *reinterpret_cast<float*>(stg.BX + kmaj(2 * L + key, t, SBO_K16)) = tf32f(xk[q] * eL[q]);
+                *reinterpret_cast<float*>(stg.VT + kmaj(key, t, SBO_K16)) = tf32f(xv[q]);  // key index = value index
             }
             sts8(&ps.Cs[t + 1][j0], cs);
             if (t == 0) {
@@ -294,7 +372,7 @@ __global__ void __launch_bounds__(NT, 1)
             }
             group_sync(BAR);
 
-            // ---- P5: Wy = Rt + Mrb Wu (WB rows 16-31); Gu^T, Gy^T = Mrb Gu^T + Mrk (BY) ----
+            // ---- P5: Wy = Rt + Mrb Wu (WB rows 16-31); Gu^T, Gy^T = Mrb Gu^T + Mrk (BX rows 0-31) ----
             {
                 auto ldB = [&](const unsigned char* src, int kk, int nn) {
                     return fbits(*reinterpret_cast<const float*>(src + kmaj(kk, nn, SBO_K64)));
@@ -347,195 +425,333 @@ __global__ void __launch_bounds__(NT, 1)
 #pragma unroll
                         for (int e = 0; e < 4; e++) {
                             const int tp = g + (e >> 1) * 8, ss = 8 * nt + 2 * tg + (e & 1);
-                            *reinterpret_cast<float*>(stg.BY + kmaj(L + tp, ss, SBO_K16)) = tf32f(gy[nt][e]);
+                            *reinterpret_cast<float*>(stg.BX + kmaj(L + tp, ss, SBO_K16)) = tf32f(gy[nt][e]);
                         }
                     }
                 } else if (pw == 1) {
 #pragma unroll
                     for (int i = 0; i < (L * L) / 32; i++) {
                         const int q = lane + 32 * i, tp = q / L, ss = q % L;
-                        *reinterpret_cast<float*>(stg.BY + kmaj(tp, ss, SBO_K16)) = ps.GuT[tp][ss];
+                        *reinterpret_cast<float*>(stg.BX + kmaj(tp, ss, SBO_K16)) = ps.GuT[tp][ss];
                     }
                 }
             }
             proxy_fence();  // make the operand stores visible to the tensor cores
+            group_sync(BAR);
+            if (pt == 0) {
+                // X = V^T [Gu | Gy | Kb] into this stage's tensor-memory columns; its
+                // completion is the 129th arrival on the stage's full barrier
+                tc_fence_after();
+                const uint32_t ix = idesc_tf32(ROWS, 96), aV = smem_u32(stg.VT), bX = smem_u32(stg.BX);
+#pragma unroll
+                for (int ks = 0; ks < 2; ks++)
+                    umma(tmem + COL_X + 96 * si, umma_desc(aV + 2 * ks * KLBO, SBO_K16),
+                         umma_desc(bX + 2 * ks * KLBO, SBO_K16), ix, ks);
+                umma_commit(&sm.full[si]);
+            }
             mbar_arrive(&sm.full[si]);
         }
         asm volatile("cp.async.wait_all;" ::: "memory");
+        if (pt == 0) {  // wait for this thread's own MMAs before the tensor memory is freed
+            umma_commit(&sm.drain[g_]);
+            drain_wait(&sm.drain[g_]);
+        }
     } else {
         // ===================== state warps =====================
-        // TMEM columns: [0,64) D2 = state, [64,96) D1a, [96,128) D1b (D1 = D1a + D1b).
+        // M=64: row i of the state lives in lane 16*(i/16) + i%16 of warp i/16's 32-lane
+        // slice (lanes 0-15 of each slice); M=128 (transition): row i in lane i.
         const int tw = warp, lane = tid & 31;
-        const bool live = lane < 16;              // M=64 accumulators use lanes 0-15 of each subpartition
-        const int row = 16 * tw + lane;            // state row (value index) held by this thread
-        const uint32_t lane_base = (uint32_t)(32 * tw) << 16;
-        const uint32_t tD2 = tmem + lane_base, tD1a = tD2 + 64, tD1b = tD2 + 96;
+        const bool live = TRANS || lane < 16;
+        const int row = TRANS ? 32 * tw + lane : 16 * tw + lane;
+        const uint32_t lb = (uint32_t)(32 * tw) << 16;
+        const uint32_t tS = tmem + lb + COL_S;
         {
             float S[N];
-            const float* p = (s0 && live) ? s0 + ((size_t)bh * N + row) * N : nullptr;
+            const float* src = nullptr;
+            if (TRANS) {
+                if (row < N && seg == 0 && p.s0) src = p.s0 + ((size_t)bh * N + row) * N;
+            } else if (live) {
+                if (seg == 0) {
+                    if (p.s0) src = p.s0 + ((size_t)bh * N + row) * N;
+                } else {
+                    src = p.seg_s0 + (((size_t)bh * p.nseg + seg) * N + row) * N;
+                }
+            }
 #pragma unroll
-            for (int j = 0; j < N; j++) S[j] = p ? p[j] : 0.f;
+            for (int j = 0; j < N; j++) S[j] = src ? src[j] : ((TRANS && row - N == j) ? 1.f : 0.f);
 #pragma unroll
-            for (int j = 0; j < N; j += 16) tmem_st16(tD2 + j, &S[j]);
+            for (int j = 0; j < N; j += 16) tmem_st16(tS + j, &S[j]);
             tmem_wait_st();
         }
         bool bad_prev = false;  // a wait of the previous chunk gave up (voted on below)
         for (int c = 0; c < nchunks; c++) {
-            const int s = c % NSTAGE;
-            Stage& stg = sm.st[s];
-            const bool bad = bad_prev || !mbar_wait(&sm.full[s], (c / NSTAGE) & 1, &sm.abort, &g_device_error_tc);
+            const int si = c % NSTAGE;
+            Stage<ROWS>& stg = sm.st[si];
+            const uint32_t tX = tmem + lb + COL_X + 96 * si;
+            const bool bad = bad_prev || !wait_tc(&sm.full[si], (c / NSTAGE) & 1, &sm.abort);
             if (group_sync_or(BAR_STATE, bad)) break;
             tc_fence_after();
-            if (tid == 0) {
-                // D1a = V^T [Gu | Gy] (intra-chunk part), then + S0 [Wu; Wy]^T over two chains
-                const uint32_t i1 = idesc_tf32(64, 32), bW = smem_u32(stg.WB), aV = smem_u32(stg.VT),
-                               bY = smem_u32(stg.BY);
+            if (lane == 0) {
+                // D1_w = S0[:, keys 16w..16w+15] [Wu; Wy][:, same keys]^T: 2 of the 8 K-steps
+                const uint32_t i1 = idesc_tf32(ROWS, 32), bW = smem_u32(stg.WB);
 #pragma unroll
-                for (int ks = 0; ks < 2; ks++)
-                    umma(tmem + 64, umma_desc(aV + 2 * ks * KLBO, SBO_K16), umma_desc(bY + 2 * ks * KLBO, SBO_K16), i1, ks);
-#pragma unroll
-                for (int ks = 0; ks < 8; ks++)
-                    umma_ts((ks & 1) ? tmem + 96 : tmem + 64, tmem + 8 * ks, umma_desc(bW + 2 * ks * KLBO, SBO_K64), i1,
-                            (ks & 1) ? (ks > 1) : 1);
+                for (int j = 0; j < 2; j++) {
+                    const int ks = 2 * tw + j;
+                    umma_ts(tmem + COL_D1 + 32 * tw, tmem + COL_S + 8 * ks, umma_desc(bW + 2 * ks * KLBO, SBO_K64), i1, j);
+                }
                 umma_commit(&sm.mma1);
             }
-            const bool bad2 = !mbar_wait(&sm.mma1, c & 1, &sm.abort, &g_device_error_tc);
+            __syncwarp();
+            const bool bad2 = !wait_tc(&sm.mma1, c & 1, &sm.abort);
             tc_fence_after();
-            float S[N], u[L], yv[L], u2[L], y2[L];
+            float u[L];
+            {
+                float p0[16], p1[16], p2[16], p3[16], px[16];
+                tmem_ld16(tmem + lb + COL_D1, p0);
+                tmem_ld16(tmem + lb + COL_D1 + 32, p1);
+                tmem_ld16(tmem + lb + COL_D1 + 64, p2);
+                tmem_ld16(tmem + lb + COL_D1 + 96, p3);
+                tmem_ld16(tX, px);
+                tmem_wait_ld();
 #pragma unroll
-            for (int j = 0; j < N; j += 16) tmem_ld16(tD2 + j, &S[j]);
-            tmem_ld16(tD1a, u);
-            tmem_ld16(tD1a + 16, yv);
-            tmem_ld16(tD1b, u2);
-            tmem_ld16(tD1b + 16, y2);
-            tmem_wait_ld();
-            // state * chunk decay -> D2
+                for (int i = 0; i < L; i++) u[i] = ((p0[i] + p1[i]) + (p2[i] + p3[i])) + px[i];
+                float ut[L];
 #pragma unroll
-            for (int j = 0; j < N; j += 4) {
-                const float4 gl = *reinterpret_cast<const float4*>(&stg.GL[j]);
-                S[j] *= gl.x, S[j + 1] *= gl.y, S[j + 2] *= gl.z, S[j + 3] *= gl.w;
+                for (int i = 0; i < L; i++) ut[i] = tf32f(u[i]);
+                tmem_st16(tmem + lb + COL_U, ut);
             }
+            // state * chunk decay + V^T Kb, two 32-column halves
 #pragma unroll
-            for (int j = 0; j < N; j += 16) tmem_st16(tD2 + j, &S[j]);
-            tmem_wait_st();
-            tc_fence_before();
-            group_sync(BAR_STATE);
-            tc_fence_after();
-            if (tid == 0) {  // V^T Kb needs only the rescaled state: start it while U is staged
-                const uint32_t i2 = idesc_tf32(64, 64), aV = smem_u32(stg.VT), bK = smem_u32(stg.BK);
+            for (int j = 0; j < N; j += 32) {
+                float s0v[16], s1v[16], x0[16], x1[16];
+                tmem_ld16(tS + j, s0v);
+                tmem_ld16(tS + j + 16, s1v);
+                tmem_ld16(tX + 2 * L + j, x0);
+                tmem_ld16(tX + 2 * L + j + 16, x1);
+                tmem_wait_ld();
 #pragma unroll
-                for (int ks = 0; ks < 2; ks++)
-                    umma(tmem, umma_desc(aV + 2 * ks * KLBO, SBO_K16), umma_desc(bK + (4 + 2 * ks) * KLBO, SBO_K32), i2, 1);
-            }
-#pragma unroll
-            for (int tt = 0; tt < L; tt++) u[tt] += u2[tt], yv[tt] += y2[tt];
-            if (live) {
-#pragma unroll
-                for (int tt = 0; tt < L; tt += 4) st4(sm.UTA + kmaj(row, tt, SBO_K16), u[tt], u[tt + 1], u[tt + 2], u[tt + 3]);
-#pragma unroll
-                for (int tt = 0; tt < L; tt++) sm.Yb[tt][row] = yv[tt];
-                if (sa_out) {
-#pragma unroll
-                    for (int tt = 0; tt < L; tt++)
-                        if (c * L + tt < T_) sa_out[base + (size_t)(c * L + tt) * tstride + row] = u[tt];
+                for (int q = 0; q < 16; q += 4) {
+                    const float4 g0 = *reinterpret_cast<const float4*>(&stg.GL[j + q]);
+                    const float4 g1 = *reinterpret_cast<const float4*>(&stg.GL[j + 16 + q]);
+                    s0v[q] = fmaf(s0v[q], g0.x, x0[q]), s0v[q + 1] = fmaf(s0v[q + 1], g0.y, x0[q + 1]);
+                    s0v[q + 2] = fmaf(s0v[q + 2], g0.z, x0[q + 2]), s0v[q + 3] = fmaf(s0v[q + 3], g0.w, x0[q + 3]);
+                    s1v[q] = fmaf(s1v[q], g1.x, x1[q]), s1v[q + 1] = fmaf(s1v[q + 1], g1.y, x1[q + 1]);
+                    s1v[q + 2] = fmaf(s1v[q + 2], g1.z, x1[q + 2]), s1v[q + 3] = fmaf(s1v[q + 3], g1.w, x1[q + 3]);
                 }
+                tmem_st16(tS + j, s0v);
+                tmem_st16(tS + j + 16, s1v);
             }
             tmem_wait_st();
-            proxy_fence();
             tc_fence_before();
             if (group_sync_or(BAR_STATE, bad2)) break;
             tc_fence_after();
-            if (tid == 0) {
-                const uint32_t i2 = idesc_tf32(64, 64);
-                const uint32_t aU = smem_u32(sm.UTA), bK = smem_u32(stg.BK);
+            if (tid == 0) {  // S_L += U^T Bb, A = U read from tensor memory
+                const uint32_t i2 = idesc_tf32(ROWS, 64), bB = smem_u32(stg.BB);
 #pragma unroll
                 for (int ks = 0; ks < 2; ks++)
-                    umma(tmem, umma_desc(aU + 2 * ks * KLBO, SBO_K16), umma_desc(bK + 2 * ks * KLBO, SBO_K32), i2, 1);
+                    umma_ts(tmem + COL_S, tmem + COL_U + 8 * ks, umma_desc(bB + 2 * ks * KLBO, SBO_K16), i2, 1);
                 umma_commit(&sm.mma2);
             }
-            {  // y rows of this chunk: 8 consecutive values per thread, one 16-byte store
-                const int rr = tid >> 3, c8 = (tid & 7) * 8, t = c * L + rr;
-                if (t < T_) {
-                    const float4 f0 = *reinterpret_cast<const float4*>(&sm.Yb[rr][c8]);
-                    const float4 f1 = *reinterpret_cast<const float4*>(&sm.Yb[rr][c8 + 4]);
-                    uint4 pk;
-                    T* pe = reinterpret_cast<T*>(&pk);
-                    pe[0] = from_f32<T>(f0.x), pe[1] = from_f32<T>(f0.y), pe[2] = from_f32<T>(f0.z), pe[3] = from_f32<T>(f0.w);
-                    pe[4] = from_f32<T>(f1.x), pe[5] = from_f32<T>(f1.y), pe[6] = from_f32<T>(f1.z), pe[7] = from_f32<T>(f1.w);
-                    *reinterpret_cast<uint4*>(y + base + (size_t)t * tstride + c8) = pk;
-                }
-            }
-            const bool bad3 = !mbar_wait(&sm.mma2, c & 1, &sm.abort, &g_device_error_tc);
-            tc_fence_after();
-            if (ckpt) {
-                const int tend = (c + 1) * L;
-                if (tend <= T_ && tend % ckpt_len == 0) {
+            __syncwarp();
+            if constexpr (!TRANS) {
+                if (live && p.sa) {
 #pragma unroll
-                    for (int j = 0; j < N; j += 16) tmem_ld16(tD2 + j, &S[j]);
+                    for (int tt = 0; tt < L; tt++)
+                        if (c * L + tt < nloc) p.sa[base + (size_t)(c * L + tt) * tstride + row] = u[tt];
+                }
+                {
+                    float p0[16], p1[16], p2[16], p3[16], px[16];
+                    tmem_ld16(tmem + lb + COL_D1 + L, p0);
+                    tmem_ld16(tmem + lb + COL_D1 + 32 + L, p1);
+                    tmem_ld16(tmem + lb + COL_D1 + 64 + L, p2);
+                    tmem_ld16(tmem + lb + COL_D1 + 96 + L, p3);
+                    tmem_ld16(tX + L, px);
                     tmem_wait_ld();
                     if (live) {
-                        float* p = ckpt + (((size_t)bh * nck + tend / ckpt_len - 1) * N + row) * N;
 #pragma unroll
-                        for (int j = 0; j < N; j += 4) *reinterpret_cast<float4*>(p + j) = make_float4(S[j], S[j + 1], S[j + 2], S[j + 3]);
+                        for (int i = 0; i < L; i++) sm.Yb[i][row] = ((p0[i] + p1[i]) + (p2[i] + p3[i])) + px[i];
+                    }
+                }
+                group_sync(BAR_STATE);
+                {  // y rows of this chunk: 8 consecutive values per thread, one 16-byte store
+                    const int rr = tid >> 3, c8 = (tid & 7) * 8, t = c * L + rr;
+                    if (t < nloc) {
+                        const float4 f0 = *reinterpret_cast<const float4*>(&sm.Yb[rr][c8]);
+                        const float4 f1 = *reinterpret_cast<const float4*>(&sm.Yb[rr][c8 + 4]);
+                        uint4 pk;
+                        T* pe = reinterpret_cast<T*>(&pk);
+                        pe[0] = from_f32<T>(f0.x), pe[1] = from_f32<T>(f0.y), pe[2] = from_f32<T>(f0.z), pe[3] = from_f32<T>(f0.w);
+                        pe[4] = from_f32<T>(f1.x), pe[5] = from_f32<T>(f1.y), pe[6] = from_f32<T>(f1.z), pe[7] = from_f32<T>(f1.w);
+                        *reinterpret_cast<uint4*>((T*)p.y + base + (size_t)t * tstride + c8) = pk;
+                    }
+                }
+            }
+            const bool bad3 = !wait_tc(&sm.mma2, c & 1, &sm.abort);
+            tc_fence_after();
+            if constexpr (!TRANS) {
+                const int tend = t_begin + (c + 1) * L;  // global step index of the chunk end
+                if (p.ckpt && tend <= p.T && tend % p.ckpt_len == 0) {
+                    float S[N];
+#pragma unroll
+                    for (int j = 0; j < N; j += 16) tmem_ld16(tS + j, &S[j]);
+                    tmem_wait_ld();
+                    if (live) {
+                        const int nck = p.T / p.ckpt_len;
+                        float* q = p.ckpt + (((size_t)bh * nck + tend / p.ckpt_len - 1) * N + row) * N;
+#pragma unroll
+                        for (int j = 0; j < N; j += 4) *reinterpret_cast<float4*>(q + j) = make_float4(S[j], S[j + 1], S[j + 2], S[j + 3]);
                     }
                 }
             }
             tc_fence_before();
-            mbar_arrive(&sm.empty[s]);
+            mbar_arrive(&sm.empty[si]);
             bad_prev = bad3;  // the next chunk's first barrier decides for the whole group
         }
         if (group_sync_or(BAR_STATE, bad_prev)) sm.abort = 1;
-        if (sT && !group_sync_or(BAR_STATE, sm.abort != 0)) {
+        float* dst = nullptr;
+        if (TRANS)
+            dst = p.trans + (((size_t)bh * (p.nseg - 1) + seg) * ROWS + row) * N;
+        else if (seg == p.nseg - 1 && p.sT && live)
+            dst = p.sT + ((size_t)bh * N + row) * N;
+        if (!group_sync_or(BAR_STATE, sm.abort != 0)) {
             tc_fence_after();
             float S[N];
 #pragma unroll
-            for (int j = 0; j < N; j += 16) tmem_ld16(tD2 + j, &S[j]);
+            for (int j = 0; j < N; j += 16) tmem_ld16(tS + j, &S[j]);
             tmem_wait_ld();
-            if (live) {
-                float* p = sT + ((size_t)bh * N + row) * N;
+            if (dst) {
 #pragma unroll
-                for (int j = 0; j < N; j += 4) *reinterpret_cast<float4*>(p + j) = make_float4(S[j], S[j + 1], S[j + 2], S[j + 3]);
+                for (int j = 0; j < N; j += 4) *reinterpret_cast<float4*>(dst + j) = make_float4(S[j], S[j + 1], S[j + 2], S[j + 3]);
             }
         }
+        if (lane == 0) {  // wait for this warp's own MMAs before the tensor memory is freed
+            umma_commit(&sm.drain[2]);
+            drain_wait(&sm.drain[2]);
+        }
+        __syncwarp();
     }
     tc_fence_before();
     __syncthreads();
+    if (sm.abort) {  // a wait gave up: no output of this CTA may look valid
+        const float fnan = __int_as_float(0x7fc00000);
+        if (TRANS) {
+            float* o = p.trans + ((size_t)bh * (p.nseg - 1) + seg) * ROWS * N;
+            for (int i = tid; i < ROWS * N; i += NT) o[i] = fnan;
+        } else {
+            for (int i = tid; i < nloc * 8; i += NT)
+                *reinterpret_cast<uint4*>((T*)p.y + base + (size_t)(i >> 3) * tstride + (i & 7) * 8) = nan_pack<T>();
+            if (p.sa)
+                for (int i = tid; i < nloc * N; i += NT) p.sa[base + (size_t)(i >> 6) * tstride + (i & 63)] = fnan;
+            if (p.sT && seg == p.nseg - 1)
+                for (int i = tid; i < N * N; i += NT) p.sT[(size_t)bh * N * N + i] = fnan;
+            if (p.ckpt) {
+                const int nck = p.T / p.ckpt_len;
+                for (int ck_i = 0; ck_i < nck; ck_i++) {
+                    const int tend = (ck_i + 1) * p.ckpt_len;
+                    if (tend <= t_begin || tend > t_begin + nloc) continue;
+                    float* q = p.ckpt + ((size_t)bh * nck + ck_i) * N * N;
+                    for (int i = tid; i < N * N; i += NT) q[i] = fnan;
+                }
+            }
+        }
+    }
     if (warp == 0) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 128;" ::"r"(tmem) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
     }
 }
 
-template <typename T, typename TW>
+// Composes the segments' affine maps: S_1 = C_0 (segment 0 started from the sequence's
+// own initial state), S_{s+1} = S_s M_s + C_s.  Rows of the state are independent, so
+// each CTA owns 8 rows of one (b, h); fp32 FMA.
+__global__ void __launch_bounds__(256) wkv7_seg_scan_kernel(const float* __restrict__ trans,
+                                                            float* __restrict__ seg_s0, int nseg) {
+    __shared__ float M[N][N + 1];
+    __shared__ float S[8][N];
+    const int bh = blockIdx.x, r0 = 8 * blockIdx.y, tid = threadIdx.x;
+    const int i = tid >> 5, c0 = tid & 31, c1 = c0 + 32;
+    const size_t cm = (size_t)ROWS_CM * N;
+    const float* CM0 = trans + (size_t)bh * (nseg - 1) * cm;
+    float s0v = CM0[(size_t)(r0 + i) * N + c0], s1v = CM0[(size_t)(r0 + i) * N + c1];
+    float* out = seg_s0 + (((size_t)bh * nseg + 1) * N + r0 + i) * N;
+    out[c0] = s0v, out[c1] = s1v;
+    S[i][c0] = s0v, S[i][c1] = s1v;
+    for (int s = 1; s < nseg - 1; s++) {
+        const float* CM = CM0 + (size_t)s * cm;
+        for (int q = tid; q < N * N; q += 256) M[q >> 6][q & 63] = CM[(size_t)N * N + q];
+        __syncthreads();
+        float a0 = CM[(size_t)(r0 + i) * N + c0], a1 = CM[(size_t)(r0 + i) * N + c1];
+#pragma unroll 16
+        for (int j = 0; j < N; j++) {
+            const float sj = S[i][j];
+            a0 = fmaf(sj, M[j][c0], a0);
+            a1 = fmaf(sj, M[j][c1], a1);
+        }
+        __syncthreads();
+        S[i][c0] = a0, S[i][c1] = a1;
+        out = seg_s0 + (((size_t)bh * nseg + s + 1) * N + r0 + i) * N;
+        out[c0] = a0, out[c1] = a1;
+    }
+}
+
+template <typename T, typename TW, bool TRANS>
 size_t smem_bytes() {
-    return ((sizeof(Smem) + 127) / 128) * 128 + 2 * (size_t)Raw<T, TW>::BYTES;
+    return ((sizeof(Smem<TRANS ? 128 : 64>) + 127) / 128) * 128 + 2 * (size_t)Raw<T, TW>::BYTES;
+}
+
+template <typename T, typename TW, bool TRANS>
+int launch(const TcArgs& a, int grid, cudaStream_t st) {
+    auto kern = wkv7_fwd_tc_kernel<T, TW, TRANS>;
+    const size_t smem = smem_bytes<T, TW, TRANS>();
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return set_cuda_error(e);
+    kern<<<grid, NT, smem, st>>>(a);
+    return check_launch();
+}
+
+template <typename T, typename TW>
+int run(const WkvFwdArgs& p, int nseg, float* ws, cudaStream_t st) {
+    const int nch = (p.T + L - 1) / L;
+    const int seg_chunks = (nch + nseg - 1) / nseg;
+    nseg = (nch + seg_chunks - 1) / seg_chunks;  // no empty segment
+    TcArgs a{p.r, p.w, p.k, p.v, p.a, p.b, p.s0, p.y, p.sT, p.ckpt, p.sa, nullptr, nullptr,
+             p.T, p.H, p.ckpt_len, nseg, seg_chunks * L};
+    const int units = p.B * p.H;
+    if (nseg > 1) {
+        a.trans = ws;
+        a.seg_s0 = ws + (size_t)units * (nseg - 1) * ROWS_CM * N;
+        int rc = launch<T, TW, true>(a, units * (nseg - 1), st);
+        if (rc) return rc;
+        wkv7_seg_scan_kernel<<<dim3(units, N / 8), 256, 0, st>>>(a.trans, a.seg_s0, nseg);
+        rc = check_launch();
+        if (rc) return rc;
+    }
+    return launch<T, TW, false>(a, units * nseg, st);
 }
 
 }  // namespace tc
 
-template <typename T, typename TW>
-static int launch_fwd_tc(const WkvFwdArgs& p, cudaStream_t st) {
-    auto kern = tc::wkv7_fwd_tc_kernel<T, TW>;
-    const size_t smem = tc::smem_bytes<T, TW>();
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return set_cuda_error(e);
-    kern<<<p.B * p.H, tc::NT, smem, st>>>((const T*)p.r, (const TW*)p.w, (const T*)p.k, (const T*)p.v,
-                                          (const T*)p.a, (const T*)p.b, p.s0, (T*)p.y, p.sT, p.ckpt, p.sa,
-                                          p.T, p.H, p.ckpt_len);
-    return check_launch();
-}
-
 bool wkv7_tc_supported(int dtype) { return dtype == RWKV_F16 || dtype == RWKV_BF16; }
 
-int wkv7_fwd_tc(const WkvFwdArgs& p, cudaStream_t st) {
+size_t wkv7_tc_ws_bytes(int B, int T, int H, int nseg) {
+    if (nseg <= 1) return 0;
+    const int nch = (T + ck::L - 1) / ck::L;
+    const int seg_chunks = (nch + nseg - 1) / nseg;
+    nseg = (nch + seg_chunks - 1) / seg_chunks;
+    if (nseg <= 1) return 0;
+    const size_t units = (size_t)B * H;
+    return units * ((size_t)(nseg - 1) * tc::ROWS_CM * ck::N + (size_t)nseg * ck::N) * ck::N * sizeof(float);
+}
+
+int wkv7_fwd_tc(const WkvFwdArgs& p, int nseg, float* ws, cudaStream_t st) {
     switch (p.dtype) {
         case RWKV_F16:
-            if (p.w_dtype == RWKV_F16) return launch_fwd_tc<__half, __half>(p, st);
-            if (p.w_dtype == RWKV_F32) return launch_fwd_tc<__half, float>(p, st);
+            if (p.w_dtype == RWKV_F16) return tc::run<__half, __half>(p, nseg, ws, st);
+            if (p.w_dtype == RWKV_F32) return tc::run<__half, float>(p, nseg, ws, st);
             return RWKV_ERR_DTYPE;
         case RWKV_BF16:
-            if (p.w_dtype == RWKV_BF16) return launch_fwd_tc<__nv_bfloat16, __nv_bfloat16>(p, st);
-            if (p.w_dtype == RWKV_F32) return launch_fwd_tc<__nv_bfloat16, float>(p, st);
+            if (p.w_dtype == RWKV_BF16) return tc::run<__nv_bfloat16, __nv_bfloat16>(p, nseg, ws, st);
+            if (p.w_dtype == RWKV_F32) return tc::run<__nv_bfloat16, float>(p, nseg, ws, st);
             return RWKV_ERR_DTYPE;
         default:
             return RWKV_ERR_DTYPE;
@@ -552,6 +768,15 @@ int read_device_error_tc(int clear) {
         if (e != cudaSuccess) return -set_cuda_error(e);
     }
     return v;
+}
+
+int set_force_wait_timeout_tc(int on) {
+    const int v = on ? 1 : 0;
+    return set_cuda_error(cudaMemcpyToSymbol(c_force_wait_timeout, &v, sizeof(int)));
+}
+
+int set_device_error_tc(int value) {
+    return set_cuda_error(cudaMemcpyToSymbol(g_device_error_tc, &value, sizeof(int)));
 }
 
 }  // namespace rwkv

@@ -70,18 +70,21 @@ def _fwd(r, w, k, v, a, b, head_size=64, s0=None, want_ckpt=True, want_sa=False,
         if s0.numel() != B * H * 64 * 64:
             raise ValueError("s0 must be (B, H, 64, 64)")
     L = nat.lib()
+    # segments of the sequence run in parallel when B*H leaves SMs idle (workspace > 0)
+    ws_bytes = L.rwkv_wkv7_forward_workspace_size(B, T, H, 64, nat.dtype_code(r))
+    ws = torch.empty((ws_bytes + 3) // 4, device=dev, dtype=torch.float32) if ws_bytes else None
     ev = _timing_events(dev)
     with torch.cuda.device(dev):
         if ev:
             ev[0].record()
-        rc = L.rwkv_wkv7_forward(
+        rc = L.rwkv_wkv7_forward_ws(
             nat.ptr(r), nat.ptr(w), nat.ptr(k), nat.ptr(v), nat.ptr(a), nat.ptr(b), nat.ptr(s0),
             nat.ptr(y), nat.ptr(sT), nat.ptr(ckpt) if (ckpt is not None and ckpt.numel()) else None,
             nat.ptr(sa), B, T, H, 64, nat.dtype_code(r), nat.dtype_code(w), ckpt_len,
-            nat.stream_ptr(dev))
+            nat.ptr(ws), ws_bytes, nat.stream_ptr(dev))
         if ev:
             ev[1].record()
-    nat.check(rc, "rwkv_wkv7_forward")
+    nat.check(rc, "rwkv_wkv7_forward_ws", kernels=3 if ws_bytes else 1)
     return y, ckpt, sa, sT
 
 

@@ -1,12 +1,17 @@
 #!/usr/bin/env python
 """Benchmark: RWKV-v7 L12 D768 GPT-mode prefill tok/s on B200 (one process per GPU).
 
-Default workload (the one BASELINE.json's metric is quoted on): a randomly
+Default workload (the one BASELINE.json's metric is quoted on, configs[1]): a randomly
 initialised L12 D768 model (12 heads x 64, ChannelMix hidden 3072, vocab 65568;
 fp16 weights with fp32 decay bias w0, orthogonal init as rwkv_mlx/train.py:209-310),
-prefill of B=8 sequences x T=4096 uniform-random tokens per GPU.  Each rank runs
-its own batch (data-parallel replicas, no collective on the data path); `value`
-is the tokens all ranks processed per second (weak scaling).
+prefill of a global batch of B=8 sequences x T=4096 uniform-random tokens, split
+over the GPUs by sequence (8/4/2/1 per GPU at 1/2/4/8 GPUs; strong scaling, no
+collective on the data path).  `value` is the tokens of all ranks per second over the
+max-over-ranks step time.  The same JSON line carries `secondary` measurements taken
+in the same run: the weak-scaled prefill (B=8 per GPU), the WKV-7 forward and
+backward kernels at B=8 T=4096 H=12 with their HBM roofline fractions, the LoRA-MoE
+ChannelMix layer of configs[3] (and its expert-parallel form over NCCL at N>1), and
+the batched decode of configs[2].
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload prefill|wkv_fwd|wkv_bwd|decode|moe|moe_full|head_loss]
@@ -75,6 +80,16 @@ def max_over_ranks(x: float, ws: int) -> float:
 
     t = torch.tensor([x], device="cuda", dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(x: float, ws: int) -> float:
+    if ws == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([float(x)], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t)
     return float(t.item())
 
 
@@ -167,7 +182,13 @@ def wkv_algo_bytes(B, T, H, act_bytes, w_bytes):
 
 
 def cpu_prefill_sample(cfg_kw, tokens_T, steps, seed=0):
-    """CPU restatement of the reference forward (oracle) on a bounded sample."""
+    """The reference path on the host cores, on a bounded sample (B=1, T=tokens_T): the
+    reference's own WKV-7 Metal kernel body compiled for the CPU (oracle/_ref, built from
+    the reference's sources by oracle/build_ref.py; 64 host threads per threadgroup with
+    real barriers, as mx.fast.metal_kernel launches it) inside the CPU restatement of the
+    model shell (oracle/model_oracle.py).  Where oracle/_ref was not built, the C
+    restatement of that kernel (oracle/wkv7_metal_port.c, OpenMP) stands in."""
+    from oracle import cpu_wkv7
     from oracle import model_oracle as mo
     from rwkv_mlx_b200.model import RWKV, RWKVConfig, init_weights
 
@@ -181,27 +202,48 @@ def cpu_prefill_sample(cfg_kw, tokens_T, steps, seed=0):
     del m
     g = torch.Generator().manual_seed(seed)
     idx = torch.randint(0, 65536, (1, tokens_T), generator=g)
-    with torch.no_grad():
-        mo.forward(sd, cfg, idx)  # warm-up
-        times = []
-        for _ in range(steps):
-            t0 = time.perf_counter()
-            mo.forward(sd, cfg, idx)
-            times.append(time.perf_counter() - t0)
-    per = statistics.median(times)
-    return {"value": tokens_T / per, "unit": "tok/s", "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"L12 D768 GPT-mode forward, fp32, B=1 T={tokens_T}, median of {steps} steps "
-                      f"(oracle/model_oracle.py + oracle/wkv7_metal_port.c, OpenMP)"}
+
+    def timed(mode, n):
+        with torch.no_grad():
+            mo.forward(sd, cfg, idx, wkv=mode)  # warm-up
+            times = []
+            for _ in range(n):
+                t0 = time.perf_counter()
+                mo.forward(sd, cfg, idx, wkv=mode)
+                times.append(time.perf_counter() - t0)
+        return tokens_T / statistics.median(times)
+
+    ref = cpu_wkv7.ref_available()
+    value = timed("ref" if ref else "port", steps)
+    port = timed("port", steps) if ref else value
+    kernel = ("the reference's own WKV-7 Metal kernel body compiled for the CPU (oracle/_ref)" if ref else
+              "oracle/wkv7_metal_port.c (C restatement of the reference kernel, OpenMP)")
+    return {"value": value, "unit": "tok/s", "cores": torch.get_num_threads(), "kind": "reference" if ref else "port",
+            "sample": f"L12 D768 GPT-mode forward, fp32, B=1 T={tokens_T}, median of {steps} steps; WKV-7: "
+                      f"{kernel}; model shell: oracle/model_oracle.py (torch CPU)",
+            "port_value": port,
+            "port_note": "the same sample with the WKV-7 recurrence in the OpenMP C restatement of the reference "
+                         "kernel (the emulated Metal launch pays for host-thread barriers at every step)"}
 
 
 # ---------------------------------------------------------------------------
 # workloads
 # ---------------------------------------------------------------------------
-def run_prefill(args, ws, rank, dev):
-    from rwkv_mlx_b200 import _native, wkv7
+def split_batch(B_global: int, ws: int, rank: int) -> int:
+    """Sequences of a global batch this rank runs (B=8 split over
+    the GPUs, 8/4/2/1 per GPU at 1/2/4/8 GPUs)."""
+    return B_global // ws + (1 if rank < B_global % ws else 0)
 
-    B, T = args.batch, args.seq
-    cfg, model = build_model(dev, CFG_L12, seed=0)
+
+def run_prefill(args, ws, rank, dev, B, model=None, strong=True, with_e2e=True):
+    """GPT-mode prefill of B sequences x T tokens on this rank; `value` = tokens of all
+    ranks / max-over-ranks time."""
+    from rwkv_mlx_b200 import _native, check_device_error, wkv7
+
+    T = args.seq
+    if model is None:
+        cfg, model = build_model(dev, CFG_L12, seed=0)
+    cfg = model.config
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
     idx = torch.randint(0, 65536, (B, T), device=dev, generator=g)
     host_idx = idx.cpu().pin_memory()
@@ -228,51 +270,63 @@ def run_prefill(args, ws, rank, dev):
     launches = _native.launch_count - launches0
     kt = [a.elapsed_time(b) for a, b in wkv7.fwd_timings]
     wkv7.fwd_timings = None
+    check_device_error()
     ms_max = max_over_ranks(ms, ws)
-    tokens = B * T * ws
-    value = tokens / (ms_max / 1e3)
+    tok_all = sum_over_ranks(B * T, ws)
+    value = tok_all / (ms_max / 1e3)
 
-    # ---- end-to-end through the public API, host buffers ----
-    dev_idx = torch.empty_like(idx)
+    e2e = None
+    if with_e2e:
+        # ---- end-to-end through the public API, host buffers ----
+        dev_idx = torch.empty_like(idx)
 
-    def e2e_step():
-        dev_idx.copy_(host_idx, non_blocking=True)
-        with torch.no_grad():
-            logits, _ = model(dev_idx)
-        host_out.copy_(logits[:, -1], non_blocking=True)
+        def e2e_step():
+            dev_idx.copy_(host_idx, non_blocking=True)
+            with torch.no_grad():
+                logits, _ = model(dev_idx)
+            host_out.copy_(logits[:, -1], non_blocking=True)
 
-    e2e_step()
-    torch.cuda.synchronize()
-    barrier(ws)
-    t0 = time.perf_counter()
-    e2e_ms = cuda_timed(e2e_step, args.steps)
-    wall_ms = (time.perf_counter() - t0) * 1e3 / args.steps
-    e2e_ms = max_over_ranks(max(e2e_ms, wall_ms), ws)
+        e2e_step()
+        torch.cuda.synchronize()
+        barrier(ws)
+        t0 = time.perf_counter()
+        e2e_ms = cuda_timed(e2e_step, args.steps)
+        wall_ms = (time.perf_counter() - t0) * 1e3 / args.steps
+        e2e_ms = max_over_ranks(max(e2e_ms, wall_ms), ws)
+        e2e = {"value": tok_all / (e2e_ms / 1e3), "unit": "tok/s", "h2d_bytes_per_step": B * T * 8,
+               "d2h_bytes_per_step": B * cfg.vocab_size * 2,
+               "path": "RWKV.forward via the public API; tokens H2D from pinned host, last-position logits D2H"}
 
     hbm, _, src = peaks()
     H = cfg.n_head
     bytes_launch = wkv_algo_bytes(B, T, H, 2, 4)
     k_ms = statistics.mean(kt) if kt else float("nan")
+    k_ms = max_over_ranks(k_ms, ws)
     achieved = bytes_launch / (k_ms / 1e3) / 1e9
+    B_global = sum_over_ranks(B, ws)
     line = {
         "metric": "prefill tok/s (L12 D768)", "value": value, "unit": "tok/s", "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "fp16 (fp32 WKV state)",
+        "scaling": "strong" if strong else "weak", "vs_baseline": None, "dtype": "fp16 (fp32 WKV state)",
         "data": "synthetic: random-init weights, uniform-random tokens",
-        "config": {"workload": "L12 D768 GPT-mode prefill (BASELINE configs[1])", "model": "RWKV-v7 L12 D768",
-                   "global_batch": B * ws, "batch_per_gpu": B, "seq_len": T, "parallelism": f"dp{ws}",
-                   "l2": "per-step working set (4.3 GB logits, 0.37 GB weights) far larger than L2"},
-        "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": "tok/s", "h2d_bytes_per_step": B * T * 8,
-                "d2h_bytes_per_step": B * cfg.vocab_size * 2,
-                "path": "RWKV.forward via the public API; tokens H2D from pinned host, last-position logits D2H"},
+        "config": {"workload": "L12 D768 GPT-mode prefill (BASELINE configs[1])" if strong else
+                   "L12 D768 GPT-mode prefill, B=8 per GPU (weak scaling)",
+                   "model": "RWKV-v7 L12 D768", "global_batch": B_global, "batch_per_gpu": B, "seq_len": T,
+                   "parallelism": f"dp{ws} (batch split, no collective on the data path)",
+                   "l2": "per-step working set (4.3 GB logits at B=8, 0.37 GB weights) far larger than L2"},
         "gpu_launches": launches,
-        "roofline": {"kernel": "wkv7_fwd (rwkv_wkv7_forward)", "bound": "hbm", "achieved": achieved,
-                     "peak": hbm, "unit": "GB/s", "frac": achieved / hbm, "traffic": traffic_for("wkv7_fwd", B, T, H),
+        "roofline": {"kernel": "wkv7_fwd (rwkv_wkv7_forward_ws: tcgen05 forward, plus transition + scan "
+                               "launches when the sequence is segmented)",
+                     "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "traffic": traffic_for("wkv7_fwd", B, T, H),
                      "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else "fallback 6650 GB/s",
-                     "algorithmic_bytes_per_launch": bytes_launch, "launch_ms": k_ms, "launches_timed": len(kt)},
+                     "algorithmic_bytes_per_launch": bytes_launch, "launch_ms": k_ms, "launches_timed": len(kt),
+                     "wkv_share_of_step": (k_ms * len(kt) / args.steps) / ms_max if kt else None},
         "clocks": clocks,
     }
-    return line
+    if e2e is not None:
+        line["e2e"] = e2e
+    return line, model
 
 
 def traffic_for(kernel, B, T, H):
@@ -286,11 +340,11 @@ def traffic_for(kernel, B, T, H):
     return d["bytes_per_unit"] * B * T * H
 
 
-def run_wkv(args, ws, rank, dev, backward=False):
-    """WKV-7 op alone at config-2 scale (B=8, T=4096, H=12, fp16 + fp32 w)."""
-    from rwkv_mlx_b200 import wkv7
+def run_wkv(args, ws, rank, dev, backward=False, B=None):
+    """WKV-7 op alone at config-2 scale (B=8, T=4096, H=12 per GPU, fp16 + fp32 w)."""
+    from rwkv_mlx_b200 import check_device_error, wkv7
 
-    B, T, H = args.batch, args.seq, 12
+    B, T, H = (args.batch if B is None else B), args.seq, 12
     C = H * 64
     g = torch.Generator(device=dev).manual_seed(rank)
     mk = lambda: torch.randn(B, T, C, device=dev, generator=g).half()
@@ -314,6 +368,7 @@ def run_wkv(args, ws, rank, dev, backward=False):
     clk = ClockSampler(dev)
     ms = cuda_timed(fn, args.steps)
     clocks = clk.stop()
+    check_device_error()
     ms = max_over_ranks(ms, ws)
     hbm, _, src = peaks()
     gbs = nbytes / (ms / 1e3) / 1e9
@@ -327,7 +382,7 @@ def run_wkv(args, ws, rank, dev, backward=False):
             "clocks": clocks}
 
 
-def run_moe(args, ws, rank, dev):
+def run_moe(args, ws, rank, dev, ep=None):
     """One LoRA-MoE ChannelMix layer: D=768, hidden 3072, E=8,
     r=16, top-2, 65536 tokens per GPU, per-expert logit bias N(0, 1.5); each rank
     routes its own tokens over a replica of the experts (no collective)."""
@@ -335,7 +390,7 @@ def run_moe(args, ws, rank, dev):
     from rwkv_mlx_b200.model import RWKV_CMix_x070, RWKVConfig
     from rwkv_mlx_b200.moe import LoRAMoE_CMix
 
-    ep = args.ep and ws > 1
+    ep = (args.ep if ep is None else ep) and ws > 1
     ntok, C = args.moe_tokens, 768
     g = torch.Generator(device=dev).manual_seed(7 + rank)
     cfg = RWKVConfig(n_embd=C, dim_ffn=3072)
@@ -516,13 +571,14 @@ def run_head_loss(args, ws, rank, dev):
             "clocks": clocks}
 
 
-def run_decode(args, ws, rank, dev):
+def run_decode(args, ws, rank, dev, model=None):
     """Batched RNN-mode decode: L12 D768, 256 sequences per GPU whose
     state comes from a 512-token GPT-mode prefill, greedy steps; tok/s over all ranks."""
     from rwkv_mlx_b200 import _native
 
     Bs, P = args.decode_seqs, args.decode_prompt
-    cfg, model = build_model(dev, CFG_L12, seed=0)
+    if model is None:
+        cfg, model = build_model(dev, CFG_L12, seed=0)
     l0_build = None
     g = torch.Generator(device=dev).manual_seed(99 + rank)
     prompt = torch.randint(0, 65536, (Bs, P), device=dev, generator=g)
@@ -561,7 +617,8 @@ def run_decode(args, ws, rank, dev):
 
 
 def run_reference(args):
-    """CPU restatement of the reference path, rank 0 only."""
+    """The reference path on the host cores (see cpu_prefill_sample), rank 0 only; the
+    other ranks of a multi-GPU launch exit without work."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return None
@@ -573,7 +630,36 @@ def run_reference(args):
             "config": {"workload": "L12 D768 GPT-mode prefill (BASELINE configs[1]), bounded CPU sample"},
             "cpu_baseline": res,
             "e2e": {"value": res["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-            "note": "reference is MLX/Metal (not installable here); this is its CPU restatement"}
+            "note": "the reference is MLX/Metal (MLX is not installable offline, no Apple GPU): its own WKV-7 "
+                    "Metal kernel body runs compiled for the host CPU inside a CPU restatement of the model"}
+
+
+def _brief(d):
+    keep = ("metric", "value", "unit", "ms_per_step", "scaling", "n_gpus", "config", "roofline", "gpu_launches",
+            "e2e", "clocks")
+    return {k: d[k] for k in keep if k in d}
+
+
+def secondary_lines(args, ws, rank, dev, model, primary):
+    """Per-GPU workloads measured in the same run as the headline, each timed on its own
+    with CUDA events (max over ranks) and reported with its own roofline where it has
+    one: the weak-scaled prefill (B=8 per GPU), the WKV-7 forward and backward at
+    B=8 T=4096 H=12, the LoRA-MoE ChannelMix layer of BASELINE configs[3] (replicated
+    experts, and expert-parallel over NCCL all-to-all at N>1) and the batched decode of
+    BASELINE configs[2]."""
+    out = {}
+    if ws > 1 or args.weak or primary["config"]["batch_per_gpu"] != 8:
+        out["prefill_weak_b8_per_gpu"] = _brief(run_prefill(args, ws, rank, dev, 8, model=model, strong=False,
+                                                            with_e2e=False)[0])
+    else:
+        out["prefill_weak_b8_per_gpu"] = "same as the headline at this GPU count (B=8 on one GPU)"
+    out["wkv7_fwd_b8_t4096_h12"] = _brief(run_wkv(args, ws, rank, dev, backward=False, B=8))
+    out["wkv7_bwd_b8_t4096_h12"] = _brief(run_wkv(args, ws, rank, dev, backward=True, B=8))
+    out["lora_moe_cmix_config3"] = _brief(run_moe(args, ws, rank, dev, ep=False))
+    if ws > 1:
+        out["lora_moe_cmix_config3_ep"] = _brief(run_moe(args, ws, rank, dev, ep=True))
+    out["decode_config2"] = _brief(run_decode(args, ws, rank, dev, model=model))
+    return out
 
 
 def main():
@@ -595,6 +681,11 @@ def main():
     ap.add_argument("--seq", type=int, default=4096)
     ap.add_argument("--cpu-sample-tokens", type=int, default=128)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--weak", action="store_true",
+                    help="prefill: --batch sequences per GPU instead of a global batch split over the GPUs")
+    ap.add_argument("--no-secondary", action="store_true",
+                    help="prefill: skip the secondary measurements (weak-scaled prefill, WKV-7 forward and "
+                         "backward, LoRA-MoE layer, expert-parallel MoE at N>1, decode)")
     args = ap.parse_args()
 
     if args.impl == "reference":
@@ -611,7 +702,10 @@ def main():
 
         _native.check(_native.lib().rwkv_set_wkv_impl(args.wkv_impl), "rwkv_set_wkv_impl")
     if args.workload == "prefill":
-        line = run_prefill(args, ws, rank, dev)
+        B = args.batch if args.weak else split_batch(args.batch, ws, rank)
+        line, model = run_prefill(args, ws, rank, dev, B, strong=not args.weak)
+        if not args.no_secondary:
+            line["secondary"] = secondary_lines(args, ws, rank, dev, model, line)
     elif args.workload == "moe":
         line = run_moe(args, ws, rank, dev)
     elif args.workload == "moe_full":

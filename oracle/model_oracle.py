@@ -12,7 +12,8 @@ may use this.  It restates rwkv_mlx/model.py with torch CPU tensors:
 
 Weights are a dict keyed by the reference's parameter names (e.g.
 ``blocks.3.att.w1``, ``blocks.3.ffn.key.weight``).  The WKV-7 recurrence is the C
-restatement of the reference Metal kernel (``oracle/wkv7_metal_port.c``, fp32) or
+restatement of the reference Metal kernel (``oracle/wkv7_metal_port.c``, fp32), the
+reference's own kernel body compiled for the CPU (``wkv="ref"``, ``oracle/_ref``) or
 the float64 oracle (``wkv="exact"``).  ``ln_x`` uses MLX's GroupNorm grouping
 (channels c = g mod H form group g) unless ``groupnorm="per_head"``.
 """
@@ -58,6 +59,8 @@ def _wkv(r, w, k, v, a, b, H, mode):
     args = [t.reshape(sh).numpy() for t in (r, w, k, v, a, b)]
     if mode == "exact":
         y = wkv7_oracle.wkv7_forward_exact(*args)[0]
+    elif mode == "ref":  # the reference's own Metal kernel body, compiled for the CPU
+        y = cpu_wkv7.ref_forward(*[x.astype(np.float32) for x in args])[0]
     else:
         y = cpu_wkv7.port_forward(*args, want_states=False)[0]
     return torch.from_numpy(np.ascontiguousarray(y)).to(r.dtype).reshape(B, T, C)
@@ -121,8 +124,9 @@ def _is_moe(cfg, i):
     return cfg.moe_num_experts > 0 and (not cfg.moe_layers or i in cfg.moe_layers)
 
 
-def forward(p, cfg, idx, wkv="port", dtype=torch.float32):
-    """GPT-mode forward: idx (B, T) int -> (logits (B, T, V), aux_loss float)."""
+def forward(p, cfg, idx, wkv="port", dtype=torch.float32, positions=None):
+    """GPT-mode forward: idx (B, T) int -> (logits (B, T, V), aux_loss float).
+    ``positions`` (optional index list): logits only at those positions (B, P, V)."""
     p = {k: v.to(dtype) for k, v in p.items()}
     H, N = cfg.n_head, cfg.head_size
     gn = getattr(cfg, "groupnorm", "mlx")
@@ -143,6 +147,8 @@ def forward(p, cfg, idx, wkv="port", dtype=torch.float32):
             x = x + out
         else:
             x = x + _cmix(p, pre + "ffn.", x2)
+    if positions is not None:
+        x = x[:, torch.as_tensor(positions)]
     x = _ln(x, p["ln_out.weight"], p["ln_out.bias"])
     return _lin(x, p["head.weight"]), aux_total
 

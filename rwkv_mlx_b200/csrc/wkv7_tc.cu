@@ -663,31 +663,42 @@ __global__ void __launch_bounds__(NT, 1) wkv7_fwd_tc_kernel(const TcArgs p) {
 
 // Composes the segments' affine maps: S_1 = C_0 (segment 0 started from the sequence's
 // own initial state), S_{s+1} = S_s M_s + C_s.  Rows of the state are independent, so
-// each CTA owns 8 rows of one (b, h); fp32 FMA.
+// each CTA owns 8 rows of one (b, h); fp32 FMA.  The next segment's M (16 KB) and C rows
+// are prefetched with cp.async while the current step computes, so a step costs its
+// arithmetic, not a global-memory round trip.
 __global__ void __launch_bounds__(256) wkv7_seg_scan_kernel(const float* __restrict__ trans,
                                                             float* __restrict__ seg_s0, int nseg) {
-    __shared__ float M[N][N + 1];
+    __shared__ __align__(16) float M[2][N][N];
+    __shared__ __align__(16) float Cr[2][8][N];
     __shared__ float S[8][N];
     const int bh = blockIdx.x, r0 = 8 * blockIdx.y, tid = threadIdx.x;
     const int i = tid >> 5, c0 = tid & 31, c1 = c0 + 32;
     const size_t cm = (size_t)ROWS_CM * N;
     const float* CM0 = trans + (size_t)bh * (nseg - 1) * cm;
+    auto fetch = [&](int s, int buf) {  // M rows (16 KB) and this CTA's 8 C rows of segment s
+        const float* CM = CM0 + (size_t)s * cm;
+        for (int q = tid; q < N * N / 4; q += 256) cp_async16(&M[buf][0][0] + 4 * q, CM + (size_t)N * N + 4 * q, true);
+        if (tid < 8 * N / 4) cp_async16(&Cr[buf][0][0] + 4 * tid, CM + (size_t)r0 * N + 4 * tid, true);
+        cp_commit();
+    };
     float s0v = CM0[(size_t)(r0 + i) * N + c0], s1v = CM0[(size_t)(r0 + i) * N + c1];
+    if (nseg > 2) fetch(1, 1);
     float* out = seg_s0 + (((size_t)bh * nseg + 1) * N + r0 + i) * N;
     out[c0] = s0v, out[c1] = s1v;
     S[i][c0] = s0v, S[i][c1] = s1v;
     for (int s = 1; s < nseg - 1; s++) {
-        const float* CM = CM0 + (size_t)s * cm;
-        for (int q = tid; q < N * N; q += 256) M[q >> 6][q & 63] = CM[(size_t)N * N + q];
-        __syncthreads();
-        float a0 = CM[(size_t)(r0 + i) * N + c0], a1 = CM[(size_t)(r0 + i) * N + c1];
+        const int buf = s & 1;
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        __syncthreads();  // M[buf], Cr[buf] and S are complete
+        if (s + 1 < nseg - 1) fetch(s + 1, buf ^ 1);
+        float a0 = Cr[buf][i][c0], a1 = Cr[buf][i][c1];
 #pragma unroll 16
         for (int j = 0; j < N; j++) {
             const float sj = S[i][j];
-            a0 = fmaf(sj, M[j][c0], a0);
-            a1 = fmaf(sj, M[j][c1], a1);
+            a0 = fmaf(sj, M[buf][j][c0], a0);
+            a1 = fmaf(sj, M[buf][j][c1], a1);
         }
-        __syncthreads();
+        __syncthreads();  // every thread has read S
         S[i][c0] = a0, S[i][c1] = a1;
         out = seg_s0 + (((size_t)bh * nseg + s + 1) * N + r0 + i) * N;
         out[c0] = a0, out[c1] = a1;

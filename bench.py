@@ -14,7 +14,7 @@ ChannelMix layer of configs[3] (and its expert-parallel form over NCCL at N>1), 
 the batched decode of configs[2].
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload prefill|wkv_fwd|wkv_bwd|decode|moe|moe_full|head_loss]
+                    [--workload prefill|wkv_fwd|wkv_bwd|decode|moe|moe_full|head_loss|config5]
 
 Multi-GPU: launched by torch.distributed.run (RANK/LOCAL_RANK/WORLD_SIZE from the
 environment).  `--impl reference` times the CPU restatement of the reference
@@ -616,6 +616,98 @@ def run_decode(args, ws, rank, dev, model=None):
             "gpu_launches": launches, "clocks": clocks}
 
 
+def run_config5(args, ws, rank, dev):
+    """L24 D1024 RWKV-v7 (16 heads x 64, vocab 65568, ChannelMix
+    hidden 3584 = the reference's default for C=1024, model.py:46-47) with LoRA-MoE (E=8,
+    top-2, rank 16; adapters and gate ~ N(0, 0.02)) in every ChannelMix, fp16 weights,
+    fp32 state.  One step = GPT-mode prefill of a global B=32 x T=4096 (split over the
+    ranks by sequence) + a WKV-7 forward/backward micro-batch of B=4 x T=1024 x H=16
+    (its 64 (b, h) units split over the ranks, by sequence then by head).  At N>1 every
+    LoRA-MoE layer is expert-parallel (experts e on rank e // (8 / N), NCCL all-to-all)."""
+    from rwkv_mlx_b200 import _native, check_device_error, wkv7
+
+    T, C, H = args.seq, 1024, 16
+    B = split_batch(32, ws, rank)
+    cfg_kw = dict(n_layer=24, n_embd=C, vocab_size=65568, moe_num_experts=8, moe_top_k=2, moe_lora_rank=16)
+    cfg, model = build_model(dev, cfg_kw, seed=0)
+    gw = torch.Generator(device=dev).manual_seed(17)  # identical adapters on every rank
+    with torch.no_grad():
+        for i, blk in enumerate(model.blocks):
+            f = blk.ffn
+            A = (torch.randn(8, C, 16, device=dev, generator=gw) * 0.02).to(f.lora_A.dtype)
+            Bw = (torch.randn(8, 16, C, device=dev, generator=gw) * 0.02).to(f.lora_B.dtype)
+            f.router.gate.weight.copy_(torch.randn(8, C, device=dev, generator=gw) * 0.02)
+            if ws > 1:
+                from rwkv_mlx_b200.ep import ExpertParallelLoRAMoE
+
+                with torch.device(dev):
+                    e = ExpertParallelLoRAMoE(f.base, 8, 16, 2)
+                e.load_experts(A.float(), Bw.float())
+                e.router.gate.weight.copy_(f.router.gate.weight.float())
+                e.lora_A.data = e.lora_A.data.to(torch.float16)
+                e.lora_B.data = e.lora_B.data.to(torch.float16)
+                e.router.gate.weight.data = e.router.gate.weight.data.to(torch.float16)
+                blk.ffn = e
+            else:
+                f.lora_A.copy_(A)
+                f.lora_B.copy_(Bw)
+    for p_ in model.parameters():
+        p_.requires_grad_(False)
+    g = torch.Generator(device=dev).manual_seed(4321 + rank)
+    idx = torch.randint(0, 65536, (B, T), device=dev, generator=g)
+    # WKV-7 backward micro-batch: 4 x 16 = 64 (b, h) units over the ranks
+    units = 64 // ws
+    mb_B = max(1, 4 // ws)
+    mb_H = units // mb_B
+    Tm = 1024
+    mk = lambda: torch.randn(mb_B, Tm, mb_H * 64, device=dev, generator=g).half()
+    r_, k_, v_, dy = mk(), mk(), mk(), mk()
+    w_ = torch.empty(mb_B, Tm, mb_H * 64, device=dev).uniform_(-6, -0.5, generator=g)
+    kk = torch.nn.functional.normalize(torch.randn(mb_B, Tm, mb_H, 64, device=dev, generator=g), dim=-1)
+    a_ = (-kk).reshape(mb_B, Tm, -1).half()
+    b_ = (kk.reshape(mb_B, Tm, -1) * torch.sigmoid(torch.randn(mb_B, Tm, mb_H * 64, device=dev, generator=g))).half()
+
+    def micro_bwd():
+        _, ck, _, _ = wkv7._fwd(r_, w_, k_, v_, a_, b_, want_ckpt=True)
+        return wkv7._bwd(r_, w_, k_, v_, a_, b_, dy, ck)
+
+    def step():
+        with torch.no_grad():
+            logits, aux = model(idx)
+        micro_bwd()
+        return logits
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    l0 = _native.launch_count
+    barrier(ws)
+    clk = ClockSampler(dev)
+    ms = cuda_timed(step, args.steps)
+    clocks = clk.stop()
+    barrier(ws)
+    launches = _native.launch_count - l0
+    check_device_error()
+    ms_max = max_over_ranks(ms, ws)
+    mb_ms = max_over_ranks(cuda_timed(micro_bwd, args.steps), ws)
+    tok_all = sum_over_ranks(B * T, ws)
+    hbm, _, src = peaks()
+    bwd_bytes = mb_B * Tm * mb_H * 64 * (12 * 2 + 4)
+    return {"metric": "configs[4] step: L24 D1024 LoRA-MoE prefill tok/s (+ WKV-7 bwd micro-batch)",
+            "value": tok_all / (ms_max / 1e3), "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "fp16 (fp32 WKV state, fp32 router)", "data": "synthetic",
+            "config": {"workload": "BASELINE configs[4]", "model": "RWKV-v7 L24 D1024, LoRA-MoE E8 r16 top2 in every "
+                       "ChannelMix", "global_batch": 32, "batch_per_gpu": B, "seq_len": T,
+                       "bwd_micro_batch": {"global": "B=4 T=1024 H=16", "per_gpu": f"B={mb_B} H={mb_H}"},
+                       "parallelism": f"dp{ws} + ep{ws} (NCCL all-to-all)" if ws > 1 else "1 GPU"},
+            "gpu_launches": launches,
+            "wkv7_bwd_micro_batch": {"ms": mb_ms, "achieved_gbs": bwd_bytes / (mb_ms / 1e3) / 1e9,
+                                     "frac": bwd_bytes / (mb_ms / 1e3) / 1e9 / hbm,
+                                     "note": "forward with snapshots + exact chunked backward"},
+            "clocks": clocks}
+
+
 def run_reference(args):
     """The reference path on the host cores (see cpu_prefill_sample), rank 0 only; the
     other ranks of a multi-GPU launch exit without work."""
@@ -669,7 +761,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="prefill",
-                    choices=["prefill", "wkv_fwd", "wkv_bwd", "moe", "moe_full", "head_loss", "decode"])
+                    choices=["prefill", "wkv_fwd", "wkv_bwd", "moe", "moe_full", "head_loss", "decode",
+                             "config5"])
     ap.add_argument("--moe-tokens", type=int, default=65536)
     ap.add_argument("--ep", action="store_true", help="moe workload: expert-parallel over the ranks")
     ap.add_argument("--decode-seqs", type=int, default=256)
@@ -714,6 +807,8 @@ def main():
         line = run_head_loss(args, ws, rank, dev)
     elif args.workload == "decode":
         line = run_decode(args, ws, rank, dev)
+    elif args.workload == "config5":
+        line = run_config5(args, ws, rank, dev)
     else:
         line = run_wkv(args, ws, rank, dev, backward=args.workload == "wkv_bwd")
     if rank == 0 and ws == 1 and not args.no_cpu_baseline and args.workload == "prefill":

@@ -433,15 +433,20 @@ def run_moe(args, ws, rank, dev, ep=None):
     clocks = clk.stop()
     launches = _native.launch_count - l0
     ms = max_over_ranks(ms, ws)
-    # MoE-path kernels alone (router + fused adapter apply, the module's path) on the same tokens
-    from rwkv_mlx_b200.moe import lora_apply, router_forward
+    # MoE-path kernels alone (the module's path: the router folded into the fused adapter
+    # apply for fp16, else router + apply) on the same tokens
+    from rwkv_mlx_b200.moe import lora_apply, lora_apply_routed, lora_apply_routed_supported, router_forward
 
     x2 = x.view(ntok, C)
     with torch.no_grad():
         base_out = base(x).view(ntok, C)
     Ah, Bh = A.half(), Bw.half()
+    routed = lora_apply_routed_supported(C, 16, 8, 2, x2.dtype)
 
     def moe_only():
+        if routed:
+            return lora_apply_routed(x2, base_out, Ah, Bh, layer.router.gate.weight, 2, layer.router.bias,
+                                     out=base_out)[0]
         r = router_forward(x2, layer.router.gate.weight, 2, layer.router.bias)
         return lora_apply(x2, base_out, Ah, Bh, r["inds"], r["scores"], out=base_out)  # as the module does
 
@@ -459,8 +464,11 @@ def run_moe(args, ws, rank, dev, ep=None):
                        "parallelism": f"ep{ws} (NCCL all-to-all)" if ep else f"dp{ws} (experts replicated)",
                        "l2": "x and outputs (3 x 100 MB) larger than L2"},
             "gpu_launches": launches,
-            "roofline": {"kernel": "MoE path (router + fused lora_apply)", "bound": "hbm", "achieved": gbs,
-                         "peak": hbm, "unit": "GB/s", "frac": gbs / hbm, "traffic": traffic_for("moe_path", ntok, 1, 1),
+            "roofline": {"kernel": "MoE path (rwkv_moe_lora_apply_routed: router folded into the fused apply, + "
+                                   "gate split and finalize)" if routed else "MoE path (router + fused lora_apply)",
+                         "bound": "hbm", "achieved": gbs,
+                         "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                         "traffic": traffic_for("moe_path_routed" if routed else "moe_path", ntok, 1, 1),
                          "launch_ms": moe_ms,
                          "algorithmic_bytes": algo, "peak_source": src},
             "clocks": clocks}

@@ -235,6 +235,27 @@ int rwkv_moe_lora_apply(const void* x, const void* base, const void* A, const vo
  * testing one against the other. */
 int rwkv_moe_set_apply_impl(int impl);
 
+/* LoRA-MoE ChannelMix delta with the router folded in (fp16): one pass over x
+ * forms the router logits (moe.py:56, x @ W^T with W split into two fp16 terms
+ * whose products are exact in fp32, + bias), the top-k routing and scores
+ * (moe.py:66-70, ties to the lower expert id, scores in fp16), the aux / z
+ * statistics (moe.py:61-84, via the router's fixed-order finalize) and
+ *   out = base + sum_s scores[:, s] * (x @ A[e_s]) @ B[e_s]   (moe.py:142-147).
+ * Replaces Router.__call__ + the expert loop of LoRAMoE_CMix.__call__
+ * (moe.py:51-86, :129-147).  Outputs inds (ntok, topk) int32, scores (ntok,
+ * topk) fp16, stats fp32[2 + E] and counts int32[E] as rwkv_moe_router; out may
+ * equal base.  Needs rwkv_moe_lora_apply_routed_supported (fp16, E <= 16,
+ * E * R in {32, 64, 128}, C % 64 == 0) and a 256-byte aligned workspace of
+ * rwkv_moe_lora_apply_routed_workspace_size(ntok, C, E) bytes.  Routing agrees
+ * with rwkv_moe_router up to near-ties (a different fp32 summation order).  */
+int rwkv_moe_lora_apply_routed_supported(int C, int R, int E, int topk, int dtype);
+size_t rwkv_moe_lora_apply_routed_workspace_size(int ntok, int C, int E);
+int rwkv_moe_lora_apply_routed(const void* x, const void* base, const void* A, const void* B,
+                               const float* gate_w, const float* bias, int32_t* inds, void* scores,
+                               float* stats, int32_t* counts, void* workspace,
+                               size_t workspace_bytes, void* out, int ntok, int C, int R, int E,
+                               int topk, int dtype, void* stream);
+
 /* Expert-parallel dispatch / combine helpers (no counterpart in the reference,
  * which runs on one device; they move the routed rows of moe.py:139-145 between
  * GPUs and back).

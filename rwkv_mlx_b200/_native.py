@@ -58,6 +58,9 @@ SIGNATURES = {
     "rwkv_moe_lora_apply_supported": (_I, [_I] * 5),
     "rwkv_moe_lora_apply": (_I, [_P] * 7 + [_I] * 6 + [_P]),
     "rwkv_moe_set_apply_impl": (_I, [_I]),
+    "rwkv_moe_lora_apply_routed_supported": (_I, [_I] * 5),
+    "rwkv_moe_lora_apply_routed_workspace_size": (_SZ, [_I] * 3),
+    "rwkv_moe_lora_apply_routed": (_I, [_P] * 11 + [_SZ, _P] + [_I] * 6 + [_P]),
     "rwkv_moe_ortho_loss": (_I, [_P] * 2 + [_I] * 4 + [_P]),
     "rwkv_moe_gather_rows": (_I, [_P] * 3 + [_I] * 4 + [_P]),
     "rwkv_moe_lora_up": (_I, [_P] * 5 + [_I] * 5 + [_P]),
@@ -120,7 +123,7 @@ def lib() -> ctypes.CDLL:
 KERNELS_PER_CALL = {
     "rwkv_wkv7_forward": 1, "rwkv_wkv7_backward": 1, "rwkv_wkv7_backward_ws": 2, "rwkv_wkv7_step": 1,
     "rwkv_moe_router": 2, "rwkv_moe_router_noalloc": 2, "rwkv_moe_permute": 3, "rwkv_moe_lora_down": 1,
-    "rwkv_moe_lora_combine": 1, "rwkv_moe_lora_apply": 1, "rwkv_moe_ortho_loss": 1, "rwkv_moe_gather_rows": 1,
+    "rwkv_moe_lora_combine": 1, "rwkv_moe_lora_apply": 1, "rwkv_moe_lora_apply_routed": 3, "rwkv_moe_ortho_loss": 1, "rwkv_moe_gather_rows": 1,
     "rwkv_moe_lora_up": 1, "rwkv_moe_combine_rows": 1, "rwkv_lerp": 1, "rwkv_lerp_prev": 1, "rwkv_lerp_prev_state": 1, "rwkv_tmix_mid": 1,
     "rwkv_tmix_post": 1, "rwkv_relu_sq": 1, "rwkv_lora_act": 1, "rwkv_argmax_rows": 1, "rwkv_add_layernorm": 1, "rwkv_moe_expert_mix_rows": 1,
     "rwkv_ce_chunk": 1, "rwkv_ce_finalize": 1, "rwkv_ce_chunk_grad": 1,

@@ -1191,6 +1191,10 @@ namespace rwkv {
 template <typename T>
 int moe_lora_apply_tc(const void* x, const void* base, const void* A, const void* B, const int32_t* inds,
                       const void* scores, void* out, int ntok, int C, int R, int E, int topk, cudaStream_t st);
+int moe_lora_apply_tc_routed(const void* x, const void* base, const void* A, const void* B, const float* gate_w,
+                             const float* bias, int32_t* inds, void* scores, void* gsplit, float* part_f,
+                             int32_t* part_c, void* out, int ntok, int C, int R, int E, int topk, cudaStream_t st);
+int moe_apply_tc_grid(int ntok);
 static int g_apply_impl = 0;  // 0 automatic (tcgen05), 1 mma.sync, 2 tcgen05
 }  // namespace rwkv
 
@@ -1228,6 +1232,47 @@ extern "C" int rwkv_moe_lora_apply(const void* x, const void* base, const void* 
     clear_error();  // the fallback below succeeds or records its own error
     if (dtype == RWKV_F16) return launch_apply_en<__half>(x, base, A, B, inds, scores, out, ntok, C, R, E, topk, st);
     return launch_apply_en<__nv_bfloat16>(x, base, A, B, inds, scores, out, ntok, C, R, E, topk, st);
+}
+
+// ---------------------------------------------------------------------------
+// Routed apply: router + adapters in one pass over x (fp16).  Workspace: the split gate
+// operand (C / 64 blocks of 4 KB), then the per-CTA routing partials.
+static size_t routed_gate_bytes(int C) { return align_up((size_t)(C / 64) * 4096, 256); }
+
+extern "C" int rwkv_moe_lora_apply_routed_supported(int C, int R, int E, int topk, int dtype) {
+    return g_apply_impl != 1 && dtype == RWKV_F16 && E <= 16 && rwkv_moe_lora_apply_supported(C, R, E, topk, dtype);
+}
+
+extern "C" size_t rwkv_moe_lora_apply_routed_workspace_size(int ntok, int C, int E) {
+    if (ntok <= 0 || C <= 0 || E <= 0) return 0;
+    const size_t nb = (size_t)moe_apply_tc_grid(ntok);
+    return routed_gate_bytes(C) + align_up(nb * (E + 1) * sizeof(float), 256) + align_up(nb * E * sizeof(int32_t), 256);
+}
+
+extern "C" int rwkv_moe_lora_apply_routed(const void* x, const void* base, const void* A, const void* B,
+                                          const float* gate_w, const float* bias, int32_t* inds, void* scores,
+                                          float* stats, int32_t* counts, void* workspace, size_t workspace_bytes,
+                                          void* out, int ntok, int C, int R, int E, int topk, int dtype,
+                                          void* stream) {
+    if (ntok <= 0) return RWKV_ERR_SHAPE;
+    if (dtype != RWKV_F16) return RWKV_ERR_DTYPE;
+    if (!rwkv_moe_lora_apply_routed_supported(C, R, E, topk, dtype)) return RWKV_ERR_SHAPE;
+    if (!x || !A || !B || !gate_w || !inds || !scores || !stats || !out || !workspace) return RWKV_ERR_ARG;
+    if (!aligned(x, 16) || !aligned(A, 16) || !aligned(B, 16) || !aligned(out, 16) || (base && !aligned(base, 16)) ||
+        !aligned(workspace, 256))
+        return RWKV_ERR_ALIGN;
+    if (workspace_bytes < rwkv_moe_lora_apply_routed_workspace_size(ntok, C, E)) return RWKV_ERR_WORKSPACE;
+    const int nb = moe_apply_tc_grid(ntok);
+    unsigned char* ws = (unsigned char*)workspace;
+    float* pf = (float*)(ws + routed_gate_bytes(C));
+    int32_t* pc = (int32_t*)((unsigned char*)pf + align_up((size_t)nb * (E + 1) * sizeof(float), 256));
+    cudaStream_t st = (cudaStream_t)stream;
+    const int rc = moe_lora_apply_tc_routed(x, base, A, B, gate_w, bias, inds, scores, ws, pf, pc, out, ntok, C, R,
+                                            E, topk, st);
+    if (rc == APPLY_TC_NO_MAPS) return RWKV_ERR_CUDA;  // the tensor maps could not be built (message set)
+    if (rc) return rc;
+    launch_finalize(pf, pc, nb, ntok, E, topk, stats, counts, st);
+    return check_launch();
 }
 
 extern "C" int rwkv_moe_ortho_loss(const void* A, float* out, int E, int C, int R, int dtype,

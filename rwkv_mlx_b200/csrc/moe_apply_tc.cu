@@ -52,33 +52,42 @@ constexpr int KS = 64;   // channels per down slice (one 128-byte swizzle row of
 constexpr int NC = 64;   // channels per up chunk
 constexpr int NEPI = 256;       // epilogue warps 0-7: warps w and w + 4 share TMEM lanes 32 (w % 4) ..
 constexpr int NTH = NEPI + 96;  // producer warp 8, MMA warp 9, store warp 10
-constexpr int NA = 10, NW = 4;  // stages of the activation ring (x / base+out) and the adapter ring
+constexpr int NA_MAX = 10, NW = 4;  // stages of the activation ring (x / base+out, <= NA_MAX) and the adapter ring
+constexpr int GATE_COLS = 32;  // routed variant: the gate's two fp16 terms, 16 expert columns each
 constexpr int BAR_EPI = 1;      // named barrier of the epilogue warps
 constexpr int X_BYTES = TM * KS * 2;  // 128 rows x 128 bytes, swizzled
 constexpr int O_BYTES = TM * NC * 2;
 
-template <int EN>
+// RT (routed): the down product also forms the router logits, N = EN + GATE_COLS.
+template <int EN, bool RT = false>
 struct Geo {
-    static constexpr int A_BYTES = KS * EN * 2;  // MN-major: K groups 128 B apart, N groups 1024 B
+    static constexpr int ENX = EN + (RT ? GATE_COLS : 0);  // N of the down product
+    static constexpr int NA = RT ? 9 : 10;                  // activation stages (shared memory)
+    static constexpr int A_BYTES = KS * ENX * 2;  // MN-major: K groups 128 B apart, N groups 1024 B
+    static constexpr int ACAT_BYTES = KS * EN * 2;
     static constexpr int B_BYTES = EN * NC * 2;  // EN rows x 128 bytes, swizzled
     static constexpr int W_STAGE = ((A_BYTES > B_BYTES ? A_BYTES : B_BYTES) + 1023) / 1024 * 1024;
     static constexpr int A_STAGE = X_BYTES;      // = O_BYTES
     static constexpr int CTRL = 1024;
     static constexpr int SMEM = 1024 /* alignment slack */ + CTRL + NA * A_STAGE + NW * W_STAGE;
     // TMEM columns: two D1 accumulators (tiles alternate), two up accumulators, H
-    static constexpr int T_D2 = 2 * EN, T_H = 2 * EN + 2 * NC;
+    static constexpr int T_D2 = 2 * ENX, T_H = 2 * ENX + 2 * NC;
     static_assert(SMEM <= 227 * 1024, "shared memory");
     static_assert(EN % 32 == 0 && T_H + EN / 2 <= 512, "TMEM columns");
+    static_assert(NA <= NA_MAX, "activation ring");
 };
 struct Ctrl {
-    unsigned long long full_a[NA], empty_a[NA];  // activation stages: landed / free
+    unsigned long long full_a[NA_MAX], empty_a[NA_MAX];  // activation stages: landed / free
     unsigned long long full_w[NW], empty_w[NW];  // adapter stages
     unsigned long long d2_full[2], d2_empty[2];  // up-projection accumulators (double buffer)
     unsigned long long d1_full, h_full;          // down-projection done / H written
     unsigned long long out_full[2], out_empty[2];  // out box of an up chunk ready / taken by the store warp
     uint32_t tmem_base;
     int abort;
+    float red_p[4][17];  // routed variant: per-warp expert probability sums (+ z), fixed order
+    int red_c[4][16];    // per-warp expert counts
 };
+static_assert(sizeof(Ctrl) <= 1024, "control block");
 
 // 128-byte-swizzled (layout type 2) shared-memory descriptor
 __device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
@@ -103,6 +112,13 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* m, int
             ck::smem_u32(dst)),
         "l"(reinterpret_cast<uint64_t>(m)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(ck::smem_u32(bar))
         : "memory");
+}
+// untiled bulk copy global -> shared (16-byte aligned, size a multiple of 16)
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, unsigned long long* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     ck::smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(ck::smem_u32(bar))
+                 : "memory");
 }
 // out += box (element-wise add in the memory system, in the tensor map's type)
 __device__ __forceinline__ void tma_add_2d(const CUtensorMap* m, int x, int y, const void* src) {
@@ -148,17 +164,29 @@ __device__ __forceinline__ int up_job_index(int t, int j, int n, int nt) {
 
 }  // namespace atc
 
-template <typename T, int EN>
+// Routing outputs of the routed variant (RT): the gate operand and where the routing goes.
+struct RouteArgs {
+    const unsigned char* gsplit;  // gate terms, one 4 KB MN-major block per 64-channel slice
+    const float* bias;            // (E,) added to the logits, or null
+    int E;
+    int32_t* inds;                // (ntok, topk) out
+    void* scores;                 // (ntok, topk) out, activation type
+    float* part_f;                // per CTA: E probability sums, then the sum of lse^2
+    int32_t* part_c;              // per CTA: E counts
+};
+
+template <typename T, int EN, bool RT>
 __global__ void __launch_bounds__(atc::NTH, 1)
     moe_lora_apply_tc_kernel(const __grid_constant__ CUtensorMap mx, const __grid_constant__ CUtensorMap ma,
                              const __grid_constant__ CUtensorMap mb, const __grid_constant__ CUtensorMap mbase,
                              const __grid_constant__ CUtensorMap mout, int has_base, int accum,
                              const int32_t* __restrict__ inds, const T* __restrict__ scores, int ntok, int C,
-                             int R, int topk) {
+                             int R, int topk, const RouteArgs ra) {
     using namespace atc;
-    using G = Geo<EN>;
+    using G = Geo<EN, RT>;
+    constexpr int NA = G::NA;
     constexpr bool BF = std::is_same<T, __nv_bfloat16>::value;
-    constexpr uint32_t IDESC_DOWN = idesc_16(TM, EN, BF, false, true);
+    constexpr uint32_t IDESC_DOWN = idesc_16(TM, G::ENX, BF, false, true);
     constexpr uint32_t IDESC_UP = idesc_16(TM, NC, BF, false, true);
 
     extern __shared__ __align__(1024) unsigned char smem_atc_raw[];
@@ -218,6 +246,9 @@ __global__ void __launch_bounds__(atc::NTH, 1)
                 if (jb.down) {
                     expect_tx(&cs.full_w[sw], G::A_BYTES);
                     tma_load_4d(stw, &ma, 0, blk(jb.t, jb.j) * KS, 0, 0, &cs.full_w[sw]);
+                    if constexpr (RT)  // the gate slice continues the N groups of the Acat slice
+                        bulk_load(stw + G::ACAT_BYTES, ra.gsplit + (size_t)blk(jb.t, jb.j) * (KS * GATE_COLS * 2),
+                                  KS * GATE_COLS * 2, &cs.full_w[sw]);
                     expect_tx(&cs.full_a[sa], X_BYTES);
                     tma_load_2d(sta, &mx, blk(jb.t, jb.j) * KS, t0, &cs.full_a[sa]);
                 } else {
@@ -251,7 +282,7 @@ __global__ void __launch_bounds__(atc::NTH, 1)
                     const uint32_t sta = ck::smem_u32(ring_a + sa * G::A_STAGE);
 #pragma unroll
                     for (int kk = 0; kk < KS / 16; kk++)
-                        umma16(tmem + (jb.t & 1) * EN, desc_sw128(sta + kk * 32, 16, 1024),
+                        umma16(tmem + (jb.t & 1) * G::ENX, desc_sw128(sta + kk * 32, 16, 1024),
                                umma_desc_ls(stw + kk * 256, 128, 1024), IDESC_DOWN, (jb.j > 0 || kk > 0) ? 1u : 0u);
                     umma_commit(&cs.empty_a[sa]);
                     umma_commit(&cs.empty_w[sw]);
@@ -307,25 +338,96 @@ __global__ void __launch_bounds__(atc::NTH, 1)
         const int hf = warp >> 2;                // which half of the columns this thread handles
         int q = 0;                               // up chunks done (TMEM buffer q & 1)
         bool bad = false;
+        float acc_p[16], acc_z = 0.f;  // routed variant: this thread's routing statistics
+        int acc_c[16];
+        float lbias[16];                // routed variant: the logit bias (0 past E)
+#pragma unroll
+        for (int e = 0; e < 16; e++) {
+            acc_p[e] = 0.f, acc_c[e] = 0;
+            lbias[e] = (RT && ra.bias && e < ra.E) ? ra.bias[e] : 0.f;
+        }
         for (int lt = 0; lt < my_tiles && !bad; lt++) {
             const int t0 = tile0(lt), tok = t0 + row;
             {
                 const int kq = tok < ntok ? topk : 0;
                 int es[8];
                 float ss[8];
+                if constexpr (!RT) {
 #pragma unroll
-                for (int s = 0; s < 8; s++) {
-                    es[s] = s < kq ? inds[(size_t)tok * topk + s] : -1;
-                    ss[s] = s < kq ? (scores ? to_f32(scores[(size_t)tok * topk + s]) : 1.f) : 0.f;
+                    for (int s = 0; s < 8; s++) {
+                        es[s] = s < kq ? inds[(size_t)tok * topk + s] : -1;
+                        ss[s] = s < kq ? (scores ? to_f32(scores[(size_t)tok * topk + s]) : 1.f) : 0.f;
+                    }
                 }
                 bad = ck::bar_or_n(BAR_EPI, NEPI, !ck::mbar_wait(&cs.d1_full, lt & 1, &cs.abort, err));
                 if (bad) break;  // the vote keeps the threads together for the named barriers
                 tc_fence_after();
+                if constexpr (RT) {
+                    // router (moe.py:56-86): logits = x W^T from the two gate terms
+                    // (W = W0 + W1 / 2048, each product exact in fp32), + bias; full-softmax
+                    // statistics, top-k by repeated argmax with ties to the lower expert id,
+                    // softmax over the selected logits rounded to the activation type
+                    float hi[16], lo[16], lg[16];
+                    tmem_ld16(tmem + lane_base + (lt & 1) * G::ENX + EN, hi);
+                    tmem_ld16(tmem + lane_base + (lt & 1) * G::ENX + EN + 16, lo);
+                    tmem_wait_ld();
+                    const int E = ra.E;
+                    float m = -INFINITY;
+#pragma unroll
+                    for (int e = 0; e < 16; e++) {
+                        lg[e] = e < E ? hi[e] + lo[e] * (1.f / 2048.f) + lbias[e] : -INFINITY;
+                        m = fmaxf(m, lg[e]);
+                    }
+                    float ex[16], se = 0.f;
+#pragma unroll
+                    for (int e = 0; e < 16; e++) ex[e] = e < E ? expf(lg[e] - m) : 0.f, se += ex[e];
+                    const bool tv = tok < ntok;
+                    if (tv && hf == 0) {
+#pragma unroll
+                        for (int e = 0; e < 16; e++) acc_p[e] += ex[e] / se;
+                        const float lse = m + logf(se);
+                        acc_z = fmaf(lse, lse, acc_z);
+                    }
+                    unsigned taken = 0;
+                    float sel0 = 0.f, denom = 0.f;
+#pragma unroll
+                    for (int s = 0; s < 8; s++) {
+                        es[s] = -1;
+                        if (s < kq) {
+                            float bv = -INFINITY;
+                            int bi = -1;
+#pragma unroll
+                            for (int e = 0; e < 16; e++)  // ascending ids, strictly greater: ties to the lower id
+                                if (e < E && !((taken >> e) & 1u) && (bi < 0 || lg[e] > bv)) bv = lg[e], bi = e;
+                            if (bi < 0) bi = 0;  // topk <= E is checked on the host
+                            taken |= 1u << bi;
+                            es[s] = bi;
+                            ss[s] = bv;  // the logit for now
+                            if (s == 0) sel0 = bv;
+                            denom += expf(bv - sel0);
+                        }
+                    }
+#pragma unroll
+                    for (int s = 0; s < 8; s++) {
+                        if (s < kq) {
+                            const T sc = from_f32<T>(expf(ss[s] - sel0) / denom);
+                            ss[s] = to_f32(sc);  // H uses the score in the activation type
+                            if (hf == 0) {
+                                ra.inds[(size_t)tok * topk + s] = es[s];
+                                reinterpret_cast<T*>(ra.scores)[(size_t)tok * topk + s] = sc;
+#pragma unroll
+                                for (int e = 0; e < 16; e++) acc_c[e] += es[s] == e ? 1 : 0;
+                            }
+                        } else {
+                            ss[s] = 0.f;
+                        }
+                    }
+                }
 #pragma unroll
                 for (int h0 = hf * (EN / 2); h0 < (hf + 1) * (EN / 2); h0 += 16) {
                     float v[16];
                     uint32_t hp[8];
-                    tmem_ld16(tmem + lane_base + (lt & 1) * EN + h0, v);
+                    tmem_ld16(tmem + lane_base + (lt & 1) * G::ENX + h0, v);
                     tmem_wait_ld();
 #pragma unroll
                     for (int c = 0; c < 16; c += 8) {
@@ -375,9 +477,41 @@ __global__ void __launch_bounds__(atc::NTH, 1)
                 proxy_fence();  // the TMA store reads these bytes through the async proxy
                 ck::bar_sync_n(BAR_EPI, NEPI);
                 if (tid == 0) {  // hand the box to the store warp
-                    if (q >= 2 && !ck::mbar_wait(&cs.out_empty[q & 1], ((q >> 1) + 1) & 1, &cs.abort, err)) bad = true;
+                    // a wait that gives up sets the abort flag: the next wait of every epilogue
+                    // thread then fails too and their vote ends the loops together
+                    if (q >= 2) ck::mbar_wait(&cs.out_empty[q & 1], ((q >> 1) + 1) & 1, &cs.abort, err);
                     ck::mbar_arrive(&cs.out_full[q & 1]);
                 }
+            }
+        }
+        if constexpr (RT) {
+            // this CTA's routing partials, in a fixed order: lanes, then warps 0-3
+            const int E = ra.E;
+            if (hf == 0) {
+#pragma unroll
+                for (int e = 0; e < 16; e++) {
+#pragma unroll
+                    for (int o = 1; o < 32; o <<= 1) {
+                        acc_p[e] += __shfl_xor_sync(0xffffffffu, acc_p[e], o);
+                        acc_c[e] += __shfl_xor_sync(0xffffffffu, acc_c[e], o);
+                    }
+                }
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) acc_z += __shfl_xor_sync(0xffffffffu, acc_z, o);
+                if (lane == 0) {
+#pragma unroll
+                    for (int e = 0; e < 16; e++) cs.red_p[warp][e] = acc_p[e], cs.red_c[warp][e] = acc_c[e];
+                    cs.red_p[warp][16] = acc_z;
+                }
+            }
+            ck::bar_sync_n(BAR_EPI, NEPI);
+            if (tid <= E) {
+                const bool ab = cs.abort != 0;
+                float sp = 0.f;
+                int sc = 0;
+                for (int w = 0; w < 4; w++) sp += cs.red_p[w][tid < E ? tid : 16], sc += tid < E ? cs.red_c[w][tid] : 0;
+                ra.part_f[(size_t)blockIdx.x * (E + 1) + tid] = ab ? __int_as_float(0x7fc00000) : sp;
+                if (tid < E) ra.part_c[(size_t)blockIdx.x * E + tid] = sc;
             }
         }
     }
@@ -429,9 +563,35 @@ static int make_map(CUtensorMap* m, bool bf16, const void* base, int rank, const
 }
 }  // namespace atc
 
-template <typename T, int EN>
+// Gate operand of the routed variant: W (E, C) fp32 split into W0 = fp16(W) and
+// W1 = fp16((W - W0) * 2048) (every fp16 x fp16 product is exact in fp32, so the logits
+// keep fp32-level rounding), laid out per 64-channel slice as the MN-major no-swizzle
+// core matrices of the down product's B operand: column n < 16 is expert n's W0,
+// 16 <= n < 32 expert (n - 16)'s W1 (zero past E); N group n / 8 at 1024 bytes, K group
+// (channel / 8) at 128 bytes, 16 bytes per channel.
+__global__ void moe_gate_split_kernel(const float* __restrict__ W, __half* __restrict__ out, int E, int C) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;  // one (channel, column) pair
+    if (i >= C * atc::GATE_COLS) return;
+    const int c = i / atc::GATE_COLS, n = i % atc::GATE_COLS, e = n & 15;
+    const float w = e < E ? W[(size_t)e * C + c] : 0.f;
+    const __half w0 = __float2half_rn(w);
+    const __half v = n < 16 ? w0 : __float2half_rn((w - __half2float(w0)) * 2048.f);
+    const int s = c / atc::KS, k = c % atc::KS;
+    const size_t byte = (size_t)s * atc::KS * atc::GATE_COLS * 2 + (n / 8) * 1024 + (k / 8) * 128 + (k % 8) * 16 + (n % 8) * 2;
+    out[byte / 2] = v;
+}
+
+int moe_apply_tc_grid(int ntok) {
+    int dev = 0, nsm = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    const int ntiles = (ntok + atc::TM - 1) / atc::TM;
+    return ntiles < nsm ? ntiles : nsm;  // persistent: one CTA per SM
+}
+
+template <typename T, int EN, bool RT>
 static int launch_apply_tc(const void* x, const void* base, const void* A, const void* B, const int32_t* inds,
-                           const void* scores, void* out, int ntok, int C, int R, int topk, cudaStream_t st) {
+                           const void* scores, void* out, int ntok, int C, int R, int topk, const RouteArgs& ra,
+                           cudaStream_t st) {
     using namespace atc;
     constexpr bool BF = std::is_same<T, __nv_bfloat16>::value;
     const int E = EN / R, rp = R / 8;
@@ -459,27 +619,44 @@ static int launch_apply_tc(const void* x, const void* base, const void* A, const
         const int rc = make_map(&mb, BF, B, 2, dims, row_stride, box, true);
         if (rc) return rc;
     }
-    auto kern = moe_lora_apply_tc_kernel<T, EN>;
-    const int smem = Geo<EN>::SMEM;
+    auto kern = moe_lora_apply_tc_kernel<T, EN, RT>;
+    const int smem = Geo<EN, RT>::SMEM;
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (err != cudaSuccess) return set_cuda_error(err);
-    int dev = 0, nsm = 148;
-    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-    const int ntiles = (ntok + TM - 1) / TM;
-    const int grid = ntiles < nsm ? ntiles : nsm;  // persistent: one CTA per SM
+    const int grid = moe_apply_tc_grid(ntok);
     const int accum = base != nullptr && base == out;
     kern<<<grid, NTH, smem, st>>>(mx, ma, mb, mbase, mout, base ? 1 : 0, accum, inds, (const T*)scores, ntok, C, R,
-                                  topk);
+                                  topk, ra);
     return check_launch();
 }
 
 template <typename T>
 int moe_lora_apply_tc(const void* x, const void* base, const void* A, const void* B, const int32_t* inds,
                       const void* scores, void* out, int ntok, int C, int R, int E, int topk, cudaStream_t st) {
+    const RouteArgs ra{};
     switch (E * R) {
-        case 32: return launch_apply_tc<T, 32>(x, base, A, B, inds, scores, out, ntok, C, R, topk, st);
-        case 64: return launch_apply_tc<T, 64>(x, base, A, B, inds, scores, out, ntok, C, R, topk, st);
-        case 128: return launch_apply_tc<T, 128>(x, base, A, B, inds, scores, out, ntok, C, R, topk, st);
+        case 32: return launch_apply_tc<T, 32, false>(x, base, A, B, inds, scores, out, ntok, C, R, topk, ra, st);
+        case 64: return launch_apply_tc<T, 64, false>(x, base, A, B, inds, scores, out, ntok, C, R, topk, ra, st);
+        case 128: return launch_apply_tc<T, 128, false>(x, base, A, B, inds, scores, out, ntok, C, R, topk, ra, st);
+        default: return RWKV_ERR_SHAPE;
+    }
+}
+
+// Routed variant (fp16): the gate split into `gsplit` (C / 64 blocks of 4 KB), then the
+// apply kernel with the router folded into its down product; the per-CTA routing
+// partials go to part_f / part_c (moe_apply_tc_grid(ntok) CTAs) for the finalize kernel.
+int moe_lora_apply_tc_routed(const void* x, const void* base, const void* A, const void* B, const float* gate_w,
+                             const float* bias, int32_t* inds, void* scores, void* gsplit, float* part_f,
+                             int32_t* part_c, void* out, int ntok, int C, int R, int E, int topk, cudaStream_t st) {
+    const int n = C * atc::GATE_COLS;
+    moe_gate_split_kernel<<<(n + 255) / 256, 256, 0, st>>>(gate_w, (__half*)gsplit, E, C);
+    int rc = check_launch();
+    if (rc) return rc;
+    const RouteArgs ra{(const unsigned char*)gsplit, bias, E, inds, scores, part_f, part_c};
+    switch (E * R) {
+        case 32: return launch_apply_tc<__half, 32, true>(x, base, A, B, nullptr, nullptr, out, ntok, C, R, topk, ra, st);
+        case 64: return launch_apply_tc<__half, 64, true>(x, base, A, B, nullptr, nullptr, out, ntok, C, R, topk, ra, st);
+        case 128: return launch_apply_tc<__half, 128, true>(x, base, A, B, nullptr, nullptr, out, ntok, C, R, topk, ra, st);
         default: return RWKV_ERR_SHAPE;
     }
 }

@@ -163,6 +163,42 @@ def lora_apply(x2d, base2d, A, Bw, inds, scores, out=None):
     return out
 
 
+def lora_apply_routed_supported(C: int, R: int, E: int, top_k: int, dtype: torch.dtype) -> bool:
+    """The router folded into the fused apply kernel: fp16, E <= 16, E * R in {32, 64, 128}."""
+    return bool(nat.lib().rwkv_moe_lora_apply_routed_supported(C, R, E, top_k, nat.dtype_code_of(dtype)))
+
+
+def lora_apply_routed(x2d, base2d, A, Bw, gate_w, top_k: int, bias=None, out=None):
+    """Router (moe.py:51-86) and adapter apply (moe.py:142-147) in one pass over x:
+    returns (out, routing dict like :func:`router_forward`, without logits)."""
+    ntok, C = x2d.shape
+    E, _, R = A.shape
+    dt = x2d.dtype
+    dev = x2d.device
+    if out is None:
+        out = torch.empty((ntok, C), device=dev, dtype=dt)
+    A = A.to(dt).contiguous()
+    Bw = Bw.to(dt).contiguous()
+    base2d = None if base2d is None else base2d.to(dt).contiguous()
+    gw = gate_w.to(torch.float32).contiguous()
+    b = None if bias is None else bias.to(torch.float32).contiguous()
+    inds = torch.empty((ntok, top_k), device=dev, dtype=torch.int32)
+    scores = torch.empty((ntok, top_k), device=dev, dtype=dt)
+    stats = torch.empty(2 + E, device=dev, dtype=torch.float32)
+    counts = torch.empty(E, device=dev, dtype=torch.int32)
+    L = nat.lib()
+    ws_bytes = L.rwkv_moe_lora_apply_routed_workspace_size(ntok, C, E)
+    ws = torch.empty(max(1, ws_bytes), device=dev, dtype=torch.uint8)
+    with torch.cuda.device(dev):
+        rc = L.rwkv_moe_lora_apply_routed(nat.ptr(x2d.contiguous()), nat.ptr(base2d), nat.ptr(A), nat.ptr(Bw),
+                                          nat.ptr(gw), nat.ptr(b), nat.ptr(inds), nat.ptr(scores), nat.ptr(stats),
+                                          nat.ptr(counts), nat.ptr(ws), ws_bytes, nat.ptr(out), ntok, C, R, E,
+                                          top_k, nat.dtype_code(x2d), _stream(dev))
+    nat.check(rc, "rwkv_moe_lora_apply_routed")
+    return out, {"inds": inds, "scores": scores, "aux": stats[0], "z": stats[1], "f": stats[2:],
+                 "counts": counts, "logits": None}
+
+
 def ortho_loss(A: torch.Tensor) -> torch.Tensor:
     E, C, R = A.shape
     A = A.contiguous()
@@ -249,6 +285,12 @@ class LoRAMoE_CMix(nn.Module):
         with torch.no_grad():
             base_out = self.base(x)
         x2 = x.reshape(B * T, C).contiguous()
+        if lora_apply_routed_supported(C, self.lora_rank, self.n_experts, self.top_k, x.dtype):
+            # router folded into the adapter pass: x is read once
+            b2 = base_out.reshape(B * T, C)
+            out, r = lora_apply_routed(x2, b2, self.lora_A.detach(), self.lora_B.detach(), self.router.gate.weight,
+                                       self.top_k, self.router.bias, out=b2)
+            return out.reshape(B, T, C), r["aux"], r["z"]
         r = router_forward(x2, self.router.gate.weight, self.top_k, self.router.bias)
         if lora_apply_supported(C, self.lora_rank, self.n_experts, self.top_k, x.dtype):
             b2 = base_out.reshape(B * T, C)  # a temporary: the adapters are added into it in place

@@ -332,3 +332,55 @@ def test_full_moe_cmix_rnn_step_matches_oracle():
     ref = mo.full_moe_step(g(x), g(xp), g(fm.x_k), g(fm.expert_key), g(fm.expert_val), inds,
                            r["scores"].double().cpu().numpy())
     assert rel_rms(out.double().cpu().numpy(), ref) < _TOL[torch.float16]
+
+
+@pytest.mark.parametrize("ntok,C,E,R,k,with_bias", [(3000, 768, 8, 16, 2, True), (65536, 768, 8, 16, 2, True),
+                                                     (1000, 256, 4, 8, 1, False), (777, 512, 16, 8, 3, True)])
+def test_routed_apply_matches_oracle(ntok, C, E, R, k, with_bias):
+    """The router folded into the tcgen05 apply kernel (one pass over x): expert sets equal
+    the oracle's routing on its own float64 logits except provable near-ties (fp32
+    summation-order bound, as in the config-4 router test); scores, aux, z, counts and the
+    output (out = base in place) against the oracle and the unfused router + apply."""
+    from rwkv_mlx_b200.moe import lora_apply, lora_apply_routed, lora_apply_routed_supported, router_forward
+
+    assert lora_apply_routed_supported(C, R, E, k, torch.float16)
+    x = _x(ntok, C, 3 + E, torch.float16)
+    rng = np.random.default_rng(E + k)
+    gw = torch.tensor(rng.standard_normal((E, C)) / np.sqrt(C), dtype=torch.float32, device="cuda")
+    bias = torch.tensor(rng.normal(0, 1.5, E), dtype=torch.float32, device="cuda") if with_bias else None
+    A = torch.tensor(rng.normal(0, 0.02, (E, C, R)), dtype=torch.float16, device="cuda")
+    Bw = torch.tensor(rng.normal(0, 0.02, (E, R, C)), dtype=torch.float16, device="cuda")
+    base = _x(ntok, C, 99, torch.float16)
+    out = base.clone()
+    out, rf = lora_apply_routed(x, out, A, Bw, gw, k, bias, out=out)  # in place, as the module calls it
+    ru = router_forward(x, gw, k, bias)
+    out_u = lora_apply(x, base, A, Bw, ru["inds"], ru["scores"])
+    torch.cuda.synchronize()
+    xn, wn = x.float().cpu().numpy(), gw.cpu().numpy()
+    bn = None if bias is None else bias.cpu().numpy()
+    lg = mo.gate_logits(xn, wn, bn)
+    ref = mo.topk_from_logits(lg, k)
+    got = rf["inds"].cpu().numpy().astype(np.int64)
+    bad = np.nonzero((got != ref).any(-1))[0]
+    mag = np.abs(xn.astype(np.float64)) @ np.abs(wn.astype(np.float64)).T
+    bound = C * 2.0 ** -24 * mag + (0 if bn is None else 2.0 ** -24 * np.abs(bn))
+    for t in bad:
+        for e_g, e_r in zip(got[t], ref[t]):
+            if e_g != e_r:
+                assert abs(lg[t, e_g] - lg[t, e_r]) <= bound[t, e_g] + bound[t, e_r], (t, e_g, e_r)
+    assert len(bad) <= max(2, ntok // 20000)
+    # everything else against the oracle on the fused routing
+    inds_r, sc_r, aux_r, z_r, f_r = mo.router(None, None, k, logits=lg)
+    sel = np.take_along_axis(lg, got, -1)
+    sc = np.exp(sel - sel.max(-1, keepdims=True))
+    sc = sc / sc.sum(-1, keepdims=True)
+    assert np.abs(rf["scores"].double().cpu().numpy() - sc).max() < 1e-3  # fp16 scores
+    assert abs(float(rf["aux"]) - aux_r) < 1e-4 * max(1.0, abs(aux_r))
+    assert abs(float(rf["z"]) - z_r) < 1e-4 * max(1.0, abs(z_r))
+    np.testing.assert_array_equal(rf["counts"].cpu().numpy(), np.bincount(got.reshape(-1), minlength=E))
+    xd = x.double().cpu().numpy()
+    ref_out = base.double().cpu().numpy() + mo.lora_moe_delta(xd, A.double().cpu().numpy(), Bw.double().cpu().numpy(),
+                                                               got, rf["scores"].double().cpu().numpy())
+    assert rel_rms(out.double().cpu().numpy(), ref_out) < 2e-3
+    same = np.nonzero((got == ru["inds"].cpu().numpy()).all(-1))[0]
+    assert rel_rms(out.double().cpu().numpy()[same], out_u.double().cpu().numpy()[same]) < 1e-3

@@ -236,9 +236,13 @@ def split_batch(B_global: int, ws: int, rank: int) -> int:
 
 
 def run_prefill(args, ws, rank, dev, B, model=None, strong=True, with_e2e=True):
-    """GPT-mode prefill of B sequences x T tokens on this rank; `value` = tokens of all
-    ranks / max-over-ranks time."""
+    """GPT-mode prefill of B sequences x T tokens on this rank, one CUDA-graph replay of
+    the model's forward per step (model.PrefillGraph); `value` = tokens of all ranks /
+    max-over-ranks time.  The WKV-7 forward's duration for the roofline is measured with
+    CUDA events around each call on its stream in eager steps right after (the kernels
+    and their inputs are the same as inside the graph)."""
     from rwkv_mlx_b200 import _native, check_device_error, wkv7
+    from rwkv_mlx_b200.model import PrefillGraph
 
     T = args.seq
     if model is None:
@@ -249,25 +253,39 @@ def run_prefill(args, ws, rank, dev, B, model=None, strong=True, with_e2e=True):
     host_idx = idx.cpu().pin_memory()
     host_out = torch.empty((B, cfg.vocab_size), dtype=torch.float16).pin_memory()
 
-    def step():
+    def eager_step():
         with torch.no_grad():
             logits, _ = model(idx)
         return logits
 
     for _ in range(args.warmup):
-        step()
+        eager_step()
+    torch.cuda.synchronize()
+    l0 = _native.launch_count
+    eager_step()
+    per_step_launches = _native.launch_count - l0  # this repository's kernels in one forward
+    graph = PrefillGraph(model, B, T, warmup=1)
+    graph(idx)  # inputs resident in the graph's buffer from here on
+    for _ in range(args.warmup):
+        graph()
+
+    def step():
+        return graph()[0]
+
     torch.cuda.synchronize()
 
     # ---- device-resident timed region ----
-    wkv7.fwd_timings = []
-    launches0 = _native.launch_count
     barrier(ws)
     torch.cuda.synchronize()
     clk = ClockSampler(dev)
     ms = cuda_timed(step, args.steps)
     clocks = clk.stop()
     barrier(ws)
-    launches = _native.launch_count - launches0
+    launches = per_step_launches * args.steps
+    check_device_error()
+    # WKV-7 forward duration per call (events on its stream), eager steps of the same batch
+    wkv7.fwd_timings = []
+    cuda_timed(eager_step, args.steps)
     kt = [a.elapsed_time(b) for a, b in wkv7.fwd_timings]
     wkv7.fwd_timings = None
     check_device_error()
@@ -278,12 +296,9 @@ def run_prefill(args, ws, rank, dev, B, model=None, strong=True, with_e2e=True):
     e2e = None
     if with_e2e:
         # ---- end-to-end through the public API, host buffers ----
-        dev_idx = torch.empty_like(idx)
 
         def e2e_step():
-            dev_idx.copy_(host_idx, non_blocking=True)
-            with torch.no_grad():
-                logits, _ = model(dev_idx)
+            logits, _ = graph(host_idx)  # H2D from pinned host memory into the graph's input
             host_out.copy_(logits[:, -1], non_blocking=True)
 
         e2e_step()
@@ -295,7 +310,8 @@ def run_prefill(args, ws, rank, dev, B, model=None, strong=True, with_e2e=True):
         e2e_ms = max_over_ranks(max(e2e_ms, wall_ms), ws)
         e2e = {"value": tok_all / (e2e_ms / 1e3), "unit": "tok/s", "h2d_bytes_per_step": B * T * 8,
                "d2h_bytes_per_step": B * cfg.vocab_size * 2,
-               "path": "RWKV.forward via the public API; tokens H2D from pinned host, last-position logits D2H"}
+               "path": "model.PrefillGraph (RWKV.forward captured as a CUDA graph) via the public API; tokens H2D "
+                       "from pinned host, last-position logits D2H"}
 
     hbm, _, src = peaks()
     H = cfg.n_head
@@ -312,7 +328,7 @@ def run_prefill(args, ws, rank, dev, B, model=None, strong=True, with_e2e=True):
         "config": {"workload": "L12 D768 GPT-mode prefill (BASELINE configs[1])" if strong else
                    "L12 D768 GPT-mode prefill, B=8 per GPU (weak scaling)",
                    "model": "RWKV-v7 L12 D768", "global_batch": B_global, "batch_per_gpu": B, "seq_len": T,
-                   "parallelism": f"dp{ws} (batch split, no collective on the data path)",
+                   "parallelism": f"dp{ws} (batch split, no collective on the data path)", "cuda_graph": True,
                    "l2": "per-step working set (4.3 GB logits at B=8, 0.37 GB weights) far larger than L2"},
         "gpu_launches": launches,
         "roofline": {"kernel": "wkv7_fwd (rwkv_wkv7_forward_ws: tcgen05 forward, plus transition + scan "
@@ -321,6 +337,8 @@ def run_prefill(args, ws, rank, dev, B, model=None, strong=True, with_e2e=True):
                      "traffic": traffic_for("wkv7_fwd", B, T, H),
                      "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else "fallback 6650 GB/s",
                      "algorithmic_bytes_per_launch": bytes_launch, "launch_ms": k_ms, "launches_timed": len(kt),
+                     "launch_timing": "CUDA events around each WKV-7 forward call on its stream, eager steps "
+                                      "after the graph-timed region",
                      "wkv_share_of_step": (k_ms * len(kt) / args.steps) / ms_max if kt else None},
         "clocks": clocks,
     }

@@ -593,6 +593,47 @@ class DecodeGraph:
         return self.tokens
 
 
+class PrefillGraph:
+    """GPT-mode forward (:meth:`RWKV.forward`) of a fixed (B, T) batch captured once in a
+    CUDA graph and replayed: one launch per step instead of ~17 per layer from Python,
+    which matters when each GPU holds few sequences (strong scaling) and the host would
+    otherwise bound the step.
+
+    ``graph(idx)`` copies ``idx`` (any device or pinned host tensor of shape (B, T)) into
+    the captured input buffer on the current stream, replays, and returns the captured
+    ``(logits, aux)`` buffers (overwritten by the next replay).  Like
+    :class:`DecodeGraph`, a replay refuses to run after a parameter was updated in place
+    or replaced (the graph holds packed copies of some weights)."""
+
+    def __init__(self, model: "RWKV", batch: int, seq_len: int, warmup: int = 2):
+        self.model = model
+        dev = model.emb.weight.device
+        self.idx = torch.zeros((batch, seq_len), dtype=torch.long, device=dev)
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side), torch.no_grad():
+            for _ in range(warmup):  # lazy one-time set-up (packed weights, kernel attributes) outside the capture
+                model(self.idx)
+        torch.cuda.current_stream().wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph), torch.no_grad():
+            self.logits, self.aux = model(self.idx)
+        self._params = list(model.parameters())
+        self._fingerprint = self._weights_fingerprint()
+
+    def _weights_fingerprint(self):
+        return tuple((p.data_ptr(), p._version) for p in self._params)
+
+    def __call__(self, idx: torch.Tensor | None = None):
+        if self._weights_fingerprint() != self._fingerprint:
+            raise RuntimeError("PrefillGraph: a model parameter was updated or replaced after the graph was "
+                               "captured; build a new PrefillGraph.")
+        if idx is not None:
+            self.idx.copy_(idx, non_blocking=True)
+        self.graph.replay()
+        return self.logits, self.aux
+
+
 # ---------------------------------------------------------------------------
 # The reference's module-level RNN-mode functions (model.py:441-506), same signatures
 # ---------------------------------------------------------------------------

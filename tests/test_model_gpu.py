@@ -285,3 +285,26 @@ def test_add_layernorm_matches_torch(dt, C, with_delta):
     ref_y = torch.nn.functional.layer_norm(ref_x.float(), (C,), w.float(), b.float(), 1e-5)
     tol = {torch.float16: 4e-3, torch.bfloat16: 3e-2, torch.float32: 1e-5}[dt]
     assert (y.float() - ref_y).abs().max().item() < tol
+
+
+def test_prefill_graph_matches_eager_forward():
+    """model.PrefillGraph (the GPT-mode forward captured as a CUDA graph) gives the eager
+    forward's logits for new inputs copied into it, and refuses stale weights."""
+    from rwkv_mlx_b200.model import PrefillGraph
+
+    for moe in (False, True):
+        cfg, m = _tiny(moe=moe)
+        g = PrefillGraph(m, 2, 48)
+        for seed in (0, 1):
+            idx = torch.randint(0, cfg.vocab_size, (2, 48), device="cuda",
+                                generator=torch.Generator(device="cuda").manual_seed(seed))
+            with torch.no_grad():
+                ref, ref_aux = m(idx)
+            got, aux = g(idx.cpu().pin_memory())
+            torch.cuda.synchronize()
+            assert rel_rms(got.float().cpu().numpy(), ref.float().cpu().numpy()) < 1e-5
+            assert abs(float(aux) - float(ref_aux)) < 1e-6 * max(1.0, abs(float(ref_aux)))
+        with torch.no_grad():
+            m.head.weight.mul_(1.0)
+        with pytest.raises(RuntimeError, match="PrefillGraph"):
+            g()

@@ -28,6 +28,8 @@
 // into high and low TF32 parts (three products, fp32-accurate).  Chunks whose
 // cumulative decay falls below e^-80 form the Mab..Mrk products and their gradients
 // element-wise from exponent differences (the factored forms would overflow).
+#include <type_traits>
+
 #include "chunk_common.cuh"
 #include "common.cuh"
 #include "wkv7.cuh"
@@ -76,6 +78,14 @@ __device__ __forceinline__ void tile_mm(float (&d)[4], const FA& A, const FB& B,
 #pragma unroll
     for (int i = 0; i < 4; i++) d[i] += e[i];
 }
+// out(m, n, v) or, when it takes a fourth argument, out(m, n, v, slot): slot 0..3 is the
+// element's place in the thread's accumulator fragment (a compile-time constant at each
+// call), so that results can accumulate in registers.
+template <typename FO>
+__device__ __forceinline__ void emit(const FO& out, int m, int n, float v, int slot) {
+    if constexpr (std::is_invocable_v<FO, int, int, float, int>) out(m, n, v, slot);
+    else out(m, n, v);
+}
 // C (M x Nn) = A (M x K) B (K x Nn) over the block's warps; out(m, n, v) once per element.
 // The element -> thread mapping depends only on (M, Nn), so successive calls with the
 // same shape may accumulate into the same elements without a barrier.
@@ -87,10 +97,10 @@ __device__ __forceinline__ void block_mm(int M, int Nn, int K, const FA& A, cons
         const int m0 = (tile / ntl) * 16, n0 = (tile % ntl) * 8;
         float d[4] = {0.f, 0.f, 0.f, 0.f};
         tile_mm(d, [&](int m, int k) { return A(m0 + m, k); }, [&](int k, int n) { return B(k, n0 + n); }, K);
-        out(m0 + g, n0 + 2 * tg, d[0]);
-        out(m0 + g, n0 + 2 * tg + 1, d[1]);
-        out(m0 + g + 8, n0 + 2 * tg, d[2]);
-        out(m0 + g + 8, n0 + 2 * tg + 1, d[3]);
+        emit(out, m0 + g, n0 + 2 * tg, d[0], 0);
+        emit(out, m0 + g, n0 + 2 * tg + 1, d[1], 1);
+        emit(out, m0 + g + 8, n0 + 2 * tg, d[2], 2);
+        emit(out, m0 + g + 8, n0 + 2 * tg + 1, d[3], 3);
     }
 }
 
@@ -116,10 +126,10 @@ __device__ __forceinline__ void block_mm_s(int M, int Nn, const FO& out, const S
         (tile_mm<S::AX, S::BX>(d, [&](int m, int k) { return segs.A(m0 + m, k); },
                                [&](int k, int n) { return segs.B(k, n0 + n); }, segs.K),
          ...);
-        out(m0 + g, n0 + 2 * tg, d[0]);
-        out(m0 + g, n0 + 2 * tg + 1, d[1]);
-        out(m0 + g + 8, n0 + 2 * tg, d[2]);
-        out(m0 + g + 8, n0 + 2 * tg + 1, d[3]);
+        emit(out, m0 + g, n0 + 2 * tg, d[0], 0);
+        emit(out, m0 + g, n0 + 2 * tg + 1, d[1], 1);
+        emit(out, m0 + g + 8, n0 + 2 * tg, d[2], 2);
+        emit(out, m0 + g + 8, n0 + 2 * tg + 1, d[3], 3);
     }
 }
 
@@ -154,13 +164,20 @@ enum { FAT = 0, FRT, FBH, FKH, FBB, FKB, NF };
 
 // Shared per-chunk front end: inputs -> cumulative decays -> factors -> intra-chunk
 // matrices -> Inv.  `which` selects the matrices needed (bit m for Mab, Mak, Mrb, Mrk).
+// The inputs other than l stay in their own type (16-bit ones are exact in fp32 and take
+// half the shared memory); l = -exp(w) is fp32.
+template <typename T>
 struct Front {
-    float in[NIN][L][LDC];
+    static constexpr int LDI = sizeof(T) == 2 ? 72 : LDC;  // conflict-free fragment reads
+    T in[NIN - 1][L][LDI];
+    float inl[L][LDC];
     float c[L][LDC];
     float f[NF][L][LDC];
     float GL[N];
     float M[4][L][LM];
     float Inv[L][LM];
+    __device__ __forceinline__ static int slot(int arr) { return arr > IL ? arr - 1 : arr; }
+    __device__ __forceinline__ float x(int arr, int t, int j) const { return to_f32(in[slot(arr)][t][j]); }
 };
 
 // One chunk's inputs: every thread issues at most one 16-byte load per array (all of
@@ -187,7 +204,7 @@ struct ChunkLoad {
             raw[arr] = __ldg(reinterpret_cast<const uint4*>(src));
         }
     }
-    __device__ __forceinline__ void store(Front& fr, int nt, unsigned mask) const {
+    __device__ __forceinline__ void store(Front<T>& fr, int nt, unsigned mask) const {
         const int tid = threadIdx.x;
 #pragma unroll
         for (int arr = 0; arr < NIN; arr++) {
@@ -197,12 +214,12 @@ struct ChunkLoad {
                 const TW* e = reinterpret_cast<const TW*>(&raw[arr]);
                 const int col = (tid % pr) * VW;
 #pragma unroll
-                for (int i = 0; i < VW; i++) fr.in[IL][row][col + i] = row < nt ? -expf(to_f32(e[i])) : 0.f;
+                for (int i = 0; i < VW; i++) fr.inl[row][col + i] = row < nt ? -expf(to_f32(e[i])) : 0.f;
             } else {
                 const T* e = reinterpret_cast<const T*>(&raw[arr]);
                 const int col = (tid % pr) * VT;
 #pragma unroll
-                for (int i = 0; i < VT; i++) fr.in[arr][row][col + i] = to_f32(e[i]);
+                for (int i = 0; i < VT; i++) fr.in[Front<T>::slot(arr)][row][col + i] = e[i];
             }
         }
     }
@@ -218,13 +235,14 @@ __device__ __forceinline__ void cp_mat(float (*dst)[LDC], const float* src) {
 }
 
 // returns the CTA-uniform "extreme decay" flag
-__device__ int front_factors(Front& fr) {
+template <typename T>
+__device__ int front_factors(Front<T>& fr) {
     const int tid = threadIdx.x;
     int ext = 0;
     if (tid < N) {
         float s = 0.f;
 #pragma unroll
-        for (int t = 0; t < L; t++) s += fr.in[IL][t][tid], fr.c[t][tid] = s;
+        for (int t = 0; t < L; t++) s += fr.inl[t][tid], fr.c[t][tid] = s;
         ext = s < EXT_C;
         fr.GL[tid] = expf(s);
     }
@@ -232,15 +250,15 @@ __device__ int front_factors(Front& fr) {
     for (int e = tid; e < L * N; e += NT) {
         const int t = e / N, j = e % N;
         const float cp = t ? fr.c[t - 1][j] : 0.f, ct = fr.c[t][j], cl = fr.c[L - 1][j];
-        fr.f[FAT][t][j] = fr.in[IA][t][j] * expf(cp);
-        fr.f[FRT][t][j] = fr.in[IR][t][j] * expf(ct);
+        fr.f[FAT][t][j] = fr.x(IA, t, j) * expf(cp);
+        fr.f[FRT][t][j] = fr.x(IR, t, j) * expf(ct);
         const float eb = expf(cl - ct);
-        fr.f[FBB][t][j] = fr.in[IB][t][j] * eb;
-        fr.f[FKB][t][j] = fr.in[IK][t][j] * eb;
+        fr.f[FBB][t][j] = fr.x(IB, t, j) * eb;
+        fr.f[FKB][t][j] = fr.x(IK, t, j) * eb;
         if (!ext) {
             const float ei = expf(-ct);
-            fr.f[FBH][t][j] = fr.in[IB][t][j] * ei;
-            fr.f[FKH][t][j] = fr.in[IK][t][j] * ei;
+            fr.f[FBH][t][j] = fr.x(IB, t, j) * ei;
+            fr.f[FKH][t][j] = fr.x(IK, t, j) * ei;
         }
     }
     __syncthreads();
@@ -248,7 +266,8 @@ __device__ int front_factors(Front& fr) {
 }
 
 // Mab, Mak (strict) and Mrb, Mrk (inclusive) for the matrices selected in `which`
-__device__ void front_matrices(Front& fr, int ext, unsigned which) {
+template <typename T>
+__device__ void front_matrices(Front<T>& fr, int ext, unsigned which) {
     if (!ext) {
         int ms[4], nb = 0;
         for (int m = 0; m < 4; m++)
@@ -269,10 +288,10 @@ __device__ void front_matrices(Front& fr, int ext, unsigned which) {
                 const int t = e / L, s = e % L;
                 float val = 0.f;
                 if (strict ? s < t : s <= t) {
-                    const float* xs = m < 2 ? fr.in[IA][t] : fr.in[IR][t];
-                    const float* ys = (m & 1) ? fr.in[IK][s] : fr.in[IB][s];
+                    const int xa = m < 2 ? IA : IR, ya = (m & 1) ? IK : IB;
                     const float* cx = m < 2 ? (t ? fr.c[t - 1] : nullptr) : fr.c[t];
-                    for (int j = 0; j < N; j++) val = fmaf(xs[j] * ys[j], expf((cx ? cx[j] : 0.f) - fr.c[s][j]), val);
+                    for (int j = 0; j < N; j++)
+                        val = fmaf(fr.x(xa, t, j) * fr.x(ya, s, j), expf((cx ? cx[j] : 0.f) - fr.c[s][j]), val);
                 }
                 fr.M[m][t][s] = val;
             }
@@ -548,33 +567,43 @@ int read_error_word(int clear) {
 }
 
 // ---------------------------------------------------------------------------
-// Pass 2: every input gradient of one chunk.
+// Pass 2: every input gradient of one chunk.  All the 16 x 64 gradient products share one
+// element -> thread mapping (thread (warp w, lane g*4+tg) owns rows g, g+8 and columns
+// 8w+2tg, 8w+2tg+1), so each thread accumulates its four elements of every gradient in
+// registers; shared memory then fits two CTAs per SM (16-bit inputs kept 16-bit).
+template <typename T>
 struct P2Smem {
-    Front fr;
-    float Sv[N][LDC];  // state at the chunk start, [value][key] (X = Sv^T)
-    float D[N][LDC];  // dX_L, [key][value]
+    Front<T> fr;
+    float Sv[N][LDC];  // state at the chunk start, [value][key] (X = Sv^T); scratch at the end
+    float D[N][LDC];   // dX_L, [key][value]
     float U[L][LDC], G[L][LDC], Lam[L][LDC];
     float dM[4][L][LM];
-    float dA[L][LDC], dR[L][LDC], dB[L][LDC], dK[L][LDC], dV[L][LDC];
-    float dC[L][LDC];   // d/dc_t from terms at index t
-    float dCp[L][LDC];  // d/dc_{t-1} from terms at index t
-    float Q[L][LDC];    // d/dc_L from terms at index t
     float dGL[N];
+};
+struct P2Acc {  // a thread's four elements (slots) of each gradient
+    float dA[4], dR[4], dB[4], dK[4], dV[4], dC[4], dCp[4], Q[4];
 };
 
 template <typename T, typename TW>
-__global__ void __launch_bounds__(NT, 1)
+__global__ void __launch_bounds__(NT, 2)
     wkv7_bwd_chunk_kernel(const T* __restrict__ r, const TW* __restrict__ w, const T* __restrict__ k,
                           const T* __restrict__ v, const T* __restrict__ a, const T* __restrict__ b,
                           const T* __restrict__ dy, const float* __restrict__ s0, const float* __restrict__ ckpt,
                           const float* __restrict__ dxl, T* __restrict__ dr, T* __restrict__ dw, T* __restrict__ dk,
                           T* __restrict__ dv, T* __restrict__ da, T* __restrict__ db, int T_, int H) {
     extern __shared__ __align__(16) unsigned char smem_p2[];
-    P2Smem& sm = *reinterpret_cast<P2Smem*>(smem_p2);
-    Front& fr = sm.fr;
+    P2Smem<T>& sm = *reinterpret_cast<P2Smem<T>*>(smem_p2);
+    Front<T>& fr = sm.fr;
     const int tid = threadIdx.x, c = blockIdx.x, bh = blockIdx.y, bi = bh / H, hi = bh % H;
     const size_t tstride = (size_t)H * N, base = ((size_t)bi * T_ * H + hi) * N;
     const int nch = gridDim.x, t0 = c * L, nt = min(L, T_ - t0);
+    const int lane = tid & 31, g = lane >> 2, tg = lane & 3, wrp = tid >> 5;
+    auto own_t = [&](int slot) { return g + 8 * (slot >> 1); };
+    auto own_j = [&](int slot) { return 8 * wrp + 2 * tg + (slot & 1); };
+    P2Acc acc;
+#pragma unroll
+    for (int q = 0; q < 4; q++)
+        acc.dA[q] = acc.dR[q] = acc.dB[q] = acc.dK[q] = acc.dV[q] = acc.dC[q] = acc.dCp[q] = acc.Q[q] = 0.f;
 
     {
         const float* S = c == 0 ? (s0 ? s0 + (size_t)bh * N * N : nullptr) : ckpt + ((size_t)bh * (T_ / L) + c - 1) * N * N;
@@ -588,29 +617,24 @@ __global__ void __launch_bounds__(NT, 1)
         ChunkLoad<T, TW> ld;
         ld.issue(r, w, k, v, a, b, dy, base, tstride, t0, nt, 0x7f);
         ld.store(fr, nt, 0x7f);
-        for (int e = tid; e < L * LDC; e += NT) {
-            (&sm.dA[0][0])[e] = 0.f, (&sm.dR[0][0])[e] = 0.f, (&sm.dB[0][0])[e] = 0.f, (&sm.dK[0][0])[e] = 0.f;
-            (&sm.dC[0][0])[e] = 0.f, (&sm.dCp[0][0])[e] = 0.f, (&sm.Q[0][0])[e] = 0.f;
-        }
         asm volatile("cp.async.wait_all;" ::: "memory");
     }
     __syncthreads();
     const int ext = front_factors(fr);
     front_matrices(fr, ext, 0b1111);
     const auto& F = fr.f;
-    const auto& IN = fr.in;
     constexpr bool EXI = sizeof(T) == 2;  // 16-bit v and dy are exact in TF32
 
     // U = Inv (At X + Mak V)
     block_mm_s(L, N, [&](int t, int vv, float val) { sm.G[t][vv] = val; },
                seg([&](int t, int j) { return F[FAT][t][j]; }, [&](int j, int vv) { return sm.Sv[vv][j]; }, N),
-               seg<false, EXI>([&](int t, int s) { return fr.M[1][t][s]; }, [&](int s, int vv) { return IN[IV][s][vv]; }, L));
+               seg<false, EXI>([&](int t, int s) { return fr.M[1][t][s]; }, [&](int s, int vv) { return fr.x(IV, s, vv); }, L));
     __syncthreads();
     block_mm(L, N, L, [&](int t, int s) { return fr.Inv[t][s]; }, [&](int s, int vv) { return sm.G[s][vv]; },
              [&](int t, int vv, float val) { sm.U[t][vv] = val; });
     // external gradient of U: Mrb^T dY + Bb dX_L
     block_mm_s(L, N, [&](int t, int vv, float val) { sm.Lam[t][vv] = val; },
-               seg<false, EXI>([&](int t, int s) { return fr.M[2][s][t]; }, [&](int s, int vv) { return IN[IDY][s][vv]; }, L),
+               seg<false, EXI>([&](int t, int s) { return fr.M[2][s][t]; }, [&](int s, int vv) { return fr.x(IDY, s, vv); }, L),
                seg([&](int t, int j) { return F[FBB][t][j]; }, [&](int j, int vv) { return sm.D[j][vv]; }, N));
     __syncthreads();
     // Lambda = Inv^T (...)  (into G, free after U)
@@ -620,14 +644,14 @@ __global__ void __launch_bounds__(NT, 1)
     const auto& Lam = sm.G;
     // gradients of the intra-chunk matrices (4 stacked 16x16 products)
     block_mm_b(4, L, N,
-               [&](int bb, int t, int vv) { return (bb < 2 ? &Lam[0][0] : &IN[IDY][0][0])[t * LDC + vv]; },
-               [&](int bb, int vv, int s) { return ((bb & 1) ? &IN[IV][0][0] : &sm.U[0][0])[s * LDC + vv]; },
+               [&](int bb, int t, int vv) { return bb < 2 ? Lam[t][vv] : fr.x(IDY, t, vv); },
+               [&](int bb, int vv, int s) { return (bb & 1) ? fr.x(IV, s, vv) : sm.U[s][vv]; },
                [&](int bb, int t, int s, float val) { sm.dM[bb][t][s] = (bb < 2 ? s < t : s <= t) ? val : 0.f; },
                EXI);
     // dV = Mak^T Lambda + Mrk^T dY + Kb dX_L
-    block_mm_s(L, N, [&](int s, int vv, float val) { sm.dV[s][vv] = val; },
+    block_mm_s(L, N, [&](int s, int vv, float val, int q) { acc.dV[q] = val; },
                seg([&](int s, int t) { return fr.M[1][t][s]; }, [&](int t, int vv) { return Lam[t][vv]; }, L),
-               seg<false, EXI>([&](int s, int t) { return fr.M[3][t][s]; }, [&](int t, int vv) { return IN[IDY][t][vv]; }, L),
+               seg<false, EXI>([&](int s, int t) { return fr.M[3][t][s]; }, [&](int t, int vv) { return fr.x(IDY, t, vv); }, L),
                seg([&](int s, int j) { return F[FKB][s][j]; }, [&](int j, int vv) { return sm.D[j][vv]; }, N));
     if (tid < N) {
         float sdg = 0.f;
@@ -635,67 +659,69 @@ __global__ void __launch_bounds__(NT, 1)
         sm.dGL[tid] = sdg * fr.GL[tid];
     }
     __syncthreads();
-    // Factor gradients.  Every call below is 16 x 64 with the same element -> thread
-    // mapping, so each thread accumulates only its own elements: no barriers needed.
+    // Factor gradients, accumulated in registers (same element -> thread mapping throughout).
     {
-        auto outA = [&](int t, int j, float val) {  // dAt: At = a e^{c_{t-1}}
+        auto outA = [&](int t, int j, float val, int q) {  // dAt: At = a e^{c_{t-1}}
             const float cp = t ? fr.c[t - 1][j] : 0.f;
-            sm.dA[t][j] += val * expf(cp);
-            sm.dCp[t][j] += val * F[FAT][t][j];
+            acc.dA[q] += val * expf(cp);
+            acc.dCp[q] += val * F[FAT][t][j];
         };
-        auto outR = [&](int t, int j, float val) {  // dRt: Rt = r e^{c_t}
-            sm.dR[t][j] += val * expf(fr.c[t][j]);
-            sm.dC[t][j] += val * F[FRT][t][j];
+        auto outR = [&](int t, int j, float val, int q) {  // dRt: Rt = r e^{c_t}
+            acc.dR[q] += val * expf(fr.c[t][j]);
+            acc.dC[q] += val * F[FRT][t][j];
         };
         auto sA = seg([&](int t, int vv) { return Lam[t][vv]; }, [&](int vv, int j) { return sm.Sv[vv][j]; }, N);
-        auto sR = seg<EXI, false>([&](int t, int vv) { return IN[IDY][t][vv]; }, [&](int vv, int j) { return sm.Sv[vv][j]; }, N);
+        auto sR = seg<EXI, false>([&](int t, int vv) { return fr.x(IDY, t, vv); }, [&](int vv, int j) { return sm.Sv[vv][j]; }, N);
         if (!ext) {
-            auto bh = [&](int s, int j) { return F[FBH][s][j]; };
-            auto kh = [&](int s, int j) { return F[FKH][s][j]; };
-            block_mm_s(L, N, outA, sA, seg([&](int t, int s) { return sm.dM[0][t][s]; }, bh, L),
-                       seg([&](int t, int s) { return sm.dM[1][t][s]; }, kh, L));
-            block_mm_s(L, N, outR, sR, seg([&](int t, int s) { return sm.dM[2][t][s]; }, bh, L),
-                       seg([&](int t, int s) { return sm.dM[3][t][s]; }, kh, L));
+            auto bh_ = [&](int s, int j) { return F[FBH][s][j]; };
+            auto kh_ = [&](int s, int j) { return F[FKH][s][j]; };
+            block_mm_s(L, N, outA, sA, seg([&](int t, int s) { return sm.dM[0][t][s]; }, bh_, L),
+                       seg([&](int t, int s) { return sm.dM[1][t][s]; }, kh_, L));
+            block_mm_s(L, N, outR, sR, seg([&](int t, int s) { return sm.dM[2][t][s]; }, bh_, L),
+                       seg([&](int t, int s) { return sm.dM[3][t][s]; }, kh_, L));
         } else {
             block_mm_s(L, N, outA, sA);
             block_mm_s(L, N, outR, sR);
         }
     }
     block_mm(L, N, N, [&](int t, int vv) { return sm.U[t][vv]; }, [&](int vv, int j) { return sm.D[j][vv]; },
-             [&](int t, int j, float val) {  // dBb: Bb = b e^{c_L - c_t}
-                 const float q = val * F[FBB][t][j];
-                 sm.dB[t][j] += val * expf(fr.c[L - 1][j] - fr.c[t][j]);
-                 sm.dC[t][j] -= q;
-                 sm.Q[t][j] += q;
+             [&](int t, int j, float val, int q) {  // dBb: Bb = b e^{c_L - c_t}
+                 const float qq = val * F[FBB][t][j];
+                 acc.dB[q] += val * expf(fr.c[L - 1][j] - fr.c[t][j]);
+                 acc.dC[q] -= qq;
+                 acc.Q[q] += qq;
              });
     block_mm_s(L, N,
-               [&](int t, int j, float val) {  // dKb: Kb = k e^{c_L - c_t}
-                   const float q = val * F[FKB][t][j];
-                   sm.dK[t][j] += val * expf(fr.c[L - 1][j] - fr.c[t][j]);
-                   sm.dC[t][j] -= q;
-                   sm.Q[t][j] += q;
+               [&](int t, int j, float val, int q) {  // dKb: Kb = k e^{c_L - c_t}
+                   const float qq = val * F[FKB][t][j];
+                   acc.dK[q] += val * expf(fr.c[L - 1][j] - fr.c[t][j]);
+                   acc.dC[q] -= qq;
+                   acc.Q[q] += qq;
                },
-               seg<EXI, false>([&](int t, int vv) { return IN[IV][t][vv]; }, [&](int vv, int j) { return sm.D[j][vv]; }, N));
+               seg<EXI, false>([&](int t, int vv) { return fr.x(IV, t, vv); }, [&](int vv, int j) { return sm.D[j][vv]; }, N));
+    float* scr = &sm.Sv[0][0];  // Sv and D are free from here on: 2 * 64 * LDC floats of scratch
+    constexpr int SA = L * LDC;  // one 16 x 64 scratch array
     if (!ext) {
         auto at = [&](int t, int j) { return F[FAT][t][j]; };
         auto rt = [&](int t, int j) { return F[FRT][t][j]; };
         block_mm_s(
             L, N,
-            [&](int s, int j, float val) {  // dBh = dMab^T At + dMrb^T Rt
-                sm.dB[s][j] += val * expf(-fr.c[s][j]);
-                sm.dC[s][j] -= val * F[FBH][s][j];
+            [&](int s, int j, float val, int q) {  // dBh = dMab^T At + dMrb^T Rt
+                acc.dB[q] += val * expf(-fr.c[s][j]);
+                acc.dC[q] -= val * F[FBH][s][j];
             },
             seg([&](int s, int t) { return sm.dM[0][t][s]; }, at, L), seg([&](int s, int t) { return sm.dM[2][t][s]; }, rt, L));
         block_mm_s(
             L, N,
-            [&](int s, int j, float val) {  // dKh = dMak^T At + dMrk^T Rt
-                sm.dK[s][j] += val * expf(-fr.c[s][j]);
-                sm.dC[s][j] -= val * F[FKH][s][j];
+            [&](int s, int j, float val, int q) {  // dKh = dMak^T At + dMrk^T Rt
+                acc.dK[q] += val * expf(-fr.c[s][j]);
+                acc.dC[q] -= val * F[FKH][s][j];
             },
             seg([&](int s, int t) { return sm.dM[1][t][s]; }, at, L), seg([&](int s, int t) { return sm.dM[3][t][s]; }, rt, L));
     } else {
         // element-wise: each term x_t y_s e^{c_p - c_s} (p = t-1 for Mab/Mak, t for Mrb/Mrk);
-        // thread (i, j) forms the a/r terms of row i and the b/k terms of column i
+        // thread (i, j) forms the a/r terms of row i and the b/k terms of column i into
+        // scratch, then every thread adds the elements it owns into its registers
         __syncthreads();
         for (int e = tid; e < L * N; e += NT) {
             const int i = e / N, j = e % N;
@@ -703,52 +729,82 @@ __global__ void __launch_bounds__(NT, 1)
             float ga = 0.f, gr = 0.f, gb = 0.f, gk = 0.f;
             for (int s = 0; s < L; s++) {
                 const float cs = fr.c[s][j];
-                if (s < i) ga = fmaf(sm.dM[0][i][s] * IN[IB][s][j] + sm.dM[1][i][s] * IN[IK][s][j], expf(cpi - cs), ga);
-                if (s <= i) gr = fmaf(sm.dM[2][i][s] * IN[IB][s][j] + sm.dM[3][i][s] * IN[IK][s][j], expf(ci - cs), gr);
+                if (s < i) ga = fmaf(sm.dM[0][i][s] * fr.x(IB, s, j) + sm.dM[1][i][s] * fr.x(IK, s, j), expf(cpi - cs), ga);
+                if (s <= i) gr = fmaf(sm.dM[2][i][s] * fr.x(IB, s, j) + sm.dM[3][i][s] * fr.x(IK, s, j), expf(ci - cs), gr);
             }
             for (int t = 0; t < L; t++) {
                 const float ct = fr.c[t][j], cpt = t ? fr.c[t - 1][j] : 0.f;
                 if (t > i) {
-                    const float e1 = expf(cpt - ci) * IN[IA][t][j];
+                    const float e1 = expf(cpt - ci) * fr.x(IA, t, j);
                     gb = fmaf(sm.dM[0][t][i], e1, gb);
                     gk = fmaf(sm.dM[1][t][i], e1, gk);
                 }
                 if (t >= i) {
-                    const float e2 = expf(ct - ci) * IN[IR][t][j];
+                    const float e2 = expf(ct - ci) * fr.x(IR, t, j);
                     gb = fmaf(sm.dM[2][t][i], e2, gb);
                     gk = fmaf(sm.dM[3][t][i], e2, gk);
                 }
             }
-            sm.dA[i][j] += ga;
-            sm.dCp[i][j] += ga * IN[IA][i][j];
-            sm.dR[i][j] += gr;
-            sm.dC[i][j] += gr * IN[IR][i][j] - gb * IN[IB][i][j] - gk * IN[IK][i][j];
-            sm.dB[i][j] += gb;
-            sm.dK[i][j] += gk;
+            const int o = i * LDC + j;
+            scr[0 * SA + o] = ga;
+            scr[1 * SA + o] = ga * fr.x(IA, i, j);
+            scr[2 * SA + o] = gr;
+            scr[3 * SA + o] = gr * fr.x(IR, i, j) - gb * fr.x(IB, i, j) - gk * fr.x(IK, i, j);
+            scr[4 * SA + o] = gb;
+            scr[5 * SA + o] = gk;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const int o = own_t(q) * LDC + own_j(q);
+            acc.dA[q] += scr[0 * SA + o];
+            acc.dCp[q] += scr[1 * SA + o];
+            acc.dR[q] += scr[2 * SA + o];
+            acc.dC[q] += scr[3 * SA + o];
+            acc.dB[q] += scr[4 * SA + o];
+            acc.dK[q] += scr[5 * SA + o];
         }
     }
     __syncthreads();
     // decay: l_t = -exp(w_t); d l_tau = sum_{t >= tau} dc_t + dc_L;  dw = dl * l
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        const int o = own_t(q) * LDC + own_j(q);
+        scr[0 * SA + o] = acc.dC[q];
+        scr[1 * SA + o] = acc.dCp[q];
+        scr[2 * SA + o] = acc.Q[q];
+    }
+    __syncthreads();
     if (tid < N) {
         const int j = tid;
         float dcl = sm.dGL[j];
-        for (int t = 0; t < L; t++) dcl += sm.Q[t][j];
-        float acc = dcl;
+        for (int t = 0; t < L; t++) dcl += scr[2 * SA + t * LDC + j];
+        float accd = dcl;
         for (int t = L - 1; t >= 0; t--) {
-            acc += sm.dC[t][j] + (t + 1 < L ? sm.dCp[t + 1][j] : 0.f);
-            sm.Q[t][j] = acc * IN[IL][t][j];  // dw_t
+            accd += scr[0 * SA + t * LDC + j] + (t + 1 < L ? scr[1 * SA + (t + 1) * LDC + j] : 0.f);
+            if (t < nt) dw[base + (size_t)(t0 + t) * tstride + j] = from_f32<T>(accd * fr.inl[t][j]);  // dw_t
         }
     }
-    __syncthreads();
-    for (int e = tid; e < nt * N; e += NT) {
-        const int t = e / N, j = e % N;
-        const size_t off = base + (size_t)(t0 + t) * tstride + j;
-        dr[off] = from_f32<T>(sm.dR[t][j]);
-        dw[off] = from_f32<T>(sm.Q[t][j]);
-        dk[off] = from_f32<T>(sm.dK[t][j]);
-        dv[off] = from_f32<T>(sm.dV[t][j]);
-        da[off] = from_f32<T>(sm.dA[t][j]);
-        db[off] = from_f32<T>(sm.dB[t][j]);
+    // the other gradients straight from registers: two adjacent columns per row
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+        const int t = own_t(2 * h), j = own_j(2 * h);
+        if (t < nt) {
+            const size_t off = base + (size_t)(t0 + t) * tstride + j;
+            auto st2 = [&](T* dst, float x0, float x1) {
+                if constexpr (sizeof(T) == 2) {
+                    T pr[2] = {from_f32<T>(x0), from_f32<T>(x1)};
+                    *reinterpret_cast<uint32_t*>(dst + off) = *reinterpret_cast<const uint32_t*>(pr);
+                } else {
+                    *reinterpret_cast<float2*>(dst + off) = make_float2(x0, x1);
+                }
+            };
+            st2(dr, acc.dR[2 * h], acc.dR[2 * h + 1]);
+            st2(dk, acc.dK[2 * h], acc.dK[2 * h + 1]);
+            st2(dv, acc.dV[2 * h], acc.dV[2 * h + 1]);
+            st2(da, acc.dA[2 * h], acc.dA[2 * h + 1]);
+            st2(db, acc.dB[2 * h], acc.dB[2 * h + 1]);
+        }
     }
 }
 
@@ -763,7 +819,7 @@ static int launch_bwd_chunked(const WkvBwdArgs& p, float* ws, cudaStream_t st) {
     using namespace bwdc;
     auto k1 = wkv7_bwd_chain_ws_kernel<T, TW>;
     auto k2 = wkv7_bwd_chunk_kernel<T, TW>;
-    const int s1 = (int)sizeof(P1WSmem<T, TW>), s2 = (int)sizeof(P2Smem);
+    const int s1 = (int)sizeof(P1WSmem<T, TW>), s2 = (int)sizeof(P2Smem<T>);
     cudaError_t e = cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, s1);
     if (e == cudaSuccess) e = cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, s2);
     if (e != cudaSuccess) return set_cuda_error(e);

@@ -301,8 +301,8 @@ __global__ void __launch_bounds__(NT, 1) wkv7_fwd_tc_kernel(const TcArgs p) {
             if (t == 15) sts8(&stg.GL[j0], ec);
             const bool extreme = group_sync_or(BAR, ext);
 
-            // ---- P2: intra-chunk matrices ----
-            if (!extreme) {
+            // ---- P2: intra-chunk matrices (the transition pass needs only Mab, Mak) ----
+            if (!extreme && (!TRANS || pw < 2)) {
                 const float(*Am)[LD4] = (pw >> 1) ? ps.Rt : ps.At;
                 const float(*Bm)[LD4] = (pw & 1) ? ps.Kh : ps.Bh;
                 float acc2[2][4] = {};
@@ -329,8 +329,8 @@ __global__ void __launch_bounds__(NT, 1) wkv7_fwd_tc_kernel(const TcArgs p) {
                         Mo[tt][sidx] = (pw == 0) ? val : tf32f(val);
                     }
                 }
-            } else {
-                for (int e = pt; e < 4 * L * L; e += 128) {
+            } else if (extreme) {
+                for (int e = pt; e < (TRANS ? 2 : 4) * L * L; e += 128) {
                     const int which = e / (L * L), tt = (e / L) % L, sidx = e % L;
                     const bool strict = which < 2;
                     float val = 0.f;
@@ -372,8 +372,17 @@ __global__ void __launch_bounds__(NT, 1) wkv7_fwd_tc_kernel(const TcArgs p) {
             }
             group_sync(BAR);
 
-            // ---- P5: Wy = Rt + Mrb Wu (WB rows 16-31); Gu^T, Gy^T = Mrb Gu^T + Mrk (BX rows 0-31) ----
-            {
+            // ---- P5: Wy = Rt + Mrb Wu (WB rows 16-31); Gu^T, Gy^T = Mrb Gu^T + Mrk (BX rows 0-31).
+            //      The transition pass produces no y: only Gu^T is needed (Wy, Gy rows stay unused) ----
+            if constexpr (TRANS) {
+                if (pw == 1) {
+#pragma unroll
+                    for (int i = 0; i < (L * L) / 32; i++) {
+                        const int q = lane + 32 * i, tp = q / L, ss = q % L;
+                        *reinterpret_cast<float*>(stg.BX + kmaj(tp, ss, SBO_K16)) = ps.GuT[tp][ss];
+                    }
+                }
+            } else {
                 auto ldB = [&](const unsigned char* src, int kk, int nn) {
                     return fbits(*reinterpret_cast<const float*>(src + kmaj(kk, nn, SBO_K64)));
                 };

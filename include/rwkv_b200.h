@@ -57,7 +57,9 @@ int rwkv_abi_version(void);
 int rwkv_device_error(int clear);
 /* Test hooks, no counterpart in the reference: make every bounded wait of the
  * tcgen05 WKV-7 forward give up at once (on != 0), exercising its abort path
- * without any real stall; set the device error word of that kernel directly.  */
+ * without any real stall; set the device error words of the tcgen05 WKV-7 forward
+ * and of the chunked backward directly (a chunked backward that finds its word set
+ * writes NaN gradients: its first pass gave up, or an earlier error is unread).  */
 int rwkv_debug_force_wait_timeout(int on);
 int rwkv_debug_set_device_error(int value);
 /* Select the WKV-7 forward kernel: 0 automatic (with all per-token inputs 16-byte

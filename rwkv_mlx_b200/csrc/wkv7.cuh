@@ -30,6 +30,7 @@ bool wkv7_tc_supported(int dtype);
 int read_device_error_tc(int clear);
 int set_force_wait_timeout_tc(int on);
 int set_device_error_tc(int value);
+int set_device_error_bwd(int value);
 int read_device_error_bwd(int clear);
 int read_device_error(int clear);
 int read_device_error_moe(int clear);

@@ -104,7 +104,10 @@ extern "C" int rwkv_set_wkv_segments(int nseg) {
 
 extern "C" int rwkv_debug_force_wait_timeout(int on) { return set_force_wait_timeout_tc(on); }
 
-extern "C" int rwkv_debug_set_device_error(int value) { return set_device_error_tc(value); }
+extern "C" int rwkv_debug_set_device_error(int value) {
+    const int rc = set_device_error_tc(value);
+    return rc ? rc : set_device_error_bwd(value);
+}
 
 extern "C" int rwkv_wkv7_backward(const void* r, const void* w, const void* k, const void* v,
                                   const void* a, const void* b, const void* dy, const float* s0,

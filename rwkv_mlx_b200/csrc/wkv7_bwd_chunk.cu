@@ -604,6 +604,17 @@ __global__ void __launch_bounds__(NT, 2)
 #pragma unroll
     for (int q = 0; q < 4; q++)
         acc.dA[q] = acc.dR[q] = acc.dB[q] = acc.dK[q] = acc.dV[q] = acc.dC[q] = acc.dCp[q] = acc.Q[q] = 0.f;
+    if (*(volatile int*)&g_device_error_bwd) {
+        // pass 1 (earlier on this stream) gave up a bounded wait, so dX_L is not valid: no
+        // gradient of this backward may look valid either (the word stays set until read
+        // and cleared through rwkv_device_error / check_device_error)
+        for (int e = tid; e < nt * N; e += NT) {
+            const size_t off = base + (size_t)(t0 + e / N) * tstride + (e % N);
+            const T nan = from_f32<T>(__int_as_float(0x7fc00000));
+            dr[off] = nan, dw[off] = nan, dk[off] = nan, dv[off] = nan, da[off] = nan, db[off] = nan;
+        }
+        return;
+    }
 
     {
         const float* S = c == 0 ? (s0 ? s0 + (size_t)bh * N * N : nullptr) : ckpt + ((size_t)bh * (T_ / L) + c - 1) * N * N;
@@ -835,6 +846,10 @@ static int launch_bwd_chunked(const WkvBwdArgs& p, float* ws, cudaStream_t st) {
 }
 
 int read_device_error_bwd(int clear) { return bwdc::read_error_word(clear); }
+
+int set_device_error_bwd(int value) {
+    return set_cuda_error(cudaMemcpyToSymbol(bwdc::g_device_error_bwd, &value, sizeof(int)));
+}
 
 int wkv7_bwd_chunked(const WkvBwdArgs& p, float* ws, cudaStream_t st) {
     RWKV_DISPATCH_DTYPE_W(p.dtype, p.w_dtype, T, TW, return launch_bwd_chunked<T, TW>(p, ws, st));

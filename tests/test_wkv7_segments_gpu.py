@@ -129,3 +129,30 @@ def test_forced_wait_timeout_fills_outputs_with_nan(nseg):
     rb.check_device_error()
     ye = wo.wkv7_forward_exact(h["r"], h["w"], h["k"], h["v"], h["a"], h["b"])[0]
     assert rel_rms(y2.double().cpu().numpy(), _bt(ye)) < 2e-3
+
+
+def test_backward_after_an_abort_returns_nan_gradients():
+    """A set backward error word (here set from the host, as a pass-1 abort would set it)
+    makes the chunked backward write NaN gradients instead of values built on an
+    invalid state-gradient chain; once the error is read and cleared it is exact again."""
+    import rwkv_mlx_b200 as rb
+    from rwkv_mlx_b200 import _native, wkv7
+
+    B, T, H = 1, 96, 2
+    d, h = _inputs(B, T, H, seed=12, dt=torch.float16)
+    dy = torch.tensor(_bt(wkv_inputs(B, T, H, seed=12)["dy"]), dtype=torch.float16, device="cuda")
+    _, ck, _, _ = wkv7._fwd(d["r"], d["w"], d["k"], d["v"], d["a"], d["b"], want_ckpt=True)
+    torch.cuda.synchronize()
+    rb.check_device_error()
+    _native.check(_native.lib().rwkv_debug_set_device_error(1), "rwkv_debug_set_device_error")
+    grads, _ = wkv7._bwd(d["r"], d["w"], d["k"], d["v"], d["a"], d["b"], dy, ck)
+    torch.cuda.synchronize()
+    assert all(torch.isnan(g).all() for g in grads)
+    with pytest.raises(rb.RwkvDeviceError):
+        rb.check_device_error()
+    grads, _ = wkv7._bwd(d["r"], d["w"], d["k"], d["v"], d["a"], d["b"], dy, ck)
+    torch.cuda.synchronize()
+    rb.check_device_error()
+    ge = wo.wkv7_backward_exact(h["r"], h["w"], h["k"], h["v"], h["a"], h["b"], dy.double().cpu().numpy().reshape(B, T, H, 64))
+    for g, e in zip(grads, ge[:6]):
+        assert rel_rms(g.double().cpu().numpy(), _bt(e)) < 2e-3

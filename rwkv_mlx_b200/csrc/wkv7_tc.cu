@@ -412,35 +412,27 @@ __global__ void __launch_bounds__(NT, 1) wkv7_fwd_tc_kernel(const TcArgs p) {
                         *reinterpret_cast<float*>(stg.WB + kmaj(tt, col, SBO_K64)) = tf32f(wy[nt][e]);
                     }
                 }
-                if (pw == 0) {
-                    float gy[2][4];
-#pragma unroll
-                    for (int nt = 0; nt < 2; nt++) {
-                        const int n0 = 8 * nt + 2 * tg;
-                        gy[nt][0] = ps.Mrk[g][n0], gy[nt][1] = ps.Mrk[g][n0 + 1];
-                        gy[nt][2] = ps.Mrk[g + 8][n0], gy[nt][3] = ps.Mrk[g + 8][n0 + 1];
-                    }
+                // Gy^T = Mrb Gu^T + Mrk: one 16x8 tile each for warps 2 and 3; Gu^T copied
+                // into BX by warps 0 and 1 (half each), so the four warps finish together
+                if (pw >= 2) {
+                    const int nt = pw - 2, n0 = 8 * nt + 2 * tg;
+                    float gy[4] = {ps.Mrk[g][n0], ps.Mrk[g][n0 + 1], ps.Mrk[g + 8][n0], ps.Mrk[g + 8][n0 + 1]};
 #pragma unroll
                     for (int ks = 0; ks < 2; ks++) {
                         const int k0 = 8 * ks;
                         const uint32_t a0 = fbits(ps.Mrb[g][k0 + tg]), a1 = fbits(ps.Mrb[g + 8][k0 + tg]);
                         const uint32_t a2 = fbits(ps.Mrb[g][k0 + tg + 4]), a3 = fbits(ps.Mrb[g + 8][k0 + tg + 4]);
-#pragma unroll
-                        for (int nt = 0; nt < 2; nt++)
-                            mma8(gy[nt], a0, a1, a2, a3, fbits(ps.GuT[k0 + tg][8 * nt + g]), fbits(ps.GuT[k0 + tg + 4][8 * nt + g]));
+                        mma8(gy, a0, a1, a2, a3, fbits(ps.GuT[k0 + tg][8 * nt + g]), fbits(ps.GuT[k0 + tg + 4][8 * nt + g]));
                     }
 #pragma unroll
-                    for (int nt = 0; nt < 2; nt++) {
-#pragma unroll
-                        for (int e = 0; e < 4; e++) {
-                            const int tp = g + (e >> 1) * 8, ss = 8 * nt + 2 * tg + (e & 1);
-                            *reinterpret_cast<float*>(stg.BX + kmaj(L + tp, ss, SBO_K16)) = tf32f(gy[nt][e]);
-                        }
+                    for (int e = 0; e < 4; e++) {
+                        const int tp = g + (e >> 1) * 8, ss = 8 * nt + 2 * tg + (e & 1);
+                        *reinterpret_cast<float*>(stg.BX + kmaj(L + tp, ss, SBO_K16)) = tf32f(gy[e]);
                     }
-                } else if (pw == 1) {
+                } else {
 #pragma unroll
-                    for (int i = 0; i < (L * L) / 32; i++) {
-                        const int q = lane + 32 * i, tp = q / L, ss = q % L;
+                    for (int i = 0; i < (L * L) / 64; i++) {
+                        const int q = lane + 32 * (2 * i + pw), tp = q / L, ss = q % L;
                         *reinterpret_cast<float*>(stg.BX + kmaj(tp, ss, SBO_K16)) = ps.GuT[tp][ss];
                     }
                 }

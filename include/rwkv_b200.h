@@ -289,6 +289,18 @@ int rwkv_moe_expert_mix_rows(const void* x, const void* prev, const void* x_k,
                              const int32_t* perm, const int32_t* offsets, void* rows, int n,
                              int T, int C, int topk, int E, int dtype, void* stream);
 
+/* Grouped GEMM on the tcgen05 tensor cores (fp16 / bf16, fp32 accumulation):
+ *   out[m, :] = epi(A[m, :] @ W[g]^T) for the rows m in [offs[g], offs[g+1]),
+ * the expert products of MoE_CMix.__call__ (moe.py:231-236: key, squared ReLU,
+ * value) over the rows that rwkv_moe_expert_mix_rows sorted by expert.  The
+ * offsets stay on the device (no host read: the call can be captured in a CUDA
+ * graph); offs NULL with G = 1 is a plain GEMM over rows [0, M).
+ * A (M, K), W (G, N, K), out (M, ldo) row-major in dtype, 16-byte aligned;
+ * K % 8 == 0.  epi 0: the product rounded to dtype; epi 1: relu(.)^2 of the
+ * product rounded to dtype (moe.py:234).  Rows outside every group are not written. */
+int rwkv_grouped_gemm(const void* a, const void* w, const int32_t* offs, void* out, int M, int N, int K,
+                      int G, long long ldo, int epi, int dtype, void* stream);
+
 /* sum_{i<j} ||A_i^T A_j||_F^2 over the expert down-projections
  * (LoRAMoE_CMix.orthogonal_loss, moe.py:149-163).  A (E, C, R) dtype;
  * out: one fp32 scalar.  R <= 64.                                          */
@@ -365,6 +377,23 @@ int rwkv_add_layernorm(const void* x, const void* delta, const void* w, const vo
  *   written to dlogits (row stride ld_out), in dtype; with scaled = 0 the values are
  *   multiplied by den / *g (O(1) entries for 16-bit types; the caller scales the
  *   products it forms from them by *g / den).                                */
+/* Fused output head + loss statistics on the tcgen05 tensor cores: for token i,
+ * the logits x[i] @ head^T (head (V, K), rounded to dtype as the reference's head
+ * output is) are folded into the rwkv_ce_chunk state float4 of all V columns at
+ * once inside the GEMM epilogue; no logit is written to memory.  x (M, K) and
+ * head in dtype (fp16 / bf16), 16-byte aligned, K % 8 == 0; workspace of
+ * rwkv_head_ce_workspace_size(M, V) bytes (16-byte aligned).  Follow with
+ * rwkv_ce_finalize.
+ * rwkv_head_ce_grad: rwkv_ce_chunk_grad of the vocabulary columns
+ * [col0, col0 + ncols) with the logits recomputed from x and the head rows
+ * w = head + col0 * K (ncols of them) instead of read from memory. */
+size_t rwkv_head_ce_workspace_size(int M, int V);
+int rwkv_head_ce_stats(const void* x, const void* head, const int32_t* targets, float* state, int M, int V,
+                       int K, void* workspace, size_t workspace_bytes, int dtype, void* stream);
+int rwkv_head_ce_grad(const void* x, const void* w, const int32_t* targets, const float* state,
+                      const float* mask, const float* out, const float* g, float l2_factor, int scaled,
+                      void* dlogits, long long ld_out, int M, int ncols, int K, int col0, int dtype,
+                      void* stream);
 int rwkv_ce_chunk(const void* logits, long long ld, const int32_t* targets, float* state, int ntok,
                   int col0, int ncols, int first, int dtype, void* stream);
 int rwkv_ce_finalize(const float* state, const float* mask, float l2_factor, float* out, int ntok,

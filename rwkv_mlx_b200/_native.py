@@ -66,6 +66,10 @@ SIGNATURES = {
     "rwkv_moe_lora_up": (_I, [_P] * 5 + [_I] * 5 + [_P]),
     "rwkv_moe_combine_rows": (_I, [_P] * 5 + [_I] * 4 + [_P]),
     "rwkv_moe_expert_mix_rows": (_I, [_P] * 6 + [_I] * 6 + [_P]),
+    "rwkv_grouped_gemm": (_I, [_P] * 4 + [_I] * 4 + [ctypes.c_longlong, _I, _I, _P]),
+    "rwkv_head_ce_workspace_size": (_SZ, [_I, _I]),
+    "rwkv_head_ce_stats": (_I, [_P] * 4 + [_I] * 3 + [_P, _SZ, _I, _P]),
+    "rwkv_head_ce_grad": (_I, [_P] * 7 + [ctypes.c_float, _I, _P, ctypes.c_longlong] + [_I] * 5 + [_P]),
     "rwkv_ce_chunk": (_I, [_P, ctypes.c_longlong, _P, _P] + [_I] * 5 + [_P]),
     "rwkv_ce_finalize": (_I, [_P, _P, ctypes.c_float, _P, _I, _P]),
     "rwkv_ce_chunk_grad": (_I, [_P, ctypes.c_longlong] + [_P] * 5 + [ctypes.c_float, _I, _P, ctypes.c_longlong]
@@ -127,6 +131,7 @@ KERNELS_PER_CALL = {
     "rwkv_moe_lora_up": 1, "rwkv_moe_combine_rows": 1, "rwkv_lerp": 1, "rwkv_lerp_prev": 1, "rwkv_lerp_prev_state": 1, "rwkv_tmix_mid": 1,
     "rwkv_tmix_post": 1, "rwkv_relu_sq": 1, "rwkv_lora_act": 1, "rwkv_argmax_rows": 1, "rwkv_add_layernorm": 1, "rwkv_moe_expert_mix_rows": 1,
     "rwkv_ce_chunk": 1, "rwkv_ce_finalize": 1, "rwkv_ce_chunk_grad": 1,
+    "rwkv_grouped_gemm": 1, "rwkv_head_ce_stats": 2, "rwkv_head_ce_grad": 1,
 }
 launch_count = 0
 

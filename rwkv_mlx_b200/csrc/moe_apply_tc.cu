@@ -34,11 +34,7 @@
 // read the same adapter slice from L2 at the same moment.
 // Every wait is bounded: a wait that gives up sets the CTA's abort flag and the device
 // error word, and every role leaves its loop.
-#include <cuda.h>
-
-#include <mutex>
-
-#include "tc_common.cuh"
+#include "tma_common.cuh"
 
 namespace rwkv {
 
@@ -46,6 +42,7 @@ __device__ int g_device_error_moe;  // set by a kernel that gave up a bounded wa
 
 namespace atc {
 using namespace tcc;
+using namespace tma;
 
 constexpr int TM = 128;  // tokens per tile
 constexpr int KS = 64;   // channels per down slice (one 128-byte swizzle row of x)
@@ -89,57 +86,6 @@ struct Ctrl {
 };
 static_assert(sizeof(Ctrl) <= 1024, "control block");
 
-// 128-byte-swizzled (layout type 2) shared-memory descriptor
-__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
-    return umma_desc_ls(saddr, lbo, sbo) | (2ull << 61);
-}
-
-__device__ __forceinline__ void expect_tx(unsigned long long* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(ck::smem_u32(bar)), "r"(bytes)
-                 : "memory");
-}
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* m, int x, int y, unsigned long long* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-            ck::smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(m)), "r"(x), "r"(y), "r"(ck::smem_u32(bar))
-        : "memory");
-}
-__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* m, int x, int y, int z, int w,
-                                            unsigned long long* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(
-            ck::smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(m)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(ck::smem_u32(bar))
-        : "memory");
-}
-// untiled bulk copy global -> shared (16-byte aligned, size a multiple of 16)
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, unsigned long long* bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     ck::smem_u32(dst)),
-                 "l"(src), "r"(bytes), "r"(ck::smem_u32(bar))
-                 : "memory");
-}
-// out += box (element-wise add in the memory system, in the tensor map's type)
-__device__ __forceinline__ void tma_add_2d(const CUtensorMap* m, int x, int y, const void* src) {
-    asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
-                     reinterpret_cast<uint64_t>(m)),
-                 "r"(x), "r"(y), "r"(ck::smem_u32(src))
-                 : "memory");
-    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-}
-__device__ __forceinline__ void tma_store_2d(const CUtensorMap* m, int x, int y, const void* src) {
-    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
-                     reinterpret_cast<uint64_t>(m)),
-                 "r"(x), "r"(y), "r"(ck::smem_u32(src))
-                 : "memory");
-    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-}
-template <int N>
-__device__ __forceinline__ void bulk_wait_read() {
-    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
-}
-__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // Job order of a CTA with nt tiles and n slices (= chunks) per tile: the down slices of
 // tile 0, then pairs (down slice j of tile t + 1, up chunk j of tile t), then the up
@@ -523,45 +469,6 @@ __global__ void __launch_bounds__(atc::NTH, 1)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
     }
 }
-
-namespace atc {
-// APPLY_TC_NO_MAPS (common.cuh): the tensor maps could not be built (before anything
-// was launched); the automatic kernel choice then runs the mma.sync kernel instead
-using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-// cuTensorMapEncodeTiled through the runtime's driver entry point (no link-time
-// dependency on the driver library).
-static EncodeFn encoder() {
-    static EncodeFn fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeFn>(p);
-    });
-    return fn;
-}
-
-// Tensor map of rank `rank` over `base` (dims[0] contiguous; strides in bytes for
-// dims 1..rank-1), box `box`, zero fill out of bounds.
-static int make_map(CUtensorMap* m, bool bf16, const void* base, int rank, const cuuint64_t* dims,
-                    const cuuint64_t* strides, const cuuint32_t* box, bool swizzle128) {
-    EncodeFn enc = encoder();
-    if (!enc) return set_error(APPLY_TC_NO_MAPS, "cuTensorMapEncodeTiled is not available");
-    const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
-    const CUresult r = enc(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                           (cuuint32_t)rank, const_cast<void*>(base), dims, strides, box, estr,
-                           CU_TENSOR_MAP_INTERLEAVE_NONE,
-                           swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
-                           CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return set_error(APPLY_TC_NO_MAPS, "cuTensorMapEncodeTiled rejected a tensor map");
-    return RWKV_OK;
-}
-}  // namespace atc
 
 // Gate operand of the routed variant: W (E, C) fp32 split into W0 = fp16(W) and
 // W1 = fp16((W - W0) * 2048) (every fp16 x fp16 product is exact in fp32, so the logits

@@ -34,6 +34,10 @@ int set_device_error_bwd(int value);
 int read_device_error_bwd(int clear);
 int read_device_error(int clear);
 int read_device_error_moe(int clear);
+// grouped tcgen05 GEMM (gemm_tc.cu): error word and test hooks
+int read_device_error_gemm(int clear);
+int set_force_wait_timeout_gemm(int on);
+int set_device_error_gemm(int value);
 extern int g_wkv_impl;  // 0 auto, 1 step-sequential, 2 chunked (mma.sync), 3 chunked (tcgen05)
 int wkv7_bwd_seq(const WkvBwdArgs& p, cudaStream_t st);
 size_t wkv7_bwd_chunk_ws_bytes(int B, int T, int H);

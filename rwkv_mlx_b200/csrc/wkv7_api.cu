@@ -102,11 +102,15 @@ extern "C" int rwkv_set_wkv_segments(int nseg) {
     return RWKV_OK;
 }
 
-extern "C" int rwkv_debug_force_wait_timeout(int on) { return set_force_wait_timeout_tc(on); }
+extern "C" int rwkv_debug_force_wait_timeout(int on) {
+    const int rc = set_force_wait_timeout_tc(on);
+    return rc ? rc : set_force_wait_timeout_gemm(on);
+}
 
 extern "C" int rwkv_debug_set_device_error(int value) {
-    const int rc = set_device_error_tc(value);
-    return rc ? rc : set_device_error_bwd(value);
+    int rc = set_device_error_tc(value);
+    if (!rc) rc = set_device_error_bwd(value);
+    return rc ? rc : set_device_error_gemm(value);
 }
 
 extern "C" int rwkv_wkv7_backward(const void* r, const void* w, const void* k, const void* v,

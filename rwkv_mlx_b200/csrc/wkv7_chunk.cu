@@ -511,10 +511,12 @@ int read_device_error(int clear) {
 
 extern "C" int rwkv_device_error(int clear) {
     const int a = rwkv::read_device_error(clear), b = rwkv::read_device_error_tc(clear),
-              c = rwkv::read_device_error_bwd(clear), d = rwkv::read_device_error_moe(clear);
+              c = rwkv::read_device_error_bwd(clear), d = rwkv::read_device_error_moe(clear),
+              e = rwkv::read_device_error_gemm(clear);
     if (a < 0) return a;
     if (b < 0) return b;
     if (c < 0) return c;
     if (d < 0) return d;
-    return a | b | c | d;
+    if (e < 0) return e;
+    return a | b | c | d | e;
 }

@@ -5,13 +5,14 @@ Reference (rwkv_mlx/train.py):
   * ``l2_wrap_loss_masked(logits, targets, mask)`` (:337-362) -> :func:`l2_wrap_loss_masked`
     mean (or mask-weighted mean) cross-entropy + 1e-4 / (B*T) * 0.5 * sum (max logit)^2.
 
-:func:`head_l2_wrap_loss` fuses the output head with the loss: the logits
-``x @ head.weight^T`` are formed one vocabulary chunk at a time (a library GEMM) and
-folded into per-token softmax statistics by ``rwkv_ce_chunk``, so that only one chunk of
-logits exists at a time (B=32, T=4096, V=65568 would need 17 GB for all of them in
-fp16).  The backward recomputes each chunk's logits and turns them into
-``d loss / d logits`` with ``rwkv_ce_chunk_grad`` before the two products of the head's
-gradient.  All three functions are autograd functions.
+:func:`head_l2_wrap_loss` fuses the output head with the loss.  For fp16 / bf16 the
+logits ``x @ head.weight^T`` are formed on the tcgen05 tensor cores and folded into
+per-token softmax statistics inside the GEMM's epilogue (``rwkv_head_ce_stats``), so no
+logit is ever written to memory (B=32, T=4096, V=65568 would need 17 GB of them in fp16);
+the backward recomputes one vocabulary chunk at a time and the same kernel writes
+``d loss / d logits`` directly (``rwkv_head_ce_grad``) before the two library products of
+the head's gradient.  Other dtypes form each chunk with a library GEMM and fold it with
+``rwkv_ce_chunk`` / ``rwkv_ce_chunk_grad``.  All three functions are autograd functions.
 """
 
 from __future__ import annotations
@@ -94,16 +95,48 @@ class _LossOnLogits(torch.autograd.Function):
         return dlog, None, None, None
 
 
+def _fused_ok(x2d, weight):
+    """The tcgen05 head kernels take fp16 / bf16 operands of one dtype with C % 8 == 0."""
+    return (x2d.dtype in (torch.float16, torch.bfloat16) and weight.dtype == x2d.dtype
+            and x2d.shape[1] % 8 == 0 and weight.is_contiguous())
+
+
+def _head_stats(x2d, weight, targets, state):
+    n, C = x2d.shape
+    V = weight.shape[0]
+    L = nat.lib()
+    ws_bytes = L.rwkv_head_ce_workspace_size(n, V)
+    ws = torch.empty(max(16, ws_bytes), device=x2d.device, dtype=torch.uint8)
+    with torch.cuda.device(x2d.device):
+        rc = L.rwkv_head_ce_stats(nat.ptr(x2d), nat.ptr(weight), nat.ptr(targets), nat.ptr(state), n, V, C,
+                                  nat.ptr(ws), ws_bytes, nat.dtype_code(x2d), nat.stream_ptr(x2d.device))
+    nat.check(rc, "rwkv_head_ce_stats")
+
+
+def _head_grad(x2d, w_chunk, targets, state, mask, out, g, l2_factor, dlog, col0):
+    n, C = x2d.shape
+    L = nat.lib()
+    with torch.cuda.device(x2d.device):
+        rc = L.rwkv_head_ce_grad(nat.ptr(x2d), nat.ptr(w_chunk), nat.ptr(targets), nat.ptr(state), nat.ptr(mask),
+                                 nat.ptr(out), nat.ptr(g), float(l2_factor), 0, nat.ptr(dlog), dlog.stride(0), n,
+                                 w_chunk.shape[0], C, col0, nat.dtype_code(x2d), nat.stream_ptr(x2d.device))
+    nat.check(rc, "rwkv_head_ce_grad")
+
+
 class _HeadLoss(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x2d, weight, targets, mask, l2_factor, chunk):
         n = x2d.shape[0]
         V = weight.shape[0]
         state = torch.empty((n, 4), device=x2d.device, dtype=torch.float32)
-        for c0 in range(0, V, chunk):
-            c1 = min(V, c0 + chunk)
-            lg = torch.mm(x2d, weight[c0:c1].t())
-            _chunk_stats(lg, c1 - c0, targets, state, c0, c1 - c0, c0 == 0)
+        if _fused_ok(x2d, weight):
+            # logits and their softmax statistics in one tcgen05 launch: no logit in HBM
+            _head_stats(x2d, weight, targets, state)
+        else:
+            for c0 in range(0, V, chunk):
+                c1 = min(V, c0 + chunk)
+                lg = torch.mm(x2d, weight[c0:c1].t())
+                _chunk_stats(lg, c1 - c0, targets, state, c0, c1 - c0, c0 == 0)
         out = _finalize(state, mask, l2_factor)
         ctx.save_for_backward(x2d, weight, targets, state, out)
         ctx.mask, ctx.l2_factor, ctx.chunk = mask, l2_factor, chunk
@@ -116,11 +149,16 @@ class _HeadLoss(torch.autograd.Function):
         g = g.to(torch.float32).reshape(1).contiguous()
         dx = torch.zeros(x2d.shape, device=x2d.device, dtype=torch.float32)
         dw = torch.empty_like(weight)
+        fused = _fused_ok(x2d, weight)
         for c0 in range(0, V, ctx.chunk):
             c1 = min(V, c0 + ctx.chunk)
-            lg = torch.mm(x2d, weight[c0:c1].t())
             # unscaled d loss / d logits (O(1) entries); g / den is applied to the products
-            _chunk_grad(lg, c1 - c0, targets, state, ctx.mask, out, g, ctx.l2_factor, False, lg, c0, c1 - c0)
+            if fused:  # logits recomputed and turned into gradients inside one tcgen05 launch
+                lg = torch.empty((x2d.shape[0], c1 - c0), device=x2d.device, dtype=x2d.dtype)
+                _head_grad(x2d, weight[c0:c1], targets, state, ctx.mask, out, g, ctx.l2_factor, lg, c0)
+            else:
+                lg = torch.mm(x2d, weight[c0:c1].t())
+                _chunk_grad(lg, c1 - c0, targets, state, ctx.mask, out, g, ctx.l2_factor, False, lg, c0, c1 - c0)
             dx = _accumulate_fp32(dx, lg, weight[c0:c1])
             dw[c0:c1] = torch.mm(lg.t(), x2d)
         s = g / out[3]

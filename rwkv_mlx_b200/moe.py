@@ -228,6 +228,28 @@ def expert_mix_rows(x2d, prev, x_k, perm, offsets, T: int, top_k: int):
     return rows
 
 
+def grouped_gemm(a: torch.Tensor, w: torch.Tensor, offsets: torch.Tensor | None = None, relu_sq: bool = False,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+    """out[m] = a[m] @ w[g]^T for the rows m in [offsets[g], offsets[g+1]) (squared ReLU of
+    the product when ``relu_sq``), on the tcgen05 grouped GEMM (``rwkv_grouped_gemm``).
+    a (M, K), w (G, N, K) fp16 / bf16; offsets (G+1,) int32 on the device, or None for
+    one group over all rows.  Rows outside every group are left as they were in ``out``."""
+    M, K = a.shape
+    G, N, K2 = w.shape
+    if K2 != K or (offsets is None and G != 1):
+        raise ValueError("grouped_gemm: shape mismatch")
+    a = a.contiguous()
+    w = w.to(a.dtype).contiguous()
+    if out is None:
+        out = torch.empty((M, N), device=a.device, dtype=a.dtype)
+    L = nat.lib()
+    with torch.cuda.device(a.device):
+        rc = L.rwkv_grouped_gemm(nat.ptr(a), nat.ptr(w), nat.ptr(offsets), nat.ptr(out), M, N, K, G, out.stride(0),
+                                 1 if relu_sq else 0, nat.dtype_code(a), _stream(a.device))
+    nat.check(rc, "rwkv_grouped_gemm")
+    return out
+
+
 def combine_rows(base2d, rows, scores, inv, ntok: int):
     """out[t] = base[t] + sum_s scores[t, s] * rows[inv[t * k + s]] (base may be None)."""
     k = scores.shape[-1]
@@ -341,8 +363,14 @@ class MoE_CMix(nn.Module):
         r = router_forward(x2d, self.router.gate.weight, k, self.router.bias)
         perm, inv, offsets = permute(r["inds"], E)
         rows = expert_mix_rows(x2d, prev, self.x_k.detach(), perm, offsets, T, k)
-        # one device -> host read of the E+1 offsets: the library GEMMs below are sized
-        # on the host, one pair per expert over its contiguous rows
+        if dt in (torch.float16, torch.bfloat16):
+            # the expert products on the tcgen05 grouped GEMM, sized on the device from the
+            # offsets (no host read): key + squared ReLU, then value
+            h = grouped_gemm(rows, self.expert_key.detach(), offsets, relu_sq=True)
+            o = grouped_gemm(h, self.expert_val.detach(), offsets)
+            return combine_rows(None, o, r["scores"], inv, ntok), r
+        # fp32 activations: one library GEMM pair per expert over its contiguous rows,
+        # sized on the host (one device -> host read of the E+1 offsets)
         offs = offsets.tolist()
         wk = self.expert_key.detach().to(dt)
         wv = self.expert_val.detach().to(dt)

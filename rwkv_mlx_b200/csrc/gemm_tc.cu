@@ -16,11 +16,12 @@
 //
 // Tiles are 128 rows x 256 columns, K in slices of 64 (one 128-byte swizzle row of a
 // 16-bit operand).  The CTA is persistent over work units and warp-specialised:
-//   warp 4 lane 0   producer: A and W boxes of each K slice by TMA into a 4-stage ring;
-//   warp 5 lane 0   MMA issuer: 4 MMAs (128 x 256 x 16) per slice into one of two
+//   warp 8 lane 0   producer: A and W boxes of each K slice by TMA into a 4-stage ring;
+//   warp 9 lane 0   MMA issuer: 4 MMAs (128 x 256 x 16) per slice into one of two
 //                   256-column accumulators (tiles alternate), commits to the ring's
 //                   "empty" barriers and the accumulator's "full" barrier;
-//   warps 0-3       epilogue: TMEM lane 32 w + l = row of the tile; 32 columns per load.
+//   warps 0-7       epilogue: TMEM lane 32 (w % 4) + l = row of the tile, warps w and w + 4
+//                   take the two 128-column halves; 32 columns per load.
 // Logits and outputs are rounded to the activation type before the epilogue uses them,
 // as the reference's 16-bit matmul result is.  Every wait is bounded: a wait that gives
 // up sets the CTA's abort flag and the device error word, the roles leave their loops,
@@ -42,8 +43,10 @@ using namespace tma;
 
 constexpr int BM = 128, BN = 256, BK = 64, NS = 4;
 constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2, STAGE = A_BYTES + B_BYTES;
-constexpr int NEPI = 128, NTH = NEPI + 64;  // epilogue warps 0-3, producer warp 4, MMA warp 5
-constexpr int CTRL = 1024;
+constexpr int NEPI = 256, NTH = NEPI + 64;  // epilogue warps 0-7, producer warp 8, MMA warp 9
+constexpr int CTRL = 6144;
+constexpr int BAR_EPI = 1;  // named barrier of the epilogue warps
+constexpr int MAXG = 256;   // groups per launch
 constexpr int SMEM = 1024 /* alignment slack */ + CTRL + NS * STAGE;
 static_assert(SMEM <= 227 * 1024, "shared memory");
 
@@ -53,7 +56,11 @@ struct Ctrl {
     unsigned long long full[NS], empty[NS], acc_full[2], acc_empty[2], drain;
     uint32_t tmem_base;
     int abort;
+    float4 ce_half[BM];  // CE: the second column half's statistics of each row
+    int goff[MAXG + 1];  // row offsets of the groups
+    int gunit[MAXG + 1]; // first unit of every group; [G] = number of units
 };
+static_assert(sizeof(Ctrl) <= CTRL, "control block");
 
 struct Args {
     const int32_t* offs;  // G + 1 row offsets, or null: one group of rows [0, M)
@@ -102,39 +109,21 @@ __device__ __forceinline__ void drain_wait(unsigned long long* b, uint32_t parit
     }
 }
 
-// Work unit u -> group g, row tile mt of the group, unit j within the row tile.
+// Work unit u -> group g, row tile mt of the group, unit j within the row tile.  The
+// group table (row offsets and the first unit of every group) is built once per CTA in
+// shared memory, so decoding a unit is a short binary search, not a chain of global loads.
 struct Unit {
     int g, mt, j, row0, rend;
 };
-__device__ __forceinline__ int group_rows(const Args& p, int g, int& r0) {
-    if (!p.offs) {
-        r0 = 0;
-        return p.M;
+__device__ __forceinline__ Unit unit_of(const Args& p, const int* goff, const int* gunit, int u) {
+    int lo = 0, hi = p.G;  // largest g with gunit[g] <= u (empty groups repeat a value)
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (gunit[mid] <= u) lo = mid;
+        else hi = mid;
     }
-    r0 = p.offs[g];
-    return p.offs[g + 1] - r0;
-}
-__device__ __forceinline__ int total_units(const Args& p) {
-    int t = 0;
-    for (int g = 0; g < p.G; g++) {
-        int r0;
-        const int rows = group_rows(p, g, r0);
-        t += rows > 0 ? (rows + BM - 1) / BM * p.nunit_n : 0;
-    }
-    return t;
-}
-__device__ __forceinline__ Unit unit_of(const Args& p, int u) {
-    for (int g = 0; g < p.G; g++) {
-        int r0;
-        const int rows = group_rows(p, g, r0);
-        const int n = rows > 0 ? (rows + BM - 1) / BM * p.nunit_n : 0;
-        if (u < n) {
-            const int mt = u / p.nunit_n;
-            return {g, mt, u % p.nunit_n, r0 + mt * BM, r0 + rows};
-        }
-        u -= n;
-    }
-    return {0, 0, 0, 0, 0};  // not reached for u < total_units
+    const int l = u - gunit[lo], mt = l / p.nunit_n;
+    return {lo, mt, l % p.nunit_n, goff[lo] + mt * BM, goff[lo + 1]};
 }
 // N tiles of unit j: one tile, or a contiguous range of tiles (CE vocabulary split).
 template <int EPI>
@@ -200,18 +189,43 @@ __global__ void __launch_bounds__(gtc::NTH, 1)
         cs.abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
+    if (tid <= p.G) cs.goff[tid] = p.offs ? p.offs[tid] : (tid == 0 ? 0 : p.M);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    if (warp == 0) {  // units per group (empty or negative groups: none), exclusive scan over the groups
+        constexpr int PER = (MAXG + 31) / 32;
+        int loc[PER], sum = 0;
+#pragma unroll
+        for (int i = 0; i < PER; i++) {
+            const int g = lane * PER + i;
+            const int rows = g < p.G ? cs.goff[g + 1] - cs.goff[g] : 0;
+            loc[i] = sum;
+            sum += rows > 0 ? (rows + BM - 1) / BM * p.nunit_n : 0;
+        }
+        int incl = sum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int t = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += t;
+        }
+#pragma unroll
+        for (int i = 0; i < PER; i++) {
+            const int g = lane * PER + i;
+            if (g < p.G) cs.gunit[g] = incl - sum + loc[i];
+        }
+        if (lane == 31) cs.gunit[p.G] = incl;
+    }
+    __syncthreads();
     const uint32_t tmem = cs.tmem_base;
-    const int nunits = total_units(p);
+    const int nunits = cs.gunit[p.G];
 
     if (warp == NEPI / 32) {
         // ===================== producer =====================
         if (lane == 0) {
             int it = 0;
             for (int u = blockIdx.x; u < nunits && !*(volatile int*)&cs.abort; u += gridDim.x) {
-                const Unit un = unit_of(p, u);
+                const Unit un = unit_of(p, cs.goff, cs.gunit, u);
                 int t0, t1;
                 tiles_of<EPI>(p, un.j, t0, t1);
                 bool bad = false;
@@ -240,7 +254,7 @@ __global__ void __launch_bounds__(gtc::NTH, 1)
         if (lane == 0) {
             int it = 0, q = 0;
             for (int u = blockIdx.x; u < nunits && !*(volatile int*)&cs.abort; u += gridDim.x) {
-                const Unit un = unit_of(p, u);
+                const Unit un = unit_of(p, cs.goff, cs.gunit, u);
                 int t0, t1;
                 tiles_of<EPI>(p, un.j, t0, t1);
                 bool bad = false;
@@ -277,8 +291,9 @@ __global__ void __launch_bounds__(gtc::NTH, 1)
         __syncwarp();
     } else {
         // ===================== epilogue =====================
-        const int rl = 32 * warp + lane;  // row of the tile = TMEM lane
-        const uint32_t tl = tmem + ((uint32_t)(32 * warp) << 16);
+        const int ew = warp & 3, half = warp >> 2;
+        const int rl = 32 * ew + lane;  // row of the tile = TMEM lane
+        const uint32_t tl = tmem + ((uint32_t)(32 * ew) << 16);
         const int N = p.N;
         bool ab = false;
         int q = 0;
@@ -290,7 +305,7 @@ __global__ void __launch_bounds__(gtc::NTH, 1)
             c2 = p.scaled ? gv * p.l2_factor : p.l2_factor * den;
         }
         for (int u = blockIdx.x; u < nunits; u += gridDim.x) {
-            const Unit un = unit_of(p, u);
+            const Unit un = unit_of(p, cs.goff, cs.gunit, u);
             const int row = un.row0 + rl;
             const bool valid = row >= 0 && row < un.rend && row < p.M;  // (offsets past M are ignored)
             int t0, t1;
@@ -316,7 +331,7 @@ __global__ void __launch_bounds__(gtc::NTH, 1)
                 ab = __any_sync(0xffffffffu, ab);
                 if (!ab) tc_fence_after();
 #pragma unroll 1
-                for (int c = 0; c < BN; c += 32) {
+                for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 32) {
                     const int n0 = nt * BN + c;
                     float v[32];
                     if (!ab) {
@@ -370,10 +385,31 @@ __global__ void __launch_bounds__(gtc::NTH, 1)
                     ck::mbar_arrive(&cs.acc_empty[acc]);
                 }
             }
-            if (EPI == CE && valid)
-                p.part[(size_t)un.j * p.M + row] =
-                    ab ? make_float4(fnan, fnan, fnan, __int_as_float(0x7fffffff))
-                       : make_float4(m, sum, zt, __int_as_float(am == 0x7fffffff ? am : am + p.col0));
+            if (EPI == CE) {  // merge the two column halves of each row (ties: lower column)
+                if (half == 1) cs.ce_half[rl] = make_float4(m, sum, zt, __int_as_float(am));
+                ck::bar_sync_n(BAR_EPI, NEPI);
+                if (half == 0) {
+                    const float4 h1 = cs.ce_half[rl];
+                    const int am1 = __float_as_int(h1.w);
+                    if (h1.y > 0.f) {
+                        if (!(sum > 0.f)) {
+                            m = h1.x, sum = h1.y, am = am1;
+                        } else if (h1.x > m || (h1.x == m && am1 < am)) {
+                            sum = h1.y + sum * __expf(m - h1.x);
+                            m = h1.x, am = am1;
+                        } else {
+                            sum += h1.y * __expf(h1.x - m);
+                        }
+                    }
+                    zt += h1.z;
+                    if (valid)
+                        p.part[(size_t)un.j * p.M + row] =
+                            (ab || *(volatile int*)&cs.abort)
+                                ? make_float4(fnan, fnan, fnan, __int_as_float(0x7fffffff))
+                                : make_float4(m, sum, zt, __int_as_float(am == 0x7fffffff ? am : am + p.col0));
+                }
+                ck::bar_sync_n(BAR_EPI, NEPI);  // ce_half is reused by the next unit
+            }
         }
     }
 
@@ -502,7 +538,7 @@ extern "C" int rwkv_grouped_gemm(const void* a, const void* w, const int32_t* of
                                  int G, long long ldo, int epi, int dtype, void* stream) {
     int rc = gtc::check_common(a, w, M, N, K, dtype);
     if (rc) return rc;
-    if (G <= 0 || (G > 1 && !offs) || !out || ldo < N) return RWKV_ERR_ARG;
+    if (G <= 0 || G > gtc::MAXG || (G > 1 && !offs) || !out || ldo < N) return RWKV_ERR_ARG;
     if (epi != gtc::STORE && epi != gtc::RELU2) return RWKV_ERR_ARG;
     gtc::Args p{};
     p.offs = offs, p.G = G, p.M = M, p.N = N, p.K = K;

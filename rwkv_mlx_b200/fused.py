@@ -1,4 +1,5 @@
-"""Python front-ends of the fused element-wise kernels (csrc/fused.cu).
+"""Python front-ends of the fused element-wise kernels (csrc/fused.cu) and of the
+tcgen05 grouped GEMM (csrc/gemm_tc.cu).
 
 They replace chains of separate torch element-wise passes in the block around the
 WKV-7 call (rwkv_mlx/model.py:187-263, 312-327); see include/rwkv_b200.h for the
@@ -103,4 +104,28 @@ def argmax_rows(x: torch.Tensor, out: torch.Tensor = None) -> torch.Tensor:
         out = torch.empty(rows, device=x.device, dtype=torch.int64)
     _call("rwkv_argmax_rows", nat.ptr(x), x.stride(0), rows, V, nat.ptr(out), nat.dtype_code(x),
           nat.stream_ptr(x.device))
+    return out
+
+
+def grouped_gemm(a: torch.Tensor, w: torch.Tensor, offsets: torch.Tensor | None = None, relu_sq: bool = False,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+    """out[m] = a[m] @ w[g]^T for the rows m in [offsets[g], offsets[g+1]) (squared ReLU of
+    the product when ``relu_sq``), on the tcgen05 grouped GEMM (``rwkv_grouped_gemm``).
+    a (M, K), w (G, N, K) fp16 / bf16; offsets (G+1,) int32 on the device, or None for
+    one group over all rows.  Rows outside every group are left as they were in ``out``."""
+    M, K = a.shape
+    G, N, K2 = w.shape
+    if K2 != K or (offsets is None and G != 1):
+        raise ValueError("grouped_gemm: shape mismatch")
+    a = a.contiguous()
+    w = w.to(a.dtype).contiguous()
+    if out is None:
+        out = torch.empty((M, N), device=a.device, dtype=a.dtype)
+    elif out.shape != (M, N) or out.stride(1) != 1 or out.dtype != a.dtype:
+        raise ValueError("grouped_gemm: out must be (M, N) in a's dtype with unit column stride")
+    L = nat.lib()
+    with torch.cuda.device(a.device):
+        rc = L.rwkv_grouped_gemm(nat.ptr(a), nat.ptr(w), nat.ptr(offsets), nat.ptr(out), M, N, K, G, out.stride(0),
+                                 1 if relu_sq else 0, nat.dtype_code(a), nat.stream_ptr(a.device))
+    nat.check(rc, "rwkv_grouped_gemm")
     return out

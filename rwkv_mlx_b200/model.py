@@ -302,8 +302,14 @@ class RWKV_CMix_x070(nn.Module):
 
     def forward(self, x):
         if self.config.fused and not torch.is_grad_enabled() and x.is_cuda:
-            k = fz.lerp(x, self.x_k.view(1, -1), x.shape[1])[0].view(x.shape)
-            return self.value(fz.relu_sq_(self.key(k)))
+            k = fz.lerp(x, self.x_k.view(1, -1), x.shape[1])[0]  # (rows, C)
+            wk = self.key.weight
+            if x.dtype in (torch.float16, torch.bfloat16) and wk.dtype == x.dtype and k.shape[1] % 8 == 0:
+                # key product and squared ReLU in one tcgen05 GEMM (no extra pass over the
+                # (rows, dim_ffn) activations)
+                h = fz.grouped_gemm(k, wk.view(1, *wk.shape), None, relu_sq=True)
+                return self.value(h).view(x.shape)
+            return self.value(fz.relu_sq_(self.key(k.view(x.shape))))
         xx = time_shift(x) - x
         k = x + xx * self.x_k
         k = torch.relu(self.key(k)) ** 2

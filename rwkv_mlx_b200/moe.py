@@ -37,7 +37,7 @@ import torch
 from torch import nn
 
 from . import _native as nat
-from .fused import relu_sq_
+from .fused import grouped_gemm, relu_sq_
 
 
 def _stream(dev):
@@ -226,28 +226,6 @@ def expert_mix_rows(x2d, prev, x_k, perm, offsets, T: int, top_k: int):
                                         nat.ptr(rows), n, T, C, top_k, E, nat.dtype_code(x2d), _stream(x2d.device))
     nat.check(rc, "rwkv_moe_expert_mix_rows")
     return rows
-
-
-def grouped_gemm(a: torch.Tensor, w: torch.Tensor, offsets: torch.Tensor | None = None, relu_sq: bool = False,
-                 out: torch.Tensor | None = None) -> torch.Tensor:
-    """out[m] = a[m] @ w[g]^T for the rows m in [offsets[g], offsets[g+1]) (squared ReLU of
-    the product when ``relu_sq``), on the tcgen05 grouped GEMM (``rwkv_grouped_gemm``).
-    a (M, K), w (G, N, K) fp16 / bf16; offsets (G+1,) int32 on the device, or None for
-    one group over all rows.  Rows outside every group are left as they were in ``out``."""
-    M, K = a.shape
-    G, N, K2 = w.shape
-    if K2 != K or (offsets is None and G != 1):
-        raise ValueError("grouped_gemm: shape mismatch")
-    a = a.contiguous()
-    w = w.to(a.dtype).contiguous()
-    if out is None:
-        out = torch.empty((M, N), device=a.device, dtype=a.dtype)
-    L = nat.lib()
-    with torch.cuda.device(a.device):
-        rc = L.rwkv_grouped_gemm(nat.ptr(a), nat.ptr(w), nat.ptr(offsets), nat.ptr(out), M, N, K, G, out.stride(0),
-                                 1 if relu_sq else 0, nat.dtype_code(a), _stream(a.device))
-    nat.check(rc, "rwkv_grouped_gemm")
-    return out
 
 
 def combine_rows(base2d, rows, scores, inv, ntok: int):

@@ -65,6 +65,14 @@ __device__ __forceinline__ void bulk_wait_read() {
     asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
 }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void tma_load_5d(void* dst, const CUtensorMap* m, int x, int y, int z, int w, int v,
+                                            unsigned long long* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(
+            ck::smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(m)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(v), "r"(ck::smem_u32(bar))
+        : "memory");
+}
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* m, int x, int y, int z,
                                             unsigned long long* bar) {
     asm volatile(
@@ -96,18 +104,22 @@ inline EncodeFn encoder() {
 // Tensor map of rank `rank` over `base` (dims[0] contiguous; strides in bytes for
 // dims 1..rank-1), box `box`, zero fill out of bounds.  APPLY_TC_NO_MAPS (common.cuh):
 // the map could not be built, nothing was launched.
-inline int make_map(CUtensorMap* m, bool bf16, const void* base, int rank, const cuuint64_t* dims,
-                    const cuuint64_t* strides, const cuuint32_t* box, bool swizzle128) {
+inline int make_map_dt(CUtensorMap* m, CUtensorMapDataType dt, const void* base, int rank, const cuuint64_t* dims,
+                       const cuuint64_t* strides, const cuuint32_t* box, bool swizzle128) {
     EncodeFn enc = encoder();
     if (!enc) return set_error(APPLY_TC_NO_MAPS, "cuTensorMapEncodeTiled is not available");
     const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
-    const CUresult r = enc(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                           (cuuint32_t)rank, const_cast<void*>(base), dims, strides, box, estr,
+    const CUresult r = enc(m, dt, (cuuint32_t)rank, const_cast<void*>(base), dims, strides, box, estr,
                            CU_TENSOR_MAP_INTERLEAVE_NONE,
                            swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return set_error(APPLY_TC_NO_MAPS, "cuTensorMapEncodeTiled rejected a tensor map");
     return RWKV_OK;
+}
+inline int make_map(CUtensorMap* m, bool bf16, const void* base, int rank, const cuuint64_t* dims,
+                    const cuuint64_t* strides, const cuuint32_t* box, bool swizzle128) {
+    return make_map_dt(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, base, rank, dims,
+                       strides, box, swizzle128);
 }
 
 }  // namespace tma

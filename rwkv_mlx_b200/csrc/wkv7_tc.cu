@@ -22,7 +22,8 @@
 //     thread issues U^T Bb with A = U read from tensor memory (2 issues).
 // Two groups of 4 "prep" warps compute the inputs-only chunk operands (decay scan,
 // intra-chunk products on mma.sync, triangular solve) for alternating chunks, straight
-// into the UMMA operand layouts.  Every wait is a bounded mbarrier wait: a CTA that
+// into the UMMA operand layouts; each group's six input boxes (16 steps of r, k, v, a, b,
+// w) arrive by TMA one own chunk ahead, issued by one thread.  Every wait is a bounded mbarrier wait: a CTA that
 // gives up sets the device error word, waits (bounded) for its own MMAs in flight,
 // fills its outputs with NaN, frees its tensor memory and exits; it never traps.
 //
@@ -41,6 +42,7 @@
 #include "chunk_common.cuh"
 #include "common.cuh"
 #include "tc_common.cuh"
+#include "tma_common.cuh"
 #include "wkv7.cuh"
 
 namespace rwkv {
@@ -53,6 +55,7 @@ static __constant__ int c_force_wait_timeout;
 namespace tc {
 using namespace ck;
 using namespace tcc;
+using namespace tma;
 
 constexpr int NT = 384;
 constexpr int NSTAGE = 3;  // operand stages for 2 prep groups: one chunk of slack
@@ -85,8 +88,46 @@ struct __align__(128) Smem {
     float Yb[L][LD8];
     PrepScratch ps[2];
     unsigned long long full[NSTAGE], empty[NSTAGE], mma1, mma2, drain[3];
+    unsigned long long ld_full[2];  // a prep group's input staging has landed (TMA)
     uint32_t tmem_base;
     int abort;
+};
+
+// Input staging of one prep group, filled by TMA with the 128-byte swizzle (16-byte piece
+// p of a 128-byte row q sits at piece p ^ (q % 8): 16 lanes reading the same column of 16
+// rows hit 8 distinct bank groups): r, k, v, a, b as 16 rows of 64 values (2 KB each),
+// then w: 16-bit like the others, fp32 as two 16-row halves of 32 values (row 16 h + t).
+template <typename T, typename TW>
+struct RawT {
+    static constexpr int ARR = L * N * (int)sizeof(T);
+    static constexpr int BYTES = 5 * ARR + L * N * (int)sizeof(TW);  // a multiple of 1024
+};
+__device__ __forceinline__ uint32_t swz(int q, int piece) { return (uint32_t)(q * 128 + ((piece ^ (q & 7)) << 4)); }
+// 8 values j0..j0+7 (j0 % 8 == 0) of row t of the 16-bit array arr
+template <typename T>
+__device__ __forceinline__ const unsigned char* raw8(const unsigned char* raw, int arr, int t, int j0) {
+    return raw + arr * (L * N * (int)sizeof(T)) + swz(t, j0 >> 3);
+}
+template <typename T>
+__device__ __forceinline__ float raw_at(const unsigned char* raw, int arr, int t, int j) {
+    return to_f32(*reinterpret_cast<const T*>(raw8<T>(raw, arr, t, j & ~7) + (j & 7) * 2));
+}
+template <typename T, typename TW>
+__device__ __forceinline__ void raw_w8(const unsigned char* raw, int t, int j0, float (&o)[8]) {
+    if constexpr (sizeof(TW) == 4) {
+        const unsigned char* wb = raw + 5 * (L * N * (int)sizeof(T));
+        const int q = 16 * (j0 >> 5) + t, pc = (j0 & 31) >> 2;
+        const float4 x0 = *reinterpret_cast<const float4*>(wb + swz(q, pc));
+        const float4 x1 = *reinterpret_cast<const float4*>(wb + swz(q, pc + 1));
+        o[0] = x0.x, o[1] = x0.y, o[2] = x0.z, o[3] = x0.w, o[4] = x1.x, o[5] = x1.y, o[6] = x1.z, o[7] = x1.w;
+    } else {
+        lds8<TW>(raw8<T>(raw, 5, t, j0), o);
+    }
+}
+// Tensor maps of the six inputs (all (B, T, H, 64) row-major): 16-bit as (64, T, H, B)
+// with a 64 x 16-step box, fp32 w as (32, T, 2, H, B) with a 32 x 16 x 2 box.
+struct InMaps {
+    CUtensorMap m[6];
 };
 
 enum { BAR_STATE = 1, BAR_PREP0 = 2 };  // BAR_PREP0 + g for prep group g
@@ -111,7 +152,7 @@ __device__ __forceinline__ bool wait_tc(unsigned long long* b, uint32_t parity, 
 }
 // Bounded wait that ignores the abort flag: the end-of-kernel drain of a thread's own
 // MMAs (tensor memory may only be freed once nothing writes it any more).
-__device__ __forceinline__ void drain_wait(unsigned long long* b) {
+__device__ __forceinline__ void drain_wait(unsigned long long* b, uint32_t parity = 0) {
     const uint32_t a = smem_u32(b);
     const long long t0 = clock64();
     while (true) {
@@ -119,7 +160,7 @@ __device__ __forceinline__ void drain_wait(unsigned long long* b) {
         asm volatile(
             "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
             : "=r"(ok)
-            : "r"(a), "r"(0u)
+            : "r"(a), "r"(parity)
             : "memory");
         if (ok) return;
         if (clock64() - t0 > WAIT_CYCLES) {
@@ -138,19 +179,15 @@ __device__ __forceinline__ uint4 nan_pack<__nv_bfloat16>() { return make_uint4(0
 
 // ---------------------------------------------------------------------------
 template <typename T, typename TW, bool TRANS>
-__global__ void __launch_bounds__(NT, 1) wkv7_fwd_tc_kernel(const TcArgs p) {
+__global__ void __launch_bounds__(NT, 1) wkv7_fwd_tc_kernel(const TcArgs p, const __grid_constant__ InMaps maps) {
     constexpr int ROWS = TRANS ? 128 : 64;
-    using R = Raw<T, TW>;
+    using R = RawT<T, TW>;
     extern __shared__ __align__(128) unsigned char smem_raw[];
     Smem<ROWS>& sm = *reinterpret_cast<Smem<ROWS>*>(smem_raw);
-    unsigned char* rawbuf = smem_raw + ((sizeof(Smem<ROWS>) + 127) / 128) * 128;  // [2 groups][R::BYTES]
+    // [2 groups][R::BYTES], 1024-byte aligned for the swizzled TMA boxes
+    const uint32_t sbase = smem_u32(smem_raw);
+    unsigned char* rawbuf = smem_raw + (((sbase + (uint32_t)sizeof(Smem<ROWS>) + 1023u) & ~1023u) - sbase);
 
-    const T* __restrict__ r = (const T*)p.r;
-    const TW* __restrict__ w = (const TW*)p.w;
-    const T* __restrict__ k = (const T*)p.k;
-    const T* __restrict__ v = (const T*)p.v;
-    const T* __restrict__ a = (const T*)p.a;
-    const T* __restrict__ b = (const T*)p.b;
     const int tid = threadIdx.x, warp = tid >> 5;
     const int nsl = TRANS ? p.nseg - 1 : p.nseg;  // segments in this launch
     const int bh = blockIdx.x / nsl, seg = blockIdx.x % nsl, H = p.H;
@@ -177,6 +214,8 @@ __global__ void __launch_bounds__(NT, 1) wkv7_fwd_tc_kernel(const TcArgs p) {
         mbar_init(&sm.drain[0], 1);
         mbar_init(&sm.drain[1], 1);
         mbar_init(&sm.drain[2], 4);
+        mbar_init(&sm.ld_full[0], 1);
+        mbar_init(&sm.ld_full[1], 1);
         sm.abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -199,54 +238,37 @@ __global__ void __launch_bounds__(NT, 1) wkv7_fwd_tc_kernel(const TcArgs p) {
         PrepScratch& ps = sm.ps[g_];
         unsigned char* raw = rawbuf + (size_t)g_ * R::BYTES;
 
-        const char* psrc[R::PER_THREAD];
-        uint32_t pdst[R::PER_THREAD];
-        int prow[R::PER_THREAD];
-#pragma unroll
-        for (int i = 0; i < R::PER_THREAD; i++) {
-            const int q = pt + 128 * i;
-            if (q < 5 * L * R::PPR) {
-                const int arr = q / (L * R::PPR), rem = q % (L * R::PPR), row = rem / R::PPR, pc = rem % R::PPR;
-                const T* src = arr == 0 ? r : arr == 1 ? k : arr == 2 ? v : arr == 3 ? a : b;
-                psrc[i] = reinterpret_cast<const char*>(src + base + (size_t)row * tstride) + pc * 16;
-                pdst[i] = arr * R::ARR + row * R::PITCH + pc * 16;
-                prow[i] = row;
-            } else if (q < R::PIECES) {
-                const int q2 = q - 5 * L * R::PPR, row = q2 / R::PPRW, pc = q2 % R::PPRW;
-                psrc[i] = reinterpret_cast<const char*>(w + base + (size_t)row * tstride) + pc * 16;
-                pdst[i] = 5 * R::ARR + row * R::PITCHW + pc * 16;
-                prow[i] = row;
-            } else {
-                psrc[i] = nullptr, pdst[i] = 0, prow[i] = -1;
-            }
-        }
+        // inputs of chunk c: one TMA box per array, issued by thread 0 of the group; the
+        // group's k-th chunk (c = g_ + 2k) completes phase k of ld_full[g_]
+        const int t_abs = t_begin;
         auto issue = [&](int c) {
-            const int t0 = c * L;
+            if (pt == 0) {
+                proxy_fence();  // the group's generic reads of the staging precede the TMA writes
+                expect_tx(&sm.ld_full[g_], R::BYTES);
+                const int tt = t_abs + c * L;
 #pragma unroll
-            for (int i = 0; i < R::PER_THREAD; i++) {
-                if (prow[i] < 0) continue;
-                const bool ok = (t0 + prow[i]) < nloc;
-                const size_t step = (size_t)t0 * tstride;
-                const char* src = ok ? psrc[i] + step * (pdst[i] >= 5u * R::ARR ? sizeof(TW) : sizeof(T)) : psrc[i];
-                cp_async16(raw + pdst[i], src, ok);
+                for (int i = 0; i < 5; i++) tma_load_4d(raw + i * R::ARR, &maps.m[i], 0, tt, hi, bi, &sm.ld_full[g_]);
+                if constexpr (sizeof(TW) == 4)
+                    tma_load_5d(raw + 5 * R::ARR, &maps.m[5], 0, tt, 0, hi, bi, &sm.ld_full[g_]);
+                else
+                    tma_load_4d(raw + 5 * R::ARR, &maps.m[5], 0, tt, hi, bi, &sm.ld_full[g_]);
             }
-            cp_commit();
         };
-
-        if (g_ < nchunks) issue(g_);
+        int n_issued = 0, n_used = 0;
+        if (g_ < nchunks) issue(g_), n_issued++;
         for (int c = g_; c < nchunks; c += 2) {
-            asm volatile("cp.async.wait_all;" ::: "memory");
-            bool bad = false;
+            bool bad = !wait_tc(&sm.ld_full[g_], n_used & 1, &sm.abort);
+            if (!bad) n_used++;
             const int si = c % NSTAGE;
             Stage<ROWS>& stg = sm.st[si];
-            if (c >= NSTAGE) bad = !wait_tc(&sm.empty[si], ((c / NSTAGE) + 1) & 1, &sm.abort);
+            if (!bad && c >= NSTAGE) bad = !wait_tc(&sm.empty[si], ((c / NSTAGE) + 1) & 1, &sm.abort);
             if (group_sync_or(BAR, bad)) break;
 
             // ---- P1: cumulative log2 decay, decayed factors, operands ----
             const int t = lane & 15, cg = 2 * pw + (lane >> 4), j0 = 8 * cg;
             const bool tok = t < nloc - c * L;
             float wv[8], cs[8], cp[8], cl[8];
-            lds8<TW>(raw + 5 * R::ARR + t * R::PITCHW + j0 * sizeof(TW), wv);
+            raw_w8<T, TW>(raw, t, j0, wv);
 #pragma unroll
             for (int q = 0; q < 8; q++) cs[q] = tok ? -ex2(wv[q] * LOG2E) * LOG2E : 0.f;
 #pragma unroll
@@ -266,11 +288,11 @@ __global__ void __launch_bounds__(NT, 1) wkv7_fwd_tc_kernel(const TcArgs p) {
                 ext |= cl[q] < -115.f;  // cumulative decay below e^-80
             }
             float xr[8], xk[8], xv[8], xa[8], xb[8], o1[8], o2[8];
-            lds8<T>(raw + 0 * R::ARR + t * R::PITCH + j0 * sizeof(T), xr);
-            lds8<T>(raw + 1 * R::ARR + t * R::PITCH + j0 * sizeof(T), xk);
-            lds8<T>(raw + 2 * R::ARR + t * R::PITCH + j0 * sizeof(T), xv);
-            lds8<T>(raw + 3 * R::ARR + t * R::PITCH + j0 * sizeof(T), xa);
-            lds8<T>(raw + 4 * R::ARR + t * R::PITCH + j0 * sizeof(T), xb);
+            lds8<T>(raw8<T>(raw, 0, t, j0), xr);
+            lds8<T>(raw8<T>(raw, 1, t, j0), xk);
+            lds8<T>(raw8<T>(raw, 2, t, j0), xv);
+            lds8<T>(raw8<T>(raw, 3, t, j0), xa);
+            lds8<T>(raw8<T>(raw, 4, t, j0), xb);
             float ec[8], ei[8], eL[8];
 #pragma unroll
             for (int q = 0; q < 8; q++) {
@@ -335,19 +357,18 @@ __global__ void __launch_bounds__(NT, 1) wkv7_fwd_tc_kernel(const TcArgs p) {
                     const bool strict = which < 2;
                     float val = 0.f;
                     if (strict ? (sidx < tt) : (sidx <= tt)) {
-                        const T* lhs = reinterpret_cast<const T*>(raw + (which < 2 ? 3 : 0) * R::ARR + tt * R::PITCH);
-                        const T* rhs = reinterpret_cast<const T*>(raw + ((which & 1) ? 1 : 4) * R::ARR + sidx * R::PITCH);
+                        const int la = which < 2 ? 3 : 0, ra = (which & 1) ? 1 : 4;
                         const float* cl2 = (which < 2) ? ps.Cs[tt] : ps.Cs[tt + 1];
                         const float* cr2 = ps.Cs[sidx + 1];
                         for (int jj = 0; jj < N; jj++)
-                            val = fmaf(to_f32(lhs[jj]) * to_f32(rhs[jj]), exp2f(cl2[jj] - cr2[jj]), val);
+                            val = fmaf(raw_at<T>(raw, la, tt, jj) * raw_at<T>(raw, ra, sidx, jj), exp2f(cl2[jj] - cr2[jj]), val);
                     }
                     float(*Mo)[LDM] = which == 0 ? ps.Mab : which == 1 ? ps.Mak : which == 2 ? ps.Mrb : ps.Mrk;
                     Mo[tt][sidx] = which == 0 ? val : tf32f(val);
                 }
             }
             group_sync(BAR);
-            if (c + 2 < nchunks) issue(c + 2);  // raw staging is free from here on
+            if (c + 2 < nchunks) issue(c + 2), n_issued++;  // raw staging is free from here on
 
             // ---- P4: forward substitution (I - Mab) X = [At | Mak]: Wu -> WB rows 0-15
             //      (threads 0-63, one key column each), Gu^T (threads 64-79) ----
@@ -452,8 +473,11 @@ __global__ void __launch_bounds__(NT, 1) wkv7_fwd_tc_kernel(const TcArgs p) {
             }
             mbar_arrive(&sm.full[si]);
         }
-        asm volatile("cp.async.wait_all;" ::: "memory");
-        if (pt == 0) {  // wait for this thread's own MMAs before the tensor memory is freed
+        if (pt == 0) {
+            // a load issued but never waited for (the loop was left early) must land before
+            // the shared memory is released; then this thread's own MMAs, before the tensor
+            // memory is freed
+            if (n_issued > n_used) drain_wait(&sm.ld_full[g_], (n_issued - 1) & 1);
             umma_commit(&sm.drain[g_]);
             drain_wait(&sm.drain[g_]);
         }
@@ -708,17 +732,46 @@ __global__ void __launch_bounds__(256) wkv7_seg_scan_kernel(const float* __restr
 
 template <typename T, typename TW, bool TRANS>
 size_t smem_bytes() {
-    return ((sizeof(Smem<TRANS ? 128 : 64>) + 127) / 128) * 128 + 2 * (size_t)Raw<T, TW>::BYTES;
+    return sizeof(Smem<TRANS ? 128 : 64>) + 1024 /* alignment of the staging */ + 2 * (size_t)RawT<T, TW>::BYTES;
 }
 
 template <typename T, typename TW, bool TRANS>
-int launch(const TcArgs& a, int grid, cudaStream_t st) {
+int launch(const TcArgs& a, const InMaps& maps, int grid, cudaStream_t st) {
     auto kern = wkv7_fwd_tc_kernel<T, TW, TRANS>;
     const size_t smem = smem_bytes<T, TW, TRANS>();
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return set_cuda_error(e);
-    kern<<<grid, NT, smem, st>>>(a);
+    kern<<<grid, NT, smem, st>>>(a, maps);
     return check_launch();
+}
+
+template <typename T>
+constexpr CUtensorMapDataType map_type() {
+    return sizeof(T) == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                          : (std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                                  : CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
+}
+
+template <typename T, typename TW>
+int make_in_maps(const WkvFwdArgs& p, InMaps& maps) {
+    const cuuint64_t B = p.B, T_ = p.T, H = p.H;
+    const void* src[6] = {p.r, p.k, p.v, p.a, p.b, p.w};
+    for (int i = 0; i < 6; i++) {
+        int rc;
+        if (i == 5 && sizeof(TW) == 4) {  // (32, T, 2, H, B): box 32 x 16 x 2 halves
+            const cuuint64_t dims[5] = {32, T_, 2, H, B};
+            const cuuint64_t strides[4] = {H * N * 4, 128, (cuuint64_t)N * 4, T_ * H * N * 4};
+            const cuuint32_t box[5] = {32, (cuuint32_t)L, 2, 1, 1};
+            rc = make_map_dt(&maps.m[i], map_type<TW>(), src[i], 5, dims, strides, box, true);
+        } else {  // (64, T, H, B): box 64 x 16
+            const cuuint64_t dims[4] = {(cuuint64_t)N, T_, H, B};
+            const cuuint64_t strides[3] = {H * N * 2, (cuuint64_t)N * 2, T_ * H * N * 2};
+            const cuuint32_t box[4] = {(cuuint32_t)N, (cuuint32_t)L, 1, 1};
+            rc = make_map_dt(&maps.m[i], i == 5 ? map_type<TW>() : map_type<T>(), src[i], 4, dims, strides, box, true);
+        }
+        if (rc) return RWKV_ERR_CUDA;
+    }
+    return RWKV_OK;
 }
 
 template <typename T, typename TW>
@@ -729,16 +782,19 @@ int run(const WkvFwdArgs& p, int nseg, float* ws, cudaStream_t st) {
     TcArgs a{p.r, p.w, p.k, p.v, p.a, p.b, p.s0, p.y, p.sT, p.ckpt, p.sa, nullptr, nullptr,
              p.T, p.H, p.ckpt_len, nseg, seg_chunks * L};
     const int units = p.B * p.H;
+    alignas(64) InMaps maps;
+    int rc = make_in_maps<T, TW>(p, maps);
+    if (rc) return rc;
     if (nseg > 1) {
         a.trans = ws;
         a.seg_s0 = ws + (size_t)units * (nseg - 1) * ROWS_CM * N;
-        int rc = launch<T, TW, true>(a, units * (nseg - 1), st);
+        rc = launch<T, TW, true>(a, maps, units * (nseg - 1), st);
         if (rc) return rc;
         wkv7_seg_scan_kernel<<<dim3(units, N / 8), 256, 0, st>>>(a.trans, a.seg_s0, nseg);
         rc = check_launch();
         if (rc) return rc;
     }
-    return launch<T, TW, false>(a, units * nseg, st);
+    return launch<T, TW, false>(a, maps, units * nseg, st);
 }
 
 }  // namespace tc

@@ -238,11 +238,18 @@ __global__ void __launch_bounds__(NT, 1) wkv7_fwd_tc_kernel(const TcArgs p, cons
         PrepScratch& ps = sm.ps[g_];
         unsigned char* raw = rawbuf + (size_t)g_ * R::BYTES;
 
-        // inputs of chunk c: one TMA box per array, issued by thread 0 of the group; the
+        // inputs of chunk c: one TMA box per array, issued by lane 0 of the group's warp 3
+        // (which has no share of the forward substitution that follows the issue); the
         // group's k-th chunk (c = g_ + 2k) completes phase k of ld_full[g_]
         const int t_abs = t_begin;
+        constexpr int ISSUER = 96;
+        if (pt == ISSUER) {
+#pragma unroll
+            for (int i = 0; i < 6; i++)
+                asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.m[i])) : "memory");
+        }
         auto issue = [&](int c) {
-            if (pt == 0) {
+            if (pt == ISSUER) {
                 proxy_fence();  // the group's generic reads of the staging precede the TMA writes
                 expect_tx(&sm.ld_full[g_], R::BYTES);
                 const int tt = t_abs + c * L;
@@ -545,6 +552,19 @@ __global__ void __launch_bounds__(NT, 1) wkv7_fwd_tc_kernel(const TcArgs p, cons
                 for (int i = 0; i < L; i++) ut[i] = tf32f(u[i]);
                 tmem_st16(tmem + lb + COL_U, ut);
             }
+            if constexpr (!TRANS) {  // y rows of this chunk (D1's Wy parts + X's Yi part) into Yb
+                float p0[16], p1[16], p2[16], p3[16], px[16];
+                tmem_ld16(tmem + lb + COL_D1 + L, p0);
+                tmem_ld16(tmem + lb + COL_D1 + 32 + L, p1);
+                tmem_ld16(tmem + lb + COL_D1 + 64 + L, p2);
+                tmem_ld16(tmem + lb + COL_D1 + 96 + L, p3);
+                tmem_ld16(tX + L, px);
+                tmem_wait_ld();
+                if (live) {
+#pragma unroll
+                    for (int i = 0; i < L; i++) sm.Yb[i][row] = ((p0[i] + p1[i]) + (p2[i] + p3[i])) + px[i];
+                }
+            }
             // state * chunk decay + V^T Kb, two 32-column halves
 #pragma unroll
             for (int j = 0; j < N; j += 32) {
@@ -568,7 +588,7 @@ __global__ void __launch_bounds__(NT, 1) wkv7_fwd_tc_kernel(const TcArgs p, cons
             }
             tmem_wait_st();
             tc_fence_before();
-            if (group_sync_or(BAR_STATE, bad2)) break;
+            if (group_sync_or(BAR_STATE, bad2)) break;  // (also: Yb complete)
             tc_fence_after();
             if (tid == 0) {  // S_L += U^T Bb, A = U read from tensor memory
                 const uint32_t i2 = idesc_tf32(ROWS, 64), bB = smem_u32(stg.BB);
@@ -584,20 +604,6 @@ __global__ void __launch_bounds__(NT, 1) wkv7_fwd_tc_kernel(const TcArgs p, cons
                     for (int tt = 0; tt < L; tt++)
                         if (c * L + tt < nloc) p.sa[base + (size_t)(c * L + tt) * tstride + row] = u[tt];
                 }
-                {
-                    float p0[16], p1[16], p2[16], p3[16], px[16];
-                    tmem_ld16(tmem + lb + COL_D1 + L, p0);
-                    tmem_ld16(tmem + lb + COL_D1 + 32 + L, p1);
-                    tmem_ld16(tmem + lb + COL_D1 + 64 + L, p2);
-                    tmem_ld16(tmem + lb + COL_D1 + 96 + L, p3);
-                    tmem_ld16(tX + L, px);
-                    tmem_wait_ld();
-                    if (live) {
-#pragma unroll
-                        for (int i = 0; i < L; i++) sm.Yb[i][row] = ((p0[i] + p1[i]) + (p2[i] + p3[i])) + px[i];
-                    }
-                }
-                group_sync(BAR_STATE);
                 {  // y rows of this chunk: 8 consecutive values per thread, one 16-byte store
                     const int rr = tid >> 3, c8 = (tid & 7) * 8, t = c * L + rr;
                     if (t < nloc) {

@@ -384,10 +384,16 @@ __global__ void __launch_bounds__(NT, 1) wkv7_fwd_tc_kernel(const TcArgs p, cons
                 const bool left = pt < N;
                 const int col = left ? pt : pt - N;
 #pragma unroll
-                for (int tt = 0; tt < L; tt++) {
+                for (int tt = 0; tt < L; tt++) {  // Mab rows read as 16-byte vectors (4x fewer loads)
                     float accx = left ? ps.At[tt][col] : ps.Mak[tt][col];
 #pragma unroll
-                    for (int s2 = 0; s2 < tt; s2++) accx = fmaf(ps.Mab[tt][s2], x[s2], accx);
+                    for (int q = 0; q < (tt + 3) / 4; q++) {
+                        const float4 m = *reinterpret_cast<const float4*>(&ps.Mab[tt][4 * q]);
+                        if (4 * q + 0 < tt) accx = fmaf(m.x, x[4 * q + 0], accx);
+                        if (4 * q + 1 < tt) accx = fmaf(m.y, x[4 * q + 1], accx);
+                        if (4 * q + 2 < tt) accx = fmaf(m.z, x[4 * q + 2], accx);
+                        if (4 * q + 3 < tt) accx = fmaf(m.w, x[4 * q + 3], accx);
+                    }
                     x[tt] = accx;
                 }
                 if (left) {

@@ -331,52 +331,56 @@ __global__ void __launch_bounds__(gtc::NTH, 1)
                 ab = __any_sync(0xffffffffu, ab);
                 if (!ab) tc_fence_after();
 #pragma unroll 1
-                for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 32) {
-                    const int n0 = nt * BN + c;
-                    float v[32];
+                for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 64) {
+                    float vv[2][32];  // two 32-column loads in flight per wait
                     if (!ab) {
-                        tmem_ld32(tl + acc * BN + c, v);
+                        tmem_ld32(tl + acc * BN + c, vv[0]);
+                        tmem_ld32(tl + acc * BN + c + 32, vv[1]);
                         tmem_wait_ld();
                     }
-                    if (n0 >= N || !valid) continue;
-                    const int ncol = N - n0 < 32 ? N - n0 : 32;
-                    if (EPI == STORE || EPI == RELU2 || EPI == CE_GRAD) {
 #pragma unroll
-                        for (int e = 0; e < 32; e++) {
-                            float x = ab ? fnan : v[e];
-                            if (EPI == RELU2) {
-                                x = round_t<T>(x);  // the key product in the activation type, then relu^2
-                                x = x > 0.f ? x * x : (x == x ? 0.f : x);
-                            } else if (EPI == CE_GRAD) {
-                                const float l = round_t<T>(x);
-                                float d = a * (__expf(l - lse) - (n0 + e == tg ? 1.f : 0.f));
-                                if (n0 + e == amg) d += l2g;
-                                x = d;
+                    for (int hh = 0; hh < 2; hh++) {
+                        const int n0 = nt * BN + c + 32 * hh;
+                        if (n0 >= N || !valid) continue;
+                        const int ncol = N - n0 < 32 ? N - n0 : 32;
+                        if (EPI == STORE || EPI == RELU2 || EPI == CE_GRAD) {
+#pragma unroll
+                            for (int e = 0; e < 32; e++) {
+                                float x = ab ? fnan : vv[hh][e];
+                                if (EPI == RELU2) {
+                                    x = round_t<T>(x);  // the key product in the activation type, then relu^2
+                                    x = x > 0.f ? x * x : (x == x ? 0.f : x);
+                                } else if (EPI == CE_GRAD) {
+                                    const float l = round_t<T>(x);
+                                    float d = a * (__expf(l - lse) - (n0 + e == tg ? 1.f : 0.f));
+                                    if (n0 + e == amg) d += l2g;
+                                    x = d;
+                                }
+                                vv[hh][e] = x;
                             }
-                            v[e] = x;
-                        }
-                        store32<T>(reinterpret_cast<T*>(p.out) + (size_t)row * p.ldo + n0, v, ncol, p.vec_out != 0);
-                    } else {  // CE
-                        if (ab) continue;
-                        float lm = -INFINITY;
-                        int li = 0;
+                            store32<T>(reinterpret_cast<T*>(p.out) + (size_t)row * p.ldo + n0, vv[hh], ncol, p.vec_out != 0);
+                        } else {  // CE
+                            if (ab) continue;
+                            float lm = -INFINITY;
+                            int li = 0;
 #pragma unroll
-                        for (int e = 0; e < 32; e++) {
-                            v[e] = round_t<T>(v[e]);
-                            if (e < ncol && v[e] > lm) lm = v[e], li = e;
-                        }
-                        if (lm > m) {
-                            sum *= __expf(m - lm);
-                            m = lm;
-                            am = n0 + li;
-                        }
-#pragma unroll
-                        for (int e = 0; e < 32; e++)
-                            if (e < ncol) sum += __expf(v[e] - m);
-                        if (tg >= n0 && tg < n0 + ncol) {
+                            for (int e = 0; e < 32; e++) {
+                                vv[hh][e] = round_t<T>(vv[hh][e]);
+                                if (e < ncol && vv[hh][e] > lm) lm = vv[hh][e], li = e;
+                            }
+                            if (lm > m) {
+                                sum *= __expf(m - lm);
+                                m = lm;
+                                am = n0 + li;
+                            }
 #pragma unroll
                             for (int e = 0; e < 32; e++)
-                                if (n0 + e == tg) zt = v[e];
+                                if (e < ncol) sum += __expf(vv[hh][e] - m);
+                            if (tg >= n0 && tg < n0 + ncol) {
+#pragma unroll
+                                for (int e = 0; e < 32; e++)
+                                    if (n0 + e == tg) zt = vv[hh][e];
+                            }
                         }
                     }
                 }

@@ -387,14 +387,16 @@ template <typename T, typename TW>
 __global__ void __launch_bounds__(p1::NTH, 1)
     wkv7_bwd_chain_ws_kernel(const T* __restrict__ r, const TW* __restrict__ w, const T* __restrict__ a,
                              const T* __restrict__ b, const T* __restrict__ dy, const float* __restrict__ dsT,
-                             float* __restrict__ dxl, float* __restrict__ ds0, int T_, int H) {
+                             float* __restrict__ dxl, float* __restrict__ ds0, int T_, int H, int c_lo, int c_hi) {
     using namespace p1;
     using RI = RawIn<T, TW>;
     extern __shared__ __align__(16) unsigned char smem_p1w[];
     P1WSmem<T, TW>& sm = *reinterpret_cast<P1WSmem<T, TW>*>(smem_p1w);
     const int tid = threadIdx.x, warp = tid >> 5, bh = blockIdx.x, bi = bh / H, hi = bh % H;
     const size_t tstride = (size_t)H * N, base = ((size_t)bi * T_ * H + hi) * N;
-    const int nch = (T_ + L - 1) / L;
+    // chunks c_hi - 1 down to c_lo (the whole sequence, or one part of it: the adjoint state
+    // enters through dxl[c_hi - 1] and leaves through dxl[c_lo - 1] between parts)
+    const int nch = (T_ + L - 1) / L, cnt = c_hi - c_lo;
     constexpr bool EXI = sizeof(T) == 2;  // 16-bit dy is exact in TF32
 
     if (tid == 0) {
@@ -411,8 +413,8 @@ __global__ void __launch_bounds__(p1::NTH, 1)
         const int BAR = BAR_PREP0 + g_;
         Prep& pg = sm.pg[g_];
         unsigned char* raw = sm.raw[g_];
-        auto issue = [&](int ii) {  // raw inputs of processing index ii (chunk nch - 1 - ii)
-            const int t0 = (nch - 1 - ii) * L, nt = min(L, T_ - t0);
+        auto issue = [&](int ii) {  // raw inputs of processing index ii (chunk c_hi - 1 - ii)
+            const int t0 = (c_hi - 1 - ii) * L, nt = min(L, T_ - t0);
             constexpr int NTP = 4 * L * RI::PR_, ALL = NTP + L * RI::PRW;
             for (int q = pt; q < ALL; q += 128) {
                 const void* src;
@@ -434,10 +436,10 @@ __global__ void __launch_bounds__(p1::NTH, 1)
             }
             asm volatile("cp.async.commit_group;" ::: "memory");
         };
-        if (g_ < nch) issue(g_);
-        for (int i = g_; i < nch; i += 2) {
+        if (g_ < cnt) issue(g_);
+        for (int i = g_; i < cnt; i += 2) {
             asm volatile("cp.async.wait_all;" ::: "memory");
-            const int s = i % NSTAGE, c = nch - 1 - i, nt = min(L, T_ - c * L);
+            const int s = i % NSTAGE, c = c_hi - 1 - i, nt = min(L, T_ - c * L);
             Stage& stg = sm.st[s];
             const bool bad = i >= NSTAGE && !ck::mbar_wait(&sm.empty[s], ((i / NSTAGE) + 1) & 1, &sm.abort, &g_device_error_bwd);
             if (ck::group_sync_or(BAR, bad)) break;
@@ -453,7 +455,7 @@ __global__ void __launch_bounds__(p1::NTH, 1)
                 pg.in[PL][t][j] = t < nt ? -ck::ex2(to_f32(wt[t * N + j]) * ck::LOG2E) : 0.f;
             }
             ck::group_sync(BAR);
-            if (i + 2 < nch) issue(i + 2);  // the raw buffer is free again
+            if (i + 2 < cnt) issue(i + 2);  // the raw buffer is free again
             // cumulative decays, GL
             int ext = 0;
             if (pt < N) {
@@ -522,13 +524,18 @@ __global__ void __launch_bounds__(p1::NTH, 1)
     } else {
         // ===================== chain warps =====================
         const Warps wp{warp, NCW};
-        for (int e = tid; e < N * N; e += 32 * NCW) {  // D = dsT^T
-            const int vv = e / N, j = e % N;
-            sm.D[j][vv] = dsT ? dsT[(size_t)bh * N * N + e] : 0.f;
+        if (c_hi == nch) {
+            for (int e = tid; e < N * N; e += 32 * NCW) {  // D = dsT^T
+                const int vv = e / N, j = e % N;
+                sm.D[j][vv] = dsT ? dsT[(size_t)bh * N * N + e] : 0.f;
+            }
+        } else {  // the adjoint state left by the part above (row-major D)
+            const float* in = dxl + ((size_t)bh * nch + c_hi - 1) * N * N;
+            for (int e = tid; e < N * N; e += 32 * NCW) sm.D[e / N][e % N] = in[e];
         }
         bool failed = false;
-        for (int i = 0; i < nch; i++) {
-            const int c = nch - 1 - i, s = i % NSTAGE;
+        for (int i = 0; i < cnt; i++) {
+            const int c = c_hi - 1 - i, s = i % NSTAGE;
             const Stage& stg = sm.st[s];
             const bool bad = !ck::mbar_wait(&sm.full[s], (i / NSTAGE) & 1, &sm.abort, &g_device_error_bwd);
             if (ck::bar_or_n(BAR_CHAIN, 32 * NCW, bad)) {
@@ -548,8 +555,13 @@ __global__ void __launch_bounds__(p1::NTH, 1)
         }
         if (failed && tid == 0) sm.abort = 1;
         ck::bar_sync_n(BAR_CHAIN, 32 * NCW);
-        if (!failed && ds0) {
+        if (!failed && ds0 && c_lo == 0) {
             for (int e = tid; e < N * N; e += 32 * NCW) ds0[(size_t)bh * N * N + e] = sm.D[e % N][e / N];
+        }
+        if (!failed && c_lo > 0) {  // hand the adjoint state to the part below
+            float* out = dxl + ((size_t)bh * nch + c_lo - 1) * N * N;
+            for (int e = tid; e < N * N / 4; e += 32 * NCW)
+                *reinterpret_cast<float4*>(out + 4 * e) = *reinterpret_cast<const float4*>(&sm.D[e / 16][(e % 16) * 4]);
         }
     }
 }
@@ -590,13 +602,13 @@ __global__ void __launch_bounds__(NT, 2)
                           const T* __restrict__ v, const T* __restrict__ a, const T* __restrict__ b,
                           const T* __restrict__ dy, const float* __restrict__ s0, const float* __restrict__ ckpt,
                           const float* __restrict__ dxl, T* __restrict__ dr, T* __restrict__ dw, T* __restrict__ dk,
-                          T* __restrict__ dv, T* __restrict__ da, T* __restrict__ db, int T_, int H) {
+                          T* __restrict__ dv, T* __restrict__ da, T* __restrict__ db, int T_, int H, int c_off) {
     extern __shared__ __align__(16) unsigned char smem_p2[];
     P2Smem<T>& sm = *reinterpret_cast<P2Smem<T>*>(smem_p2);
     Front<T>& fr = sm.fr;
-    const int tid = threadIdx.x, c = blockIdx.x, bh = blockIdx.y, bi = bh / H, hi = bh % H;
+    const int tid = threadIdx.x, c = blockIdx.x + c_off, bh = blockIdx.y, bi = bh / H, hi = bh % H;
     const size_t tstride = (size_t)H * N, base = ((size_t)bi * T_ * H + hi) * N;
-    const int nch = gridDim.x, t0 = c * L, nt = min(L, T_ - t0);
+    const int nch = (T_ + L - 1) / L, t0 = c * L, nt = min(L, T_ - t0);
     const int lane = tid & 31, g = lane >> 2, tg = lane & 3, wrp = tid >> 5;
     auto own_t = [&](int slot) { return g + 8 * (slot >> 1); };
     auto own_j = [&](int slot) { return 8 * wrp + 2 * tg + (slot & 1); };
@@ -825,6 +837,37 @@ size_t wkv7_bwd_chunk_ws_bytes(int B, int T, int H) {
     return (size_t)B * H * ((T + bwdc::L - 1) / bwdc::L) * bwdc::N * bwdc::N * sizeof(float);
 }
 
+namespace {
+int sm_count() {
+    int dev = 0, n = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n;
+}
+// A high-priority side stream and the events that order the parts, per device and per
+// calling thread (so that two host threads never interleave records of the same event).
+struct PartStreams {
+    static constexpr int NP = 4;
+    cudaStream_t side = nullptr;
+    cudaEvent_t ev[NP + 1] = {};
+};
+const PartStreams* part_streams() {
+    thread_local PartStreams cache[16];
+    thread_local bool made[16] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 16) return nullptr;
+    if (!made[dev]) {
+        PartStreams& c = cache[dev];
+        int least = 0, greatest = 0;
+        if (cudaDeviceGetStreamPriorityRange(&least, &greatest) != cudaSuccess) return nullptr;
+        if (cudaStreamCreateWithPriority(&c.side, cudaStreamNonBlocking, greatest) != cudaSuccess) return nullptr;
+        for (int i = 0; i <= PartStreams::NP; i++)
+            if (cudaEventCreateWithFlags(&c.ev[i], cudaEventDisableTiming) != cudaSuccess) return nullptr;
+        made[dev] = true;
+    }
+    return &cache[dev];
+}
+}  // namespace
+
 template <typename T, typename TW>
 static int launch_bwd_chunked(const WkvBwdArgs& p, float* ws, cudaStream_t st) {
     using namespace bwdc;
@@ -834,15 +877,43 @@ static int launch_bwd_chunked(const WkvBwdArgs& p, float* ws, cudaStream_t st) {
     cudaError_t e = cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, s1);
     if (e == cudaSuccess) e = cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, s2);
     if (e != cudaSuccess) return set_cuda_error(e);
-    const int nch = (p.T + L - 1) / L;
-    k1<<<p.B * p.H, p1::NTH, s1, st>>>((const T*)p.r, (const TW*)p.w, (const T*)p.a, (const T*)p.b, (const T*)p.dy,
-                                       p.dsT, ws, p.ds0, p.T, p.H);
-    int rc = check_launch();
-    if (rc) return rc;
-    k2<<<dim3(nch, p.B * p.H), NT, s2, st>>>((const T*)p.r, (const TW*)p.w, (const T*)p.k, (const T*)p.v,
-                                             (const T*)p.a, (const T*)p.b, (const T*)p.dy, p.s0, p.ckpt, ws,
-                                             (T*)p.dr, (T*)p.dw, (T*)p.dk, (T*)p.dv, (T*)p.da, (T*)p.db, p.T, p.H);
-    return check_launch();
+    const int nch = (p.T + L - 1) / L, units = p.B * p.H;
+    auto pass1 = [&](cudaStream_t s, int lo, int hi) {
+        k1<<<units, p1::NTH, s1, s>>>((const T*)p.r, (const TW*)p.w, (const T*)p.a, (const T*)p.b, (const T*)p.dy,
+                                      p.dsT, ws, p.ds0, p.T, p.H, lo, hi);
+        return check_launch();
+    };
+    auto pass2 = [&](cudaStream_t s, int lo, int hi) {
+        k2<<<dim3(hi - lo, units), NT, s2, s>>>((const T*)p.r, (const TW*)p.w, (const T*)p.k, (const T*)p.v,
+                                                (const T*)p.a, (const T*)p.b, (const T*)p.dy, p.s0, p.ckpt, ws,
+                                                (T*)p.dr, (T*)p.dw, (T*)p.dk, (T*)p.dv, (T*)p.da, (T*)p.db, p.T,
+                                                p.H, lo);
+        return check_launch();
+    };
+    // Pass 1 occupies one SM per (b, h).  When that leaves SMs idle, the chain runs in
+    // parts (top chunks first) on a high-priority side stream, and pass 2 of each part
+    // starts on the caller's stream as soon as its part of the chain is done, on the SMs
+    // the chain leaves free.
+    const PartStreams* ps = (sm_count() - units >= 32 && nch >= 16) ? part_streams() : nullptr;
+    if (!ps) {
+        int rc = pass1(st, 0, nch);
+        return rc ? rc : pass2(st, 0, nch);
+    }
+    constexpr int NP = PartStreams::NP;
+    cudaError_t ce = cudaEventRecord(ps->ev[0], st);
+    if (ce == cudaSuccess) ce = cudaStreamWaitEvent(ps->side, ps->ev[0], 0);
+    if (ce != cudaSuccess) return set_cuda_error(ce);
+    for (int q = 0; q < NP; q++) {
+        const int hi = nch - (int)((long long)q * nch / NP), lo = nch - (int)((long long)(q + 1) * nch / NP);
+        int rc = pass1(ps->side, lo, hi);
+        if (rc) return rc;
+        ce = cudaEventRecord(ps->ev[q + 1], ps->side);
+        if (ce == cudaSuccess) ce = cudaStreamWaitEvent(st, ps->ev[q + 1], 0);
+        if (ce != cudaSuccess) return set_cuda_error(ce);
+        rc = pass2(st, lo, hi);
+        if (rc) return rc;
+    }
+    return RWKV_OK;
 }
 
 int read_device_error_bwd(int clear) { return bwdc::read_error_word(clear); }

@@ -51,7 +51,7 @@ struct __align__(16) Smem {
     float At[L][LD4], Rt[L][LD4], Bh[L][LD4], Kh[L][LD4];
     float Mab[L][LDM], Mak[L][LDM], Mrb[L][LDM], Mrk[L][LDM];
     float MakV[L][LD8];
-    float Cs[L + 1][N];  // cumulative log decay, Cs[0] = 0, Cs[t+1] = c_t
+    float Cs[L + 1][LD4];  // cumulative log decay, Cs[0] = 0, Cs[t+1] = c_t (rows padded: conflict-free stores)
     unsigned long long full[2], empty[2];
     int abort;
 };

@@ -80,7 +80,7 @@ struct __align__(16) PrepScratch {
     float At[L][LD4], Rt[L][LD4], Bh[L][LD4], Kh[L][LD4];
     float Mab[L][LDM], Mak[L][LDM], Mrb[L][LDM], Mrk[L][LDM];
     float GuT[L][LDM];  // (I - Mab)^-1 Mak
-    float Cs[L + 1][N];  // cumulative log2 decay, Cs[0] = 0
+    float Cs[L + 1][LD4];  // cumulative log2 decay, Cs[0] = 0 (rows padded: conflict-free stores)
 };
 template <int ROWS>
 struct __align__(128) Smem {

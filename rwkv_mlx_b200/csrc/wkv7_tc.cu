@@ -610,16 +610,18 @@ __global__ void __launch_bounds__(NT, 1) wkv7_fwd_tc_kernel(const TcArgs p, cons
                     for (int tt = 0; tt < L; tt++)
                         if (c * L + tt < nloc) p.sa[base + (size_t)(c * L + tt) * tstride + row] = u[tt];
                 }
-                {  // y rows of this chunk: 8 consecutive values per thread, one 16-byte store
-                    const int rr = tid >> 3, c8 = (tid & 7) * 8, t = c * L + rr;
+                {  // y rows of this chunk: values c4..c4+3 and 32+c4..35+c4 per thread (8 lanes
+                   // read 128 contiguous bytes of Yb: conflict-free), two 8-byte stores
+                    const int rr = tid >> 3, c4 = (tid & 7) * 4, t = c * L + rr;
                     if (t < nloc) {
-                        const float4 f0 = *reinterpret_cast<const float4*>(&sm.Yb[rr][c8]);
-                        const float4 f1 = *reinterpret_cast<const float4*>(&sm.Yb[rr][c8 + 4]);
-                        uint4 pk;
-                        T* pe = reinterpret_cast<T*>(&pk);
-                        pe[0] = from_f32<T>(f0.x), pe[1] = from_f32<T>(f0.y), pe[2] = from_f32<T>(f0.z), pe[3] = from_f32<T>(f0.w);
-                        pe[4] = from_f32<T>(f1.x), pe[5] = from_f32<T>(f1.y), pe[6] = from_f32<T>(f1.z), pe[7] = from_f32<T>(f1.w);
-                        *reinterpret_cast<uint4*>((T*)p.y + base + (size_t)t * tstride + c8) = pk;
+#pragma unroll
+                        for (int hh = 0; hh < 2; hh++) {
+                            const float4 f = *reinterpret_cast<const float4*>(&sm.Yb[rr][32 * hh + c4]);
+                            uint2 pk;
+                            T* pe = reinterpret_cast<T*>(&pk);
+                            pe[0] = from_f32<T>(f.x), pe[1] = from_f32<T>(f.y), pe[2] = from_f32<T>(f.z), pe[3] = from_f32<T>(f.w);
+                            *reinterpret_cast<uint2*>((T*)p.y + base + (size_t)t * tstride + 32 * hh + c4) = pk;
+                        }
                     }
                 }
             }

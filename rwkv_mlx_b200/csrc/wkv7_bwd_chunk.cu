@@ -318,13 +318,13 @@ __device__ void front_matrices(Front<T>& fr, int ext, unsigned which) {
 // Pass 1, warp-specialized.  The chain itself needs per chunk only Wu, Wy, Bb, dY and
 // GL, all functions of the inputs: two "prep" groups of 4 warps build them for
 // alternating chunks into a 3-stage ring (inputs streamed with cp.async one own chunk
-// ahead), while 8 "chain" warps run dX_0 = GL o dX_L + Wu^T (Bb dX_L) + Wy^T dY.
+// ahead and read from that staging in their own type), while 8 "chain" warps run
+// dX_0 = GL o dX_L + Wu^T (Bb dX_L) + Wy^T dY.
 // Wu = (I - Mab)^-1 At comes from a forward substitution in fp32 (one key column per
 // thread); the products run on mma.sync with 3xTF32 operands as elsewhere here.
 namespace p1 {
 constexpr int NTH = 512, NSTAGE = 3, NCW = 8;  // 8 chain warps, then two prep groups of 4 warps
 enum { BAR_CHAIN = 1, BAR_PREP0 = 2 };
-enum { PR = 0, PL, PA, PB, PD, NP };  // inputs kept per chunk: r, l = -exp(w), a, b, dy
 struct Stage {
     float WU[L][LDC], WY[L][LDC], BB[L][LDC], DY[L][LDC];
     float GL[N];
@@ -336,7 +336,6 @@ struct RawIn {  // one chunk's raw inputs as cp.async deposits them: r, a, b, dy
     static constexpr int BYTES = 4 * L * ROW + L * ROWW;
 };
 struct Prep {
-    float in[NP][L][LDC];
     float c[L][LDC];
     float At[L][LDC], Rt[L][LDC], Bh[L][LDC];
     float M[2][L][LM];  // Mab (strict), Mrb (inclusive)
@@ -443,25 +442,20 @@ __global__ void __launch_bounds__(p1::NTH, 1)
             Stage& stg = sm.st[s];
             const bool bad = i >= NSTAGE && !ck::mbar_wait(&sm.empty[s], ((i / NSTAGE) + 1) & 1, &sm.abort, &g_device_error_bwd);
             if (ck::group_sync_or(BAR, bad)) break;
-            // raw -> fp32 (l = -exp(w); rows past the sequence end are zero)
-            for (int e = pt; e < L * N; e += 128) {
-                const int t = e / N, j = e % N;
-                const T* rt = reinterpret_cast<const T*>(raw);
-                pg.in[PR][t][j] = to_f32(rt[0 * L * N + t * N + j]);
-                pg.in[PA][t][j] = to_f32(rt[1 * L * N + t * N + j]);
-                pg.in[PB][t][j] = to_f32(rt[2 * L * N + t * N + j]);
-                pg.in[PD][t][j] = to_f32(rt[3 * L * N + t * N + j]);
-                const TW* wt = reinterpret_cast<const TW*>(raw + 4 * (L * RI::ROW));
-                pg.in[PL][t][j] = t < nt ? -ck::ex2(to_f32(wt[t * N + j]) * ck::LOG2E) : 0.f;
-            }
-            ck::group_sync(BAR);
-            if (i + 2 < cnt) issue(i + 2);  // the raw buffer is free again
+            // inputs read straight from the staging: r, a, b, dy in their 16-bit (or fp32)
+            // type, w in its own; rows past the sequence end are zero there
+            const T* rt = reinterpret_cast<const T*>(raw);
+            const TW* wt = reinterpret_cast<const TW*>(raw + 4 * (L * RI::ROW));
+            auto xin = [&](int arr, int t, int j) { return to_f32(rt[(arr * L + t) * N + j]); };  // r, a, b, dy
             // cumulative decays, GL
             int ext = 0;
             if (pt < N) {
                 float sum = 0.f;
 #pragma unroll
-                for (int t = 0; t < L; t++) sum += pg.in[PL][t][pt], pg.c[t][pt] = sum;
+                for (int t = 0; t < L; t++) {  // l = -exp(w)
+                    sum += t < nt ? -ck::ex2(to_f32(wt[t * N + pt]) * ck::LOG2E) : 0.f;
+                    pg.c[t][pt] = sum;
+                }
                 ext = sum < EXT_C;
                 stg.GL[pt] = ck::ex2(sum * ck::LOG2E);
             }
@@ -470,11 +464,12 @@ __global__ void __launch_bounds__(p1::NTH, 1)
             for (int e = pt; e < L * N; e += 128) {
                 const int t = e / N, j = e % N;
                 const float cp = t ? pg.c[t - 1][j] : 0.f, ct = pg.c[t][j], cl = pg.c[L - 1][j];
-                pg.At[t][j] = pg.in[PA][t][j] * ck::ex2(cp * ck::LOG2E);
-                pg.Rt[t][j] = pg.in[PR][t][j] * ck::ex2(ct * ck::LOG2E);
-                stg.BB[t][j] = pg.in[PB][t][j] * ck::ex2((cl - ct) * ck::LOG2E);
-                if (!ext) pg.Bh[t][j] = pg.in[PB][t][j] * ck::ex2(-ct * ck::LOG2E);
-                stg.DY[t][j] = pg.in[PD][t][j];
+                const float xb = xin(2, t, j);
+                pg.At[t][j] = xin(1, t, j) * ck::ex2(cp * ck::LOG2E);
+                pg.Rt[t][j] = xin(0, t, j) * ck::ex2(ct * ck::LOG2E);
+                stg.BB[t][j] = xb * ck::ex2((cl - ct) * ck::LOG2E);
+                if (!ext) pg.Bh[t][j] = xb * ck::ex2(-ct * ck::LOG2E);
+                stg.DY[t][j] = xin(3, t, j);
             }
             ck::group_sync(BAR);
             // Mab (strict) and Mrb (inclusive): 4 tiles of 16 x 8, one per warp
@@ -493,15 +488,15 @@ __global__ void __launch_bounds__(p1::NTH, 1)
                     const int which = e / (L * L), tt = (e / L) % L, ss = e % L;
                     float val = 0.f;
                     if (which ? ss <= tt : ss < tt) {
-                        const float* xs = which ? pg.in[PR][tt] : pg.in[PA][tt];
                         const float* cx = which ? pg.c[tt] : (tt ? pg.c[tt - 1] : nullptr);
                         for (int j = 0; j < N; j++)
-                            val = fmaf(xs[j] * pg.in[PB][ss][j], expf((cx ? cx[j] : 0.f) - pg.c[ss][j]), val);
+                            val = fmaf(xin(which ? 0 : 1, tt, j) * xin(2, ss, j), expf((cx ? cx[j] : 0.f) - pg.c[ss][j]), val);
                     }
                     pg.M[which][tt][ss] = val;
                 }
             }
             ck::group_sync(BAR);
+            if (i + 2 < cnt) issue(i + 2);  // the raw staging is free again
             // Wu = (I - Mab)^-1 At by forward substitution, one key column per thread
             if (pt < N) {
                 float x[L];

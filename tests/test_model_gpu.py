@@ -308,3 +308,32 @@ def test_prefill_graph_matches_eager_forward():
             m.head.weight.mul_(1.0)
         with pytest.raises(RuntimeError, match="PrefillGraph"):
             g()
+
+
+def test_channel_mix_fused_key_gemm_matches_op_by_op():
+    """At >= 24576 rows the fused ChannelMix runs key + squared ReLU as one tcgen05 GEMM;
+    its output matches the op-by-op torch path (key product rounded to fp16, relu, square,
+    value product)."""
+    from rwkv_mlx_b200 import model as md
+
+    cfg = md.RWKVConfig(n_layer=2, n_embd=768, dim_ffn=3072)
+    torch.manual_seed(3)
+    cm = md.RWKV_CMix_x070(cfg, 1).cuda()
+    with torch.no_grad():
+        cm.x_k.uniform_(0, 1)
+        cm.key.weight.normal_(0, 768 ** -0.5)
+        cm.value.weight.normal_(0, 3072 ** -0.5)
+    cm = cm.half()
+    B, T = 6, 4096
+    assert B * T >= md._FUSED_KEY_MIN_ROWS
+    x = torch.randn(B, T, 768, device="cuda").half()
+    with torch.no_grad():
+        fused = cm(x)
+        cfg.fused = False
+        try:
+            ref = cm(x)
+        finally:
+            cfg.fused = True
+    torch.cuda.synchronize()
+    assert rel_rms(fused.double().cpu().numpy(), ref.double().cpu().numpy()) < 3e-3
+

@@ -793,14 +793,31 @@ __global__ void __launch_bounds__(NT, 2)
         scr[2 * SA + o] = acc.Q[q];
     }
     __syncthreads();
-    if (tid < N) {
-        const int j = tid;
-        float dcl = sm.dGL[j];
-        for (int t = 0; t < L; t++) dcl += scr[2 * SA + t * LDC + j];
-        float accd = dcl;
-        for (int t = L - 1; t >= 0; t--) {
-            accd += scr[0 * SA + t * LDC + j] + (t + 1 < L ? scr[1 * SA + (t + 1) * LDC + j] : 0.f);
-            if (t < nt) dw[base + (size_t)(t0 + t) * tstride + j] = from_f32<T>(accd * fr.inl[t][j]);  // dw_t
+    {  // four threads per column j, four steps each: d l_t = dc_L + suffix sum from t
+        static_assert(NT == 4 * N && L == 16, "decay-gradient thread layout");
+        const int j = tid & (N - 1), part = tid >> 6;
+        float2* red = reinterpret_cast<float2*>(scr + 3 * SA);  // (part, column): (sum of Q, block sum)
+        float suf[4], q = 0.f;
+#pragma unroll
+        for (int i = 3; i >= 0; i--) {
+            const int t = 4 * part + i;
+            q += scr[2 * SA + t * LDC + j];
+            const float e = scr[0 * SA + t * LDC + j] + (t + 1 < L ? scr[1 * SA + (t + 1) * LDC + j] : 0.f);
+            suf[i] = i == 3 ? e : suf[i + 1] + e;
+        }
+        red[part * N + j] = make_float2(q, suf[0]);
+        __syncthreads();
+        float dcl = sm.dGL[j], later = 0.f;
+#pragma unroll
+        for (int pp = 0; pp < 4; pp++) {
+            const float2 r2 = red[pp * N + j];
+            dcl += r2.x;
+            if (pp > part) later += r2.y;
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int t = 4 * part + i;
+            if (t < nt) dw[base + (size_t)(t0 + t) * tstride + j] = from_f32<T>((dcl + later + suf[i]) * fr.inl[t][j]);
         }
     }
     // the other gradients straight from registers: two adjacent columns per row

@@ -117,6 +117,9 @@ def grouped_gemm(a: torch.Tensor, w: torch.Tensor, offsets: torch.Tensor | None 
     G, N, K2 = w.shape
     if K2 != K or (offsets is None and G != 1):
         raise ValueError("grouped_gemm: shape mismatch")
+    if offsets is not None and (offsets.dtype != torch.int32 or offsets.numel() != G + 1
+                                or not offsets.is_contiguous() or offsets.device != a.device):
+        raise ValueError("grouped_gemm: offsets must be a contiguous int32 (G + 1,) tensor on a's device")
     a = a.contiguous()
     w = w.to(a.dtype).contiguous()
     if out is None:

@@ -24,8 +24,10 @@
 //   dBb = U dX_L^T,  dKb = V dX_L^T,  dGL = rowsum(dX_L o X)
 //   dV  = Mak^T Lambda + Mrk^T dY + Kb dX_L
 // then the factor chain rule back to r, k, a, b and the reverse cumulative sum of
-// the decay gradients back to w.  All products run on mma.sync with operands split
-// into high and low TF32 parts (three products, fp32-accurate).  Chunks whose
+// the decay gradients back to w.  All products run on mma.sync: for fp32 inputs with
+// operands split into high and low TF32 parts (three products, fp32-accurate), for
+// 16-bit inputs as one product of TF32-rounded operands (the forward's precision;
+// ~6e-4 relative error against float64 for fp16).  Chunks whose
 // cumulative decay falls below e^-80 form the Mab..Mrk products and their gradients
 // element-wise from exponent differences (the factored forms would overflow).
 #include <type_traits>
@@ -50,10 +52,13 @@ __device__ __forceinline__ void split(float x, uint32_t& hi, uint32_t& lo) {
     lo = tf32(x - __uint_as_float(hi));
 }
 
-// d (one 16x8 tile) += A(16 x K) B(K x 8); accessors take tile-local indices.  AX / BX:
-// the operand's values are exactly representable in TF32 (16-bit inputs), so its low
-// part is zero and the product that uses it is skipped.
-template <bool AX = false, bool BX = false, typename FA, typename FB>
+// d (one 16x8 tile) += A(16 x K) B(K x 8); accessors take tile-local indices.  P3: split
+// each operand into high and low TF32 parts (three products, fp32-accurate; used for
+// fp32 inputs); otherwise one product of the TF32-rounded operands (16-bit inputs, the
+// precision of the forward's TF32 products).  AX / BX: the operand's values are exactly
+// representable in TF32 (16-bit inputs), so its low part is zero and the product that
+// uses it is skipped.
+template <bool P3, bool AX = false, bool BX = false, typename FA, typename FB>
 __device__ __forceinline__ void tile_mm(float (&d)[4], const FA& A, const FB& B, int K) {
     const int lane = threadIdx.x & 31, g = lane >> 2, tg = lane & 3;
     float e[4] = {0.f, 0.f, 0.f, 0.f};  // correction terms: a separate chain from d
@@ -64,19 +69,22 @@ __device__ __forceinline__ void tile_mm(float (&d)[4], const FA& A, const FB& B,
 #pragma unroll
         for (int i = 0; i < 4; i++) {
             if (AX) ah[i] = __float_as_uint(av[i]), al[i] = 0u;
-            else split(av[i], ah[i], al[i]);
+            else if (P3) split(av[i], ah[i], al[i]);
+            else ah[i] = tf32(av[i]), al[i] = 0u;
         }
 #pragma unroll
         for (int i = 0; i < 2; i++) {
             if (BX) bh[i] = __float_as_uint(bv[i]), bl[i] = 0u;
-            else split(bv[i], bh[i], bl[i]);
+            else if (P3) split(bv[i], bh[i], bl[i]);
+            else bh[i] = tf32(bv[i]), bl[i] = 0u;
         }
-        if (!AX) mma8(e, al[0], al[1], al[2], al[3], bh[0], bh[1]);
-        if (!BX) mma8(e, ah[0], ah[1], ah[2], ah[3], bl[0], bl[1]);
+        if (P3 && !AX) mma8(e, al[0], al[1], al[2], al[3], bh[0], bh[1]);
+        if (P3 && !BX) mma8(e, ah[0], ah[1], ah[2], ah[3], bl[0], bl[1]);
         mma8(d, ah[0], ah[1], ah[2], ah[3], bh[0], bh[1]);
     }
 #pragma unroll
-    for (int i = 0; i < 4; i++) d[i] += e[i];
+    for (int i = 0; i < 4; i++)
+        if (P3) d[i] += e[i];
 }
 // out(m, n, v) or, when it takes a fourth argument, out(m, n, v, slot): slot 0..3 is the
 // element's place in the thread's accumulator fragment (a compile-time constant at each
@@ -89,14 +97,14 @@ __device__ __forceinline__ void emit(const FO& out, int m, int n, float v, int s
 // C (M x Nn) = A (M x K) B (K x Nn) over the block's warps; out(m, n, v) once per element.
 // The element -> thread mapping depends only on (M, Nn), so successive calls with the
 // same shape may accumulate into the same elements without a barrier.
-template <typename FA, typename FB, typename FO>
+template <bool P3, typename FA, typename FB, typename FO>
 __device__ __forceinline__ void block_mm(int M, int Nn, int K, const FA& A, const FB& B, const FO& out) {
     const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tg = lane & 3;
     const int ntl = Nn / 8, tiles = (M / 16) * ntl;
     for (int tile = warp; tile < tiles; tile += nw) {
         const int m0 = (tile / ntl) * 16, n0 = (tile % ntl) * 8;
         float d[4] = {0.f, 0.f, 0.f, 0.f};
-        tile_mm(d, [&](int m, int k) { return A(m0 + m, k); }, [&](int k, int n) { return B(k, n0 + n); }, K);
+        tile_mm<P3>(d, [&](int m, int k) { return A(m0 + m, k); }, [&](int k, int n) { return B(k, n0 + n); }, K);
         emit(out, m0 + g, n0 + 2 * tg, d[0], 0);
         emit(out, m0 + g, n0 + 2 * tg + 1, d[1], 1);
         emit(out, m0 + g + 8, n0 + 2 * tg, d[2], 2);
@@ -116,14 +124,14 @@ template <bool AX = false, bool BX = false, typename FA, typename FB>
 __device__ __forceinline__ Seg<AX, BX, FA, FB> seg(const FA& A, const FB& B, int K) {
     return Seg<AX, BX, FA, FB>{A, B, K};
 }
-template <typename FO, typename... S>
+template <bool P3, typename FO, typename... S>
 __device__ __forceinline__ void block_mm_s(int M, int Nn, const FO& out, const S&... segs) {
     const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tg = lane & 3;
     const int ntl = Nn / 8, tiles = (M / 16) * ntl;
     for (int tile = warp; tile < tiles; tile += nw) {
         const int m0 = (tile / ntl) * 16, n0 = (tile % ntl) * 8;
         float d[4] = {0.f, 0.f, 0.f, 0.f};
-        (tile_mm<S::AX, S::BX>(d, [&](int m, int k) { return segs.A(m0 + m, k); },
+        (tile_mm<P3, S::AX, S::BX>(d, [&](int m, int k) { return segs.A(m0 + m, k); },
                                [&](int k, int n) { return segs.B(k, n0 + n); }, segs.K),
          ...);
         emit(out, m0 + g, n0 + 2 * tg, d[0], 0);
@@ -137,7 +145,7 @@ __device__ __forceinline__ void block_mm_s(int M, int Nn, const FO& out, const S
 // spread over the block's warps; out(b, m, n, v) once per element.
 // With `exact` set, block 1's B, block 2's A and both operands of block 3 are taken as
 // exactly representable in TF32 (the layout of the stacked gradient products below).
-template <typename FA, typename FB, typename FO>
+template <bool P3, typename FA, typename FB, typename FO>
 __device__ __forceinline__ void block_mm_b(int nblk, int Nn, int K, const FA& A, const FB& B, const FO& out,
                                            bool exact = false) {
     const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tg = lane & 3;
@@ -148,10 +156,10 @@ __device__ __forceinline__ void block_mm_b(int nblk, int Nn, int K, const FA& A,
         auto a_ = [&](int m, int k) { return A(bb, m, k); };
         auto b_ = [&](int k, int n) { return B(bb, k, n0 + n); };
         const int kind = exact ? bb : 0;
-        if (kind == 1) tile_mm<false, true>(d, a_, b_, K);
-        else if (kind == 2) tile_mm<true, false>(d, a_, b_, K);
-        else if (kind == 3) tile_mm<true, true>(d, a_, b_, K);
-        else tile_mm(d, a_, b_, K);
+        if (kind == 1) tile_mm<P3, false, true>(d, a_, b_, K);
+        else if (kind == 2) tile_mm<P3, true, false>(d, a_, b_, K);
+        else if (kind == 3) tile_mm<P3, true, true>(d, a_, b_, K);
+        else tile_mm<P3>(d, a_, b_, K);
         out(bb, g, n0 + 2 * tg, d[0]);
         out(bb, g, n0 + 2 * tg + 1, d[1]);
         out(bb, g + 8, n0 + 2 * tg, d[2]);
@@ -266,13 +274,13 @@ __device__ int front_factors(Front<T>& fr) {
 }
 
 // Mab, Mak (strict) and Mrb, Mrk (inclusive) for the matrices selected in `which`
-template <typename T>
+template <bool P3, typename T>
 __device__ void front_matrices(Front<T>& fr, int ext, unsigned which) {
     if (!ext) {
         int ms[4], nb = 0;
         for (int m = 0; m < 4; m++)
             if ((which >> m) & 1) ms[nb++] = m;
-        block_mm_b(nb, L, N,
+        block_mm_b<P3>(nb, L, N,
                    [&](int bb, int t, int j) { return (&fr.f[ms[bb] < 2 ? FAT : FRT][0][0])[t * LDC + j]; },
                    [&](int bb, int j, int s) { return (&fr.f[(ms[bb] & 1) ? FKH : FBH][0][0])[s * LDC + j]; },
                    [&](int bb, int t, int s, float val) {
@@ -321,7 +329,7 @@ __device__ void front_matrices(Front<T>& fr, int ext, unsigned which) {
 // ahead and read from that staging in their own type), while 8 "chain" warps run
 // dX_0 = GL o dX_L + Wu^T (Bb dX_L) + Wy^T dY.
 // Wu = (I - Mab)^-1 At comes from a forward substitution in fp32 (one key column per
-// thread); the products run on mma.sync with 3xTF32 operands as elsewhere here.
+// thread); the products run on mma.sync at the input type's precision (tile_mm).
 namespace p1 {
 constexpr int NTH = 512, NSTAGE = 3, NCW = 8;  // 8 chain warps, then two prep groups of 4 warps
 enum { BAR_CHAIN = 1, BAR_PREP0 = 2 };
@@ -345,14 +353,14 @@ struct Warps {
 };
 
 // C (M x Nn) = sum over segments A_i B_i, tiles over the group's warps (see block_mm_s)
-template <typename FO, typename... S>
+template <bool P3, typename FO, typename... S>
 __device__ __forceinline__ void gmm(Warps wp, int M, int Nn, const FO& out, const S&... segs) {
     const int lane = threadIdx.x & 31, g = lane >> 2, tg = lane & 3;
     const int ntl = Nn / 8, tiles = (M / 16) * ntl;
     for (int tile = wp.w; tile < tiles; tile += wp.n) {
         const int m0 = (tile / ntl) * 16, n0 = (tile % ntl) * 8;
         float d[4] = {0.f, 0.f, 0.f, 0.f};
-        (tile_mm<S::AX, S::BX>(d, [&](int m, int k) { return segs.A(m0 + m, k); },
+        (tile_mm<P3, S::AX, S::BX>(d, [&](int m, int k) { return segs.A(m0 + m, k); },
                                [&](int k, int n) { return segs.B(k, n0 + n); }, segs.K),
          ...);
         out(m0 + g, n0 + 2 * tg, d[0]);
@@ -397,6 +405,7 @@ __global__ void __launch_bounds__(p1::NTH, 1)
     // enters through dxl[c_hi - 1] and leaves through dxl[c_lo - 1] between parts)
     const int nch = (T_ + L - 1) / L, cnt = c_hi - c_lo;
     constexpr bool EXI = sizeof(T) == 2;  // 16-bit dy is exact in TF32
+    constexpr bool P3 = !EXI;             // three-term TF32 products for fp32 inputs
 
     if (tid == 0) {
         for (int i = 0; i < NSTAGE; i++) ck::mbar_init(&sm.full[i], 128), ck::mbar_init(&sm.empty[i], 32 * NCW);
@@ -477,7 +486,7 @@ __global__ void __launch_bounds__(p1::NTH, 1)
                 const int which = wp.w >> 1, n0 = (wp.w & 1) * 8, g = lane >> 2, tg = lane & 3;
                 float d[4] = {0.f, 0.f, 0.f, 0.f};
                 const float(*X)[LDC] = which ? pg.Rt : pg.At;
-                tile_mm(d, [&](int m, int k) { return X[m][k]; }, [&](int k, int n) { return pg.Bh[n0 + n][k]; }, N);
+                tile_mm<P3>(d, [&](int m, int k) { return X[m][k]; }, [&](int k, int n) { return pg.Bh[n0 + n][k]; }, N);
 #pragma unroll
                 for (int q = 0; q < 4; q++) {
                     const int tt = g + (q >> 1) * 8, ss = n0 + 2 * tg + (q & 1);
@@ -511,7 +520,7 @@ __global__ void __launch_bounds__(p1::NTH, 1)
             }
             ck::group_sync(BAR);
             // Wy = Rt + Mrb Wu
-            gmm(wp, L, N, [&](int t, int j, float val) { stg.WY[t][j] = pg.Rt[t][j] + val; },
+            gmm<P3>(wp, L, N, [&](int t, int j, float val) { stg.WY[t][j] = pg.Rt[t][j] + val; },
                 seg([&](int t, int s2) { return pg.M[1][t][s2]; }, [&](int s2, int j) { return stg.WU[s2][j]; }, L));
             ck::mbar_arrive(&sm.full[s]);
         }
@@ -537,13 +546,13 @@ __global__ void __launch_bounds__(p1::NTH, 1)
                 failed = true;
                 break;
             }
-            gmm(wp, L, N, [&](int t, int vv, float val) { sm.DU[t][vv] = val; },
+            gmm<P3>(wp, L, N, [&](int t, int vv, float val) { sm.DU[t][vv] = val; },
                 seg([&](int t, int j) { return stg.BB[t][j]; }, [&](int j, int vv) { return sm.D[j][vv]; }, N));
             float* out = dxl + ((size_t)bh * nch + c) * N * N;
             for (int e = tid; e < N * N / 4; e += 32 * NCW)
                 *reinterpret_cast<float4*>(out + 4 * e) = *reinterpret_cast<const float4*>(&sm.D[e / 16][(e % 16) * 4]);
             ck::bar_sync_n(BAR_CHAIN, 32 * NCW);
-            gmm(wp, N, N, [&](int j, int vv, float val) { sm.D[j][vv] = fmaf(stg.GL[j], sm.D[j][vv], val); },
+            gmm<P3>(wp, N, N, [&](int j, int vv, float val) { sm.D[j][vv] = fmaf(stg.GL[j], sm.D[j][vv], val); },
                 seg([&](int j, int t) { return stg.WU[t][j]; }, [&](int t, int vv) { return sm.DU[t][vv]; }, L),
                 seg<false, EXI>([&](int j, int t) { return stg.WY[t][j]; }, [&](int t, int vv) { return stg.DY[t][vv]; }, L));
             ck::mbar_arrive(&sm.empty[s]);
@@ -638,36 +647,37 @@ __global__ void __launch_bounds__(NT, 2)
         asm volatile("cp.async.wait_all;" ::: "memory");
     }
     __syncthreads();
-    const int ext = front_factors(fr);
-    front_matrices(fr, ext, 0b1111);
-    const auto& F = fr.f;
     constexpr bool EXI = sizeof(T) == 2;  // 16-bit v and dy are exact in TF32
+    constexpr bool P3 = !EXI;             // three-term TF32 products for fp32 inputs
+    const int ext = front_factors(fr);
+    front_matrices<P3>(fr, ext, 0b1111);
+    const auto& F = fr.f;
 
     // U = Inv (At X + Mak V)
-    block_mm_s(L, N, [&](int t, int vv, float val) { sm.G[t][vv] = val; },
+    block_mm_s<P3>(L, N, [&](int t, int vv, float val) { sm.G[t][vv] = val; },
                seg([&](int t, int j) { return F[FAT][t][j]; }, [&](int j, int vv) { return sm.Sv[vv][j]; }, N),
                seg<false, EXI>([&](int t, int s) { return fr.M[1][t][s]; }, [&](int s, int vv) { return fr.x(IV, s, vv); }, L));
     __syncthreads();
-    block_mm(L, N, L, [&](int t, int s) { return fr.Inv[t][s]; }, [&](int s, int vv) { return sm.G[s][vv]; },
+    block_mm<P3>(L, N, L, [&](int t, int s) { return fr.Inv[t][s]; }, [&](int s, int vv) { return sm.G[s][vv]; },
              [&](int t, int vv, float val) { sm.U[t][vv] = val; });
     // external gradient of U: Mrb^T dY + Bb dX_L
-    block_mm_s(L, N, [&](int t, int vv, float val) { sm.Lam[t][vv] = val; },
+    block_mm_s<P3>(L, N, [&](int t, int vv, float val) { sm.Lam[t][vv] = val; },
                seg<false, EXI>([&](int t, int s) { return fr.M[2][s][t]; }, [&](int s, int vv) { return fr.x(IDY, s, vv); }, L),
                seg([&](int t, int j) { return F[FBB][t][j]; }, [&](int j, int vv) { return sm.D[j][vv]; }, N));
     __syncthreads();
     // Lambda = Inv^T (...)  (into G, free after U)
-    block_mm(L, N, L, [&](int t, int s) { return fr.Inv[s][t]; }, [&](int s, int vv) { return sm.Lam[s][vv]; },
+    block_mm<P3>(L, N, L, [&](int t, int s) { return fr.Inv[s][t]; }, [&](int s, int vv) { return sm.Lam[s][vv]; },
              [&](int t, int vv, float val) { sm.G[t][vv] = val; });
     __syncthreads();
     const auto& Lam = sm.G;
     // gradients of the intra-chunk matrices (4 stacked 16x16 products)
-    block_mm_b(4, L, N,
+    block_mm_b<P3>(4, L, N,
                [&](int bb, int t, int vv) { return bb < 2 ? Lam[t][vv] : fr.x(IDY, t, vv); },
                [&](int bb, int vv, int s) { return (bb & 1) ? fr.x(IV, s, vv) : sm.U[s][vv]; },
                [&](int bb, int t, int s, float val) { sm.dM[bb][t][s] = (bb < 2 ? s < t : s <= t) ? val : 0.f; },
                EXI);
     // dV = Mak^T Lambda + Mrk^T dY + Kb dX_L
-    block_mm_s(L, N, [&](int s, int vv, float val, int q) { acc.dV[q] = val; },
+    block_mm_s<P3>(L, N, [&](int s, int vv, float val, int q) { acc.dV[q] = val; },
                seg([&](int s, int t) { return fr.M[1][t][s]; }, [&](int t, int vv) { return Lam[t][vv]; }, L),
                seg<false, EXI>([&](int s, int t) { return fr.M[3][t][s]; }, [&](int t, int vv) { return fr.x(IDY, t, vv); }, L),
                seg([&](int s, int j) { return F[FKB][s][j]; }, [&](int j, int vv) { return sm.D[j][vv]; }, N));
@@ -693,23 +703,23 @@ __global__ void __launch_bounds__(NT, 2)
         if (!ext) {
             auto bh_ = [&](int s, int j) { return F[FBH][s][j]; };
             auto kh_ = [&](int s, int j) { return F[FKH][s][j]; };
-            block_mm_s(L, N, outA, sA, seg([&](int t, int s) { return sm.dM[0][t][s]; }, bh_, L),
+            block_mm_s<P3>(L, N, outA, sA, seg([&](int t, int s) { return sm.dM[0][t][s]; }, bh_, L),
                        seg([&](int t, int s) { return sm.dM[1][t][s]; }, kh_, L));
-            block_mm_s(L, N, outR, sR, seg([&](int t, int s) { return sm.dM[2][t][s]; }, bh_, L),
+            block_mm_s<P3>(L, N, outR, sR, seg([&](int t, int s) { return sm.dM[2][t][s]; }, bh_, L),
                        seg([&](int t, int s) { return sm.dM[3][t][s]; }, kh_, L));
         } else {
-            block_mm_s(L, N, outA, sA);
-            block_mm_s(L, N, outR, sR);
+            block_mm_s<P3>(L, N, outA, sA);
+            block_mm_s<P3>(L, N, outR, sR);
         }
     }
-    block_mm(L, N, N, [&](int t, int vv) { return sm.U[t][vv]; }, [&](int vv, int j) { return sm.D[j][vv]; },
+    block_mm<P3>(L, N, N, [&](int t, int vv) { return sm.U[t][vv]; }, [&](int vv, int j) { return sm.D[j][vv]; },
              [&](int t, int j, float val, int q) {  // dBb: Bb = b e^{c_L - c_t}
                  const float qq = val * F[FBB][t][j];
                  acc.dB[q] += val * expf(fr.c[L - 1][j] - fr.c[t][j]);
                  acc.dC[q] -= qq;
                  acc.Q[q] += qq;
              });
-    block_mm_s(L, N,
+    block_mm_s<P3>(L, N,
                [&](int t, int j, float val, int q) {  // dKb: Kb = k e^{c_L - c_t}
                    const float qq = val * F[FKB][t][j];
                    acc.dK[q] += val * expf(fr.c[L - 1][j] - fr.c[t][j]);
@@ -722,14 +732,14 @@ __global__ void __launch_bounds__(NT, 2)
     if (!ext) {
         auto at = [&](int t, int j) { return F[FAT][t][j]; };
         auto rt = [&](int t, int j) { return F[FRT][t][j]; };
-        block_mm_s(
+        block_mm_s<P3>(
             L, N,
             [&](int s, int j, float val, int q) {  // dBh = dMab^T At + dMrb^T Rt
                 acc.dB[q] += val * expf(-fr.c[s][j]);
                 acc.dC[q] -= val * F[FBH][s][j];
             },
             seg([&](int s, int t) { return sm.dM[0][t][s]; }, at, L), seg([&](int s, int t) { return sm.dM[2][t][s]; }, rt, L));
-        block_mm_s(
+        block_mm_s<P3>(
             L, N,
             [&](int s, int j, float val, int q) {  // dKh = dMak^T At + dMrk^T Rt
                 acc.dK[q] += val * expf(-fr.c[s][j]);

@@ -56,6 +56,25 @@ __device__ __forceinline__ bool mbar_wait(unsigned long long* b, uint32_t parity
         }
     }
 }
+// Bounded wait that ignores the abort flag: a CTA that is leaving waits for its own copies
+// still in flight before its shared memory is released.
+__device__ __forceinline__ void mbar_drain(unsigned long long* b, uint32_t parity, int* err_word) {
+    const uint32_t a = smem_u32(b);
+    const long long t0 = clock64();
+    while (true) {
+        uint32_t ok;
+        asm volatile(
+            "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+            : "=r"(ok)
+            : "r"(a), "r"(parity)
+            : "memory");
+        if (ok) return;
+        if (clock64() - t0 > WAIT_CYCLES) {
+            atomicOr(err_word, 4);
+            return;
+        }
+    }
+}
 // Named barrier over one warp group (128 threads) that also ORs a predicate.
 __device__ __forceinline__ bool group_sync_or(int id, bool v) {
     uint32_t r;

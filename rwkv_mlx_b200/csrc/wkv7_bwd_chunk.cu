@@ -35,6 +35,7 @@
 #include "chunk_common.cuh"
 #include "common.cuh"
 #include "wkv7.cuh"
+#include "wkv_stage.cuh"
 
 namespace rwkv {
 namespace bwdc {
@@ -325,8 +326,9 @@ __device__ void front_matrices(Front<T>& fr, int ext, unsigned which) {
 // ---------------------------------------------------------------------------
 // Pass 1, warp-specialized.  The chain itself needs per chunk only Wu, Wy, Bb, dY and
 // GL, all functions of the inputs: two "prep" groups of 4 warps build them for
-// alternating chunks into a 3-stage ring (inputs streamed with cp.async one own chunk
-// ahead and read from that staging in their own type), while 8 "chain" warps run
+// alternating chunks into a 3-stage ring (each chunk's r, a, b, dy and w arrive as five
+// TMA boxes one own chunk ahead and are read from that staging in their own type), while
+// 8 "chain" warps run
 // dX_0 = GL o dX_L + Wu^T (Bb dX_L) + Wy^T dY.
 // Wu = (I - Mab)^-1 At comes from a forward substitution in fp32 (one key column per
 // thread); the products run on mma.sync at the input type's precision (tile_mm).
@@ -338,13 +340,12 @@ struct Stage {
     float GL[N];
 };
 template <typename T, typename TW>
-struct RawIn {  // one chunk's raw inputs as cp.async deposits them: r, a, b, dy (T), w (TW)
-    static constexpr int ROW = N * sizeof(T), ROWW = N * sizeof(TW);
-    static constexpr int PR_ = ROW / 16, PRW = ROWW / 16;  // 16-byte pieces per row
-    static constexpr int BYTES = 4 * L * ROW + L * ROWW;
+struct RawIn {  // one chunk's inputs as the TMA boxes land them (wkv_stage.cuh): r, a, b, dy, then w
+    static constexpr int ARR = wst::box_bytes<T>();
+    static constexpr int BYTES = 4 * ARR + wst::box_bytes<TW>();  // a multiple of 1024
 };
 struct Prep {
-    float c[L][LDC];
+    float c[L][LDC];  // cumulative natural-log decays (read by the extreme-decay path)
     float At[L][LDC], Rt[L][LDC], Bh[L][LDC];
     float M[2][L][LM];  // Mab (strict), Mrb (inclusive)
 };
@@ -370,37 +371,38 @@ __device__ __forceinline__ void gmm(Warps wp, int M, int Nn, const FO& out, cons
     }
 }
 
-__device__ __forceinline__ void cp16z(unsigned char* dst, const void* src, bool ok) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
-                 "l"(src), "r"(ok ? 16 : 0)
-                 : "memory");
-}
 }  // namespace p1
 
 template <typename T, typename TW>
 struct P1WSmem {
     p1::Stage st[p1::NSTAGE];
     p1::Prep pg[2];
-    unsigned char raw[2][p1::RawIn<T, TW>::BYTES];
     float D[N][LDC];  // dX_L [key][value]
     float DU[L][LDC];
     unsigned long long full[p1::NSTAGE], empty[p1::NSTAGE];
+    unsigned long long ld_full[2];  // a prep group's input boxes have landed
     int abort;
 };
+// dynamic shared memory of pass 1: the struct, then (1024-byte aligned) the two groups' staging
+template <typename T, typename TW>
+constexpr size_t p1_smem_bytes() {
+    return sizeof(P1WSmem<T, TW>) + 1024 + 2 * (size_t)p1::RawIn<T, TW>::BYTES;
+}
 
 __device__ int g_device_error_bwd;
 
 template <typename T, typename TW>
 __global__ void __launch_bounds__(p1::NTH, 1)
-    wkv7_bwd_chain_ws_kernel(const T* __restrict__ r, const TW* __restrict__ w, const T* __restrict__ a,
-                             const T* __restrict__ b, const T* __restrict__ dy, const float* __restrict__ dsT,
-                             float* __restrict__ dxl, float* __restrict__ ds0, int T_, int H, int c_lo, int c_hi) {
+    wkv7_bwd_chain_ws_kernel(const float* __restrict__ dsT, float* __restrict__ dxl, float* __restrict__ ds0, int T_,
+                             int H, int c_lo, int c_hi, const __grid_constant__ wst::InMaps maps) {
+    // maps.m[0..4]: r, a, b, dy (T) and w (TW), as wst::make_box_map builds them
     using namespace p1;
     using RI = RawIn<T, TW>;
     extern __shared__ __align__(16) unsigned char smem_p1w[];
     P1WSmem<T, TW>& sm = *reinterpret_cast<P1WSmem<T, TW>*>(smem_p1w);
+    unsigned char* rawbuf = reinterpret_cast<unsigned char*>(
+        (reinterpret_cast<uintptr_t>(smem_p1w) + sizeof(P1WSmem<T, TW>) + 1023) & ~(uintptr_t)1023);
     const int tid = threadIdx.x, warp = tid >> 5, bh = blockIdx.x, bi = bh / H, hi = bh % H;
-    const size_t tstride = (size_t)H * N, base = ((size_t)bi * T_ * H + hi) * N;
     // chunks c_hi - 1 down to c_lo (the whole sequence, or one part of it: the adjoint state
     // enters through dxl[c_hi - 1] and leaves through dxl[c_lo - 1] between parts)
     const int nch = (T_ + L - 1) / L, cnt = c_hi - c_lo;
@@ -409,6 +411,7 @@ __global__ void __launch_bounds__(p1::NTH, 1)
 
     if (tid == 0) {
         for (int i = 0; i < NSTAGE; i++) ck::mbar_init(&sm.full[i], 128), ck::mbar_init(&sm.empty[i], 32 * NCW);
+        ck::mbar_init(&sm.ld_full[0], 1), ck::mbar_init(&sm.ld_full[1], 1);
         sm.abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -420,69 +423,93 @@ __global__ void __launch_bounds__(p1::NTH, 1)
         const Warps wp{pt >> 5, 4};
         const int BAR = BAR_PREP0 + g_;
         Prep& pg = sm.pg[g_];
-        unsigned char* raw = sm.raw[g_];
-        auto issue = [&](int ii) {  // raw inputs of processing index ii (chunk c_hi - 1 - ii)
-            const int t0 = (c_hi - 1 - ii) * L, nt = min(L, T_ - t0);
-            constexpr int NTP = 4 * L * RI::PR_, ALL = NTP + L * RI::PRW;
-            for (int q = pt; q < ALL; q += 128) {
-                const void* src;
-                unsigned char* dst;
-                bool ok;
-                if (q < NTP) {
-                    const int arr = q / (L * RI::PR_), rem = q % (L * RI::PR_), row = rem / RI::PR_, pc = rem % RI::PR_;
-                    const T* ab = arr == 0 ? r : arr == 1 ? a : arr == 2 ? b : dy;
-                    ok = row < nt;
-                    src = ok ? (const void*)(ab + base + (size_t)(t0 + row) * tstride + pc * (16 / sizeof(T))) : (const void*)ab;
-                    dst = raw + arr * (L * RI::ROW) + row * RI::ROW + pc * 16;
-                } else {
-                    const int q2 = q - NTP, row = q2 / RI::PRW, pc = q2 % RI::PRW;
-                    ok = row < nt;
-                    src = ok ? (const void*)(w + base + (size_t)(t0 + row) * tstride + pc * (16 / sizeof(TW))) : (const void*)w;
-                    dst = raw + 4 * (L * RI::ROW) + row * RI::ROWW + pc * 16;
-                }
-                cp16z(dst, src, ok);
+        unsigned char* raw = rawbuf + (size_t)g_ * RI::BYTES;
+        // the inputs of processing index ii (chunk c_hi - 1 - ii): five TMA boxes issued by
+        // lane 0 of the group's warp 3 (no share of the forward substitution); the group's
+        // k-th chunk completes phase k of ld_full[g_]
+        constexpr int ISSUER = 96;
+        if (pt == ISSUER) {
+#pragma unroll
+            for (int i = 0; i < 5; i++)
+                asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.m[i])) : "memory");
+        }
+        auto issue = [&](int ii) {
+            if (pt == ISSUER) {
+                tcc::proxy_fence();  // the group's generic reads of the staging precede the TMA writes
+                tma::expect_tx(&sm.ld_full[g_], RI::BYTES);
+                const int tt = (c_hi - 1 - ii) * L;
+#pragma unroll
+                for (int i = 0; i < 4; i++) wst::load_box<T>(raw + i * RI::ARR, &maps.m[i], tt, hi, bi, &sm.ld_full[g_]);
+                wst::load_box<TW>(raw + 4 * RI::ARR, &maps.m[4], tt, hi, bi, &sm.ld_full[g_]);
             }
-            asm volatile("cp.async.commit_group;" ::: "memory");
         };
-        if (g_ < cnt) issue(g_);
+        int n_issued = 0, n_used = 0;
+        if (g_ < cnt) issue(g_), n_issued++;
         for (int i = g_; i < cnt; i += 2) {
-            asm volatile("cp.async.wait_all;" ::: "memory");
+            bool bad = !ck::mbar_wait(&sm.ld_full[g_], n_used & 1, &sm.abort, &g_device_error_bwd);
+            if (!bad) n_used++;
             const int s = i % NSTAGE, c = c_hi - 1 - i, nt = min(L, T_ - c * L);
             Stage& stg = sm.st[s];
-            const bool bad = i >= NSTAGE && !ck::mbar_wait(&sm.empty[s], ((i / NSTAGE) + 1) & 1, &sm.abort, &g_device_error_bwd);
+            if (!bad && i >= NSTAGE) bad = !ck::mbar_wait(&sm.empty[s], ((i / NSTAGE) + 1) & 1, &sm.abort, &g_device_error_bwd);
             if (ck::group_sync_or(BAR, bad)) break;
-            // inputs read straight from the staging: r, a, b, dy in their 16-bit (or fp32)
-            // type, w in its own; rows past the sequence end are zero there
-            const T* rt = reinterpret_cast<const T*>(raw);
-            const TW* wt = reinterpret_cast<const TW*>(raw + 4 * (L * RI::ROW));
-            auto xin = [&](int arr, int t, int j) { return to_f32(rt[(arr * L + t) * N + j]); };  // r, a, b, dy
-            // cumulative decays, GL
-            int ext = 0;
-            if (pt < N) {
-                float sum = 0.f;
+            // cumulative natural-log decays c_t = sum_{s <= t} -exp(w_s): step t in lane t of a
+            // 16-lane half-warp, keys j0..j0+7 per thread, a shuffle scan over the steps
+            // (rows past the sequence end are zero in the staging: their decay is 1)
+            const int t = lane & 15, j0 = 8 * (2 * wp.w + (lane >> 4));
+            const bool tok = t < nt;
+            float wv[8], cs[8], cp[8], cl[8];
+            wst::box8<TW>(raw + 4 * RI::ARR, t, j0, wv);
 #pragma unroll
-                for (int t = 0; t < L; t++) {  // l = -exp(w)
-                    sum += t < nt ? -ck::ex2(to_f32(wt[t * N + pt]) * ck::LOG2E) : 0.f;
-                    pg.c[t][pt] = sum;
+            for (int q = 0; q < 8; q++) cs[q] = tok ? -ck::ex2(wv[q] * ck::LOG2E) : 0.f;
+#pragma unroll
+            for (int o = 1; o < 16; o <<= 1) {
+#pragma unroll
+                for (int q = 0; q < 8; q++) {
+                    const float u = __shfl_up_sync(0xffffffffu, cs[q], o, 16);
+                    if (t >= o) cs[q] += u;
                 }
-                ext = sum < EXT_C;
-                stg.GL[pt] = ck::ex2(sum * ck::LOG2E);
             }
-            ext = ck::group_sync_or(BAR, ext);
+            bool ext = false;
+#pragma unroll
+            for (int q = 0; q < 8; q++) {
+                const float u = __shfl_up_sync(0xffffffffu, cs[q], 1, 16);
+                cp[q] = t ? u : 0.f;
+                cl[q] = __shfl_sync(0xffffffffu, cs[q], 15, 16);
+                ext |= cl[q] < EXT_C;
+            }
+            ck::sts8(&pg.c[t][j0], cs);
+            if (t == L - 1) {
+                float gl[8];
+#pragma unroll
+                for (int q = 0; q < 8; q++) gl[q] = ck::ex2(cs[q] * ck::LOG2E);
+                ck::sts8(&stg.GL[j0], gl);
+            }
+            const bool extg = ck::group_sync_or(BAR, ext);
             // decayed factors; Bb and dY go straight to the stage
-            for (int e = pt; e < L * N; e += 128) {
-                const int t = e / N, j = e % N;
-                const float cp = t ? pg.c[t - 1][j] : 0.f, ct = pg.c[t][j], cl = pg.c[L - 1][j];
-                const float xb = xin(2, t, j);
-                pg.At[t][j] = xin(1, t, j) * ck::ex2(cp * ck::LOG2E);
-                pg.Rt[t][j] = xin(0, t, j) * ck::ex2(ct * ck::LOG2E);
-                stg.BB[t][j] = xb * ck::ex2((cl - ct) * ck::LOG2E);
-                if (!ext) pg.Bh[t][j] = xb * ck::ex2(-ct * ck::LOG2E);
-                stg.DY[t][j] = xin(3, t, j);
+            {
+                float xr[8], xa[8], xb[8], xd[8], o1[8], o2[8];
+                wst::box8<T>(raw + 0 * RI::ARR, t, j0, xr);
+                wst::box8<T>(raw + 1 * RI::ARR, t, j0, xa);
+                wst::box8<T>(raw + 2 * RI::ARR, t, j0, xb);
+                wst::box8<T>(raw + 3 * RI::ARR, t, j0, xd);
+#pragma unroll
+                for (int q = 0; q < 8; q++)
+                    o1[q] = xa[q] * ck::ex2(cp[q] * ck::LOG2E), o2[q] = xr[q] * ck::ex2(cs[q] * ck::LOG2E);
+                ck::sts8(&pg.At[t][j0], o1);
+                ck::sts8(&pg.Rt[t][j0], o2);
+#pragma unroll
+                for (int q = 0; q < 8; q++) o1[q] = xb[q] * ck::ex2((cl[q] - cs[q]) * ck::LOG2E);
+                ck::sts8(&stg.BB[t][j0], o1);
+                if (!extg) {
+#pragma unroll
+                    for (int q = 0; q < 8; q++) o2[q] = xb[q] * ck::ex2(-cs[q] * ck::LOG2E);
+                    ck::sts8(&pg.Bh[t][j0], o2);
+                }
+                ck::sts8(&stg.DY[t][j0], xd);
             }
             ck::group_sync(BAR);
             // Mab (strict) and Mrb (inclusive): 4 tiles of 16 x 8, one per warp
-            if (!ext) {
+            if (!extg) {
                 const int which = wp.w >> 1, n0 = (wp.w & 1) * 8, g = lane >> 2, tg = lane & 3;
                 float d[4] = {0.f, 0.f, 0.f, 0.f};
                 const float(*X)[LDC] = which ? pg.Rt : pg.At;
@@ -499,13 +526,14 @@ __global__ void __launch_bounds__(p1::NTH, 1)
                     if (which ? ss <= tt : ss < tt) {
                         const float* cx = which ? pg.c[tt] : (tt ? pg.c[tt - 1] : nullptr);
                         for (int j = 0; j < N; j++)
-                            val = fmaf(xin(which ? 0 : 1, tt, j) * xin(2, ss, j), expf((cx ? cx[j] : 0.f) - pg.c[ss][j]), val);
+                            val = fmaf(wst::box1<T>(raw + (which ? 0 : 1) * RI::ARR, tt, j) * wst::box1<T>(raw + 2 * RI::ARR, ss, j),
+                                   expf((cx ? cx[j] : 0.f) - pg.c[ss][j]), val);
                     }
                     pg.M[which][tt][ss] = val;
                 }
             }
             ck::group_sync(BAR);
-            if (i + 2 < cnt) issue(i + 2);  // the raw staging is free again
+            if (i + 2 < cnt) issue(i + 2), n_issued++;  // the raw staging is free again
             // Wu = (I - Mab)^-1 At by forward substitution, one key column per thread
             if (pt < N) {
                 float x[L];
@@ -524,7 +552,9 @@ __global__ void __launch_bounds__(p1::NTH, 1)
                 seg([&](int t, int s2) { return pg.M[1][t][s2]; }, [&](int s2, int j) { return stg.WU[s2][j]; }, L));
             ck::mbar_arrive(&sm.full[s]);
         }
-        asm volatile("cp.async.wait_all;" ::: "memory");
+        // a box issued but never waited for (the loop was left early) must land before the
+        // shared memory is released
+        if (pt == ISSUER && n_issued > n_used) ck::mbar_drain(&sm.ld_full[g_], (n_issued - 1) & 1, &g_device_error_bwd);
     } else {
         // ===================== chain warps =====================
         const Warps wp{warp, NCW};
@@ -895,14 +925,20 @@ static int launch_bwd_chunked(const WkvBwdArgs& p, float* ws, cudaStream_t st) {
     using namespace bwdc;
     auto k1 = wkv7_bwd_chain_ws_kernel<T, TW>;
     auto k2 = wkv7_bwd_chunk_kernel<T, TW>;
-    const int s1 = (int)sizeof(P1WSmem<T, TW>), s2 = (int)sizeof(P2Smem<T>);
+    const int s1 = (int)p1_smem_bytes<T, TW>(), s2 = (int)sizeof(P2Smem<T>);
     cudaError_t e = cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, s1);
     if (e == cudaSuccess) e = cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, s2);
     if (e != cudaSuccess) return set_cuda_error(e);
     const int nch = (p.T + L - 1) / L, units = p.B * p.H;
+    alignas(64) wst::InMaps maps;  // pass 1's inputs: r, a, b, dy, w
+    {
+        const void* src[4] = {p.r, p.a, p.b, p.dy};
+        for (int i = 0; i < 4; i++)
+            if (wst::make_box_map<T>(&maps.m[i], src[i], p.B, p.T, p.H)) return RWKV_ERR_CUDA;
+        if (wst::make_box_map<TW>(&maps.m[4], p.w, p.B, p.T, p.H)) return RWKV_ERR_CUDA;
+    }
     auto pass1 = [&](cudaStream_t s, int lo, int hi) {
-        k1<<<units, p1::NTH, s1, s>>>((const T*)p.r, (const TW*)p.w, (const T*)p.a, (const T*)p.b, (const T*)p.dy,
-                                      p.dsT, ws, p.ds0, p.T, p.H, lo, hi);
+        k1<<<units, p1::NTH, s1, s>>>(p.dsT, ws, p.ds0, p.T, p.H, lo, hi, maps);
         return check_launch();
     };
     auto pass2 = [&](cudaStream_t s, int lo, int hi) {

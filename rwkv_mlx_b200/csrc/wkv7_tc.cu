@@ -44,6 +44,7 @@
 #include "tc_common.cuh"
 #include "tma_common.cuh"
 #include "wkv7.cuh"
+#include "wkv_stage.cuh"
 
 namespace rwkv {
 
@@ -93,42 +94,14 @@ struct __align__(128) Smem {
     int abort;
 };
 
-// Input staging of one prep group, filled by TMA with the 128-byte swizzle (16-byte piece
-// p of a 128-byte row q sits at piece p ^ (q % 8): 16 lanes reading the same column of 16
-// rows hit 8 distinct bank groups): r, k, v, a, b as 16 rows of 64 values (2 KB each),
-// then w: 16-bit like the others, fp32 as two 16-row halves of 32 values (row 16 h + t).
+// Input staging of one prep group (one TMA box per array, wkv_stage.cuh): r, k, v, a, b,
+// then w.
 template <typename T, typename TW>
 struct RawT {
-    static constexpr int ARR = L * N * (int)sizeof(T);
-    static constexpr int BYTES = 5 * ARR + L * N * (int)sizeof(TW);  // a multiple of 1024
+    static constexpr int ARR = wst::box_bytes<T>();
+    static constexpr int BYTES = 5 * ARR + wst::box_bytes<TW>();  // a multiple of 1024
 };
-__device__ __forceinline__ uint32_t swz(int q, int piece) { return (uint32_t)(q * 128 + ((piece ^ (q & 7)) << 4)); }
-// 8 values j0..j0+7 (j0 % 8 == 0) of row t of the 16-bit array arr
-template <typename T>
-__device__ __forceinline__ const unsigned char* raw8(const unsigned char* raw, int arr, int t, int j0) {
-    return raw + arr * (L * N * (int)sizeof(T)) + swz(t, j0 >> 3);
-}
-template <typename T>
-__device__ __forceinline__ float raw_at(const unsigned char* raw, int arr, int t, int j) {
-    return to_f32(*reinterpret_cast<const T*>(raw8<T>(raw, arr, t, j & ~7) + (j & 7) * 2));
-}
-template <typename T, typename TW>
-__device__ __forceinline__ void raw_w8(const unsigned char* raw, int t, int j0, float (&o)[8]) {
-    if constexpr (sizeof(TW) == 4) {
-        const unsigned char* wb = raw + 5 * (L * N * (int)sizeof(T));
-        const int q = 16 * (j0 >> 5) + t, pc = (j0 & 31) >> 2;
-        const float4 x0 = *reinterpret_cast<const float4*>(wb + swz(q, pc));
-        const float4 x1 = *reinterpret_cast<const float4*>(wb + swz(q, pc + 1));
-        o[0] = x0.x, o[1] = x0.y, o[2] = x0.z, o[3] = x0.w, o[4] = x1.x, o[5] = x1.y, o[6] = x1.z, o[7] = x1.w;
-    } else {
-        lds8<TW>(raw8<T>(raw, 5, t, j0), o);
-    }
-}
-// Tensor maps of the six inputs (all (B, T, H, 64) row-major): 16-bit as (64, T, H, B)
-// with a 64 x 16-step box, fp32 w as (32, T, 2, H, B) with a 32 x 16 x 2 box.
-struct InMaps {
-    CUtensorMap m[6];
-};
+using wst::InMaps;
 
 enum { BAR_STATE = 1, BAR_PREP0 = 2 };  // BAR_PREP0 + g for prep group g
 
@@ -254,11 +227,8 @@ __global__ void __launch_bounds__(NT, 1) wkv7_fwd_tc_kernel(const TcArgs p, cons
                 expect_tx(&sm.ld_full[g_], R::BYTES);
                 const int tt = t_abs + c * L;
 #pragma unroll
-                for (int i = 0; i < 5; i++) tma_load_4d(raw + i * R::ARR, &maps.m[i], 0, tt, hi, bi, &sm.ld_full[g_]);
-                if constexpr (sizeof(TW) == 4)
-                    tma_load_5d(raw + 5 * R::ARR, &maps.m[5], 0, tt, 0, hi, bi, &sm.ld_full[g_]);
-                else
-                    tma_load_4d(raw + 5 * R::ARR, &maps.m[5], 0, tt, hi, bi, &sm.ld_full[g_]);
+                for (int i = 0; i < 5; i++) wst::load_box<T>(raw + i * R::ARR, &maps.m[i], tt, hi, bi, &sm.ld_full[g_]);
+                wst::load_box<TW>(raw + 5 * R::ARR, &maps.m[5], tt, hi, bi, &sm.ld_full[g_]);
             }
         };
         int n_issued = 0, n_used = 0;
@@ -275,7 +245,7 @@ __global__ void __launch_bounds__(NT, 1) wkv7_fwd_tc_kernel(const TcArgs p, cons
             const int t = lane & 15, cg = 2 * pw + (lane >> 4), j0 = 8 * cg;
             const bool tok = t < nloc - c * L;
             float wv[8], cs[8], cp[8], cl[8];
-            raw_w8<T, TW>(raw, t, j0, wv);
+            wst::box8<TW>(raw + 5 * R::ARR, t, j0, wv);
 #pragma unroll
             for (int q = 0; q < 8; q++) cs[q] = tok ? -ex2(wv[q] * LOG2E) * LOG2E : 0.f;
 #pragma unroll
@@ -295,11 +265,11 @@ __global__ void __launch_bounds__(NT, 1) wkv7_fwd_tc_kernel(const TcArgs p, cons
                 ext |= cl[q] < -115.f;  // cumulative decay below e^-80
             }
             float xr[8], xk[8], xv[8], xa[8], xb[8], o1[8], o2[8];
-            lds8<T>(raw8<T>(raw, 0, t, j0), xr);
-            lds8<T>(raw8<T>(raw, 1, t, j0), xk);
-            lds8<T>(raw8<T>(raw, 2, t, j0), xv);
-            lds8<T>(raw8<T>(raw, 3, t, j0), xa);
-            lds8<T>(raw8<T>(raw, 4, t, j0), xb);
+            wst::box8<T>(raw + 0 * R::ARR, t, j0, xr);
+            wst::box8<T>(raw + 1 * R::ARR, t, j0, xk);
+            wst::box8<T>(raw + 2 * R::ARR, t, j0, xv);
+            wst::box8<T>(raw + 3 * R::ARR, t, j0, xa);
+            wst::box8<T>(raw + 4 * R::ARR, t, j0, xb);
             float ec[8], ei[8], eL[8];
 #pragma unroll
             for (int q = 0; q < 8; q++) {
@@ -368,7 +338,8 @@ __global__ void __launch_bounds__(NT, 1) wkv7_fwd_tc_kernel(const TcArgs p, cons
                         const float* cl2 = (which < 2) ? ps.Cs[tt] : ps.Cs[tt + 1];
                         const float* cr2 = ps.Cs[sidx + 1];
                         for (int jj = 0; jj < N; jj++)
-                            val = fmaf(raw_at<T>(raw, la, tt, jj) * raw_at<T>(raw, ra, sidx, jj), exp2f(cl2[jj] - cr2[jj]), val);
+                            val = fmaf(wst::box1<T>(raw + la * R::ARR, tt, jj) * wst::box1<T>(raw + ra * R::ARR, sidx, jj),
+                                        exp2f(cl2[jj] - cr2[jj]), val);
                     }
                     float(*Mo)[LDM] = which == 0 ? ps.Mab : which == 1 ? ps.Mak : which == 2 ? ps.Mrb : ps.Mrk;
                     Mo[tt][sidx] = which == 0 ? val : tf32f(val);
@@ -759,32 +730,12 @@ int launch(const TcArgs& a, const InMaps& maps, int grid, cudaStream_t st) {
     return check_launch();
 }
 
-template <typename T>
-constexpr CUtensorMapDataType map_type() {
-    return sizeof(T) == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
-                          : (std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                                                  : CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
-}
-
 template <typename T, typename TW>
 int make_in_maps(const WkvFwdArgs& p, InMaps& maps) {
-    const cuuint64_t B = p.B, T_ = p.T, H = p.H;
-    const void* src[6] = {p.r, p.k, p.v, p.a, p.b, p.w};
-    for (int i = 0; i < 6; i++) {
-        int rc;
-        if (i == 5 && sizeof(TW) == 4) {  // (32, T, 2, H, B): box 32 x 16 x 2 halves
-            const cuuint64_t dims[5] = {32, T_, 2, H, B};
-            const cuuint64_t strides[4] = {H * N * 4, 128, (cuuint64_t)N * 4, T_ * H * N * 4};
-            const cuuint32_t box[5] = {32, (cuuint32_t)L, 2, 1, 1};
-            rc = make_map_dt(&maps.m[i], map_type<TW>(), src[i], 5, dims, strides, box, true);
-        } else {  // (64, T, H, B): box 64 x 16
-            const cuuint64_t dims[4] = {(cuuint64_t)N, T_, H, B};
-            const cuuint64_t strides[3] = {H * N * 2, (cuuint64_t)N * 2, T_ * H * N * 2};
-            const cuuint32_t box[4] = {(cuuint32_t)N, (cuuint32_t)L, 1, 1};
-            rc = make_map_dt(&maps.m[i], i == 5 ? map_type<TW>() : map_type<T>(), src[i], 4, dims, strides, box, true);
-        }
-        if (rc) return RWKV_ERR_CUDA;
-    }
+    const void* src[5] = {p.r, p.k, p.v, p.a, p.b};
+    for (int i = 0; i < 5; i++)
+        if (wst::make_box_map<T>(&maps.m[i], src[i], p.B, p.T, p.H)) return RWKV_ERR_CUDA;
+    if (wst::make_box_map<TW>(&maps.m[5], p.w, p.B, p.T, p.H)) return RWKV_ERR_CUDA;
     return RWKV_OK;
 }
 

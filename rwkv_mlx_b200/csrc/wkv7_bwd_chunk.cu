@@ -41,6 +41,7 @@ namespace rwkv {
 namespace bwdc {
 using ck::L;
 using ck::N;
+using ck::LD8;
 using ck::mma8;
 using ck::tf32;
 constexpr int NT = 256;
@@ -335,8 +336,8 @@ __device__ void front_matrices(Front<T>& fr, int ext, unsigned which) {
 namespace p1 {
 constexpr int NTH = 512, NSTAGE = 3, NCW = 8;  // 8 chain warps, then two prep groups of 4 warps
 enum { BAR_CHAIN = 1, BAR_PREP0 = 2 };
-struct Stage {
-    float WU[L][LDC], WY[L][LDC], BB[L][LDC], DY[L][LDC];
+struct Stage {  // WU, WY are read as transposed operands: row pitch LD8 (conflict-free fragments)
+    float WU[L][LD8], WY[L][LD8], BB[L][LDC], DY[L][LDC];
     float GL[N];
 };
 template <typename T, typename TW>
@@ -371,14 +372,76 @@ __device__ __forceinline__ void gmm(Warps wp, int M, int Nn, const FO& out, cons
     }
 }
 
+// d[nt] (NTL adjacent 16x8 tiles) += A(16 x K) B(K x 8 NTL): each k-step's A fragment is
+// loaded and rounded once for the NTL tiles, and the NTL accumulators are independent
+// chains (see tile_mm for P3 / AX / BX; e holds the correction terms when P3).
+template <bool P3, bool AX, bool BX, int NTL, typename FA, typename FB>
+__device__ __forceinline__ void strip_mm(float (&d)[NTL][4], float (&e)[NTL][4], const FA& A, const FB& B, int K) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, tg = lane & 3;
+    for (int k0 = 0; k0 < K; k0 += 8) {
+        uint32_t ah[4], al[4];
+        const float av[4] = {A(g, k0 + tg), A(g + 8, k0 + tg), A(g, k0 + tg + 4), A(g + 8, k0 + tg + 4)};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            if (AX) ah[i] = __float_as_uint(av[i]), al[i] = 0u;
+            else if (P3) split(av[i], ah[i], al[i]);
+            else ah[i] = tf32(av[i]), al[i] = 0u;
+        }
+#pragma unroll
+        for (int nt = 0; nt < NTL; nt++) {
+            uint32_t bh[2], bl[2];
+            const float bv[2] = {B(k0 + tg, 8 * nt + g), B(k0 + tg + 4, 8 * nt + g)};
+#pragma unroll
+            for (int i = 0; i < 2; i++) {
+                if (BX) bh[i] = __float_as_uint(bv[i]), bl[i] = 0u;
+                else if (P3) split(bv[i], bh[i], bl[i]);
+                else bh[i] = tf32(bv[i]), bl[i] = 0u;
+            }
+            if (P3 && !AX) mma8(e[nt], al[0], al[1], al[2], al[3], bh[0], bh[1]);
+            if (P3 && !BX) mma8(e[nt], ah[0], ah[1], ah[2], ah[3], bl[0], bl[1]);
+            mma8(d[nt], ah[0], ah[1], ah[2], ah[3], bh[0], bh[1]);
+        }
+    }
+}
+// gmm with each warp computing a strip of NTL adjacent tiles of one 16-row block
+// (Nn a multiple of 8 NTL); out(m, n, v) once per element.
+template <bool P3, int NTL, typename FO, typename... S>
+__device__ __forceinline__ void gmm_strip(Warps wp, int M, int Nn, const FO& out, const S&... segs) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, tg = lane & 3;
+    const int nst = Nn / (8 * NTL), strips = (M / 16) * nst;
+    for (int sp = wp.w; sp < strips; sp += wp.n) {
+        const int m0 = (sp / nst) * 16, n0 = (sp % nst) * 8 * NTL;
+        float d[NTL][4], e[NTL][4];
+#pragma unroll
+        for (int nt = 0; nt < NTL; nt++)
+#pragma unroll
+            for (int i = 0; i < 4; i++) d[nt][i] = 0.f, e[nt][i] = 0.f;
+        (strip_mm<P3, S::AX, S::BX, NTL>(d, e, [&](int m, int k) { return segs.A(m0 + m, k); },
+                                         [&](int k, int n) { return segs.B(k, n0 + n); }, segs.K),
+         ...);
+#pragma unroll
+        for (int nt = 0; nt < NTL; nt++) {
+            if (P3) {
+#pragma unroll
+                for (int i = 0; i < 4; i++) d[nt][i] += e[nt][i];
+            }
+            const int n = n0 + 8 * nt + 2 * tg;
+            out(m0 + g, n, d[nt][0]);
+            out(m0 + g, n + 1, d[nt][1]);
+            out(m0 + g + 8, n, d[nt][2]);
+            out(m0 + g + 8, n + 1, d[nt][3]);
+        }
+    }
+}
+
 }  // namespace p1
 
 template <typename T, typename TW>
 struct P1WSmem {
     p1::Stage st[p1::NSTAGE];
     p1::Prep pg[2];
-    float D[N][LDC];  // dX_L [key][value]
-    float DU[L][LDC];
+    float D[N][LD8];  // dX_L [key][value]; D and DU are read as B operands: row pitch LD8
+    float DU[L][LD8];
     unsigned long long full[p1::NSTAGE], empty[p1::NSTAGE];
     unsigned long long ld_full[2];  // a prep group's input boxes have landed
     int abort;
@@ -534,21 +597,41 @@ __global__ void __launch_bounds__(p1::NTH, 1)
             }
             ck::group_sync(BAR);
             if (i + 2 < cnt) issue(i + 2), n_issued++;  // the raw staging is free again
-            // Wu = (I - Mab)^-1 At by forward substitution, one key column per thread
+            // Wu = (I - Mab)^-1 At by forward substitution, one key column per thread, in
+            // blocks of 4 rows: the earlier blocks' terms of the 4 rows are 4 independent
+            // chains, Mab rows are read as 16-byte vectors (same summation order per row)
             if (pt < N) {
                 float x[L];
 #pragma unroll
-                for (int tt = 0; tt < L; tt++) {
-                    float acc = pg.At[tt][pt];
+                for (int tb = 0; tb < L; tb += 4) {
+                    float acc[4];
 #pragma unroll
-                    for (int s2 = 0; s2 < tt; s2++) acc = fmaf(pg.M[0][tt][s2], x[s2], acc);
-                    x[tt] = acc;
-                    stg.WU[tt][pt] = acc;
+                    for (int r = 0; r < 4; r++) acc[r] = pg.At[tb + r][pt];
+#pragma unroll
+                    for (int q = 0; q < tb / 4; q++) {
+#pragma unroll
+                        for (int r = 0; r < 4; r++) {
+                            const float4 m = *reinterpret_cast<const float4*>(&pg.M[0][tb + r][4 * q]);
+                            acc[r] = fmaf(m.x, x[4 * q], acc[r]);
+                            acc[r] = fmaf(m.y, x[4 * q + 1], acc[r]);
+                            acc[r] = fmaf(m.z, x[4 * q + 2], acc[r]);
+                            acc[r] = fmaf(m.w, x[4 * q + 3], acc[r]);
+                        }
+                    }
+                    float4 md[4];
+#pragma unroll
+                    for (int r = 1; r < 4; r++) md[r] = *reinterpret_cast<const float4*>(&pg.M[0][tb + r][tb]);
+                    x[tb] = acc[0];
+                    x[tb + 1] = fmaf(md[1].x, x[tb], acc[1]);
+                    x[tb + 2] = fmaf(md[2].y, x[tb + 1], fmaf(md[2].x, x[tb], acc[2]));
+                    x[tb + 3] = fmaf(md[3].z, x[tb + 2], fmaf(md[3].y, x[tb + 1], fmaf(md[3].x, x[tb], acc[3])));
+#pragma unroll
+                    for (int r = 0; r < 4; r++) stg.WU[tb + r][pt] = x[tb + r];
                 }
             }
             ck::group_sync(BAR);
             // Wy = Rt + Mrb Wu
-            gmm<P3>(wp, L, N, [&](int t, int j, float val) { stg.WY[t][j] = pg.Rt[t][j] + val; },
+            gmm_strip<P3, 2>(wp, L, N, [&](int t, int j, float val) { stg.WY[t][j] = pg.Rt[t][j] + val; },
                 seg([&](int t, int s2) { return pg.M[1][t][s2]; }, [&](int s2, int j) { return stg.WU[s2][j]; }, L));
             ck::mbar_arrive(&sm.full[s]);
         }
@@ -582,7 +665,7 @@ __global__ void __launch_bounds__(p1::NTH, 1)
             for (int e = tid; e < N * N / 4; e += 32 * NCW)
                 *reinterpret_cast<float4*>(out + 4 * e) = *reinterpret_cast<const float4*>(&sm.D[e / 16][(e % 16) * 4]);
             ck::bar_sync_n(BAR_CHAIN, 32 * NCW);
-            gmm<P3>(wp, N, N, [&](int j, int vv, float val) { sm.D[j][vv] = fmaf(stg.GL[j], sm.D[j][vv], val); },
+            gmm_strip<P3, 4>(wp, N, N, [&](int j, int vv, float val) { sm.D[j][vv] = fmaf(stg.GL[j], sm.D[j][vv], val); },
                 seg([&](int j, int t) { return stg.WU[t][j]; }, [&](int t, int vv) { return sm.DU[t][vv]; }, L),
                 seg<false, EXI>([&](int j, int t) { return stg.WY[t][j]; }, [&](int t, int vv) { return stg.DY[t][vv]; }, L));
             ck::mbar_arrive(&sm.empty[s]);

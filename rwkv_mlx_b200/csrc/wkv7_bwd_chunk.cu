@@ -225,11 +225,9 @@ struct ChunkLoad {
                 const int col = (tid % pr) * VW;
 #pragma unroll
                 for (int i = 0; i < VW; i++) fr.inl[row][col + i] = row < nt ? -expf(to_f32(e[i])) : 0.f;
-            } else {
-                const T* e = reinterpret_cast<const T*>(&raw[arr]);
+            } else {  // one 16-byte store (rows are 16-byte aligned: pitch LDI)
                 const int col = (tid % pr) * VT;
-#pragma unroll
-                for (int i = 0; i < VT; i++) fr.in[Front<T>::slot(arr)][row][col + i] = e[i];
+                *reinterpret_cast<uint4*>(&fr.in[Front<T>::slot(arr)][row][col]) = raw[arr];
             }
         }
     }
@@ -244,32 +242,84 @@ __device__ __forceinline__ void cp_mat(float (*dst)[LDC], const float* src) {
     for (int e = threadIdx.x; e < N * N / 4; e += NT) cp16(&dst[e / 16][(e % 16) * 4], src + 4 * e);
 }
 
-// returns the CTA-uniform "extreme decay" flag
+// 4 consecutive values of a 16-bit or fp32 row in shared memory (8- / 16-byte aligned)
+template <typename T>
+__device__ __forceinline__ void lds4(const T* p, float (&o)[4]) {
+    if constexpr (sizeof(T) == 4) {
+        const float4 x = *reinterpret_cast<const float4*>(p);
+        o[0] = x.x, o[1] = x.y, o[2] = x.z, o[3] = x.w;
+    } else {
+        const uint2 x = *reinterpret_cast<const uint2*>(p);
+        const T* h = reinterpret_cast<const T*>(&x);
+#pragma unroll
+        for (int q = 0; q < 4; q++) o[q] = to_f32(h[q]);
+    }
+}
+__device__ __forceinline__ void sts4(float* p, const float (&o)[4]) {
+    *reinterpret_cast<float4*>(p) = make_float4(o[0], o[1], o[2], o[3]);
+}
+__device__ __forceinline__ float exp_(float x) { return ck::ex2(x * ck::LOG2E); }
+
+// Cumulative decays, GL and the decayed factors: step t in lane t of a 16-lane half-warp,
+// keys j0..j0+3 per thread (a shuffle scan over the steps, 16-byte row accesses).
+// Returns the CTA-uniform "extreme decay" flag.
 template <typename T>
 __device__ int front_factors(Front<T>& fr) {
-    const int tid = threadIdx.x;
-    int ext = 0;
-    if (tid < N) {
-        float s = 0.f;
+    static_assert(NT == 16 * 16, "front_factors thread layout: 16 steps x 16 groups of 4 keys");
+    const int tid = threadIdx.x, lane = tid & 31, t = lane & 15, j0 = 4 * (2 * (tid >> 5) + (lane >> 4));
+    float cs[4], cp[4], cl[4];
+    {
+        const float4 l = *reinterpret_cast<const float4*>(&fr.inl[t][j0]);
+        cs[0] = l.x, cs[1] = l.y, cs[2] = l.z, cs[3] = l.w;
+    }
 #pragma unroll
-        for (int t = 0; t < L; t++) s += fr.inl[t][tid], fr.c[t][tid] = s;
-        ext = s < EXT_C;
-        fr.GL[tid] = expf(s);
+    for (int o = 1; o < L; o <<= 1) {
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const float u = __shfl_up_sync(0xffffffffu, cs[q], o, 16);
+            if (t >= o) cs[q] += u;
+        }
+    }
+    int ext = 0;
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        const float u = __shfl_up_sync(0xffffffffu, cs[q], 1, 16);
+        cp[q] = t ? u : 0.f;
+        cl[q] = __shfl_sync(0xffffffffu, cs[q], L - 1, 16);
+        ext |= cl[q] < EXT_C;
+    }
+    sts4(&fr.c[t][j0], cs);
+    if (t == L - 1) {
+        float gl[4];
+#pragma unroll
+        for (int q = 0; q < 4; q++) gl[q] = exp_(cs[q]);
+        sts4(&fr.GL[j0], gl);
     }
     ext = __syncthreads_or(ext);
-    for (int e = tid; e < L * N; e += NT) {
-        const int t = e / N, j = e % N;
-        const float cp = t ? fr.c[t - 1][j] : 0.f, ct = fr.c[t][j], cl = fr.c[L - 1][j];
-        fr.f[FAT][t][j] = fr.x(IA, t, j) * expf(cp);
-        fr.f[FRT][t][j] = fr.x(IR, t, j) * expf(ct);
-        const float eb = expf(cl - ct);
-        fr.f[FBB][t][j] = fr.x(IB, t, j) * eb;
-        fr.f[FKB][t][j] = fr.x(IK, t, j) * eb;
-        if (!ext) {
-            const float ei = expf(-ct);
-            fr.f[FBH][t][j] = fr.x(IB, t, j) * ei;
-            fr.f[FKH][t][j] = fr.x(IK, t, j) * ei;
+    float xr[4], xa[4], xb[4], xk[4], o1[4], o2[4];
+    lds4<T>(&fr.in[Front<T>::slot(IR)][t][j0], xr);
+    lds4<T>(&fr.in[Front<T>::slot(IA)][t][j0], xa);
+    lds4<T>(&fr.in[Front<T>::slot(IB)][t][j0], xb);
+    lds4<T>(&fr.in[Front<T>::slot(IK)][t][j0], xk);
+#pragma unroll
+    for (int q = 0; q < 4; q++) o1[q] = xa[q] * exp_(cp[q]), o2[q] = xr[q] * exp_(cs[q]);
+    sts4(&fr.f[FAT][t][j0], o1);
+    sts4(&fr.f[FRT][t][j0], o2);
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        const float eb = exp_(cl[q] - cs[q]);
+        o1[q] = xb[q] * eb, o2[q] = xk[q] * eb;
+    }
+    sts4(&fr.f[FBB][t][j0], o1);
+    sts4(&fr.f[FKB][t][j0], o2);
+    if (!ext) {
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const float ei = exp_(-cs[q]);
+            o1[q] = xb[q] * ei, o2[q] = xk[q] * ei;
         }
+        sts4(&fr.f[FBH][t][j0], o1);
+        sts4(&fr.f[FKH][t][j0], o2);
     }
     __syncthreads();
     return ext;
@@ -659,8 +709,20 @@ __global__ void __launch_bounds__(p1::NTH, 1)
                 failed = true;
                 break;
             }
-            gmm<P3>(wp, L, N, [&](int t, int vv, float val) { sm.DU[t][vv] = val; },
-                seg([&](int t, int j) { return stg.BB[t][j]; }, [&](int j, int vv) { return sm.D[j][vv]; }, N));
+            {  // DU = Bb dX_L: one 16x8 tile per warp, its K = 64 as two independent chains
+                static_assert(NCW * 8 == N, "one DU tile per chain warp");
+                const int n0 = 8 * warp, g = (tid & 31) >> 2, tg = tid & 3;
+                float d0[1][4] = {}, d1[1][4] = {}, e0[1][4] = {}, e1[1][4] = {};
+                strip_mm<P3, false, false, 1>(d0, e0, [&](int m, int k) { return stg.BB[m][k]; },
+                                              [&](int k, int n) { return sm.D[k][n0 + n]; }, N / 2);
+                strip_mm<P3, false, false, 1>(d1, e1, [&](int m, int k) { return stg.BB[m][N / 2 + k]; },
+                                              [&](int k, int n) { return sm.D[N / 2 + k][n0 + n]; }, N / 2);
+                float du[4];
+#pragma unroll
+                for (int i = 0; i < 4; i++) du[i] = (d0[0][i] + d1[0][i]) + (P3 ? e0[0][i] + e1[0][i] : 0.f);
+                sm.DU[g][n0 + 2 * tg] = du[0], sm.DU[g][n0 + 2 * tg + 1] = du[1];
+                sm.DU[g + 8][n0 + 2 * tg] = du[2], sm.DU[g + 8][n0 + 2 * tg + 1] = du[3];
+            }
             float* out = dxl + ((size_t)bh * nch + c) * N * N;
             for (int e = tid; e < N * N / 4; e += 32 * NCW)
                 *reinterpret_cast<float4*>(out + 4 * e) = *reinterpret_cast<const float4*>(&sm.D[e / 16][(e % 16) * 4]);
@@ -733,18 +795,8 @@ __global__ void __launch_bounds__(NT, 2)
 #pragma unroll
     for (int q = 0; q < 4; q++)
         acc.dA[q] = acc.dR[q] = acc.dB[q] = acc.dK[q] = acc.dV[q] = acc.dC[q] = acc.dCp[q] = acc.Q[q] = 0.f;
-    if (*(volatile int*)&g_device_error_bwd) {
-        // pass 1 (earlier on this stream) gave up a bounded wait, so dX_L is not valid: no
-        // gradient of this backward may look valid either (the word stays set until read
-        // and cleared through rwkv_device_error / check_device_error)
-        for (int e = tid; e < nt * N; e += NT) {
-            const size_t off = base + (size_t)(t0 + e / N) * tstride + (e % N);
-            const T nan = from_f32<T>(__int_as_float(0x7fc00000));
-            dr[off] = nan, dw[off] = nan, dk[off] = nan, dv[off] = nan, da[off] = nan, db[off] = nan;
-        }
-        return;
-    }
-
+    // the state snapshot and dX_L by cp.async (waited for after the front below), the
+    // inputs into registers; the error word is read while they are in flight
     {
         const float* S = c == 0 ? (s0 ? s0 + (size_t)bh * N * N : nullptr) : ckpt + ((size_t)bh * (T_ / L) + c - 1) * N * N;
         if (S) {
@@ -754,17 +806,31 @@ __global__ void __launch_bounds__(NT, 2)
         }
         cp_mat(sm.D, dxl + ((size_t)bh * nch + c) * N * N);
         asm volatile("cp.async.commit_group;" ::: "memory");
-        ChunkLoad<T, TW> ld;
-        ld.issue(r, w, k, v, a, b, dy, base, tstride, t0, nt, 0x7f);
-        ld.store(fr, nt, 0x7f);
-        asm volatile("cp.async.wait_all;" ::: "memory");
     }
+    ChunkLoad<T, TW> ld;
+    ld.issue(r, w, k, v, a, b, dy, base, tstride, t0, nt, 0x7f);
+    if (*(volatile int*)&g_device_error_bwd) {
+        // pass 1 (earlier on this stream) gave up a bounded wait, so dX_L is not valid: no
+        // gradient of this backward may look valid either (the word stays set until read
+        // and cleared through rwkv_device_error / check_device_error)
+        asm volatile("cp.async.wait_all;" ::: "memory");  // nothing may still write this CTA's shared memory
+        for (int e = tid; e < nt * N; e += NT) {
+            const size_t off = base + (size_t)(t0 + e / N) * tstride + (e % N);
+            const T nan = from_f32<T>(__int_as_float(0x7fc00000));
+            dr[off] = nan, dw[off] = nan, dk[off] = nan, dv[off] = nan, da[off] = nan, db[off] = nan;
+        }
+        return;
+    }
+    ld.store(fr, nt, 0x7f);
     __syncthreads();
     constexpr bool EXI = sizeof(T) == 2;  // 16-bit v and dy are exact in TF32
     constexpr bool P3 = !EXI;             // three-term TF32 products for fp32 inputs
     const int ext = front_factors(fr);
     front_matrices<P3>(fr, ext, 0b1111);
     const auto& F = fr.f;
+    // the state snapshot and dX_L (cp.async, issued first) landed while the front ran
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncthreads();
 
     // U = Inv (At X + Mak V)
     block_mm_s<P3>(L, N, [&](int t, int vv, float val) { sm.G[t][vv] = val; },
@@ -804,11 +870,11 @@ __global__ void __launch_bounds__(NT, 2)
     {
         auto outA = [&](int t, int j, float val, int q) {  // dAt: At = a e^{c_{t-1}}
             const float cp = t ? fr.c[t - 1][j] : 0.f;
-            acc.dA[q] += val * expf(cp);
+            acc.dA[q] += val * exp_(cp);
             acc.dCp[q] += val * F[FAT][t][j];
         };
         auto outR = [&](int t, int j, float val, int q) {  // dRt: Rt = r e^{c_t}
-            acc.dR[q] += val * expf(fr.c[t][j]);
+            acc.dR[q] += val * exp_(fr.c[t][j]);
             acc.dC[q] += val * F[FRT][t][j];
         };
         auto sA = seg([&](int t, int vv) { return Lam[t][vv]; }, [&](int vv, int j) { return sm.Sv[vv][j]; }, N);
@@ -828,14 +894,14 @@ __global__ void __launch_bounds__(NT, 2)
     block_mm<P3>(L, N, N, [&](int t, int vv) { return sm.U[t][vv]; }, [&](int vv, int j) { return sm.D[j][vv]; },
              [&](int t, int j, float val, int q) {  // dBb: Bb = b e^{c_L - c_t}
                  const float qq = val * F[FBB][t][j];
-                 acc.dB[q] += val * expf(fr.c[L - 1][j] - fr.c[t][j]);
+                 acc.dB[q] += val * exp_(fr.c[L - 1][j] - fr.c[t][j]);
                  acc.dC[q] -= qq;
                  acc.Q[q] += qq;
              });
     block_mm_s<P3>(L, N,
                [&](int t, int j, float val, int q) {  // dKb: Kb = k e^{c_L - c_t}
                    const float qq = val * F[FKB][t][j];
-                   acc.dK[q] += val * expf(fr.c[L - 1][j] - fr.c[t][j]);
+                   acc.dK[q] += val * exp_(fr.c[L - 1][j] - fr.c[t][j]);
                    acc.dC[q] -= qq;
                    acc.Q[q] += qq;
                },
@@ -848,14 +914,14 @@ __global__ void __launch_bounds__(NT, 2)
         block_mm_s<P3>(
             L, N,
             [&](int s, int j, float val, int q) {  // dBh = dMab^T At + dMrb^T Rt
-                acc.dB[q] += val * expf(-fr.c[s][j]);
+                acc.dB[q] += val * exp_(-fr.c[s][j]);
                 acc.dC[q] -= val * F[FBH][s][j];
             },
             seg([&](int s, int t) { return sm.dM[0][t][s]; }, at, L), seg([&](int s, int t) { return sm.dM[2][t][s]; }, rt, L));
         block_mm_s<P3>(
             L, N,
             [&](int s, int j, float val, int q) {  // dKh = dMak^T At + dMrk^T Rt
-                acc.dK[q] += val * expf(-fr.c[s][j]);
+                acc.dK[q] += val * exp_(-fr.c[s][j]);
                 acc.dC[q] -= val * F[FKH][s][j];
             },
             seg([&](int s, int t) { return sm.dM[1][t][s]; }, at, L), seg([&](int s, int t) { return sm.dM[3][t][s]; }, rt, L));

@@ -63,8 +63,9 @@ __device__ __forceinline__ void split(float x, uint32_t& hi, uint32_t& lo) {
 template <bool P3, bool AX = false, bool BX = false, typename FA, typename FB>
 __device__ __forceinline__ void tile_mm(float (&d)[4], const FA& A, const FB& B, int K) {
     const int lane = threadIdx.x & 31, g = lane >> 2, tg = lane & 3;
-    float e[4] = {0.f, 0.f, 0.f, 0.f};  // correction terms: a separate chain from d
-    for (int k0 = 0; k0 < K; k0 += 8) {
+    float e[4] = {0.f, 0.f, 0.f, 0.f};   // correction terms: a separate chain from d
+    float d2[4] = {0.f, 0.f, 0.f, 0.f};  // odd k-steps: a second, independent chain
+    auto step = [&](int k0, float (&acc)[4]) {
         uint32_t ah[4], al[4], bh[2], bl[2];
         const float av[4] = {A(g, k0 + tg), A(g + 8, k0 + tg), A(g, k0 + tg + 4), A(g + 8, k0 + tg + 4)};
         const float bv[2] = {B(k0 + tg, g), B(k0 + tg + 4, g)};
@@ -82,11 +83,17 @@ __device__ __forceinline__ void tile_mm(float (&d)[4], const FA& A, const FB& B,
         }
         if (P3 && !AX) mma8(e, al[0], al[1], al[2], al[3], bh[0], bh[1]);
         if (P3 && !BX) mma8(e, ah[0], ah[1], ah[2], ah[3], bl[0], bl[1]);
-        mma8(d, ah[0], ah[1], ah[2], ah[3], bh[0], bh[1]);
+        mma8(acc, ah[0], ah[1], ah[2], ah[3], bh[0], bh[1]);
+    };
+    for (int k0 = 0; k0 < K; k0 += 16) {
+        step(k0, d);
+        if (k0 + 8 < K) step(k0 + 8, d2);
     }
 #pragma unroll
-    for (int i = 0; i < 4; i++)
+    for (int i = 0; i < 4; i++) {
+        d[i] += d2[i];
         if (P3) d[i] += e[i];
+    }
 }
 // out(m, n, v) or, when it takes a fourth argument, out(m, n, v, slot): slot 0..3 is the
 // element's place in the thread's accumulator fragment (a compile-time constant at each
@@ -767,9 +774,10 @@ struct P2Smem {
     Front<T> fr;
     float Sv[N][LDC];  // state at the chunk start, [value][key] (X = Sv^T); scratch at the end
     float D[N][LDC];   // dX_L, [key][value]
-    float U[L][LDC], G[L][LDC], Lam[L][LDC];
+    float U[L][LDC], G[L][LDC];
+    float Lam[L][LD8];  // read only as a B operand (row pitch LD8: conflict-free fragments)
     float dM[4][L][LM];
-    float dGL[N];
+    float dGLp[4][N];  // partial sums of dGL over four 16-value ranges
 };
 struct P2Acc {  // a thread's four elements (slots) of each gradient
     float dA[4], dR[4], dB[4], dK[4], dV[4], dC[4], dCp[4], Q[4];
@@ -860,10 +868,17 @@ __global__ void __launch_bounds__(NT, 2)
                seg([&](int s, int t) { return fr.M[1][t][s]; }, [&](int t, int vv) { return Lam[t][vv]; }, L),
                seg<false, EXI>([&](int s, int t) { return fr.M[3][t][s]; }, [&](int t, int vv) { return fr.x(IDY, t, vv); }, L),
                seg([&](int s, int j) { return F[FKB][s][j]; }, [&](int j, int vv) { return sm.D[j][vv]; }, N));
-    if (tid < N) {
+    {  // dGL = rowsum(dX_L o X), four threads per key (values 16 part .. 16 part + 15, rotated
+       // by the key so that the reads spread over the banks); the parts are summed below
+        static_assert(NT == 4 * N, "dGL thread layout");
+        const int j = tid & (N - 1), part = tid >> 6;
         float sdg = 0.f;
-        for (int vv = 0; vv < N; vv++) sdg = fmaf(sm.D[tid][vv], sm.Sv[vv][tid], sdg);
-        sm.dGL[tid] = sdg * fr.GL[tid];
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+            const int vv = 16 * part + ((i + j) & 15);
+            sdg = fmaf(sm.D[j][vv], sm.Sv[vv][j], sdg);
+        }
+        sm.dGLp[part][j] = sdg;
     }
     __syncthreads();
     // Factor gradients, accumulated in registers (same element -> thread mapping throughout).
@@ -996,7 +1011,7 @@ __global__ void __launch_bounds__(NT, 2)
         }
         red[part * N + j] = make_float2(q, suf[0]);
         __syncthreads();
-        float dcl = sm.dGL[j], later = 0.f;
+        float dcl = ((sm.dGLp[0][j] + sm.dGLp[1][j]) + (sm.dGLp[2][j] + sm.dGLp[3][j])) * fr.GL[j], later = 0.f;
 #pragma unroll
         for (int pp = 0; pp < 4; pp++) {
             const float2 r2 = red[pp * N + j];

@@ -126,7 +126,11 @@ int rwkv_wkv7_backward(const void* r, const void* w, const void* k, const void* 
  * gradients at every 16-step chunk boundary).  Two launches: the adjoint of the
  * chunk state chain per (b, h), then every chunk's input gradients in parallel.
  * Needs ckpt_len == 16 (a snapshot at every chunk boundary); other ckpt_len values,
- * or rwkv_set_wkv_impl(1), run the step-sequential backward of rwkv_wkv7_backward.  */
+ * or rwkv_set_wkv_impl(1), run the step-sequential backward of rwkv_wkv7_backward.
+ * Precision: the chunk products run on the tensor cores in TF32.  With fp16 / bf16
+ * inputs each product is one TF32 product (as in the chunked forward; gradient error
+ * ~6e-4 relative to RMS against float64 for fp16); with fp32 inputs each operand is
+ * split into two TF32 terms (three products, fp32-level gradients).  */
 size_t rwkv_wkv7_backward_workspace_size(int B, int T, int H, int N);
 int rwkv_wkv7_backward_ws(const void* r, const void* w, const void* k, const void* v,
                           const void* a, const void* b, const void* dy, const float* s0,

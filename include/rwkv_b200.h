@@ -102,9 +102,10 @@ int rwkv_wkv7_forward_ws(const void* r, const void* w, const void* k, const void
                          float* sT, float* ckpt, float* sa, int B, int T, int H, int N,
                          int dtype, int w_dtype, int ckpt_len, void* workspace,
                          size_t workspace_bytes, void* stream);
-/* Segments per sequence of rwkv_wkv7_forward_ws: 0 automatic (default), n >= 1
- * fixed (capped at the chunk count).  Process-wide; meant for testing.  No
- * counterpart in the reference. */
+/* Segments per sequence of rwkv_wkv7_forward_ws and of the chunked backward's
+ * adjoint chain (rwkv_wkv7_backward_ws): 0 automatic (default), n >= 1 fixed
+ * (capped at the chunk count; the backward keeps segments of at least 3 chunks).
+ * Process-wide; meant for testing.  No counterpart in the reference. */
 int rwkv_set_wkv_segments(int nseg);
 
 /* WKV-7 backward, exact (no division by the decay).
@@ -125,6 +126,10 @@ int rwkv_wkv7_backward(const void* r, const void* w, const void* k, const void* 
  * workspace of rwkv_wkv7_backward_workspace_size(B, T, H, N) bytes (fp32 state
  * gradients at every 16-step chunk boundary).  Two launches: the adjoint of the
  * chunk state chain per (b, h), then every chunk's input gradients in parallel.
+ * When B*H chains would leave most SMs idle (B*H <= #SMs / 4), the chain is cut into
+ * segments: a transition pass computes each segment's affine map of the state gradient
+ * (in the workspace's own per-chunk slots), a scan composes them, and all segments run
+ * in parallel; the workspace size is the same.
  * Needs ckpt_len == 16 (a snapshot at every chunk boundary); other ckpt_len values,
  * or rwkv_set_wkv_impl(1), run the step-sequential backward of rwkv_wkv7_backward.
  * Precision: the chunk products run on the tensor cores in TF32.  With fp16 / bf16

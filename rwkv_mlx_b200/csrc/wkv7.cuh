@@ -41,7 +41,8 @@ int set_device_error_gemm(int value);
 extern int g_wkv_impl;  // 0 auto, 1 step-sequential, 2 chunked (mma.sync), 3 chunked (tcgen05)
 int wkv7_bwd_seq(const WkvBwdArgs& p, cudaStream_t st);
 size_t wkv7_bwd_chunk_ws_bytes(int B, int T, int H);
-int wkv7_bwd_chunked(const WkvBwdArgs& p, float* ws, cudaStream_t st);
+// force_nseg > 0: pass-1 segment count (tests); 0: automatic
+int wkv7_bwd_chunked(const WkvBwdArgs& p, float* ws, int force_nseg, cudaStream_t st);
 int wkv7_step_launch(float* S, const void* r, const void* w, const void* k, const void* v,
                      const void* a, const void* b, void* y, int Bs, int H, int dtype, int w_dtype,
                      int w_mode, cudaStream_t st);

@@ -156,7 +156,7 @@ extern "C" int rwkv_wkv7_backward_ws(const void* r, const void* w, const void* k
     if (g_wkv_impl == 1 || ckpt_len != 16 || !al) return wkv7_bwd_seq(p, (cudaStream_t)stream);
     if (!workspace || workspace_bytes < wkv7_bwd_chunk_ws_bytes(B, T, H)) return RWKV_ERR_WORKSPACE;
     if (!aligned(workspace, 16)) return RWKV_ERR_ALIGN;
-    return wkv7_bwd_chunked(p, (float*)workspace, (cudaStream_t)stream);
+    return wkv7_bwd_chunked(p, (float*)workspace, g_wkv_segments, (cudaStream_t)stream);
 }
 
 extern "C" int rwkv_wkv7_step(float* S, const void* r, const void* w, const void* k,

@@ -493,39 +493,54 @@ __device__ __forceinline__ void gmm_strip(Warps wp, int M, int Nn, const FO& out
 
 }  // namespace p1
 
-template <typename T, typename TW>
+template <typename T, typename TW, bool TR>
 struct P1WSmem {
+    // D and DU are read as B operands: a row pitch of 8 mod 32 floats (conflict-free
+    // fragments).  The transition pass (TR) carries 128 value columns: [C | M].
+    static constexpr int DC = TR ? 2 * N : N, DP = TR ? 2 * N + 8 : LD8;
     p1::Stage st[p1::NSTAGE];
     p1::Prep pg[2];
-    float D[N][LD8];  // dX_L [key][value]; D and DU are read as B operands: row pitch LD8
-    float DU[L][LD8];
+    float D[N][DP];  // dX_L [key][value]
+    float DU[L][DP];
     unsigned long long full[p1::NSTAGE], empty[p1::NSTAGE];
     unsigned long long ld_full[2];  // a prep group's input boxes have landed
     int abort;
 };
 // dynamic shared memory of pass 1: the struct, then (1024-byte aligned) the two groups' staging
-template <typename T, typename TW>
+template <typename T, typename TW, bool TR>
 constexpr size_t p1_smem_bytes() {
-    return sizeof(P1WSmem<T, TW>) + 1024 + 2 * (size_t)p1::RawIn<T, TW>::BYTES;
+    return sizeof(P1WSmem<T, TW, TR>) + 1024 + 2 * (size_t)p1::RawIn<T, TW>::BYTES;
 }
 
 __device__ int g_device_error_bwd;
 
-template <typename T, typename TW>
+// MODE: P1_PLAIN runs chunks c_hi0 - 1 down to c_lo0 (the whole sequence, or one part of
+// it: the adjoint state enters through dxl[c_hi - 1] and leaves through dxl[c_lo - 1]
+// between parts).  Segmented (blockIdx.y = segment s of seg_len chunks, the top segment
+// taking the remainder): P1_TRANS runs segments s >= 1 from the augmented state
+// [0 | I] (64 x 128) and stores the segment's affine map D_out = M D_in + C as C into
+// dxl[lo] and M into dxl[lo + 1]; P1_FINAL runs every segment from the state the scan
+// left in dxl[hi - 1] (dsT for the top segment) and writes dX_L of its chunks.
+enum { P1_PLAIN = 0, P1_TRANS = 1, P1_FINAL = 2 };
+template <typename T, typename TW, int MODE>
 __global__ void __launch_bounds__(p1::NTH, 1)
     wkv7_bwd_chain_ws_kernel(const float* __restrict__ dsT, float* __restrict__ dxl, float* __restrict__ ds0, int T_,
-                             int H, int c_lo, int c_hi, const __grid_constant__ wst::InMaps maps) {
+                             int H, int c_lo0, int c_hi0, int seg_len, const __grid_constant__ wst::InMaps maps) {
     // maps.m[0..4]: r, a, b, dy (T) and w (TW), as wst::make_box_map builds them
     using namespace p1;
     using RI = RawIn<T, TW>;
+    constexpr bool TR = MODE == P1_TRANS;
+    using SM = P1WSmem<T, TW, TR>;
     extern __shared__ __align__(16) unsigned char smem_p1w[];
-    P1WSmem<T, TW>& sm = *reinterpret_cast<P1WSmem<T, TW>*>(smem_p1w);
+    SM& sm = *reinterpret_cast<SM*>(smem_p1w);
     unsigned char* rawbuf = reinterpret_cast<unsigned char*>(
-        (reinterpret_cast<uintptr_t>(smem_p1w) + sizeof(P1WSmem<T, TW>) + 1023) & ~(uintptr_t)1023);
+        (reinterpret_cast<uintptr_t>(smem_p1w) + sizeof(SM) + 1023) & ~(uintptr_t)1023);
     const int tid = threadIdx.x, warp = tid >> 5, bh = blockIdx.x, bi = bh / H, hi = bh % H;
-    // chunks c_hi - 1 down to c_lo (the whole sequence, or one part of it: the adjoint state
-    // enters through dxl[c_hi - 1] and leaves through dxl[c_lo - 1] between parts)
-    const int nch = (T_ + L - 1) / L, cnt = c_hi - c_lo;
+    const int nch = (T_ + L - 1) / L, nsegs = MODE == P1_PLAIN ? 1 : nch / seg_len;
+    const int sg = MODE == P1_TRANS ? (int)blockIdx.y + 1 : (int)blockIdx.y;
+    const int c_lo = MODE == P1_PLAIN ? c_lo0 : sg * seg_len;
+    const int c_hi = MODE == P1_PLAIN ? c_hi0 : (sg == nsegs - 1 ? nch : c_lo + seg_len);
+    const int cnt = c_hi - c_lo;
     constexpr bool EXI = sizeof(T) == 2;  // 16-bit dy is exact in TF32
     constexpr bool P3 = !EXI;             // three-term TF32 products for fp32 inputs
 
@@ -698,7 +713,12 @@ __global__ void __launch_bounds__(p1::NTH, 1)
     } else {
         // ===================== chain warps =====================
         const Warps wp{warp, NCW};
-        if (c_hi == nch) {
+        if constexpr (TR) {  // [C | M] = [0 | I]
+            for (int e = tid; e < N * 2 * N; e += 32 * NCW) {
+                const int j = e / (2 * N), vv = e % (2 * N);
+                sm.D[j][vv] = vv == N + j ? 1.f : 0.f;
+            }
+        } else if (c_hi == nch) {
             for (int e = tid; e < N * N; e += 32 * NCW) {  // D = dsT^T
                 const int vv = e / N, j = e % N;
                 sm.D[j][vv] = dsT ? dsT[(size_t)bh * N * N + e] : 0.f;
@@ -716,9 +736,11 @@ __global__ void __launch_bounds__(p1::NTH, 1)
                 failed = true;
                 break;
             }
-            {  // DU = Bb dX_L: one 16x8 tile per warp, its K = 64 as two independent chains
+#pragma unroll
+            for (int hv = 0; hv < SM::DC / N; hv++) {  // DU = Bb dX_L: one 16x8 tile per warp
+                // and 64 columns, its K = 64 as two independent chains
                 static_assert(NCW * 8 == N, "one DU tile per chain warp");
-                const int n0 = 8 * warp, g = (tid & 31) >> 2, tg = tid & 3;
+                const int n0 = N * hv + 8 * warp, g = (tid & 31) >> 2, tg = tid & 3;
                 float d0[1][4] = {}, d1[1][4] = {}, e0[1][4] = {}, e1[1][4] = {};
                 strip_mm<P3, false, false, 1>(d0, e0, [&](int m, int k) { return stg.BB[m][k]; },
                                               [&](int k, int n) { return sm.D[k][n0 + n]; }, N / 2);
@@ -730,25 +752,80 @@ __global__ void __launch_bounds__(p1::NTH, 1)
                 sm.DU[g][n0 + 2 * tg] = du[0], sm.DU[g][n0 + 2 * tg + 1] = du[1];
                 sm.DU[g + 8][n0 + 2 * tg] = du[2], sm.DU[g + 8][n0 + 2 * tg + 1] = du[3];
             }
-            float* out = dxl + ((size_t)bh * nch + c) * N * N;
-            for (int e = tid; e < N * N / 4; e += 32 * NCW)
-                *reinterpret_cast<float4*>(out + 4 * e) = *reinterpret_cast<const float4*>(&sm.D[e / 16][(e % 16) * 4]);
+            if constexpr (!TR) {
+                float* out = dxl + ((size_t)bh * nch + c) * N * N;
+                for (int e = tid; e < N * N / 4; e += 32 * NCW)
+                    *reinterpret_cast<float4*>(out + 4 * e) = *reinterpret_cast<const float4*>(&sm.D[e / 16][(e % 16) * 4]);
+            }
             ck::bar_sync_n(BAR_CHAIN, 32 * NCW);
             gmm_strip<P3, 4>(wp, N, N, [&](int j, int vv, float val) { sm.D[j][vv] = fmaf(stg.GL[j], sm.D[j][vv], val); },
                 seg([&](int j, int t) { return stg.WU[t][j]; }, [&](int t, int vv) { return sm.DU[t][vv]; }, L),
                 seg<false, EXI>([&](int j, int t) { return stg.WY[t][j]; }, [&](int t, int vv) { return stg.DY[t][vv]; }, L));
+            if constexpr (TR) {  // the M columns: no dY term
+                gmm_strip<P3, 4>(wp, N, N, [&](int j, int vv, float val) { sm.D[j][N + vv] = fmaf(stg.GL[j], sm.D[j][N + vv], val); },
+                    seg([&](int j, int t) { return stg.WU[t][j]; }, [&](int t, int vv) { return sm.DU[t][N + vv]; }, L));
+            }
             ck::mbar_arrive(&sm.empty[s]);
         }
         if (failed && tid == 0) sm.abort = 1;
         ck::bar_sync_n(BAR_CHAIN, 32 * NCW);
+        if constexpr (TR) {  // the segment's map: C into dxl[c_lo], M into dxl[c_lo + 1] (row-major)
+            if (!failed) {
+                float* oc = dxl + ((size_t)bh * nch + c_lo) * N * N;
+                for (int e = tid; e < 2 * N * N / 4; e += 32 * NCW) {
+                    const int half = e / (N * N / 4), q = e % (N * N / 4);
+                    *reinterpret_cast<float4*>(oc + (size_t)half * N * N + 4 * q) =
+                        *reinterpret_cast<const float4*>(&sm.D[q / 16][N * half + (q % 16) * 4]);
+                }
+            }
+            return;
+        }
         if (!failed && ds0 && c_lo == 0) {
             for (int e = tid; e < N * N; e += 32 * NCW) ds0[(size_t)bh * N * N + e] = sm.D[e % N][e / N];
         }
-        if (!failed && c_lo > 0) {  // hand the adjoint state to the part below
+        if (!failed && c_lo > 0 && MODE == P1_PLAIN) {  // hand the adjoint state to the part below
             float* out = dxl + ((size_t)bh * nch + c_lo - 1) * N * N;
             for (int e = tid; e < N * N / 4; e += 32 * NCW)
                 *reinterpret_cast<float4*>(out + 4 * e) = *reinterpret_cast<const float4*>(&sm.D[e / 16][(e % 16) * 4]);
         }
+    }
+}
+
+// Segmented pass 1, between the two launches: the adjoint state entering each segment
+// from above, top segment first: D_in(nsegs - 1) = dsT^T (or 0), then
+// D_in(s - 1) = M_s D_in(s) + C_s with segment s's map from the transition pass, written
+// to dxl[lo(s) - 1] (the top chunk slot of segment s - 1, where the final pass starts).
+// The value columns are independent: eight per CTA, fp32 FMAs.
+__global__ void __launch_bounds__(256)
+    wkv7_bwd_seg_scan_kernel(const float* __restrict__ dsT, float* __restrict__ dxl, int nch, int seg_len) {
+    __shared__ __align__(16) float Ms[N][LDC];
+    __shared__ float Din[N][8], Cs[N][8];
+    const int bh = blockIdx.x, v0 = 8 * blockIdx.y, tid = threadIdx.x, k = tid >> 2, c2 = (tid & 3) * 2;
+    const int nsegs = nch / seg_len;
+    float* base = dxl + (size_t)bh * nch * N * N;
+    for (int e = tid; e < N * 8; e += 256) {
+        const int j = e >> 3, cc = e & 7;
+        Din[j][cc] = dsT ? dsT[((size_t)bh * N + v0 + cc) * N + j] : 0.f;
+    }
+    for (int sg = nsegs - 1; sg >= 1; sg--) {
+        const float* C = base + (size_t)(sg * seg_len) * N * N;
+        const float* M = C + (size_t)N * N;
+        __syncthreads();  // Din written, the previous step's reads of Ms done
+        for (int e = tid; e < N * N / 4; e += 256)
+            *reinterpret_cast<float4*>(&Ms[e >> 4][(e & 15) * 4]) = reinterpret_cast<const float4*>(M)[e];
+        for (int e = tid; e < N * 8; e += 256) Cs[e >> 3][e & 7] = C[(size_t)(e >> 3) * N + v0 + (e & 7)];
+        __syncthreads();
+        float a0 = Cs[k][c2], a1 = Cs[k][c2 + 1];
+#pragma unroll 8
+        for (int j = 0; j < N; j++) {
+            const float m = Ms[k][j];
+            a0 = fmaf(m, Din[j][c2], a0);
+            a1 = fmaf(m, Din[j][c2 + 1], a1);
+        }
+        __syncthreads();  // every read of Din done
+        Din[k][c2] = a0, Din[k][c2 + 1] = a1;
+        float* out = base + (size_t)(sg * seg_len - 1) * N * N + (size_t)k * N + v0 + c2;
+        out[0] = a0, out[1] = a1;
     }
 }
 
@@ -1085,12 +1162,17 @@ const PartStreams* part_streams() {
 }  // namespace
 
 template <typename T, typename TW>
-static int launch_bwd_chunked(const WkvBwdArgs& p, float* ws, cudaStream_t st) {
+static int launch_bwd_chunked(const WkvBwdArgs& p, float* ws, int force_nseg, cudaStream_t st) {
     using namespace bwdc;
-    auto k1 = wkv7_bwd_chain_ws_kernel<T, TW>;
+    auto k1 = wkv7_bwd_chain_ws_kernel<T, TW, P1_PLAIN>;
+    auto k1t = wkv7_bwd_chain_ws_kernel<T, TW, P1_TRANS>;
+    auto k1f = wkv7_bwd_chain_ws_kernel<T, TW, P1_FINAL>;
     auto k2 = wkv7_bwd_chunk_kernel<T, TW>;
-    const int s1 = (int)p1_smem_bytes<T, TW>(), s2 = (int)sizeof(P2Smem<T>);
+    const int s1 = (int)p1_smem_bytes<T, TW, false>(), s1t = (int)p1_smem_bytes<T, TW, true>();
+    const int s2 = (int)sizeof(P2Smem<T>);
     cudaError_t e = cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, s1);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k1t, cudaFuncAttributeMaxDynamicSharedMemorySize, s1t);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k1f, cudaFuncAttributeMaxDynamicSharedMemorySize, s1);
     if (e == cudaSuccess) e = cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, s2);
     if (e != cudaSuccess) return set_cuda_error(e);
     const int nch = (p.T + L - 1) / L, units = p.B * p.H;
@@ -1102,7 +1184,7 @@ static int launch_bwd_chunked(const WkvBwdArgs& p, float* ws, cudaStream_t st) {
         if (wst::make_box_map<TW>(&maps.m[4], p.w, p.B, p.T, p.H)) return RWKV_ERR_CUDA;
     }
     auto pass1 = [&](cudaStream_t s, int lo, int hi) {
-        k1<<<units, p1::NTH, s1, s>>>(p.dsT, ws, p.ds0, p.T, p.H, lo, hi, maps);
+        k1<<<units, p1::NTH, s1, s>>>(p.dsT, ws, p.ds0, p.T, p.H, lo, hi, 0, maps);
         return check_launch();
     };
     auto pass2 = [&](cudaStream_t s, int lo, int hi) {
@@ -1112,6 +1194,28 @@ static int launch_bwd_chunked(const WkvBwdArgs& p, float* ws, cudaStream_t st) {
                                                 p.H, lo);
         return check_launch();
     };
+    // Few (b, h) chains (at most a quarter of the SMs): pass 1 runs in segments of whole
+    // chunks.  The adjoint map over a segment is affine in the state entering it from above,
+    // D_out = M D_in + C (M: 64 x 64 over the keys), so a transition pass computes every
+    // segment's [C | M] from [0 | I] (twice the chain's columns), a scan composes them top
+    // down, and the final pass runs all segments in parallel; then pass 2 on all SMs.
+    {
+        int want = force_nseg > 0 ? force_nseg : min(sm_count() / units, nch / 8);
+        if (force_nseg <= 0 && want < 4) want = 1;
+        const int seg_len = want > 1 ? max(3, nch / want) : nch;
+        const int nsegs = nch / seg_len;  // the top segment takes the remainder
+        if (nsegs >= 2) {
+            k1t<<<dim3(units, nsegs - 1), p1::NTH, s1t, st>>>(p.dsT, ws, nullptr, p.T, p.H, 0, 0, seg_len, maps);
+            int rc = check_launch();
+            if (rc) return rc;
+            wkv7_bwd_seg_scan_kernel<<<dim3(units, N / 8), 256, 0, st>>>(p.dsT, ws, nch, seg_len);
+            rc = check_launch();
+            if (rc) return rc;
+            k1f<<<dim3(units, nsegs), p1::NTH, s1, st>>>(p.dsT, ws, p.ds0, p.T, p.H, 0, 0, seg_len, maps);
+            rc = check_launch();
+            return rc ? rc : pass2(st, 0, nch);
+        }
+    }
     // Pass 1 occupies one SM per (b, h).  When that leaves SMs idle, the chain runs in
     // parts (top chunks first) on a high-priority side stream, and pass 2 of each part
     // starts on the caller's stream as soon as its part of the chain is done, on the SMs
@@ -1144,8 +1248,8 @@ int set_device_error_bwd(int value) {
     return set_cuda_error(cudaMemcpyToSymbol(bwdc::g_device_error_bwd, &value, sizeof(int)));
 }
 
-int wkv7_bwd_chunked(const WkvBwdArgs& p, float* ws, cudaStream_t st) {
-    RWKV_DISPATCH_DTYPE_W(p.dtype, p.w_dtype, T, TW, return launch_bwd_chunked<T, TW>(p, ws, st));
+int wkv7_bwd_chunked(const WkvBwdArgs& p, float* ws, int force_nseg, cudaStream_t st) {
+    RWKV_DISPATCH_DTYPE_W(p.dtype, p.w_dtype, T, TW, return launch_bwd_chunked<T, TW>(p, ws, force_nseg, st));
     return RWKV_OK;
 }
 

@@ -1,9 +1,13 @@
-"""Segment-parallel tcgen05 WKV-7 forward and the abort path (need a B200).
+"""Segment-parallel tcgen05 WKV-7 forward, segmented backward chain, and the abort path
+(need a B200).
 
 The sequence is cut into segments whose affine state maps are computed by a
 transition pass and composed by a scan; every output (y, sa, 16-step snapshots,
 final state) must match the float64 oracle run over the whole sequence, within the
-chunked kernels' TF32 tolerance (2e-3 relative to RMS for fp16, 6e-3 for bf16).
+chunked kernels' TF32 tolerance (2e-3 relative to RMS for fp16 and fp32, 6e-3 for
+bf16).  The backward's adjoint chain is segmented the same way (affine maps of the
+state gradient, composed top down); its gradients, including the initial-state
+gradient with a final-state gradient given, must match the float64 oracle too.
 """
 
 import numpy as np
@@ -85,6 +89,66 @@ def test_automatic_segments_at_one_sequence_per_gpu():
     assert rel_rms(y.double().cpu().numpy(), _bt(ye)) < 2e-3
     assert rel_rms(sT.cpu().numpy(), sTe) < 2e-3
     assert rel_rms(y.double().cpu().numpy(), y1.double().cpu().numpy()) < 2e-3
+
+
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("B,T,H,nseg", [(1, 1024, 2, 3), (2, 777, 1, 5), (1, 256, 2, 16)])
+def test_segmented_backward_matches_oracle(dt, B, T, H, nseg):
+    """Forced segment counts for the backward's adjoint chain (a ragged top segment,
+    three-chunk segments), with an initial state, a final-state gradient and ds0."""
+    from rwkv_mlx_b200 import _native, wkv7
+
+    inp = wkv_inputs(B, T, H, seed=T + 7 * nseg)
+    d, h = {}, {}
+    for n, x in inp.items():
+        t = torch.tensor(_bt(x), dtype=torch.float32 if n == "w" else dt, device="cuda")
+        d[n], h[n] = t, t.double().cpu().numpy().reshape(x.shape)
+    rng = np.random.default_rng(nseg + 1)
+    s0 = rng.standard_normal((B, H, 64, 64)) * 0.3
+    dsT = rng.standard_normal((B, H, 64, 64)) * 0.1
+    s0d = torch.tensor(s0, dtype=torch.float32, device="cuda")
+    dsTd = torch.tensor(dsT, dtype=torch.float32, device="cuda")
+    _, ck, _, _ = wkv7._fwd(d["r"], d["w"], d["k"], d["v"], d["a"], d["b"], s0=s0d, want_ckpt=True)
+    _segments(nseg)
+    try:
+        grads, ds0 = wkv7._bwd(d["r"], d["w"], d["k"], d["v"], d["a"], d["b"], d["dy"], ck, s0=s0d, dsT=dsTd,
+                               want_ds0=True)
+        torch.cuda.synchronize()
+    finally:
+        _segments(0)
+    assert _native.lib().rwkv_device_error(1) == 0
+    ge = wo.wkv7_backward_exact(h["r"], h["w"], h["k"], h["v"], h["a"], h["b"], h["dy"], s0=s0, dsT=dsT)
+    tol = 6e-3 if dt == torch.bfloat16 else 2e-3
+    for name, g, e in zip(["dr", "dw", "dk", "dv", "da", "db"], grads, ge[:6]):
+        err = rel_rms(g.double().cpu().numpy(), _bt(e))
+        assert err < tol, f"{name}: {err}"
+    assert rel_rms(ds0.cpu().numpy(), ge[6]) < tol
+
+
+def test_automatic_backward_segments_at_one_sequence_per_gpu():
+    """B=1, T=4096, H=12: the automatic choice segments the adjoint chain; the gradients
+    match the oracle and the unsegmented chain."""
+    from rwkv_mlx_b200 import _native, wkv7
+
+    B, T, H = 1, 4096, 12
+    inp = wkv_inputs(B, T, H, seed=31)
+    d, h = {}, {}
+    for n, x in inp.items():
+        t = torch.tensor(_bt(x), dtype=torch.float32 if n == "w" else torch.float16, device="cuda")
+        d[n], h[n] = t, t.double().cpu().numpy().reshape(x.shape)
+    _, ck, _, _ = wkv7._fwd(d["r"], d["w"], d["k"], d["v"], d["a"], d["b"], want_ckpt=True)
+    grads, _ = wkv7._bwd(d["r"], d["w"], d["k"], d["v"], d["a"], d["b"], d["dy"], ck)
+    _segments(1)
+    try:
+        grads1, _ = wkv7._bwd(d["r"], d["w"], d["k"], d["v"], d["a"], d["b"], d["dy"], ck)
+    finally:
+        _segments(0)
+    torch.cuda.synchronize()
+    assert _native.lib().rwkv_device_error(1) == 0
+    ge = wo.wkv7_backward_exact(h["r"], h["w"], h["k"], h["v"], h["a"], h["b"], h["dy"])
+    for name, g, g1, e in zip(["dr", "dw", "dk", "dv", "da", "db"], grads, grads1, ge[:6]):
+        assert rel_rms(g.double().cpu().numpy(), _bt(e)) < 2e-3, name
+        assert rel_rms(g.double().cpu().numpy(), g1.double().cpu().numpy()) < 2e-3, name
 
 
 def test_host_set_device_error_raises():

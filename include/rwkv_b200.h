@@ -137,6 +137,10 @@ int rwkv_wkv7_backward(const void* r, const void* w, const void* k, const void* 
  * ~6e-4 relative to RMS against float64 for fp16); with fp32 inputs each operand is
  * split into two TF32 terms (three products, fp32-level gradients).  */
 size_t rwkv_wkv7_backward_workspace_size(int B, int T, int H, int N);
+/* Kernels rwkv_wkv7_backward_ws enqueues on the chunked path for these sizes on the
+ * current device (2, 4 when segmented, 8 when the chain runs in parts; 0 for invalid
+ * sizes), for callers that count launches.  No counterpart in the reference. */
+int rwkv_wkv7_backward_launch_count(int B, int T, int H, int N);
 int rwkv_wkv7_backward_ws(const void* r, const void* w, const void* k, const void* v,
                           const void* a, const void* b, const void* dy, const float* s0,
                           const float* dsT, const float* ckpt, void* dr, void* dw, void* dk,

@@ -41,6 +41,7 @@ SIGNATURES = {
     "rwkv_wkv7_forward_workspace_size": (_SZ, [_I] * 5),
     "rwkv_wkv7_forward_ws": (_I, [_P] * 11 + [_I] * 7 + [_P, _SZ, _P]),
     "rwkv_set_wkv_segments": (_I, [_I]),
+    "rwkv_wkv7_backward_launch_count": (_I, [_I, _I, _I, _I]),
     "rwkv_debug_force_wait_timeout": (_I, [_I]),
     "rwkv_debug_set_device_error": (_I, [_I]),
     "rwkv_wkv7_backward": (_I, [_P] * 17 + [_I] * 7 + [_P]),

@@ -43,6 +43,8 @@ int wkv7_bwd_seq(const WkvBwdArgs& p, cudaStream_t st);
 size_t wkv7_bwd_chunk_ws_bytes(int B, int T, int H);
 // force_nseg > 0: pass-1 segment count (tests); 0: automatic
 int wkv7_bwd_chunked(const WkvBwdArgs& p, float* ws, int force_nseg, cudaStream_t st);
+// kernels wkv7_bwd_chunked enqueues for these sizes on the current device
+int wkv7_bwd_chunk_launches(int B, int T, int H, int force_nseg);
 int wkv7_step_launch(float* S, const void* r, const void* w, const void* k, const void* v,
                      const void* a, const void* b, void* y, int Bs, int H, int dtype, int w_dtype,
                      int w_mode, cudaStream_t st);

@@ -159,6 +159,11 @@ extern "C" int rwkv_wkv7_backward_ws(const void* r, const void* w, const void* k
     return wkv7_bwd_chunked(p, (float*)workspace, g_wkv_segments, (cudaStream_t)stream);
 }
 
+extern "C" int rwkv_wkv7_backward_launch_count(int B, int T, int H, int N) {
+    if (check_dims(B, T, H, N, RWKV_F32)) return 0;
+    return wkv7_bwd_chunk_launches(B, T, H, g_wkv_segments);
+}
+
 extern "C" int rwkv_wkv7_step(float* S, const void* r, const void* w, const void* k,
                               const void* v, const void* a, const void* b, void* y, int Bs, int H,
                               int N, int dtype, int w_dtype, int w_mode, void* stream) {

@@ -30,6 +30,7 @@
 // ~6e-4 relative error against float64 for fp16).  Chunks whose
 // cumulative decay falls below e^-80 form the Mab..Mrk products and their gradients
 // element-wise from exponent differences (the factored forms would overflow).
+#include <algorithm>
 #include <type_traits>
 
 #include "chunk_common.cuh"
@@ -1159,7 +1160,26 @@ const PartStreams* part_streams() {
     }
     return &cache[dev];
 }
+// Segmenting of pass 1 for units (b, h) chains of nch chunks: segments of seg_len chunks
+// (at least 3; the top segment takes the remainder), used when nsegs >= 2.  Automatic
+// when force_nseg <= 0: only when the chains leave at least three quarters of the SMs idle.
+struct SegPlan {
+    int seg_len, nsegs;
+};
+SegPlan seg_plan(int units, int nch, int force_nseg) {
+    int want = force_nseg > 0 ? force_nseg : std::min(sm_count() / units, nch / 8);
+    if (force_nseg <= 0 && want < 4) want = 1;
+    const int seg_len = want > 1 ? std::max(3, nch / want) : nch;
+    return SegPlan{seg_len, nch / seg_len};
+}
+bool use_parts(int units, int nch) { return sm_count() - units >= 32 && nch >= 16; }
 }  // namespace
+
+int wkv7_bwd_chunk_launches(int B, int T, int H, int force_nseg) {
+    const int units = B * H, nch = (T + bwdc::L - 1) / bwdc::L;
+    if (seg_plan(units, nch, force_nseg).nsegs >= 2) return 4;  // transition, scan, final, pass 2
+    return use_parts(units, nch) ? 2 * PartStreams::NP : 2;
+}
 
 template <typename T, typename TW>
 static int launch_bwd_chunked(const WkvBwdArgs& p, float* ws, int force_nseg, cudaStream_t st) {
@@ -1200,10 +1220,8 @@ static int launch_bwd_chunked(const WkvBwdArgs& p, float* ws, int force_nseg, cu
     // segment's [C | M] from [0 | I] (twice the chain's columns), a scan composes them top
     // down, and the final pass runs all segments in parallel; then pass 2 on all SMs.
     {
-        int want = force_nseg > 0 ? force_nseg : min(sm_count() / units, nch / 8);
-        if (force_nseg <= 0 && want < 4) want = 1;
-        const int seg_len = want > 1 ? max(3, nch / want) : nch;
-        const int nsegs = nch / seg_len;  // the top segment takes the remainder
+        const SegPlan pl = seg_plan(units, nch, force_nseg);
+        const int seg_len = pl.seg_len, nsegs = pl.nsegs;
         if (nsegs >= 2) {
             k1t<<<dim3(units, nsegs - 1), p1::NTH, s1t, st>>>(p.dsT, ws, nullptr, p.T, p.H, 0, 0, seg_len, maps);
             int rc = check_launch();
@@ -1220,7 +1238,7 @@ static int launch_bwd_chunked(const WkvBwdArgs& p, float* ws, int force_nseg, cu
     // parts (top chunks first) on a high-priority side stream, and pass 2 of each part
     // starts on the caller's stream as soon as its part of the chain is done, on the SMs
     // the chain leaves free.
-    const PartStreams* ps = (sm_count() - units >= 32 && nch >= 16) ? part_streams() : nullptr;
+    const PartStreams* ps = use_parts(units, nch) ? part_streams() : nullptr;
     if (!ps) {
         int rc = pass1(st, 0, nch);
         return rc ? rc : pass2(st, 0, nch);

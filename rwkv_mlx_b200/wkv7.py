@@ -125,7 +125,8 @@ def _bwd(r, w, k, v, a, b, dy, ckpt, head_size=64, s0=None, dsT=None, want_ds0=F
             nat.ptr(s0), nat.ptr(dsT), nat.ptr(ckpt) if (ckpt is not None and ckpt.numel()) else None,
             *[nat.ptr(g) for g in grads], nat.ptr(ds0), B, T, H, 64, nat.dtype_code(r),
             nat.dtype_code(w), ckpt_len, nat.ptr(ws), ws_bytes, nat.stream_ptr(dev))
-    nat.check(rc, "rwkv_wkv7_backward_ws")
+        kernels = L.rwkv_wkv7_backward_launch_count(B, T, H, 64)  # depends on the device's SM count
+    nat.check(rc, "rwkv_wkv7_backward_ws", kernels=kernels)
     # dw is produced in r.dtype like the reference's (wkv7_metal.py:317), whatever w's dtype
     return tuple(grads), ds0
 

@@ -799,31 +799,41 @@ __global__ void __launch_bounds__(p1::NTH, 1)
 // The value columns are independent: eight per CTA, fp32 FMAs.
 __global__ void __launch_bounds__(256)
     wkv7_bwd_seg_scan_kernel(const float* __restrict__ dsT, float* __restrict__ dxl, int nch, int seg_len) {
-    __shared__ __align__(16) float Ms[N][LDC];
-    __shared__ float Din[N][8], Cs[N][8];
+    __shared__ __align__(16) float Ms[2][N][LDC];  // the next segment's M lands while this one is used
+    __shared__ __align__(16) float Cs[2][N][8];
+    __shared__ float Din[N][8];
     const int bh = blockIdx.x, v0 = 8 * blockIdx.y, tid = threadIdx.x, k = tid >> 2, c2 = (tid & 3) * 2;
     const int nsegs = nch / seg_len;
     float* base = dxl + (size_t)bh * nch * N * N;
+    auto load = [&](int sg, int buf) {  // C and M of segment sg (dxl[lo], dxl[lo + 1]), by cp.async
+        const float* C = base + (size_t)(sg * seg_len) * N * N;
+        const float* M = C + (size_t)N * N;
+        for (int e = tid; e < N * N / 4; e += 256) cp16(&Ms[buf][e >> 4][(e & 15) * 4], M + 4 * e);
+        for (int e = tid; e < N * 2; e += 256) cp16(&Cs[buf][e >> 1][4 * (e & 1)], C + (size_t)(e >> 1) * N + v0 + 4 * (e & 1));
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
     for (int e = tid; e < N * 8; e += 256) {
         const int j = e >> 3, cc = e & 7;
         Din[j][cc] = dsT ? dsT[((size_t)bh * N + v0 + cc) * N + j] : 0.f;
     }
-    for (int sg = nsegs - 1; sg >= 1; sg--) {
-        const float* C = base + (size_t)(sg * seg_len) * N * N;
-        const float* M = C + (size_t)N * N;
-        __syncthreads();  // Din written, the previous step's reads of Ms done
-        for (int e = tid; e < N * N / 4; e += 256)
-            *reinterpret_cast<float4*>(&Ms[e >> 4][(e & 15) * 4]) = reinterpret_cast<const float4*>(M)[e];
-        for (int e = tid; e < N * 8; e += 256) Cs[e >> 3][e & 7] = C[(size_t)(e >> 3) * N + v0 + (e & 7)];
-        __syncthreads();
-        float a0 = Cs[k][c2], a1 = Cs[k][c2 + 1];
+    if (nsegs >= 2) load(nsegs - 1, 0);
+    for (int sg = nsegs - 1, it = 0; sg >= 1; sg--, it++) {
+        const int buf = it & 1;
+        if (sg >= 2) {
+            load(sg - 1, buf ^ 1);  // buf ^ 1 was last read in the previous step, before its barrier
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        __syncthreads();  // this step's M, C and the current Din visible to all
+        float a0 = Cs[buf][k][c2], a1 = Cs[buf][k][c2 + 1];
 #pragma unroll 8
         for (int j = 0; j < N; j++) {
-            const float m = Ms[k][j];
+            const float m = Ms[buf][k][j];
             a0 = fmaf(m, Din[j][c2], a0);
             a1 = fmaf(m, Din[j][c2 + 1], a1);
         }
-        __syncthreads();  // every read of Din done
+        __syncthreads();  // every read of Din and of this step's buffers done
         Din[k][c2] = a0, Din[k][c2 + 1] = a1;
         float* out = base + (size_t)(sg * seg_len - 1) * N * N + (size_t)k * N + v0 + c2;
         out[0] = a0, out[1] = a1;

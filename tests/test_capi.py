@@ -64,6 +64,7 @@ def test_workspace_queries(lib):
     assert lib.rwkv_moe_router_workspace_size(65536, 8) > 0
     assert lib.rwkv_moe_permute_workspace_size(131072, 8) >= 2 * 64 * 8 * 4
     assert lib.rwkv_moe_router_workspace_size(0, 8) == 0
+    assert lib.rwkv_wkv7_backward_launch_count(1, 16, 1, 32) == 0  # head size 32: invalid sizes
 
 
 def test_python_api_refuses_cpu_tensors():

@@ -151,6 +151,19 @@ def test_automatic_backward_segments_at_one_sequence_per_gpu():
         assert rel_rms(g.double().cpu().numpy(), g1.double().cpu().numpy()) < 2e-3, name
 
 
+def test_backward_launch_count_follows_the_plan():
+    """The launch count the binding reports for the chunked backward: segmented chain at
+    one sequence (transition, scan, final, per-chunk gradients), the chain in four parts
+    at eight sequences (four launches of each pass), two launches for a short sequence."""
+    from rwkv_mlx_b200 import _native
+
+    L = _native.lib()
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    assert L.rwkv_wkv7_backward_launch_count(1, 4096, 12, 64) == (4 if sms // 12 >= 4 else 2 + 6 * (sms - 12 >= 32))
+    assert L.rwkv_wkv7_backward_launch_count(8, 4096, 12, 64) == (8 if sms - 96 >= 32 else 2)
+    assert L.rwkv_wkv7_backward_launch_count(1, 96, 2, 64) == 2
+
+
 def test_host_set_device_error_raises():
     """The Python check surfaces the device error word (set here from the host)."""
     import rwkv_mlx_b200 as rb

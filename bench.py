@@ -159,6 +159,24 @@ def cuda_timed(fn, steps, stream=None):
     return e0.elapsed_time(e1) / steps
 
 
+def cuda_timed_flushed(fn, steps):
+    """Like cuda_timed for inputs that fit in L2: before every step a 256 MB buffer is
+    written (evicting L2) outside the timed interval; each step is bracketed by its own
+    CUDA events and the per-step times are averaged."""
+    s = torch.cuda.current_stream()
+    buf = torch.empty(64 * 1024 * 1024, device=s.device, dtype=torch.float32)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    torch.cuda.nvtx.range_push("timed")
+    for e0, e1 in ev:
+        buf.zero_()
+        e0.record(s)
+        fn()
+        e1.record(s)
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    return sum(e0.elapsed_time(e1) for e0, e1 in ev) / steps
+
+
 # ---------------------------------------------------------------------------
 # model construction
 # ---------------------------------------------------------------------------
@@ -359,7 +377,8 @@ def traffic_for(kernel, B, T, H):
 
 
 def run_wkv(args, ws, rank, dev, backward=False, B=None):
-    """WKV-7 op alone at config-2 scale (B=8, T=4096, H=12 per GPU, fp16 + fp32 w)."""
+    """WKV-7 op alone at config-2 scale (B=8, T=4096, H=12 per GPU, fp16 + fp32 w).  Below
+    B=4 the inputs fit in L2, so L2 is flushed before every step (outside the timing)."""
     from rwkv_mlx_b200 import check_device_error, wkv7
 
     B, T, H = (args.batch if B is None else B), args.seq, 12
@@ -384,7 +403,8 @@ def run_wkv(args, ws, rank, dev, backward=False, B=None):
     torch.cuda.synchronize()
     barrier(ws)
     clk = ClockSampler(dev)
-    ms = cuda_timed(fn, args.steps)
+    flush = B < 4
+    ms = cuda_timed_flushed(fn, args.steps) if flush else cuda_timed(fn, args.steps)
     clocks = clk.stop()
     check_device_error()
     ms = max_over_ranks(ms, ws)
@@ -394,7 +414,8 @@ def run_wkv(args, ws, rank, dev, backward=False, B=None):
     return {"metric": f"{name} HBM GB/s", "value": gbs * ws, "unit": "GB/s", "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "fp16 (fp32 w, fp32 state)", "data": "synthetic (config 1 distributions)",
-            "config": {"workload": f"{name} B={B} T={T} H={H}", "l2": "inputs larger than L2"},
+            "config": {"workload": f"{name} B={B} T={T} H={H}",
+                       "l2": "flushed before every step (256 MB write, untimed)" if flush else "inputs larger than L2"},
             "roofline": {"kernel": name, "bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s",
                          "frac": gbs / hbm, "traffic": traffic_for(name, B, T, H), "peak_source": src},
             "clocks": clocks}
@@ -762,7 +783,7 @@ def secondary_lines(args, ws, rank, dev, model, primary):
     """Per-GPU workloads measured in the same run as the headline, each timed on its own
     with CUDA events (max over ranks) and reported with its own roofline where it has
     one: the weak-scaled prefill (B=8 per GPU), the WKV-7 forward and backward at
-    B=8 T=4096 H=12, the LoRA-MoE ChannelMix layer of BASELINE configs[3] (replicated
+    B=8 T=4096 H=12, the backward at B=1, the LoRA-MoE ChannelMix layer of BASELINE configs[3] (replicated
     experts, and expert-parallel over NCCL all-to-all at N>1) and the batched decode of
     BASELINE configs[2]."""
     out = {}
@@ -773,6 +794,8 @@ def secondary_lines(args, ws, rank, dev, model, primary):
         out["prefill_weak_b8_per_gpu"] = "same as the headline at this GPU count (B=8 on one GPU)"
     out["wkv7_fwd_b8_t4096_h12"] = _brief(run_wkv(args, ws, rank, dev, backward=False, B=8))
     out["wkv7_bwd_b8_t4096_h12"] = _brief(run_wkv(args, ws, rank, dev, backward=True, B=8))
+    # one sequence per GPU (configs[1] over 8 GPUs): the segmented adjoint chain
+    out["wkv7_bwd_b1_t4096_h12"] = _brief(run_wkv(args, ws, rank, dev, backward=True, B=1))
     out["lora_moe_cmix_config3"] = _brief(run_moe(args, ws, rank, dev, ep=False))
     if ws > 1:
         out["lora_moe_cmix_config3_ep"] = _brief(run_moe(args, ws, rank, dev, ep=True))
